@@ -1,0 +1,363 @@
+// Quantisation and normalisation kernels.
+//
+//  * rmsnorm_quant: optional residual add, RMSNorm (plain w or Gemma 1+w), bf16 output and/or MXFP8
+//    (e4m3 + ue8m0 per 32) output laid out for the GEMM's B operand. This is the producer-side fusion
+//    of the reference's per-token fp8 quant (kernels/r9k_moe_mxfp4a8.hip:1683-1780) into the norm.
+//  * quant_act_mxfp8: standalone activation quant (kept for R9K_*=stock style A/B and odd producers).
+//  * weight quantisers: MXFP4 with an MSE search over exponent shifts -2..+2 (generalising the
+//    reference's two-candidate search, r9700_vllm/quant/nvfp4.py:54-76), MXFP8, NVFP4, and the
+//    NVFP4 -> MXFP4 load-time conversion (r9700_vllm/quant/nvfp4.py:78-112).
+//  * dequantisers used by tests and by fallbacks that need bf16 weights.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+
+namespace r9k {
+
+// e2m1 magnitude code for |v| (v already divided by the block scale), round-to-nearest-even,
+// saturating at 6.
+R9K_DEVINL uint32_t e2m1_code_abs(float v) {
+  return (uint32_t)(v > 0.25f) + (uint32_t)(v >= 0.75f) + (uint32_t)(v > 1.25f) + (uint32_t)(v >= 1.75f) +
+         (uint32_t)(v > 2.5f) + (uint32_t)(v >= 3.5f) + (uint32_t)(v > 5.0f);
+}
+R9K_DEVINL float e2m1_value(uint32_t code) {
+  const float mag[8] = {0.f, 0.5f, 1.f, 1.5f, 2.f, 3.f, 4.f, 6.f};
+  const float m = mag[code & 7];
+  return (code & 8) ? -m : m;
+}
+R9K_DEVINL uint32_t e2m1_encode(float v) {
+  const uint32_t c = e2m1_code_abs(fabsf(v));
+  return (v < 0.f && c != 0) ? (c | 8u) : c;
+}
+
+// ------------------------------------------------------------------------------------------------
+// RMSNorm (+ residual) (+ MXFP8 quant)
+// ------------------------------------------------------------------------------------------------
+template <typename TIn>
+__global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ res_in,
+                                     __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
+                                     int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                     uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  extern __shared__ float srow[];
+  __shared__ float sred[32];
+  const int64_t r = blockIdx.x;
+  const TIn* xr = x + r * ldx;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < K; i += blockDim.x) {
+    float v;
+    if constexpr (std::is_same<TIn, float>::value) v = xr[i];
+    else v = __bfloat162float(xr[i]);
+    if (res_in != nullptr) {
+      v += __bfloat162float(res_in[r * (int64_t)K + i]);
+    }
+    if (res_out != nullptr) {
+      const __nv_bfloat16 hb = __float2bfloat16(v);
+      res_out[r * (int64_t)K + i] = hb;
+      v = __bfloat162float(hb);  // the residual stream is bf16: normalise what is stored
+    }
+    srow[i] = v;
+    ss += v * v;
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sred[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) sred[0] = t;
+  }
+  __syncthreads();
+  const float rr = rsqrtf(sred[0] / (float)K + eps);
+  const int kblocks = K / 32;
+  // each warp handles 32-element blocks: lane i owns element i of the block
+  const int lane = threadIdx.x & 31;
+  for (int blk = threadIdx.x >> 5; blk < kblocks; blk += blockDim.x >> 5) {
+    const int i = blk * 32 + lane;
+    float wv = __bfloat162float(w[i]);
+    if (plus_one) wv += 1.f;
+    float v = srow[i] * rr * wv;
+    if (y != nullptr) {
+      const __nv_bfloat16 vb = __float2bfloat16(v);
+      y[r * ldy + i] = vb;
+      v = __bfloat162float(vb);
+    }
+    if (q != nullptr) {
+      float am = fabsf(v);
+      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      const int e = mx_exponent(am, 448.f);
+      q[r * (int64_t)K + i] = f32_to_e4m3(v * exp2i(-e));
+      if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+    }
+  }
+}
+
+// x: [M, K] bf16 or f32; residual (optional, bf16 [M,K]) is added first and the sum written to
+// res_out; then y = rmsnorm(.) * (w or 1+w). Outputs: y (bf16, optional), q/sf (MXFP8, optional).
+void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
+                   torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
+                   c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf) {
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 32 == 0 && x.stride(1) == 1, "rmsnorm_quant: K % 32 == 0, contiguous rows");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const int threads = K >= 4096 ? 512 : 256;
+  const size_t smem = K * sizeof(float);
+  auto ptr_bf = [](const c10::optional<torch::Tensor>& t) -> __nv_bfloat16* {
+    return (t.has_value() && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
+  };
+  auto ptr_u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
+    return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
+  };
+  const int64_t ldy = (y.has_value() && y->defined()) ? y->stride(0) : K;
+  if (q.has_value() && q->defined()) {
+    TORCH_CHECK(sf.has_value() && sf->defined(), "rmsnorm_quant: q needs sf");
+    TORCH_CHECK(sf->numel() >= ((M + 127) / 128) * ((K / 32 + 3) / 4) * 512, "rmsnorm_quant: sf too small");
+  }
+  if (x.dtype() == torch::kFloat32) {
+    rmsnorm_quant_kernel<float><<<M, threads, smem, st>>>(x.data_ptr<float>(), x.stride(0), ptr_bf(res_in), ptr_bf(res_out),
+                                                           reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K,
+                                                           (float)eps, plus_one, ptr_bf(y), ldy, ptr_u8(q), ptr_u8(sf));
+  } else {
+    rmsnorm_quant_kernel<__nv_bfloat16><<<M, threads, smem, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), ptr_bf(res_in), ptr_bf(res_out),
+        reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K, (float)eps, plus_one, ptr_bf(y), ldy, ptr_u8(q),
+        ptr_u8(sf));
+  }
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------------------------
+// standalone activation quant: bf16 [M, K] (row stride ldx) -> e4m3 [M, K] + ue8m0 chunk scales
+// ------------------------------------------------------------------------------------------------
+__global__ void quant_act_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int K,
+                                       uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  const int kblocks = K / 32;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = (int64_t)M * kblocks;
+  for (int64_t b = gw; b < total; b += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = b / kblocks;
+    const int blk = (int)(b % kblocks);
+    const float v = __bfloat162float(x[r * ldx + blk * 32 + lane]);
+    float am = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int e = mx_exponent(am, 448.f);
+    q[r * K + blk * 32 + lane] = f32_to_e4m3(v * exp2i(-e));
+    if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+  }
+}
+
+void quant_act_mxfp8(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 32 == 0 && x.stride(1) == 1 && x.dtype() == torch::kBFloat16, "quant_act_mxfp8: bf16 [M, K%32]");
+  TORCH_CHECK(sf.numel() >= ((M + 127) / 128) * ((K / 32 + 3) / 4) * 512, "quant_act_mxfp8: sf too small");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  const int64_t warps = M * (K / 32);
+  const int threads = 256;
+  const int64_t blocks = std::min<int64_t>((warps * 32 + threads - 1) / threads, 148 * 16);
+  quant_act_mxfp8_kernel<<<(int)blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)M, (int)K, q.data_ptr<uint8_t>(),
+      sf.data_ptr<uint8_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------------------------
+// weight quantisers (one warp per 32-element block)
+// ------------------------------------------------------------------------------------------------
+// MXFP4 with an exponent search over base-2 .. base+2 (base = ceil(log2(amax/6))), keeping the
+// candidate with the lowest squared error (ties -> the larger exponent, i.e. fewer clipped values).
+__global__ void quant_w_mxfp4_kernel(const float* __restrict__ w, int64_t N, int K, int search,
+                                     uint8_t* __restrict__ packed, uint8_t* __restrict__ sf) {
+  const int kblocks = K / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = N * kblocks;
+  for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < total;
+       b += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = b / kblocks;
+    const int blk = (int)(b % kblocks);
+    const float v = w[r * K + blk * 32 + lane];
+    float am = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int base = mx_exponent(am, 6.f);
+    int best_e = base;
+    if (search) {
+      float best_err = 3.4e38f;
+      for (int d = 2; d >= -2; --d) {
+        const int e = max(-127, min(127, base + d));
+        const float s = exp2i(e);
+        const float dq = e2m1_value(e2m1_encode(v / s)) * s;
+        float err = (dq - v) * (dq - v);
+        for (int o = 16; o > 0; o >>= 1) err += __shfl_xor_sync(0xffffffffu, err, o);
+        if (err < best_err) { best_err = err; best_e = e; }
+      }
+    }
+    const uint32_t code = e2m1_encode(v / exp2i(best_e));
+    const uint32_t other = __shfl_down_sync(0xffffffffu, code, 1);
+    if ((lane & 1) == 0) packed[r * (K / 2) + blk * 16 + (lane >> 1)] = (uint8_t)(code | (other << 4));
+    if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(best_e + 127);
+  }
+}
+
+__global__ void quant_w_mxfp8_kernel(const float* __restrict__ w, int64_t N, int K, uint8_t* __restrict__ q,
+                                     uint8_t* __restrict__ sf) {
+  const int kblocks = K / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = N * kblocks;
+  for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < total;
+       b += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = b / kblocks;
+    const int blk = (int)(b % kblocks);
+    const float v = w[r * K + blk * 32 + lane];
+    float am = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int e = mx_exponent(am, 448.f);
+    q[r * K + blk * 32 + lane] = f32_to_e4m3(v * exp2i(-e));
+    if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+  }
+}
+
+static int grid_for(int64_t warps) {
+  return (int)std::min<int64_t>((warps * 32 + 255) / 256, 148 * 32);
+}
+
+void quant_weight_mxfp4(torch::Tensor w, torch::Tensor packed, torch::Tensor sf, bool search) {
+  TORCH_CHECK(w.dtype() == torch::kFloat32 && w.is_contiguous(), "quant_weight_mxfp4: contiguous f32");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(K % 32 == 0, "K % 32");
+  const at::cuda::CUDAGuard guard(w.device());
+  quant_w_mxfp4_kernel<<<grid_for(N * (K / 32)), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      w.data_ptr<float>(), N, (int)K, search ? 1 : 0, packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void quant_weight_mxfp8(torch::Tensor w, torch::Tensor q, torch::Tensor sf) {
+  TORCH_CHECK(w.dtype() == torch::kFloat32 && w.is_contiguous(), "quant_weight_mxfp8: contiguous f32");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(K % 32 == 0, "K % 32");
+  const at::cuda::CUDAGuard guard(w.device());
+  quant_w_mxfp8_kernel<<<grid_for(N * (K / 32)), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      w.data_ptr<float>(), N, (int)K, q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------------------------
+// NVFP4: e2m1 values, e4m3 scale per 16, fp32 global scale g:  w = v * s / g
+// ------------------------------------------------------------------------------------------------
+// nvfp4 -> dequantised f32 -> MXFP4 (search), fused: one warp per 32-element MX block (two NVFP4 blocks)
+__global__ void nvfp4_to_mxfp4_kernel(const uint8_t* __restrict__ packed_in, const uint8_t* __restrict__ s16,
+                                      float inv_g, int64_t N, int K, int search, uint8_t* __restrict__ packed_out,
+                                      uint8_t* __restrict__ sf) {
+  const int kblocks = K / 32;
+  const int lane = threadIdx.x & 31;
+  const int64_t total = N * kblocks;
+  for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; b < total;
+       b += ((int64_t)gridDim.x * blockDim.x) >> 5) {
+    const int64_t r = b / kblocks;
+    const int blk = (int)(b % kblocks);
+    const int k = blk * 32 + lane;
+    const uint8_t byte = packed_in[r * (K / 2) + (k >> 1)];
+    const uint32_t code = (k & 1) ? (byte >> 4) : (byte & 15);
+    const float s = e4m3_to_f32(s16[r * (K / 16) + (k >> 4)]);
+    const float v = e2m1_value(code) * s * inv_g;
+    float am = fabsf(v);
+    for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const int base = mx_exponent(am, 6.f);
+    int best_e = base;
+    if (search) {
+      float best_err = 3.4e38f;
+      for (int d = 2; d >= -2; --d) {
+        const int e = max(-127, min(127, base + d));
+        const float sc = exp2i(e);
+        const float dq = e2m1_value(e2m1_encode(v / sc)) * sc;
+        float err = (dq - v) * (dq - v);
+        for (int o = 16; o > 0; o >>= 1) err += __shfl_xor_sync(0xffffffffu, err, o);
+        if (err < best_err) { best_err = err; best_e = e; }
+      }
+    }
+    const uint32_t c = e2m1_encode(v / exp2i(best_e));
+    const uint32_t other = __shfl_down_sync(0xffffffffu, c, 1);
+    if ((lane & 1) == 0) packed_out[r * (K / 2) + blk * 16 + (lane >> 1)] = (uint8_t)(c | (other << 4));
+    if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(best_e + 127);
+  }
+}
+
+void nvfp4_to_mxfp4(torch::Tensor packed_in, torch::Tensor s16, double global_scale, torch::Tensor packed_out,
+                    torch::Tensor sf, bool search) {
+  const int64_t N = packed_in.size(0), K = packed_in.size(1) * 2;
+  TORCH_CHECK(K % 32 == 0 && s16.size(1) == K / 16, "nvfp4_to_mxfp4: shapes");
+  const at::cuda::CUDAGuard guard(packed_in.device());
+  nvfp4_to_mxfp4_kernel<<<grid_for(N * (K / 32)), 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      packed_in.data_ptr<uint8_t>(), s16.data_ptr<uint8_t>(), (float)(1.0 / global_scale), N, (int)K, search ? 1 : 0,
+      packed_out.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// f32 weights -> NVFP4 (per-16 e4m3 scale s = amax/6 * g, rounded to e4m3; v = w * g / s)
+__global__ void quant_w_nvfp4_kernel(const float* __restrict__ w, int64_t N, int K, float g,
+                                     uint8_t* __restrict__ packed, uint8_t* __restrict__ s16) {
+  const int kb = K / 16;
+  const int lane = threadIdx.x & 15;  // half-warp per 16-block
+  const int64_t total = N * kb;
+  for (int64_t b = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 4; b < total;
+       b += ((int64_t)gridDim.x * blockDim.x) >> 4) {
+    const int64_t r = b / kb;
+    const int blk = (int)(b % kb);
+    const float v = w[r * K + blk * 16 + lane];
+    float am = fabsf(v);
+    for (int o = 8; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o, 16));
+    const uint8_t sq = f32_to_e4m3(am / 6.f * g);
+    const float s = e4m3_to_f32(sq);
+    const uint32_t c = (s > 0.f) ? e2m1_encode(v * g / s) : 0u;
+    const uint32_t other = __shfl_down_sync(0xffffffffu, c, 1, 16);
+    if ((lane & 1) == 0) packed[r * (K / 2) + blk * 8 + (lane >> 1)] = (uint8_t)(c | (other << 4));
+    if (lane == 0) s16[r * kb + blk] = sq;
+  }
+}
+
+void quant_weight_nvfp4(torch::Tensor w, double global_scale, torch::Tensor packed, torch::Tensor s16) {
+  TORCH_CHECK(w.dtype() == torch::kFloat32 && w.is_contiguous(), "quant_weight_nvfp4: contiguous f32");
+  const int64_t N = w.size(0), K = w.size(1);
+  TORCH_CHECK(K % 16 == 0, "K % 16");
+  const at::cuda::CUDAGuard guard(w.device());
+  const int64_t hw = N * (K / 16);
+  const int blocks = (int)std::min<int64_t>((hw * 16 + 255) / 256, 148 * 32);
+  quant_w_nvfp4_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      w.data_ptr<float>(), N, (int)K, (float)global_scale, packed.data_ptr<uint8_t>(), s16.data_ptr<uint8_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// ------------------------------------------------------------------------------------------------
+// dequantisers (MX chunk layout -> f32), used by tests and bf16 fallbacks
+// ------------------------------------------------------------------------------------------------
+__global__ void dequant_mx_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf, int64_t N, int K,
+                                  int fp4, float* __restrict__ out) {
+  const int64_t total = N * K;
+  const int kblocks = K / 32;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / K;
+    const int k = (int)(i % K);
+    float v;
+    if (fp4) {
+      const uint8_t byte = q[r * (K / 2) + (k >> 1)];
+      v = e2m1_value((k & 1) ? (byte >> 4) : (byte & 15));
+    } else {
+      v = e4m3_to_f32(q[r * K + k]);
+    }
+    const int e = (int)sf[sf_offset(r, k >> 5, kblocks)] - 127;
+    out[i] = v * exp2i(max(-126, e)) * (e < -126 ? 0.5f : 1.f);
+  }
+}
+
+void dequant_mx(torch::Tensor q, torch::Tensor sf, bool fp4, torch::Tensor out) {
+  const int64_t N = out.size(0), K = out.size(1);
+  const at::cuda::CUDAGuard guard(q.device());
+  const int blocks = (int)std::min<int64_t>((N * K + 255) / 256, 148 * 64);
+  dequant_mx_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(),
+                                                                            N, (int)K, fp4 ? 1 : 0, out.data_ptr<float>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

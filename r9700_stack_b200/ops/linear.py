@@ -1,0 +1,205 @@
+"""Linear layers on the tcgen05 GEMM core.
+
+Weights are held in one of three device formats:
+
+* ``MXWeight(fp4=True)``  - MXFP4: packed e2m1 [N, K/2] + ue8m0 scales per 32 (chunk layout).
+  NVFP4 checkpoints convert to this at load (MSE-searched exponents), as the reference does
+  (r9700_vllm/quant/nvfp4.py:78-112).
+* ``MXWeight(fp4=False)`` - MXFP8: e4m3 [N, K] + ue8m0 scales per 32. Block-128 fp8 and per-row fp8
+  checkpoints (lm heads, drafters) convert to this at load.
+* ``BF16Weight``           - unquantised weights.
+
+Activations feeding MX weights are MXFP8 (``MXAct``), produced directly by the fused
+RMSNorm/SwiGLU epilogues, or by :func:`quant_act` for other producers.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native
+from ..quant import formats as F
+from ..utils import status as _status
+
+
+def _ops():
+    return _native.ops()
+
+
+def sf_bytes(rows: int, K: int) -> int:
+    return F.sf_num_bytes(rows, K // 32)
+
+
+@dataclass
+class MXWeight:
+    q: torch.Tensor  # uint8 [N, K/2] (fp4) or [N, K] (e4m3)
+    sf: torch.Tensor  # uint8 chunk layout
+    fp4: bool
+    N: int
+    K: int
+
+    @property
+    def nbytes(self) -> int:
+        return self.q.numel() + self.sf.numel()
+
+    def dequant(self) -> torch.Tensor:
+        out = torch.empty(self.N, self.K, dtype=torch.float32, device=self.q.device)
+        _ops().dequant_mx(self.q, self.sf, self.fp4, out)
+        return out
+
+    def narrow_rows(self, start: int, length: int) -> "MXWeight":
+        """Row slice (start and length multiples of 128 so that scale chunks stay whole)."""
+        assert start % 128 == 0 and (length % 128 == 0 or start + length == self.N)
+        kchunks = (self.K // 32 + 3) // 4
+        c0 = (start // 128) * kchunks * 512
+        c1 = ((start + length + 127) // 128) * kchunks * 512
+        return MXWeight(self.q[start : start + length], self.sf[c0:c1], self.fp4, length, self.K)
+
+
+@dataclass
+class BF16Weight:
+    w: torch.Tensor  # bf16 [N, K]
+
+    @property
+    def N(self) -> int:
+        return self.w.shape[0]
+
+    @property
+    def K(self) -> int:
+        return self.w.shape[1]
+
+
+@dataclass
+class MXAct:
+    q: torch.Tensor  # uint8 [M, K] e4m3
+    sf: torch.Tensor  # uint8 chunk layout (rows padded to 128)
+
+    @property
+    def M(self) -> int:
+        return self.q.shape[0]
+
+    def narrow(self, m: int) -> "MXAct":
+        return MXAct(self.q[:m], self.sf)
+
+
+def act_sf_bytes(M: int, K: int) -> int:
+    """Activation scale buffers cover the token count rounded up to 256 (the widest GEMM tile)."""
+    return sf_bytes(max(256, (M + 255) // 256 * 256), K)
+
+
+def alloc_act(M: int, K: int, device) -> MXAct:
+    return MXAct(
+        torch.empty(M, K, dtype=torch.uint8, device=device),
+        torch.zeros(act_sf_bytes(M, K), dtype=torch.uint8, device=device),
+    )
+
+
+# ------------------------------------------------------------------------------------------------
+# weight construction
+# ------------------------------------------------------------------------------------------------
+def mx_from_float(w: torch.Tensor, fp4: bool = True, search: bool = True) -> MXWeight:
+    """Quantise a float weight [N, K] on the device (f32 staging, one matrix at a time)."""
+    N, K = w.shape
+    dev = w.device
+    wf = w.float().contiguous()
+    sf = torch.zeros(sf_bytes(N, K), dtype=torch.uint8, device=dev)
+    if fp4:
+        q = torch.empty(N, K // 2, dtype=torch.uint8, device=dev)
+        _ops().quant_weight_mxfp4(wf, q, sf, search)
+    else:
+        q = torch.empty(N, K, dtype=torch.uint8, device=dev)
+        _ops().quant_weight_mxfp8(wf, q, sf)
+    return MXWeight(q, sf, fp4, N, K)
+
+
+def nvfp4_quantize(w: torch.Tensor, global_scale: float | None = None):
+    """float [N, K] -> NVFP4 (packed, s16 e4m3 bytes, g) on the device."""
+    N, K = w.shape
+    wf = w.float().contiguous()
+    g = F.nvfp4_global_scale(wf) if global_scale is None else global_scale
+    packed = torch.empty(N, K // 2, dtype=torch.uint8, device=w.device)
+    s16 = torch.empty(N, K // 16, dtype=torch.uint8, device=w.device)
+    _ops().quant_weight_nvfp4(wf, float(g), packed, s16)
+    return packed, s16, float(g)
+
+
+def mx_from_nvfp4(packed: torch.Tensor, s16: torch.Tensor, g: float, search: bool = True) -> MXWeight:
+    N, K2 = packed.shape
+    K = K2 * 2
+    sf = torch.zeros(sf_bytes(N, K), dtype=torch.uint8, device=packed.device)
+    out = torch.empty(N, K2, dtype=torch.uint8, device=packed.device)
+    _ops().nvfp4_to_mxfp4(packed.contiguous(), s16.contiguous(), float(g), out, sf, search)
+    return MXWeight(out, sf, True, N, K)
+
+
+# ------------------------------------------------------------------------------------------------
+# activations and GEMMs
+# ------------------------------------------------------------------------------------------------
+def quant_act(x: torch.Tensor, out: MXAct | None = None) -> MXAct:
+    M, K = x.shape
+    if out is None:
+        out = alloc_act(M, K, x.device)
+    _ops().quant_act_mxfp8(x, out.q, out.sf)
+    return out
+
+
+def rmsnorm(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    eps: float,
+    *,
+    plus_one: bool = False,
+    residual: torch.Tensor | None = None,
+    residual_out: torch.Tensor | None = None,
+    out: torch.Tensor | None = None,
+    quant_out: MXAct | None = None,
+) -> None:
+    """Fused (residual add) + RMSNorm (+ MXFP8 quant). Writes into the given outputs."""
+    _ops().rmsnorm_quant(
+        x,
+        residual,
+        residual_out,
+        w,
+        float(eps),
+        bool(plus_one),
+        out,
+        quant_out.q if quant_out is not None else None,
+        quant_out.sf if quant_out is not None else None,
+    )
+
+
+def mx_linear(
+    x: MXAct,
+    w: MXWeight,
+    out: torch.Tensor | None = None,
+    residual: torch.Tensor | None = None,
+    alpha: float = 1.0,
+    out_dtype=torch.bfloat16,
+) -> torch.Tensor:
+    M = x.M
+    if out is None:
+        out = torch.empty(M, w.N, dtype=out_dtype, device=x.q.device)
+    _ops().gemm_mx(w.q, w.sf, w.fp4, x.q, x.sf, out, residual, float(alpha), _status.status(x.q.device))
+    return out
+
+
+def mx_swiglu(x: MXAct, w_gate: MXWeight, w_up: MXWeight, out: MXAct | None = None) -> MXAct:
+    M = x.M
+    if out is None:
+        out = alloc_act(M, w_gate.N, x.q.device)
+    _ops().gemm_mx_swiglu(
+        w_gate.q, w_gate.sf, w_up.q, w_up.sf, w_gate.fp4, x.q, x.sf, out.q, out.sf, _status.status(x.q.device)
+    )
+    return out
+
+
+def bf16_linear(
+    x: torch.Tensor, w: BF16Weight, out: torch.Tensor | None = None, residual: torch.Tensor | None = None,
+    alpha: float = 1.0, out_dtype=torch.bfloat16,
+) -> torch.Tensor:
+    M = x.shape[0]
+    if out is None:
+        out = torch.empty(M, w.N, dtype=out_dtype, device=x.device)
+    _ops().gemm_bf16(w.w, x, out, residual, float(alpha), _status.status(x.device))
+    return out
