@@ -24,6 +24,28 @@ void quant_weight_nvfp4(torch::Tensor w, double global_scale, torch::Tensor pack
 void nvfp4_to_mxfp4(torch::Tensor packed_in, torch::Tensor s16, double global_scale, torch::Tensor packed_out,
                     torch::Tensor sf, bool search);
 void dequant_mx(torch::Tensor q, torch::Tensor sf, bool fp4, torch::Tensor out);
+// attention.cu
+void qk_norm_rope_cache(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t q_off, int64_t k_off, int64_t v_off,
+                        torch::Tensor qw, torch::Tensor kw, double eps, bool plus_one, torch::Tensor positions,
+                        torch::Tensor cos_sin, int64_t rot, torch::Tensor slots, torch::Tensor q_out,
+                        torch::Tensor k_cache, torch::Tensor v_cache, double k_scale, double v_scale);
+void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                     torch::Tensor tok_seq, torch::Tensor tok_ctx, double sm_scale, double k_scale, double v_scale,
+                     c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
+                     c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, int64_t window);
+// gdn.cu
+void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv, int64_t b_off, int64_t a_off,
+                   torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor tok_slot, torch::Tensor tok_pos,
+                   torch::Tensor tok_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor q_out,
+                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out);
+void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::Tensor seq_slot,
+                           torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_has_state);
+void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                   torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
+                   torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
+void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torch::Tensor w, double eps,
+                        c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> out_q,
+                        c10::optional<torch::Tensor> out_sf);
 }  // namespace r9k
 
 TORCH_LIBRARY(r9k, m) {
@@ -41,6 +63,21 @@ TORCH_LIBRARY(r9k, m) {
   m.def("nvfp4_to_mxfp4(Tensor packed_in, Tensor s16, float global_scale, Tensor(a!) packed_out, Tensor(b!) sf, "
         "bool search) -> ()");
   m.def("dequant_mx(Tensor q, Tensor sf, bool fp4, Tensor(a!) out) -> ()");
+  m.def("qk_norm_rope_cache(Tensor qkv, int Hq, int Hkv, int q_off, int k_off, int v_off, Tensor qw, Tensor kw, "
+        "float eps, bool plus_one, Tensor positions, Tensor cos_sin, int rot, Tensor slots, Tensor(a!) q_out, "
+        "Tensor(b!) k_cache, Tensor(c!) v_cache, float k_scale, float v_scale) -> ()");
+  m.def("paged_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_seq, "
+        "Tensor tok_ctx, float sm_scale, float k_scale, float v_scale, Tensor? gate, Tensor(a!)? out, "
+        "Tensor(b!)? out_q, Tensor(c!)? out_sf, int window) -> ()");
+  m.def("gdn_conv_prep(Tensor proj, int Hk, int Hv, int dk, int dv, int b_off, int a_off, Tensor conv_w, "
+        "Tensor conv_state, Tensor tok_slot, Tensor tok_pos, Tensor tok_has_state, Tensor A_log, Tensor dt_bias, "
+        "Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!) g_out, Tensor(e!) beta_out) -> ()");
+  m.def("gdn_conv_state_update(Tensor proj, Tensor(a!) conv_state, Tensor seq_slot, Tensor seq_start, "
+        "Tensor seq_len, Tensor seq_has_state) -> ()");
+  m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
+        "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
+  m.def("gdn_out_norm_quant(Tensor o, Tensor proj, int z_off, Tensor w, float eps, Tensor(a!)? y, "
+        "Tensor(b!)? out_q, Tensor(c!)? out_sf) -> ()");
 }
 
 TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
@@ -54,6 +91,12 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("quant_weight_nvfp4", &r9k::quant_weight_nvfp4);
   m.impl("nvfp4_to_mxfp4", &r9k::nvfp4_to_mxfp4);
   m.impl("dequant_mx", &r9k::dequant_mx);
+  m.impl("qk_norm_rope_cache", &r9k::qk_norm_rope_cache);
+  m.impl("paged_attention", &r9k::paged_attention);
+  m.impl("gdn_conv_prep", &r9k::gdn_conv_prep);
+  m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
+  m.impl("gdn_recurrent", &r9k::gdn_recurrent);
+  m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "r9700_stack_b200 sm_100a kernel library"; }

@@ -1,0 +1,324 @@
+// Gated DeltaNet (linear attention) kernels.
+//
+// Per value head h (key head h / (Hv/Hk)), per token:
+//   g    = -exp(A_log[h]) * softplus(a + dt_bias[h])        beta = sigmoid(b)
+//   q, k = l2norm(q) * dk^-1/2, l2norm(k)
+//   S    = S * exp(g);  delta = beta * (v - S^T k);  S += k (x) delta;  o = S^T q
+//   out  = rmsnorm(o) * w * silu(z)
+// (reference: kernels/r9k_gdn.hip:4-21, :90-647; the reference's long prefill path calls stock
+// Triton, r9700_vllm/models/gdn.py:28-33, which has no counterpart here: the recurrent core below
+// serves prefill too.)
+//
+// Kernels:
+//  * gdn_conv_prep      - causal depthwise conv1d (width W) over the q|k|v channels + SiLU, l2-norms,
+//                         g and beta; reads the per-sequence conv state for the first W-1 taps.
+//  * gdn_conv_state_update - stores the last W-1 conv inputs of each sequence (skipped during spec
+//                         verify, run on commit).
+//  * gdn_recurrent      - the delta-rule recurrence. Columns of S evolve independently, so the grid
+//                         splits each head's dv columns over CTAs (32 per CTA); four lanes share a
+//                         column (32 rows each) and reduce with shuffles, so no block barrier runs
+//                         per token. Serves decode (1 token), spec verify (T tokens, state not
+//                         written), commit (accepted tokens, state written) and prefill.
+//  * gdn_out_norm_quant - RMSNormGated + MXFP8 quantisation of the result for out_proj.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+
+namespace r9k {
+
+template <typename T> R9K_DEVINL float to_f(T v);
+template <> R9K_DEVINL float to_f<float>(float v) { return v; }
+template <> R9K_DEVINL float to_f<__nv_bfloat16>(__nv_bfloat16 v) { return __bfloat162float(v); }
+template <typename T> R9K_DEVINL T from_f(float v);
+template <> R9K_DEVINL float from_f<float>(float v) { return v; }
+template <> R9K_DEVINL __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
+
+// ------------------------------------------------------------------------------------------------
+// conv + prep: one CTA per token. Channels: [q: Hk*dk][k: Hk*dk][v: Hv*dv] at proj offset 0.
+// ------------------------------------------------------------------------------------------------
+template <typename ST>
+__global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int dk,
+                                     int dv, int b_off, int a_off, const __nv_bfloat16* __restrict__ conv_w, int W,
+                                     const ST* __restrict__ conv_state, const int32_t* __restrict__ tok_slot,
+                                     const int32_t* __restrict__ tok_pos_in_chunk,
+                                     const int32_t* __restrict__ has_state_tok, const float* __restrict__ A_log,
+                                     const float* __restrict__ dt_bias, float* __restrict__ q_out,
+                                     float* __restrict__ k_out, float* __restrict__ v_out, float* __restrict__ g_out,
+                                     float* __restrict__ beta_out) {
+  extern __shared__ float sh[];  // conv outputs for all channels of this token
+  const int t = blockIdx.x;
+  const int C = 2 * Hk * dk + Hv * dv;
+  const int j = tok_pos_in_chunk[t];  // index of this token within its sequence's chunk
+  const int slot = tok_slot[t];
+  const bool hs = has_state_tok[t] != 0;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float acc = 0.f;
+    for (int w = 0; w < W; ++w) {
+      const int back = W - 1 - w;  // how many tokens before this one
+      float x;
+      if (j - back >= 0) {
+        x = __bfloat162float(proj[(int64_t)(t - back) * ld + c]);
+      } else {
+        // from the conv state: state holds the last W-1 inputs, index W-2 = most recent
+        const int si = (W - 1) - (back - j);
+        x = (hs && si >= 0) ? to_f<ST>(conv_state[((int64_t)slot * C + c) * (W - 1) + si]) : 0.f;
+      }
+      acc += x * __bfloat162float(conv_w[(int64_t)c * W + w]);
+    }
+    sh[c] = silu_f(acc);
+  }
+  __syncthreads();
+  // l2 norms: one warp per key head of q and of k
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+  for (int hh = warp; hh < 2 * Hk; hh += nwarps) {
+    const float* src = sh + hh * dk;
+    float ss = 0.f;
+    for (int i = lane; i < dk; i += 32) ss += src[i] * src[i];
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float inv = rsqrtf(ss + 1e-6f);
+    if (hh < Hk) inv *= rsqrtf((float)dk);
+    float* dst = (hh < Hk ? q_out + ((int64_t)t * Hk + hh) * dk : k_out + ((int64_t)t * Hk + (hh - Hk)) * dk);
+    for (int i = lane; i < dk; i += 32) dst[i] = src[i] * inv;
+  }
+  for (int c = threadIdx.x; c < Hv * dv; c += blockDim.x) v_out[(int64_t)t * Hv * dv + c] = sh[2 * Hk * dk + c];
+  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
+    const float a = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
+    const float b = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
+    g_out[(int64_t)t * Hv + h] = -__expf(A_log[h]) * softplus_f(a + dt_bias[h]);
+    beta_out[(int64_t)t * Hv + h] = sigmoid_f(b);
+  }
+}
+
+// state update: one CTA per sequence. The new state holds the last W-1 inputs of (old state ++ chunk).
+template <typename ST>
+__global__ void gdn_conv_state_update_kernel(const __nv_bfloat16* __restrict__ proj, int64_t ld, int C, int W,
+                                             ST* __restrict__ conv_state, const int32_t* __restrict__ seq_slot,
+                                             const int32_t* __restrict__ seq_start, const int32_t* __restrict__ seq_len,
+                                             const int32_t* __restrict__ seq_has_state) {
+  const int s = blockIdx.x;
+  const int slot = seq_slot[s], st0 = seq_start[s], n = seq_len[s];
+  const bool hs = seq_has_state[s] != 0;
+  if (n <= 0) return;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float nv[8];
+    ST* cs = conv_state + ((int64_t)slot * C + c) * (W - 1);
+    for (int i = 0; i < W - 1; ++i) {
+      // element i of the new state is input (n - (W-1) + i) of the concatenation old ++ chunk
+      const int idx = n - (W - 1) + i;
+      if (idx >= 0) nv[i] = __bfloat162float(proj[(int64_t)(st0 + idx) * ld + c]);
+      else {
+        const int oi = (W - 1) + idx;
+        nv[i] = (hs && oi >= 0) ? to_f<ST>(cs[oi]) : 0.f;
+      }
+    }
+    for (int i = 0; i < W - 1; ++i) cs[i] = from_f<ST>(nv[i]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// recurrent core: grid (num_seqs, Hv, dv / 32), 128 threads.
+// thread tid: column c = tid / 4 (0..31), row group rg = tid % 4; rows i = rg + 4 r, r = 0..dk/4-1.
+// ------------------------------------------------------------------------------------------------
+template <typename ST, int DK>
+__global__ void __launch_bounds__(128) gdn_recurrent_kernel(
+    const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
+    const float* __restrict__ g, const float* __restrict__ beta, int Hk, int Hv, int dv, ST* __restrict__ state,
+    const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_start, const int32_t* __restrict__ seq_len,
+    const int32_t* __restrict__ seq_has_state, int write_state, float* __restrict__ o) {
+  constexpr int R = DK / 4;
+  constexpr int CH = 16;  // tokens staged per chunk
+  __shared__ float sq[CH][DK], sk[CH][DK], sv[CH][32], sg[CH], sb[CH];
+  const int s = blockIdx.x, h = blockIdx.y, cs = blockIdx.z;
+  const int tid = threadIdx.x, c = tid >> 2, rg = tid & 3;
+  const int col = cs * 32 + c;
+  const int kh = h / (Hv / Hk);
+  const int slot = seq_slot[s], t0 = seq_start[s], n = seq_len[s];
+  if (n <= 0 && !write_state) return;
+  ST* Sp = state + ((int64_t)slot * Hv + h) * DK * dv;
+  float S[R];
+  const bool hs = seq_has_state[s] != 0;
+#pragma unroll
+  for (int r = 0; r < R; ++r) S[r] = hs ? to_f<ST>(Sp[(int64_t)(rg + 4 * r) * dv + col]) : 0.f;
+  for (int base = 0; base < n; base += CH) {
+    const int cnt = min(CH, n - base);
+    __syncthreads();
+    for (int e = tid; e < cnt * DK; e += 128) {
+      const int tt = e / DK, i = e % DK;
+      const int64_t tok = t0 + base + tt;
+      sq[tt][i] = q[(tok * Hk + kh) * DK + i];
+      sk[tt][i] = k[(tok * Hk + kh) * DK + i];
+    }
+    for (int e = tid; e < cnt * 32; e += 128) {
+      const int tt = e / 32, cc = e % 32;
+      const int64_t tok = t0 + base + tt;
+      sv[tt][cc] = v[(tok * Hv + h) * dv + cs * 32 + cc];
+    }
+    if (tid < cnt) {
+      const int64_t tok = t0 + base + tid;
+      sg[tid] = __expf(g[tok * Hv + h]);
+      sb[tid] = beta[tok * Hv + h];
+    }
+    __syncthreads();
+    for (int tt = 0; tt < cnt; ++tt) {
+      const float decay = sg[tt];
+      float kv = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) kv += S[r] * sk[tt][rg + 4 * r];
+      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+      kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+      const float delta = sb[tt] * (sv[tt][c] - decay * kv);
+      float ov = 0.f;
+#pragma unroll
+      for (int r = 0; r < R; ++r) {
+        S[r] = S[r] * decay + sk[tt][rg + 4 * r] * delta;
+        ov += S[r] * sq[tt][rg + 4 * r];
+      }
+      ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+      ov += __shfl_xor_sync(0xffffffffu, ov, 2);
+      if (o != nullptr && rg == 0) o[((int64_t)(t0 + base + tt) * Hv + h) * dv + col] = ov;
+    }
+  }
+  if (write_state) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) Sp[(int64_t)(rg + 4 * r) * dv + col] = from_f<ST>(S[r]);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// RMSNormGated + MXFP8: one warp per (token, head), dv = 128 (4 elements per lane)
+// ------------------------------------------------------------------------------------------------
+__global__ void gdn_out_norm_quant_kernel(const float* __restrict__ o, const __nv_bfloat16* __restrict__ proj,
+                                          int64_t ld, int z_off, const __nv_bfloat16* __restrict__ w, float eps,
+                                          int T, int Hv, int dv, __nv_bfloat16* __restrict__ y,
+                                          uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (int64_t)T * Hv) return;
+  const int t = (int)(gw / Hv), h = (int)(gw % Hv);
+  const int per = dv / 32;
+  float x[8];
+  float ss = 0.f;
+  for (int i = 0; i < per; ++i) {
+    x[i] = o[((int64_t)t * Hv + h) * dv + lane + 32 * i];
+    ss += x[i] * x[i];
+  }
+  for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
+  const float rr = rsqrtf(ss / (float)dv + eps);
+  const int kblocks = Hv * dv / 32;
+  for (int i = 0; i < per; ++i) {
+    const int d = lane + 32 * i;
+    const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * dv + d]);
+    float val = x[i] * rr * __bfloat162float(w[d]) * silu_f(z);
+    val = __bfloat162float(__float2bfloat16(val));
+    if (y != nullptr) y[((int64_t)t * Hv + h) * dv + d] = __float2bfloat16(val);
+    if (out_q != nullptr) {
+      float am = fabsf(val);
+      for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
+      const int e = mx_exponent(am, 448.f);
+      out_q[(int64_t)t * Hv * dv + h * dv + d] = f32_to_e4m3(val * exp2i(-e));
+      if (lane == 0) out_sf[sf_offset(t, (h * dv + 32 * i) >> 5, kblocks)] = (uint8_t)(e + 127);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host wrappers
+// ------------------------------------------------------------------------------------------------
+void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv, int64_t b_off, int64_t a_off,
+                   torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor tok_slot, torch::Tensor tok_pos,
+                   torch::Tensor tok_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor q_out,
+                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out) {
+  const int64_t T = proj.size(0);
+  if (T == 0) return;
+  const int64_t C = 2 * Hk * dk + Hv * dv;
+  const int W = (int)conv_w.size(1);
+  TORCH_CHECK(conv_state.size(-1) == W - 1 && conv_state.size(1) == C, "gdn_conv_prep: conv state shape");
+  const at::cuda::CUDAGuard guard(proj.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const size_t smem = C * sizeof(float);
+#define R9K_CONV(ST_T)                                                                                                \
+  {                                                                                                                   \
+    auto kern = gdn_conv_prep_kernel<ST_T>;                                                                           \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
+    kern<<<T, 512, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk,      \
+                               (int)Hv, (int)dk, (int)dv, (int)b_off, (int)a_off,                                     \
+                               reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()), W,                         \
+                               reinterpret_cast<const ST_T*>(conv_state.data_ptr()), tok_slot.data_ptr<int32_t>(),    \
+                               tok_pos.data_ptr<int32_t>(), tok_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(), \
+                               dt_bias.data_ptr<float>(), q_out.data_ptr<float>(), k_out.data_ptr<float>(),           \
+                               v_out.data_ptr<float>(), g_out.data_ptr<float>(), beta_out.data_ptr<float>());        \
+  }
+  if (conv_state.dtype() == torch::kFloat32) R9K_CONV(float) else R9K_CONV(__nv_bfloat16)
+#undef R9K_CONV
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::Tensor seq_slot,
+                           torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_has_state) {
+  const int64_t S = seq_slot.size(0);
+  if (S == 0) return;
+  const int C = (int)conv_state.size(1);
+  const int W = (int)conv_state.size(2) + 1;
+  TORCH_CHECK(W - 1 <= 8, "conv width <= 9");
+  const at::cuda::CUDAGuard guard(proj.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  if (conv_state.dtype() == torch::kFloat32)
+    gdn_conv_state_update_kernel<float><<<S, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W, conv_state.data_ptr<float>(),
+        seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(),
+        seq_has_state.data_ptr<int32_t>());
+  else
+    gdn_conv_state_update_kernel<__nv_bfloat16><<<S, 256, 0, st>>>(
+        reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W,
+        reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr()), seq_slot.data_ptr<int32_t>(),
+        seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                   torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
+                   torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o) {
+  const int64_t S = seq_slot.size(0);
+  if (S == 0) return;
+  const int Hk = (int)q.size(1), DK = (int)q.size(2);
+  const int Hv = (int)v.size(1), dv = (int)v.size(2);
+  TORCH_CHECK(dv % 32 == 0 && DK == 128, "gdn_recurrent: dk 128, dv % 32");
+  TORCH_CHECK(state.size(1) == Hv && state.size(2) == DK && state.size(3) == dv, "gdn_recurrent: state shape");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  dim3 grid((unsigned)S, (unsigned)Hv, (unsigned)(dv / 32));
+  float* op = (o.has_value() && o->defined()) ? o->data_ptr<float>() : nullptr;
+  if (state.dtype() == torch::kFloat32)
+    gdn_recurrent_kernel<float, 128><<<grid, 128, 0, st>>>(
+        q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), Hk,
+        Hv, dv, state.data_ptr<float>(), seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(),
+        seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(), write_state ? 1 : 0, op);
+  else
+    gdn_recurrent_kernel<__nv_bfloat16, 128><<<grid, 128, 0, st>>>(
+        q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), Hk,
+        Hv, dv, reinterpret_cast<__nv_bfloat16*>(state.data_ptr()), seq_slot.data_ptr<int32_t>(),
+        seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(),
+        write_state ? 1 : 0, op);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torch::Tensor w, double eps,
+                        c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> out_q,
+                        c10::optional<torch::Tensor> out_sf) {
+  const int64_t T = o.size(0), Hv = o.size(1), dv = o.size(2);
+  if (T == 0) return;
+  TORCH_CHECK(dv % 32 == 0 && dv <= 256, "gdn_out_norm_quant: dv");
+  const at::cuda::CUDAGuard guard(o.device());
+  const int64_t warps = T * Hv;
+  const int blocks = (int)((warps * 32 + 255) / 256);
+  gdn_out_norm_quant_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      o.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)z_off,
+      reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps, (int)T, (int)Hv, (int)dv,
+      (y.has_value() && y->defined()) ? reinterpret_cast<__nv_bfloat16*>(y->data_ptr()) : nullptr,
+      (out_q.has_value() && out_q->defined()) ? out_q->data_ptr<uint8_t>() : nullptr,
+      (out_sf.has_value() && out_sf->defined()) ? out_sf->data_ptr<uint8_t>() : nullptr);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

@@ -1,0 +1,76 @@
+"""Public serving API.
+
+    llm = LLM(tiny_hybrid(), EngineConfig(max_batch=4))
+    outs = llm.generate([[1, 2, 3]], SamplingParams(max_tokens=8))
+
+``LLM`` owns the model (one tensor-parallel rank per process), the paged KV cache and recurrent-state
+pools, the scheduler and the model runner. ``add_request`` / ``step`` expose the engine loop for
+benchmarks and servers; ``generate`` runs it to completion.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..models.config import EngineConfig, HybridConfig, ParallelConfig
+from .runner import ModelRunner
+from .scheduler import SamplingParams, Scheduler, Sequence
+
+
+class LLM:
+    def __init__(self, model_cfg, engine_cfg: EngineConfig | None = None, par: ParallelConfig | None = None,
+                 device=None, seed: int = 0, comm=None, model=None):
+        self.engine_cfg = ec = engine_cfg or EngineConfig()
+        self.par = par or ParallelConfig()
+        if device is None:
+            device = torch.device("cuda", torch.cuda.current_device())
+        self.device = torch.device(device)
+        if model is None:
+            model = build_model(model_cfg, self.par, self.device, seed=seed, comm=comm)
+        self.model = model
+        blocks_per_seq = math.ceil(ec.max_model_len / ec.kv_block)
+        num_blocks = ec.num_kv_blocks or (ec.max_batch * blocks_per_seq + 1)
+        num_slots = ec.max_batch + 1
+        model.alloc_caches(num_blocks, num_slots, ec.kv_block)
+        self.scheduler = Scheduler(num_blocks, num_slots, ec.kv_block, ec.max_batch, ec.max_prefill_tokens,
+                                   ec.max_model_len)
+        max_tokens = max(ec.max_prefill_tokens, ec.max_batch * (1 + ec.spec_tokens))
+        self.runner = ModelRunner(model, ec, ec.kv_block, max_tokens, ec.max_batch, blocks_per_seq)
+        if ec.cuda_graphs:
+            self.runner.capture_decode_graphs()
+
+    # ------------------------------------------------------------------------------------------
+    def add_request(self, prompt: list[int], params: SamplingParams | None = None) -> Sequence:
+        seq = Sequence(list(prompt), params or SamplingParams())
+        self.scheduler.add(seq)
+        return seq
+
+    def step(self) -> list[Sequence]:
+        """One engine step (a prefill chunk or a decode step). Returns sequences that finished."""
+        out = self.scheduler.schedule()
+        if out.kind == "idle":
+            return []
+        toks = self.runner.execute(out)
+        return self.scheduler.finish_step(out, toks)
+
+    def has_unfinished(self) -> bool:
+        return self.scheduler.has_work
+
+    def generate(self, prompts: list[list[int]], params: SamplingParams | None = None) -> list[list[int]]:
+        seqs = [self.add_request(p, params) for p in prompts]
+        while self.has_unfinished():
+            self.step()
+        return [s.output for s in seqs]
+
+
+def build_model(cfg, par, device, seed=0, comm=None):
+    if isinstance(cfg, HybridConfig):
+        if cfg.moe_experts:
+            from ..models.hybrid_moe import HybridMoELM
+
+            return HybridMoELM(cfg, par, device, seed=seed, comm=comm)
+        from ..models.hybrid import HybridLM
+
+        return HybridLM(cfg, par, device, seed=seed, comm=comm)
+    raise TypeError(f"unsupported model config {type(cfg)}")

@@ -1,0 +1,255 @@
+"""Model runner: step metadata, CUDA graphs for decode, sampling.
+
+Per step the host packs every int32 metadata field into one pinned buffer with a layout that depends
+only on (tokens, sequences, block-table width), issues one ``cudaMemcpyAsync`` into a device buffer of
+the same layout and runs the model on views of it. Decode steps replay a CUDA graph captured per
+padded batch size (padding rows are real one-token sequences on the reserved block 0 / state slot 0,
+so they never touch live memory). Prefill steps run eagerly.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+import torch
+
+from ..models.hybrid import StepMeta
+from .scheduler import SchedulerOutput
+
+_FIELDS_T = ["input_ids", "positions", "slots", "tok_seq", "tok_ctx", "tok_state_slot", "tok_pos_in_chunk",
+             "tok_has_state"]
+_FIELDS_S = ["seq_state_slot", "seq_start", "seq_len", "seq_has_state"]
+
+
+@dataclass
+class Layout:
+    T: int
+    S: int
+    MB: int
+    R: int
+
+    def offsets(self):
+        off, o = {}, 0
+        for f in _FIELDS_T:
+            off[f] = o
+            o += self.T
+        for f in _FIELDS_S:
+            off[f] = o
+            o += self.S
+        off["logits_idx"] = o
+        o += self.R
+        off["block_table"] = o
+        o += self.S * self.MB
+        return off, o
+
+
+class MetaBuffers:
+    def __init__(self, device, capacity: int):
+        self.device = device
+        self.capacity = capacity
+        self.host = torch.zeros(capacity, dtype=torch.int32, pin_memory=True)
+        self.dev = torch.zeros(capacity, dtype=torch.int32, device=device)
+        self._views: dict[tuple, StepMeta] = {}
+
+    def views(self, lay: Layout, write_state: bool = True) -> StepMeta:
+        key = (lay.T, lay.S, lay.MB, lay.R, write_state)
+        m = self._views.get(key)
+        if m is None:
+            off, total = lay.offsets()
+            assert total <= self.capacity, "metadata buffer too small"
+            d = self.dev
+            kw = {f: d[off[f] : off[f] + lay.T] for f in _FIELDS_T}
+            kw.update({f: d[off[f] : off[f] + lay.S] for f in _FIELDS_S})
+            kw["logits_idx"] = d[off["logits_idx"] : off["logits_idx"] + lay.R]
+            kw["block_table"] = d[off["block_table"] : off["block_table"] + lay.S * lay.MB].view(lay.S, lay.MB)
+            m = StepMeta(write_state=write_state, **kw)
+            self._views[key] = m
+        return m
+
+
+def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft: dict | None = None):
+    """Host-side metadata for a scheduled step. Returns (Layout, np.int32 array, sample_rows, chunks)."""
+    chunks = out.chunks
+    S_real = len(chunks)
+    S = max(S_real, pad_to_seqs)
+    toks, pos, slots, tseq, tctx, tslot, tpic, ths = [], [], [], [], [], [], [], []
+    sslot, sstart, slen, shs = [], [], [], []
+    logits_idx = []
+    MB = 1
+    for ch in chunks:
+        MB = max(MB, len(ch.seq.blocks))
+    MB = max(MB, 1)
+    bt = np.zeros((S, MB), dtype=np.int32)
+    t = 0
+    for i, ch in enumerate(chunks):
+        seq = ch.seq
+        all_toks = seq.tokens
+        ids = all_toks[ch.start : ch.start + ch.n]
+        if draft is not None and seq.seq_id in draft:
+            ids = ids + draft[seq.seq_id]
+        n = len(ids)
+        p = np.arange(ch.start, ch.start + n, dtype=np.int64)
+        blocks = np.asarray(seq.blocks, dtype=np.int64)
+        toks.extend(ids)
+        pos.extend(p.tolist())
+        slots.extend((blocks[p // block_size] * block_size + p % block_size).tolist())
+        tseq.extend([i] * n)
+        tctx.extend((p + 1).tolist())
+        tslot.extend([seq.state_slot] * n)
+        tpic.extend(range(n))
+        hs = 1 if ch.start > 0 else 0
+        ths.extend([hs] * n)
+        sslot.append(seq.state_slot)
+        sstart.append(t)
+        slen.append(n)
+        shs.append(hs)
+        bt[i, : len(seq.blocks)] = seq.blocks
+        if ch.sample:
+            if draft is not None and seq.seq_id in draft:
+                logits_idx.extend(range(t + ch.n - 1, t + n))
+            else:
+                logits_idx.append(t + n - 1)
+        t += n
+    # padding sequences: one token each on block 0 / state slot 0, no KV write
+    for i in range(S_real, S):
+        toks.append(0); pos.append(0); slots.append(-1); tseq.append(i); tctx.append(1)
+        tslot.append(0); tpic.append(0); ths.append(0)
+        sslot.append(0); sstart.append(t); slen.append(1); shs.append(0)
+        logits_idx.append(t)
+        t += 1
+    T = t
+    R = len(logits_idx)
+    lay = Layout(T, S, MB, R)
+    off, total = lay.offsets()
+    arr = np.zeros(total, dtype=np.int32)
+    for name, vals in (("input_ids", toks), ("positions", pos), ("slots", slots), ("tok_seq", tseq),
+                       ("tok_ctx", tctx), ("tok_state_slot", tslot), ("tok_pos_in_chunk", tpic),
+                       ("tok_has_state", ths), ("seq_state_slot", sslot), ("seq_start", sstart),
+                       ("seq_len", slen), ("seq_has_state", shs), ("logits_idx", logits_idx)):
+        arr[off[name] : off[name] + len(vals)] = vals
+    arr[off["block_table"] : off["block_table"] + S * MB] = bt.reshape(-1)
+    return lay, arr
+
+
+class ModelRunner:
+    def __init__(self, model, engine_cfg, block_size: int, max_tokens: int, max_seqs: int, max_blocks_per_seq: int):
+        self.model = model
+        self.cfg = engine_cfg
+        self.device = model.device
+        self.block_size = block_size
+        self.max_blocks_per_seq = max_blocks_per_seq
+        self.max_tokens = max_tokens
+        self.max_seqs = max_seqs
+        self.ws = model.alloc_workspace(max_tokens, max(max_seqs * (1 + engine_cfg.spec_tokens), max_seqs))
+        cap = 8 * max_tokens + 5 * max_seqs + 2 * max_tokens + max_seqs * max_blocks_per_seq + 64
+        self.meta = MetaBuffers(self.device, cap)
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_pool = None
+        self.sample_out = torch.zeros(self.ws.logit_rows, dtype=torch.int64, device=self.device)
+        self.sample_host = torch.zeros(self.ws.logit_rows, dtype=torch.int64, pin_memory=True)
+        self.stream = torch.cuda.current_stream(self.device)
+        self.h2d_bytes = 0
+        self.d2h_bytes = 0
+
+    # ------------------------------------------------------------------------------------------
+    def _upload(self, arr: np.ndarray) -> None:
+        n = arr.size
+        self.meta.host[:n].numpy()[:] = arr
+        self.meta.dev[:n].copy_(self.meta.host[:n], non_blocking=True)
+        self.h2d_bytes = n * 4
+
+    def _graph_bs(self, S: int) -> int | None:
+        if not self.cfg.cuda_graphs:
+            return None
+        for b in sorted(self.cfg.graph_batch_sizes):
+            if b >= S and b in self.graphs:
+                return b
+        return None
+
+    def capture_decode_graphs(self, max_blocks: int | None = None) -> None:
+        """Capture one decode graph per batch size on padding-only batches."""
+        from .scheduler import SchedulerOutput
+
+        mb = max_blocks or self.max_blocks_per_seq
+        for b in sorted(self.cfg.graph_batch_sizes):
+            if b > self.max_seqs:
+                continue
+            lay, arr = pack_step(SchedulerOutput("decode", []), self.block_size, pad_to_seqs=b)
+            lay = Layout(lay.T, lay.S, mb, lay.R)
+            off, total = lay.offsets()
+            arr2 = np.zeros(total, dtype=np.int32)
+            small_off, _ = Layout(b, b, 1, b).offsets()
+            for k in off:
+                if k == "block_table":
+                    continue
+                ln = lay.T if k in _FIELDS_T else (lay.S if k in _FIELDS_S else lay.R)
+                arr2[off[k] : off[k] + ln] = arr[small_off[k] : small_off[k] + ln]
+            self._upload(arr2)
+            meta = self.meta.views(lay)
+            s = torch.cuda.Stream(self.device)
+            s.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(s):
+                for _ in range(2):
+                    self.model.forward(meta, self.ws, lay.T, lay.R)
+                    torch.argmax(self.ws.logits[: lay.R], dim=-1, out=self.sample_out[: lay.R])
+            torch.cuda.current_stream(self.device).wait_stream(s)
+            torch.cuda.synchronize(self.device)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, pool=self.graph_pool):
+                self.model.forward(meta, self.ws, lay.T, lay.R)
+                torch.argmax(self.ws.logits[: lay.R], dim=-1, out=self.sample_out[: lay.R])
+            self.graph_pool = g.pool()
+            self.graphs[b] = g
+        torch.cuda.synchronize(self.device)
+
+    # ------------------------------------------------------------------------------------------
+    def execute(self, out: SchedulerOutput, sample: bool = True, draft=None, write_state: bool = True):
+        """Run one scheduled step. Returns {seq_id: [token, ...]} (one token per sampled row)."""
+        if not out.chunks:
+            return {}
+        gb = self._graph_bs(len(out.chunks)) if (out.kind == "decode" and draft is None) else None
+        if gb is not None:
+            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb)
+            lay_g = Layout(lay.T, lay.S, self.max_blocks_per_seq, lay.R)
+            arr = _relayout(arr, lay, lay_g)
+            self._upload(arr)
+            self.graphs[gb].replay()
+            R = lay.R
+        else:
+            lay, arr = pack_step(out, self.block_size, draft=draft)
+            self._upload(arr)
+            meta = self.meta.views(lay, write_state=write_state)
+            self.model.forward(meta, self.ws, lay.T, lay.R)
+            R = lay.R
+            torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
+        if not sample:
+            return {}
+        self.sample_host[:R].copy_(self.sample_out[:R], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.d2h_bytes = R * 8
+        toks = self.sample_host[:R].tolist()
+        res: dict[int, list[int]] = {}
+        r = 0
+        for ch in out.chunks:
+            if not ch.sample:
+                continue
+            nd = len(draft[ch.seq.seq_id]) if draft is not None and ch.seq.seq_id in draft else 0
+            res[ch.seq.seq_id] = toks[r : r + 1 + nd]
+            r += 1 + nd
+        return res
+
+
+def _relayout(arr: np.ndarray, src: Layout, dst: Layout) -> np.ndarray:
+    so, _ = src.offsets()
+    do, total = dst.offsets()
+    out = np.zeros(total, dtype=np.int32)
+    for k in so:
+        if k == "block_table":
+            bt = arr[so[k] : so[k] + src.S * src.MB].reshape(src.S, src.MB)
+            full = np.zeros((dst.S, dst.MB), dtype=np.int32)
+            full[: src.S, : src.MB] = bt
+            out[do[k] : do[k] + dst.S * dst.MB] = full.reshape(-1)
+        else:
+            ln = src.T if k in _FIELDS_T else (src.S if k in _FIELDS_S else src.R)
+            out[do[k] : do[k] + ln] = arr[so[k] : so[k] + ln]
+    return out

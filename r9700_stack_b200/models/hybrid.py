@@ -1,0 +1,301 @@
+"""Hybrid Gated-DeltaNet / full-attention decoder on the sm_100a kernel library.
+
+Layer pattern: three GDN layers then one gated full-attention layer (``full_attn_interval``), each
+followed by a SwiGLU FFN (dense, or routed MoE in the Flash-Next class). This is the architecture
+class of the reference's Qwen3.5/3.8 dense and Flash-Next models (r9700_vllm/models/qwen3_5.py,
+r9700_vllm/models/qwen4_exp.py, r9700_vllm/models/gdn.py).
+
+Tensor parallelism: heads, FFN columns and experts are sharded over ``tp_size`` ranks; the outputs of
+o_proj / out_proj / down_proj are partial sums reduced by ``comm.all_reduce_`` (the fused NVLink
+kernels of ``parallel`` or NCCL), and the residual add is fused into the next RMSNorm.
+
+Every op writes into a preallocated :class:`Workspace`, so a decode step is capturable in a CUDA
+graph.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native
+from ..ops import linear as L
+from .config import HybridConfig, ParallelConfig
+from .weights import WeightFactory, from_float
+
+
+def _ops():
+    return _native.ops()
+
+
+class NoComm:
+    world_size = 1
+    rank = 0
+
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        return t
+
+    def all_gather_lastdim(self, t: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        if out is not None:
+            out.copy_(t)
+            return out
+        return t
+
+
+# ------------------------------------------------------------------------------------------------
+# step metadata (device tensors; the runner fills static copies for graph replay)
+# ------------------------------------------------------------------------------------------------
+@dataclass
+class StepMeta:
+    input_ids: torch.Tensor  # [T] int32
+    positions: torch.Tensor  # [T] int32
+    slots: torch.Tensor  # [T] int32 KV slot (-1 = padding)
+    tok_seq: torch.Tensor  # [T] int32 row in block_table
+    tok_ctx: torch.Tensor  # [T] int32 attention context length (pos + 1)
+    block_table: torch.Tensor  # [S, max_blocks] int32
+    # GDN
+    tok_state_slot: torch.Tensor  # [T] int32
+    tok_pos_in_chunk: torch.Tensor  # [T] int32
+    tok_has_state: torch.Tensor  # [T] int32
+    seq_state_slot: torch.Tensor  # [S] int32
+    seq_start: torch.Tensor  # [S] int32
+    seq_len: torch.Tensor  # [S] int32
+    seq_has_state: torch.Tensor  # [S] int32
+    logits_idx: torch.Tensor  # [R] int32 rows of the token batch whose logits are needed
+    write_state: bool = True  # False during speculative verification
+
+
+class Workspace:
+    """Persistent activation buffers for up to ``max_tokens`` tokens."""
+
+    def __init__(self, model: "HybridLM", max_tokens: int, max_logit_rows: int):
+        c, dev = model.cfg, model.device
+        H = c.hidden
+        self.max_tokens = max_tokens
+        self.resid = torch.zeros(max_tokens, H, dtype=torch.bfloat16, device=dev)
+        self.y = torch.zeros(max_tokens, H, dtype=torch.bfloat16, device=dev)  # mixer / ffn partial output
+        self.norm_out = torch.zeros(max_tokens, H, dtype=torch.bfloat16, device=dev)
+        self.act = L.alloc_act(max_tokens, H, dev)
+        a = model.attn_dims
+        self.qkv = torch.zeros(max_tokens, a["qkv_rows"], dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros(max_tokens, a["hq"], c.head_dim, dtype=torch.bfloat16, device=dev)
+        self.attn_act = L.alloc_act(max_tokens, a["hq"] * c.head_dim, dev)
+        self.attn_bf16 = torch.zeros(max_tokens, a["hq"] * c.head_dim, dtype=torch.bfloat16, device=dev)
+        g = model.gdn_dims
+        self.proj = torch.zeros(max_tokens, g["proj_rows"], dtype=torch.bfloat16, device=dev)
+        self.gq = torch.zeros(max_tokens, g["hk"], c.gdn_head_dim, dtype=torch.float32, device=dev)
+        self.gk = torch.zeros(max_tokens, g["hk"], c.gdn_head_dim, dtype=torch.float32, device=dev)
+        self.gv = torch.zeros(max_tokens, g["hv"], c.gdn_head_dim, dtype=torch.float32, device=dev)
+        self.gg = torch.zeros(max_tokens, g["hv"], dtype=torch.float32, device=dev)
+        self.gb = torch.zeros(max_tokens, g["hv"], dtype=torch.float32, device=dev)
+        self.go = torch.zeros(max_tokens, g["hv"], c.gdn_head_dim, dtype=torch.float32, device=dev)
+        self.gdn_act = L.alloc_act(max_tokens, g["hv"] * c.gdn_head_dim, dev)
+        self.gdn_bf16 = torch.zeros(max_tokens, g["hv"] * c.gdn_head_dim, dtype=torch.bfloat16, device=dev)
+        if model.ffn_local > 0:
+            self.ffn_act = L.alloc_act(max_tokens, model.ffn_local, dev)
+        self.logit_rows = max_logit_rows
+        self.final_act = L.alloc_act(max_logit_rows, H, dev)
+        self.final_bf16 = torch.zeros(max_logit_rows, H, dtype=torch.bfloat16, device=dev)
+        self.logits_local = torch.zeros(max_logit_rows, model.vocab_local, dtype=torch.float32, device=dev)
+        self.logits = torch.zeros(max_logit_rows, c.vocab, dtype=torch.float32, device=dev)
+
+
+class HybridLM:
+    def __init__(self, cfg: HybridConfig, par: ParallelConfig | None = None, device="cuda", seed: int = 0,
+                 comm=None):
+        self.cfg = cfg
+        self.par = par or ParallelConfig()
+        self.device = torch.device(device)
+        self.comm = comm or NoComm()
+        tp, r = self.par.tp_size, self.par.tp_rank
+        c = cfg
+        assert c.n_q_heads % tp == 0 and c.gdn_v_heads % tp == 0 and c.gdn_k_heads % tp == 0
+        hq = c.n_q_heads // tp
+        hkv = max(1, c.n_kv_heads // tp)  # kv heads replicate when tp > n_kv_heads
+        self.attn_dims = dict(hq=hq, hkv=hkv, qkv_rows=(2 * hq if c.attn_output_gate else hq) * c.head_dim + 2 * hkv * c.head_dim)
+        hk, hv, d = c.gdn_k_heads // tp, c.gdn_v_heads // tp, c.gdn_head_dim
+        self.gdn_dims = dict(hk=hk, hv=hv, conv_ch=2 * hk * d + hv * d, proj_rows=2 * hk * d + 2 * hv * d + 2 * hv)
+        self.ffn_local = c.ffn // tp if c.ffn else 0
+        assert c.vocab % tp == 0
+        self.vocab_local = c.vocab // tp
+        self.sm_scale = 1.0 / math.sqrt(c.head_dim)
+        self.k_scale = 1.0
+        self.v_scale = 1.0
+        self._build(seed)
+        self._rope_cache(8192 * 8)
+
+    # --------------------------------------------------------------------------------------------
+    def _build(self, seed: int):
+        c, tp, r = self.cfg, self.par.tp_size, self.par.tp_rank
+        wf = WeightFactory(self.device, seed=seed * 1000 + 17, std=c.init_std)
+        fmt = c.weight_format
+        H = c.hidden
+        # embeddings replicated on every rank (HBM is plentiful; saves an all-reduce per step)
+        self.embed = wf.randn(c.vocab, H, std=c.init_std, dtype=torch.bfloat16)
+        self.layers = []
+        a, g = self.attn_dims, self.gdn_dims
+        wf_rank = WeightFactory(self.device, seed=seed * 1000 + 31 + r, std=c.init_std)
+        for i in range(c.layers):
+            lay = {"attn": c.is_attention(i)}
+            lay["in_norm"] = wf.norm(H, c.norm_plus_one)
+            lay["post_norm"] = wf.norm(H, c.norm_plus_one)
+            if lay["attn"]:
+                lay["w_qkv"] = wf_rank.linear(a["qkv_rows"], H, fmt)
+                lay["w_o"] = wf_rank.linear(H, a["hq"] * c.head_dim, fmt)
+                lay["q_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
+                lay["k_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
+            else:
+                d = c.gdn_head_dim
+                lay["w_in"] = wf_rank.linear(g["proj_rows"], H, fmt)
+                lay["w_out"] = wf_rank.linear(H, g["hv"] * d, fmt)
+                lay["conv_w"] = wf_rank.randn(g["conv_ch"], c.conv_width, std=0.3, dtype=torch.bfloat16)
+                lay["A_log"] = torch.log(torch.empty(g["hv"], device=self.device).uniform_(1, 16, generator=wf_rank.gen))
+                lay["dt_bias"] = wf_rank.randn(g["hv"], std=0.5)
+                lay["gdn_norm"] = (1.0 + wf.randn(d, std=0.1)).to(torch.bfloat16)
+            if self.ffn_local:
+                lay["w_gate"] = wf_rank.linear(self.ffn_local, H, fmt)
+                lay["w_up"] = wf_rank.linear(self.ffn_local, H, fmt)
+                lay["w_down"] = wf_rank.linear(H, self.ffn_local, fmt)
+            self.layers.append(lay)
+        self.final_norm = wf.norm(H, c.norm_plus_one)
+        self.lm_head = wf_rank.linear(self.vocab_local, H, c.lm_head_format)
+        self.mx = not isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.BF16Weight)
+
+    def _rope_cache(self, max_pos: int):
+        c = self.cfg
+        rot = c.rotary_dim
+        inv = 1.0 / (c.rope_theta ** (torch.arange(0, rot, 2, dtype=torch.float64, device=self.device) / rot))
+        t = torch.arange(max_pos, dtype=torch.float64, device=self.device)
+        f = torch.outer(t, inv)
+        self.cos_sin = torch.cat([f.cos(), f.sin()], dim=-1).float().contiguous()
+
+    # --------------------------------------------------------------------------------------------
+    def weight_bytes(self) -> int:
+        from .weights import weight_nbytes
+
+        n = self.embed.numel() * 2 + weight_nbytes(self.lm_head)
+        for lay in self.layers:
+            for v in lay.values():
+                n += weight_nbytes(v)
+        return n
+
+    def alloc_workspace(self, max_tokens: int, max_logit_rows: int) -> Workspace:
+        return Workspace(self, max_tokens, max_logit_rows)
+
+    def alloc_caches(self, num_kv_blocks: int, num_state_slots: int, kv_block: int = 64):
+        c, a, g = self.cfg, self.attn_dims, self.gdn_dims
+        kv = {}
+        for i in c.attn_layers:
+            kv[i] = (
+                torch.zeros(num_kv_blocks, a["hkv"], kv_block, c.head_dim, dtype=torch.uint8, device=self.device),
+                torch.zeros(num_kv_blocks, a["hkv"], kv_block, c.head_dim, dtype=torch.uint8, device=self.device),
+            )
+        sdt = torch.float32 if c.gdn_state_dtype == "fp32" else torch.bfloat16
+        ssm, conv = {}, {}
+        for i in c.gdn_layers:
+            ssm[i] = torch.zeros(num_state_slots, g["hv"], c.gdn_head_dim, c.gdn_head_dim, dtype=sdt, device=self.device)
+            conv[i] = torch.zeros(num_state_slots, g["conv_ch"], c.conv_width - 1, dtype=sdt, device=self.device)
+        self.kv, self.ssm, self.conv = kv, ssm, conv
+
+    # --------------------------------------------------------------------------------------------
+    def _linear(self, act: L.MXAct, xb: torch.Tensor, w, out: torch.Tensor):
+        if isinstance(w, L.MXWeight):
+            L.mx_linear(act, w, out=out)
+        else:
+            L.bf16_linear(xb, w, out=out)
+
+    def _norm(self, x, w, ws: Workspace, T: int, residual: bool):
+        """(residual add) + RMSNorm, producing MXFP8 (MX weights) or bf16 (bf16 weights) input."""
+        c = self.cfg
+        L.rmsnorm(
+            x[:T], w, c.rms_eps, plus_one=c.norm_plus_one,
+            residual=ws.resid[:T] if residual else None,
+            residual_out=ws.resid[:T] if residual else None,
+            out=None if self.mx else ws.norm_out[:T],
+            quant_out=ws.act.narrow(T) if self.mx else None,
+        )
+
+    def _attention(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):
+        c, a = self.cfg, self.attn_dims
+        hq, hkv, D = a["hq"], a["hkv"], c.head_dim
+        qkv = ws.qkv[:T]
+        self._linear(ws.act.narrow(T), ws.norm_out[:T], lay["w_qkv"], qkv)
+        gate_off = hq * D if c.attn_output_gate else -1
+        k_off = (2 * hq if c.attn_output_gate else hq) * D
+        v_off = k_off + hkv * D
+        kc, vc = self.kv[i]
+        _ops().qk_norm_rope_cache(qkv, hq, hkv, 0, k_off, v_off, lay["q_norm"], lay["k_norm"], c.rms_eps,
+                                  c.norm_plus_one, meta.positions, self.cos_sin, c.rotary_dim, meta.slots,
+                                  ws.q[:T], kc, vc, self.k_scale, self.v_scale)
+        gate = qkv[:, gate_off:gate_off + hq * D] if gate_off >= 0 else None
+        if self.mx:
+            _ops().paged_attention(ws.q[:T], kc, vc, meta.block_table, meta.tok_seq, meta.tok_ctx, self.sm_scale,
+                                   self.k_scale, self.v_scale, gate, None, ws.attn_act.q[:T], ws.attn_act.sf, 0)
+        else:
+            _ops().paged_attention(ws.q[:T], kc, vc, meta.block_table, meta.tok_seq, meta.tok_ctx, self.sm_scale,
+                                   self.k_scale, self.v_scale, gate, ws.attn_bf16[:T], None, None, 0)
+        self._linear(ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"], ws.y[:T])
+
+    def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):
+        c, g = self.cfg, self.gdn_dims
+        hk, hv, d = g["hk"], g["hv"], c.gdn_head_dim
+        proj = ws.proj[:T]
+        self._linear(ws.act.narrow(T), ws.norm_out[:T], lay["w_in"], proj)
+        z_off = 2 * hk * d + hv * d
+        b_off = z_off + hv * d
+        a_off = b_off + hv
+        ssm, conv = self.ssm[i], self.conv[i]
+        o = _ops()
+        o.gdn_conv_prep(proj, hk, hv, d, d, b_off, a_off, lay["conv_w"], conv, meta.tok_state_slot,
+                        meta.tok_pos_in_chunk, meta.tok_has_state, lay["A_log"], lay["dt_bias"],
+                        ws.gq[:T], ws.gk[:T], ws.gv[:T], ws.gg[:T], ws.gb[:T])
+        if meta.write_state:
+            o.gdn_conv_state_update(proj, conv, meta.seq_state_slot, meta.seq_start, meta.seq_len, meta.seq_has_state)
+        o.gdn_recurrent(ws.gq[:T], ws.gk[:T], ws.gv[:T], ws.gg[:T], ws.gb[:T], ssm, meta.seq_state_slot,
+                        meta.seq_start, meta.seq_len, meta.seq_has_state, meta.write_state, ws.go[:T])
+        if self.mx:
+            o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, None, ws.gdn_act.q[:T],
+                                 ws.gdn_act.sf)
+        else:
+            o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, ws.gdn_bf16[:T], None, None)
+        self._linear(ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"], ws.y[:T])
+
+    def _ffn(self, lay, ws: Workspace, T: int):
+        if self.mx:
+            L.mx_swiglu(ws.act.narrow(T), lay["w_gate"], lay["w_up"], out=ws.ffn_act.narrow(T))
+            L.mx_linear(ws.ffn_act.narrow(T), lay["w_down"], out=ws.y[:T])
+        else:
+            raise NotImplementedError("bf16 dense FFN path")
+
+    def forward(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
+        """Run T tokens; returns fp32 logits [R, vocab] for the rows in meta.logits_idx[:R]."""
+        c = self.cfg
+        torch.index_select(self.embed, 0, meta.input_ids[:T], out=ws.resid[:T])
+        first = True
+        for i, lay in enumerate(self.layers):
+            # input norm: the residual add of the previous sublayer's output is fused in
+            if first:
+                self._norm(ws.resid, lay["in_norm"], ws, T, residual=False)
+                first = False
+            else:
+                self._norm(ws.y, lay["in_norm"], ws, T, residual=True)
+            if lay["attn"]:
+                self._attention(i, lay, meta, ws, T)
+            else:
+                self._gdn(i, lay, meta, ws, T)
+            self.comm.all_reduce_(ws.y[:T])
+            self._norm(ws.y, lay["post_norm"], ws, T, residual=True)
+            self._ffn(lay, ws, T)
+            self.comm.all_reduce_(ws.y[:T])
+        # final: residual add + norm on the rows that need logits
+        L.rmsnorm(ws.y[:T], self.final_norm, c.rms_eps, plus_one=c.norm_plus_one, residual=ws.resid[:T],
+                  residual_out=ws.resid[:T], out=ws.norm_out[:T])
+        rows = ws.final_bf16[:R]
+        torch.index_select(ws.norm_out[:T], 0, meta.logits_idx[:R], out=rows)
+        if isinstance(self.lm_head, L.MXWeight):
+            L.quant_act(rows, out=ws.final_act.narrow(R))
+            L.mx_linear(ws.final_act.narrow(R), self.lm_head, out=ws.logits_local[:R])
+        else:
+            L.bf16_linear(rows, self.lm_head, out=ws.logits_local[:R])
+        return self.comm.all_gather_lastdim(ws.logits_local[:R], out=ws.logits[:R])

@@ -1,0 +1,182 @@
+"""Plain-PyTorch fp32 restatement of the hybrid decoder, used as the oracle for the fused kernels.
+
+It reads the same weights as :class:`HybridLM` (dequantised to fp32) and applies the same
+quantisation points (MXFP8 activations before MX GEMMs, e4m3 KV cache, bf16 residual stream), but
+every op is a textbook torch expression: no custom kernel runs here.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as Fn
+
+from ..ops import linear as L
+from ..quant import formats as F
+
+
+def fake_mxfp8(x: torch.Tensor) -> torch.Tensor:
+    """Quantise rows to MXFP8 and back (block 32 along the last dim), in fp32 on x's device."""
+    shp = x.shape
+    b = x.float().reshape(-1, shp[-1] // 32, 32)
+    amax = b.abs().amax(-1)
+    e = F.mx_exponent(amax.cpu(), F.E4M3_MAX).to(x.device)
+    s = torch.ldexp(torch.ones_like(amax), e)
+    q = (b / s[..., None]).clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    return (q * s[..., None]).reshape(shp)
+
+
+def e4m3_roundtrip(x: torch.Tensor) -> torch.Tensor:
+    return x.float().clamp(-448, 448).to(torch.float8_e4m3fn).float()
+
+
+def bf16(x: torch.Tensor) -> torch.Tensor:
+    return x.to(torch.bfloat16).float()
+
+
+def _w(w) -> torch.Tensor:
+    if isinstance(w, L.MXWeight):
+        return w.dequant()
+    if isinstance(w, L.BF16Weight):
+        return w.w.float()
+    return w.float()
+
+
+def _lin(x: torch.Tensor, w, mx: bool) -> torch.Tensor:
+    xin = fake_mxfp8(x) if mx else bf16(x)
+    return xin @ _w(w).T
+
+
+def rmsnorm(x, w, eps, plus_one):
+    wf = w.float() + (1.0 if plus_one else 0.0)
+    return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * wf
+
+
+class ReferenceState:
+    def __init__(self, model):
+        c = model.cfg
+        self.k = {i: [] for i in c.attn_layers}
+        self.v = {i: [] for i in c.attn_layers}
+        g = model.gdn_dims
+        self.S = {i: torch.zeros(g["hv"], c.gdn_head_dim, c.gdn_head_dim, device=model.device) for i in c.gdn_layers}
+        self.conv = {i: torch.zeros(g["conv_ch"], c.conv_width - 1, device=model.device) for i in c.gdn_layers}
+        self.pos = 0
+
+
+@torch.no_grad()
+def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Tensor:
+    """Process `tokens` (continuing from `st`); returns fp32 logits [len(tokens), vocab_local]."""
+    c, dev = model.cfg, model.device
+    mx = model.mx
+    T = len(tokens)
+    pos = torch.arange(st.pos, st.pos + T, device=dev)
+    resid = model.embed[torch.tensor(tokens, device=dev)].float()
+    y = None
+    for i, lay in enumerate(model.layers):
+        if y is not None:
+            resid = bf16(resid + y)
+        h = rmsnorm(resid, lay["in_norm"], c.rms_eps, c.norm_plus_one)
+        if lay["attn"]:
+            y = bf16(_attn(model, i, lay, h, pos, st, mx))
+        else:
+            y = bf16(_gdn(model, i, lay, h, st, mx))
+        resid = bf16(resid + y)
+        h = rmsnorm(resid, lay["post_norm"], c.rms_eps, c.norm_plus_one)
+        g = _lin(h, lay["w_gate"], mx)
+        u = _lin(h, lay["w_up"], mx)
+        y = bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
+    resid = bf16(resid + y)
+    h = bf16(rmsnorm(resid, model.final_norm, c.rms_eps, c.norm_plus_one))
+    lm_mx = isinstance(model.lm_head, L.MXWeight)
+    logits = (fake_mxfp8(h) if lm_mx else h) @ _w(model.lm_head).T
+    st.pos += T
+    # recurrent state is stored in the state dtype between steps
+    if c.gdn_state_dtype == "bf16":
+        for k in st.S:
+            st.S[k] = bf16(st.S[k])
+            st.conv[k] = bf16(st.conv[k])
+    return logits
+
+
+def _rope(x, pos, rot, theta):
+    half = rot // 2
+    inv = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float64, device=x.device) / rot))
+    f = torch.outer(pos.double(), inv).float()
+    cos, sin = f.cos()[:, None, :], f.sin()[:, None, :]
+    x1, x2 = x[..., :half], x[..., half:rot]
+    out = x.clone()
+    out[..., :half] = x1 * cos - x2 * sin
+    out[..., half:rot] = x2 * cos + x1 * sin
+    return out
+
+
+def _attn(model, i, lay, h, pos, st, mx):
+    c, a = model.cfg, model.attn_dims
+    hq, hkv, D = a["hq"], a["hkv"], c.head_dim
+    T = h.shape[0]
+    qkv = bf16(_lin(h, lay["w_qkv"], mx))
+    q = qkv[:, : hq * D].reshape(T, hq, D)
+    gate = qkv[:, hq * D : 2 * hq * D]
+    k_off = 2 * hq * D
+    k = qkv[:, k_off : k_off + hkv * D].reshape(T, hkv, D)
+    v = qkv[:, k_off + hkv * D : k_off + 2 * hkv * D].reshape(T, hkv, D)
+    q = bf16(rmsnorm(q, lay["q_norm"], c.rms_eps, c.norm_plus_one))
+    k = bf16(rmsnorm(k, lay["k_norm"], c.rms_eps, c.norm_plus_one))
+    q = bf16(_rope(q, pos, c.rotary_dim, c.rope_theta))
+    k = _rope(k, pos, c.rotary_dim, c.rope_theta)
+    st.k[i].append(e4m3_roundtrip(bf16(k)))
+    st.v[i].append(e4m3_roundtrip(v))
+    K = torch.cat(st.k[i], 0)  # [ctx, hkv, D]
+    V = torch.cat(st.v[i], 0)
+    ctx = K.shape[0]
+    G = hq // hkv
+    Kx = K.repeat_interleave(G, dim=1)
+    Vx = V.repeat_interleave(G, dim=1)
+    s = torch.einsum("thd,chd->thc", q, Kx) * model.sm_scale
+    qpos = pos[:, None]
+    kpos = torch.arange(ctx, device=h.device)[None, :]
+    s = s.masked_fill((kpos > qpos)[:, None, :], float("-inf"))
+    p = torch.softmax(s, dim=-1)
+    o = torch.einsum("thc,chd->thd", p, Vx).reshape(T, hq * D)
+    o = bf16(o * torch.sigmoid(gate))
+    return _lin(o, lay["w_o"], mx)
+
+
+def _gdn(model, i, lay, h, st, mx):
+    c, g = model.cfg, model.gdn_dims
+    hk, hv, d = g["hk"], g["hv"], c.gdn_head_dim
+    T = h.shape[0]
+    proj = bf16(_lin(h, lay["w_in"], mx))
+    C = g["conv_ch"]
+    x = proj[:, :C]
+    z_off = 2 * hk * d + hv * d
+    z = proj[:, z_off : z_off + hv * d].reshape(T, hv, d)
+    b = proj[:, z_off + hv * d : z_off + hv * d + hv]
+    a = proj[:, z_off + hv * d + hv : z_off + hv * d + 2 * hv]
+    W = c.conv_width
+    full = torch.cat([st.conv[i].T, x], 0)  # [(W-1) + T, C]
+    cw = lay["conv_w"].float()
+    conv = torch.stack([(full[t : t + W] * cw.T).sum(0) for t in range(T)], 0)
+    st.conv[i] = full[-(W - 1) :].T.clone()
+    conv = Fn.silu(conv)
+    q = conv[:, : hk * d].reshape(T, hk, d)
+    k = conv[:, hk * d : 2 * hk * d].reshape(T, hk, d)
+    v = conv[:, 2 * hk * d :].reshape(T, hv, d)
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) * (d**-0.5)
+    k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    gg = -torch.exp(lay["A_log"]) * Fn.softplus(a + lay["dt_bias"])
+    beta = torch.sigmoid(b)
+    rep = hv // hk
+    S = st.S[i]
+    outs = []
+    for t in range(T):
+        kt = k[t].repeat_interleave(rep, 0)  # [hv, d]
+        qt = q[t].repeat_interleave(rep, 0)
+        S = S * torch.exp(gg[t])[:, None, None]
+        kv = torch.einsum("hij,hi->hj", S, kt)
+        delta = beta[t][:, None] * (v[t] - kv)
+        S = S + kt[:, :, None] * delta[:, None, :]
+        outs.append(torch.einsum("hij,hi->hj", S, qt))
+    st.S[i] = S
+    o = torch.stack(outs, 0)  # [T, hv, d]
+    o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + c.rms_eps) * lay["gdn_norm"].float() * Fn.silu(z)
+    o = bf16(o.reshape(T, hv * d))
+    return _lin(o, lay["w_out"], mx)
