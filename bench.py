@@ -1,0 +1,266 @@
+"""Headline benchmark: decode tok/s (1 and 16 streams) and 8k-prompt prefill tok/s of the dense hybrid
+GDN/attention 27B-class model, tensor-parallel over the job's GPUs.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W]            # this framework
+    python bench.py --impl reference ...                           # the reference (prints unavailable)
+
+For N > 1 launch with torchrun (one rank per GPU, NCCL). Weights are random N(0, 0.02) quantised to
+NVFP4 (converted to MXFP4 at load), lm_head block fp8 (-> MXFP8), fp8 KV cache; prompts are uniform
+random token ids. Rank 0 prints one JSON line.
+
+Timing: W untimed decode steps, then exactly K decode steps of 16 streams, each step's CUDA-graph replay
+bracketed by CUDA events on the launching stream; a barrier + synchronize on both sides; the max over
+ranks. Each step reads all weights (~15 GB at TP=1), far more than L2 (126 MB), so no L2 flush is
+needed. The ``e2e`` figure times the same K steps through the public ``LLM.step()`` API (host
+scheduling, per-step H2D of the step's metadata from pinned memory, D2H of the sampled tokens).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, HERE)
+
+METRIC = "decode tok/s (1 and 16 streams), prefill tok/s @8k prompt, device-timed max/rank"
+BASELINE_DECODE16 = 640.0  # reference: 27B NVFP4 TP2, 16 streams (README.md:69)
+REF_UNAVAILABLE = (
+    "reference is a ROCm/gfx1201 vLLM plugin: its platform detect() returns None on a CUDA host and its "
+    "libr9k.so kernels need hipcc for gfx1201 (absent); it has no CUDA path to run on B200"
+)
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=40)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--streams", type=int, default=16)
+    ap.add_argument("--prompt-len", type=int, default=8192)
+    ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the metric)")
+    ap.add_argument("--no-prefill-metric", action="store_true")
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self):
+        self.proc = None
+        self.path = os.path.join(HERE, "gpurun_out", "clocks.csv")
+
+    def start(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        self.fh.close()
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in open(self.path):
+            p = [x.strip() for x in line.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                clk, cmax, pw = float(p[1]), float(p[2]), float(p[3])
+            except ValueError:
+                continue
+            mx.append(cmax)
+            if pw > 300:  # under load
+                sm.append(clk)
+                for n, v in zip(names, p[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+        return {
+            "sm_mhz": statistics.median(sm) if sm else None,
+            "sm_max_mhz": max(mx) if mx else None,
+            "reasons": sorted(reasons),
+            "samples_under_load": len(sm),
+        }
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE, "metric": METRIC}))
+        return 0
+
+    import numpy as np
+    import torch
+
+    from r9700_stack_b200 import _native
+    from r9700_stack_b200.engine.llm import LLM
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.config import EngineConfig, ParallelConfig, qwen27b_hybrid
+    from r9700_stack_b200.parallel.comm import NcclComm, init_distributed
+
+    rank, world, local = init_distributed()
+    dev = torch.device("cuda", local)
+    comm = NcclComm() if world > 1 else None
+    cfg = qwen27b_hybrid()
+    if args.layers:
+        cfg = cfg.scaled(layers=args.layers)
+    S, P = args.streams, args.prompt_len
+    ec = EngineConfig(max_batch=S, max_model_len=P + args.warmup + 2 * args.steps + 64, max_prefill_tokens=P,
+                      cuda_graphs=True, graph_batch_sizes=[1, 2, 4, 8, 16])
+    t0 = time.time()
+    llm = LLM(cfg, ec, ParallelConfig(tp_size=world, tp_rank=rank), device=dev, seed=0, comm=comm)
+    build_s = time.time() - t0
+
+    def barrier_sync():
+        torch.cuda.synchronize(dev)
+        if comm is not None:
+            comm.barrier()
+        torch.cuda.synchronize(dev)
+
+    rng = np.random.default_rng(1234)
+    prompt = lambda: rng.integers(0, cfg.vocab, P).tolist()
+
+    # ---------------- prefill @8k (1 stream): one warm-up prefill, then two timed ----------------
+    prefill_ms = []
+    if not args.no_prefill_metric:
+        for it in range(3):
+            llm.add_request(prompt(), SamplingParams(max_tokens=1))
+            barrier_sync()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            llm.step()
+            e1.record()
+            barrier_sync()
+            if it > 0:
+                prefill_ms.append(e0.elapsed_time(e1))
+            assert not llm.has_unfinished()
+    prefill_ms_max = max(comm.max_scalar(m, dev) if comm else m for m in prefill_ms) if prefill_ms else None
+
+    # ---------------- decode @16 streams ----------------
+    total_new = args.warmup + 2 * args.steps + 8
+    seqs = [llm.add_request(prompt(), SamplingParams(max_tokens=total_new)) for _ in range(S)]
+    while any(not s.prefill_done or not s.output for s in seqs):
+        llm.step()
+    for _ in range(args.warmup):
+        llm.step()
+    # count this library's kernel launches in one decode step (eager run of the same step shape)
+    lc = _native.launch_counter
+    barrier_sync()
+
+    clocks = ClockSampler() if rank == 0 else None
+    if clocks:
+        clocks.start()
+    # device-timed: CUDA events around each step's graph replay
+    llm.runner.device_events = []
+    barrier_sync()
+    w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0.record()
+    for _ in range(args.steps):
+        llm.step()
+    w1.record()
+    barrier_sync()
+    dev_ms = sum(a.elapsed_time(b) for a, b in llm.runner.device_events)
+    e2e_ms = w0.elapsed_time(w1)
+    llm.runner.device_events = None
+    h2d, d2h = llm.runner.h2d_bytes, llm.runner.d2h_bytes
+    clk = clocks.stop() if clocks else None
+    dev_ms = comm.max_scalar(dev_ms, dev) if comm else dev_ms
+    e2e_ms = comm.max_scalar(e2e_ms, dev) if comm else e2e_ms
+    decode16 = S * args.steps / (dev_ms / 1e3)
+    e2e16 = S * args.steps / (e2e_ms / 1e3)
+
+    # launch count: an eager run of the decode step shape with the counter on
+    from r9700_stack_b200.engine.runner import pack_step
+    from r9700_stack_b200.engine.scheduler import ScheduledChunk, SchedulerOutput
+
+    out = SchedulerOutput("decode", [ScheduledChunk(s, s.length - 1, 1, True) for s in seqs])
+    lay, arr = pack_step(out, ec.kv_block)
+    llm.runner._upload(arr)
+    meta = llm.runner.meta.views(lay)
+    lc.count, lc.counting = 0, True
+    llm.model.forward(meta, llm.runner.ws, lay.T, lay.R)
+    lc.counting = False
+    launches_per_step = lc.count
+    torch.cuda.synchronize(dev)
+
+    # ---------------- decode @1 stream: keep one sequence ----------------
+    keep = seqs[0]
+    for s in seqs[1:]:
+        llm.scheduler.running.remove(s)
+        llm.scheduler._release(s)
+    for _ in range(3):
+        llm.step()
+    llm.runner.device_events = []
+    barrier_sync()
+    for _ in range(args.steps):
+        llm.step()
+    barrier_sync()
+    one_ms = sum(a.elapsed_time(b) for a, b in llm.runner.device_events)
+    llm.runner.device_events = None
+    one_ms = comm.max_scalar(one_ms, dev) if comm else one_ms
+    decode1 = args.steps / (one_ms / 1e3)
+
+    if rank == 0:
+        res = {
+            "metric": METRIC,
+            "value": round(decode16, 2),
+            "unit": "tok/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 4),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": round(decode16 / BASELINE_DECODE16, 3),
+            "dtype": "nvfp4->mxfp4 weights x mxfp8 activations (fp32 accumulate), fp8 KV; reference: mxfp4 x fp8",
+            "data": "synthetic: random-init N(0,0.02) weights of the named architecture, uniform random prompt ids",
+            "config": {
+                "model": "hybrid-dense-27b (BASELINE config 2: 64 layers 3:1 GDN:GQA, hidden 5120, ffn 17408, vocab 248320)",
+                "global_batch": S,
+                "seq_len": P,
+                "parallelism": f"tp{world}",
+                "l2": "inputs larger than L2: every step streams all weights (~15 GB / tp) and the KV cache",
+                "layers": cfg.layers,
+            },
+            "decode_16_streams_tok_s": round(decode16, 2),
+            "decode_1_stream_tok_s": round(decode1, 2),
+            "prefill_8k_tok_s": round(P / (prefill_ms_max / 1e3), 1) if prefill_ms_max else None,
+            "prefill_8k_ms": round(prefill_ms_max, 2) if prefill_ms_max else None,
+            "e2e": {"value": round(e2e16, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h)},
+            "gpu_launches": int(launches_per_step * args.steps),
+            "gpu_launches_per_step": int(launches_per_step),
+            "clocks": clk,
+            "build_s": round(build_s, 1),
+            "weights_gb_per_rank": round(llm.model.weight_bytes() / 1e9, 2),
+        }
+        print(json.dumps(res), flush=True)
+    if comm is not None:
+        import torch.distributed as dist
+
+        llm.runner.graphs.clear()
+        torch.cuda.synchronize(dev)
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -116,7 +116,33 @@ def available() -> bool:
         return False
 
 
+class _LaunchCounter:
+    """Proxy over ``torch.ops.r9k`` that counts op calls while ``counting`` is set.
+
+    Every op of the library launches exactly one kernel, so the count is the number of this
+    library's kernel launches (used by the benchmark's ``gpu_launches`` field)."""
+
+    def __init__(self):
+        self.counting = False
+        self.count = 0
+
+    def __getattr__(self, name):
+        fn = getattr(torch.ops.r9k, name)
+        if not self.counting:
+            return fn
+
+        def wrapped(*a, **k):
+            self.count += 1
+            return fn(*a, **k)
+
+        return wrapped
+
+
+launch_counter = _LaunchCounter()
+
+
 def ops():
     """``torch.ops.r9k`` with the native library loaded; raises if it cannot be."""
-    load_library()
-    return torch.ops.r9k
+    if not _loaded:
+        load_library()
+    return launch_counter

@@ -1,0 +1,566 @@
+// tcgen05 flash attention over the paged fp8 KV cache (sm_100a).
+//
+// One CTA = one KV head x one query tile of up to 128 rows, where a row is a (query token, q head of
+// this KV head's GQA group) pair, so the G heads of a group share every K/V byte loaded. Two modes:
+//   * decode / verify (mode 0): grid (seqs, kv heads, splits). A sequence's 1..21 query tokens form
+//     the tile and the KV range [0, ctx) is cut into `nsplit` chunks of whole 128-key tiles; each split
+//     writes an unnormalised partial (O, max, sum) that attn_combine merges.
+//   * prefill (mode 1): grid (tiles, kv heads). A host table lists (sequence, first token, tokens) per
+//     tile; each CTA covers the whole causal KV range and writes the final output directly.
+// Reference counterparts: kernels/r9k_attn.hip:226-447 (paged causal prefill, fp8 KV) and the stock
+// split-KV verify backend wrapped by r9700_vllm/attn/triton3d.py:125-290.
+//
+// Data path (all tiles 128-byte swizzled):
+//   K, V pages -> TMA (2D map over [blocks * kv_heads * 64 rows, 256 B]) -> smem, e4m3 as stored.
+//   Q rows -> e4m3 with a per-row scale, written into smem by the softmax warps.
+//   S = Q K^T : tcgen05.mma kind::f8f6f4, M=128 (rows) N=128 (keys) K=256, accumulator in TMEM
+//               (two S buffers so the next tile's QK^T overlaps this tile's softmax).
+//   softmax  : one thread per row reads its S row from TMEM, P = exp2(s - m_ref) quantised to e4m3
+//              into smem (m_ref lags the running max by up to 2^8, so P <= 256 fits e4m3; O is
+//              rescaled in TMEM only when the max grows past that).
+//   O += P V  : kind::f8f6f4 with V as an MN-major operand (d contiguous), N=256, O in TMEM.
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer (TMEM owner), warps 2-5 softmax/epilogue.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+#include "tmap.h"
+
+namespace r9k {
+
+namespace fa {
+constexpr int D = 256;
+constexpr int BLK = 64;          // KV page size (tokens)
+constexpr int KT = 128;          // keys per tile (two pages)
+constexpr int ROWS = 128;
+constexpr int Q_BYTES = ROWS * D;            // e4m3, two 16 KB swizzle atoms (d halves)
+constexpr int KV_TILE_BYTES = KT * D;        // 32 KB (two d-half atoms of 16 KB)
+constexpr int P_BYTES = ROWS * KT;           // 16 KB
+constexpr int OFF_Q = 0;
+constexpr int OFF_K = OFF_Q + Q_BYTES;       // 2 stages
+constexpr int OFF_V = OFF_K + 2 * KV_TILE_BYTES;
+constexpr int OFF_P = OFF_V + 2 * KV_TILE_BYTES;
+constexpr int OFF_BAR = OFF_P + P_BYTES;
+// barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_free[2], p_full, pv_done
+constexpr int NBAR = 1 + 2 * 6 + 2;
+constexpr int OFF_TMEM = OFF_BAR + NBAR * 8;
+constexpr int SMEM = OFF_TMEM + 16 + 1024;
+constexpr int TMEM_COLS = 512;   // O: [0,256), S0: [256,384), S1: [384,512)
+constexpr int O_COL = 0, S_COL = 256;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P <= 2^8
+}  // namespace fa
+
+struct AttnArgs {
+  const __nv_bfloat16* q;  // [T, Hq, D]
+  int Hq, Hkv, G;
+  const int32_t* block_table;
+  int max_blocks;
+  const int32_t* tok_ctx;   // [T] visible keys of each query token (position + 1)
+  const int32_t* seq_start; // mode 0: [S]
+  const int32_t* seq_len;   // mode 0: [S]
+  const int32_t* tile_tab;  // mode 1: [ntiles][3] = seq row, first token, tokens
+  int ntiles;
+  int mode;
+  float scale_log2;         // sm_scale * k_scale * log2(e)
+  float v_scale;
+  // mode 0 outputs
+  float* part_o;            // [T * Hq][nsplit][D]
+  float* part_ml;           // [T * Hq][nsplit][2]
+  int nsplit;
+  // mode 1 outputs
+  const __nv_bfloat16* gate;
+  int64_t ld_gate;
+  uint8_t* out_q;
+  uint8_t* out_sf;
+  int out_kblocks;
+  __nv_bfloat16* out_bf16;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+R9K_DEVINL uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// store 16 bytes into a 128-byte-swizzled K-major tile: row r, 16-byte chunk c
+R9K_DEVINL void st_swz16(uint8_t* tile, int r, int c, uint4 v) {
+  *reinterpret_cast<uint4*>(tile + r * 128 + ((c ^ (r & 7)) << 4)) = v;
+}
+
+R9K_DEVINL uint32_t pack4_e4m3(float a, float b, float c, float d) {
+  const uint32_t lo = (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3);
+  const uint32_t hi = (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(c, d), __NV_SATFINITE, __NV_E4M3);
+  return lo | (hi << 16);
+}
+
+__global__ void __launch_bounds__(192, 1)
+    attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  using namespace fa;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars;
+  uint64_t* k_full = bars + 1;
+  uint64_t* k_empty = bars + 3;
+  uint64_t* v_full = bars + 5;
+  uint64_t* v_empty = bars + 7;
+  uint64_t* s_full = bars + 9;
+  uint64_t* s_free = bars + 11;
+  uint64_t* p_full = bars + 13;
+  uint64_t* pv_done = bars + 14;
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + OFF_TMEM);
+
+  const int warp = warp_id(), lane = lane_id();
+  const int kvh = blockIdx.y;
+
+  // ---- work item ----
+  int seq, tok0, ntok, kv0, kv1;
+  if (a.mode == 0) {
+    seq = blockIdx.x;
+    tok0 = a.seq_start[seq];
+    ntok = a.seq_len[seq];
+    const int ctx = a.tok_ctx[tok0 + ntok - 1];
+    // each sequence's key range is cut into nsplit chunks of a multiple of 128 keys
+    const int chunk = ((ctx + a.nsplit - 1) / a.nsplit + KT - 1) / KT * KT;
+    kv0 = blockIdx.z * chunk;
+    kv1 = min(ctx, kv0 + chunk);
+  } else {
+    if ((int)blockIdx.x >= a.ntiles) return;
+    seq = a.tile_tab[blockIdx.x * 3 + 0];
+    tok0 = a.tile_tab[blockIdx.x * 3 + 1];
+    ntok = a.tile_tab[blockIdx.x * 3 + 2];
+    kv0 = 0;
+    kv1 = a.tok_ctx[tok0 + ntok - 1];
+  }
+  const int nrows = min(ROWS, ntok * a.G);
+  const int ntiles = kv1 > kv0 ? (kv1 - kv0 + KT - 1) / KT : 0;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 128);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&s_free[s], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(pv_done, 1);
+    fence_mbar_init();
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmV);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tmem_holder;
+  const int32_t* bt = a.block_table + (int64_t)seq * a.max_blocks;
+
+  if (warp == 0) {
+    // ------------------------------------ producer ------------------------------------
+    if (lane == 0) {
+      for (int j = 0; j < ntiles; ++j) {
+        const int s = j & 1;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        const int key0 = kv0 + j * KT;
+        int blk[2];
+#pragma unroll
+        for (int p = 0; p < 2; ++p) {
+          const int pi = key0 / BLK + p;
+          blk[p] = (pi < a.max_blocks && key0 + p * BLK < kv1) ? bt[pi] : 0;
+        }
+        if (!mbar_wait(&k_empty[s], ph ^ 1u, a.timeout_ns)) { report_error(a.status, kErrMbarTimeout, 200, j); break; }
+        uint8_t* ks = smem + OFF_K + s * KV_TILE_BYTES;
+        mbar_arrive_expect_tx(&k_full[s], KV_TILE_BYTES);
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(ks + h * (KT * 128) + p * (BLK * 128), &tmK, &k_full[s], h * 128, (blk[p] * a.Hkv + kvh) * BLK);
+        if (!mbar_wait(&v_empty[s], ph ^ 1u, a.timeout_ns)) { report_error(a.status, kErrMbarTimeout, 201, j); break; }
+        uint8_t* vs = smem + OFF_V + s * KV_TILE_BYTES;
+        mbar_arrive_expect_tx(&v_full[s], KV_TILE_BYTES);
+#pragma unroll
+        for (int p = 0; p < 2; ++p)
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+            tma_load_2d(vs + h * (KT * 128) + p * (BLK * 128), &tmV, &v_full[s], h * 128, (blk[p] * a.Hkv + kvh) * BLK);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------ MMA issuer ------------------------------------
+    if (lane == 0 && ntiles > 0) {
+      constexpr uint32_t idesc_s = idesc_dense(kFmtE4M3, kFmtE4M3, ROWS, KT);
+      constexpr uint32_t idesc_o = idesc_dense(kFmtE4M3, kFmtE4M3, ROWS, D) | (1u << 16);  // B (V) MN-major
+      const uint32_t sq = smem_u32(smem + OFF_Q);
+      const uint32_t sp = smem_u32(smem + OFF_P);
+      bool ok = mbar_wait(q_full, 0, a.timeout_ns);
+      if (!ok) report_error(a.status, kErrMbarTimeout, 210, 0);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j & 1;
+        const uint32_t ph = (uint32_t)((j >> 1) & 1);
+        if (!mbar_wait(&k_full[s], ph, a.timeout_ns)) return false;
+        if (!mbar_wait(&s_free[s], ph ^ 1u, a.timeout_ns)) return false;
+        tc_fence_after();
+        const uint32_t sk = smem_u32(smem + OFF_K + s * KV_TILE_BYTES);
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f8f6f4_ss(tbase + S_COL + s * KT, sdesc_k_sw128(sq + h * (ROWS * 128) + 32 * k),
+                          sdesc_k_sw128(sk + h * (KT * 128) + 32 * k), idesc_s, (h > 0 || k > 0) ? 1u : 0u);
+        tc_commit(&s_full[s]);
+        tc_commit(&k_empty[s]);
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      for (int j = 0; ok && j < ntiles; ++j) {
+        if (j + 1 < ntiles && !issue_s(j + 1)) { ok = false; break; }
+        const int s = j & 1;
+        if (!mbar_wait(p_full, (uint32_t)(j & 1), a.timeout_ns)) { ok = false; break; }
+        if (!mbar_wait(&v_full[s], (uint32_t)((j >> 1) & 1), a.timeout_ns)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t sv = smem_u32(smem + OFF_V + s * KV_TILE_BYTES);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          mma_f8f6f4_ss(tbase + O_COL, sdesc_k_sw128(sp + 32 * k), sdesc_mn_sw128(sv + k * 4096, KT * 128, 1024),
+                        idesc_o, (j > 0 || k > 0) ? 1u : 0u);
+        tc_commit(pv_done);
+        tc_commit(&v_empty[s]);
+      }
+      if (!ok) report_error(a.status, kErrMbarTimeout, 211, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------ softmax / epilogue ------------------------------------
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // TMEM lane == tile row
+    const bool valid = r < nrows;
+    const int rt = r / a.G, rg = r % a.G;
+    const int tok = tok0 + rt;
+    const int head = kvh * a.G + rg;
+    const int ctx = valid ? a.tok_ctx[tok] : 0;
+    // Q row -> e4m3 with per-row scale, into the swizzled Q tile
+    float qscale = 1.f;
+    {
+      uint8_t* sq = smem + OFF_Q;
+      float amax = 0.f;
+      const __nv_bfloat16* qr = a.q + ((int64_t)tok * a.Hq + head) * D;
+      if (valid) {
+        for (int c = 0; c < D / 8; ++c) {
+          const uint4 raw = reinterpret_cast<const uint4*>(qr)[c];
+          const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(__bfloat162float(e[i])));
+        }
+      }
+      qscale = amax > 0.f ? amax / 448.f : 1.f;
+      const float inv = 1.f / qscale;
+      for (int c = 0; c < D / 16; ++c) {  // 16 elements -> 16 bytes
+        uint4 w = make_uint4(0, 0, 0, 0);
+        if (valid) {
+          const uint4 r0 = reinterpret_cast<const uint4*>(qr)[2 * c];
+          const uint4 r1 = reinterpret_cast<const uint4*>(qr)[2 * c + 1];
+          const __nv_bfloat16* e0 = reinterpret_cast<const __nv_bfloat16*>(&r0);
+          const __nv_bfloat16* e1 = reinterpret_cast<const __nv_bfloat16*>(&r1);
+          float f[16];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) { f[i] = __bfloat162float(e0[i]) * inv; f[8 + i] = __bfloat162float(e1[i]) * inv; }
+          w.x = pack4_e4m3(f[0], f[1], f[2], f[3]);
+          w.y = pack4_e4m3(f[4], f[5], f[6], f[7]);
+          w.z = pack4_e4m3(f[8], f[9], f[10], f[11]);
+          w.w = pack4_e4m3(f[12], f[13], f[14], f[15]);
+        }
+        const int h = c / 8, cc = c % 8;
+        st_swz16(sq + h * (ROWS * 128), r, cc, w);
+      }
+      fence_proxy_async();
+      mbar_arrive(q_full);
+    }
+    const float sl2 = a.scale_log2 * qscale;
+    float m_ref = -INFINITY, l = 0.f;
+    const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
+    uint8_t* sp = smem + OFF_P;
+    bool ok = true;
+    for (int j = 0; j < ntiles; ++j) {
+      const int s = j & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[s], (uint32_t)((j >> 1) & 1), a.timeout_ns));
+      if (!ok) break;
+      tc_fence_after();
+      float sv[KT];
+#pragma unroll
+      for (int c = 0; c < KT; c += 16) tmem_ld16(trow + S_COL + s * KT + c, sv + c);
+      tmem_ld_wait();
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);
+      const int key0 = kv0 + j * KT;
+      float tmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < KT; ++c) {
+        const int key = key0 + c;
+        const bool vis = valid && key < ctx && key < kv1;
+        sv[c] = vis ? sv[c] * sl2 : -INFINITY;
+        tmax = fmaxf(tmax, sv[c]);
+      }
+      // the P buffer and O must be free: PV of the previous tile has completed
+      if (j > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)((j - 1) & 1), a.timeout_ns));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      // O is rescaled only when some row's max grew past the threshold; the decision is made per
+      // warp because tcgen05.ld/st are warp-collective
+      const bool need = (m_ref != -INFINITY) && (tmax > m_ref + RESCALE_THRESHOLD);
+      if (__any_sync(0xffffffffu, need)) {
+        const float f = need ? exp2f(m_ref - tmax) : 1.f;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          float o[16];
+          tmem_ld16(trow + O_COL + c, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] *= f;
+          tmem_st16(trow + O_COL + c, o);
+        }
+        tmem_st_wait();
+        if (need) l *= f;
+      }
+      if (need || (m_ref == -INFINITY && tmax != -INFINITY)) m_ref = tmax;
+      float lsum = 0.f;
+#pragma unroll
+      for (int c = 0; c < KT; c += 16) {
+        float p[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          p[i] = (sv[c + i] == -INFINITY) ? 0.f : exp2f(sv[c + i] - m_ref);
+          lsum += p[i];
+        }
+        uint4 w;
+        w.x = pack4_e4m3(p[0], p[1], p[2], p[3]);
+        w.y = pack4_e4m3(p[4], p[5], p[6], p[7]);
+        w.z = pack4_e4m3(p[8], p[9], p[10], p[11]);
+        w.w = pack4_e4m3(p[12], p[13], p[14], p[15]);
+        st_swz16(sp, r, c / 16, w);
+      }
+      l += lsum;
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- epilogue ----
+    if (ok && ntiles > 0) {
+      ok = __all_sync(0xffffffffu, mbar_wait(pv_done, (uint32_t)((ntiles - 1) & 1), a.timeout_ns));
+      tc_fence_after();
+    }
+    if (!ok) report_error(a.status, kErrMbarTimeout, 220, r);
+    if (a.mode == 0) {
+      const int64_t pidx = ((int64_t)tok * a.Hq + head) * a.nsplit + blockIdx.z;
+      const bool have = ntiles > 0 && ok;  // warp-uniform
+      if (have) {
+        float* po = a.part_o + pidx * D;
+#pragma unroll 1
+        for (int c = 0; c < D; c += 16) {
+          float o[16];
+          tmem_ld16(trow + O_COL + c, o);
+          tmem_ld_wait();
+          if (valid) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(po + c + i) = make_float4(o[i], o[i + 1], o[i + 2], o[i + 3]);
+          }
+        }
+      }
+      if (valid) {
+        a.part_ml[pidx * 2 + 0] = have ? m_ref : -INFINITY;
+        a.part_ml[pidx * 2 + 1] = have ? l : 0.f;
+      }
+    } else {
+      const float inv_l = (l > 0.f) ? a.v_scale / l : 0.f;
+#pragma unroll 1
+      for (int c = 0; c < D && ok && ntiles > 0; c += 32) {
+        float o[32];
+        tmem_ld16(trow + O_COL + c, o);
+        tmem_ld16(trow + O_COL + c + 16, o + 16);
+        tmem_ld_wait();
+        if (!valid) continue;
+        float am = 0.f;
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float v = o[i] * inv_l;
+          if (a.gate != nullptr) v *= sigmoid_f(__bfloat162float(a.gate[(int64_t)tok * a.ld_gate + head * D + c + i]));
+          v = __bfloat162float(__float2bfloat16(v));
+          o[i] = v;
+          am = fmaxf(am, fabsf(v));
+        }
+        const int64_t obase = (int64_t)tok * a.Hq * D + head * D + c;
+        if (a.out_bf16 != nullptr) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) a.out_bf16[obase + i] = __float2bfloat16(o[i]);
+        }
+        if (a.out_q != nullptr) {
+          const int e = mx_exponent(am, 448.f);
+          const float si = exp2i(-e);
+          uint32_t* dst = reinterpret_cast<uint32_t*>(a.out_q + obase);
+#pragma unroll
+          for (int i = 0; i < 32; i += 4) dst[i / 4] = pack4_e4m3(o[i] * si, o[i + 1] * si, o[i + 2] * si, o[i + 3] * si);
+          a.out_sf[sf_offset(tok, (head * D + c) >> 5, a.out_kblocks)] = (uint8_t)(e + 127);
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, fa::TMEM_COLS);
+  }
+}
+
+// merge split-KV partials, apply the output gate, write bf16 and/or MXFP8. One warp per (token, head).
+__global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int T, int Hq,
+                                    int nsplit, float v_scale, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
+                                    __nv_bfloat16* __restrict__ out_bf16, uint8_t* __restrict__ out_q,
+                                    uint8_t* __restrict__ out_sf, int out_kblocks) {
+  pdl_trigger();  // the next GEMM may start streaming its weights
+  constexpr int D = fa::D;
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (int64_t)T * Hq) return;
+  const int tok = (int)(gw / Hq), head = (int)(gw % Hq);
+  const float* ml = part_ml + gw * nsplit * 2;
+  const int used = nsplit;  // every split writes (max, sum); empty ones carry sum 0
+  float M = -INFINITY;
+  for (int s = 0; s < used; ++s) M = fmaxf(M, ml[2 * s]);
+  float L = 0.f, acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int s = 0; s < used; ++s) {
+    const float m = ml[2 * s], l = ml[2 * s + 1];
+    if (l <= 0.f || m == -INFINITY) continue;
+    const float w = exp2f(m - M);
+    L += w * l;
+    const float* po = part_o + (gw * nsplit + s) * D;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] += w * po[lane + 32 * i];
+  }
+  const float inv = L > 0.f ? v_scale / L : 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int d = lane + 32 * i;
+    float o = acc[i] * inv;
+    if (gate != nullptr) o *= sigmoid_f(__bfloat162float(gate[(int64_t)tok * ld_gate + head * D + d]));
+    o = __bfloat162float(__float2bfloat16(o));
+    if (out_bf16 != nullptr) out_bf16[(int64_t)tok * Hq * D + head * D + d] = __float2bfloat16(o);
+    if (out_q != nullptr) {
+      float am = fabsf(o);
+      for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
+      const int e = mx_exponent(am, 448.f);
+      out_q[(int64_t)tok * Hq * D + head * D + d] = f32_to_e4m3(o * exp2i(-e));
+      if (lane == 0) out_sf[sf_offset(tok, (head * D + 32 * i) >> 5, out_kblocks)] = (uint8_t)(e + 127);
+    }
+  }
+}
+
+static void attn_tc_launch(const AttnArgs& a, const CUtensorMap& tk, const CUtensorMap& tv, dim3 grid, cudaStream_t st) {
+  static bool set = false;
+  if (!set) {
+    TORCH_CHECK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) == cudaSuccess,
+                "attn_tc: smem attribute");
+    set = true;
+  }
+  attn_tc_kernel<<<grid, 192, fa::SMEM, st>>>(tk, tv, a);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+static AttnArgs base_args(const torch::Tensor& q, const torch::Tensor& kc, const torch::Tensor& block_table,
+                          const torch::Tensor& tok_ctx, double sm_scale, double k_scale, double v_scale,
+                          const torch::Tensor& status) {
+  AttnArgs a = {};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.Hq = (int)q.size(1);
+  a.Hkv = (int)kc.size(1);
+  a.G = a.Hq / a.Hkv;
+  TORCH_CHECK(a.Hq % a.Hkv == 0, "attn_tc: Hq % Hkv");
+  TORCH_CHECK(q.size(2) == fa::D && kc.size(3) == fa::D && kc.size(2) == fa::BLK, "attn_tc: head_dim 256, page 64");
+  a.block_table = block_table.data_ptr<int32_t>();
+  a.max_blocks = (int)block_table.size(1);
+  a.tok_ctx = tok_ctx.data_ptr<int32_t>();
+  a.scale_log2 = (float)(sm_scale * k_scale * 1.4426950408889634);
+  a.v_scale = (float)v_scale;
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 1000000000ull;
+  return a;
+}
+
+static CUtensorMap kv_tmap(const torch::Tensor& c) {
+  const int64_t rows = c.size(0) * c.size(1) * c.size(2);
+  return tmap_u8_kmajor(c.data_ptr(), rows, fa::D, fa::BLK);
+}
+
+// decode / verify: split-KV partials + combine
+void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                    torch::Tensor tok_ctx, torch::Tensor seq_start, torch::Tensor seq_len, double sm_scale,
+                    double k_scale, double v_scale, torch::Tensor part_o, torch::Tensor part_ml,
+                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
+                    c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status) {
+  const int64_t T = q.size(0), S = seq_start.size(0);
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  AttnArgs a = base_args(q, k_cache, block_table, tok_ctx, sm_scale, k_scale, v_scale, status);
+  a.mode = 0;
+  a.seq_start = seq_start.data_ptr<int32_t>();
+  a.seq_len = seq_len.data_ptr<int32_t>();
+  a.nsplit = (int)part_ml.size(1);
+  TORCH_CHECK(part_o.size(0) >= T * a.Hq && part_o.size(1) == a.nsplit && part_o.size(2) == fa::D && part_o.is_contiguous() &&
+                  part_ml.is_contiguous(), "attn_tc: part_o / part_ml must be contiguous [T*Hq, nsplit, ...]");
+  TORCH_CHECK(seq_start.size(0) == S && S <= 65535, "attn_tc: seq count");
+  a.part_o = part_o.data_ptr<float>();
+  a.part_ml = part_ml.data_ptr<float>();
+  auto st = at::cuda::getCurrentCUDAStream();
+  attn_tc_launch(a, kv_tmap(k_cache), kv_tmap(v_cache), dim3((unsigned)S, (unsigned)a.Hkv, (unsigned)a.nsplit), st);
+  const __nv_bfloat16* g = (gate.has_value() && gate->defined()) ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
+  const int64_t warps = T * a.Hq;
+  attn_combine_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+      a.part_o, a.part_ml, (int)T, a.Hq, a.nsplit, a.v_scale, g, g ? gate->stride(0) : 0,
+      (out.has_value() && out->defined()) ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr,
+      (out_q.has_value() && out_q->defined()) ? out_q->data_ptr<uint8_t>() : nullptr,
+      (out_sf.has_value() && out_sf->defined()) ? out_sf->data_ptr<uint8_t>() : nullptr, (int)(a.Hq * fa::D / 32));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// prefill: one CTA per (query tile, kv head), output written directly (gate + MXFP8 fused)
+void attn_tc_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                     torch::Tensor tok_ctx, torch::Tensor tile_tab, int64_t ntiles, double sm_scale, double k_scale,
+                     double v_scale, c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
+                     c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status) {
+  if (ntiles == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  AttnArgs a = base_args(q, k_cache, block_table, tok_ctx, sm_scale, k_scale, v_scale, status);
+  a.mode = 1;
+  a.tile_tab = tile_tab.data_ptr<int32_t>();
+  a.ntiles = (int)ntiles;
+  if (gate.has_value() && gate->defined()) {
+    a.gate = reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr());
+    a.ld_gate = gate->stride(0);
+  }
+  a.out_bf16 = (out.has_value() && out->defined()) ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr;
+  a.out_q = (out_q.has_value() && out_q->defined()) ? out_q->data_ptr<uint8_t>() : nullptr;
+  a.out_sf = (out_sf.has_value() && out_sf->defined()) ? out_sf->data_ptr<uint8_t>() : nullptr;
+  a.out_kblocks = a.Hq * fa::D / 32;
+  attn_tc_launch(a, kv_tmap(k_cache), kv_tmap(v_cache), dim3((unsigned)ntiles, (unsigned)a.Hkv, 1),
+                 at::cuda::getCurrentCUDAStream());
+}
+
+}  // namespace r9k

@@ -8,11 +8,13 @@
 namespace r9k {
 // gemm_tc.cu
 void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, torch::Tensor out,
-             c10::optional<torch::Tensor> residual, double alpha, torch::Tensor status);
+             c10::optional<torch::Tensor> residual, double alpha, torch::Tensor status,
+             c10::optional<torch::Tensor> workspace);
 void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, torch::Tensor wu_sf, bool w_fp4,
-                    torch::Tensor x, torch::Tensor x_sf, torch::Tensor out_q, torch::Tensor out_sf, torch::Tensor status);
+                    torch::Tensor x, torch::Tensor x_sf, torch::Tensor out_q, torch::Tensor out_sf, torch::Tensor status,
+                    c10::optional<torch::Tensor> workspace);
 void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha,
-               torch::Tensor status);
+               torch::Tensor status, c10::optional<torch::Tensor> workspace);
 // quant.cu
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
                    torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
@@ -33,6 +35,16 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
                      torch::Tensor tok_seq, torch::Tensor tok_ctx, double sm_scale, double k_scale, double v_scale,
                      c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
                      c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, int64_t window);
+// attention_tc.cu
+void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                    torch::Tensor tok_ctx, torch::Tensor seq_start, torch::Tensor seq_len, double sm_scale,
+                    double k_scale, double v_scale, torch::Tensor part_o, torch::Tensor part_ml,
+                    c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
+                    c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status);
+void attn_tc_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
+                     torch::Tensor tok_ctx, torch::Tensor tile_tab, int64_t ntiles, double sm_scale, double k_scale,
+                     double v_scale, c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
+                     c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status);
 // gdn.cu
 void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv, int64_t b_off, int64_t a_off,
                    torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor tok_slot, torch::Tensor tok_pos,
@@ -50,10 +62,11 @@ void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torc
 
 TORCH_LIBRARY(r9k, m) {
   m.def("gemm_mx(Tensor w, Tensor w_sf, bool w_fp4, Tensor x, Tensor x_sf, Tensor(a!) out, Tensor? residual, "
-        "float alpha, Tensor(b!) status) -> ()");
+        "float alpha, Tensor(b!) status, Tensor(c!)? workspace=None) -> ()");
   m.def("gemm_mx_swiglu(Tensor wg, Tensor wg_sf, Tensor wu, Tensor wu_sf, bool w_fp4, Tensor x, Tensor x_sf, "
-        "Tensor(a!) out_q, Tensor(b!) out_sf, Tensor(c!) status) -> ()");
-  m.def("gemm_bf16(Tensor w, Tensor x, Tensor(a!) out, Tensor? residual, float alpha, Tensor(b!) status) -> ()");
+        "Tensor(a!) out_q, Tensor(b!) out_sf, Tensor(c!) status, Tensor(d!)? workspace=None) -> ()");
+  m.def("gemm_bf16(Tensor w, Tensor x, Tensor(a!) out, Tensor? residual, float alpha, Tensor(b!) status, "
+        "Tensor(c!)? workspace=None) -> ()");
   m.def("rmsnorm_quant(Tensor x, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf) -> ()");
   m.def("quant_act_mxfp8(Tensor x, Tensor(a!) q, Tensor(b!) sf) -> ()");
@@ -69,6 +82,13 @@ TORCH_LIBRARY(r9k, m) {
   m.def("paged_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_seq, "
         "Tensor tok_ctx, float sm_scale, float k_scale, float v_scale, Tensor? gate, Tensor(a!)? out, "
         "Tensor(b!)? out_q, Tensor(c!)? out_sf, int window) -> ()");
+  m.def("attn_tc_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_ctx, "
+        "Tensor seq_start, Tensor seq_len, float sm_scale, float k_scale, float v_scale, Tensor(a!) part_o, "
+        "Tensor(b!) part_ml, Tensor? gate, Tensor(c!)? out, Tensor(d!)? out_q, Tensor(e!)? out_sf, "
+        "Tensor(f!) status) -> ()");
+  m.def("attn_tc_prefill(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_ctx, "
+        "Tensor tile_tab, int ntiles, float sm_scale, float k_scale, float v_scale, Tensor? gate, "
+        "Tensor(a!)? out, Tensor(b!)? out_q, Tensor(c!)? out_sf, Tensor(d!) status) -> ()");
   m.def("gdn_conv_prep(Tensor proj, int Hk, int Hv, int dk, int dv, int b_off, int a_off, Tensor conv_w, "
         "Tensor conv_state, Tensor tok_slot, Tensor tok_pos, Tensor tok_has_state, Tensor A_log, Tensor dt_bias, "
         "Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!) g_out, Tensor(e!) beta_out) -> ()");
@@ -93,6 +113,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("dequant_mx", &r9k::dequant_mx);
   m.impl("qk_norm_rope_cache", &r9k::qk_norm_rope_cache);
   m.impl("paged_attention", &r9k::paged_attention);
+  m.impl("attn_tc_decode", &r9k::attn_tc_decode);
+  m.impl("attn_tc_prefill", &r9k::attn_tc_prefill);
   m.impl("gdn_conv_prep", &r9k::gdn_conv_prep);
   m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);

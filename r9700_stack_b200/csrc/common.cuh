@@ -59,6 +59,14 @@ R9K_DEVINL bool elect_one() {
 }
 
 // ---------------------------------------------------------------------------------------------
+// programmatic dependent launch: a kernel launched with the programmatic-serialization attribute may
+// start before its predecessor finishes; it must call pdl_wait() before touching anything the
+// predecessor writes (or reads). pdl_trigger() lets the successor launch early.
+// ---------------------------------------------------------------------------------------------
+R9K_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+R9K_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------------------------------------
 // mbarrier
 // ---------------------------------------------------------------------------------------------
 R9K_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
@@ -117,6 +125,14 @@ R9K_DEVINL void tma_load_2d_hint(void* smem_dst, const CUtensorMap* map, uint64_
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
       "%4}], [%2], %5;" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "l"(hint)
+      : "memory");
+}
+R9K_DEVINL void tma_load_3d_hint(void* smem_dst, const CUtensorMap* map, uint64_t* bar, int x, int y, int z,
+                                 uint64_t hint) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+      "%4, %5}], [%2], %6;" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(hint)
       : "memory");
 }
 // Plain bulk copy global -> shared (16-byte aligned addresses, size multiple of 16).

@@ -14,7 +14,8 @@
 //                         g and beta; reads the per-sequence conv state for the first W-1 taps.
 //  * gdn_conv_state_update - stores the last W-1 conv inputs of each sequence (skipped during spec
 //                         verify, run on commit).
-//  * gdn_recurrent      - the delta-rule recurrence. Columns of S evolve independently, so the grid
+//  * gdn_recurrent      - the delta-rule recurrence (state stored transposed, [dv][dk] per head).
+//                         Columns of S evolve independently, so the grid
 //                         splits each head's dv columns over CTAs (32 per CTA); four lanes share a
 //                         column (32 rows each) and reduce with shuffles, so no block barrier runs
 //                         per token. Serves decode (1 token), spec verify (T tokens, state not
@@ -35,7 +36,9 @@ template <> R9K_DEVINL float from_f<float>(float v) { return v; }
 template <> R9K_DEVINL __nv_bfloat16 from_f<__nv_bfloat16>(float v) { return __float2bfloat16(v); }
 
 // ------------------------------------------------------------------------------------------------
-// conv + prep: one CTA per token. Channels: [q: Hk*dk][k: Hk*dk][v: Hv*dv] at proj offset 0.
+// conv + prep: grid (T, ceil((2*Hk + Hv + 1) / 8)), 8 warps; warp w handles 128-channel head
+// hh = blockIdx.y * 8 + w of [q heads | k heads | v heads], the last index computes g and beta.
+// Lane l owns channels 4l..4l+3 of the head. Requires dk == dv == 128.
 // ------------------------------------------------------------------------------------------------
 template <typename ST>
 __global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int dk,
@@ -46,47 +49,61 @@ __global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int
                                      const float* __restrict__ dt_bias, float* __restrict__ q_out,
                                      float* __restrict__ k_out, float* __restrict__ v_out, float* __restrict__ g_out,
                                      float* __restrict__ beta_out) {
-  extern __shared__ float sh[];  // conv outputs for all channels of this token
   const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31;
+  const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const int NH = 2 * Hk + Hv;
+  if (hh > NH) return;
+  if (hh == NH) {
+    for (int h = lane; h < Hv; h += 32) {
+      const float av = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
+      const float bv = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
+      g_out[(int64_t)t * Hv + h] = -__expf(A_log[h]) * softplus_f(av + dt_bias[h]);
+      beta_out[(int64_t)t * Hv + h] = sigmoid_f(bv);
+    }
+    return;
+  }
   const int C = 2 * Hk * dk + Hv * dv;
-  const int j = tok_pos_in_chunk[t];  // index of this token within its sequence's chunk
+  const int c0 = hh * 128 + lane * 4;
+  const int j = tok_pos_in_chunk[t];
   const int slot = tok_slot[t];
   const bool hs = has_state_tok[t] != 0;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float acc = 0.f;
-    for (int w = 0; w < W; ++w) {
-      const int back = W - 1 - w;  // how many tokens before this one
-      float x;
-      if (j - back >= 0) {
-        x = __bfloat162float(proj[(int64_t)(t - back) * ld + c]);
-      } else {
-        // from the conv state: state holds the last W-1 inputs, index W-2 = most recent
-        const int si = (W - 1) - (back - j);
-        x = (hs && si >= 0) ? to_f<ST>(conv_state[((int64_t)slot * C + c) * (W - 1) + si]) : 0.f;
-      }
-      acc += x * __bfloat162float(conv_w[(int64_t)c * W + w]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  // weights: 4 channels x W taps, contiguous
+  float wt[4][8];
+#pragma unroll
+  for (int e = 0; e < 4; ++e)
+    for (int w = 0; w < W; ++w) wt[e][w] = __bfloat162float(conv_w[(int64_t)(c0 + e) * W + w]);
+  for (int w = 0; w < W; ++w) {
+    const int back = W - 1 - w;
+    float x[4];
+    if (j - back >= 0) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(proj + (int64_t)(t - back) * ld + c0);
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 4; ++k) x[k] = __bfloat162float(e[k]);
+    } else {
+      const int si = (W - 1) - (back - j);
+#pragma unroll
+      for (int k = 0; k < 4; ++k)
+        x[k] = (hs && si >= 0) ? to_f<ST>(conv_state[((int64_t)slot * C + c0 + k) * (W - 1) + si]) : 0.f;
     }
-    sh[c] = silu_f(acc);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] += x[k] * wt[k][w];
   }
-  __syncthreads();
-  // l2 norms: one warp per key head of q and of k
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
-  for (int hh = warp; hh < 2 * Hk; hh += nwarps) {
-    const float* src = sh + hh * dk;
-    float ss = 0.f;
-    for (int i = lane; i < dk; i += 32) ss += src[i] * src[i];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) acc[k] = silu_f(acc[k]);
+  if (hh < 2 * Hk) {
+    float ss = acc[0] * acc[0] + acc[1] * acc[1] + acc[2] * acc[2] + acc[3] * acc[3];
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     float inv = rsqrtf(ss + 1e-6f);
-    if (hh < Hk) inv *= rsqrtf((float)dk);
-    float* dst = (hh < Hk ? q_out + ((int64_t)t * Hk + hh) * dk : k_out + ((int64_t)t * Hk + (hh - Hk)) * dk);
-    for (int i = lane; i < dk; i += 32) dst[i] = src[i] * inv;
-  }
-  for (int c = threadIdx.x; c < Hv * dv; c += blockDim.x) v_out[(int64_t)t * Hv * dv + c] = sh[2 * Hk * dk + c];
-  for (int h = threadIdx.x; h < Hv; h += blockDim.x) {
-    const float a = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
-    const float b = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
-    g_out[(int64_t)t * Hv + h] = -__expf(A_log[h]) * softplus_f(a + dt_bias[h]);
-    beta_out[(int64_t)t * Hv + h] = sigmoid_f(b);
+    float* dst;
+    if (hh < Hk) { inv *= rsqrtf((float)dk); dst = q_out + ((int64_t)t * Hk + hh) * dk; }
+    else dst = k_out + ((int64_t)t * Hk + (hh - Hk)) * dk;
+    *reinterpret_cast<float4*>(dst + lane * 4) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+  } else {
+    float* dst = v_out + ((int64_t)t * Hv + (hh - 2 * Hk)) * dv;
+    *reinterpret_cast<float4*>(dst + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
   }
 }
 
@@ -100,7 +117,9 @@ __global__ void gdn_conv_state_update_kernel(const __nv_bfloat16* __restrict__ p
   const int slot = seq_slot[s], st0 = seq_start[s], n = seq_len[s];
   const bool hs = seq_has_state[s] != 0;
   if (n <= 0) return;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+  {
+    const int c = blockIdx.y * blockDim.x + threadIdx.x;
+    if (c >= C) return;
     float nv[8];
     ST* cs = conv_state + ((int64_t)slot * C + c) * (W - 1);
     for (int i = 0; i < W - 1; ++i) {
@@ -117,16 +136,54 @@ __global__ void gdn_conv_state_update_kernel(const __nv_bfloat16* __restrict__ p
 }
 
 // ------------------------------------------------------------------------------------------------
-// recurrent core: grid (num_seqs, Hv, dv / 32), 128 threads.
-// thread tid: column c = tid / 4 (0..31), row group rg = tid % 4; rows i = rg + 4 r, r = 0..dk/4-1.
+// recurrent core: grid (num_seqs, Hv, dv / 32), 128 threads. The state is stored transposed,
+// [slot][h][dv][dk], so thread tid (column c = tid / 4 of this CTA's 32, row group rg = tid % 4)
+// owns 32 contiguous dk entries of its column and moves them with 16-byte vectors.
+// k/q are staged in smem interleaved as [token][r * 4 + rg] (row i = rg * 32 + r): conflict-free.
 // ------------------------------------------------------------------------------------------------
+template <typename ST> struct StateVec;
+template <> struct StateVec<float> {
+  R9K_DEVINL static void load(const float* p, float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+  }
+  R9K_DEVINL static void store(float* p, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+};
+template <> struct StateVec<__nv_bfloat16> {
+  R9K_DEVINL static void load(const __nv_bfloat16* p, float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint4 raw = reinterpret_cast<const uint4*>(p)[i];
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[8 * i + k] = __bfloat162float(e[k]);
+    }
+  }
+  R9K_DEVINL static void store(__nv_bfloat16* p, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 raw;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16(v[8 * i + k]);
+      reinterpret_cast<uint4*>(p)[i] = raw;
+    }
+  }
+};
+
 template <typename ST, int DK>
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
     const float* __restrict__ g, const float* __restrict__ beta, int Hk, int Hv, int dv, ST* __restrict__ state,
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_start, const int32_t* __restrict__ seq_len,
     const int32_t* __restrict__ seq_has_state, int write_state, float* __restrict__ o) {
-  constexpr int R = DK / 4;
+  static_assert(DK == 128, "row groups of 32");
   constexpr int CH = 16;  // tokens staged per chunk
   __shared__ float sq[CH][DK], sk[CH][DK], sv[CH][32], sg[CH], sb[CH];
   const int s = blockIdx.x, h = blockIdx.y, cs = blockIdx.z;
@@ -135,19 +192,22 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
   const int kh = h / (Hv / Hk);
   const int slot = seq_slot[s], t0 = seq_start[s], n = seq_len[s];
   if (n <= 0 && !write_state) return;
-  ST* Sp = state + ((int64_t)slot * Hv + h) * DK * dv;
-  float S[R];
-  const bool hs = seq_has_state[s] != 0;
+  ST* Sp = state + (((int64_t)slot * Hv + h) * dv + col) * DK + rg * 32;
+  float S[32];
+  if (seq_has_state[s] != 0) StateVec<ST>::load(Sp, S);
+  else {
 #pragma unroll
-  for (int r = 0; r < R; ++r) S[r] = hs ? to_f<ST>(Sp[(int64_t)(rg + 4 * r) * dv + col]) : 0.f;
+    for (int r = 0; r < 32; ++r) S[r] = 0.f;
+  }
   for (int base = 0; base < n; base += CH) {
     const int cnt = min(CH, n - base);
     __syncthreads();
     for (int e = tid; e < cnt * DK; e += 128) {
       const int tt = e / DK, i = e % DK;
       const int64_t tok = t0 + base + tt;
-      sq[tt][i] = q[(tok * Hk + kh) * DK + i];
-      sk[tt][i] = k[(tok * Hk + kh) * DK + i];
+      const int si = (i & 31) * 4 + (i >> 5);  // interleave: row i = rg*32 + r -> r*4 + rg
+      sq[tt][si] = q[(tok * Hk + kh) * DK + i];
+      sk[tt][si] = k[(tok * Hk + kh) * DK + i];
     }
     for (int e = tid; e < cnt * 32; e += 128) {
       const int tt = e / 32, cc = e % 32;
@@ -162,27 +222,26 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     __syncthreads();
     for (int tt = 0; tt < cnt; ++tt) {
       const float decay = sg[tt];
+      const float* kk = &sk[tt][rg];
+      const float* qq = &sq[tt][rg];
       float kv = 0.f;
 #pragma unroll
-      for (int r = 0; r < R; ++r) kv += S[r] * sk[tt][rg + 4 * r];
+      for (int r = 0; r < 32; ++r) kv += S[r] * kk[4 * r];
       kv += __shfl_xor_sync(0xffffffffu, kv, 1);
       kv += __shfl_xor_sync(0xffffffffu, kv, 2);
       const float delta = sb[tt] * (sv[tt][c] - decay * kv);
       float ov = 0.f;
 #pragma unroll
-      for (int r = 0; r < R; ++r) {
-        S[r] = S[r] * decay + sk[tt][rg + 4 * r] * delta;
-        ov += S[r] * sq[tt][rg + 4 * r];
+      for (int r = 0; r < 32; ++r) {
+        S[r] = S[r] * decay + kk[4 * r] * delta;
+        ov += S[r] * qq[4 * r];
       }
       ov += __shfl_xor_sync(0xffffffffu, ov, 1);
       ov += __shfl_xor_sync(0xffffffffu, ov, 2);
       if (o != nullptr && rg == 0) o[((int64_t)(t0 + base + tt) * Hv + h) * dv + col] = ov;
     }
   }
-  if (write_state) {
-#pragma unroll
-    for (int r = 0; r < R; ++r) Sp[(int64_t)(rg + 4 * r) * dv + col] = from_f<ST>(S[r]);
-  }
+  if (write_state) StateVec<ST>::store(Sp, S);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -192,6 +251,7 @@ __global__ void gdn_out_norm_quant_kernel(const float* __restrict__ o, const __n
                                           int64_t ld, int z_off, const __nv_bfloat16* __restrict__ w, float eps,
                                           int T, int Hv, int dv, __nv_bfloat16* __restrict__ y,
                                           uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf) {
+  pdl_trigger();  // the next GEMM may start streaming its weights
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (gw >= (int64_t)T * Hv) return;
@@ -236,20 +296,17 @@ void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64
   TORCH_CHECK(conv_state.size(-1) == W - 1 && conv_state.size(1) == C, "gdn_conv_prep: conv state shape");
   const at::cuda::CUDAGuard guard(proj.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  const size_t smem = C * sizeof(float);
+  TORCH_CHECK(dk == 128 && dv == 128 && W <= 8, "gdn_conv_prep: head dim 128, conv width <= 8");
+  TORCH_CHECK(proj.stride(0) % 4 == 0 && proj.stride(1) == 1, "gdn_conv_prep: proj rows must be 8-byte aligned");
+  const dim3 grid((unsigned)T, (unsigned)((2 * Hk + Hv + 1 + 7) / 8));
 #define R9K_CONV(ST_T)                                                                                                \
-  {                                                                                                                   \
-    auto kern = gdn_conv_prep_kernel<ST_T>;                                                                           \
-    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);       \
-    kern<<<T, 512, smem, st>>>(reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk,      \
-                               (int)Hv, (int)dk, (int)dv, (int)b_off, (int)a_off,                                     \
-                               reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()), W,                         \
-                               reinterpret_cast<const ST_T*>(conv_state.data_ptr()), tok_slot.data_ptr<int32_t>(),    \
-                               tok_pos.data_ptr<int32_t>(), tok_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(), \
-                               dt_bias.data_ptr<float>(), q_out.data_ptr<float>(), k_out.data_ptr<float>(),           \
-                               v_out.data_ptr<float>(), g_out.data_ptr<float>(), beta_out.data_ptr<float>());        \
-  }
-  if (conv_state.dtype() == torch::kFloat32) R9K_CONV(float) else R9K_CONV(__nv_bfloat16)
+  gdn_conv_prep_kernel<ST_T><<<grid, 256, 0, st>>>(                                                                    \
+      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)dk, (int)dv,     \
+      (int)b_off, (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()), W,                           \
+      reinterpret_cast<const ST_T*>(conv_state.data_ptr()), tok_slot.data_ptr<int32_t>(), tok_pos.data_ptr<int32_t>(),  \
+      tok_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), q_out.data_ptr<float>(),  \
+      k_out.data_ptr<float>(), v_out.data_ptr<float>(), g_out.data_ptr<float>(), beta_out.data_ptr<float>());
+  if (conv_state.dtype() == torch::kFloat32) { R9K_CONV(float) } else { R9K_CONV(__nv_bfloat16) }
 #undef R9K_CONV
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -263,13 +320,14 @@ void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::
   TORCH_CHECK(W - 1 <= 8, "conv width <= 9");
   const at::cuda::CUDAGuard guard(proj.device());
   auto st = at::cuda::getCurrentCUDAStream();
+  const dim3 grid((unsigned)S, (unsigned)((C + 255) / 256));
   if (conv_state.dtype() == torch::kFloat32)
-    gdn_conv_state_update_kernel<float><<<S, 256, 0, st>>>(
+    gdn_conv_state_update_kernel<float><<<grid, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W, conv_state.data_ptr<float>(),
         seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(),
         seq_has_state.data_ptr<int32_t>());
   else
-    gdn_conv_state_update_kernel<__nv_bfloat16><<<S, 256, 0, st>>>(
+    gdn_conv_state_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
         reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W,
         reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr()), seq_slot.data_ptr<int32_t>(),
         seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>());
@@ -284,7 +342,7 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   const int Hk = (int)q.size(1), DK = (int)q.size(2);
   const int Hv = (int)v.size(1), dv = (int)v.size(2);
   TORCH_CHECK(dv % 32 == 0 && DK == 128, "gdn_recurrent: dk 128, dv % 32");
-  TORCH_CHECK(state.size(1) == Hv && state.size(2) == DK && state.size(3) == dv, "gdn_recurrent: state shape");
+  TORCH_CHECK(state.size(1) == Hv && state.size(2) == dv && state.size(3) == DK, "gdn_recurrent: state [slots, Hv, dv, dk]");
   const at::cuda::CUDAGuard guard(q.device());
   auto st = at::cuda::getCurrentCUDAStream();
   dim3 grid((unsigned)S, (unsigned)Hv, (unsigned)(dv / 32));

@@ -1,0 +1,85 @@
+// Shared definitions of the tcgen05 GEMM kernels (tiled: gemm_tc.cu, stream-K: gemm_sk.cu).
+#pragma once
+#include "common.cuh"
+#include "tmap.h"
+
+namespace r9k {
+
+enum { KIND_BF16 = 0, KIND_MX = 1 };
+enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2 };
+
+struct GemmArgs {
+  int N;               // weight rows (output features)
+  int M;               // tokens
+  int K;               // reduction length (elements)
+  int kchunks;         // K / chunk elements (chunk = 128 bytes of a smem row)
+  int kc_per_split;    // chunks handled by one split
+  int splits;          // K splits (tiled kernel)
+  uint32_t a_fmt;      // kFmtE2M1 / kFmtE4M3 for KIND_MX
+  int a_tiled;         // weights stored as contiguous 128x128 units (3-D tensor map)
+  const uint8_t* sfa;  // weight scales, 512-byte chunk layout
+  const uint8_t* sfa2; // second weight (dual) scales
+  const uint8_t* sfb;  // activation scales
+  int sf_kblocks;      // K / 32
+  void* out;
+  int ldo;
+  const __nv_bfloat16* residual;
+  int ldr;
+  uint8_t* out_sf;     // SwiGLU-quant output scales
+  int out_kblocks;     // (output features) / 32
+  float alpha;
+  int* status;
+  uint64_t timeout_ns;
+};
+
+// A (weight) tile load: row-major 2-D map, or pre-tiled 3-D map indexed by unit
+R9K_DEVINL void load_a_tile(void* dst, const CUtensorMap* map, uint64_t* bar, const GemmArgs& a, int kc, int box_x,
+                            int m0, uint64_t pol) {
+  if (a.a_tiled) tma_load_3d_hint(dst, map, bar, 0, 0, (m0 >> 7) * a.kchunks + kc, pol);
+  else tma_load_2d_hint(dst, map, bar, kc * box_x, m0, pol);
+}
+
+template <int BN, bool DUAL, int EPI>
+R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u, int row, int tok0, int lane) {
+  if constexpr (EPI == EPI_SWIGLU_MXFP8) {
+    uint8_t* outq = reinterpret_cast<uint8_t*>(a.out);
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      const int tok = tok0 + t;
+      float h = (row < a.N) ? silu_f(g[t]) * u[t] : 0.f;
+      float am = fabsf(h);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+      const int e = mx_exponent(am, 448.f);
+      const uint8_t qv = f32_to_e4m3(h * exp2i(-e));
+      if (tok < a.M) {
+        if (row < a.N) outq[(int64_t)tok * a.ldo + row] = qv;
+        if (lane == 0) a.out_sf[sf_offset(tok, row >> 5, a.out_kblocks)] = (uint8_t)(e + 127);
+      }
+    }
+  } else if constexpr (EPI == EPI_F32) {
+    float* out = reinterpret_cast<float*>(a.out);
+    if (row < a.N) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int tok = tok0 + t;
+        if (tok < a.M) out[(int64_t)tok * a.ldo + row] = g[t] * a.alpha;
+      }
+    }
+  } else {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    if (row < a.N) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int tok = tok0 + t;
+        if (tok < a.M) {
+          float y = g[t] * a.alpha;
+          if (a.residual != nullptr) y += __bfloat162float(a.residual[(int64_t)tok * a.ldr + row]);
+          out[(int64_t)tok * a.ldo + row] = __float2bfloat16(y);
+        }
+      }
+    }
+  }
+}
+
+}  // namespace r9k

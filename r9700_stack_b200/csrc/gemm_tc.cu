@@ -16,9 +16,12 @@
 // 128-byte swizzle; fp4 weights use the 16U4_ALIGN16B form the f8f6f4 MMA reads. Scale factors
 // arrive as 512-byte bulk copies and go to TMEM with tcgen05.cp.
 //
-// Split-K: for skinny decode GEMMs the grid's y dimension holds S splits of K grouped into one
-// thread-block cluster; each CTA parks its fp32 partial tile in shared memory and the cluster's
-// rank-0 CTA sums them over DSMEM in a fixed order (deterministic), then runs the epilogue.
+// Skinny (decode) GEMMs stream weights: fp4 weights are TMA-loaded packed (plain byte copies of
+// contiguous 8 KB units, a deep ring) and the epilogue warps, idle during the main loop, expand each
+// tile into the padded 16-element-group layout the f8f6f4 MMA reads -- the TMA's own fp4 expansion
+// form streams at about half the rate. K is split so that two CTAs run per SM; each split parks its
+// fp32 partial in a global workspace and the last split of a tile to arrive (per-tile counter, left
+// at zero) sums the splits in split order (deterministic) and runs the epilogue.
 //
 // Epilogues: bf16 store (+ residual add, alpha), fp32 store, and the fused SwiGLU -> MXFP8 quant
 // used by gate_up projections (two accumulators, gate and up, per CTA) that writes the down
@@ -29,123 +32,77 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <mutex>
 #include <unordered_map>
-#include "common.cuh"
-#include "tmap.h"
+#include "gemm_common.cuh"
 
 namespace r9k {
 
-enum { KIND_BF16 = 0, KIND_MX = 1 };
-enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2 };
-
-struct GemmArgs {
-  int N;               // weight rows (output features)
-  int M;               // tokens
-  int K;               // reduction length (elements)
-  int kchunks;         // K / chunk elements (chunk = 128 bytes of a smem row)
-  int kc_per_split;    // chunks handled by one split
-  uint32_t a_fmt;      // kFmtE2M1 / kFmtE4M3 for KIND_MX
-  const uint8_t* sfa;  // weight scales, 512-byte chunk layout
-  const uint8_t* sfa2; // second weight (dual) scales
-  const uint8_t* sfb;  // activation scales
-  int sf_kblocks;      // K / 32
-  void* out;
-  int ldo;
-  const __nv_bfloat16* residual;
-  int ldr;
-  uint8_t* out_sf;     // SwiGLU-quant output scales
-  int out_kblocks;     // (output features) / 32
-  float alpha;
-  int* status;
-  uint64_t timeout_ns;
-};
-
-template <int KIND, int BN, bool DUAL, int STAGES>
+template <int KIND, int BN, bool DUAL, int NP, int NC, bool UNPACK>
 struct GemmCfg {
-  static constexpr int A_BYTES = 128 * 128;
-  static constexpr int B_BYTES = BN * 128;
   static constexpr int NA = DUAL ? 2 : 1;
+  static constexpr int A_BYTES = 128 * 128;                  // MMA-ready A tile (SW128)
+  static constexpr int AL_BYTES = UNPACK ? 128 * 64 : A_BYTES;  // A as loaded (packed fp4 when UNPACK)
+  static constexpr int B_BYTES = BN * 128;
   static constexpr int NB_SF = (BN + 127) / 128;
   static constexpr int SFA_BYTES = (KIND == KIND_MX) ? 512 : 0;
   static constexpr int SFB_BYTES = (KIND == KIND_MX) ? 512 * NB_SF : 0;
+  // load ring (NP stages): A as loaded, B, scale factors
   static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + STAGES * NA * A_BYTES;
-  static constexpr int OFF_SFA = OFF_B + STAGES * B_BYTES;
-  static constexpr int OFF_SFB = OFF_SFA + STAGES * NA * SFA_BYTES;
-  static constexpr int OFF_BAR = (OFF_SFB + STAGES * SFB_BYTES + 15) / 16 * 16;
-  static constexpr int NUM_BARS = 2 * STAGES + 1;
+  static constexpr int OFF_B = OFF_A + NP * NA * AL_BYTES;
+  static constexpr int OFF_SFA = OFF_B + NP * B_BYTES;
+  static constexpr int OFF_SFB = OFF_SFA + NP * NA * SFA_BYTES;
+  // converted ring (NC stages, UNPACK only), 1 KiB aligned for the 128-byte swizzle
+  static constexpr int OFF_C = (OFF_SFB + NP * SFB_BYTES + 1023) / 1024 * 1024;
+  static constexpr int OFF_BAR = OFF_C + (UNPACK ? NC * NA * A_BYTES : 0);
+  static constexpr int NUM_BARS = 2 * NP + 2 * NC + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEMPTR + 16 + 1024;  // + alignment slack
-  // TMEM columns: accumulators, then scale factors
-  static constexpr int ACC_COLS = BN * NA;
+  // TMEM columns: NACC independent accumulators (skinny tiles round-robin their K steps over them so
+  // consecutive MMAs do not serialise on one accumulator), then scale factors
+  static constexpr int NACC = BN == 16 ? 4 : BN == 32 ? (DUAL ? 2 : 4) : BN == 64 ? (DUAL ? 1 : 2) : 1;  // <= 256 TMEM cols (2 CTAs/SM)
+  static constexpr int ACC_COLS = BN * NA * NACC;
   static constexpr int SFA_COL = ACC_COLS;
   static constexpr int SFB_COL = SFA_COL + 4 * NA;
   static constexpr int USED_COLS = (KIND == KIND_MX) ? SFB_COL + 4 * NB_SF : ACC_COLS;
   static constexpr int TMEM_COLS = USED_COLS <= 32 ? 32 : USED_COLS <= 64 ? 64 : USED_COLS <= 128 ? 128
                                    : USED_COLS <= 256 ? 256 : 512;
-  static constexpr int PART_BYTES = 128 * BN * 4 * NA;  // split-K partial tile (fp32)
-  static_assert(PART_BYTES <= OFF_SFA || BN > 64, "split-K partial must fit in the stage buffers");
+  static constexpr int TILE_F = NA * BN * 128;  // floats of one split-K partial tile
+  static_assert(!UNPACK || KIND == KIND_MX, "fp4 unpacking is for MX weights");
 };
 
-template <int BN, bool DUAL, int EPI>
-R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u, int row, int tok0, int lane) {
-  if constexpr (EPI == EPI_SWIGLU_MXFP8) {
-    uint8_t* outq = reinterpret_cast<uint8_t*>(a.out);
+// Expand a packed e2m1 tile (128 rows x 64 B, row-major) into the 16U4_ALIGN16B form the f8f6f4 MMA
+// reads (each 16-element group in the low 8 bytes of a 16-byte chunk), 128-byte swizzled.
+// Thread t (0..127) converts row t.
+R9K_DEVINL void unpack_fp4_tile(const uint8_t* src, uint8_t* dst, int r) {
+  const uint4* s4 = reinterpret_cast<const uint4*>(src + r * 64);
 #pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      const int tok = tok0 + t;
-      float h = (row < a.N) ? silu_f(g[t]) * u[t] : 0.f;
-      float am = fabsf(h);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-      const int e = mx_exponent(am, 448.f);
-      const uint8_t qv = f32_to_e4m3(h * exp2i(-e));
-      if (tok < a.M) {
-        if (row < a.N) outq[(int64_t)tok * a.ldo + row] = qv;
-        if (lane == 0) a.out_sf[sf_offset(tok, row >> 5, a.out_kblocks)] = (uint8_t)(e + 127);
-      }
-    }
-  } else if constexpr (EPI == EPI_F32) {
-    float* out = reinterpret_cast<float*>(a.out);
-    if (row < a.N) {
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int tok = tok0 + t;
-        if (tok < a.M) out[(int64_t)tok * a.ldo + row] = g[t] * a.alpha;
-      }
-    }
-  } else {
-    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
-    if (row < a.N) {
-#pragma unroll
-      for (int t = 0; t < 16; ++t) {
-        const int tok = tok0 + t;
-        if (tok < a.M) {
-          float y = g[t] * a.alpha;
-          if (a.residual != nullptr) y += __bfloat162float(a.residual[(int64_t)tok * a.ldr + row]);
-          out[(int64_t)tok * a.ldo + row] = __float2bfloat16(y);
-        }
-      }
-    }
+  for (int jj = 0; jj < 4; ++jj) {
+    const int j = (jj + r) & 3;  // rotate to spread shared-memory banks
+    const uint4 v = s4[j];
+    const int c0 = 2 * j, c1 = 2 * j + 1;
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c0 ^ (r & 7)) << 4)) = make_uint4(v.x, v.y, 0u, 0u);
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c1 ^ (r & 7)) << 4)) = make_uint4(v.z, v.w, 0u, 0u);
   }
 }
 
-template <int KIND, int BN, bool DUAL, int EPI, int STAGES>
+template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
-                   const __grid_constant__ CUtensorMap tmB, const GemmArgs args) {
-  using C = GemmCfg<KIND, BN, DUAL, STAGES>;
+                   const __grid_constant__ CUtensorMap tmB, const GemmArgs args, float* __restrict__ ws_part,
+                   int* __restrict__ ws_cnt) {
+  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* tmem_full = empty_bar + STAGES;
+  uint64_t* l_full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
+  uint64_t* l_empty = l_full + NP;
+  uint64_t* c_full = l_empty + NP;
+  uint64_t* c_empty = c_full + NC;
+  uint64_t* tmem_full = c_empty + NC;
   uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + C::OFF_TMEMPTR);
-  __shared__ int s_abort;
+  __shared__ int s_last, s_ok;
 
   const int warp = warp_id(), lane = lane_id();
   const int m0 = blockIdx.x * 128;
-  // cluster along y groups the S splits of one token tile
-  const int S = (int)cluster_nctarank();
+  const int S = args.splits;
   const int split = (int)(blockIdx.y % S);
   const int n_tile = (int)(blockIdx.y / S);
   const int n0 = n_tile * BN;
@@ -154,10 +111,13 @@ __global__ void __launch_bounds__(192, 1)
   const int nk = max(0, kc1 - kc0);
 
   if (threadIdx.x == 0) {
-    s_abort = 0;
-    for (int i = 0; i < STAGES; ++i) {
-      mbar_init(&full_bar[i], 1);
-      mbar_init(&empty_bar[i], 1);
+    for (int i = 0; i < NP; ++i) {
+      mbar_init(&l_full[i], 1);
+      mbar_init(&l_empty[i], 1);
+    }
+    for (int i = 0; i < NC; ++i) {
+      mbar_init(&c_full[i], 128);
+      mbar_init(&c_empty[i], 1);
     }
     mbar_init(tmem_full, 1);
     fence_mbar_init();
@@ -174,60 +134,72 @@ __global__ void __launch_bounds__(192, 1)
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
 
-  constexpr uint32_t A_TX = (KIND == KIND_BF16) ? 128 * 128 : 0;  // per A tile, set below for MX
-  const uint32_t a_tx = (KIND == KIND_BF16) ? A_TX : (args.a_fmt == kFmtE2M1 ? 128 * 64 : 128 * 128);
+  const uint32_t a_tx = (KIND == KIND_BF16) ? 128 * 128 : (args.a_fmt == kFmtE2M1 ? 128 * 64 : 128 * 128);
   const uint32_t stage_tx = a_tx * C::NA + BN * 128 + (KIND == KIND_MX ? 512 * C::NA + 512 * C::NB_SF : 0);
-  const int box_x = (KIND == KIND_BF16) ? 64 : 128;  // elements per 128-byte smem row
+  const int box_x = (KIND == KIND_BF16) ? 64 : (UNPACK ? 64 : 128);  // TMA box inner extent (elements of the map)
+  const int kchunks_sf = (args.sf_kblocks + 3) / 4;
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       const uint64_t pol_x = policy_evict_last();
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)((i / STAGES) & 1);
-        if (!mbar_wait(&empty_bar[s], ph ^ 1u, args.timeout_ns)) {
-          report_error(args.status, kErrMbarTimeout, 100, i);
-          s_abort = 1;
-          break;
-        }
+      // Weights do not depend on the previous kernel: the first NP weight tiles are requested before
+      // waiting on the predecessor grid (programmatic dependent launch). Activations come after.
+      auto load_a = [&](int i) {
+        const int s = i % NP;
         const int kc = kc0 + i;
-        uint8_t* sa = smem + C::OFF_A + s * C::NA * C::A_BYTES;
-        uint8_t* sb = smem + C::OFF_B + s * C::B_BYTES;
-        mbar_arrive_expect_tx(&full_bar[s], stage_tx);
-        tma_load_2d_hint(sa, &tmA, &full_bar[s], kc * box_x, m0, pol_w);
-        if (DUAL) tma_load_2d_hint(sa + C::A_BYTES, &tmA2, &full_bar[s], kc * box_x, m0, pol_w);
-        tma_load_2d_hint(sb, &tmB, &full_bar[s], kc * box_x, n0, pol_x);
+        uint8_t* sa = smem + C::OFF_A + s * C::NA * C::AL_BYTES;
+        mbar_arrive_expect_tx(&l_full[s], stage_tx);
+        load_a_tile(sa, &tmA, &l_full[s], args, kc, box_x, m0, pol_w);
+        if (DUAL) load_a_tile(sa + C::AL_BYTES, &tmA2, &l_full[s], args, kc, box_x, m0, pol_w);
         if constexpr (KIND == KIND_MX) {
           uint8_t* ssfa = smem + C::OFF_SFA + s * C::NA * 512;
+          bulk_load(ssfa, args.sfa + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
+          if (DUAL) bulk_load(ssfa + 512, args.sfa2 + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
+        }
+      };
+      auto load_b = [&](int i) {
+        const int s = i % NP;
+        const int kc = kc0 + i;
+        tma_load_2d_hint(smem + C::OFF_B + s * C::B_BYTES, &tmB, &l_full[s], kc * ((KIND == KIND_BF16) ? 64 : 128), n0,
+                         pol_x);
+        if constexpr (KIND == KIND_MX) {
           uint8_t* ssfb = smem + C::OFF_SFB + s * C::SFB_BYTES;
-          const int kchunks_sf = (args.sf_kblocks + 3) / 4;
-          bulk_load(ssfa, args.sfa + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &full_bar[s]);
-          if (DUAL) bulk_load(ssfa + 512, args.sfa2 + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &full_bar[s]);
 #pragma unroll
           for (int c = 0; c < C::NB_SF; ++c)
-            bulk_load(ssfb + 512 * c, args.sfb + ((int64_t)((n0 >> 7) + c) * kchunks_sf + kc) * 512, 512,
-                      &full_bar[s]);
+            bulk_load(ssfb + 512 * c, args.sfb + ((int64_t)((n0 >> 7) + c) * kchunks_sf + kc) * 512, 512, &l_full[s]);
         }
+      };
+      const int npre = min(NP, nk);
+      for (int i = 0; i < npre; ++i) load_a(i);
+      pdl_wait();
+      for (int i = 0; i < nk; ++i) {
+        if (i >= npre) {
+          if (!mbar_wait(&l_empty[i % NP], (uint32_t)(((i / NP) & 1) ^ 1), args.timeout_ns)) {
+            report_error(args.status, kErrMbarTimeout, 100, i);
+            break;
+          }
+          load_a(i);
+        }
+        load_b(i);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      bool ok = true;
       for (int i = 0; i < nk; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (uint32_t)((i / STAGES) & 1);
-        if (!mbar_wait(&full_bar[s], ph, args.timeout_ns)) {
+        const int s = i % NP;
+        const int sc = i % NC;
+        if (!mbar_wait(&l_full[s], (uint32_t)((i / NP) & 1), args.timeout_ns) ||
+            (UNPACK && !mbar_wait(&c_full[sc], (uint32_t)((i / NC) & 1), args.timeout_ns))) {
           report_error(args.status, kErrMbarTimeout, 101, i);
-          s_abort = 1;
-          ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t sa = smem_u32(smem + C::OFF_A + s * C::NA * C::A_BYTES);
+        const uint32_t sa = UNPACK ? smem_u32(smem + C::OFF_C + sc * C::NA * C::A_BYTES)
+                                   : smem_u32(smem + C::OFF_A + s * C::NA * C::AL_BYTES);
         const uint32_t sb = smem_u32(smem + C::OFF_B + s * C::B_BYTES);
         if constexpr (KIND == KIND_MX) {
           const uint32_t ssfa = smem_u32(smem + C::OFF_SFA + s * C::NA * 512);
@@ -240,102 +212,138 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
-          const uint32_t acc = (i > 0 || k > 0) ? 1u : 0u;
+          const int ai = k % C::NACC;
+          const uint32_t dacc = tbase + (uint32_t)(ai * BN * C::NA);
+          const uint32_t acc = (i > 0 || k >= C::NACC) ? 1u : 0u;
           if constexpr (KIND == KIND_MX) {
             const uint32_t idesc = idesc_block_scaled(args.a_fmt, kFmtE4M3, 128, BN, (uint32_t)k, (uint32_t)k);
             const uint32_t sfb_addr = (tbase + C::SFB_COL) | ((uint32_t)k << 30);
-            mma_mxf8f6f4_ss(tbase, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc,
+            mma_mxf8f6f4_ss(dacc, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc,
                             (tbase + C::SFA_COL) | ((uint32_t)k << 30), sfb_addr);
             if (DUAL)
-              mma_mxf8f6f4_ss(tbase + BN, sdesc_k_sw128(sa + C::A_BYTES + 32 * k), bd, idesc, acc,
+              mma_mxf8f6f4_ss(dacc + BN, sdesc_k_sw128(sa + C::A_BYTES + 32 * k), bd, idesc, acc,
                               (tbase + C::SFA_COL + 4) | ((uint32_t)k << 30), sfb_addr);
           } else {
             constexpr uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, BN);
-            mma_f16_ss(tbase, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc);
-            if (DUAL) mma_f16_ss(tbase + BN, sdesc_k_sw128(sa + C::A_BYTES + 32 * k), bd, idesc, acc);
+            mma_f16_ss(dacc, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc);
+            if (DUAL) mma_f16_ss(dacc + BN, sdesc_k_sw128(sa + C::A_BYTES + 32 * k), bd, idesc, acc);
           }
         }
-        tc_commit(&empty_bar[s]);
+        tc_commit(&l_empty[s]);
+        if (UNPACK) tc_commit(&c_empty[sc]);
       }
-      (void)ok;
       tc_commit(tmem_full);  // arrives once every MMA issued above has completed
+      pdl_trigger();
     }
     __syncwarp();
-  }
-
-  // ------------------------------ epilogue ------------------------------
-  const bool epi_warp = warp >= 2;
-  const int q = warp & 3;  // TMEM lane quadrant this warp may access
-  const int row_local = q * 32 + lane;
-  const int row = m0 + row_local;
-  float* part = reinterpret_cast<float*>(smem);  // reuses the stage buffers once the MMAs are done
-  bool have_acc = false;
-  if (epi_warp) {
-    have_acc = mbar_wait(tmem_full, 0, args.timeout_ns);
-    if (!have_acc) report_error(args.status, kErrMbarTimeout, 102, 0);
-    tc_fence_after();
-  }
-  if (S == 1) {
-    if (epi_warp && have_acc && nk > 0 && !s_abort) {
-      const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float g[16], u[16];
-        tmem_ld16(trow + c, g);
-        if (DUAL) tmem_ld16(trow + BN + c, u);
-        tmem_ld_wait();
-        epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+  } else {
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row_local = q * 32 + lane;
+    const int ct = threadIdx.x - 64;  // 0..127
+    // ------------------------------ fp4 expansion (UNPACK) ------------------------------
+    if constexpr (UNPACK) {
+      for (int i = 0; i < nk; ++i) {
+        const int s = i % NP, sc = i % NC;
+        const bool w1 = mbar_wait(&l_full[s], (uint32_t)((i / NP) & 1), args.timeout_ns);
+        const bool w2 = mbar_wait(&c_empty[sc], (uint32_t)(((i / NC) & 1) ^ 1), args.timeout_ns);
+        if (!w1 || !w2) {
+          report_error(args.status, kErrMbarTimeout, 103, i);
+          break;
+        }
+        const uint8_t* src = smem + C::OFF_A + s * C::NA * C::AL_BYTES;
+        uint8_t* dst = smem + C::OFF_C + sc * C::NA * C::A_BYTES;
+        unpack_fp4_tile(src, dst, ct);
+        if (DUAL) unpack_fp4_tile(src + C::AL_BYTES, dst + C::A_BYTES, ct);
+        fence_proxy_async();
+        mbar_arrive(&c_full[sc]);
       }
     }
-  } else {
-    if (epi_warp) {
-      const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
+    // ------------------------------ epilogue ------------------------------
+    const int row = m0 + row_local;
+    const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
+    pdl_wait();
+    const bool wok = __all_sync(0xffffffffu, nk == 0 || mbar_wait(tmem_full, 0, args.timeout_ns));
+    if (threadIdx.x == 64) s_ok = 1;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    if (!wok && lane == 0) s_ok = 0;
+    asm volatile("bar.sync 1, 128;" ::: "memory");
+    const bool ok = s_ok != 0;
+    if (!ok) report_error(args.status, kErrMbarTimeout, 102, 0);
+    tc_fence_after();
+    // load one 16-column chunk of the accumulator(s), summing the NACC partial accumulators
+    auto load_acc = [&](int c, float* g, float* u) {
+      tmem_ld16(trow + c, g);
+      if (DUAL) tmem_ld16(trow + BN + c, u);
+      tmem_ld_wait();
+#pragma unroll
+      for (int ai = 1; ai < C::NACC; ++ai) {
+        float g2[16], u2[16];
+        tmem_ld16(trow + ai * BN * C::NA + c, g2);
+        if (DUAL) tmem_ld16(trow + ai * BN * C::NA + BN + c, u2);
+        tmem_ld_wait();
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          g[t] += g2[t];
+          if (DUAL) u[t] += u2[t];
+        }
+      }
+    };
+    if (S == 1) {
+      if (ok && nk > 0) {
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          float g[16], u[16];
+          load_acc(c, g, u);
+          epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+        }
+      }
+    } else if (ok) {
+      // split-K: park the fp32 partial, the last split to arrive sums all splits in split order
+      const int tile_id = n_tile * gridDim.x + blockIdx.x;
+      float* mypart = ws_part + ((int64_t)tile_id * S + split) * C::TILE_F;
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
         float g[16], u[16];
-        if (have_acc && nk > 0) {
-          tmem_ld16(trow + c, g);
-          if (DUAL) tmem_ld16(trow + BN + c, u);
-          tmem_ld_wait();
+        if (nk > 0) {
+          load_acc(c, g, u);
         } else {
 #pragma unroll
           for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
         }
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
-          part[(c + t) * 128 + row_local] = g[t];
-          if (DUAL) part[BN * 128 + (c + t) * 128 + row_local] = u[t];
+          mypart[(c + t) * 128 + row_local] = g[t];
+          if (DUAL) mypart[BN * 128 + (c + t) * 128 + row_local] = u[t];
         }
       }
-    }
-    cluster_sync();
-    if (split == 0 && epi_warp) {
-      const uint32_t base = smem_u32(part);
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) {
+        const int old = atomicAdd(&ws_cnt[tile_id], 1);
+        s_last = (old == S - 1) ? 1 : 0;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (s_last) {
+        __threadfence();
+        const float* base = ws_part + (int64_t)tile_id * S * C::TILE_F;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
-        float g[16], u[16];
+        for (int c = 0; c < BN; c += 16) {
+          float g[16], u[16];
 #pragma unroll
-        for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
-        for (int r = 0; r < S; ++r) {
-          const uint32_t pb = mapa_shared(base, (uint32_t)r);
+          for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
+          for (int r = 0; r < S; ++r) {
+            const float* src = base + (int64_t)r * C::TILE_F;
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            float v;
-            asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(pb + (uint32_t)(((c + t) * 128 + row_local) * 4)) : "memory");
-            g[t] += v;
-            if (DUAL) {
-              asm volatile("ld.shared::cluster.f32 %0, [%1];"
-                           : "=f"(v)
-                           : "r"(pb + (uint32_t)((BN * 128 + (c + t) * 128 + row_local) * 4))
-                           : "memory");
-              u[t] += v;
+            for (int t = 0; t < 16; ++t) {
+              g[t] += __ldcg(src + (c + t) * 128 + row_local);
+              if (DUAL) u[t] += __ldcg(src + BN * 128 + (c + t) * 128 + row_local);
             }
           }
+          epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
         }
-        epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+        if (threadIdx.x == 64) ws_cnt[tile_id] = 0;
       }
     }
-    cluster_sync();
   }
 
   tc_fence_before();
@@ -349,10 +357,15 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
+template <int KIND, bool DUAL, int EPI>
+bool gemm_sk_dispatch(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, const GemmArgs& a,
+                      torch::Tensor& ws, cudaStream_t st);
+
 struct LaunchPlan {
   int BN;
-  int S;  // splits (cluster size)
+  int S;        // K splits
   int n_tiles;
+  bool unpack;  // fp4 weights loaded packed and expanded on chip
 };
 
 static int g_num_sms = 0;
@@ -365,7 +378,7 @@ static int num_sms() {
   return g_num_sms;
 }
 
-static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual) {
+static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
   LaunchPlan p;
   if (M <= 16) p.BN = 16;
   else if (M <= 32) p.BN = 32;
@@ -373,62 +386,94 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual) {
   else if (M <= 128) p.BN = 128;
   else p.BN = dual ? 128 : 256;  // two accumulators of 256 columns would not fit in TMEM
   if (p.BN == 256 && M > 256) {
-    // use 128-token tiles when 256-token tiles would leave SMs idle
     const int rt = (N + 127) / 128;
     if ((long)rt * ((M + 255) / 256) < num_sms()) p.BN = 128;
   }
   p.n_tiles = (M + p.BN - 1) / p.BN;
+  static int unpack_knob = -1;
+  if (unpack_knob < 0) {
+    const char* e = getenv("R9K_FP4_UNPACK");
+    unpack_knob = (e && e[0] == '1') ? 1 : 0;
+  }
+  p.unpack = unpack_knob == 1 && fp4 && p.BN <= 64;
   const int row_tiles = (N + 127) / 128;
   const int tiles = row_tiles * p.n_tiles;
   p.S = 1;
   if (p.BN <= 64) {
-    // split K across a cluster until about two CTAs per SM are busy; keep >= 4 chunks per split
-    const int target = 2 * num_sms();
-    while (p.S < 8 && tiles * p.S * 2 <= target && kchunks / (p.S * 2) >= 4) p.S *= 2;
+    // fill the resident CTA slots: split K (global-memory fix-up, no clusters) with >= 4 chunks/split
+    const int per_sm = (dual && p.unpack) ? 1 : 2;
+    const int target = per_sm * num_sms();
+    p.S = std::max(1, std::min(16, target / std::max(1, tiles)));
+    while (p.S > 1 && kchunks / p.S < 4) --p.S;
   }
   return p;
 }
 
-template <int KIND, int BN, bool DUAL, int EPI, int STAGES>
+// workspace layout: [65536 int counters][partials]
+static constexpr int64_t kWsCounters = 65536;
+
+template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, GemmArgs args,
-                        const LaunchPlan& p, cudaStream_t stream) {
-  using C = GemmCfg<KIND, BN, DUAL, STAGES>;
-  auto kern = gemm_tc_kernel<KIND, BN, DUAL, EPI, STAGES>;
+                        LaunchPlan p, torch::Tensor* ws, cudaStream_t stream) {
+  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK>;
+  auto kern = gemm_tc_kernel<KIND, BN, DUAL, EPI, NP, NC, UNPACK>;
   static bool attr_set = false;
   if (!attr_set) {
     TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) == cudaSuccess,
                 "r9k gemm: cannot set smem size");
-    cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     attr_set = true;
   }
+  const int grid_x = (args.N + 127) / 128;
+  float* part = nullptr;
+  int* cnt = nullptr;
+  if (p.S > 1) {
+    const int64_t need = (int64_t)grid_x * p.n_tiles * p.S * C::TILE_F;
+    if (ws == nullptr || ws->numel() < kWsCounters + need || grid_x * p.n_tiles > kWsCounters) p.S = 1;
+    else {
+      cnt = reinterpret_cast<int*>(ws->data_ptr<float>());
+      part = ws->data_ptr<float>() + kWsCounters;
+    }
+  }
+  args.splits = p.S;
   args.kc_per_split = (args.kchunks + p.S - 1) / p.S;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((args.N + 127) / 128, p.n_tiles * p.S, 1);
+  cfg.gridDim = dim3(grid_x, p.n_tiles * p.S, 1);
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = p.S;
-  attr[0].val.clusterDim.z = 1;
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, args);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, args, part, cnt);
   TORCH_CHECK(e == cudaSuccess, "r9k gemm launch failed: ", cudaGetErrorString(e));
 }
 
 template <int KIND, bool DUAL, int EPI>
 static void dispatch_bn(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, GemmArgs args,
-                        const LaunchPlan& p, cudaStream_t st) {
-  // stage counts sized for ~2 CTAs/SM on skinny tiles and 1 CTA/SM on wide tiles
+                        const LaunchPlan& p, torch::Tensor* ws, cudaStream_t st) {
+  // skinny tiles: two CTAs/SM (~110 KB each), fp4 expanded on chip with a deep packed ring;
+  // wide tiles: one CTA/SM
+  if constexpr (KIND == KIND_MX) {
+    if (p.unpack) {
+      switch (p.BN) {
+        case 16: DUAL ? launch_gemm<KIND, 16, DUAL, EPI, 7, 2, true>(ta, ta2, tb, args, p, ws, st)
+                      : launch_gemm<KIND, 16, DUAL, EPI, 6, 2, true>(ta, ta2, tb, args, p, ws, st); return;
+        case 32: DUAL ? launch_gemm<KIND, 32, DUAL, EPI, 6, 2, true>(ta, ta2, tb, args, p, ws, st)
+                      : launch_gemm<KIND, 32, DUAL, EPI, 5, 2, true>(ta, ta2, tb, args, p, ws, st); return;
+        default: DUAL ? launch_gemm<KIND, 64, DUAL, EPI, 5, 2, true>(ta, ta2, tb, args, p, ws, st)
+                      : launch_gemm<KIND, 64, DUAL, EPI, 4, 2, true>(ta, ta2, tb, args, p, ws, st); return;
+      }
+    }
+  }
   switch (p.BN) {
-    case 16: launch_gemm<KIND, 16, DUAL, EPI, DUAL ? 3 : 5>(ta, ta2, tb, args, p, st); break;
-    case 32: launch_gemm<KIND, 32, DUAL, EPI, DUAL ? 3 : 5>(ta, ta2, tb, args, p, st); break;
-    case 64: launch_gemm<KIND, 64, DUAL, EPI, DUAL ? 2 : 4>(ta, ta2, tb, args, p, st); break;
-    case 128: launch_gemm<KIND, 128, DUAL, EPI, DUAL ? 3 : 4>(ta, ta2, tb, args, p, st); break;
+    case 16: launch_gemm<KIND, 16, DUAL, EPI, DUAL ? 3 : 5, 1, false>(ta, ta2, tb, args, p, ws, st); break;
+    case 32: launch_gemm<KIND, 32, DUAL, EPI, DUAL ? 3 : 5, 1, false>(ta, ta2, tb, args, p, ws, st); break;
+    case 64: launch_gemm<KIND, 64, DUAL, EPI, DUAL ? 2 : 4, 1, false>(ta, ta2, tb, args, p, ws, st); break;
+    case 128: launch_gemm<KIND, 128, DUAL, EPI, DUAL ? 3 : 4, 1, false>(ta, ta2, tb, args, p, ws, st); break;
     default:
-      if constexpr (!DUAL) launch_gemm<KIND, 256, false, EPI, 4>(ta, ta2, tb, args, p, st);
+      if constexpr (!DUAL) launch_gemm<KIND, 256, false, EPI, 4, 1, false>(ta, ta2, tb, args, p, ws, st);
       break;
   }
 }
@@ -450,24 +495,49 @@ static void check_sf(const torch::Tensor& sf, int64_t rows, int64_t K, const cha
 //   w: uint8 [N, K/2] (fp4, w_fp4=true) or [N, K] (e4m3); w_sf: chunk-layout ue8m0
 //   x: uint8 [M, K] e4m3; x_sf: chunk-layout ue8m0
 //   epi: 0 bf16 (+residual), 1 f32
+// weights: [N, K/2 | K] row-major, or pre-tiled [units, 128, 64 | 128] (units = ceil(N/128) * K/128)
+static CUtensorMap weight_tmap(const torch::Tensor& w, bool fp4, int64_t N, int64_t K, bool unpack) {
+  if (w.dim() == 3) {
+    TORCH_CHECK(w.size(1) == 128 && w.size(2) == (fp4 ? 64 : 128) && w.is_contiguous(), "tiled weight shape");
+    TORCH_CHECK(w.size(0) == ((N + 127) / 128) * (K / 128), "tiled weight: unit count does not match N, K");
+    if (unpack) return tmap_units_packed_3d(w.data_ptr(), w.size(0));
+    return tmap_units_3d(w.data_ptr(), w.size(0), fp4);
+  }
+  TORCH_CHECK(w.size(0) == N && w.size(1) == (fp4 ? K / 2 : K), "weight/activation shape mismatch");
+  if (unpack) return tmap_fp4_packed(w.data_ptr(), N, K);
+  return fp4 ? tmap_fp4_kmajor(w.data_ptr(), N, K, 128) : tmap_u8_kmajor(w.data_ptr(), N, K, 128);
+}
+
+static bool use_stream_k() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("R9K_GEMM_SK");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf,
-             torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha, torch::Tensor status) {
-  const int64_t N = w.size(0), M = x.size(0), K = x.size(1);
+             torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha, torch::Tensor status,
+             c10::optional<torch::Tensor> workspace) {
+  const int64_t N = out.size(1), M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 128 == 0, "gemm_mx: K must be a multiple of 128");
-  TORCH_CHECK(w.size(1) == (w_fp4 ? K / 2 : K), "gemm_mx: weight/activation K mismatch");
   check_sf(w_sf, N, K, "gemm_mx weight");
   check_sf(x_sf, M, K, "gemm_mx activation");
   TORCH_CHECK(out.size(0) == M && out.size(1) == N && out.stride(1) == 1, "gemm_mx: bad out");
   const bool f32 = out.dtype() == torch::kFloat32;
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
-  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 128), false);
+  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 128), false, w_fp4);
   check_act_sf(x_sf, p, K, "gemm_mx");
-  CUtensorMap ta = w_fp4 ? tmap_fp4_kmajor(w.data_ptr(), N, K, 128) : tmap_u8_kmajor(w.data_ptr(), N, K, 128);
+  const bool sk = use_stream_k() && M <= 64;
+  if (sk) p.unpack = false;
+  CUtensorMap ta = weight_tmap(w, w_fp4, N, K, p.unpack);
   CUtensorMap tb = tmap_u8_kmajor(x.data_ptr(), M, K, p.BN);
   GemmArgs a = {};
   a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
   a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
+  a.a_tiled = w.dim() == 3;
   a.sfa = w_sf.data_ptr<uint8_t>(); a.sfb = x_sf.data_ptr<uint8_t>(); a.sf_kblocks = (int)(K / 32);
   a.out = out.data_ptr(); a.ldo = (int)out.stride(0);
   if (residual.has_value() && residual->defined()) {
@@ -479,17 +549,25 @@ void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, t
   a.status = status.data_ptr<int>();
   a.timeout_ns = 1000000000ull;
   auto st = at::cuda::getCurrentCUDAStream();
-  if (f32) dispatch_bn<KIND_MX, false, EPI_F32>(ta, ta, tb, a, p, st);
-  else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, a, p, st);
+  torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
+  if (sk && ws != nullptr) {
+    const bool done = f32 ? gemm_sk_dispatch<KIND_MX, false, EPI_F32>(ta, ta, tb, a, *ws, st)
+                          : gemm_sk_dispatch<KIND_MX, false, EPI_BF16>(ta, ta, tb, a, *ws, st);
+    if (done) return;
+    p = plan_gemm((int)N, (int)M, (int)(K / 128), false, w_fp4);
+    ta = weight_tmap(w, w_fp4, N, K, p.unpack);
+  }
+  if (f32) dispatch_bn<KIND_MX, false, EPI_F32>(ta, ta, tb, a, p, ws, st);
+  else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, a, p, ws, st);
 }
 
 // Fused gate/up projection + SwiGLU + MXFP8 quantisation of the result.
 void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, torch::Tensor wu_sf, bool w_fp4,
                     torch::Tensor x, torch::Tensor x_sf, torch::Tensor out_q, torch::Tensor out_sf,
-                    torch::Tensor status) {
-  const int64_t N = wg.size(0), M = x.size(0), K = x.size(1);
+                    torch::Tensor status, c10::optional<torch::Tensor> workspace) {
+  const int64_t N = out_q.size(1), M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 128 == 0 && N % 32 == 0, "gemm_mx_swiglu: K % 128 and N % 32 required");
-  TORCH_CHECK(wu.size(0) == N, "gemm_mx_swiglu: gate/up mismatch");
+  TORCH_CHECK(wu.sizes() == wg.sizes(), "gemm_mx_swiglu: gate/up mismatch");
   check_sf(wg_sf, N, K, "swiglu gate");
   check_sf(wu_sf, N, K, "swiglu up");
   check_sf(x_sf, M, K, "swiglu act");
@@ -497,14 +575,17 @@ void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, tor
   TORCH_CHECK(out_q.size(0) == M && out_q.size(1) == N, "gemm_mx_swiglu: bad out");
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
-  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 128), true);
+  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 128), true, w_fp4);
   check_act_sf(x_sf, p, K, "gemm_mx_swiglu");
-  CUtensorMap ta = w_fp4 ? tmap_fp4_kmajor(wg.data_ptr(), N, K, 128) : tmap_u8_kmajor(wg.data_ptr(), N, K, 128);
-  CUtensorMap ta2 = w_fp4 ? tmap_fp4_kmajor(wu.data_ptr(), N, K, 128) : tmap_u8_kmajor(wu.data_ptr(), N, K, 128);
+  const bool sk = use_stream_k() && M <= 64;
+  if (sk) p.unpack = false;
+  CUtensorMap ta = weight_tmap(wg, w_fp4, N, K, p.unpack);
+  CUtensorMap ta2 = weight_tmap(wu, w_fp4, N, K, p.unpack);
   CUtensorMap tb = tmap_u8_kmajor(x.data_ptr(), M, K, p.BN);
   GemmArgs a = {};
   a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
   a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
+  a.a_tiled = wg.dim() == 3;
   a.sfa = wg_sf.data_ptr<uint8_t>(); a.sfa2 = wu_sf.data_ptr<uint8_t>(); a.sfb = x_sf.data_ptr<uint8_t>();
   a.sf_kblocks = (int)(K / 32);
   a.out = out_q.data_ptr(); a.ldo = (int)out_q.stride(0);
@@ -512,12 +593,20 @@ void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, tor
   a.alpha = 1.f;
   a.status = status.data_ptr<int>();
   a.timeout_ns = 1000000000ull;
-  dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, a, p, at::cuda::getCurrentCUDAStream());
+  auto st = at::cuda::getCurrentCUDAStream();
+  torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
+  if (sk && ws != nullptr) {
+    if (gemm_sk_dispatch<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, a, *ws, st)) return;
+    p = plan_gemm((int)N, (int)M, (int)(K / 128), true, w_fp4);
+    ta = weight_tmap(wg, w_fp4, N, K, p.unpack);
+    ta2 = weight_tmap(wu, w_fp4, N, K, p.unpack);
+  }
+  dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, a, p, ws, st);
 }
 
 // bf16 x bf16 -> bf16/f32 (kind::f16)
 void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optional<torch::Tensor> residual,
-               double alpha, torch::Tensor status) {
+               double alpha, torch::Tensor status, c10::optional<torch::Tensor> workspace) {
   const int64_t N = w.size(0), M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 64 == 0 && w.size(1) == K, "gemm_bf16: K must match and be a multiple of 64");
   TORCH_CHECK(w.dtype() == torch::kBFloat16 && x.dtype() == torch::kBFloat16, "gemm_bf16: bf16 inputs");
@@ -525,7 +614,7 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
   const bool f32 = out.dtype() == torch::kFloat32;
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
-  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 64), false);
+  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 64), false, false);
   CUtensorMap ta = tmap_bf16_kmajor(w.data_ptr(), N, K, w.stride(0), 128);
   CUtensorMap tb = tmap_bf16_kmajor(x.data_ptr(), M, K, x.stride(0), p.BN);
   GemmArgs a = {};
@@ -539,8 +628,14 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
   a.status = status.data_ptr<int>();
   a.timeout_ns = 1000000000ull;
   auto st = at::cuda::getCurrentCUDAStream();
-  if (f32) dispatch_bn<KIND_BF16, false, EPI_F32>(ta, ta, tb, a, p, st);
-  else dispatch_bn<KIND_BF16, false, EPI_BF16>(ta, ta, tb, a, p, st);
+  torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
+  if (use_stream_k() && M <= 64 && ws != nullptr) {
+    const bool done = f32 ? gemm_sk_dispatch<KIND_BF16, false, EPI_F32>(ta, ta, tb, a, *ws, st)
+                          : gemm_sk_dispatch<KIND_BF16, false, EPI_BF16>(ta, ta, tb, a, *ws, st);
+    if (done) return;
+  }
+  if (f32) dispatch_bn<KIND_BF16, false, EPI_F32>(ta, ta, tb, a, p, ws, st);
+  else dispatch_bn<KIND_BF16, false, EPI_BF16>(ta, ta, tb, a, p, ws, st);
 }
 
 }  // namespace r9k

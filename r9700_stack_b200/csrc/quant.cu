@@ -34,30 +34,64 @@ R9K_DEVINL uint32_t e2m1_encode(float v) {
 // ------------------------------------------------------------------------------------------------
 // RMSNorm (+ residual) (+ MXFP8 quant)
 // ------------------------------------------------------------------------------------------------
+// One CTA per row; one thread per 32-element block (the MX quantisation block), so the quantisation
+// needs no cross-thread reduction and every load/store is a 16-byte vector.
 template <typename TIn>
 __global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, const __nv_bfloat16* __restrict__ res_in,
                                      __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
                                      int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y, int64_t ldy,
                                      uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
-  extern __shared__ float srow[];
+  pdl_trigger();  // the next GEMM may start streaming its weights
   __shared__ float sred[32];
   const int64_t r = blockIdx.x;
-  const TIn* xr = x + r * ldx;
+  const int kblocks = K / 32;
+  const int blk = threadIdx.x;
+  const bool act = blk < kblocks;
+  float v[32];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < K; i += blockDim.x) {
-    float v;
-    if constexpr (std::is_same<TIn, float>::value) v = xr[i];
-    else v = __bfloat162float(xr[i]);
+  if (act) {
+    const TIn* xr = x + r * ldx + blk * 32;
+    if constexpr (std::is_same<TIn, float>::value) {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const float4 f = reinterpret_cast<const float4*>(xr)[i];
+        v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = reinterpret_cast<const uint4*>(xr)[i];
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] = __bfloat162float(e[k]);
+      }
+    }
     if (res_in != nullptr) {
-      v += __bfloat162float(res_in[r * (int64_t)K + i]);
+      const __nv_bfloat16* rr = res_in + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = reinterpret_cast<const uint4*>(rr)[i];
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] += __bfloat162float(e[k]);
+      }
     }
     if (res_out != nullptr) {
-      const __nv_bfloat16 hb = __float2bfloat16(v);
-      res_out[r * (int64_t)K + i] = hb;
-      v = __bfloat162float(hb);  // the residual stream is bf16: normalise what is stored
+      __nv_bfloat16* ro = res_out + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 raw;
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          e[k] = __float2bfloat16(v[8 * i + k]);
+          v[8 * i + k] = __bfloat162float(e[k]);  // the residual stream is bf16: normalise what is stored
+        }
+        reinterpret_cast<uint4*>(ro)[i] = raw;
+      }
     }
-    srow[i] = v;
-    ss += v * v;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
   }
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = ss;
@@ -68,27 +102,50 @@ __global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, con
     if (threadIdx.x == 0) sred[0] = t;
   }
   __syncthreads();
+  if (!act) return;
   const float rr = rsqrtf(sred[0] / (float)K + eps);
-  const int kblocks = K / 32;
-  // each warp handles 32-element blocks: lane i owns element i of the block
-  const int lane = threadIdx.x & 31;
-  for (int blk = threadIdx.x >> 5; blk < kblocks; blk += blockDim.x >> 5) {
-    const int i = blk * 32 + lane;
-    float wv = __bfloat162float(w[i]);
-    if (plus_one) wv += 1.f;
-    float v = srow[i] * rr * wv;
-    if (y != nullptr) {
-      const __nv_bfloat16 vb = __float2bfloat16(v);
-      y[r * ldy + i] = vb;
-      v = __bfloat162float(vb);
+  const __nv_bfloat16* wb = w + blk * 32;
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 raw = reinterpret_cast<const uint4*>(wb)[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float wv = __bfloat162float(e[k]);
+      if (plus_one) wv += 1.f;
+      v[8 * i + k] = v[8 * i + k] * rr * wv;
     }
-    if (q != nullptr) {
-      float am = fabsf(v);
-      for (int o = 16; o > 0; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
-      const int e = mx_exponent(am, 448.f);
-      q[r * (int64_t)K + i] = f32_to_e4m3(v * exp2i(-e));
-      if (lane == 0) sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+  }
+  if (y != nullptr) {
+    __nv_bfloat16* yo = y + r * ldy + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 raw;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        e[k] = __float2bfloat16(v[8 * i + k]);
+        v[8 * i + k] = __bfloat162float(e[k]);
+      }
+      reinterpret_cast<uint4*>(yo)[i] = raw;
     }
+  }
+  if (q != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+    const int e = mx_exponent(am, 448.f);
+    const float si = exp2i(-e);
+    uint8_t* qo = q + r * (int64_t)K + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint4 raw;
+      uint8_t* b8 = reinterpret_cast<uint8_t*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) b8[k] = f32_to_e4m3(v[16 * i + k] * si);
+      reinterpret_cast<uint4*>(qo)[i] = raw;
+    }
+    sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
   }
 }
 
@@ -102,8 +159,11 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::op
   if (M == 0) return;
   const at::cuda::CUDAGuard guard(x.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  const int threads = K >= 4096 ? 512 : 256;
-  const size_t smem = K * sizeof(float);
+  const int threads = std::max(32, (int)((K / 32 + 31) / 32 * 32));
+  TORCH_CHECK(threads <= 1024, "rmsnorm_quant: K <= 32768");
+  TORCH_CHECK((x.stride(0) * x.element_size()) % 16 == 0 && (y.has_value() && y->defined() ? y->stride(0) % 8 == 0 : true),
+              "rmsnorm_quant: rows must be 16-byte aligned");
+  const size_t smem = 0;
   auto ptr_bf = [](const c10::optional<torch::Tensor>& t) -> __nv_bfloat16* {
     return (t.has_value() && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
   };

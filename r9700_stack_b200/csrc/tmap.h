@@ -60,4 +60,39 @@ inline CUtensorMap tmap_bf16_kmajor(void* base, int64_t rows, int64_t K, int64_t
                       (uint32_t)box_rows);
 }
 
+// Packed fp4 weights read as plain bytes (expanded on chip): box of 128 rows x 64 bytes, no swizzle.
+inline CUtensorMap tmap_fp4_packed(void* base, int64_t rows, int64_t K) {
+  return make_tmap_2d(CU_TENSOR_MAP_DATA_TYPE_UINT8, base, (uint64_t)(K / 2), (uint64_t)rows, (uint64_t)(K / 2), 64, 128,
+                      CU_TENSOR_MAP_SWIZZLE_NONE);
+}
+inline CUtensorMap tmap_units_packed_3d(void* base, int64_t units) {
+  CUtensorMap m;
+  cuuint64_t dims[3] = {64, 128, (cuuint64_t)units};
+  cuuint64_t strides[2] = {64, 64 * 128};
+  cuuint32_t box[3] = {64, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base, dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "r9k: packed tiled weight tensor map failed (", (int)r, ")");
+  return m;
+}
+
+// Pre-tiled weights: [units][128 rows][row_bytes] with every unit (128 rows x 128 K elements)
+// contiguous, so one TMA box is one contiguous 8 KB (fp4) / 16 KB (fp8) read from HBM.
+inline CUtensorMap tmap_units_3d(void* base, int64_t units, bool fp4) {
+  const uint64_t row_bytes = fp4 ? 64 : 128;
+  CUtensorMap m;
+  cuuint64_t dims[3] = {128, 128, (cuuint64_t)units};
+  cuuint64_t strides[2] = {row_bytes, row_bytes * 128};
+  cuuint32_t box[3] = {128, 128, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 31) == 0, "tiled weight: base must be 32-byte aligned");
+  CUresult r = get_encode_fn()(&m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, base,
+                               dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "r9k: tiled weight tensor map failed (", (int)r, ")");
+  return m;
+}
+
 }  // namespace r9k

@@ -150,6 +150,7 @@ class ModelRunner:
         self.stream = torch.cuda.current_stream(self.device)
         self.h2d_bytes = 0
         self.d2h_bytes = 0
+        self.device_events: list | None = None  # (start, end) CUDA events around each replayed step
 
     # ------------------------------------------------------------------------------------------
     def _upload(self, arr: np.ndarray) -> None:
@@ -213,12 +214,20 @@ class ModelRunner:
             lay_g = Layout(lay.T, lay.S, self.max_blocks_per_seq, lay.R)
             arr = _relayout(arr, lay, lay_g)
             self._upload(arr)
-            self.graphs[gb].replay()
+            if self.device_events is not None:
+                ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                ev0.record()
+                self.graphs[gb].replay()
+                ev1.record()
+                self.device_events.append((ev0, ev1))
+            else:
+                self.graphs[gb].replay()
             R = lay.R
         else:
             lay, arr = pack_step(out, self.block_size, draft=draft)
             self._upload(arr)
             meta = self.meta.views(lay, write_state=write_state)
+            meta.host_seqs = _host_seqs(out, draft)
             self.model.forward(meta, self.ws, lay.T, lay.R)
             R = lay.R
             torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
@@ -237,6 +246,15 @@ class ModelRunner:
             res[ch.seq.seq_id] = toks[r : r + 1 + nd]
             r += 1 + nd
         return res
+
+
+def _host_seqs(out: SchedulerOutput, draft=None) -> list[tuple[int, int]]:
+    res, t = [], 0
+    for ch in out.chunks:
+        n = ch.n + (len(draft[ch.seq.seq_id]) if draft is not None and ch.seq.seq_id in draft else 0)
+        res.append((t, n))
+        t += n
+    return res
 
 
 def _relayout(arr: np.ndarray, src: Layout, dst: Layout) -> np.ndarray:

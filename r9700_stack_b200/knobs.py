@@ -1,0 +1,47 @@
+"""``R9K_*`` environment knobs.
+
+Every kernel path has a switch that selects an alternative implementation without a rebuild, in the
+spirit of the reference's ``R9K_*=stock`` contract (README.md:144-145): e.g. ``R9K_ATTN=simple``
+selects the CUDA-core paged attention instead of the tcgen05 flash-attention kernel, and
+``R9K_COMM=nccl`` routes every collective through NCCL. ``R9K_DISABLE=a,b`` lists coarse opt-outs.
+Values are read once per process (``refresh()`` re-reads them, for tests).
+"""
+from __future__ import annotations
+
+import os
+
+_DEFAULTS = {
+    "R9K_ATTN": "tc",  # tc | simple
+    "R9K_WEIGHT_TILED": "1",  # 1: MX weights stored as contiguous 128x128 units; 0: row-major
+    "R9K_GEMM_SK": "0",  # 1: skinny GEMMs use the persistent stream-K kernel
+    "R9K_FP4_UNPACK": "0",  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
+    "R9K_COMM": "fused",  # fused | nccl
+    "R9K_GDN_STATE": "",  # "" (model default) | bf16 | fp32
+    "R9K_DISABLE": "",
+    "R9K_AR_ONESHOT_MAX_KB": "512",
+    "R9K_SPIN_TIMEOUT_MS": "1000",
+}
+_cache: dict[str, str] = {}
+
+
+def get(name: str) -> str:
+    if name not in _cache:
+        _cache[name] = os.environ.get(name, _DEFAULTS.get(name, ""))
+    return _cache[name]
+
+
+def get_int(name: str) -> int:
+    return int(get(name) or 0)
+
+
+def disabled(feature: str) -> bool:
+    return feature in {x.strip() for x in get("R9K_DISABLE").split(",") if x.strip()}
+
+
+def refresh() -> None:
+    _cache.clear()
+
+
+def all_knobs() -> dict[str, str]:
+    keys = set(_DEFAULTS) | {k for k in os.environ if k.startswith("R9K_")}
+    return {k: get(k) for k in sorted(keys)}

@@ -19,9 +19,10 @@ from dataclasses import dataclass
 
 import torch
 
-from .. import _native
+from .. import _native, knobs
 from ..ops import linear as L
 from .config import HybridConfig, ParallelConfig
+from ..utils import status as _status
 from .weights import WeightFactory, from_float
 
 
@@ -64,6 +65,8 @@ class StepMeta:
     seq_has_state: torch.Tensor  # [S] int32
     logits_idx: torch.Tensor  # [R] int32 rows of the token batch whose logits are needed
     write_state: bool = True  # False during speculative verification
+    # host copy of (first token, tokens) per sequence for eager prefill steps; None on the decode path
+    host_seqs: list | None = None
 
 
 class Workspace:
@@ -94,6 +97,11 @@ class Workspace:
         self.gdn_bf16 = torch.zeros(max_tokens, g["hv"] * c.gdn_head_dim, dtype=torch.bfloat16, device=dev)
         if model.ffn_local > 0:
             self.ffn_act = L.alloc_act(max_tokens, model.ffn_local, dev)
+        # split-KV partials for the tcgen05 decode attention
+        self.nsplit_max = 16
+        rows = max_logit_rows * a["hq"]
+        self.part_o = torch.zeros(rows, self.nsplit_max, c.head_dim, dtype=torch.float32, device=dev)
+        self.part_ml = torch.zeros(rows, self.nsplit_max, 2, dtype=torch.float32, device=dev)
         self.logit_rows = max_logit_rows
         self.final_act = L.alloc_act(max_logit_rows, H, dev)
         self.final_bf16 = torch.zeros(max_logit_rows, H, dtype=torch.bfloat16, device=dev)
@@ -229,12 +237,32 @@ class HybridLM:
                                   c.norm_plus_one, meta.positions, self.cos_sin, c.rotary_dim, meta.slots,
                                   ws.q[:T], kc, vc, self.k_scale, self.v_scale)
         gate = qkv[:, gate_off:gate_off + hq * D] if gate_off >= 0 else None
-        if self.mx:
+        out_q = ws.attn_act.q[:T] if self.mx else None
+        out_sf = ws.attn_act.sf if self.mx else None
+        out_bf = None if self.mx else ws.attn_bf16[:T]
+        G = hq // hkv
+        if knobs.get("R9K_ATTN") == "simple" or D != 256:
             _ops().paged_attention(ws.q[:T], kc, vc, meta.block_table, meta.tok_seq, meta.tok_ctx, self.sm_scale,
-                                   self.k_scale, self.v_scale, gate, None, ws.attn_act.q[:T], ws.attn_act.sf, 0)
+                                   self.k_scale, self.v_scale, gate, out_bf, out_q, out_sf, 0)
+        elif meta.host_seqs is not None and (T > ws.logit_rows or any(n * G > 128 for _, n in meta.host_seqs)):
+            # prefill: query tiles of floor(128 / G) tokens, whole causal key range per CTA
+            qt = 128 // G
+            tab = []
+            for si, (t0, n) in enumerate(meta.host_seqs):
+                for j in range(0, n, qt):
+                    tab += [si, t0 + j, min(qt, n - j)]
+            tt = torch.tensor(tab, dtype=torch.int32).to(self.device, non_blocking=True)
+            _ops().attn_tc_prefill(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, tt, len(tab) // 3,
+                                   self.sm_scale, self.k_scale, self.v_scale, gate, out_bf, out_q, out_sf,
+                                   _status.status(self.device))
         else:
-            _ops().paged_attention(ws.q[:T], kc, vc, meta.block_table, meta.tok_seq, meta.tok_ctx, self.sm_scale,
-                                   self.k_scale, self.v_scale, gate, ws.attn_bf16[:T], None, None, 0)
+            S = meta.seq_start.shape[0]
+            nsplit = max(1, min(ws.nsplit_max, -(-296 // (S * hkv))))
+            po = ws.part_o.view(-1)[: T * hq * nsplit * D].view(T * hq, nsplit, D)
+            pml = ws.part_ml.view(-1)[: T * hq * nsplit * 2].view(T * hq, nsplit, 2)
+            _ops().attn_tc_decode(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, meta.seq_start, meta.seq_len,
+                                  self.sm_scale, self.k_scale, self.v_scale, po, pml, gate, out_bf, out_q, out_sf,
+                                  _status.status(self.device))
         self._linear(ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"], ws.y[:T])
 
     def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):

@@ -10,6 +10,7 @@ from __future__ import annotations
 
 import torch
 
+from .. import knobs
 from ..ops import linear as L
 from ..quant import formats as F
 
@@ -37,18 +38,23 @@ class WeightFactory:
         return (1.0 + self.randn(n, std=0.1)).to(torch.bfloat16)
 
 
-def from_float(w: torch.Tensor, fmt: str):
+def from_float(w: torch.Tensor, fmt: str, tiled: bool | None = None):
+    """Quantise into `fmt`, then apply the load-time transforms (format conversion, and the
+    contiguous-unit tiling of MX weights that makes every TMA box one contiguous HBM read)."""
+    if tiled is None:
+        tiled = knobs.get("R9K_WEIGHT_TILED") != "0"
     if fmt == "nvfp4":
         packed, s16, g = L.nvfp4_quantize(w)
-        return L.mx_from_nvfp4(packed, s16, g, search=True)
+        mw = L.mx_from_nvfp4(packed, s16, g, search=True)
+        return mw.to_tiled() if tiled else mw
     if fmt == "mxfp4":
-        return L.mx_from_float(w, fp4=True, search=True)
+        return L.mx_from_float(w, fp4=True, search=True, tiled=tiled)
     if fmt == "mxfp8":
-        return L.mx_from_float(w, fp4=False)
+        return L.mx_from_float(w, fp4=False, tiled=tiled)
     if fmt == "block_fp8":
         # block-128 fp8 checkpoint tensor -> MXFP8 at load
         q, s = block_fp8_quantize_device(w)
-        return L.mx_from_float(block_fp8_dequant_device(q, s), fp4=False)
+        return L.mx_from_float(block_fp8_dequant_device(q, s), fp4=False, tiled=tiled)
     if fmt == "bf16":
         return L.BF16Weight(w.to(torch.bfloat16).contiguous())
     raise ValueError(f"unknown weight format {fmt}")

@@ -27,25 +27,70 @@ def _ops():
     return _native.ops()
 
 
+_WS: dict[int, torch.Tensor] = {}
+SK_WORKSPACE_FLOATS = 65536 + 4 * 148 * 2 * 2 * 64 * 128 + 4096
+
+
+def gemm_workspace(device) -> torch.Tensor | None:
+    """Per-device fp32 scratch of the split-K / stream-K decode GEMMs: 65536 per-tile arrival counters
+    (kept at zero between calls by the kernels themselves) followed by partial-tile slots. GEMMs that
+    share it must run in stream order (one stream per device)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    t = _WS.get(idx)
+    if t is None:
+        t = torch.zeros(SK_WORKSPACE_FLOATS, dtype=torch.float32, device=f"cuda:{idx}")
+        _WS[idx] = t
+    return t
+
+
 def sf_bytes(rows: int, K: int) -> int:
     return F.sf_num_bytes(rows, K // 32)
 
 
 @dataclass
 class MXWeight:
-    q: torch.Tensor  # uint8 [N, K/2] (fp4) or [N, K] (e4m3)
+    """MX weight. ``q`` is row-major [N, K/2 | K], or pre-tiled [units, 128, 64 | 128] where unit
+    (t, kc) = rows 128t..128t+127 x K elements 128kc..128kc+127 is contiguous (rows padded to 128):
+    one TMA box is then one contiguous HBM read. The scale chunks use the same unit order."""
+
+    q: torch.Tensor
     sf: torch.Tensor  # uint8 chunk layout
     fp4: bool
     N: int
     K: int
 
     @property
+    def tiled(self) -> bool:
+        return self.q.dim() == 3
+
+    @property
     def nbytes(self) -> int:
         return self.q.numel() + self.sf.numel()
 
+    def rowmajor_q(self) -> torch.Tensor:
+        if not self.tiled:
+            return self.q
+        cb = self.q.shape[-1]
+        kch = self.K // 128
+        rt = self.q.shape[0] // kch
+        return self.q.view(rt, kch, 128, cb).permute(0, 2, 1, 3).reshape(rt * 128, kch * cb)[: self.N].contiguous()
+
+    def to_tiled(self) -> "MXWeight":
+        if self.tiled:
+            return self
+        cb = 64 if self.fp4 else 128
+        kch = self.K // 128
+        rt = (self.N + 127) // 128
+        q = self.q
+        if rt * 128 != self.N:
+            q = torch.cat([q, torch.zeros(rt * 128 - self.N, q.shape[1], dtype=q.dtype, device=q.device)], 0)
+        t = q.view(rt, 128, kch, cb).permute(0, 2, 1, 3).contiguous().view(rt * kch, 128, cb)
+        return MXWeight(t, self.sf, self.fp4, self.N, self.K)
+
     def dequant(self) -> torch.Tensor:
         out = torch.empty(self.N, self.K, dtype=torch.float32, device=self.q.device)
-        _ops().dequant_mx(self.q, self.sf, self.fp4, out)
+        _ops().dequant_mx(self.rowmajor_q(), self.sf, self.fp4, out)
         return out
 
     def narrow_rows(self, start: int, length: int) -> "MXWeight":
@@ -54,7 +99,12 @@ class MXWeight:
         kchunks = (self.K // 32 + 3) // 4
         c0 = (start // 128) * kchunks * 512
         c1 = ((start + length + 127) // 128) * kchunks * 512
-        return MXWeight(self.q[start : start + length], self.sf[c0:c1], self.fp4, length, self.K)
+        if self.tiled:
+            kch = self.K // 128
+            q = self.q[(start // 128) * kch : ((start + length + 127) // 128) * kch]
+        else:
+            q = self.q[start : start + length]
+        return MXWeight(q, self.sf[c0:c1], self.fp4, length, self.K)
 
 
 @dataclass
@@ -98,7 +148,7 @@ def alloc_act(M: int, K: int, device) -> MXAct:
 # ------------------------------------------------------------------------------------------------
 # weight construction
 # ------------------------------------------------------------------------------------------------
-def mx_from_float(w: torch.Tensor, fp4: bool = True, search: bool = True) -> MXWeight:
+def mx_from_float(w: torch.Tensor, fp4: bool = True, search: bool = True, tiled: bool = False) -> MXWeight:
     """Quantise a float weight [N, K] on the device (f32 staging, one matrix at a time)."""
     N, K = w.shape
     dev = w.device
@@ -110,7 +160,8 @@ def mx_from_float(w: torch.Tensor, fp4: bool = True, search: bool = True) -> MXW
     else:
         q = torch.empty(N, K, dtype=torch.uint8, device=dev)
         _ops().quant_weight_mxfp8(wf, q, sf)
-    return MXWeight(q, sf, fp4, N, K)
+    mw = MXWeight(q, sf, fp4, N, K)
+    return mw.to_tiled() if tiled else mw
 
 
 def nvfp4_quantize(w: torch.Tensor, global_scale: float | None = None):
@@ -180,7 +231,8 @@ def mx_linear(
     M = x.M
     if out is None:
         out = torch.empty(M, w.N, dtype=out_dtype, device=x.q.device)
-    _ops().gemm_mx(w.q, w.sf, w.fp4, x.q, x.sf, out, residual, float(alpha), _status.status(x.q.device))
+    _ops().gemm_mx(w.q, w.sf, w.fp4, x.q, x.sf, out, residual, float(alpha), _status.status(x.q.device),
+                   gemm_workspace(x.q.device))
     return out
 
 
@@ -189,7 +241,8 @@ def mx_swiglu(x: MXAct, w_gate: MXWeight, w_up: MXWeight, out: MXAct | None = No
     if out is None:
         out = alloc_act(M, w_gate.N, x.q.device)
     _ops().gemm_mx_swiglu(
-        w_gate.q, w_gate.sf, w_up.q, w_up.sf, w_gate.fp4, x.q, x.sf, out.q, out.sf, _status.status(x.q.device)
+        w_gate.q, w_gate.sf, w_up.q, w_up.sf, w_gate.fp4, x.q, x.sf, out.q, out.sf, _status.status(x.q.device),
+        gemm_workspace(x.q.device),
     )
     return out
 
@@ -201,5 +254,5 @@ def bf16_linear(
     M = x.shape[0]
     if out is None:
         out = torch.empty(M, w.N, dtype=out_dtype, device=x.device)
-    _ops().gemm_bf16(w.w, x, out, residual, float(alpha), _status.status(x.device))
+    _ops().gemm_bf16(w.w, x, out, residual, float(alpha), _status.status(x.device), gemm_workspace(x.device))
     return out

@@ -77,7 +77,8 @@ def _ref_gemm(x_act, w_dq):
 
 @pytest.mark.parametrize("fp4", [True, False])
 @pytest.mark.parametrize("N,K,M", [(128, 128, 1), (256, 512, 16), (384, 1024, 40), (200, 512, 7), (256, 512, 130),
-                                   (128, 4096, 1), (640, 2048, 300)])
+                                   (128, 4096, 1), (640, 2048, 300), (5120, 4096, 16), (640, 256, 5), (128, 8192, 3),
+                                   (2048, 512, 64), (1152, 17408, 2)])
 def test_gemm_mx(L, fp4, N, K, M):
     torch.manual_seed(N + K + M)
     w = torch.randn(N, K) * 0.02
@@ -97,7 +98,7 @@ def test_gemm_mx(L, fp4, N, K, M):
     torch.testing.assert_close(y2.float().cpu(), ref + res.float().cpu(), rtol=2e-2, atol=2e-2 * float(ref.abs().max()))
 
 
-@pytest.mark.parametrize("N,K,M", [(256, 512, 3), (512, 1024, 64), (256, 256, 200)])
+@pytest.mark.parametrize("N,K,M", [(256, 512, 3), (512, 1024, 64), (256, 256, 200), (2048, 4096, 16), (128, 8192, 1)])
 def test_gemm_swiglu_mxfp8(L, N, K, M):
     torch.manual_seed(7)
     wg = torch.randn(N, K) * 0.05
@@ -118,7 +119,7 @@ def test_gemm_swiglu_mxfp8(L, N, K, M):
     assert bool((err <= tol).all()), float((err / tol).max())
 
 
-@pytest.mark.parametrize("N,K,M", [(128, 64, 1), (256, 512, 16), (384, 1024, 100), (256, 256, 513)])
+@pytest.mark.parametrize("N,K,M", [(128, 64, 1), (256, 512, 16), (384, 1024, 100), (256, 256, 513), (2048, 4096, 8)])
 def test_gemm_bf16(L, N, K, M):
     torch.manual_seed(11)
     w = (torch.randn(N, K) * 0.05).bfloat16()
@@ -127,3 +128,34 @@ def test_gemm_bf16(L, N, K, M):
     _check_status()
     ref = x.float() @ w.float().T
     torch.testing.assert_close(y.cpu(), ref, rtol=1e-3, atol=1e-3 * float(ref.abs().max()))
+
+
+def test_stream_k_is_deterministic(L):
+    torch.manual_seed(21)
+    w = L.mx_from_float((torch.randn(3072, 8192) * 0.02).cuda())
+    x = L.quant_act(torch.randn(16, 8192).bfloat16().cuda())
+    a = L.mx_linear(x, w, out_dtype=torch.float32)
+    b = L.mx_linear(x, w, out_dtype=torch.float32)
+    _check_status()
+    assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("fp4", [True, False])
+@pytest.mark.parametrize("N,K,M", [(200, 512, 7), (5120, 4096, 16), (384, 1024, 300)])
+def test_gemm_tiled_weights_match_rowmajor(L, fp4, N, K, M):
+    torch.manual_seed(5)
+    mw = L.mx_from_float((torch.randn(N, K) * 0.02).cuda(), fp4=fp4)
+    mt = mw.to_tiled()
+    assert torch.equal(mt.rowmajor_q(), mw.q)
+    xa = L.quant_act(torch.randn(M, K).bfloat16().cuda())
+    a = L.mx_linear(xa, mw, out_dtype=torch.float32)
+    b = L.mx_linear(xa, mt, out_dtype=torch.float32)
+    _check_status()
+    assert torch.equal(a, b)
+    # fused swiglu on tiled weights
+    g, u = mw, L.mx_from_float((torch.randn(N, K) * 0.02).cuda(), fp4=fp4)
+    if N % 32 == 0:
+        h1 = L.mx_swiglu(xa, g, u)
+        h2 = L.mx_swiglu(xa, g.to_tiled(), u.to_tiled())
+        _check_status()
+        assert torch.equal(h1.q, h2.q)

@@ -123,7 +123,7 @@ def test_gdn_kernels_match_torch():
         b = pf[t0:t0 + n, b_off:b_off + Hv]
         g = -torch.exp(A_log) * Fn.softplus(a + dt_bias)
         beta = torch.sigmoid(b)
-        S = st0[slots[s]].clone() if has[s] else torch.zeros(Hv, d, d, device="cuda")
+        S = st0[slots[s]].transpose(-1, -2).clone() if has[s] else torch.zeros(Hv, d, d, device="cuda")
         rep = Hv // Hk
         for j in range(n):
             kt, qt = k[j].repeat_interleave(rep, 0), q[j].repeat_interleave(rep, 0)
@@ -135,7 +135,7 @@ def test_gdn_kernels_match_torch():
             z = pf[t0 + j, z_off:z_off + Hv * d].reshape(Hv, d)
             yr = oj * torch.rsqrt(oj.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float() * Fn.silu(z)
             torch.testing.assert_close(y[t0 + j].float().reshape(Hv, d), yr, rtol=2e-2, atol=2e-2)
-        torch.testing.assert_close(state[slots[s]], S, rtol=2e-3, atol=2e-4)
+        torch.testing.assert_close(state[slots[s]].transpose(-1, -2), S, rtol=2e-3, atol=2e-4)
 
 
 def _cos(a, b):
@@ -186,3 +186,62 @@ def test_decode_graph_replay_equals_eager():
         outs.append(llm.generate(prompts, SamplingParams(max_tokens=6)))
         _check()
     assert outs[0] == outs[1]
+
+
+@pytest.mark.parametrize("case", ["decode", "verify", "prefill"])
+def test_attn_tc_matches_simple_kernel(case):
+    """tcgen05 flash attention (split-KV decode / prefill tiles) vs the CUDA-core kernel above."""
+    torch.manual_seed(4)
+    D, Hq, Hkv, BLK = 256, 12, 2, 64
+    G = Hq // Hkv
+    if case == "decode":
+        ctxs, nq = [1, 63, 200, 1000, 2049], [1, 1, 1, 1, 1]
+    elif case == "verify":
+        ctxs, nq = [9, 300, 777], [8, 3, 5]
+    else:
+        ctxs, nq = [100, 700], [100, 450]
+    maxb = max((c + BLK - 1) // BLK for c in ctxs) + 1
+    nblocks = sum((c + BLK - 1) // BLK for c in ctxs) + 2
+    kc = (torch.randn(nblocks, Hkv, BLK, D) * 0.7).to(torch.float8_e4m3fn).view(torch.uint8).cuda()
+    vc = (torch.randn(nblocks, Hkv, BLK, D) * 0.7).to(torch.float8_e4m3fn).view(torch.uint8).cuda()
+    bt = torch.zeros(len(ctxs), maxb, dtype=torch.int32)
+    perm = (torch.randperm(nblocks - 1) + 1).tolist()
+    for s, c in enumerate(ctxs):
+        for b in range((c + BLK - 1) // BLK):
+            bt[s, b] = perm.pop()
+    tok_seq, tok_ctx, starts = [], [], []
+    for s, (c, n) in enumerate(zip(ctxs, nq)):
+        starts.append(len(tok_seq))
+        for j in range(n):
+            tok_seq.append(s)
+            tok_ctx.append(c - n + 1 + j)
+    T = len(tok_seq)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32).cuda()
+    q = (torch.randn(T, Hq, D) * 2).bfloat16().cuda()
+    gate = torch.randn(T, Hq * D).bfloat16().cuda()
+    scale = 1 / math.sqrt(D)
+    ref = torch.empty(T, Hq * D, dtype=torch.bfloat16, device="cuda")
+    _ops().paged_attention(q, kc, vc, bt.cuda(), i32(tok_seq), i32(tok_ctx), scale, 1.0, 1.0, gate, ref, None, None, 0)
+    out = torch.zeros(T, Hq * D, dtype=torch.bfloat16, device="cuda")
+    from r9700_stack_b200.utils import status
+    st = status.status()
+    if case == "prefill":
+        qt = 128 // G
+        tab = []
+        for si, (t0, n) in enumerate(zip(starts, nq)):
+            for j in range(0, n, qt):
+                tab += [si, t0 + j, min(qt, n - j)]
+        _ops().attn_tc_prefill(q, kc, vc, bt.cuda(), i32(tok_ctx), i32(tab), len(tab) // 3, scale, 1.0, 1.0, gate,
+                               out, None, None, st)
+    else:
+        nsplit = 4
+        po = torch.zeros(T * Hq, nsplit, D, device="cuda")
+        pml = torch.zeros(T * Hq, nsplit, 2, device="cuda")
+        _ops().attn_tc_decode(q, kc, vc, bt.cuda(), i32(tok_ctx), i32(starts), i32(nq), scale, 1.0, 1.0, po, pml,
+                              gate, out, None, None, st)
+    _check()
+    # fp8 Q and P inside the tensor-core kernel: compare with a tolerance relative to the output scale
+    err = (out.float() - ref.float()).abs()
+    assert float(err.max()) < 0.05 * float(ref.float().abs().max()) + 0.02, float(err.max())
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), dim=0)
+    assert float(cos) > 0.999, float(cos)
