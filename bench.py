@@ -118,11 +118,17 @@ def main():
 
     rank, world, local = init_distributed()
     dev = torch.device("cuda", local)
-    comm = NcclComm() if world > 1 else None
     cfg = qwen27b_hybrid()
     if args.layers:
         cfg = cfg.scaled(layers=args.layers)
     S, P = args.streams, args.prompt_len
+    comm = None
+    if world > 1:
+        from r9700_stack_b200.parallel.symm import SymmComm
+
+        # decode all-reduces fused into the row-parallel GEMMs and the following norms (NVLink P2P);
+        # prefill-sized messages go through NCCL
+        comm = SymmComm(cfg.hidden, max_tokens=S, calls_per_step=2 * cfg.layers, device=dev)
     ec = EngineConfig(max_batch=S, max_model_len=P + args.warmup + 2 * args.steps + 64, max_prefill_tokens=P,
                       cuda_graphs=True, graph_batch_sizes=[1, 2, 4, 8, 16])
     t0 = time.time()
@@ -237,6 +243,7 @@ def main():
                 "global_batch": S,
                 "seq_len": P,
                 "parallelism": f"tp{world}",
+                "collectives": "fused GEMM->NVLink push + all-reduce-RMSNorm (decode), NCCL (prefill)" if world > 1 else "none",
                 "l2": "inputs larger than L2: every step streams all weights (~15 GB / tp) and the KV cache",
                 "layers": cfg.layers,
             },
@@ -258,6 +265,8 @@ def main():
 
         llm.runner.graphs.clear()
         torch.cuda.synchronize(dev)
+        comm.barrier()
+        comm.close()
         dist.destroy_process_group()
     return 0
 

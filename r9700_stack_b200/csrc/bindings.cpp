@@ -15,6 +15,24 @@ void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, tor
                     c10::optional<torch::Tensor> workspace);
 void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optional<torch::Tensor> residual, double alpha,
                torch::Tensor status, c10::optional<torch::Tensor> workspace);
+void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, int64_t N,
+                  torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
+                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace);
+// comm.cu
+int64_t symm_alloc(int64_t nbytes);
+void symm_free(int64_t ptr);
+torch::Tensor symm_ipc_handle(int64_t ptr);
+int64_t symm_open(torch::Tensor handle);
+void symm_close(int64_t ptr);
+torch::Tensor symm_view(int64_t ptr, int64_t offset_bytes, int64_t rows, int64_t cols, int64_t device);
+void symm_step_begin(torch::Tensor step);
+void push_partial(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems,
+                  int64_t call, torch::Tensor step, int64_t calls_per_step);
+void ar_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
+                int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in,
+                c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
+                c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
+                torch::Tensor status, double timeout_s);
 // quant.cu
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
                    torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
@@ -58,6 +76,11 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
 void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torch::Tensor w, double eps,
                         c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> out_q,
                         c10::optional<torch::Tensor> out_sf);
+void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,
+                      torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor state, torch::Tensor seq_slot,
+                      torch::Tensor seq_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
+                      double eps, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf,
+                      c10::optional<torch::Tensor> out_bf16);
 }  // namespace r9k
 
 TORCH_LIBRARY(r9k, m) {
@@ -67,6 +90,15 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(a!) out_q, Tensor(b!) out_sf, Tensor(c!) status, Tensor(d!)? workspace=None) -> ()");
   m.def("gemm_bf16(Tensor w, Tensor x, Tensor(a!) out, Tensor? residual, float alpha, Tensor(b!) status, "
         "Tensor(c!)? workspace=None) -> ()");
+  m.def("gemm_mx_push(Tensor w, Tensor w_sf, bool w_fp4, Tensor x, Tensor x_sf, int N, Tensor peers, int rank, "
+        "int world, int slot_elems, int call, Tensor step, int calls_per_step, Tensor(a!) status, "
+        "Tensor(b!)? workspace=None) -> ()");
+  m.def("symm_step_begin(Tensor(a!) step) -> ()");
+  m.def("push_partial(Tensor x, Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
+        "int calls_per_step) -> ()");
+  m.def("ar_rmsnorm(Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, int calls_per_step, "
+        "int T, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, Tensor(b!)? y, "
+        "Tensor(c!)? q, Tensor(d!)? sf, Tensor(e!) status, float timeout_s) -> ()");
   m.def("rmsnorm_quant(Tensor x, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf) -> ()");
   m.def("quant_act_mxfp8(Tensor x, Tensor(a!) q, Tensor(b!) sf) -> ()");
@@ -96,6 +128,9 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor seq_len, Tensor seq_has_state) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
+  m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
+        "Tensor(a!) conv_state, Tensor(b!) state, Tensor seq_slot, Tensor seq_has_state, Tensor A_log, "
+        "Tensor dt_bias, Tensor norm_w, float eps, Tensor(c!)? out_q, Tensor(d!)? out_sf, Tensor(e!)? out_bf16) -> ()");
   m.def("gdn_out_norm_quant(Tensor o, Tensor proj, int z_off, Tensor w, float eps, Tensor(a!)? y, "
         "Tensor(b!)? out_q, Tensor(c!)? out_sf) -> ()");
 }
@@ -105,6 +140,10 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gemm_mx_swiglu", &r9k::gemm_mx_swiglu);
   m.impl("gemm_bf16", &r9k::gemm_bf16);
   m.impl("rmsnorm_quant", &r9k::rmsnorm_quant);
+  m.impl("gemm_mx_push", &r9k::gemm_mx_push);
+  m.impl("symm_step_begin", &r9k::symm_step_begin);
+  m.impl("push_partial", &r9k::push_partial);
+  m.impl("ar_rmsnorm", &r9k::ar_rmsnorm);
   m.impl("quant_act_mxfp8", &r9k::quant_act_mxfp8);
   m.impl("quant_weight_mxfp4", &r9k::quant_weight_mxfp4);
   m.impl("quant_weight_mxfp8", &r9k::quant_weight_mxfp8);
@@ -119,6 +158,17 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
+  m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);
+}
+
+// host-only helpers of the symmetric-memory runtime (no tensors on the device side of the call)
+TORCH_LIBRARY_FRAGMENT(r9k, m) {
+  m.def("symm_alloc(int nbytes) -> int", &r9k::symm_alloc);
+  m.def("symm_free(int ptr) -> ()", &r9k::symm_free);
+  m.def("symm_ipc_handle(int ptr) -> Tensor", &r9k::symm_ipc_handle);
+  m.def("symm_open(Tensor handle) -> int", &r9k::symm_open);
+  m.def("symm_close(int ptr) -> ()", &r9k::symm_close);
+  m.def("symm_view(int ptr, int offset_bytes, int rows, int cols, int device) -> Tensor", &r9k::symm_view);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "r9700_stack_b200 sm_100a kernel library"; }

@@ -1,0 +1,269 @@
+// Tensor-parallel communication over NVLink / NVSwitch peer memory.
+//
+// Symmetric buffers: each rank cudaMalloc's one region and shares it with its peers through CUDA IPC
+// handles (exchanged on the host); every rank then holds device pointers to all peers' regions.
+//
+// Fused all-reduce (decode path):
+//   producer  - the row-parallel GEMM (o_proj / out_proj / down_proj) epilogue, or push_partial for
+//               other producers, writes its bf16 partial [T, H] into slot [src rank] of every rank's
+//               region (P2P stores over NVLink) and then raises, per 128-column tile, a flag word
+//               (fence.acq_rel.sys + st.release.sys) holding the call's epoch.
+//   consumer  - ar_rmsnorm: per token row, waits (bounded, acquire loads) for the flags of every
+//               tile from every rank, sums the ranks' partials in rank order in fp32 (so all ranks
+//               get bit-identical results), adds the residual, applies RMSNorm and writes the new
+//               residual plus MXFP8 (or bf16) input of the next GEMM.
+// Epochs: a device-resident step counter (bumped once per model step by step_begin) and the call's
+// static index k within the step give the global call g = step * calls_per_step + k (calls_per_step
+// even), epoch g + 1 and buffer g % 2. A rank can only write call g+2's data after every rank
+// finished reading call g (it needed their call g+1 flags, raised after their call g consumer), so
+// two alternating buffers suffice and the scheme replays inside CUDA graphs. Reference counterpart: r9k_ar_oneshot_nrank + double-buffered device
+// seq counters, kernels/r9k_ar.hip:12-48, :304-358 (PCIe P2P); here the reduction is fused into the
+// producing GEMM and the consuming norm.
+//
+// Waits give up after a deadline and record {code, kernel, block, detail} in the status word.
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+#include "comm.cuh"
+
+namespace r9k {
+
+// ------------------------------------------------------------------------------------------------
+// host: symmetric regions through CUDA IPC
+// ------------------------------------------------------------------------------------------------
+int64_t symm_alloc(int64_t nbytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, (size_t)nbytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, (size_t)nbytes) == cudaSuccess, "symm_alloc: memset failed");
+  TORCH_CHECK(cudaDeviceSynchronize() == cudaSuccess, "symm_alloc: sync failed");
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+
+torch::Tensor symm_ipc_handle(int64_t ptr) {
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)) == cudaSuccess, "cudaIpcGetMemHandle failed");
+  auto t = torch::empty({(int64_t)sizeof(h)}, torch::dtype(torch::kUInt8));
+  memcpy(t.data_ptr(), &h, sizeof(h));
+  return t;
+}
+
+int64_t symm_open(torch::Tensor handle) {
+  TORCH_CHECK(handle.numel() == (int64_t)sizeof(cudaIpcMemHandle_t), "symm_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data_ptr(), sizeof(h));
+  void* p = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  TORCH_CHECK(e == cudaSuccess, "cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+
+// a bf16 [rows, cols] view of device memory at ptr (for tests and local reads)
+torch::Tensor symm_view(int64_t ptr, int64_t offset_bytes, int64_t rows, int64_t cols, int64_t device) {
+  auto opts = torch::dtype(torch::kBFloat16).device(torch::kCUDA, device);
+  return torch::from_blob(reinterpret_cast<uint8_t*>(ptr) + offset_bytes, {rows, cols}, opts);
+}
+
+// ------------------------------------------------------------------------------------------------
+// kernels
+// ------------------------------------------------------------------------------------------------
+__global__ void step_begin_kernel(uint32_t* step) {
+  if (threadIdx.x == 0) step[0] = step[0] + 1;
+}
+
+void symm_step_begin(torch::Tensor step) {
+  step_begin_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint32_t*>(step.data_ptr()));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// standalone producer: push x [T, H] (bf16) into every rank's slot and raise the tile flags
+__global__ void push_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, ArPeers pe, int T, int H,
+                                    int call) {
+  const uint32_t epoch = ar_epoch(pe, call);
+  const int tile = blockIdx.x;  // 128-column tile
+  const int c0 = tile * 128;
+  for (int t = threadIdx.y; t < T; t += blockDim.y) {
+    const int c = c0 + threadIdx.x * 4;
+    if (c >= H) continue;
+    const uint2 v = *reinterpret_cast<const uint2*>(x + (int64_t)t * ldx + c);
+    for (int p = 0; p < pe.world; ++p) {
+      __nv_bfloat16* dst = ar_slot(pe, p, call, pe.rank) + (int64_t)t * H + c;
+      *reinterpret_cast<uint2*>(dst) = v;
+    }
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0 && threadIdx.y == 0) ar_raise_flags(pe, call, tile, epoch);
+}
+
+void push_partial(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems,
+                  int64_t call, torch::Tensor step, int64_t calls_per_step) {
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(H % 128 == 0 && T * H <= slot_elems, "push_partial: H % 128 and T*H within the slot");
+  const at::cuda::CUDAGuard guard(x.device());
+  ArPeers pe = make_peers(peers, rank, world, slot_elems, H, step, calls_per_step);
+  push_partial_kernel<<<dim3((unsigned)(H / 128)), dim3(32, 8), 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), pe, (int)T, (int)H, (int)call);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// consumer: all-reduce (rank order) + residual add + RMSNorm (+ MXFP8). One CTA per token row,
+// one thread per 32-element block.
+__global__ void ar_rmsnorm_kernel(ArPeers pe, int call, const __nv_bfloat16* __restrict__ res_in,
+                                  __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w, int K,
+                                  float eps, int plus_one, __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
+                                  uint8_t* __restrict__ sf, int* status, uint64_t timeout_ns) {
+  __shared__ float sred[32];
+  __shared__ int s_fail;
+  const int64_t r = blockIdx.x;
+  const int kblocks = K / 32;
+  const int blk = threadIdx.x;
+  const uint32_t epoch = ar_epoch(pe, call);
+  if (threadIdx.x == 0) s_fail = 0;
+  __syncthreads();
+  // wait for every (rank, tile) flag of this call: thread i polls flags i, i + blockDim, ...
+  const int ntiles = K / 128;
+  const uint64_t t0 = globaltimer_ns();
+  for (int f = threadIdx.x; f < pe.world * ntiles; f += blockDim.x) {
+    const int src = f / ntiles, tile = f % ntiles;
+    const uint32_t* fl = ar_flag_ptr(pe, pe.rank, call, src, tile);
+    while (ld_acquire_sys(fl) < epoch) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        s_fail = 1;
+        report_error(status, kErrPeerTimeout, 300, src * 65536 + tile);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  const bool act = blk < kblocks && !s_fail;
+  float v[32];
+  float ss = 0.f;
+  if (act) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    for (int src = 0; src < pe.world; ++src) {  // fixed rank order: identical sums on every rank
+      const __nv_bfloat16* p = ar_slot(pe, pe.rank, call, src) + r * K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = ld_volatile_u4(reinterpret_cast<const uint4*>(p) + i);
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] += __bfloat162float(e[k]);
+      }
+    }
+    // the reduced partial is rounded to bf16 (as a stored GEMM output would be) before the residual add
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+    if (res_in != nullptr) {
+      const __nv_bfloat16* rr = res_in + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = reinterpret_cast<const uint4*>(rr)[i];
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] += __bfloat162float(e[k]);
+      }
+    }
+    if (res_out != nullptr) {
+      __nv_bfloat16* ro = res_out + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 raw;
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          e[k] = __float2bfloat16(v[8 * i + k]);
+          v[8 * i + k] = __bfloat162float(e[k]);
+        }
+        reinterpret_cast<uint4*>(ro)[i] = raw;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sred[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) sred[0] = t;
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (!act) return;
+  const float rrs = rsqrtf(sred[0] / (float)K + eps);
+  const __nv_bfloat16* wb = w + blk * 32;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 raw = reinterpret_cast<const uint4*>(wb)[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float wv = __bfloat162float(e[k]);
+      if (plus_one) wv += 1.f;
+      v[8 * i + k] = v[8 * i + k] * rrs * wv;
+    }
+  }
+  if (y != nullptr) {
+    __nv_bfloat16* yo = y + r * (int64_t)K + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 raw;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        e[k] = __float2bfloat16(v[8 * i + k]);
+        v[8 * i + k] = __bfloat162float(e[k]);
+      }
+      reinterpret_cast<uint4*>(yo)[i] = raw;
+    }
+  }
+  if (q != nullptr) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+    const int e = mx_exponent(am, 448.f);
+    const float si = exp2i(-e);
+    uint8_t* qo = q + r * (int64_t)K + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint4 raw;
+      uint8_t* b8 = reinterpret_cast<uint8_t*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) b8[k] = f32_to_e4m3(v[16 * i + k] * si);
+      reinterpret_cast<uint4*>(qo)[i] = raw;
+    }
+    sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+  }
+}
+
+void ar_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
+                int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out, torch::Tensor w,
+                double eps, bool plus_one, c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q,
+                c10::optional<torch::Tensor> sf, torch::Tensor status, double timeout_s) {
+  const int64_t K = w.size(0);
+  TORCH_CHECK(K % 128 == 0 && K / 32 <= 1024, "ar_rmsnorm: hidden must be a multiple of 128 and <= 32768");
+  TORCH_CHECK(T * K <= slot_elems, "ar_rmsnorm: rows exceed the slot");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(w.device());
+  ArPeers pe = make_peers(peers, rank, world, slot_elems, K, step, calls_per_step);
+  auto bf = [](const c10::optional<torch::Tensor>& t) -> __nv_bfloat16* {
+    return (t.has_value() && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
+  };
+  auto u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
+    return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
+  };
+  const int threads = std::max(32, (int)((K / 32 + 31) / 32 * 32));
+  ar_rmsnorm_kernel<<<(unsigned)T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+      pe, (int)call, bf(res_in), bf(res_out), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K, (float)eps,
+      plus_one ? 1 : 0, bf(y), u8(q), u8(sf), status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

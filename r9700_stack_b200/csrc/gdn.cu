@@ -380,3 +380,167 @@ void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torc
 }
 
 }  // namespace r9k
+
+namespace r9k {
+
+// ------------------------------------------------------------------------------------------------
+// Fused decode step (every sequence contributes exactly one token): one CTA per (sequence, key head)
+// does the causal conv (and conv-state update) of the key head's q/k channels and of its `rep` value
+// heads, the l2-norms and gates, then for each value head the delta-rule update (state read and
+// written once), RMSNormGated and the MXFP8 quantisation of the output for out_proj.
+// The CTA owns every conv channel it touches, so no other CTA reads state it writes.
+// 512 threads: recurrence thread (c = tid / 4, rg = tid % 4) owns 32 contiguous dk rows of column c.
+// ------------------------------------------------------------------------------------------------
+template <typename ST>
+__global__ void __launch_bounds__(512) gdn_decode_fused_kernel(
+    const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int z_off, int b_off, int a_off,
+    const __nv_bfloat16* __restrict__ conv_w, ST* __restrict__ conv_state, ST* __restrict__ state,
+    const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_has_state, const float* __restrict__ A_log,
+    const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ norm_w, float eps,
+    uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf, __nv_bfloat16* __restrict__ out_bf16) {
+  constexpr int D = 128, W = 4;
+  constexpr int MAXREP = 8;
+  __shared__ float sq[D], sk[D], sv[MAXREP][D], so[D], sred[32];
+  __shared__ float sg[MAXREP], sb[MAXREP];
+  const int t = blockIdx.x;  // token == sequence
+  const int kh = blockIdx.y;
+  const int rep = Hv / Hk;
+  const int tid = threadIdx.x;
+  const int slot = seq_slot[t];
+  const bool hs = seq_has_state[t] != 0;
+  const int C = 2 * Hk * D + Hv * D;
+  // ---- conv over this CTA's channels: q (128) | k (128) | v heads kh*rep .. (rep x 128)
+  const int nch = (2 + rep) * D;
+  for (int i = tid; i < nch; i += blockDim.x) {
+    int c;
+    if (i < D) c = kh * D + i;
+    else if (i < 2 * D) c = Hk * D + kh * D + (i - D);
+    else c = 2 * Hk * D + kh * rep * D + (i - 2 * D);
+    ST* cs = conv_state + ((int64_t)slot * C + c) * (W - 1);
+    float x[W];
+#pragma unroll
+    for (int w = 0; w < W - 1; ++w) x[w] = hs ? to_f<ST>(cs[w]) : 0.f;
+    x[W - 1] = __bfloat162float(proj[(int64_t)t * ld + c]);
+    float acc = 0.f;
+#pragma unroll
+    for (int w = 0; w < W; ++w) acc += x[w] * __bfloat162float(conv_w[(int64_t)c * W + w]);
+#pragma unroll
+    for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(x[w + 1]);
+    const float y = silu_f(acc);
+    if (i < D) sq[i] = y;
+    else if (i < 2 * D) sk[i - D] = y;
+    else sv[(i - 2 * D) / D][(i - 2 * D) % D] = y;
+  }
+  if (tid < rep) {
+    const int h = kh * rep + tid;
+    const float av = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
+    const float bv = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
+    sg[tid] = __expf(-__expf(A_log[h]) * softplus_f(av + dt_bias[h]));  // decay factor exp(g)
+    sb[tid] = sigmoid_f(bv);
+  }
+  __syncthreads();
+  // ---- l2 norms of q and k (warps 0 and 1)
+  if (tid < 64) {
+    const float* src = tid < 32 ? sq : sk;
+    const int l = tid & 31;
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ss += src[l + 32 * j] * src[l + 32 * j];
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if (l == 0) sred[tid >> 5] = rsqrtf(ss + 1e-6f);
+  }
+  __syncthreads();
+  const float qs = sred[0] * rsqrtf((float)D), ks = sred[1];
+  const int c = tid >> 2, rg = tid & 3;
+  float qv[32], kv_[32];
+#pragma unroll
+  for (int r = 0; r < 32; ++r) {
+    qv[r] = sq[rg * 32 + r] * qs;
+    kv_[r] = sk[rg * 32 + r] * ks;
+  }
+  for (int j = 0; j < rep; ++j) {
+    const int h = kh * rep + j;
+    ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * 32;
+    float S[32];
+    if (hs) StateVec<ST>::load(Sp, S);
+    else {
+#pragma unroll
+      for (int r = 0; r < 32; ++r) S[r] = 0.f;
+    }
+    const float decay = sg[j];
+    float kvs = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) kvs += S[r] * kv_[r];
+    kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
+    kvs += __shfl_xor_sync(0xffffffffu, kvs, 2);
+    const float delta = sb[j] * (sv[j][c] - decay * kvs);
+    float ov = 0.f;
+#pragma unroll
+    for (int r = 0; r < 32; ++r) {
+      S[r] = S[r] * decay + kv_[r] * delta;
+      ov += S[r] * qv[r];
+    }
+    ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+    ov += __shfl_xor_sync(0xffffffffu, ov, 2);
+    StateVec<ST>::store(Sp, S);
+    if (rg == 0) so[c] = ov;
+    __syncthreads();
+    // ---- RMSNormGated + MXFP8 for this head (warps 0..3, lane l owns column 32*warp + l)
+    if (tid < D) {
+      const float o = so[tid];
+      float ss = o * o;
+      for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
+      if ((tid & 31) == 0) sred[2 + (tid >> 5)] = ss;
+    }
+    __syncthreads();
+    if (tid < D) {
+      const float rr = rsqrtf((sred[2] + sred[3] + sred[4] + sred[5]) / (float)D + eps);
+      const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tid]);
+      float val = so[tid] * rr * __bfloat162float(norm_w[tid]) * silu_f(z);
+      val = __bfloat162float(__float2bfloat16(val));
+      const int64_t oi = (int64_t)t * Hv * D + h * D + tid;
+      if (out_bf16 != nullptr) out_bf16[oi] = __float2bfloat16(val);
+      if (out_q != nullptr) {
+        float am = fabsf(val);
+        for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
+        const int e = mx_exponent(am, 448.f);
+        out_q[oi] = f32_to_e4m3(val * exp2i(-e));
+        if ((tid & 31) == 0) out_sf[sf_offset(t, (h * D + tid) >> 5, Hv * D / 32)] = (uint8_t)(e + 127);
+      }
+    }
+    __syncthreads();
+  }
+  pdl_trigger();
+}
+
+void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,
+                      torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor state, torch::Tensor seq_slot,
+                      torch::Tensor seq_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
+                      double eps, c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf,
+                      c10::optional<torch::Tensor> out_bf16) {
+  const int64_t S = seq_slot.size(0);
+  if (S == 0) return;
+  TORCH_CHECK(proj.size(0) == S, "gdn_decode_fused: one token per sequence");
+  TORCH_CHECK(conv_w.size(1) == 4 && Hv % Hk == 0 && Hv / Hk <= 8, "gdn_decode_fused: conv width 4, rep <= 8");
+  TORCH_CHECK(state.size(2) == 128 && state.size(3) == 128, "gdn_decode_fused: head dim 128");
+  const at::cuda::CUDAGuard guard(proj.device());
+  dim3 grid((unsigned)S, (unsigned)Hk);
+  auto st = at::cuda::getCurrentCUDAStream();
+  auto u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
+    return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
+  };
+  __nv_bfloat16* ob = (out_bf16.has_value() && out_bf16->defined()) ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
+#define R9K_GDF(ST_T)                                                                                                 \
+  gdn_decode_fused_kernel<ST_T><<<grid, 512, 0, st>>>(                                                                 \
+      reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)z_off, (int)b_off, \
+      (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()),                                          \
+      reinterpret_cast<ST_T*>(conv_state.data_ptr()), reinterpret_cast<ST_T*>(state.data_ptr()),                      \
+      seq_slot.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(),                        \
+      dt_bias.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr()), (float)eps, u8(out_q),      \
+      u8(out_sf), ob)
+  if (state.dtype() == torch::kFloat32) { R9K_GDF(float); } else { R9K_GDF(__nv_bfloat16); }
+#undef R9K_GDF
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

@@ -1,12 +1,13 @@
 // Shared definitions of the tcgen05 GEMM kernels (tiled: gemm_tc.cu, stream-K: gemm_sk.cu).
 #pragma once
 #include "common.cuh"
+#include "comm.cuh"
 #include "tmap.h"
 
 namespace r9k {
 
 enum { KIND_BF16 = 0, KIND_MX = 1 };
-enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2 };
+enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2, EPI_PUSH = 3 };
 
 struct GemmArgs {
   int N;               // weight rows (output features)
@@ -30,6 +31,9 @@ struct GemmArgs {
   float alpha;
   int* status;
   uint64_t timeout_ns;
+  // EPI_PUSH: the bf16 result goes to slot [rank] of every rank's all-reduce region (NVLink stores)
+  ArPeers peers;
+  int ar_call;
 };
 
 // A (weight) tile load: row-major 2-D map, or pre-tiled 3-D map indexed by unit
@@ -55,6 +59,18 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
       if (tok < a.M) {
         if (row < a.N) outq[(int64_t)tok * a.ldo + row] = qv;
         if (lane == 0) a.out_sf[sf_offset(tok, row >> 5, a.out_kblocks)] = (uint8_t)(e + 127);
+      }
+    }
+  } else if constexpr (EPI == EPI_PUSH) {
+    if (row < a.N) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int tok = tok0 + t;
+        if (tok < a.M) {
+          const __nv_bfloat16 v = __float2bfloat16(g[t] * a.alpha);
+          for (int p = 0; p < a.peers.world; ++p)
+            ar_slot(a.peers, p, a.ar_call, a.peers.rank)[(int64_t)tok * a.N + row] = v;
+        }
       }
     }
   } else if constexpr (EPI == EPI_F32) {

@@ -297,6 +297,11 @@ __global__ void __launch_bounds__(192, 1)
           epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
         }
       }
+      if constexpr (EPI == EPI_PUSH) {
+        __threadfence_system();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (threadIdx.x == 64) ar_raise_flags(args.peers, args.ar_call, blockIdx.x, ar_epoch(args.peers, args.ar_call));
+      }
     } else if (ok) {
       // split-K: park the fp32 partial, the last split to arrive sums all splits in split order
       const int tile_id = n_tile * gridDim.x + blockIdx.x;
@@ -340,6 +345,11 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
           epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+        }
+        if constexpr (EPI == EPI_PUSH) {
+          __threadfence_system();
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          if (threadIdx.x == 64) ar_raise_flags(args.peers, args.ar_call, blockIdx.x, ar_epoch(args.peers, args.ar_call));
         }
         if (threadIdx.x == 64) ws_cnt[tile_id] = 0;
       }
@@ -559,6 +569,37 @@ void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, t
   }
   if (f32) dispatch_bn<KIND_MX, false, EPI_F32>(ta, ta, tb, a, p, ws, st);
   else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, a, p, ws, st);
+}
+
+// Row-parallel GEMM whose epilogue performs the all-reduce's communication: the bf16 result tile is
+// stored into slot [rank] of every rank's symmetric region and the tile's flag is raised; ar_rmsnorm
+// on each rank then reduces. Decode-sized batches only (one token tile).
+void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, int64_t N,
+                  torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
+                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace) {
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "gemm_mx_push: K and N multiples of 128");
+  TORCH_CHECK(M * N <= slot_elems, "gemm_mx_push: output exceeds the slot");
+  check_sf(w_sf, N, K, "gemm_mx_push weight");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 128), false, w_fp4);
+  TORCH_CHECK(p.n_tiles == 1, "gemm_mx_push: at most one token tile (<= 256 tokens)");
+  check_act_sf(x_sf, p, K, "gemm_mx_push");
+  CUtensorMap ta = weight_tmap(w, w_fp4, N, K, p.unpack);
+  CUtensorMap tb = tmap_u8_kmajor(x.data_ptr(), M, K, p.BN);
+  GemmArgs a = {};
+  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
+  a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
+  a.a_tiled = w.dim() == 3;
+  a.sfa = w_sf.data_ptr<uint8_t>(); a.sfb = x_sf.data_ptr<uint8_t>(); a.sf_kblocks = (int)(K / 32);
+  a.alpha = 1.f;
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 1000000000ull;
+  a.peers = make_peers(peers, rank, world, slot_elems, N, step, calls_per_step);
+  a.ar_call = (int)call;
+  torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
+  dispatch_bn<KIND_MX, false, EPI_PUSH>(ta, ta, tb, a, p, ws, at::cuda::getCurrentCUDAStream());
 }
 
 // Fused gate/up projection + SwiGLU + MXFP8 quantisation of the result.

@@ -14,7 +14,8 @@ _DEFAULTS = {
     "R9K_ATTN": "tc",  # tc | simple
     "R9K_WEIGHT_TILED": "1",  # 1: MX weights stored as contiguous 128x128 units; 0: row-major
     "R9K_GEMM_SK": "0",  # 1: skinny GEMMs use the persistent stream-K kernel
-    "R9K_FP4_UNPACK": "0",  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
+    "R9K_FP4_UNPACK": "0",
+    "R9K_GDN_FUSED": "1",  # 1: decode steps run the one-kernel GDN layer core  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
     "R9K_COMM": "fused",  # fused | nccl
     "R9K_GDN_STATE": "",  # "" (model default) | bf16 | fp32
     "R9K_DISABLE": "",

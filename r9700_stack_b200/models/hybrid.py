@@ -263,7 +263,7 @@ class HybridLM:
             _ops().attn_tc_decode(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, meta.seq_start, meta.seq_len,
                                   self.sm_scale, self.k_scale, self.v_scale, po, pml, gate, out_bf, out_q, out_sf,
                                   _status.status(self.device))
-        self._linear(ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"], ws.y[:T])
+        return ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"]
 
     def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):
         c, g = self.cfg, self.gdn_dims
@@ -275,6 +275,13 @@ class HybridLM:
         a_off = b_off + hv
         ssm, conv = self.ssm[i], self.conv[i]
         o = _ops()
+        if meta.write_state and T == meta.seq_start.shape[0] and knobs.get("R9K_GDN_FUSED") != "0":
+            # decode: every sequence has one token -> one fused kernel per layer
+            o.gdn_decode_fused(proj, hk, hv, z_off, b_off, a_off, lay["conv_w"], conv, ssm, meta.seq_state_slot,
+                               meta.seq_has_state, lay["A_log"], lay["dt_bias"], lay["gdn_norm"], c.rms_eps,
+                               ws.gdn_act.q[:T] if self.mx else None, ws.gdn_act.sf if self.mx else None,
+                               None if self.mx else ws.gdn_bf16[:T])
+            return ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"]
         o.gdn_conv_prep(proj, hk, hv, d, d, b_off, a_off, lay["conv_w"], conv, meta.tok_state_slot,
                         meta.tok_pos_in_chunk, meta.tok_has_state, lay["A_log"], lay["dt_bias"],
                         ws.gq[:T], ws.gk[:T], ws.gv[:T], ws.gg[:T], ws.gb[:T])
@@ -287,38 +294,65 @@ class HybridLM:
                                  ws.gdn_act.sf)
         else:
             o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, ws.gdn_bf16[:T], None, None)
-        self._linear(ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"], ws.y[:T])
+        return ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"]
 
     def _ffn(self, lay, ws: Workspace, T: int):
+        """Gate/up + SwiGLU (fused); returns the down projection's input and weight."""
         if self.mx:
             L.mx_swiglu(ws.act.narrow(T), lay["w_gate"], lay["w_up"], out=ws.ffn_act.narrow(T))
-            L.mx_linear(ws.ffn_act.narrow(T), lay["w_down"], out=ws.y[:T])
+            return ws.ffn_act.narrow(T), None, lay["w_down"]
+        raise NotImplementedError("bf16 dense FFN path")
+
+    def _row_parallel(self, act, xb, w, ws: Workspace, T: int, call: int, fused: bool) -> None:
+        """Output projection of a sublayer: partial sums pushed to every rank (fused) or written to
+        ws.y and all-reduced by NCCL."""
+        if fused and isinstance(w, L.MXWeight):
+            self.comm.gemm_push(act, w, call)
+            return
+        self._linear(act, xb, w, ws.y[:T])
+        if fused:
+            self.comm.push(ws.y[:T], call)
         else:
-            raise NotImplementedError("bf16 dense FFN path")
+            self.comm.all_reduce_(ws.y[:T])
+
+    def _post_reduce_norm(self, w, ws: Workspace, T: int, call: int, fused: bool, first: bool = False,
+                          final: bool = False) -> None:
+        """Reduce the previous sublayer's output (fused path) + residual add + RMSNorm."""
+        c = self.cfg
+        if fused:
+            self.comm.ar_rmsnorm(call, T, w, c.rms_eps, c.norm_plus_one, residual=ws.resid[:T],
+                                 residual_out=ws.resid[:T],
+                                 y=ws.norm_out[:T] if (final or not self.mx) else None,
+                                 quant_out=None if (final or not self.mx) else ws.act.narrow(T))
+        elif final:
+            L.rmsnorm(ws.y[:T], w, c.rms_eps, plus_one=c.norm_plus_one, residual=ws.resid[:T],
+                      residual_out=ws.resid[:T], out=ws.norm_out[:T])
+        else:
+            self._norm(ws.y, w, ws, T, residual=True)
 
     def forward(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
         """Run T tokens; returns fp32 logits [R, vocab] for the rows in meta.logits_idx[:R]."""
         c = self.cfg
+        fused = getattr(self.comm, "fused", False) and self.comm.can_fuse(T) and knobs.get("R9K_COMM") != "nccl"
+        if fused:
+            self.comm.step_begin()
         torch.index_select(self.embed, 0, meta.input_ids[:T], out=ws.resid[:T])
-        first = True
+        nl = len(self.layers)
         for i, lay in enumerate(self.layers):
-            # input norm: the residual add of the previous sublayer's output is fused in
-            if first:
+            if i == 0:
                 self._norm(ws.resid, lay["in_norm"], ws, T, residual=False)
-                first = False
             else:
-                self._norm(ws.y, lay["in_norm"], ws, T, residual=True)
+                self._post_reduce_norm(lay["in_norm"], ws, T, call=2 * i - 1, fused=fused)
             if lay["attn"]:
-                self._attention(i, lay, meta, ws, T)
+                act, xb, w = self._attention(i, lay, meta, ws, T)
             else:
-                self._gdn(i, lay, meta, ws, T)
-            self.comm.all_reduce_(ws.y[:T])
-            self._norm(ws.y, lay["post_norm"], ws, T, residual=True)
-            self._ffn(lay, ws, T)
-            self.comm.all_reduce_(ws.y[:T])
-        # final: residual add + norm on the rows that need logits
-        L.rmsnorm(ws.y[:T], self.final_norm, c.rms_eps, plus_one=c.norm_plus_one, residual=ws.resid[:T],
-                  residual_out=ws.resid[:T], out=ws.norm_out[:T])
+                act, xb, w = self._gdn(i, lay, meta, ws, T)
+            self._row_parallel(act, xb, w, ws, T, call=2 * i, fused=fused)
+            self._post_reduce_norm(lay["post_norm"], ws, T, call=2 * i, fused=fused)
+            act, xb, w = self._ffn(lay, ws, T)
+            self._row_parallel(act, xb, w, ws, T, call=2 * i + 1, fused=fused)
+        # final: residual add + norm, then the rows that need logits
+        self._post_reduce_norm(self.final_norm, ws, T, call=2 * nl - 1, fused=fused, final=True)
         rows = ws.final_bf16[:R]
         torch.index_select(ws.norm_out[:T], 0, meta.logits_idx[:R], out=rows)
         if isinstance(self.lm_head, L.MXWeight):

@@ -39,8 +39,11 @@ def init_distributed(timeout_s: int = 120) -> tuple[int, int, int]:
 class NcclComm:
     def __init__(self, group=None):
         self.group = group
-        self.world_size = dist.get_world_size(group)
-        self.rank = dist.get_rank(group)
+        if dist.is_initialized():
+            self.world_size = dist.get_world_size(group)
+            self.rank = dist.get_rank(group)
+        else:  # single process: collectives are identities
+            self.world_size, self.rank = 1, 0
         self._gather_bufs: dict[tuple, torch.Tensor] = {}
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
@@ -69,7 +72,8 @@ class NcclComm:
         return res
 
     def barrier(self) -> None:
-        dist.barrier(group=self.group)
+        if self.world_size > 1:
+            dist.barrier(group=self.group)
 
     def max_scalar(self, x: float, device) -> float:
         if self.world_size == 1:

@@ -1,0 +1,103 @@
+"""Symmetric-memory tensor-parallel communicator with the all-reduce fused into its neighbours.
+
+Each rank allocates one device region (CUDA IPC shared with its peers). For decode-sized batches:
+
+* the row-parallel GEMM that ends a sublayer (o_proj, GDN out_proj, FFN down_proj) runs with the
+  push epilogue (``gemm_mx_push``): its bf16 partial tiles are stored straight into every rank's
+  region over NVLink and a per-tile flag is raised;
+* the RMSNorm that follows runs as ``ar_rmsnorm``: it waits for every rank's flags, sums the
+  partials in rank order (bit-identical on every rank), adds the residual and emits the next GEMM's
+  MXFP8 input.
+
+No separate all-reduce kernel runs. Batches larger than the slot (prefill) fall back to NCCL.
+Reference counterpart: the one-kernel P2P all-reduce family of r9700_vllm/comm/r9k_ar.py:87-601
+(PCIe pair/quartet/host stages); on NVSwitch every peer is one hop, so there is no hierarchy.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from .. import _native
+from ..utils import status as _status
+from .comm import NcclComm
+
+AR_FLAG_BYTES = 64 * 1024
+
+
+class SymmComm(NcclComm):
+    """NCCL communicator plus the fused push / reduce-norm path for up to ``max_tokens`` rows."""
+
+    fused = True
+
+    def __init__(self, hidden: int, max_tokens: int, calls_per_step: int, device, group=None,
+                 timeout_s: float = 2.0):
+        super().__init__(group)
+        assert calls_per_step % 2 == 0
+        self.device = torch.device(device)
+        self.hidden = hidden
+        self.max_tokens = max_tokens
+        self.calls_per_step = calls_per_step
+        self.timeout_s = timeout_s
+        self.slot_elems = max_tokens * hidden
+        ops = _native.ops()
+        nbytes = AR_FLAG_BYTES + 2 * self.world_size * self.slot_elems * 2
+        self.local_ptr = int(ops.symm_alloc(nbytes))
+        handle = ops.symm_ipc_handle(self.local_ptr).numpy().tobytes()
+        handles = [None] * self.world_size
+        if self.world_size > 1:
+            dist.all_gather_object(handles, handle, group=group)
+        else:
+            handles = [handle]
+        ptrs = []
+        self._opened = []
+        for i, h in enumerate(handles):
+            if i == self.rank:
+                ptrs.append(self.local_ptr)
+            else:
+                p = int(ops.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+                self._opened.append(p)
+                ptrs.append(p)
+        self.peers = torch.tensor(ptrs, dtype=torch.int64)
+        self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.barrier()
+
+    # -------------------------------------------------------------------------------------------
+    def can_fuse(self, T: int) -> bool:
+        return 0 < T <= self.max_tokens
+
+    def step_begin(self) -> None:
+        _native.ops().symm_step_begin(self.step)
+
+    def gemm_push(self, act, w, call: int) -> None:
+        _native.ops().gemm_mx_push(w.q, w.sf, w.fp4, act.q, act.sf, w.N, self.peers, self.rank, self.world_size,
+                                   self.slot_elems, call, self.step, self.calls_per_step,
+                                   _status.status(self.device), _gemm_ws(self.device))
+
+    def push(self, x: torch.Tensor, call: int) -> None:
+        _native.ops().push_partial(x, self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
+                                   self.calls_per_step)
+
+    def ar_rmsnorm(self, call: int, T: int, w: torch.Tensor, eps: float, plus_one: bool, *, residual=None,
+                   residual_out=None, y=None, quant_out=None) -> None:
+        _native.ops().ar_rmsnorm(self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
+                                 self.calls_per_step, T, residual, residual_out, w, float(eps), bool(plus_one), y,
+                                 quant_out.q if quant_out is not None else None,
+                                 quant_out.sf if quant_out is not None else None,
+                                 _status.status(self.device), float(self.timeout_s))
+
+    def close(self) -> None:
+        ops = _native.ops()
+        torch.cuda.synchronize(self.device)
+        for p in self._opened:
+            ops.symm_close(p)
+        self._opened = []
+        if self.local_ptr:
+            ops.symm_free(self.local_ptr)
+            self.local_ptr = 0
+
+
+def _gemm_ws(device):
+    from ..ops.linear import gemm_workspace
+
+    return gemm_workspace(device)

@@ -23,7 +23,12 @@ class DeviceWaitError(RuntimeError):
 def status(device: torch.device | int | None = None) -> torch.Tensor:
     if device is None:
         device = torch.cuda.current_device()
-    idx = device.index if isinstance(device, torch.device) else int(device)
+    if isinstance(device, str):
+        device = torch.device(device)
+    if isinstance(device, torch.device):
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+    else:
+        idx = int(device)
     t = _STATUS.get(idx)
     if t is None:
         t = torch.zeros(4, dtype=torch.int32, device=f"cuda:{idx}")

@@ -245,3 +245,42 @@ def test_attn_tc_matches_simple_kernel(case):
     assert float(err.max()) < 0.05 * float(ref.float().abs().max()) + 0.02, float(err.max())
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), ref.float().flatten(), dim=0)
     assert float(cos) > 0.999, float(cos)
+
+
+@pytest.mark.parametrize("sdt", [torch.float32, torch.bfloat16])
+def test_gdn_decode_fused_matches_unfused(sdt):
+    """The one-kernel decode step equals conv_prep + state update + recurrent + out-norm."""
+    torch.manual_seed(9)
+    Hk, Hv, d, W, S = 2, 6, 128, 4, 5
+    C = 2 * Hk * d + Hv * d
+    z_off = C
+    b_off, a_off = z_off + Hv * d, z_off + Hv * d + Hv
+    proj = (torch.randn(S, C + Hv * d + 2 * Hv) * 0.5).bfloat16().cuda()
+    conv_w = (torch.randn(C, W) * 0.3).bfloat16().cuda()
+    slots = torch.tensor([3, 1, 4, 2, 5], dtype=torch.int32).cuda()
+    has = torch.tensor([1, 0, 1, 1, 0], dtype=torch.int32).cuda()
+    cs = (torch.randn(7, C, W - 1) * 0.5).to(sdt).cuda()
+    st = (torch.randn(7, Hv, d, d) * 0.05).to(sdt).cuda()
+    A_log = torch.log(torch.rand(Hv) * 15 + 1).cuda()
+    dt_bias = (torch.randn(Hv) * 0.5).cuda()
+    nw = (1 + torch.randn(d) * 0.1).bfloat16().cuda()
+    o = _ops()
+    cs1, st1 = cs.clone(), st.clone()
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32).cuda()
+    qo = torch.empty(S, Hk, d, device="cuda"); ko = torch.empty(S, Hk, d, device="cuda")
+    vo = torch.empty(S, Hv, d, device="cuda"); go = torch.empty(S, Hv, device="cuda"); bo = torch.empty(S, Hv, device="cuda")
+    o.gdn_conv_prep(proj, Hk, Hv, d, d, b_off, a_off, conv_w, cs1, slots, i32([0] * S), has, A_log, dt_bias,
+                    qo, ko, vo, go, bo)
+    o.gdn_conv_state_update(proj, cs1, slots, i32(list(range(S))), i32([1] * S), has)
+    out = torch.empty(S, Hv, d, device="cuda")
+    o.gdn_recurrent(qo, ko, vo, go, bo, st1, slots, i32(list(range(S))), i32([1] * S), has, True, out)
+    y1 = torch.empty(S, Hv * d, dtype=torch.bfloat16, device="cuda")
+    o.gdn_out_norm_quant(out, proj, z_off, nw, 1e-6, y1, None, None)
+    cs2, st2 = cs.clone(), st.clone()
+    y2 = torch.empty(S, Hv * d, dtype=torch.bfloat16, device="cuda")
+    o.gdn_decode_fused(proj, Hk, Hv, z_off, b_off, a_off, conv_w, cs2, st2, slots, has, A_log, dt_bias, nw, 1e-6,
+                       None, None, y2)
+    _check()
+    torch.testing.assert_close(cs2.float(), cs1.float())
+    torch.testing.assert_close(st2.float(), st1.float(), rtol=1e-3, atol=1e-4)
+    torch.testing.assert_close(y2.float(), y1.float(), rtol=2e-2, atol=2e-2)
