@@ -123,7 +123,7 @@ def main():
         cfg = cfg.scaled(layers=args.layers)
     S, P = args.streams, args.prompt_len
     comm = None
-    if world > 1:
+    if world > 1 or os.environ.get("R9K_BENCH_SYMM") == "1":
         from r9700_stack_b200.parallel.symm import SymmComm
 
         # decode all-reduces fused into the row-parallel GEMMs and the following norms (NVLink P2P);

@@ -29,6 +29,8 @@ __global__ void qk_norm_rope_cache_kernel(const __nv_bfloat16* __restrict__ qkv,
                                           int rot, const int32_t* __restrict__ slots, __nv_bfloat16* __restrict__ q_out,
                                           uint8_t* __restrict__ k_cache, uint8_t* __restrict__ v_cache, float k_inv_scale,
                                           float v_inv_scale, int T) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   constexpr int PER = D / 32;
   const int lane = threadIdx.x & 31;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -112,7 +114,7 @@ void qk_norm_rope_cache(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t q_of
   const int blocks = (int)((warps * 32 + threads - 1) / threads);
   auto st = at::cuda::getCurrentCUDAStream();
 #define R9K_QKNR(DD)                                                                                                 \
-  qk_norm_rope_cache_kernel<DD><<<blocks, threads, 0, st>>>(                                                         \
+  launch_pdl(qk_norm_rope_cache_kernel<DD>, dim3(blocks), dim3(threads), 0, st,                                                         \
       reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), qkv.stride(0), (int)Hq, (int)Hkv, (int)q_off, (int)k_off, \
       (int)v_off, reinterpret_cast<const __nv_bfloat16*>(qw.data_ptr()),                                             \
       reinterpret_cast<const __nv_bfloat16*>(kw.data_ptr()), (float)eps, plus_one ? 1 : 0,                           \
@@ -136,6 +138,8 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(
     const int32_t* __restrict__ tok_seq, const int32_t* __restrict__ tok_ctx, float sm_scale, float k_scale,
     float v_scale, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate, __nv_bfloat16* __restrict__ out,
     uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf, int out_kblocks, int window) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   constexpr int PER = D / 32;
   const int t = blockIdx.x, h = blockIdx.y;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -211,7 +215,7 @@ void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
   uint8_t* osf = (out_sf.has_value() && out_sf->defined()) ? out_sf->data_ptr<uint8_t>() : nullptr;
   dim3 grid((unsigned)T, (unsigned)Hq);
 #define R9K_PA(DD)                                                                                                   \
-  paged_attention_kernel<DD><<<grid, 128, 0, st>>>(                                                                  \
+  launch_pdl(paged_attention_kernel<DD>, grid, dim3(128), 0, st,                                                                  \
       reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), (int)Hq, (int)Hkv, k_cache.data_ptr<uint8_t>(),          \
       v_cache.data_ptr<uint8_t>(), block_table.data_ptr<int32_t>(), (int)block_table.size(1),                       \
       tok_seq.data_ptr<int32_t>(), tok_ctx.data_ptr<int32_t>(), (float)sm_scale, (float)k_scale, (float)v_scale, g,   \

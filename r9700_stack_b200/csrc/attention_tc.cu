@@ -100,6 +100,8 @@ R9K_DEVINL uint32_t pack4_e4m3(float a, float b, float c, float d) {
 
 __global__ void __launch_bounds__(192, 1)
     attn_tc_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, const AttnArgs a) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   using namespace fa;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -433,6 +435,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
                                     int nsplit, float v_scale, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
                                     __nv_bfloat16* __restrict__ out_bf16, uint8_t* __restrict__ out_q,
                                     uint8_t* __restrict__ out_sf, int out_kblocks) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   pdl_trigger();  // the next GEMM may start streaming its weights
   constexpr int D = fa::D;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -480,7 +484,7 @@ static void attn_tc_launch(const AttnArgs& a, const CUtensorMap& tk, const CUten
                 "attn_tc: smem attribute");
     set = true;
   }
-  attn_tc_kernel<<<grid, 192, fa::SMEM, st>>>(tk, tv, a);
+  TORCH_CHECK(launch_pdl(attn_tc_kernel, grid, dim3(192), (size_t)fa::SMEM, st, tk, tv, a) == cudaSuccess, "attn_tc launch");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -532,7 +536,7 @@ void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cach
   attn_tc_launch(a, kv_tmap(k_cache), kv_tmap(v_cache), dim3((unsigned)S, (unsigned)a.Hkv, (unsigned)a.nsplit), st);
   const __nv_bfloat16* g = (gate.has_value() && gate->defined()) ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
   const int64_t warps = T * a.Hq;
-  attn_combine_kernel<<<(unsigned)((warps * 32 + 255) / 256), 256, 0, st>>>(
+  launch_pdl(attn_combine_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0, st,
       a.part_o, a.part_ml, (int)T, a.Hq, a.nsplit, a.v_scale, g, g ? gate->stride(0) : 0,
       (out.has_value() && out->defined()) ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr,
       (out_q.has_value() && out_q->defined()) ? out_q->data_ptr<uint8_t>() : nullptr,

@@ -33,6 +33,11 @@ void ar_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_e
                 c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
                 c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
                 torch::Tensor status, double timeout_s);
+void ar_pull_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+                     torch::Tensor step, int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in,
+                     c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
+                     c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
+                     torch::Tensor status, double timeout_s);
 // quant.cu
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
                    torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
@@ -99,6 +104,9 @@ TORCH_LIBRARY(r9k, m) {
   m.def("ar_rmsnorm(Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, int calls_per_step, "
         "int T, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, Tensor(b!)? y, "
         "Tensor(c!)? q, Tensor(d!)? sf, Tensor(e!) status, float timeout_s) -> ()");
+  m.def("ar_pull_rmsnorm(Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
+        "int calls_per_step, int T, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
+        "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf, Tensor(e!) status, float timeout_s) -> ()");
   m.def("rmsnorm_quant(Tensor x, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf) -> ()");
   m.def("quant_act_mxfp8(Tensor x, Tensor(a!) q, Tensor(b!) sf) -> ()");
@@ -144,6 +152,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("symm_step_begin", &r9k::symm_step_begin);
   m.impl("push_partial", &r9k::push_partial);
   m.impl("ar_rmsnorm", &r9k::ar_rmsnorm);
+  m.impl("ar_pull_rmsnorm", &r9k::ar_pull_rmsnorm);
   m.impl("quant_act_mxfp8", &r9k::quant_act_mxfp8);
   m.impl("quant_weight_mxfp4", &r9k::quant_weight_mxfp4);
   m.impl("quant_weight_mxfp8", &r9k::quant_weight_mxfp8);

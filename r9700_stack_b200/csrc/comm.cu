@@ -72,32 +72,34 @@ torch::Tensor symm_view(int64_t ptr, int64_t offset_bytes, int64_t rows, int64_t
 // kernels
 // ------------------------------------------------------------------------------------------------
 __global__ void step_begin_kernel(uint32_t* step) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   if (threadIdx.x == 0) step[0] = step[0] + 1;
 }
 
 void symm_step_begin(torch::Tensor step) {
-  step_begin_kernel<<<1, 32, 0, at::cuda::getCurrentCUDAStream()>>>(reinterpret_cast<uint32_t*>(step.data_ptr()));
+  launch_pdl(step_begin_kernel, dim3(1), dim3(32), 0, at::cuda::getCurrentCUDAStream(),reinterpret_cast<uint32_t*>(step.data_ptr()));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
 // standalone producer: push x [T, H] (bf16) into every rank's slot and raise the tile flags
 __global__ void push_partial_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, ArPeers pe, int T, int H,
                                     int call) {
-  const uint32_t epoch = ar_epoch(pe, call);
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
+  const ArCall arc = ar_resolve(pe, call);
   const int tile = blockIdx.x;  // 128-column tile
   const int c0 = tile * 128;
   for (int t = threadIdx.y; t < T; t += blockDim.y) {
     const int c = c0 + threadIdx.x * 4;
     if (c >= H) continue;
     const uint2 v = *reinterpret_cast<const uint2*>(x + (int64_t)t * ldx + c);
-    for (int p = 0; p < pe.world; ++p) {
-      __nv_bfloat16* dst = ar_slot(pe, p, call, pe.rank) + (int64_t)t * H + c;
-      *reinterpret_cast<uint2*>(dst) = v;
-    }
+#pragma unroll
+    for (int p = 0; p < AR_MAX_WORLD; ++p)
+      if (p < pe.world) *reinterpret_cast<uint2*>(arc.dst[p] + (int64_t)t * H + c) = v;
   }
-  __threadfence_system();
   __syncthreads();
-  if (threadIdx.x == 0 && threadIdx.y == 0) ar_raise_flags(pe, call, tile, epoch);
+  if (threadIdx.x == 0 && threadIdx.y == 0) ar_raise_flags(pe, call, tile, arc.epoch);
 }
 
 void push_partial(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems,
@@ -106,7 +108,7 @@ void push_partial(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t wo
   TORCH_CHECK(H % 128 == 0 && T * H <= slot_elems, "push_partial: H % 128 and T*H within the slot");
   const at::cuda::CUDAGuard guard(x.device());
   ArPeers pe = make_peers(peers, rank, world, slot_elems, H, step, calls_per_step);
-  push_partial_kernel<<<dim3((unsigned)(H / 128)), dim3(32, 8), 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(push_partial_kernel, dim3((unsigned)(H / 128)), dim3(32, 8), 0, at::cuda::getCurrentCUDAStream(),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), pe, (int)T, (int)H, (int)call);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -117,12 +119,16 @@ __global__ void ar_rmsnorm_kernel(ArPeers pe, int call, const __nv_bfloat16* __r
                                   __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w, int K,
                                   float eps, int plus_one, __nv_bfloat16* __restrict__ y, uint8_t* __restrict__ q,
                                   uint8_t* __restrict__ sf, int* status, uint64_t timeout_ns) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   __shared__ float sred[32];
   __shared__ int s_fail;
   const int64_t r = blockIdx.x;
   const int kblocks = K / 32;
   const int blk = threadIdx.x;
-  const uint32_t epoch = ar_epoch(pe, call);
+  const uint32_t gcall = ar_global_call(pe, call);
+  const uint32_t epoch = gcall + 1u;
+  const uint32_t buf = gcall & 1u;
   if (threadIdx.x == 0) s_fail = 0;
   __syncthreads();
   // wait for every (rank, tile) flag of this call: thread i polls flags i, i + blockDim, ...
@@ -130,7 +136,8 @@ __global__ void ar_rmsnorm_kernel(ArPeers pe, int call, const __nv_bfloat16* __r
   const uint64_t t0 = globaltimer_ns();
   for (int f = threadIdx.x; f < pe.world * ntiles; f += blockDim.x) {
     const int src = f / ntiles, tile = f % ntiles;
-    const uint32_t* fl = ar_flag_ptr(pe, pe.rank, call, src, tile);
+    const uint32_t* fl = reinterpret_cast<const uint32_t*>(pe.base[pe.rank]) +
+                         ((int64_t)buf * AR_MAX_WORLD + src) * AR_MAX_TILES + tile;
     while (ld_acquire_sys(fl) < epoch) {
       if (globaltimer_ns() - t0 > timeout_ns) {
         s_fail = 1;
@@ -147,7 +154,8 @@ __global__ void ar_rmsnorm_kernel(ArPeers pe, int call, const __nv_bfloat16* __r
 #pragma unroll
     for (int i = 0; i < 32; ++i) v[i] = 0.f;
     for (int src = 0; src < pe.world; ++src) {  // fixed rank order: identical sums on every rank
-      const __nv_bfloat16* p = ar_slot(pe, pe.rank, call, src) + r * K + blk * 32;
+      const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(pe.base[pe.rank] + AR_FLAG_BYTES) +
+                               ((int64_t)buf * pe.world + src) * pe.slot_elems + r * K + blk * 32;
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const uint4 raw = ld_volatile_u4(reinterpret_cast<const uint4*>(p) + i);
@@ -260,10 +268,190 @@ void ar_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_e
     return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
   };
   const int threads = std::max(32, (int)((K / 32 + 31) / 32 * 32));
-  ar_rmsnorm_kernel<<<(unsigned)T, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(ar_rmsnorm_kernel, dim3((unsigned)T), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
       pe, (int)call, bf(res_in), bf(res_out), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K, (float)eps,
       plus_one ? 1 : 0, bf(y), u8(q), u8(sf), status.data_ptr<int>(), (uint64_t)(timeout_s * 1e9));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k
+
+namespace r9k {
+
+// ------------------------------------------------------------------------------------------------
+// Pull variant: every rank's row-parallel GEMM writes its bf16 partial into its OWN region, buffer
+// k % 2 (a static address per call site, so graphs capture it). The consumer kernel raises this
+// rank's ready flag for the call in every peer's region (one release store per peer, after the
+// producing grid completed), waits for the peers' flags, then reads the peers' partials over NVLink
+// and reduces them in rank order together with the residual add, RMSNorm and quantisation.
+// Flag words live at [AR_MAX_WORLD .. 2*AR_MAX_WORLD) x 2 buffers of the flag page (per source).
+// ------------------------------------------------------------------------------------------------
+R9K_DEVINL uint32_t* ar_ready_flag(uint8_t* base, uint32_t buf, int src) {
+  return reinterpret_cast<uint32_t*>(base) + 8192 + buf * AR_MAX_WORLD + src;
+}
+
+__global__ void ar_pull_rmsnorm_kernel(ArPeers pe, int call, const __nv_bfloat16* __restrict__ res_in,
+                                       __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
+                                       int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y,
+                                       uint8_t* __restrict__ q, uint8_t* __restrict__ sf, int* status,
+                                       uint64_t timeout_ns) {
+  pdl_wait();  // this rank's producer grid has completed
+  __shared__ float sred[32];
+  __shared__ int s_fail;
+  const int64_t r = blockIdx.x;
+  const int kblocks = K / 32;
+  const int blk = threadIdx.x;
+  const uint32_t gcall = ar_global_call(pe, call);
+  const uint32_t epoch = gcall + 1u;
+  const uint32_t buf = (uint32_t)call & 1u;  // static per call site (calls_per_step is even)
+  if (threadIdx.x == 0) {
+    s_fail = 0;
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < pe.world; ++p) st_release_sys(ar_ready_flag(pe.base[p], buf, pe.rank), epoch);
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x < pe.world) {
+    const uint32_t* fl = ar_ready_flag(pe.base[pe.rank], buf, threadIdx.x);
+    const uint64_t t0 = globaltimer_ns();
+    while (ld_acquire_sys(fl) < epoch) {
+      if (globaltimer_ns() - t0 > timeout_ns) {
+        s_fail = 1;
+        report_error(status, kErrPeerTimeout, 310, threadIdx.x);
+        break;
+      }
+    }
+  }
+  __syncthreads();
+  pdl_trigger();
+  const bool act = blk < kblocks && !s_fail;
+  float v[32];
+  float ss = 0.f;
+  if (act) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = 0.f;
+    for (int src = 0; src < pe.world; ++src) {  // fixed rank order: identical sums on every rank
+      const __nv_bfloat16* p = reinterpret_cast<const __nv_bfloat16*>(pe.base[src] + AR_FLAG_BYTES) +
+                               (int64_t)buf * pe.slot_elems + r * K + blk * 32;
+      uint4 raw[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) raw[i] = ld_volatile_u4(reinterpret_cast<const uint4*>(p) + i);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw[i]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] += __bfloat162float(e[k]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+    if (res_in != nullptr) {
+      const __nv_bfloat16* rr = res_in + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 raw = reinterpret_cast<const uint4*>(rr)[i];
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) v[8 * i + k] += __bfloat162float(e[k]);
+      }
+    }
+    if (res_out != nullptr) {
+      __nv_bfloat16* ro = res_out + r * (int64_t)K + blk * 32;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint4 raw;
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          e[k] = __float2bfloat16(v[8 * i + k]);
+          v[8 * i + k] = __bfloat162float(e[k]);
+        }
+        reinterpret_cast<uint4*>(ro)[i] = raw;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) ss += v[i] * v[i];
+  }
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((threadIdx.x & 31) == 0) sred[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? sred[threadIdx.x] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (threadIdx.x == 0) sred[0] = t;
+  }
+  __syncthreads();
+  if (!act) return;
+  const float rrs = rsqrtf(sred[0] / (float)K + eps);
+  const __nv_bfloat16* wb = w + blk * 32;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint4 raw = reinterpret_cast<const uint4*>(wb)[i];
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float wv = __bfloat162float(e[k]);
+      if (plus_one) wv += 1.f;
+      v[8 * i + k] = v[8 * i + k] * rrs * wv;
+    }
+  }
+  if (y != nullptr) {
+    __nv_bfloat16* yo = y + r * (int64_t)K + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      uint4 raw;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        e[k] = __float2bfloat16(v[8 * i + k]);
+        v[8 * i + k] = __bfloat162float(e[k]);
+      }
+      reinterpret_cast<uint4*>(yo)[i] = raw;
+    }
+  }
+  if (q != nullptr) {
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) am = fmaxf(am, fabsf(v[i]));
+    const int e = mx_exponent(am, 448.f);
+    const float si = exp2i(-e);
+    uint8_t* qo = q + r * (int64_t)K + blk * 32;
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint4 raw;
+      uint8_t* b8 = reinterpret_cast<uint8_t*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 16; ++k) b8[k] = f32_to_e4m3(v[16 * i + k] * si);
+      reinterpret_cast<uint4*>(qo)[i] = raw;
+    }
+    sf[sf_offset(r, blk, kblocks)] = (uint8_t)(e + 127);
+  }
+}
+
+void ar_pull_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+                     torch::Tensor step, int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in,
+                     c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
+                     c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
+                     torch::Tensor status, double timeout_s) {
+  const int64_t K = w.size(0);
+  TORCH_CHECK(K % 128 == 0 && K / 32 <= 1024, "ar_pull_rmsnorm: hidden must be a multiple of 128 and <= 32768");
+  TORCH_CHECK(T * K <= slot_elems, "ar_pull_rmsnorm: rows exceed the buffer");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(w.device());
+  ArPeers pe = make_peers(peers, rank, world, slot_elems, K, step, calls_per_step);
+  auto bf = [](const c10::optional<torch::Tensor>& t) -> __nv_bfloat16* {
+    return (t.has_value() && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
+  };
+  auto u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
+    return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
+  };
+  const int threads = std::max(32, (int)((K / 32 + 31) / 32 * 32));
+  TORCH_CHECK(launch_pdl(ar_pull_rmsnorm_kernel, dim3((unsigned)T), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
+                         pe, (int)call, bf(res_in), bf(res_out), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+                         (int)K, (float)eps, plus_one ? 1 : 0, bf(y), u8(q), u8(sf), status.data_ptr<int>(),
+                         (uint64_t)(timeout_s * 1e9)) == cudaSuccess,
+              "ar_pull_rmsnorm launch");
 }
 
 }  // namespace r9k

@@ -51,12 +51,30 @@ R9K_DEVINL uint4 ld_volatile_u4(const uint4* p) {
   return v;
 }
 
-// Raise tile `tile`'s flag for this rank's contribution in every rank's region. The caller has made
-// its data stores visible system-wide (each writing thread ran __threadfence_system before the
-// barrier that precedes this call).
+// Raise tile `tile`'s flag for this rank's contribution in every rank's region. Called by one thread
+// after a CTA barrier that orders every writer's data stores before it: the system-scope fence plus
+// the release store make those (cumulatively ordered) stores visible before the flag.
 R9K_DEVINL void ar_raise_flags(const ArPeers& pe, int call, int tile, uint32_t epoch) {
   __threadfence_system();
   for (int p = 0; p < pe.world; ++p) st_release_sys(ar_flag_ptr(pe, p, call, pe.rank, tile), epoch);
+}
+
+// Resolved once per kernel: this call's epoch and the destination slot of this rank in every region.
+struct ArCall {
+  uint32_t epoch;
+  __nv_bfloat16* dst[AR_MAX_WORLD];
+};
+R9K_DEVINL ArCall ar_resolve(const ArPeers& pe, int call) {
+  ArCall c;
+  const uint32_t g = ar_global_call(pe, call);
+  c.epoch = g + 1u;
+  const uint32_t b = g & 1u;
+#pragma unroll
+  for (int p = 0; p < AR_MAX_WORLD; ++p)
+    c.dst[p] = p < pe.world ? reinterpret_cast<__nv_bfloat16*>(pe.base[p] + AR_FLAG_BYTES) +
+                                  ((int64_t)b * pe.world + pe.rank) * pe.slot_elems
+                            : nullptr;
+  return c;
 }
 
 inline ArPeers make_peers(const torch::Tensor& peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t H,

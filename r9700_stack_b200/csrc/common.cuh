@@ -10,6 +10,7 @@
 #include <cuda_fp16.h>
 #include <cuda_fp8.h>
 #include <stdint.h>
+#include <utility>
 
 #define R9K_DEVINL __device__ __forceinline__
 
@@ -65,6 +66,24 @@ R9K_DEVINL bool elect_one() {
 // ---------------------------------------------------------------------------------------------
 R9K_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 R9K_DEVINL void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launch with programmatic stream serialisation (the kernel must pdl_wait() before it touches
+// memory its predecessor writes or reads). Launch errors are returned to the caller's check.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------------------------
 // mbarrier

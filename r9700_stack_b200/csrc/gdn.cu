@@ -49,6 +49,8 @@ __global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int
                                      const float* __restrict__ dt_bias, float* __restrict__ q_out,
                                      float* __restrict__ k_out, float* __restrict__ v_out, float* __restrict__ g_out,
                                      float* __restrict__ beta_out) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   const int t = blockIdx.x;
   const int lane = threadIdx.x & 31;
   const int hh = blockIdx.y * 8 + (threadIdx.x >> 5);
@@ -113,6 +115,8 @@ __global__ void gdn_conv_state_update_kernel(const __nv_bfloat16* __restrict__ p
                                              ST* __restrict__ conv_state, const int32_t* __restrict__ seq_slot,
                                              const int32_t* __restrict__ seq_start, const int32_t* __restrict__ seq_len,
                                              const int32_t* __restrict__ seq_has_state) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   const int s = blockIdx.x;
   const int slot = seq_slot[s], st0 = seq_start[s], n = seq_len[s];
   const bool hs = seq_has_state[s] != 0;
@@ -183,6 +187,8 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ g, const float* __restrict__ beta, int Hk, int Hv, int dv, ST* __restrict__ state,
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_start, const int32_t* __restrict__ seq_len,
     const int32_t* __restrict__ seq_has_state, int write_state, float* __restrict__ o) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   static_assert(DK == 128, "row groups of 32");
   constexpr int CH = 16;  // tokens staged per chunk
   __shared__ float sq[CH][DK], sk[CH][DK], sv[CH][32], sg[CH], sb[CH];
@@ -251,6 +257,8 @@ __global__ void gdn_out_norm_quant_kernel(const float* __restrict__ o, const __n
                                           int64_t ld, int z_off, const __nv_bfloat16* __restrict__ w, float eps,
                                           int T, int Hv, int dv, __nv_bfloat16* __restrict__ y,
                                           uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   pdl_trigger();  // the next GEMM may start streaming its weights
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -300,7 +308,7 @@ void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64
   TORCH_CHECK(proj.stride(0) % 4 == 0 && proj.stride(1) == 1, "gdn_conv_prep: proj rows must be 8-byte aligned");
   const dim3 grid((unsigned)T, (unsigned)((2 * Hk + Hv + 1 + 7) / 8));
 #define R9K_CONV(ST_T)                                                                                                \
-  gdn_conv_prep_kernel<ST_T><<<grid, 256, 0, st>>>(                                                                    \
+  launch_pdl(gdn_conv_prep_kernel<ST_T>, grid, dim3(256), 0, st,                                                                    \
       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)dk, (int)dv,     \
       (int)b_off, (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()), W,                           \
       reinterpret_cast<const ST_T*>(conv_state.data_ptr()), tok_slot.data_ptr<int32_t>(), tok_pos.data_ptr<int32_t>(),  \
@@ -322,12 +330,12 @@ void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::
   auto st = at::cuda::getCurrentCUDAStream();
   const dim3 grid((unsigned)S, (unsigned)((C + 255) / 256));
   if (conv_state.dtype() == torch::kFloat32)
-    gdn_conv_state_update_kernel<float><<<grid, 256, 0, st>>>(
+    launch_pdl(gdn_conv_state_update_kernel<float>, grid, dim3(256), 0, st,
         reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W, conv_state.data_ptr<float>(),
         seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(),
         seq_has_state.data_ptr<int32_t>());
   else
-    gdn_conv_state_update_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(
+    launch_pdl(gdn_conv_state_update_kernel<__nv_bfloat16>, grid, dim3(256), 0, st,
         reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), C, W,
         reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr()), seq_slot.data_ptr<int32_t>(),
         seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>());
@@ -348,12 +356,12 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   dim3 grid((unsigned)S, (unsigned)Hv, (unsigned)(dv / 32));
   float* op = (o.has_value() && o->defined()) ? o->data_ptr<float>() : nullptr;
   if (state.dtype() == torch::kFloat32)
-    gdn_recurrent_kernel<float, 128><<<grid, 128, 0, st>>>(
+    launch_pdl(gdn_recurrent_kernel<float, 128>, grid, dim3(128), 0, st,
         q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), Hk,
         Hv, dv, state.data_ptr<float>(), seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(),
         seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(), write_state ? 1 : 0, op);
   else
-    gdn_recurrent_kernel<__nv_bfloat16, 128><<<grid, 128, 0, st>>>(
+    launch_pdl(gdn_recurrent_kernel<__nv_bfloat16, 128>, grid, dim3(128), 0, st,
         q.data_ptr<float>(), k.data_ptr<float>(), v.data_ptr<float>(), g.data_ptr<float>(), beta.data_ptr<float>(), Hk,
         Hv, dv, reinterpret_cast<__nv_bfloat16*>(state.data_ptr()), seq_slot.data_ptr<int32_t>(),
         seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(),
@@ -370,7 +378,7 @@ void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torc
   const at::cuda::CUDAGuard guard(o.device());
   const int64_t warps = T * Hv;
   const int blocks = (int)((warps * 32 + 255) / 256);
-  gdn_out_norm_quant_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(gdn_out_norm_quant_kernel, dim3(blocks), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
       o.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)z_off,
       reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (float)eps, (int)T, (int)Hv, (int)dv,
       (y.has_value() && y->defined()) ? reinterpret_cast<__nv_bfloat16*>(y->data_ptr()) : nullptr,
@@ -398,6 +406,8 @@ __global__ void __launch_bounds__(512) gdn_decode_fused_kernel(
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_has_state, const float* __restrict__ A_log,
     const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ norm_w, float eps,
     uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf, __nv_bfloat16* __restrict__ out_bf16) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   constexpr int D = 128, W = 4;
   constexpr int MAXREP = 8;
   __shared__ float sq[D], sk[D], sv[MAXREP][D], so[D], sred[32];
@@ -531,7 +541,7 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   };
   __nv_bfloat16* ob = (out_bf16.has_value() && out_bf16->defined()) ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
 #define R9K_GDF(ST_T)                                                                                                 \
-  gdn_decode_fused_kernel<ST_T><<<grid, 512, 0, st>>>(                                                                 \
+  launch_pdl(gdn_decode_fused_kernel<ST_T>, grid, dim3(512), 0, st,                                                                 \
       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)z_off, (int)b_off, \
       (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()),                                          \
       reinterpret_cast<ST_T*>(conv_state.data_ptr()), reinterpret_cast<ST_T*>(state.data_ptr()),                      \

@@ -44,7 +44,8 @@ R9K_DEVINL void load_a_tile(void* dst, const CUtensorMap* map, uint64_t* bar, co
 }
 
 template <int BN, bool DUAL, int EPI>
-R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u, int row, int tok0, int lane) {
+R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u, int row, int tok0, int lane,
+                               const ArCall* arc = nullptr) {
   if constexpr (EPI == EPI_SWIGLU_MXFP8) {
     uint8_t* outq = reinterpret_cast<uint8_t*>(a.out);
 #pragma unroll
@@ -63,13 +64,16 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
     }
   } else if constexpr (EPI == EPI_PUSH) {
     if (row < a.N) {
+      const int W = a.peers.world;
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const int tok = tok0 + t;
         if (tok < a.M) {
           const __nv_bfloat16 v = __float2bfloat16(g[t] * a.alpha);
-          for (int p = 0; p < a.peers.world; ++p)
-            ar_slot(a.peers, p, a.ar_call, a.peers.rank)[(int64_t)tok * a.N + row] = v;
+          const int64_t off = (int64_t)tok * a.N + row;
+#pragma unroll
+          for (int p = 0; p < AR_MAX_WORLD; ++p)
+            if (p < W) arc->dst[p][off] = v;
         }
       }
     }

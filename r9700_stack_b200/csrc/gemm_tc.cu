@@ -262,6 +262,8 @@ __global__ void __launch_bounds__(192, 1)
     const int row = m0 + row_local;
     const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
     pdl_wait();
+    ArCall arc;
+    if constexpr (EPI == EPI_PUSH) arc = ar_resolve(args.peers, args.ar_call);
     const bool wok = __all_sync(0xffffffffu, nk == 0 || mbar_wait(tmem_full, 0, args.timeout_ns));
     if (threadIdx.x == 64) s_ok = 1;
     asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -288,20 +290,42 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     };
+    // EPI_PUSH: the bf16 tile is staged in shared memory as [token][128 rows] (the operand buffers are
+    // free once the accumulator is complete) and pushed to every rank's slot as 16-byte vectors, so
+    // NVLink carries full 256-byte row segments; then one thread raises the tile's flags.
+    __nv_bfloat16* stg = reinterpret_cast<__nv_bfloat16*>(smem);
+    auto stage_push = [&](int c, const float* g) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) stg[(c + t) * 128 + row_local] = __float2bfloat16(g[t] * args.alpha);
+    };
+    auto flush_push = [&]() {
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const uint4* src = reinterpret_cast<const uint4*>(stg);
+      const int W = args.peers.world;
+      for (int idx = ct; idx < args.M * 16; idx += 128) {
+        const int tok = idx >> 4, ch = idx & 15;
+        const uint4 v = src[tok * 16 + ch];
+        const int64_t off = (int64_t)tok * args.N + m0 + ch * 8;
+#pragma unroll
+        for (int p = 0; p < AR_MAX_WORLD; ++p)
+          if (p < W) *reinterpret_cast<uint4*>(arc.dst[p] + off) = v;
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (threadIdx.x == 64) ar_raise_flags(args.peers, args.ar_call, blockIdx.x, arc.epoch);
+    };
+    (void)stage_push;
+    (void)flush_push;
     if (S == 1) {
       if (ok && nk > 0) {
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
           float g[16], u[16];
           load_acc(c, g, u);
-          epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+          if constexpr (EPI == EPI_PUSH) stage_push(c, g);
+          else epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane, &arc);
         }
       }
-      if constexpr (EPI == EPI_PUSH) {
-        __threadfence_system();
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (threadIdx.x == 64) ar_raise_flags(args.peers, args.ar_call, blockIdx.x, ar_epoch(args.peers, args.ar_call));
-      }
+      if constexpr (EPI == EPI_PUSH) flush_push();
     } else if (ok) {
       // split-K: park the fp32 partial, the last split to arrive sums all splits in split order
       const int tile_id = n_tile * gridDim.x + blockIdx.x;
@@ -344,13 +368,10 @@ __global__ void __launch_bounds__(192, 1)
               if (DUAL) u[t] += __ldcg(src + BN * 128 + (c + t) * 128 + row_local);
             }
           }
-          epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane);
+          if constexpr (EPI == EPI_PUSH) stage_push(c, g);
+          else epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane, &arc);
         }
-        if constexpr (EPI == EPI_PUSH) {
-          __threadfence_system();
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (threadIdx.x == 64) ar_raise_flags(args.peers, args.ar_call, blockIdx.x, ar_epoch(args.peers, args.ar_call));
-        }
+        if constexpr (EPI == EPI_PUSH) flush_push();
         if (threadIdx.x == 64) ws_cnt[tile_id] = 0;
       }
     }

@@ -41,6 +41,8 @@ __global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, con
                                      __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
                                      int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y, int64_t ldy,
                                      uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   pdl_trigger();  // the next GEMM may start streaming its weights
   __shared__ float sred[32];
   const int64_t r = blockIdx.x;
@@ -176,11 +178,11 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::op
     TORCH_CHECK(sf->numel() >= ((M + 127) / 128) * ((K / 32 + 3) / 4) * 512, "rmsnorm_quant: sf too small");
   }
   if (x.dtype() == torch::kFloat32) {
-    rmsnorm_quant_kernel<float><<<M, threads, smem, st>>>(x.data_ptr<float>(), x.stride(0), ptr_bf(res_in), ptr_bf(res_out),
+    launch_pdl(rmsnorm_quant_kernel<float>, dim3((unsigned)M), dim3(threads), smem, st,x.data_ptr<float>(), x.stride(0), ptr_bf(res_in), ptr_bf(res_out),
                                                            reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K,
                                                            (float)eps, plus_one, ptr_bf(y), ldy, ptr_u8(q), ptr_u8(sf));
   } else {
-    rmsnorm_quant_kernel<__nv_bfloat16><<<M, threads, smem, st>>>(
+    launch_pdl(rmsnorm_quant_kernel<__nv_bfloat16>, dim3((unsigned)M), dim3(threads), smem, st,
         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), ptr_bf(res_in), ptr_bf(res_out),
         reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)K, (float)eps, plus_one, ptr_bf(y), ldy, ptr_u8(q),
         ptr_u8(sf));
@@ -193,6 +195,8 @@ void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::op
 // ------------------------------------------------------------------------------------------------
 __global__ void quant_act_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int M, int K,
                                        uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  pdl_wait();
+  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   const int kblocks = K / 32;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -218,7 +222,7 @@ void quant_act_mxfp8(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
   const int64_t warps = M * (K / 32);
   const int threads = 256;
   const int64_t blocks = std::min<int64_t>((warps * 32 + threads - 1) / threads, 148 * 16);
-  quant_act_mxfp8_kernel<<<(int)blocks, threads, 0, at::cuda::getCurrentCUDAStream()>>>(
+  launch_pdl(quant_act_mxfp8_kernel, dim3((unsigned)blocks), dim3(threads), 0, at::cuda::getCurrentCUDAStream(),
       reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)M, (int)K, q.data_ptr<uint8_t>(),
       sf.data_ptr<uint8_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -17,6 +17,7 @@ _DEFAULTS = {
     "R9K_FP4_UNPACK": "0",
     "R9K_GDN_FUSED": "1",  # 1: decode steps run the one-kernel GDN layer core  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
     "R9K_COMM": "fused",  # fused | nccl
+    "R9K_AR_MODE": "pull",  # pull: consumer reads peers' partials; push: GEMM epilogue stores into peers
     "R9K_GDN_STATE": "",  # "" (model default) | bf16 | fp32
     "R9K_DISABLE": "",
     "R9K_AR_ONESHOT_MAX_KB": "512",

@@ -306,6 +306,10 @@ class HybridLM:
     def _row_parallel(self, act, xb, w, ws: Workspace, T: int, call: int, fused: bool) -> None:
         """Output projection of a sublayer: partial sums pushed to every rank (fused) or written to
         ws.y and all-reduced by NCCL."""
+        if fused and self.comm.mode == "pull":
+            # partial written into this rank's symmetric buffer; the next norm pulls and reduces
+            self._linear(act, xb, w, self.comm.out_buffer(call, T))
+            return
         if fused and isinstance(w, L.MXWeight):
             self.comm.gemm_push(act, w, call)
             return

@@ -74,13 +74,26 @@ class SymmComm(NcclComm):
                                    self.slot_elems, call, self.step, self.calls_per_step,
                                    _status.status(self.device), _gemm_ws(self.device))
 
+    @property
+    def mode(self) -> str:
+        from .. import knobs
+
+        return knobs.get("R9K_AR_MODE") or "pull"
+
+    def out_buffer(self, call: int, T: int) -> torch.Tensor:
+        """Pull mode: where this rank's row-parallel GEMM writes its partial for call `call` (a static
+        address per call site: buffer call % 2 of this rank's region)."""
+        off = AR_FLAG_BYTES + (call & 1) * self.slot_elems * 2
+        return _native.ops().symm_view(self.local_ptr, off, T, self.hidden, self.device.index or 0)
+
     def push(self, x: torch.Tensor, call: int) -> None:
         _native.ops().push_partial(x, self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
                                    self.calls_per_step)
 
     def ar_rmsnorm(self, call: int, T: int, w: torch.Tensor, eps: float, plus_one: bool, *, residual=None,
                    residual_out=None, y=None, quant_out=None) -> None:
-        _native.ops().ar_rmsnorm(self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
+        fn = _native.ops().ar_pull_rmsnorm if self.mode == "pull" else _native.ops().ar_rmsnorm
+        fn(self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
                                  self.calls_per_step, T, residual, residual_out, w, float(eps), bool(plus_one), y,
                                  quant_out.q if quant_out is not None else None,
                                  quant_out.sf if quant_out is not None else None,

@@ -14,9 +14,14 @@ def _check():
     status.check()
 
 
-def test_gemm_push_then_ar_rmsnorm_matches_unfused():
+@pytest.mark.parametrize("mode", ["push", "pull"])
+def test_fused_allreduce_norm_matches_unfused(mode, monkeypatch):
+    from r9700_stack_b200 import knobs
     from r9700_stack_b200.ops import linear as L
     from r9700_stack_b200.parallel.symm import SymmComm
+
+    monkeypatch.setenv("R9K_AR_MODE", mode)
+    knobs.refresh()
 
     torch.manual_seed(0)
     H, K, T = 1024, 2048, 12
@@ -35,9 +40,15 @@ def test_gemm_push_then_ar_rmsnorm_matches_unfused():
         r2 = resid.clone()
         a2 = L.alloc_act(T, H, "cuda")
         comm.step_begin()
-        comm.gemm_push(x, w, call=0)
+        if mode == "push":
+            comm.gemm_push(x, w, call=0)
+        else:
+            L.mx_linear(x, w, out=comm.out_buffer(0, T))
         comm.ar_rmsnorm(0, T, nw, 1e-6, True, residual=r2, residual_out=r2, quant_out=a2)
-        comm.push(y, call=1)
+        if mode == "push":
+            comm.push(y, call=1)
+        else:
+            comm.out_buffer(1, T).copy_(y)
         y3 = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
         r3 = resid.clone()
         comm.ar_rmsnorm(1, T, nw, 1e-6, True, residual=r3, residual_out=r3, y=y3)
@@ -45,6 +56,7 @@ def test_gemm_push_then_ar_rmsnorm_matches_unfused():
         assert torch.equal(r1, r2) and torch.equal(a1.q, a2.q), step
         assert torch.equal(r1, r3)
     comm.close()
+    knobs.refresh()
 
 
 def test_tiny_model_fused_comm_equals_plain():
