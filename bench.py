@@ -267,7 +267,8 @@ def main():
         torch.cuda.synchronize(dev)
         comm.barrier()
         comm.close()
-        dist.destroy_process_group()
+        if dist.is_initialized():
+            dist.destroy_process_group()
     return 0
 
 

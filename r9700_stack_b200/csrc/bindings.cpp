@@ -18,6 +18,21 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
 void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, int64_t N,
                   torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
                   int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace);
+void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::Tensor> w2,
+                     c10::optional<torch::Tensor> w2_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf,
+                     torch::Tensor work, torch::Tensor work_count, int64_t N, int64_t E, int64_t BN, torch::Tensor out,
+                     c10::optional<torch::Tensor> out_sf, torch::Tensor status);
+void gemm_bf16_swiglu(torch::Tensor wg, torch::Tensor wu, torch::Tensor x, torch::Tensor out, torch::Tensor status,
+                      c10::optional<torch::Tensor> workspace);
+// moe.cu
+void moe_route(torch::Tensor logits, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias, int64_t n_group,
+               int64_t topk_group, double scale, bool renorm, torch::Tensor ids, torch::Tensor w);
+void moe_align(torch::Tensor ids, int64_t e0, int64_t E_local, int64_t BN, torch::Tensor perm_row,
+               torch::Tensor seg_start, torch::Tensor work, torch::Tensor work_count);
+void moe_gather(torch::Tensor q, torch::Tensor sf, int64_t k, torch::Tensor perm_row, torch::Tensor oq,
+                torch::Tensor osf);
+void moe_combine(torch::Tensor y, torch::Tensor perm_row, torch::Tensor w, int64_t k,
+                 c10::optional<torch::Tensor> shared, c10::optional<torch::Tensor> shared_gate, torch::Tensor out);
 // comm.cu
 int64_t symm_alloc(int64_t nbytes);
 void symm_free(int64_t ptr);
@@ -98,6 +113,18 @@ TORCH_LIBRARY(r9k, m) {
   m.def("gemm_mx_push(Tensor w, Tensor w_sf, bool w_fp4, Tensor x, Tensor x_sf, int N, Tensor peers, int rank, "
         "int world, int slot_elems, int call, Tensor step, int calls_per_step, Tensor(a!) status, "
         "Tensor(b!)? workspace=None) -> ()");
+  m.def("gemm_mx_grouped(Tensor w, Tensor w_sf, Tensor? w2, Tensor? w2_sf, bool w_fp4, Tensor x, Tensor x_sf, "
+        "Tensor work, Tensor work_count, int N, int E, int BN, Tensor(a!) out, Tensor(b!)? out_sf, "
+        "Tensor(c!) status) -> ()");
+  m.def("gemm_bf16_swiglu(Tensor wg, Tensor wu, Tensor x, Tensor(a!) out, Tensor(b!) status, "
+        "Tensor(c!)? workspace=None) -> ()");
+  m.def("moe_route(Tensor logits, int k, int mode, Tensor? bias, int n_group, int topk_group, float scale, "
+        "bool renorm, Tensor(a!) ids, Tensor(b!) w) -> ()");
+  m.def("moe_align(Tensor ids, int e0, int E_local, int BN, Tensor(a!) perm_row, Tensor(b!) seg_start, "
+        "Tensor(c!) work, Tensor(d!) work_count) -> ()");
+  m.def("moe_gather(Tensor q, Tensor sf, int k, Tensor perm_row, Tensor(a!) oq, Tensor(b!) osf) -> ()");
+  m.def("moe_combine(Tensor y, Tensor perm_row, Tensor w, int k, Tensor? shared, Tensor? shared_gate, "
+        "Tensor(a!) out) -> ()");
   m.def("symm_step_begin(Tensor(a!) step) -> ()");
   m.def("push_partial(Tensor x, Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
         "int calls_per_step) -> ()");
@@ -150,6 +177,12 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("rmsnorm_quant", &r9k::rmsnorm_quant);
   m.impl("gemm_mx_push", &r9k::gemm_mx_push);
   m.impl("symm_step_begin", &r9k::symm_step_begin);
+  m.impl("gemm_mx_grouped", &r9k::gemm_mx_grouped);
+  m.impl("gemm_bf16_swiglu", &r9k::gemm_bf16_swiglu);
+  m.impl("moe_route", &r9k::moe_route);
+  m.impl("moe_align", &r9k::moe_align);
+  m.impl("moe_gather", &r9k::moe_gather);
+  m.impl("moe_combine", &r9k::moe_combine);
   m.impl("push_partial", &r9k::push_partial);
   m.impl("ar_rmsnorm", &r9k::ar_rmsnorm);
   m.impl("ar_pull_rmsnorm", &r9k::ar_pull_rmsnorm);

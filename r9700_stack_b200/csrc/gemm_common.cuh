@@ -7,7 +7,7 @@
 namespace r9k {
 
 enum { KIND_BF16 = 0, KIND_MX = 1 };
-enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2, EPI_PUSH = 3 };
+enum { EPI_BF16 = 0, EPI_F32 = 1, EPI_SWIGLU_MXFP8 = 2, EPI_PUSH = 3, EPI_SWIGLU_BF16 = 4 };
 
 struct GemmArgs {
   int N;               // weight rows (output features)
@@ -34,6 +34,11 @@ struct GemmArgs {
   // EPI_PUSH: the bf16 result goes to slot [rank] of every rank's all-reduce region (NVLink stores)
   ArPeers peers;
   int ar_call;
+  // grouped (MoE) mode: grid.y walks a device work list of (expert, first row, rows) token tiles;
+  // expert e's weight is row tiles [e * g_row_tiles, (e + 1) * g_row_tiles) of the stacked matrix
+  const int32_t* g_work;
+  const int32_t* g_count;
+  int g_row_tiles;
 };
 
 // A (weight) tile load: row-major 2-D map, or pre-tiled 3-D map indexed by unit
@@ -75,6 +80,15 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
           for (int p = 0; p < AR_MAX_WORLD; ++p)
             if (p < W) arc->dst[p][off] = v;
         }
+      }
+    }
+  } else if constexpr (EPI == EPI_SWIGLU_BF16) {
+    __nv_bfloat16* out = reinterpret_cast<__nv_bfloat16*>(a.out);
+    if (row < a.N) {
+#pragma unroll
+      for (int t = 0; t < 16; ++t) {
+        const int tok = tok0 + t;
+        if (tok < a.M) out[(int64_t)tok * a.ldo + row] = __float2bfloat16(silu_f(g[t]) * u[t]);
       }
     }
   } else if constexpr (EPI == EPI_F32) {

@@ -101,11 +101,21 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int s_last, s_ok;
 
   const int warp = warp_id(), lane = lane_id();
-  const int m0 = blockIdx.x * 128;
+  int m0 = blockIdx.x * 128;  // row (A) coordinate in the weight matrix
   const int S = args.splits;
   const int split = (int)(blockIdx.y % S);
   const int n_tile = (int)(blockIdx.y / S);
-  const int n0 = n_tile * BN;
+  int n0 = n_tile * BN;
+  int m_valid = args.M;  // token rows [0, m_valid) are stored
+  if (args.g_work != nullptr) {
+    // grouped: the work list comes from the previous kernel
+    pdl_wait();
+    if ((int)blockIdx.y >= *args.g_count) return;
+    const int e = args.g_work[3 * blockIdx.y + 0];
+    n0 = args.g_work[3 * blockIdx.y + 1];
+    m_valid = n0 + args.g_work[3 * blockIdx.y + 2];
+    m0 = (e * args.g_row_tiles + (int)blockIdx.x) * 128;
+  }
   const int kc0 = split * args.kc_per_split;
   const int kc1 = min(args.kchunks, kc0 + args.kc_per_split);
   const int nk = max(0, kc1 - kc0);
@@ -259,7 +269,9 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     // ------------------------------ epilogue ------------------------------
-    const int row = m0 + row_local;
+    GemmArgs ea = args;  // grouped mode: rows are the expert's own, tokens end at m_valid
+    ea.M = m_valid;
+    const int row = (args.g_work != nullptr ? (int)blockIdx.x * 128 : m0) + row_local;
     const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
     pdl_wait();
     ArCall arc;
@@ -322,7 +334,7 @@ __global__ void __launch_bounds__(192, 1)
           float g[16], u[16];
           load_acc(c, g, u);
           if constexpr (EPI == EPI_PUSH) stage_push(c, g);
-          else epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane, &arc);
+          else epilogue_chunk<BN, DUAL, EPI>(ea, g, u, row, n0 + c, lane, &arc);
         }
       }
       if constexpr (EPI == EPI_PUSH) flush_push();
@@ -369,7 +381,7 @@ __global__ void __launch_bounds__(192, 1)
             }
           }
           if constexpr (EPI == EPI_PUSH) stage_push(c, g);
-          else epilogue_chunk<BN, DUAL, EPI>(args, g, u, row, n0 + c, lane, &arc);
+          else epilogue_chunk<BN, DUAL, EPI>(ea, g, u, row, n0 + c, lane, &arc);
         }
         if constexpr (EPI == EPI_PUSH) flush_push();
         if (threadIdx.x == 64) ws_cnt[tile_id] = 0;
@@ -623,6 +635,50 @@ void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor
   dispatch_bn<KIND_MX, false, EPI_PUSH>(ta, ta, tb, a, p, ws, at::cuda::getCurrentCUDAStream());
 }
 
+// Grouped expert GEMM over expert-sorted token rows (see moe.cu). w / w_sf: stacked experts
+// [E * N, K] (pre-tiled units); with w2 the gate/up pair runs with the SwiGLU -> MXFP8 epilogue,
+// otherwise the bf16 result goes to out. Rows are processed in the BN-row tiles of the work list.
+void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::Tensor> w2,
+                     c10::optional<torch::Tensor> w2_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf,
+                     torch::Tensor work, torch::Tensor work_count, int64_t N, int64_t E, int64_t BN, torch::Tensor out,
+                     c10::optional<torch::Tensor> out_sf, torch::Tensor status) {
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "gemm_mx_grouped: K and N multiples of 128");
+  const bool dual = w2.has_value() && w2->defined();
+  const at::cuda::CUDAGuard guard(x.device());
+  LaunchPlan p;
+  p.BN = (int)BN;
+  p.S = 1;
+  p.n_tiles = (int)work.size(0);
+  p.unpack = false;
+  TORCH_CHECK(!(dual && BN > 128), "gemm_mx_grouped: dual needs BN <= 128");
+  CUtensorMap ta = weight_tmap(w, w_fp4, E * N, K, false);
+  CUtensorMap ta2 = dual ? weight_tmap(*w2, w_fp4, E * N, K, false) : ta;
+  CUtensorMap tb = tmap_u8_kmajor(x.data_ptr(), M, K, p.BN);
+  GemmArgs a = {};
+  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
+  a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
+  a.a_tiled = w.dim() == 3;
+  a.sfa = w_sf.data_ptr<uint8_t>(); a.sfb = x_sf.data_ptr<uint8_t>(); a.sf_kblocks = (int)(K / 32);
+  if (dual) a.sfa2 = w2_sf->data_ptr<uint8_t>();
+  a.out = out.data_ptr(); a.ldo = (int)out.stride(0);
+  if (dual) { a.out_sf = out_sf->data_ptr<uint8_t>(); a.out_kblocks = (int)(N / 32); }
+  a.alpha = 1.f;
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 1000000000ull;
+  a.g_work = work.data_ptr<int32_t>();
+  a.g_count = work_count.data_ptr<int32_t>();
+  a.g_row_tiles = (int)(N / 128);
+  // grid.x = N / 128 row tiles of one expert; grid.y = work items (the launcher multiplies by S = 1)
+  auto st = at::cuda::getCurrentCUDAStream();
+  a.N = (int)N;
+  GemmArgs ga = a;
+  ga.N = (int)N;
+  // launch_gemm derives grid.x from args.N
+  if (dual) dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, ga, p, nullptr, st);
+  else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, ga, p, nullptr, st);
+}
+
 // Fused gate/up projection + SwiGLU + MXFP8 quantisation of the result.
 void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, torch::Tensor wu_sf, bool w_fp4,
                     torch::Tensor x, torch::Tensor x_sf, torch::Tensor out_q, torch::Tensor out_sf,
@@ -664,6 +720,27 @@ void gemm_mx_swiglu(torch::Tensor wg, torch::Tensor wg_sf, torch::Tensor wu, tor
     ta2 = weight_tmap(wu, w_fp4, N, K, p.unpack);
   }
   dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, a, p, ws, st);
+}
+
+// bf16 gate/up projection with the SwiGLU epilogue (bf16 result): dense bf16 FFNs and shared experts.
+void gemm_bf16_swiglu(torch::Tensor wg, torch::Tensor wu, torch::Tensor x, torch::Tensor out, torch::Tensor status,
+                      c10::optional<torch::Tensor> workspace) {
+  const int64_t N = wg.size(0), M = x.size(0), K = x.size(1);
+  TORCH_CHECK(K % 64 == 0 && wg.sizes() == wu.sizes() && wg.size(1) == K, "gemm_bf16_swiglu: shapes");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  LaunchPlan p = plan_gemm((int)N, (int)M, (int)(K / 64), true, false);
+  CUtensorMap ta = tmap_bf16_kmajor(wg.data_ptr(), N, K, wg.stride(0), 128);
+  CUtensorMap ta2 = tmap_bf16_kmajor(wu.data_ptr(), N, K, wu.stride(0), 128);
+  CUtensorMap tb = tmap_bf16_kmajor(x.data_ptr(), M, K, x.stride(0), p.BN);
+  GemmArgs a = {};
+  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 64);
+  a.out = out.data_ptr(); a.ldo = (int)out.stride(0);
+  a.alpha = 1.f;
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 1000000000ull;
+  torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
+  dispatch_bn<KIND_BF16, true, EPI_SWIGLU_BF16>(ta, ta2, tb, a, p, ws, at::cuda::getCurrentCUDAStream());
 }
 
 // bf16 x bf16 -> bf16/f32 (kind::f16)

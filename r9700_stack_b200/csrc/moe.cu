@@ -1,0 +1,284 @@
+// Mixture-of-experts kernels: routing, expert-sorted layout, activation gather and the weighted
+// combine (with the gated shared expert fused in).
+//
+//  * moe_route: one warp per token. Mode 0 = softmax over the router logits, top-k (ties to the lower
+//    expert id), optional renormalisation (Qwen / Flash-Next class; reference
+//    kernels/r9k_moe_route.hip:4-31). Mode 1 = sigmoid scores plus a correction bias, group-limited
+//    top-k (groups ranked by the sum of their two best biased scores), weights = unbiased scores,
+//    optionally renormalised, times a routing scale (GLM / DeepSeek class; reference
+//    r9700_vllm/dsv4_glue.py:180 route, kernels/r9k_dsv4_glue.hip:300 sqrt-softplus variant = mode 2).
+//  * moe_align: one CTA. Counts the assignments of the local experts [e0, e0 + E_local), lays every
+//    expert's rows out in a segment starting on a 128-row boundary (so MX scale chunks of the
+//    activation rows line up with GEMM tiles), and emits the (expert, first row, rows) work list of
+//    BN-row tiles the grouped GEMMs run over. Non-local assignments get row -1 (expert parallelism:
+//    another rank owns them and the all-reduce that follows sums the partials).
+//  * moe_gather: copies each assignment's MXFP8 token row (+ scale bytes) to its sorted row.
+//  * moe_combine: out[t] = sum_j w[t,j] * y[row(t,j)] (+ sigmoid(shared gate) * shared[t]), fp32, one
+//    rounding (reference kernels/r9k_moe_sum.hip:4-12).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+
+namespace r9k {
+
+constexpr int MOE_MAX_E = 1024;
+constexpr int MOE_MAX_K = 16;
+
+// warp argmax over (value, id) pairs, ties -> lower id
+R9K_DEVINL void warp_argmax(float& v, int& id) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, id, o);
+    if (ov > v || (ov == v && oi < id)) { v = ov; id = oi; }
+  }
+}
+
+__global__ void moe_route_kernel(const float* __restrict__ logits, int64_t ld, int T, int E, int k, int mode,
+                                 const float* __restrict__ bias, int n_group, int topk_group, float scale,
+                                 int renorm, int32_t* __restrict__ ids, float* __restrict__ w) {
+  pdl_wait();
+  extern __shared__ float sh[];  // per warp: E scores + E biased scores
+  const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
+  const int t = blockIdx.x * (blockDim.x >> 5) + wib;
+  if (t >= T) return;
+  float* sc = sh + wib * 2 * E;
+  float* bs = sc + E;
+  const float* row = logits + (int64_t)t * ld;
+  if (mode == 0) {
+    float m = -INFINITY;
+    for (int e = lane; e < E; e += 32) m = fmaxf(m, row[e]);
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float s = 0.f;
+    for (int e = lane; e < E; e += 32) {
+      const float p = __expf(row[e] - m);
+      sc[e] = p;
+      s += p;
+    }
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float inv = 1.f / s;
+    for (int e = lane; e < E; e += 32) { sc[e] *= inv; bs[e] = sc[e]; }
+  } else {
+    for (int e = lane; e < E; e += 32) {
+      const float x = row[e];
+      const float s = mode == 1 ? sigmoid_f(x) : sqrtf(softplus_f(x));
+      sc[e] = s;
+      bs[e] = s + (bias != nullptr ? bias[e] : 0.f);
+    }
+    __syncwarp();
+    if (n_group > 1) {
+      // rank groups by the sum of their two best biased scores, keep topk_group groups
+      const int gs = E / n_group;
+      float gscore = -INFINITY;
+      if (lane < n_group) {
+        float b1 = -INFINITY, b2 = -INFINITY;
+        for (int e = lane * gs; e < (lane + 1) * gs; ++e) {
+          const float v = bs[e];
+          if (v > b1) { b2 = b1; b1 = v; } else if (v > b2) b2 = v;
+        }
+        gscore = b1 + b2;
+      }
+      uint32_t keep = 0;
+      for (int i = 0; i < topk_group; ++i) {
+        float v = (lane < n_group && !((keep >> lane) & 1u)) ? gscore : -INFINITY;
+        int id = lane;
+        warp_argmax(v, id);
+        keep |= 1u << id;
+      }
+      __syncwarp();
+      for (int e = lane; e < E; e += 32)
+        if (!((keep >> (e / gs)) & 1u)) bs[e] = -INFINITY;
+    }
+  }
+  __syncwarp();
+  // top-k by the (biased) selection score
+  float sel_w[MOE_MAX_K];
+  int sel_id[MOE_MAX_K];
+  float wsum = 0.f;
+  for (int i = 0; i < k; ++i) {
+    float v = -INFINITY;
+    int id = 0x7fffffff;
+    for (int e = lane; e < E; e += 32)
+      if (bs[e] > v || (bs[e] == v && e < id)) { v = bs[e]; id = e; }
+    warp_argmax(v, id);
+    if (lane == (id & 31)) bs[id] = -INFINITY;
+    __syncwarp();
+    sel_id[i] = id;
+    sel_w[i] = sc[id];
+    wsum += sc[id];
+  }
+  if (lane < k) {
+    float wv = 0.f;
+    int iv = 0;
+#pragma unroll
+    for (int i = 0; i < MOE_MAX_K; ++i)
+      if (i == lane) { wv = sel_w[i]; iv = sel_id[i]; }
+    if (renorm) wv /= wsum;
+    ids[(int64_t)t * k + lane] = iv;
+    w[(int64_t)t * k + lane] = wv * scale;
+  }
+}
+
+void moe_route(torch::Tensor logits, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias, int64_t n_group,
+               int64_t topk_group, double scale, bool renorm, torch::Tensor ids, torch::Tensor w) {
+  const int64_t T = logits.size(0), E = logits.size(1);
+  TORCH_CHECK(E <= MOE_MAX_E && k <= MOE_MAX_K && k <= 32 && logits.dtype() == torch::kFloat32, "moe_route: shapes");
+  TORCH_CHECK(n_group <= 32 && (n_group <= 1 || E % n_group == 0), "moe_route: groups");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(logits.device());
+  const int wpb = 4;
+  const size_t smem = (size_t)wpb * 2 * E * sizeof(float);
+  TORCH_CHECK(launch_pdl(moe_route_kernel, dim3((unsigned)((T + wpb - 1) / wpb)), dim3(32 * wpb), smem,
+                         at::cuda::getCurrentCUDAStream(), logits.data_ptr<float>(), logits.stride(0), (int)T, (int)E,
+                         (int)k, (int)mode, (bias.has_value() && bias->defined()) ? bias->data_ptr<float>() : nullptr,
+                         (int)n_group, (int)topk_group, (float)scale, renorm ? 1 : 0, ids.data_ptr<int32_t>(),
+                         w.data_ptr<float>()) == cudaSuccess,
+              "moe_route launch");
+}
+
+// ------------------------------------------------------------------------------------------------
+// align: counts -> 128-aligned segments -> BN-row work tiles; scatter assignment rows
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restrict__ ids, int A, int e0, int E_local,
+                                                         int BN, int32_t* __restrict__ perm_row,
+                                                         int32_t* __restrict__ seg_start, int32_t* __restrict__ work,
+                                                         int32_t* __restrict__ work_count, int max_work) {
+  pdl_wait();
+  __shared__ int cnt[MOE_MAX_E], start[MOE_MAX_E], cursor[MOE_MAX_E], tiles[MOE_MAX_E];
+  __shared__ int s_tot, s_tiles;
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  for (int a = threadIdx.x; a < A; a += blockDim.x) {
+    const int e = ids[a] - e0;
+    if (e >= 0 && e < E_local) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int s = 0, tl = 0;
+    for (int e = 0; e < E_local; ++e) {
+      start[e] = s;
+      cursor[e] = 0;
+      tiles[e] = tl;
+      s += (cnt[e] + 127) / 128 * 128;
+      tl += (cnt[e] + BN - 1) / BN;
+    }
+    s_tot = s;
+    s_tiles = min(tl, max_work);
+    *work_count = s_tiles;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
+    seg_start[e] = start[e];
+    const int nt = (cnt[e] + BN - 1) / BN;
+    for (int i = 0; i < nt; ++i) {
+      const int wi = tiles[e] + i;
+      if (wi < max_work) {
+        work[wi * 3 + 0] = e;
+        work[wi * 3 + 1] = start[e] + i * BN;
+        work[wi * 3 + 2] = min(BN, cnt[e] - i * BN);
+      }
+    }
+  }
+  // rows in assignment order within each expert (a serial pass per expert keeps the layout deterministic)
+  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
+    if (cnt[e] == 0) continue;
+    int c = 0;
+    for (int a = 0; a < A; ++a)
+      if (ids[a] - e0 == e) perm_row[a] = start[e] + c++;
+  }
+  for (int a = threadIdx.x; a < A; a += blockDim.x) {
+    const int e = ids[a] - e0;
+    if (e < 0 || e >= E_local) perm_row[a] = -1;
+  }
+}
+
+void moe_align(torch::Tensor ids, int64_t e0, int64_t E_local, int64_t BN, torch::Tensor perm_row,
+               torch::Tensor seg_start, torch::Tensor work, torch::Tensor work_count) {
+  TORCH_CHECK(E_local <= MOE_MAX_E, "moe_align: too many local experts");
+  TORCH_CHECK(BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256, "moe_align: BN");
+  const at::cuda::CUDAGuard guard(ids.device());
+  TORCH_CHECK(launch_pdl(moe_align_kernel, dim3(1), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
+                         ids.data_ptr<int32_t>(), (int)ids.numel(), (int)e0, (int)E_local, (int)BN,
+                         perm_row.data_ptr<int32_t>(), seg_start.data_ptr<int32_t>(), work.data_ptr<int32_t>(),
+                         work_count.data_ptr<int32_t>(), (int)work.size(0)) == cudaSuccess,
+              "moe_align launch");
+}
+
+// ------------------------------------------------------------------------------------------------
+// gather: sorted activation row p <- token row t (MXFP8 bytes + ue8m0 scales)
+// ------------------------------------------------------------------------------------------------
+__global__ void moe_gather_kernel(const uint8_t* __restrict__ q, const uint8_t* __restrict__ sf, int K, int k,
+                                  const int32_t* __restrict__ perm_row, uint8_t* __restrict__ oq,
+                                  uint8_t* __restrict__ osf) {
+  pdl_wait();
+  const int a = blockIdx.x;
+  const int p = perm_row[a];
+  if (p < 0) return;
+  const int t = a / k;
+  const int kblocks = K / 32;
+  const uint4* src = reinterpret_cast<const uint4*>(q + (int64_t)t * K);
+  uint4* dst = reinterpret_cast<uint4*>(oq + (int64_t)p * K);
+  for (int i = threadIdx.x; i < K / 16; i += blockDim.x) dst[i] = src[i];
+  for (int b = threadIdx.x; b < kblocks; b += blockDim.x) osf[sf_offset(p, b, kblocks)] = sf[sf_offset(t, b, kblocks)];
+}
+
+void moe_gather(torch::Tensor q, torch::Tensor sf, int64_t k, torch::Tensor perm_row, torch::Tensor oq,
+                torch::Tensor osf) {
+  const int64_t A = perm_row.numel(), K = q.size(1);
+  TORCH_CHECK(K % 32 == 0, "moe_gather: K % 32");
+  if (A == 0) return;
+  const at::cuda::CUDAGuard guard(q.device());
+  TORCH_CHECK(launch_pdl(moe_gather_kernel, dim3((unsigned)A), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+                         q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), (int)K, (int)k, perm_row.data_ptr<int32_t>(),
+                         oq.data_ptr<uint8_t>(), osf.data_ptr<uint8_t>()) == cudaSuccess,
+              "moe_gather launch");
+}
+
+// ------------------------------------------------------------------------------------------------
+// combine
+// ------------------------------------------------------------------------------------------------
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, const int32_t* __restrict__ perm_row,
+                                   const float* __restrict__ w, int k, int H, const __nv_bfloat16* __restrict__ shared,
+                                   const float* __restrict__ shared_gate, __nv_bfloat16* __restrict__ out,
+                                   int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int t = blockIdx.x;
+  float gs = 1.f;
+  if (shared_gate != nullptr) gs = sigmoid_f(shared_gate[t]);
+  for (int h = threadIdx.x * 2; h < H; h += blockDim.x * 2) {
+    float a0 = 0.f, a1 = 0.f;
+    for (int j = 0; j < k; ++j) {
+      const int p = perm_row[(int64_t)t * k + j];
+      if (p < 0) continue;
+      const float wj = w[(int64_t)t * k + j];
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (int64_t)p * H + h);
+      a0 += wj * __bfloat162float(v.x);
+      a1 += wj * __bfloat162float(v.y);
+    }
+    if (shared != nullptr) {
+      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(shared + (int64_t)t * H + h);
+      a0 += gs * __bfloat162float(v.x);
+      a1 += gs * __bfloat162float(v.y);
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + (int64_t)t * ldo + h) = __floats2bfloat162_rn(a0, a1);
+  }
+}
+
+void moe_combine(torch::Tensor y, torch::Tensor perm_row, torch::Tensor w, int64_t k,
+                 c10::optional<torch::Tensor> shared, c10::optional<torch::Tensor> shared_gate, torch::Tensor out) {
+  const int64_t T = out.size(0), H = out.size(1);
+  TORCH_CHECK(H % 2 == 0, "moe_combine: H even");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(out.device());
+  TORCH_CHECK(launch_pdl(moe_combine_kernel, dim3((unsigned)T), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                         reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), perm_row.data_ptr<int32_t>(),
+                         w.data_ptr<float>(), (int)k, (int)H,
+                         (shared.has_value() && shared->defined()) ? reinterpret_cast<const __nv_bfloat16*>(shared->data_ptr()) : nullptr,
+                         (shared_gate.has_value() && shared_gate->defined()) ? shared_gate->data_ptr<float>() : nullptr,
+                         reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0)) == cudaSuccess,
+              "moe_combine launch");
+}
+
+}  // namespace r9k

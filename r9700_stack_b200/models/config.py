@@ -99,6 +99,30 @@ def flashnext_moe() -> HybridConfig:
     )
 
 
+def tiny_moe(**kw) -> HybridConfig:
+    """A small Flash-Next-class MoE config (bf16 attention/dense, NVFP4 experts), for tests."""
+    base = dict(
+        name="tiny-moe",
+        hidden=256,
+        layers=4,
+        vocab=512,
+        n_q_heads=4,
+        n_kv_heads=2,
+        head_dim=256,
+        gdn_k_heads=2,
+        gdn_v_heads=4,
+        ffn=0,
+        moe_experts=8,
+        moe_topk=3,
+        moe_ffn=256,
+        moe_shared_ffn=256,
+        weight_format="bf16",
+        lm_head_format="bf16",
+    )
+    base.update(kw)
+    return HybridConfig(**base)
+
+
 def tiny_hybrid(**kw) -> HybridConfig:
     """A small config of the same class, for tests."""
     base = dict(

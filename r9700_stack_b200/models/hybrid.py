@@ -97,6 +97,8 @@ class Workspace:
         self.gdn_bf16 = torch.zeros(max_tokens, g["hv"] * c.gdn_head_dim, dtype=torch.bfloat16, device=dev)
         if model.ffn_local > 0:
             self.ffn_act = L.alloc_act(max_tokens, model.ffn_local, dev)
+            if not model.mx:
+                self.ffn_bf16 = torch.zeros(max_tokens, model.ffn_local, dtype=torch.bfloat16, device=dev)
         # split-KV partials for the tcgen05 decode attention
         self.nsplit_max = 16
         rows = max_logit_rows * a["hq"]
@@ -301,7 +303,28 @@ class HybridLM:
         if self.mx:
             L.mx_swiglu(ws.act.narrow(T), lay["w_gate"], lay["w_up"], out=ws.ffn_act.narrow(T))
             return ws.ffn_act.narrow(T), None, lay["w_down"]
-        raise NotImplementedError("bf16 dense FFN path")
+        L.bf16_swiglu(ws.norm_out[:T], lay["w_gate"], lay["w_up"], out=ws.ffn_bf16[:T])
+        return None, ws.ffn_bf16[:T], lay["w_down"]
+
+    def _ffn_block(self, i: int, lay, meta, ws: Workspace, T: int, call: int, fused: bool) -> None:
+        """The FFN sublayer including its row-parallel reduction (overridden by the MoE model)."""
+        act, xb, w = self._ffn(lay, ws, T)
+        self._row_parallel(act, xb, w, ws, T, call=call, fused=fused)
+
+    def _reduce_target(self, ws: Workspace, T: int, call: int, fused: bool) -> torch.Tensor:
+        """Where a sublayer writes its partial sum: this rank's symmetric buffer (pull) or ws.y."""
+        if fused and self.comm.mode == "pull":
+            return self.comm.out_buffer(call, T)
+        return ws.y[:T]
+
+    def _after_partial(self, ws: Workspace, T: int, call: int, fused: bool) -> None:
+        """Complete the reduction of a partial written to _reduce_target()."""
+        if fused and self.comm.mode == "pull":
+            return
+        if fused:
+            self.comm.push(ws.y[:T], call)
+        else:
+            self.comm.all_reduce_(ws.y[:T])
 
     def _row_parallel(self, act, xb, w, ws: Workspace, T: int, call: int, fused: bool) -> None:
         """Output projection of a sublayer: partial sums pushed to every rank (fused) or written to
@@ -353,8 +376,7 @@ class HybridLM:
                 act, xb, w = self._gdn(i, lay, meta, ws, T)
             self._row_parallel(act, xb, w, ws, T, call=2 * i, fused=fused)
             self._post_reduce_norm(lay["post_norm"], ws, T, call=2 * i, fused=fused)
-            act, xb, w = self._ffn(lay, ws, T)
-            self._row_parallel(act, xb, w, ws, T, call=2 * i + 1, fused=fused)
+            self._ffn_block(i, lay, meta, ws, T, call=2 * i + 1, fused=fused)
         # final: residual add + norm, then the rows that need logits
         self._post_reduce_norm(self.final_norm, ws, T, call=2 * nl - 1, fused=fused, final=True)
         rows = ws.final_bf16[:R]

@@ -80,9 +80,12 @@ def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Ten
             y = bf16(_gdn(model, i, lay, h, st, mx))
         resid = bf16(resid + y)
         h = rmsnorm(resid, lay["post_norm"], c.rms_eps, c.norm_plus_one)
-        g = _lin(h, lay["w_gate"], mx)
-        u = _lin(h, lay["w_up"], mx)
-        y = bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
+        if "router" in lay:
+            y = bf16(_moe(model, lay, bf16(h)))
+        else:
+            g = _lin(h, lay["w_gate"], mx)
+            u = _lin(h, lay["w_up"], mx)
+            y = bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
     resid = bf16(resid + y)
     h = bf16(rmsnorm(resid, model.final_norm, c.rms_eps, c.norm_plus_one))
     lm_mx = isinstance(model.lm_head, L.MXWeight)
@@ -180,3 +183,33 @@ def _gdn(model, i, lay, h, st, mx):
     o = o * torch.rsqrt(o.pow(2).mean(-1, keepdim=True) + c.rms_eps) * lay["gdn_norm"].float() * Fn.silu(z)
     o = bf16(o.reshape(T, hv * d))
     return _lin(o, lay["w_out"], mx)
+
+
+def _moe(model, lay, x):
+    """Routed experts (softmax top-k, renormalised) + sigmoid-gated shared expert, fp32 math."""
+    c = model.cfg
+    T = x.shape[0]
+    logits = bf16(x) @ lay["router"].w.float().T
+    p = torch.softmax(logits, -1)
+    w, ids = torch.topk(p, c.moe_topk, dim=-1)
+    w = w / w.sum(-1, keepdim=True)
+    xq = fake_mxfp8(x)
+    I, El = c.moe_ffn, model.e_local
+    e0 = model.par.tp_rank * El
+    G = lay["e_gate"].dequant().view(El, I, -1)
+    U = lay["e_up"].dequant().view(El, I, -1)
+    D = lay["e_down"].dequant().view(El, c.hidden, I)
+    out = torch.zeros(T, c.hidden, device=x.device)
+    for t in range(T):
+        for j in range(c.moe_topk):
+            e = int(ids[t, j]) - e0
+            if not 0 <= e < El:
+                continue
+            hh = Fn.silu(xq[t] @ G[e].T) * (xq[t] @ U[e].T)
+            out[t] += w[t, j] * (fake_mxfp8(hh[None])[0] @ D[e].T).to(torch.bfloat16).float()
+    if "s_gate" in lay:
+        sh = bf16(Fn.silu(x @ lay["s_gate"].w.float().T) * (x @ lay["s_up"].w.float().T))
+        sh = bf16(sh @ lay["s_down"].w.float().T)
+        gt = torch.sigmoid(x @ lay["s_gvec"].w.float().T)
+        out = out + gt * sh
+    return out

@@ -256,3 +256,21 @@ def bf16_linear(
         out = torch.empty(M, w.N, dtype=out_dtype, device=x.device)
     _ops().gemm_bf16(w.w, x, out, residual, float(alpha), _status.status(x.device), gemm_workspace(x.device))
     return out
+
+
+def bf16_swiglu(x: torch.Tensor, w_gate: BF16Weight, w_up: BF16Weight, out: torch.Tensor | None = None):
+    """silu(x W_gate^T) * (x W_up^T) in one tcgen05 kernel (bf16 weights, bf16 result)."""
+    if out is None:
+        out = torch.empty(x.shape[0], w_gate.N, dtype=torch.bfloat16, device=x.device)
+    _ops().gemm_bf16_swiglu(w_gate.w, w_up.w, x, out, _status.status(x.device), gemm_workspace(x.device))
+    return out
+
+
+def stack_experts(ws: list[MXWeight]) -> MXWeight:
+    """Stack per-expert MX weights [N, K] into one [E * N, K] matrix (pre-tiled units, scale chunks
+    concatenated in the same order) for the grouped GEMM."""
+    assert all(w.N == ws[0].N and w.K == ws[0].K and w.fp4 == ws[0].fp4 for w in ws) and ws[0].N % 128 == 0
+    tiled = [w.to_tiled() for w in ws]
+    q = torch.cat([w.q for w in tiled], 0)
+    sf = torch.cat([w.sf for w in tiled], 0)
+    return MXWeight(q, sf, ws[0].fp4, ws[0].N * len(ws), ws[0].K)
