@@ -778,3 +778,157 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
 }
 
 }  // namespace r9k
+
+// ---------------------------------------------------------------------------------------------
+// r9k_gemm_bf16_noalloc: the skinny bf16 GEMM with split-K scratch in a fixed device array (no
+// allocation of any kind; declared and documented in r9k_noalloc.h).
+// ---------------------------------------------------------------------------------------------
+#include <cstdio>
+#include "r9k_noalloc.h"
+
+namespace {
+
+constexpr int64_t kNaCounterInts = 1024;  // 4 KiB of per-tile counters
+constexpr int64_t kNaPartFloats = (int64_t)(R9K_NOALLOC_SCRATCH_BYTES / 4) - kNaCounterInts;
+constexpr int kNaMaxDev = 64;
+
+__device__ __align__(256) float r9k_noalloc_scratch[R9K_NOALLOC_SCRATCH_BYTES / 4];
+
+struct NaDevice {
+  bool ready = false;
+  float* scratch = nullptr;  // device address of r9k_noalloc_scratch on this device
+};
+NaDevice g_na[kNaMaxDev];
+std::mutex g_na_mu;
+r9k::EncodeTiledFn g_na_encode = nullptr;
+
+template <int BN, int NP>
+cudaError_t na_set_attr() {
+  using C = r9k::GemmCfg<r9k::KIND_BF16, BN, false, NP, 1, false>;
+  return cudaFuncSetAttribute(r9k::gemm_tc_kernel<r9k::KIND_BF16, BN, false, r9k::EPI_BF16, NP, 1, false>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES);
+}
+
+int na_setup(int dev) {
+  std::lock_guard<std::mutex> lk(g_na_mu);
+  if (g_na[dev].ready) return R9K_NOALLOC_OK;
+  void* p = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&p, r9k_noalloc_scratch);
+  if (e != cudaSuccess || p == nullptr) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: scratch address lookup failed on device %d: %s\n", dev,
+            cudaGetErrorString(e));
+    return R9K_NOALLOC_ESETUP;
+  }
+  e = na_set_attr<16, 5>();
+  if (e == cudaSuccess) e = na_set_attr<32, 5>();
+  if (e == cudaSuccess) e = na_set_attr<64, 4>();
+  if (e != cudaSuccess) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: kernel attribute set-up failed: %s\n", cudaGetErrorString(e));
+    return R9K_NOALLOC_ESETUP;
+  }
+  if (g_na_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || fn == nullptr) {
+      fprintf(stderr, "r9k_gemm_bf16_noalloc: cuTensorMapEncodeTiled unavailable\n");
+      return R9K_NOALLOC_ESETUP;
+    }
+    g_na_encode = reinterpret_cast<r9k::EncodeTiledFn>(fn);
+  }
+  g_na[dev].scratch = static_cast<float*>(p);
+  g_na[dev].ready = true;
+  return R9K_NOALLOC_OK;
+}
+
+bool na_tmap(CUtensorMap* m, const void* base, int64_t rows, int64_t K, int64_t ld, int box_rows) {
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  return g_na_encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int NP>
+int na_launch(const CUtensorMap& ta, const CUtensorMap& tb, r9k::GemmArgs a, int S, int grid_x, float* scratch,
+              cudaStream_t stream) {
+  using C = r9k::GemmCfg<r9k::KIND_BF16, BN, false, NP, 1, false>;
+  int* cnt = nullptr;
+  float* part = nullptr;
+  if (S > 1) {
+    const int64_t tiles = grid_x;  // M <= 64 is one token tile
+    const int64_t need = tiles * S * C::TILE_F;
+    if (tiles > kNaCounterInts || need > kNaPartFloats) {
+      fprintf(stderr,
+              "r9k_gemm_bf16_noalloc: N=%d needs %lld bytes of split-K scratch, more than the fixed %u-byte "
+              "array holds\n",
+              a.N, (long long)(need * 4 + kNaCounterInts * 4), (unsigned)R9K_NOALLOC_SCRATCH_BYTES);
+      return R9K_NOALLOC_ETOOLARGE;
+    }
+    cnt = reinterpret_cast<int*>(scratch);
+    part = scratch + kNaCounterInts;
+  }
+  a.splits = S;
+  a.kc_per_split = (a.kchunks + S - 1) / S;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid_x, S, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = C::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, r9k::gemm_tc_kernel<r9k::KIND_BF16, BN, false, r9k::EPI_BF16, NP, 1, false>,
+                                           ta, ta, tb, a, part, cnt);
+  if (e != cudaSuccess) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: launch failed: %s\n", cudaGetErrorString(e));
+    return R9K_NOALLOC_ELAUNCH;
+  }
+  return R9K_NOALLOC_OK;
+}
+
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) int r9k_gemm_bf16_noalloc(
+    const void* w, int64_t ldw, const void* x, int64_t ldx, void* out, int64_t ldo, int N, int M, int K, float alpha,
+    int* status, cudaStream_t stream) {
+  auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (w == nullptr || x == nullptr || out == nullptr || N < 1 || M < 1 || K < 64 || K % 64 != 0 || ldw < K ||
+      ldx < K || ldo < N || ldw % 8 != 0 || ldx % 8 != 0 || !aligned16(w) || !aligned16(x)) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: invalid arguments (N=%d M=%d K=%d ldw=%lld ldx=%lld ldo=%lld)\n", N, M,
+            K, (long long)ldw, (long long)ldx, (long long)ldo);
+    return R9K_NOALLOC_EINVAL;
+  }
+  if (M > 64) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: M=%d tokens; this entry point serves M <= 64\n", M);
+    return R9K_NOALLOC_ETOOLARGE;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNaMaxDev) return R9K_NOALLOC_ESETUP;
+  if (!g_na[dev].ready) {
+    const int rc = na_setup(dev);
+    if (rc != R9K_NOALLOC_OK) return rc;
+  }
+  const r9k::LaunchPlan p = r9k::plan_gemm(N, M, K / 64, false, false);
+  CUtensorMap ta, tb;
+  if (!na_tmap(&ta, w, N, K, ldw, 128) || !na_tmap(&tb, x, M, K, ldx, p.BN)) {
+    fprintf(stderr, "r9k_gemm_bf16_noalloc: tensor-map encoding rejected the operands\n");
+    return R9K_NOALLOC_EINVAL;
+  }
+  r9k::GemmArgs a = {};
+  a.N = N; a.M = M; a.K = K; a.kchunks = K / 64;
+  a.out = out; a.ldo = (int)ldo;
+  a.alpha = alpha;
+  a.status = status;
+  a.timeout_ns = 1000000000ull;
+  const int grid_x = (N + 127) / 128;
+  switch (p.BN) {
+    case 16: return na_launch<16, 5>(ta, tb, a, p.S, grid_x, g_na[dev].scratch, stream);
+    case 32: return na_launch<32, 5>(ta, tb, a, p.S, grid_x, g_na[dev].scratch, stream);
+    default: return na_launch<64, 4>(ta, tb, a, p.S, grid_x, g_na[dev].scratch, stream);
+  }
+}
