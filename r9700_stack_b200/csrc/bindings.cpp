@@ -90,6 +90,11 @@ void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64
                    torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out);
 void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::Tensor seq_slot,
                            torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_has_state);
+void gdn_spec_commit(torch::Tensor table, int64_t Hk, int64_t Hv, int64_t dv, int64_t C, int64_t W, int64_t ld,
+                     bool state_f32, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor acc_len,
+                     torch::Tensor seq_has_state);
+void spec_accept(torch::Tensor input_ids, torch::Tensor target, torch::Tensor seq_start, torch::Tensor seq_len,
+                 torch::Tensor acc_len);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -161,6 +166,9 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!) g_out, Tensor(e!) beta_out) -> ()");
   m.def("gdn_conv_state_update(Tensor proj, Tensor(a!) conv_state, Tensor seq_slot, Tensor seq_start, "
         "Tensor seq_len, Tensor seq_has_state) -> ()");
+  m.def("gdn_spec_commit(Tensor table, int Hk, int Hv, int dv, int C, int W, int ld, bool state_f32, "
+        "Tensor seq_slot, Tensor seq_start, Tensor acc_len, Tensor seq_has_state) -> ()");
+  m.def("spec_accept(Tensor input_ids, Tensor target, Tensor seq_start, Tensor seq_len, Tensor(a!) acc_len) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -198,6 +206,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("attn_tc_prefill", &r9k::attn_tc_prefill);
   m.impl("gdn_conv_prep", &r9k::gdn_conv_prep);
   m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
+  m.impl("gdn_spec_commit", &r9k::gdn_spec_commit);
+  m.impl("spec_accept", &r9k::spec_accept);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);

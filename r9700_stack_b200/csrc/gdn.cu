@@ -553,4 +553,123 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------------------------
+// speculative commit: after a verify pass (state not written) accepted n_s tokens of sequence s;
+// replay the recurrence over those tokens from the saved per-layer k/v/g/beta and store the state,
+// and shift the conv state by the same tokens' saved inputs. All GDN layers in one launch:
+// grid (S, Hv * dv/32 + ceil(C / 128), layers), 128 threads. CTAs y < Hv * dv/32 run the recurrence
+// of (head, 32-column group) exactly as gdn_recurrent_kernel (without q / output); the others update
+// 128 conv channels each. The two parts touch disjoint state, so they need no ordering.
+// (reference: kernels/r9k_gdn.hip:575-647 r9k_gdn_spec_commit_kernel.)
+// ------------------------------------------------------------------------------------------------
+struct GdnCommitLayer {
+  const float* k;     // [Tv, Hk, 128]
+  const float* v;     // [Tv, Hv, dv]
+  const float* g;     // [Tv, Hv] (log decay)
+  const float* beta;  // [Tv, Hv]
+  const __nv_bfloat16* proj;  // [Tv, ld]: conv inputs in the first C channels
+  void* ssm;          // [slots, Hv, dv, 128]
+  void* conv;         // [slots, C, W-1]
+  int64_t pad;
+};
+
+template <typename ST>
+__global__ void __launch_bounds__(128) gdn_spec_commit_kernel(
+    const GdnCommitLayer* __restrict__ layers, int Hk, int Hv, int dv, int C, int W, int64_t ld,
+    const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_start, const int32_t* __restrict__ acc_len,
+    const int32_t* __restrict__ seq_has_state) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int DK = 128, CH = 16;
+  __shared__ float sk[CH][DK], sv[CH][32], sg[CH], sb[CH];
+  const GdnCommitLayer Lr = layers[blockIdx.z];
+  const int s = blockIdx.x, tid = threadIdx.x;
+  const int slot = seq_slot[s], t0 = seq_start[s], n = acc_len[s];
+  const bool hs = seq_has_state[s] != 0;
+  if (n <= 0) return;
+  const int nrec = Hv * (dv / 32);
+  if ((int)blockIdx.y >= nrec) {
+    const int c = ((int)blockIdx.y - nrec) * 128 + tid;
+    if (c >= C) return;
+    ST* cs = reinterpret_cast<ST*>(Lr.conv) + ((int64_t)slot * C + c) * (W - 1);
+    float nv[8];
+    for (int i = 0; i < W - 1; ++i) {
+      const int idx = n - (W - 1) + i;
+      if (idx >= 0) nv[i] = __bfloat162float(Lr.proj[(int64_t)(t0 + idx) * ld + c]);
+      else {
+        const int oi = (W - 1) + idx;
+        nv[i] = (hs && oi >= 0) ? to_f<ST>(cs[oi]) : 0.f;
+      }
+    }
+    for (int i = 0; i < W - 1; ++i) cs[i] = from_f<ST>(nv[i]);
+    return;
+  }
+  const int h = (int)blockIdx.y / (dv / 32), cgrp = (int)blockIdx.y % (dv / 32);
+  const int c = tid >> 2, rg = tid & 3;
+  const int col = cgrp * 32 + c;
+  const int kh = h / (Hv / Hk);
+  ST* Sp = reinterpret_cast<ST*>(Lr.ssm) + (((int64_t)slot * Hv + h) * dv + col) * DK + rg * 32;
+  float S[32];
+  if (hs) StateVec<ST>::load(Sp, S);
+  else {
+#pragma unroll
+    for (int r = 0; r < 32; ++r) S[r] = 0.f;
+  }
+  for (int base = 0; base < n; base += CH) {
+    const int cnt = min(CH, n - base);
+    __syncthreads();
+    for (int e = tid; e < cnt * DK; e += 128) {
+      const int tt = e / DK, i = e % DK;
+      const int64_t tok = t0 + base + tt;
+      sk[tt][(i & 31) * 4 + (i >> 5)] = Lr.k[(tok * Hk + kh) * DK + i];
+    }
+    for (int e = tid; e < cnt * 32; e += 128) {
+      const int tt = e / 32, cc = e % 32;
+      sv[tt][cc] = Lr.v[((int64_t)(t0 + base + tt) * Hv + h) * dv + cgrp * 32 + cc];
+    }
+    if (tid < cnt) {
+      const int64_t tok = t0 + base + tid;
+      sg[tid] = __expf(Lr.g[tok * Hv + h]);
+      sb[tid] = Lr.beta[tok * Hv + h];
+    }
+    __syncthreads();
+    for (int tt = 0; tt < cnt; ++tt) {
+      const float decay = sg[tt];
+      const float* kk = &sk[tt][rg];
+      float kv = 0.f;
+#pragma unroll
+      for (int r = 0; r < 32; ++r) kv += S[r] * kk[4 * r];
+      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
+      kv += __shfl_xor_sync(0xffffffffu, kv, 2);
+      const float delta = sb[tt] * (sv[tt][c] - decay * kv);
+#pragma unroll
+      for (int r = 0; r < 32; ++r) S[r] = S[r] * decay + kk[4 * r] * delta;
+    }
+  }
+  StateVec<ST>::store(Sp, S);
+}
+
+void gdn_spec_commit(torch::Tensor table, int64_t Hk, int64_t Hv, int64_t dv, int64_t C, int64_t W, int64_t ld,
+                     bool state_f32, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor acc_len,
+                     torch::Tensor seq_has_state) {
+  const int64_t S = seq_slot.size(0), nl = table.size(0);
+  if (S == 0 || nl == 0) return;
+  TORCH_CHECK(table.is_cuda() && table.dtype() == torch::kInt64 && table.size(1) * 8 == (int64_t)sizeof(GdnCommitLayer),
+              "gdn_spec_commit: layer table must be a device int64 [layers, 8] tensor");
+  TORCH_CHECK(dv % 32 == 0 && W - 1 <= 8 && Hv % Hk == 0, "gdn_spec_commit: dv % 32, conv width <= 9");
+  const at::cuda::CUDAGuard guard(seq_slot.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  const dim3 grid((unsigned)S, (unsigned)(Hv * (dv / 32) + (C + 127) / 128), (unsigned)nl);
+  const GdnCommitLayer* tab = reinterpret_cast<const GdnCommitLayer*>(table.data_ptr<int64_t>());
+  if (state_f32)
+    launch_pdl(gdn_spec_commit_kernel<float>, grid, dim3(128), 0, st, tab, (int)Hk, (int)Hv, (int)dv, (int)C,
+               (int)W, ld, seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(), acc_len.data_ptr<int32_t>(),
+               seq_has_state.data_ptr<int32_t>());
+  else
+    launch_pdl(gdn_spec_commit_kernel<__nv_bfloat16>, grid, dim3(128), 0, st, tab, (int)Hk, (int)Hv, (int)dv,
+               (int)C, (int)W, ld, seq_slot.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(),
+               acc_len.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace r9k

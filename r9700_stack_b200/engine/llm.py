@@ -20,7 +20,7 @@ from .scheduler import SamplingParams, Scheduler, Sequence
 
 class LLM:
     def __init__(self, model_cfg, engine_cfg: EngineConfig | None = None, par: ParallelConfig | None = None,
-                 device=None, seed: int = 0, comm=None, model=None):
+                 device=None, seed: int = 0, comm=None, model=None, drafter=None):
         self.engine_cfg = ec = engine_cfg or EngineConfig()
         self.par = par or ParallelConfig()
         if device is None:
@@ -37,6 +37,12 @@ class LLM:
                                    ec.max_model_len)
         max_tokens = max(ec.max_prefill_tokens, ec.max_batch * (1 + ec.spec_tokens))
         self.runner = ModelRunner(model, ec, ec.kv_block, max_tokens, ec.max_batch, blocks_per_seq)
+        self.drafter = None
+        self.spec_stats = {"steps": 0, "drafted": 0, "accepted": 0}
+        if ec.spec_tokens > 0:
+            model.alloc_spec(self.runner.ws, ec.max_batch * (1 + ec.spec_tokens))
+            self.drafter = drafter if drafter is not None else make_drafter(
+                ec.spec_method, model, ec, num_blocks, num_slots, seed)
         if ec.cuda_graphs:
             self.runner.capture_decode_graphs()
 
@@ -48,11 +54,28 @@ class LLM:
 
     def step(self) -> list[Sequence]:
         """One engine step (a prefill chunk or a decode step). Returns sequences that finished."""
-        out = self.scheduler.schedule()
+        k = self.engine_cfg.spec_tokens if self.drafter is not None else 0
+        out = self.scheduler.schedule(lookahead=1 + k)
         if out.kind == "idle":
             return []
-        toks = self.runner.execute(out)
-        return self.scheduler.finish_step(out, toks)
+        if out.kind == "decode" and self.drafter is not None:
+            drafts = self.drafter.drafts([c.seq for c in out.chunks])
+            toks, accepted = self.runner.execute_spec(out, drafts)
+            st = self.spec_stats
+            st["steps"] += 1
+            st["drafted"] += sum(len(d) for d in drafts.values())
+            st["accepted"] += sum(a - 1 for a in accepted.values())
+            done = self.scheduler.finish_step(out, toks)
+            self.drafter.after_step(self, out, accepted, drafts)
+        else:
+            toks = self.runner.execute(out)
+            done = self.scheduler.finish_step(out, toks)
+            if self.drafter is not None:
+                self.drafter.after_step(self, out, None, None)
+        if self.drafter is not None:
+            for s in done:
+                self.drafter.release(s)
+        return done
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work
@@ -62,6 +85,17 @@ class LLM:
         while self.has_unfinished():
             self.step()
         return [s.output for s in seqs]
+
+
+def make_drafter(method: str, model, ec: EngineConfig, num_blocks: int, num_slots: int, seed: int = 0):
+    """The drafter named by ``EngineConfig.spec_method``: ngram | mtp | block."""
+    from ..spec.drafters import ModelDrafter, NgramDrafter
+
+    if method == "ngram":
+        return NgramDrafter(ec.spec_tokens)
+    if method in ("mtp", "block"):
+        return ModelDrafter(model, method, ec.spec_tokens, ec, num_blocks, num_slots, seed=seed)
+    raise ValueError(f"unknown speculative method {method!r}")
 
 
 def build_model(cfg, par, device, seed=0, comm=None):

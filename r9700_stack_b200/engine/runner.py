@@ -248,6 +248,48 @@ class ModelRunner:
         return res
 
 
+    def execute_spec(self, out: SchedulerOutput, draft: dict[int, list[int]]):
+        """Speculative verify + commit: run [last token, drafts] of every sequence with the recurrent
+        state read-only, take the target's argmax at every position, accept drafts greedily on the device,
+        fold the accepted tokens into the GDN state (one launch) and return per sequence the accepted
+        drafts plus the bonus token, and the number of verified positions committed."""
+        from .. import _native
+
+        lay, arr = pack_step(out, self.block_size, draft=draft)
+        assert lay.R == lay.T
+        self._upload(arr)
+        meta = self.meta.views(lay, write_state=False)
+        meta.host_seqs = _host_seqs(out, draft)
+        ev = None
+        if self.device_events is not None:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            ev[0].record()
+        self.model.forward(meta, self.ws, lay.T, lay.R)
+        R = lay.R
+        torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
+        acc = self.ws.acc_len[: lay.S]
+        _native.ops().spec_accept(meta.input_ids, self.sample_out, meta.seq_start, meta.seq_len, acc)
+        self.model.commit(meta, self.ws, acc)
+        if ev is not None:
+            ev[1].record()
+            self.device_events.append(ev)
+        self.sample_host[:R].copy_(self.sample_out[:R], non_blocking=True)
+        torch.cuda.current_stream(self.device).synchronize()
+        self.d2h_bytes = R * 8
+        y = self.sample_host[:R].tolist()
+        res, accepted = {}, {}
+        t = 0
+        for ch in out.chunks:
+            d = draft.get(ch.seq.seq_id, [])
+            j = 0
+            while j < len(d) and d[j] == y[t + j]:
+                j += 1
+            res[ch.seq.seq_id] = y[t: t + j + 1]
+            accepted[ch.seq.seq_id] = j + 1
+            t += 1 + len(d)
+        return res, accepted
+
+
 def _host_seqs(out: SchedulerOutput, draft=None) -> list[tuple[int, int]]:
     res, t = [], 0
     for ch in out.chunks:

@@ -105,6 +105,12 @@ class Scheduler:
         seq.blocks.extend(self.blocks.allocate(n))
         return True
 
+    def ensure(self, seq: Sequence, upto: int) -> bool:
+        """Make sure the blocks of ``seq`` cover positions < upto (drafters write ahead)."""
+        if upto > self.max_model_len + 64:
+            return False
+        return self._grow(seq, upto)
+
     def _release(self, seq: Sequence) -> None:
         if seq.blocks:
             self.blocks.free(seq.blocks)
@@ -164,14 +170,15 @@ class Scheduler:
             if out.kind == "prefill":
                 seq.num_computed += ch.n
             toks = new_tokens.get(seq.seq_id, [])
-            if out.kind == "decode":
-                seq.num_computed = seq.length  # all previous tokens now cached
             for t in toks:
                 if len(seq.output) >= seq.params.max_tokens:
                     break
                 seq.output.append(t)
                 if not seq.params.ignore_eos and t == seq.params.eos_token_id:
                     break
+            if out.kind == "decode":
+                # every token but the newest is in the cache (a verify step commits the accepted drafts)
+                seq.num_computed = seq.length - 1
             if len(seq.output) >= seq.params.max_tokens or (
                 not seq.params.ignore_eos and seq.output and seq.output[-1] == seq.params.eos_token_id
             ):

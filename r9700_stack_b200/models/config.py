@@ -161,4 +161,5 @@ class EngineConfig:
     num_kv_blocks: int = 0  # 0 -> sized from max_batch * max_model_len
     cuda_graphs: bool = True
     graph_batch_sizes: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16])
-    spec_tokens: int = 0
+    spec_tokens: int = 0  # draft tokens verified per step (0: no speculative decoding)
+    spec_method: str = "ngram"  # ngram | mtp | block

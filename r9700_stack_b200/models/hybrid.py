@@ -109,6 +109,9 @@ class Workspace:
         self.final_bf16 = torch.zeros(max_logit_rows, H, dtype=torch.bfloat16, device=dev)
         self.logits_local = torch.zeros(max_logit_rows, model.vocab_local, dtype=torch.float32, device=dev)
         self.logits = torch.zeros(max_logit_rows, c.vocab, dtype=torch.float32, device=dev)
+        self.spec = None  # per-GDN-layer verify buffers (alloc_spec)
+        self.spec_table = None
+        self.acc_len = torch.zeros(max_logit_rows, dtype=torch.int32, device=dev)
 
 
 class HybridLM:
@@ -208,6 +211,38 @@ class HybridLM:
             conv[i] = torch.zeros(num_state_slots, g["conv_ch"], c.conv_width - 1, dtype=sdt, device=self.device)
         self.kv, self.ssm, self.conv = kv, ssm, conv
 
+    def alloc_spec(self, ws: Workspace, max_verify_tokens: int) -> None:
+        """Per-GDN-layer buffers a verify pass fills (projections and the conv/recurrence inputs of
+        every verified token), from which :meth:`commit` replays the accepted tokens, plus the
+        device table of their addresses that the one-launch commit kernel reads."""
+        c, g, dev = self.cfg, self.gdn_dims, self.device
+        Tv, d = max_verify_tokens, c.gdn_head_dim
+        ws.spec, rows = {}, []
+        for i in c.gdn_layers:
+            b = dict(
+                proj=torch.zeros(Tv, g["proj_rows"], dtype=torch.bfloat16, device=dev),
+                k=torch.zeros(Tv, g["hk"], d, dtype=torch.float32, device=dev),
+                v=torch.zeros(Tv, g["hv"], d, dtype=torch.float32, device=dev),
+                g=torch.zeros(Tv, g["hv"], dtype=torch.float32, device=dev),
+                b=torch.zeros(Tv, g["hv"], dtype=torch.float32, device=dev),
+            )
+            ws.spec[i] = b
+            rows.append([b["k"].data_ptr(), b["v"].data_ptr(), b["g"].data_ptr(), b["b"].data_ptr(),
+                         b["proj"].data_ptr(), self.ssm[i].data_ptr(), self.conv[i].data_ptr(), 0])
+        ws.spec_table = torch.tensor(rows, dtype=torch.int64).reshape(-1, 8).to(dev)
+        ws.spec_tokens = Tv
+
+    def commit(self, meta: StepMeta, ws: Workspace, acc_len: torch.Tensor) -> None:
+        """Fold the first acc_len[s] verified tokens of every sequence into its GDN state (conv and
+        recurrent), all layers in one launch. Attention needs nothing: the verify pass wrote every
+        verified token's KV, and positions past the accepted length are rewritten before use."""
+        if not self.cfg.gdn_layers:
+            return
+        c, g = self.cfg, self.gdn_dims
+        _ops().gdn_spec_commit(ws.spec_table, g["hk"], g["hv"], c.gdn_head_dim, g["conv_ch"], c.conv_width,
+                               g["proj_rows"], self.ssm[c.gdn_layers[0]].dtype == torch.float32,
+                               meta.seq_state_slot, meta.seq_start, acc_len, meta.seq_has_state)
+
     # --------------------------------------------------------------------------------------------
     def _linear(self, act: L.MXAct, xb: torch.Tensor, w, out: torch.Tensor):
         if isinstance(w, L.MXWeight):
@@ -270,7 +305,12 @@ class HybridLM:
     def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):
         c, g = self.cfg, self.gdn_dims
         hk, hv, d = g["hk"], g["hv"], c.gdn_head_dim
-        proj = ws.proj[:T]
+        sb = None
+        if not meta.write_state and ws.spec is not None:
+            # speculative verify: keep this layer's projections and recurrence inputs for commit()
+            assert T <= ws.spec_tokens, "verify batch exceeds the speculative buffers"
+            sb = ws.spec[i]
+        proj = (sb["proj"] if sb is not None else ws.proj)[:T]
         self._linear(ws.act.narrow(T), ws.norm_out[:T], lay["w_in"], proj)
         z_off = 2 * hk * d + hv * d
         b_off = z_off + hv * d
@@ -284,12 +324,13 @@ class HybridLM:
                                ws.gdn_act.q[:T] if self.mx else None, ws.gdn_act.sf if self.mx else None,
                                None if self.mx else ws.gdn_bf16[:T])
             return ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"]
+        gk, gv, gg, gb = (ws.gk, ws.gv, ws.gg, ws.gb) if sb is None else (sb["k"], sb["v"], sb["g"], sb["b"])
         o.gdn_conv_prep(proj, hk, hv, d, d, b_off, a_off, lay["conv_w"], conv, meta.tok_state_slot,
                         meta.tok_pos_in_chunk, meta.tok_has_state, lay["A_log"], lay["dt_bias"],
-                        ws.gq[:T], ws.gk[:T], ws.gv[:T], ws.gg[:T], ws.gb[:T])
+                        ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T])
         if meta.write_state:
             o.gdn_conv_state_update(proj, conv, meta.seq_state_slot, meta.seq_start, meta.seq_len, meta.seq_has_state)
-        o.gdn_recurrent(ws.gq[:T], ws.gk[:T], ws.gv[:T], ws.gg[:T], ws.gb[:T], ssm, meta.seq_state_slot,
+        o.gdn_recurrent(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, meta.seq_state_slot,
                         meta.seq_start, meta.seq_len, meta.seq_has_state, meta.write_state, ws.go[:T])
         if self.mx:
             o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, None, ws.gdn_act.q[:T],
@@ -357,13 +398,17 @@ class HybridLM:
         else:
             self._norm(ws.y, w, ws, T, residual=True)
 
+    def _embed(self, meta: StepMeta, ws: Workspace, T: int) -> None:
+        """Input of the first layer into ws.resid (token embeddings; drafters override this)."""
+        torch.index_select(self.embed, 0, meta.input_ids[:T], out=ws.resid[:T])
+
     def forward(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
         """Run T tokens; returns fp32 logits [R, vocab] for the rows in meta.logits_idx[:R]."""
         c = self.cfg
         fused = getattr(self.comm, "fused", False) and self.comm.can_fuse(T) and knobs.get("R9K_COMM") != "nccl"
         if fused:
             self.comm.step_begin()
-        torch.index_select(self.embed, 0, meta.input_ids[:T], out=ws.resid[:T])
+        self._embed(meta, ws, T)
         nl = len(self.layers)
         for i, lay in enumerate(self.layers):
             if i == 0:

@@ -68,13 +68,13 @@ class HybridMoELM(HybridLM):
         H, I = c.hidden, c.moe_ffn
         for lay in self.layers:
             lay["router"] = L.BF16Weight(wrep.randn(c.moe_experts, H, dtype=torch.bfloat16))
-            gate, up, down = [], [], []
-            for _ in range(self.e_local):
-                gate.append(from_float(wf.randn(I, H), "nvfp4", tiled=True))
-                up.append(from_float(wf.randn(I, H), "nvfp4", tiled=True))
-                down.append(from_float(wf.randn(H, I), "nvfp4", tiled=True))
-            lay["e_gate"], lay["e_up"], lay["e_down"] = L.stack_experts(gate), L.stack_experts(up), L.stack_experts(down)
-            del gate, up, down
+            # the local experts of a layer are generated and quantised as one stacked [E * rows, K] tensor
+            # (one NVFP4 global scale per layer); tiling the stacked tensor gives exactly the unit order
+            # of stack_experts() over per-expert weights, since every expert spans whole 128-row tiles
+            El = self.e_local
+            lay["e_gate"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
+            lay["e_up"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
+            lay["e_down"] = from_float(wf.randn(El * H, I), "nvfp4", tiled=True)
             if self.shared_local:
                 lay["s_gate"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
                 lay["s_up"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))

@@ -1,0 +1,169 @@
+"""Kernel micro-benchmark: one kernel family at one shape, CUDA-event timed, with a roofline fraction.
+
+    python -m r9700_stack_b200.tuning.kbench gemm --N 5120 --K 17408 --M 16 --fmt fp4
+    python -m r9700_stack_b200.tuning.kbench gemm --N 17408 --K 5120 --M 16 --fmt fp4 --swiglu
+    python -m r9700_stack_b200.tuning.kbench moe --T 16 --E 288 --topk 10 --H 2048 --I 512
+    python -m r9700_stack_b200.tuning.kbench gemm ... --reps 1 --warmup 0     # one launch (for ncu -c 1)
+
+Weights rotate over enough copies that one pass over them exceeds L2 (126 MB), so every timed launch
+streams its weights from HBM; achieved bandwidth is algorithmic bytes / event time and the fraction is
+taken against the measured copy bandwidth and bf16 GEMM rate in MEASURED_PEAKS.json at the repository
+root (falling back to 6.65 TB/s and 1.59 PFLOP/s). The reference's counterparts are its graph-timed
+sweeps (tuning/tune_dense.py, tuning/decode_moe_sweep.py).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+L2_BYTES = 126 * 2**20
+
+
+def peaks() -> dict:
+    p = os.path.join(HERE, "..", "..", "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "src": "measured"}
+    except (OSError, KeyError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+def _time(fn, reps: int, warmup: int) -> float:
+    for i in range(warmup):
+        fn(i)
+    torch.cuda.synchronize()
+    if reps <= 0:
+        return 0.0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(reps):
+        fn(i)
+    e1.record()
+    torch.cuda.synchronize()
+    from ..utils import status
+
+    status.check()
+    return e0.elapsed_time(e1) * 1e3 / reps  # us
+
+
+def bench_gemm(a) -> dict:
+    from ..ops import linear as L
+
+    torch.manual_seed(0)
+    N, K, M = a.N, a.K, a.M
+    fp4 = a.fmt == "fp4"
+    per = N * K * (2 if a.fmt == "bf16" else (0.5 if fp4 else 1.0)) * (2 if a.swiglu else 1)
+    nw = max(1, min(a.max_copies, int(2 * L2_BYTES // per) + 1))
+
+    def mk():
+        w = torch.randn(N, K, device="cuda") * 0.02
+        if a.fmt == "bf16":
+            return L.BF16Weight(w.bfloat16())
+        return L.mx_from_float(w, fp4=fp4, search=False, tiled=a.tiled)
+
+    ws = [(mk(), mk()) if a.swiglu else mk() for _ in range(nw)]
+    xb = torch.randn(M, K, device="cuda").bfloat16()
+    if a.fmt == "bf16":
+        out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+        if a.swiglu:
+            f = lambda i: L.bf16_swiglu(xb, ws[i % nw][0], ws[i % nw][1], out=out)
+        else:
+            f = lambda i: L.bf16_linear(xb, ws[i % nw], out=out)
+    else:
+        x = L.quant_act(xb)
+        if a.swiglu:
+            o = L.alloc_act(M, N, "cuda")
+            f = lambda i: L.mx_swiglu(x, ws[i % nw][0], ws[i % nw][1], out=o)
+        else:
+            out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
+            f = lambda i: L.mx_linear(x, ws[i % nw], out=out)
+    us = _time(f, a.reps, a.warmup)
+    wbytes = per + (N * K // 32) * (0 if a.fmt == "bf16" else 1) * (2 if a.swiglu else 1)
+    flops = 2.0 * M * N * K * (2 if a.swiglu else 1)
+    return {"kernel": "gemm", "fmt": a.fmt, "swiglu": a.swiglu, "N": N, "K": K, "M": M, "copies": nw,
+            "us": us, "weight_bytes": wbytes, "flops": flops}
+
+
+def bench_moe(a) -> dict:
+    from .. import _native
+    from ..ops import linear as L
+    from ..utils import status
+
+    torch.manual_seed(0)
+    T, E, k, H, I = a.T, a.E, a.topk, a.H, a.I
+    ops = _native.ops()
+    G = L.stack_experts([L.mx_from_float(torch.randn(I, H, device="cuda") * 0.02, search=False) for _ in range(E)])
+    U = L.stack_experts([L.mx_from_float(torch.randn(I, H, device="cuda") * 0.02, search=False) for _ in range(E)])
+    D = L.stack_experts([L.mx_from_float(torch.randn(H, I, device="cuda") * 0.02, search=False) for _ in range(E)])
+    x = L.quant_act(torch.randn(T, H, device="cuda").bfloat16())
+    logits = torch.randn(T, E, device="cuda")
+    A = T * k
+    BN = 16 if T <= 16 else 128
+    max_rows = A + 128 * min(E, A)
+    ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
+    wts = torch.empty(T, k, device="cuda")
+    perm = torch.empty(A, dtype=torch.int32, device="cuda")
+    seg = torch.empty(E, dtype=torch.int32, device="cuda")
+    work = torch.zeros(A + E, 3, dtype=torch.int32, device="cuda")
+    wc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    sa = L.alloc_act(max_rows, H, "cuda")
+    h = L.alloc_act(max_rows, I, "cuda")
+    y = torch.empty(max_rows, H, dtype=torch.bfloat16, device="cuda")
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    st = status.status()
+
+    def f(i):
+        ops.moe_route(logits, k, 0, None, 1, 1, 1.0, True, ids, wts)
+        ops.moe_align(ids, 0, E, BN, perm, seg, work, wc)
+        ops.moe_gather(x.q, x.sf, k, perm, sa.q, sa.sf)
+        ops.gemm_mx_grouped(G.q, G.sf, U.q, U.sf, True, sa.q, sa.sf, work, wc, I, E, BN, h.q, h.sf, st)
+        ops.gemm_mx_grouped(D.q, D.sf, None, None, True, h.q, h.sf, work, wc, H, E, BN, y, None, st)
+        ops.moe_combine(y, perm, wts, k, None, None, out)
+
+    us = _time(f, a.reps, a.warmup)
+    active = int((torch.bincount(ids.flatten().long(), minlength=E) > 0).sum()) if a.reps else E
+    wbytes = active * 3 * I * H * (0.5 + 1 / 32)
+    return {"kernel": "moe_layer", "T": T, "E": E, "topk": k, "H": H, "I": I, "active_experts": active,
+            "us": us, "weight_bytes": wbytes, "flops": 2.0 * A * 3 * I * H}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("--N", type=int, default=5120)
+    g.add_argument("--K", type=int, default=17408)
+    g.add_argument("--M", type=int, default=16)
+    g.add_argument("--fmt", choices=["fp4", "fp8", "bf16"], default="fp4")
+    g.add_argument("--swiglu", action="store_true")
+    g.add_argument("--tiled", type=int, default=1)
+    g.add_argument("--max-copies", type=int, default=16)
+    m = sub.add_parser("moe")
+    m.add_argument("--T", type=int, default=16)
+    m.add_argument("--E", type=int, default=288)
+    m.add_argument("--topk", type=int, default=10)
+    m.add_argument("--H", type=int, default=2048)
+    m.add_argument("--I", type=int, default=512)
+    for p in (g, m):
+        p.add_argument("--reps", type=int, default=50)
+        p.add_argument("--warmup", type=int, default=5)
+    a = ap.parse_args(argv)
+    r = bench_gemm(a) if a.cmd == "gemm" else bench_moe(a)
+    pk = peaks()
+    if r["us"] > 0:
+        r["gbs"] = r["weight_bytes"] / r["us"] / 1e3
+        r["tflops"] = r["flops"] / r["us"] / 1e6
+        r["frac_hbm"] = round(r["gbs"] / pk["hbm_gbs"], 3)
+        r["frac_bf16"] = round(r["tflops"] / pk["bf16_tflops"], 4)
+        r["peaks"] = pk["src"]
+    print(json.dumps(r))
+    return r
+
+
+if __name__ == "__main__":
+    main()
