@@ -29,6 +29,7 @@ sys.path.insert(0, HERE)
 
 METRIC = "decode tok/s (1 and 16 streams), prefill tok/s @8k prompt, device-timed max/rank"
 BASELINE_DECODE16 = 640.0  # reference: 27B NVFP4 TP2, 16 streams (README.md:69)
+BASELINE_FLASHNEXT16 = 913.0  # reference: Flash-Next MTP-3 TP4, 16 streams (README.md:70)
 REF_UNAVAILABLE = (
     "reference is a ROCm/gfx1201 vLLM plugin: its platform detect() returns None on a CUDA host and its "
     "libr9k.so kernels need hipcc for gfx1201 (absent); it has no CUDA path to run on B200"
@@ -44,29 +45,44 @@ def parse():
     ap.add_argument("--streams", type=int, default=16)
     ap.add_argument("--prompt-len", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the metric)")
+    ap.add_argument("--model", default="dense27b", choices=["dense27b", "flashnext"],
+                    help="dense27b: BASELINE config 2 (headline); flashnext: config 3 (hybrid MoE)")
     ap.add_argument("--no-prefill-metric", action="store_true")
     return ap.parse_args()
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms; only samples whose timestamp falls
+    inside the marked timed region are kept (the nearest one if the region is shorter than a period)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self):
+    def __init__(self, gpu_index="0"):
         self.proc = None
+        self.gpu = gpu_index
         self.path = os.path.join(HERE, "gpurun_out", "clocks.csv")
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                                          "-lms", "200"], stdout=self.fh, stderr=subprocess.DEVNULL)
+                                          "-i", str(self.gpu), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
+            deadline = time.time() + 10
+            while time.time() < deadline and os.path.getsize(self.path) == 0:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
+
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
 
     def stop(self) -> dict:
         if self.proc is None:
@@ -77,28 +93,44 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
         self.fh.close()
-        sm, mx, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        from datetime import datetime
+
+        samples = []
         for line in open(self.path):
             p = [x.strip() for x in line.split(",")]
-            if len(p) < 9:
+            if len(p) < 10:
                 continue
             try:
-                clk, cmax, pw = float(p[1]), float(p[2]), float(p[3])
+                ts = datetime.strptime(p[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                clk, cmax = float(p[2]), float(p[3])
             except ValueError:
                 continue
-            mx.append(cmax)
-            if pw > 300:  # under load
-                sm.append(clk)
-                for n, v in zip(names, p[5:9]):
-                    if v.lower() == "active":
-                        reasons.add(n)
+            samples.append((ts, clk, cmax, [n for n, v in zip(self.NAMES, p[6:10]) if v.lower() == "active"]))
+        if not samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        t0, t1 = self.t0 or samples[0][0], self.t1 or samples[-1][0]
+        inside = [x for x in samples if t0 <= x[0] <= t1]
+        if not inside:
+            mid = 0.5 * (t0 + t1)
+            inside = [min(samples, key=lambda x: abs(x[0] - mid))]
+        reasons = sorted({r for x in inside for r in x[3]})
         return {
-            "sm_mhz": statistics.median(sm) if sm else None,
-            "sm_max_mhz": max(mx) if mx else None,
-            "reasons": sorted(reasons),
-            "samples_under_load": len(sm),
+            "sm_mhz": statistics.median(x[1] for x in inside),
+            "sm_max_mhz": max(x[2] for x in inside),
+            "reasons": reasons,
+            "samples": len(inside),
         }
+
+
+def _smi_id(dev) -> str:
+    """nvidia-smi's name for this process's GPU: its UUID (robust to CUDA_VISIBLE_DEVICES)."""
+    import torch
+
+    try:
+        u = str(torch.cuda.get_device_properties(dev).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(dev.index or 0)
 
 
 def main():
@@ -113,12 +145,13 @@ def main():
     from r9700_stack_b200 import _native
     from r9700_stack_b200.engine.llm import LLM
     from r9700_stack_b200.engine.scheduler import SamplingParams
-    from r9700_stack_b200.models.config import EngineConfig, ParallelConfig, qwen27b_hybrid
+    from r9700_stack_b200.models.config import EngineConfig, ParallelConfig, flashnext_moe, qwen27b_hybrid
     from r9700_stack_b200.parallel.comm import NcclComm, init_distributed
 
     rank, world, local = init_distributed()
     dev = torch.device("cuda", local)
-    cfg = qwen27b_hybrid()
+    cfg = qwen27b_hybrid() if args.model == "dense27b" else flashnext_moe()
+    base16 = BASELINE_DECODE16 if args.model == "dense27b" else BASELINE_FLASHNEXT16
     if args.layers:
         cfg = cfg.scaled(layers=args.layers)
     S, P = args.streams, args.prompt_len
@@ -171,18 +204,22 @@ def main():
     lc = _native.launch_counter
     barrier_sync()
 
-    clocks = ClockSampler() if rank == 0 else None
+    clocks = ClockSampler(_smi_id(dev)) if rank == 0 else None
     if clocks:
         clocks.start()
     # device-timed: CUDA events around each step's graph replay
     llm.runner.device_events = []
     barrier_sync()
     w0, w1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if clocks:
+        clocks.mark_start()
     w0.record()
     for _ in range(args.steps):
         llm.step()
     w1.record()
     barrier_sync()
+    if clocks:
+        clocks.mark_end()
     dev_ms = sum(a.elapsed_time(b) for a, b in llm.runner.device_events)
     e2e_ms = w0.elapsed_time(w1)
     llm.runner.device_events = None
@@ -235,11 +272,16 @@ def main():
             "ms_per_step": round(dev_ms / args.steps, 4),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(decode16 / BASELINE_DECODE16, 3),
-            "dtype": "nvfp4->mxfp4 weights x mxfp8 activations (fp32 accumulate), fp8 KV; reference: mxfp4 x fp8",
+            "vs_baseline": round(decode16 / base16, 3),
+            "dtype": ("nvfp4->mxfp4 weights x mxfp8 activations (fp32 accumulate), fp8 KV; reference: mxfp4 x fp8"
+                      if args.model == "dense27b" else
+                      "experts nvfp4->mxfp4 x mxfp8, attention/GDN/router/shared expert bf16 (fp32 accumulate), fp8 KV"),
             "data": "synthetic: random-init N(0,0.02) weights of the named architecture, uniform random prompt ids",
             "config": {
-                "model": "hybrid-dense-27b (BASELINE config 2: 64 layers 3:1 GDN:GQA, hidden 5120, ffn 17408, vocab 248320)",
+                "model": ("hybrid-dense-27b (BASELINE config 2: 64 layers 3:1 GDN:GQA, hidden 5120, ffn 17408, vocab 248320)"
+                          if args.model == "dense27b" else
+                          "hybrid-moe-flashnext (BASELINE config 3: 48 layers 3:1 GDN:GQA, hidden 2048, 288 experts "
+                          "top-10 (I=512) + shared expert, vocab 248320; experts NVFP4, rest bf16)"),
                 "global_batch": S,
                 "seq_len": P,
                 "parallelism": f"tp{world}",

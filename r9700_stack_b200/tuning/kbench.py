@@ -4,6 +4,8 @@
     python -m r9700_stack_b200.tuning.kbench gemm --N 17408 --K 5120 --M 16 --fmt fp4 --swiglu
     python -m r9700_stack_b200.tuning.kbench moe --T 16 --E 288 --topk 10 --H 2048 --I 512
     python -m r9700_stack_b200.tuning.kbench gemm ... --reps 1 --warmup 0     # one launch (for ncu -c 1)
+    python -m r9700_stack_b200.tuning.kbench decode --model dense27b --streams 16 --steps 2
+        # eager decode steps of a whole model inside NVTX ranges "decode_step" (ncu --nvtx-include)
 
 Weights rotate over enough copies that one pass over them exceeds L2 (126 MB), so every timed launch
 streams its weights from HBM; achieved bandwidth is algorithmic bytes / event time and the fraction is
@@ -132,6 +134,45 @@ def bench_moe(a) -> dict:
             "us": us, "weight_bytes": wbytes, "flops": 2.0 * A * 3 * I * H}
 
 
+def bench_decode(a) -> dict:
+    """Eager (graph-free) decode steps of a full model, each inside an NVTX range, so a launch list
+    taken with ``ncu --nvtx --nvtx-include decode_step/`` covers exactly the decode kernels."""
+    import numpy as np
+
+    from ..engine.llm import LLM
+    from ..engine.runner import pack_step
+    from ..engine.scheduler import SamplingParams, ScheduledChunk, SchedulerOutput
+    from ..models.config import EngineConfig, flashnext_moe, qwen27b_hybrid
+
+    cfg = qwen27b_hybrid() if a.model == "dense27b" else flashnext_moe()
+    if a.layers:
+        cfg = cfg.scaled(layers=a.layers)
+    ec = EngineConfig(max_batch=a.streams, max_model_len=a.prompt + 64, max_prefill_tokens=max(a.prompt, 256),
+                      cuda_graphs=False)
+    llm = LLM(cfg, ec, seed=0)
+    rng = np.random.default_rng(0)
+    seqs = [llm.add_request(rng.integers(0, cfg.vocab, a.prompt).tolist(), SamplingParams(max_tokens=32))
+            for _ in range(a.streams)]
+    while any(not s.prefill_done or not s.output for s in seqs):
+        llm.step()
+    for s in seqs:
+        assert llm.scheduler.ensure(s, s.length + 1)
+    out = SchedulerOutput("decode", [ScheduledChunk(s, s.length - 1, 1, True) for s in seqs])
+    lay, arr = pack_step(out, ec.kv_block)
+    llm.runner._upload(arr)
+    meta = llm.runner.meta.views(lay)
+    ws = llm.runner.ws
+
+    def f(i):
+        torch.cuda.nvtx.range_push("decode_step")
+        llm.model.forward(meta, ws, lay.T, lay.R)
+        torch.cuda.nvtx.range_pop()
+
+    us = _time(f, a.reps, a.warmup)
+    return {"kernel": "decode_step_eager", "model": cfg.name, "streams": a.streams, "layers": cfg.layers,
+            "us": us, "weight_bytes": llm.model.weight_bytes(), "flops": 0.0}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -149,11 +190,16 @@ def main(argv=None):
     m.add_argument("--topk", type=int, default=10)
     m.add_argument("--H", type=int, default=2048)
     m.add_argument("--I", type=int, default=512)
-    for p in (g, m):
+    d = sub.add_parser("decode")
+    d.add_argument("--model", choices=["dense27b", "flashnext"], default="dense27b")
+    d.add_argument("--streams", type=int, default=16)
+    d.add_argument("--prompt", type=int, default=256)
+    d.add_argument("--layers", type=int, default=0)
+    for p in (g, m, d):
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = bench_gemm(a) if a.cmd == "gemm" else bench_moe(a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:
         r["gbs"] = r["weight_bytes"] / r["us"] / 1e3
