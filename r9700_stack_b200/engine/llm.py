@@ -59,7 +59,8 @@ class LLM:
         if out.kind == "idle":
             return []
         if out.kind == "decode" and self.drafter is not None:
-            drafts = self.drafter.drafts([c.seq for c in out.chunks])
+            # speculative verification is greedy; requests that sample with temperature get no drafts
+            drafts = self.drafter.drafts([c.seq for c in out.chunks if c.seq.params.temperature <= 0])
             toks, accepted = self.runner.execute_spec(out, drafts)
             st = self.spec_stats
             st["steps"] += 1
@@ -76,6 +77,11 @@ class LLM:
             for s in done:
                 self.drafter.release(s)
         return done
+
+    def abort(self, seq: Sequence) -> None:
+        self.scheduler.abort(seq)
+        if self.drafter is not None:
+            self.drafter.release(seq)
 
     def has_unfinished(self) -> bool:
         return self.scheduler.has_work

@@ -239,13 +239,27 @@ class ModelRunner:
         toks = self.sample_host[:R].tolist()
         res: dict[int, list[int]] = {}
         r = 0
+        hot = []  # (logits row, params, generated so far) of rows that sample with temperature
         for ch in out.chunks:
             if not ch.sample:
                 continue
             nd = len(draft[ch.seq.seq_id]) if draft is not None and ch.seq.seq_id in draft else 0
             res[ch.seq.seq_id] = toks[r : r + 1 + nd]
+            if ch.seq.params.temperature > 0 and nd == 0:
+                hot.append((r, ch.seq))
             r += 1 + nd
+        if hot:
+            self._resample(hot, res)
         return res
+
+    def _resample(self, hot, res) -> None:
+        from .sampler import sample_rows
+
+        rows = torch.tensor([r for r, _ in hot], device=self.device)
+        new = sample_rows(self.ws.logits.index_select(0, rows), [s.params for _, s in hot],
+                          [len(s.output) for _, s in hot])
+        for (_, s), t in zip(hot, new):
+            res[s.seq_id] = [t]
 
 
     def execute_spec(self, out: SchedulerOutput, draft: dict[int, list[int]]):
@@ -278,6 +292,7 @@ class ModelRunner:
         self.d2h_bytes = R * 8
         y = self.sample_host[:R].tolist()
         res, accepted = {}, {}
+        hot = []
         t = 0
         for ch in out.chunks:
             d = draft.get(ch.seq.seq_id, [])
@@ -286,7 +301,11 @@ class ModelRunner:
                 j += 1
             res[ch.seq.seq_id] = y[t: t + j + 1]
             accepted[ch.seq.seq_id] = j + 1
+            if ch.seq.params.temperature > 0 and not d:
+                hot.append((t, ch.seq))
             t += 1 + len(d)
+        if hot:
+            self._resample(hot, res)
         return res, accepted
 
 

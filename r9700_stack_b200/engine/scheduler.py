@@ -119,6 +119,18 @@ class Scheduler:
             self.slots.free_one(seq.state_slot)
             seq.state_slot = -1
 
+    def abort(self, seq: Sequence) -> None:
+        """Drop a request wherever it is (waiting or running) and free its blocks and state slot."""
+        if seq.finished:
+            return
+        if seq in self.waiting:
+            self.waiting.remove(seq)
+        if seq in self.running:
+            self.running.remove(seq)
+        self._release(seq)
+        seq.finished = True
+        self.finished.append(seq)
+
     def preempt(self, seq: Sequence) -> None:
         self._release(seq)
         seq.num_computed = 0

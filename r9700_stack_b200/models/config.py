@@ -144,6 +144,22 @@ def tiny_hybrid(**kw) -> HybridConfig:
     return HybridConfig(**base)
 
 
+MODELS = {
+    "dense27b": qwen27b_hybrid,
+    "flashnext": flashnext_moe,
+    "tiny-hybrid": tiny_hybrid,
+    "tiny-moe": tiny_moe,
+}
+
+
+def model_config(name: str) -> HybridConfig:
+    """A named model preset (the synthetic configs of the BASELINE classes, and their tiny variants)."""
+    try:
+        return MODELS[name]()
+    except KeyError:
+        raise ValueError(f"unknown model {name!r}; known: {sorted(MODELS)}") from None
+
+
 @dataclass
 class ParallelConfig:
     tp_size: int = 1

@@ -188,11 +188,15 @@ def test_decode_graph_replay_equals_eager():
     assert outs[0] == outs[1]
 
 
+@pytest.mark.parametrize("heads", [(12, 2), (3, 1), (2, 1)])
 @pytest.mark.parametrize("case", ["decode", "verify", "prefill"])
-def test_attn_tc_matches_simple_kernel(case):
-    """tcgen05 flash attention (split-KV decode / prefill tiles) vs the CUDA-core kernel above."""
+def test_attn_tc_matches_simple_kernel(case, heads):
+    """tcgen05 flash attention (split-KV decode / prefill tiles) vs the CUDA-core kernel above; the
+    head counts cover TP1 (24/4 -> 12/2 per rank at TP2), TP8 (3 q heads on a replicated kv head) and
+    the Flash-Next TP8 split (16/2 -> 2/1)."""
     torch.manual_seed(4)
-    D, Hq, Hkv, BLK = 256, 12, 2, 64
+    D, BLK = 256, 64
+    Hq, Hkv = heads
     G = Hq // Hkv
     if case == "decode":
         ctxs, nq = [1, 63, 200, 1000, 2049], [1, 1, 1, 1, 1]
