@@ -95,6 +95,17 @@ void gdn_spec_commit(torch::Tensor table, int64_t Hk, int64_t Hv, int64_t dv, in
                      torch::Tensor seq_has_state);
 void spec_accept(torch::Tensor input_ids, torch::Tensor target, torch::Tensor seq_start, torch::Tensor seq_len,
                  torch::Tensor acc_len);
+void mhc_seam(torch::Tensor R, c10::optional<torch::Tensor> so, c10::optional<torch::Tensor> post_in,
+              c10::optional<torch::Tensor> comb_in, torch::Tensor fn, torch::Tensor scale, torch::Tensor base,
+              double rms_eps, double pre_eps, double sk_eps, double post_mult, int64_t sk_repeat, torch::Tensor R_out,
+              torch::Tensor post_out, torch::Tensor comb_out, torch::Tensor li, torch::Tensor part);
+void exl3_dequant(torch::Tensor trellis, torch::Tensor suh, torch::Tensor svh, int64_t K, int64_t cb, torch::Tensor out);
+void exl3_gemv(torch::Tensor trellis, torch::Tensor suh, int64_t K, int64_t cb, torch::Tensor x, int64_t M,
+               c10::optional<torch::Tensor> work, c10::optional<torch::Tensor> work_count, int64_t nz, int64_t ksplit,
+               torch::Tensor part);
+void exl3_finish(torch::Tensor part, c10::optional<torch::Tensor> part_up, torch::Tensor svh,
+                 c10::optional<torch::Tensor> svh_up, int64_t ksplit, int64_t nz, int64_t M, int64_t n_out,
+                 c10::optional<torch::Tensor> work, c10::optional<torch::Tensor> work_count, torch::Tensor out);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -169,6 +180,14 @@ TORCH_LIBRARY(r9k, m) {
   m.def("gdn_spec_commit(Tensor table, int Hk, int Hv, int dv, int C, int W, int ld, bool state_f32, "
         "Tensor seq_slot, Tensor seq_start, Tensor acc_len, Tensor seq_has_state) -> ()");
   m.def("spec_accept(Tensor input_ids, Tensor target, Tensor seq_start, Tensor seq_len, Tensor(a!) acc_len) -> ()");
+  m.def("mhc_seam(Tensor R, Tensor? so, Tensor? post_in, Tensor? comb_in, Tensor fn, Tensor scale, Tensor base, "
+        "float rms_eps, float pre_eps, float sk_eps, float post_mult, int sk_repeat, Tensor(a!) R_out, "
+        "Tensor(b!) post_out, Tensor(c!) comb_out, Tensor(d!) li, Tensor(e!) part) -> ()");
+  m.def("exl3_dequant(Tensor trellis, Tensor suh, Tensor svh, int K, int cb, Tensor(a!) out) -> ()");
+  m.def("exl3_gemv(Tensor trellis, Tensor suh, int K, int cb, Tensor x, int M, Tensor? work, Tensor? work_count, "
+        "int nz, int ksplit, Tensor(a!) part) -> ()");
+  m.def("exl3_finish(Tensor part, Tensor? part_up, Tensor svh, Tensor? svh_up, int ksplit, int nz, int M, int n_out, "
+        "Tensor? work, Tensor? work_count, Tensor(a!) out) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -208,6 +227,10 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
   m.impl("gdn_spec_commit", &r9k::gdn_spec_commit);
   m.impl("spec_accept", &r9k::spec_accept);
+  m.impl("mhc_seam", &r9k::mhc_seam);
+  m.impl("exl3_dequant", &r9k::exl3_dequant);
+  m.impl("exl3_gemv", &r9k::exl3_gemv);
+  m.impl("exl3_finish", &r9k::exl3_finish);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);
