@@ -106,6 +106,17 @@ void exl3_gemv(torch::Tensor trellis, torch::Tensor suh, int64_t K, int64_t cb, 
 void exl3_finish(torch::Tensor part, c10::optional<torch::Tensor> part_up, torch::Tensor svh,
                  c10::optional<torch::Tensor> svh_up, int64_t ksplit, int64_t nz, int64_t M, int64_t n_out,
                  c10::optional<torch::Tensor> work, c10::optional<torch::Tensor> work_count, torch::Tensor out);
+void mla_cache_write(torch::Tensor kv, torch::Tensor kv_w, c10::optional<torch::Tensor> ik,
+                     c10::optional<torch::Tensor> ik_w, double eps, torch::Tensor positions, torch::Tensor cos_sin,
+                     torch::Tensor slots, torch::Tensor lat_cache, c10::optional<torch::Tensor> idx_cache);
+void rope_heads(torch::Tensor x, int64_t H, int64_t off, torch::Tensor positions, torch::Tensor cos_sin);
+void indexer_score(torch::Tensor q, torch::Tensor w, torch::Tensor idx_cache, torch::Tensor block_table,
+                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores);
+void topk_select(torch::Tensor scores, torch::Tensor tok_ctx, int64_t k, torch::Tensor out, torch::Tensor count);
+void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
+                       torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
+                       torch::Tensor part_ml, torch::Tensor out);
+void head_gemv(torch::Tensor x, torch::Tensor W, torch::Tensor out);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -188,6 +199,15 @@ TORCH_LIBRARY(r9k, m) {
         "int nz, int ksplit, Tensor(a!) part) -> ()");
   m.def("exl3_finish(Tensor part, Tensor? part_up, Tensor svh, Tensor? svh_up, int ksplit, int nz, int M, int n_out, "
         "Tensor? work, Tensor? work_count, Tensor(a!) out) -> ()");
+  m.def("mla_cache_write(Tensor kv, Tensor kv_w, Tensor? ik, Tensor? ik_w, float eps, Tensor positions, "
+        "Tensor cos_sin, Tensor slots, Tensor(a!) lat_cache, Tensor(b!)? idx_cache) -> ()");
+  m.def("rope_heads(Tensor(a!) x, int H, int off, Tensor positions, Tensor cos_sin) -> ()");
+  m.def("indexer_score(Tensor q, Tensor w, Tensor idx_cache, Tensor block_table, Tensor tok_seq, Tensor tok_ctx, "
+        "int max_ctx, Tensor(a!) scores) -> ()");
+  m.def("topk_select(Tensor scores, Tensor tok_ctx, int k, Tensor(a!) out, Tensor(b!) count) -> ()");
+  m.def("sparse_mla_decode(Tensor q, Tensor lat_cache, Tensor block_table, Tensor tok_seq, Tensor sel, "
+        "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out) -> ()");
+  m.def("head_gemv(Tensor x, Tensor W, Tensor(a!) out) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -231,6 +251,12 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("exl3_dequant", &r9k::exl3_dequant);
   m.impl("exl3_gemv", &r9k::exl3_gemv);
   m.impl("exl3_finish", &r9k::exl3_finish);
+  m.impl("mla_cache_write", &r9k::mla_cache_write);
+  m.impl("rope_heads", &r9k::rope_heads);
+  m.impl("indexer_score", &r9k::indexer_score);
+  m.impl("topk_select", &r9k::topk_select);
+  m.impl("sparse_mla_decode", &r9k::sparse_mla_decode);
+  m.impl("head_gemv", &r9k::head_gemv);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);

@@ -181,6 +181,42 @@ template <> struct StateVec<__nv_bfloat16> {
   }
 };
 
+template <typename ST> struct StateVec16;
+template <> struct StateVec16<float> {
+  R9K_DEVINL static void load(const float* p, float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(p)[i];
+      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+  }
+  R9K_DEVINL static void store(float* p, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) reinterpret_cast<float4*>(p)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+};
+template <> struct StateVec16<__nv_bfloat16> {
+  R9K_DEVINL static void load(const __nv_bfloat16* p, float* v) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      const uint4 raw = reinterpret_cast<const uint4*>(p)[i];
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[8 * i + k] = __bfloat162float(e[k]);
+    }
+  }
+  R9K_DEVINL static void store(__nv_bfloat16* p, const float* v) {
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+      uint4 raw;
+      __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) e[k] = __float2bfloat16(v[8 * i + k]);
+      reinterpret_cast<uint4*>(p)[i] = raw;
+    }
+  }
+};
+
 template <typename ST, int DK>
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
@@ -400,127 +436,154 @@ namespace r9k {
 // 512 threads: recurrence thread (c = tid / 4, rg = tid % 4) owns 32 contiguous dk rows of column c.
 // ------------------------------------------------------------------------------------------------
 template <typename ST>
-__global__ void __launch_bounds__(512) gdn_decode_fused_kernel(
+__global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
     const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int z_off, int b_off, int a_off,
     const __nv_bfloat16* __restrict__ conv_w, ST* __restrict__ conv_state, ST* __restrict__ state,
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_has_state, const float* __restrict__ A_log,
     const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ norm_w, float eps,
     uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf, __nv_bfloat16* __restrict__ out_bf16) {
-  pdl_wait();
-  pdl_trigger();  // dependents may launch and prefetch while this grid runs
-  constexpr int D = 128, W = 4;
-  constexpr int MAXREP = 8;
-  __shared__ float sq[D], sk[D], sv[MAXREP][D], so[D], sred[32];
-  __shared__ float sg[MAXREP], sb[MAXREP];
-  const int t = blockIdx.x;  // token == sequence
-  const int kh = blockIdx.y;
+  // grid (sequence, key head, value head within the key head's group); the rep CTAs of one key head
+  // form a cluster: all of them read the q/k conv state, and only after a cluster barrier does rank 0
+  // store its update (each CTA owns its value head's conv channels outright).
+  // The head's state (128 x 128) streams into shared memory with asynchronous copies issued before
+  // anything else, so four CTAs per SM keep 4 x 32 KB (bf16) of state reads in flight; thread
+  // (column c = tid / 2, half rg = tid % 2) then owns 64 entries and walks them in 16-entry pieces.
+  constexpr int D = 128, W = 4, PER = 64, PC = 16;
+  __shared__ float sq[D], sk[D], sv[D], so[D], sred[8];
+  __shared__ float snew[3 * D][W - 1];
+  __shared__ float sg, sb;
+  extern __shared__ __align__(16) uint8_t s_state[];
+  const int t = blockIdx.x, kh = blockIdx.y, j = blockIdx.z;
   const int rep = Hv / Hk;
+  const int h = kh * rep + j;
   const int tid = threadIdx.x;
-  const int slot = seq_slot[t];
-  const bool hs = seq_has_state[t] != 0;
   const int C = 2 * Hk * D + Hv * D;
-  // ---- conv over this CTA's channels: q (128) | k (128) | v heads kh*rep .. (rep x 128)
-  const int nch = (2 + rep) * D;
-  for (int i = tid; i < nch; i += blockDim.x) {
-    int c;
-    if (i < D) c = kh * D + i;
-    else if (i < 2 * D) c = Hk * D + kh * D + (i - D);
-    else c = 2 * Hk * D + kh * rep * D + (i - 2 * D);
-    ST* cs = conv_state + ((int64_t)slot * C + c) * (W - 1);
+  const int slot = seq_slot[t];  // step metadata: copied in before the forward began
+  const bool hs = seq_has_state[t] != 0;
+  const int c = tid >> 1, rg = tid & 1;
+  ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * PER;
+  ST* myS = reinterpret_cast<ST*>(s_state) + tid * PER;
+  if (hs) {
+    constexpr int NV = PER * sizeof(ST) / 16;
+#pragma unroll
+    for (int v = 0; v < NV; ++v)
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(myS) + 16 * v),
+                   "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  pdl_wait();
+  pdl_trigger();
+  // ---- conv over q (128) | k (128) | this value head (128) channels
+  for (int ch = tid; ch < 3 * D; ch += 256) {
+    const int part = ch / D, i = ch % D;
+    const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + h * D + i;
+    const ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
     float x[W];
 #pragma unroll
     for (int w = 0; w < W - 1; ++w) x[w] = hs ? to_f<ST>(cs[w]) : 0.f;
-    x[W - 1] = __bfloat162float(proj[(int64_t)t * ld + c]);
+    x[W - 1] = __bfloat162float(proj[(int64_t)t * ld + cch]);
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < W; ++w) acc += x[w] * __bfloat162float(conv_w[(int64_t)c * W + w]);
+    for (int w = 0; w < W; ++w) acc += x[w] * __bfloat162float(conv_w[(int64_t)cch * W + w]);
 #pragma unroll
-    for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(x[w + 1]);
+    for (int w = 0; w < W - 1; ++w) snew[ch][w] = x[w + 1];
     const float y = silu_f(acc);
-    if (i < D) sq[i] = y;
-    else if (i < 2 * D) sk[i - D] = y;
-    else sv[(i - 2 * D) / D][(i - 2 * D) % D] = y;
+    if (part == 0) sq[i] = y;
+    else if (part == 1) sk[i] = y;
+    else sv[i] = y;
   }
-  if (tid < rep) {
-    const int h = kh * rep + tid;
+  if (tid == 0) {
     const float av = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
     const float bv = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
-    sg[tid] = __expf(-__expf(A_log[h]) * softplus_f(av + dt_bias[h]));  // decay factor exp(g)
-    sb[tid] = sigmoid_f(bv);
+    sg = __expf(-__expf(A_log[h]) * softplus_f(av + dt_bias[h]));  // decay factor exp(g)
+    sb = sigmoid_f(bv);
   }
-  __syncthreads();
+  // every CTA of the cluster has read the shared q/k conv state before rank 0 overwrites it
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+  for (int ch = tid; ch < 3 * D; ch += 256) {
+    const int part = ch / D, i = ch % D;
+    if (part == 2 || j == 0) {
+      const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + h * D + i;
+      ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
+#pragma unroll
+      for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(snew[ch][w]);
+    }
+  }
   // ---- l2 norms of q and k (warps 0 and 1)
   if (tid < 64) {
     const float* src = tid < 32 ? sq : sk;
     const int l = tid & 31;
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) ss += src[l + 32 * j] * src[l + 32 * j];
+    for (int jj = 0; jj < 4; ++jj) ss += src[l + 32 * jj] * src[l + 32 * jj];
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (l == 0) sred[tid >> 5] = rsqrtf(ss + 1e-6f);
   }
+  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   const float qs = sred[0] * rsqrtf((float)D), ks = sred[1];
-  const int c = tid >> 2, rg = tid & 3;
-  float qv[32], kv_[32];
-#pragma unroll
-  for (int r = 0; r < 32; ++r) {
-    qv[r] = sq[rg * 32 + r] * qs;
-    kv_[r] = sk[rg * 32 + r] * ks;
-  }
-  for (int j = 0; j < rep; ++j) {
-    const int h = kh * rep + j;
-    ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * 32;
-    float S[32];
-    if (hs) StateVec<ST>::load(Sp, S);
+  const float decay = sg;
+  const float* kk = sk + rg * PER;
+  const float* qq = sq + rg * PER;
+  float kvs = 0.f;
+#pragma unroll 1
+  for (int p = 0; p < PER / PC; ++p) {
+    float S[PC];
+    if (hs) StateVec16<ST>::load(myS + p * PC, S);
     else {
 #pragma unroll
-      for (int r = 0; r < 32; ++r) S[r] = 0.f;
+      for (int r = 0; r < PC; ++r) S[r] = 0.f;
     }
-    const float decay = sg[j];
-    float kvs = 0.f;
 #pragma unroll
-    for (int r = 0; r < 32; ++r) kvs += S[r] * kv_[r];
-    kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
-    kvs += __shfl_xor_sync(0xffffffffu, kvs, 2);
-    const float delta = sb[j] * (sv[j][c] - decay * kvs);
-    float ov = 0.f;
-#pragma unroll
-    for (int r = 0; r < 32; ++r) {
-      S[r] = S[r] * decay + kv_[r] * delta;
-      ov += S[r] * qv[r];
-    }
-    ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-    ov += __shfl_xor_sync(0xffffffffu, ov, 2);
-    StateVec<ST>::store(Sp, S);
-    if (rg == 0) so[c] = ov;
-    __syncthreads();
-    // ---- RMSNormGated + MXFP8 for this head (warps 0..3, lane l owns column 32*warp + l)
-    if (tid < D) {
-      const float o = so[tid];
-      float ss = o * o;
-      for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
-      if ((tid & 31) == 0) sred[2 + (tid >> 5)] = ss;
-    }
-    __syncthreads();
-    if (tid < D) {
-      const float rr = rsqrtf((sred[2] + sred[3] + sred[4] + sred[5]) / (float)D + eps);
-      const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tid]);
-      float val = so[tid] * rr * __bfloat162float(norm_w[tid]) * silu_f(z);
-      val = __bfloat162float(__float2bfloat16(val));
-      const int64_t oi = (int64_t)t * Hv * D + h * D + tid;
-      if (out_bf16 != nullptr) out_bf16[oi] = __float2bfloat16(val);
-      if (out_q != nullptr) {
-        float am = fabsf(val);
-        for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
-        const int e = mx_exponent(am, 448.f);
-        out_q[oi] = f32_to_e4m3(val * exp2i(-e));
-        if ((tid & 31) == 0) out_sf[sf_offset(t, (h * D + tid) >> 5, Hv * D / 32)] = (uint8_t)(e + 127);
-      }
-    }
-    __syncthreads();
+    for (int r = 0; r < PC; ++r) kvs += S[r] * kk[p * PC + r];
   }
-  pdl_trigger();
+  kvs *= ks;
+  kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
+  const float delta = sb * (sv[c] - decay * kvs);
+  const float dk = delta * ks;
+  float ov = 0.f;
+#pragma unroll 1
+  for (int p = 0; p < PER / PC; ++p) {
+    float S[PC];
+    if (hs) StateVec16<ST>::load(myS + p * PC, S);
+    else {
+#pragma unroll
+      for (int r = 0; r < PC; ++r) S[r] = 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < PC; ++r) {
+      S[r] = S[r] * decay + kk[p * PC + r] * dk;
+      ov += S[r] * qq[p * PC + r];
+    }
+    StateVec16<ST>::store(Sp + p * PC, S);
+  }
+  ov *= qs;
+  ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+  if (rg == 0) so[c] = ov;
+  __syncthreads();
+  // ---- RMSNormGated + MXFP8 of this head (warps 0..3, lane l owns column 32 * warp + l)
+  if (tid < D) {
+    const float o = so[tid];
+    float ss = o * o;
+    for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
+    if ((tid & 31) == 0) sred[2 + (tid >> 5)] = ss;
+  }
+  __syncthreads();
+  if (tid < D) {
+    const float rr = rsqrtf((sred[2] + sred[3] + sred[4] + sred[5]) / (float)D + eps);
+    const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tid]);
+    float val = so[tid] * rr * __bfloat162float(norm_w[tid]) * silu_f(z);
+    val = __bfloat162float(__float2bfloat16(val));
+    const int64_t oi = (int64_t)t * Hv * D + h * D + tid;
+    if (out_bf16 != nullptr) out_bf16[oi] = __float2bfloat16(val);
+    if (out_q != nullptr) {
+      float am = fabsf(val);
+      for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
+      const int e = mx_exponent(am, 448.f);
+      out_q[oi] = f32_to_e4m3(val * exp2i(-e));
+      if ((tid & 31) == 0) out_sf[sf_offset(t, (h * D + tid) >> 5, Hv * D / 32)] = (uint8_t)(e + 127);
+    }
+  }
 }
 
 void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,
@@ -534,20 +597,36 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   TORCH_CHECK(conv_w.size(1) == 4 && Hv % Hk == 0 && Hv / Hk <= 8, "gdn_decode_fused: conv width 4, rep <= 8");
   TORCH_CHECK(state.size(2) == 128 && state.size(3) == 128, "gdn_decode_fused: head dim 128");
   const at::cuda::CUDAGuard guard(proj.device());
-  dim3 grid((unsigned)S, (unsigned)Hk);
+  const int rep = (int)(Hv / Hk);
   auto st = at::cuda::getCurrentCUDAStream();
   auto u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
     return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
   };
   __nv_bfloat16* ob = (out_bf16.has_value() && out_bf16->defined()) ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)S, (unsigned)Hk, (unsigned)rep);
+  cfg.blockDim = dim3(256);
+  cfg.dynamicSmemBytes = (size_t)128 * 128 * state.element_size();
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = (unsigned)rep;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
 #define R9K_GDF(ST_T)                                                                                                 \
-  launch_pdl(gdn_decode_fused_kernel<ST_T>, grid, dim3(512), 0, st,                                                                 \
+  cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,                     \
+                       (int)cfg.dynamicSmemBytes);                                                                    \
+  TORCH_CHECK(cudaLaunchKernelEx(&cfg, gdn_decode_fused_kernel<ST_T>,                                                 \
       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)z_off, (int)b_off, \
       (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()),                                          \
       reinterpret_cast<ST_T*>(conv_state.data_ptr()), reinterpret_cast<ST_T*>(state.data_ptr()),                      \
       seq_slot.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(),                        \
       dt_bias.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr()), (float)eps, u8(out_q),      \
-      u8(out_sf), ob)
+      u8(out_sf), ob) == cudaSuccess, "gdn_decode_fused launch")
   if (state.dtype() == torch::kFloat32) { R9K_GDF(float); } else { R9K_GDF(__nv_bfloat16); }
 #undef R9K_GDF
   C10_CUDA_KERNEL_LAUNCH_CHECK();

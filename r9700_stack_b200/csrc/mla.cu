@@ -1,0 +1,514 @@
+// Multi-head latent attention (MLA) with a lightning indexer and top-k sparse selection (GLM-5.3 /
+// DeepSeek-V3.2 class, BASELINE configs 4 and 5), decode-oriented.
+//
+// Cache per attention layer: latent rows [blocks][64][576] bf16 = [rmsnorm(c_kv) (512) | rope(k_pe) (64)],
+// and the indexer's keys [blocks][64][128] e4m3. Per query token t:
+//   indexer : score[s] = sum_h w[t, h] * relu(q_i[t, h] . k_i[s])            (s < ctx(t))
+//   top-k   : the k highest-scoring positions (all of them when ctx <= k), in position order
+//   attention over the selected rows, heads absorbed into the latent space:
+//             logit[h, s] = (q_lat[t, h] . c[s] + q_pe[t, h] . k_pe[s]) * scale,  o_lat[h] = softmax . c
+//   then o[h] = W_uv[h] o_lat[h] (head_gemv) and the output projection.
+// (reference: kernels/r9k_sparse_mla.hip:99-245 (split-K sparse MLA decode + combine),
+// r9700_vllm/attn/indexer_logits.py (paged indexer logits, Triton there), r9700_vllm/models/glm5next.py:39-77
+// (top_k_per_row).)
+//
+// Kernels: mla_cache_write (latent rmsnorm + rope + store, indexer key norm + rope + e4m3 store),
+// rope_heads (rope of a strided head slice), indexer_score, topk_select (radix select, deterministic
+// order), sparse_mla_decode (split over the selected rows, online softmax, 8 heads per CTA) +
+// mla_combine, head_gemv (per-head [K -> N] projections: q absorption with W_uk, output with W_uv).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_fp8.h>
+#include "common.cuh"
+
+namespace r9k {
+
+namespace {
+constexpr int MLA_BLK = 64, LAT = 512, PE = 64, ROW = LAT + PE, IDXD = 128;
+
+R9K_DEVINL float e4m3_to_f(uint8_t b) {
+  __nv_fp8_e4m3 v;
+  v.__x = b;
+  return float(v);
+}
+R9K_DEVINL uint8_t f_to_e4m3(float f) {
+  __nv_fp8_e4m3 v(fminf(fmaxf(f, -448.f), 448.f));
+  return v.__x;
+}
+R9K_DEVINL int64_t slot_of(const int32_t* bt, int mb, int seq, int pos) {
+  return (int64_t)bt[(int64_t)seq * mb + pos / MLA_BLK] * MLA_BLK + pos % MLA_BLK;
+}
+}  // namespace
+
+// ------------------------------------------------------------------------------------------------
+// cache write: one warp per token for the latent row, one for the indexer key
+// ------------------------------------------------------------------------------------------------
+__global__ void mla_cache_write_kernel(const __nv_bfloat16* __restrict__ kv, int64_t ldkv,
+                                       const __nv_bfloat16* __restrict__ kv_w, const __nv_bfloat16* __restrict__ ik,
+                                       int64_t ldik, const __nv_bfloat16* __restrict__ ik_w, float eps,
+                                       const int32_t* __restrict__ positions, const float* __restrict__ cos_sin,
+                                       const int32_t* __restrict__ slots, __nv_bfloat16* __restrict__ lat_cache,
+                                       uint8_t* __restrict__ idx_cache, int T) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int t = warp >> 1, which = warp & 1;
+  if (t >= T) return;
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  const int pos = positions[t];
+  if (which == 0) {
+    // latent: rmsnorm over 512 (16 per lane), then rope over the 64 pe dims (neox halves of 32)
+    const __nv_bfloat16* src = kv + (int64_t)t * ldkv;
+    float x[16];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      x[i] = __bfloat162float(src[lane + 32 * i]);
+      ss += x[i] * x[i];
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rr = rsqrtf(ss / LAT + eps);
+    __nv_bfloat16* dst = lat_cache + slot * ROW;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) dst[lane + 32 * i] = __float2bfloat16(x[i] * rr * __bfloat162float(kv_w[lane + 32 * i]));
+    const float* cs = cos_sin + (int64_t)pos * PE;
+    const float a = __bfloat162float(src[LAT + lane]), b = __bfloat162float(src[LAT + 32 + lane]);
+    const float c = cs[lane], s = cs[32 + lane];
+    dst[LAT + lane] = __float2bfloat16(a * c - b * s);
+    dst[LAT + 32 + lane] = __float2bfloat16(b * c + a * s);
+  } else if (ik != nullptr) {
+    // indexer key: rmsnorm over 128 (4 per lane), rope over the first 64 dims, e4m3
+    const __nv_bfloat16* src = ik + (int64_t)t * ldik;
+    float x[4];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      x[i] = __bfloat162float(src[lane + 32 * i]);
+      ss += x[i] * x[i];
+    }
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    const float rr = rsqrtf(ss / IDXD + eps);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) x[i] = x[i] * rr * __bfloat162float(ik_w[lane + 32 * i]);
+    const float* cs = cos_sin + (int64_t)pos * PE;
+    const float c = cs[lane], s = cs[32 + lane];
+    const float a = x[0], b = x[1];  // dims lane and 32 + lane form the rotary pairs of the first 64
+    x[0] = a * c - b * s;
+    x[1] = b * c + a * s;
+    uint8_t* dst = idx_cache + slot * IDXD;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dst[lane + 32 * i] = f_to_e4m3(x[i]);
+  }
+}
+
+// rope over dims [off, off + 64) of each head row: x [T, H, ld_h] (row stride ld_t), in place
+__global__ void rope_heads_kernel(__nv_bfloat16* __restrict__ x, int64_t ld_t, int ld_h, int H, int off,
+                                  const int32_t* __restrict__ positions, const float* __restrict__ cos_sin, int T) {
+  pdl_wait();
+  pdl_trigger();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  if (warp >= T * H) return;
+  const int t = warp / H, h = warp % H;
+  __nv_bfloat16* p = x + (int64_t)t * ld_t + (int64_t)h * ld_h + off;
+  const float* cs = cos_sin + (int64_t)positions[t] * PE;
+  const float a = __bfloat162float(p[lane]), b = __bfloat162float(p[32 + lane]);
+  const float c = cs[lane], s = cs[32 + lane];
+  p[lane] = __float2bfloat16(a * c - b * s);
+  p[32 + lane] = __float2bfloat16(b * c + a * s);
+}
+
+// ------------------------------------------------------------------------------------------------
+// indexer scores: grid (T, ceil(max_ctx / 128)), one key per thread
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128) indexer_score_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq, const float* __restrict__ w, int Hi,
+    const uint8_t* __restrict__ idx_cache, const int32_t* __restrict__ bt, int mb, const int32_t* __restrict__ tok_seq,
+    const int32_t* __restrict__ tok_ctx, float* __restrict__ scores, int64_t lds) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float sq[];  // [Hi][128] then w [Hi]
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int ctx = tok_ctx[t], seq = tok_seq[t];
+  const int s = blockIdx.y * 128 + tid;
+  if ((int)blockIdx.y * 128 >= ctx) {
+    if (s < lds) scores[(int64_t)t * lds + s] = -INFINITY;
+    return;
+  }
+  float* sw = sq + Hi * IDXD;
+  for (int e = tid; e < Hi * IDXD; e += 128) sq[e] = __bfloat162float(q[(int64_t)t * ldq + e]);
+  for (int e = tid; e < Hi; e += 128) sw[e] = w[(int64_t)t * Hi + e];
+  __syncthreads();
+  if (s >= lds) return;
+  if (s >= ctx) {
+    scores[(int64_t)t * lds + s] = -INFINITY;
+    return;
+  }
+  const uint8_t* kr = idx_cache + slot_of(bt, mb, seq, s) * IDXD;
+  float k[IDXD];
+#pragma unroll
+  for (int i = 0; i < IDXD / 16; ++i) {
+    const uint4 v = reinterpret_cast<const uint4*>(kr)[i];
+    const uint8_t* b = reinterpret_cast<const uint8_t*>(&v);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) k[16 * i + j] = e4m3_to_f(b[j]);
+  }
+  float acc = 0.f;
+  for (int h = 0; h < Hi; ++h) {
+    const float* qh = sq + h * IDXD;
+    float d = 0.f;
+#pragma unroll
+    for (int i = 0; i < IDXD; ++i) d = fmaf(qh[i], k[i], d);
+    acc = fmaf(sw[h], fmaxf(d, 0.f), acc);
+  }
+  scores[(int64_t)t * lds + s] = acc;
+}
+
+// ------------------------------------------------------------------------------------------------
+// top-k of each token's scores[0, ctx): radix select of the k-th largest key, then the selected
+// positions in ascending order (greater-than first by position, ties filled lowest position first)
+// ------------------------------------------------------------------------------------------------
+R9K_DEVINL uint32_t order_key(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+__global__ void __launch_bounds__(1024) topk_select_kernel(const float* __restrict__ scores, int64_t lds,
+                                                           const int32_t* __restrict__ tok_ctx, int k,
+                                                           int32_t* __restrict__ out, int32_t* __restrict__ count) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ uint32_t hist[256];
+  __shared__ uint32_t s_prefix, s_need;
+  __shared__ uint32_t s_cnt[1024];
+  const int t = blockIdx.x, tid = threadIdx.x;
+  const int ctx = tok_ctx[t];
+  const float* sc = scores + (int64_t)t * lds;
+  int32_t* o = out + (int64_t)t * k;
+  if (ctx <= k) {
+    for (int i = tid; i < k; i += 1024) o[i] = i < ctx ? i : -1;
+    if (tid == 0) count[t] = ctx;
+    return;
+  }
+  if (tid == 0) {
+    s_prefix = 0;
+    s_need = (uint32_t)k;
+  }
+  // four 8-bit digit passes, most significant first
+  for (int pass = 0; pass < 4; ++pass) {
+    const int shift = 24 - 8 * pass;
+    for (int i = tid; i < 256; i += 1024) hist[i] = 0;
+    __syncthreads();
+    const uint32_t pre = s_prefix;
+    const uint32_t mask = pass == 0 ? 0u : (0xFFFFFFFFu << (32 - 8 * pass));
+    for (int i = tid; i < ctx; i += 1024) {
+      const uint32_t key = order_key(sc[i]);
+      if ((key & mask) == pre) atomicAdd(&hist[(key >> shift) & 0xFF], 1u);
+    }
+    __syncthreads();
+    if (tid == 0) {
+      uint32_t need = s_need, acc = 0;
+      int d = 255;
+      for (; d > 0; --d) {
+        if (acc + hist[d] >= need) break;
+        acc += hist[d];
+      }
+      s_need = need - acc;
+      s_prefix = pre | ((uint32_t)d << shift);
+    }
+    __syncthreads();
+  }
+  const uint32_t thr = s_prefix;  // the k-th largest key; s_need of the keys equal to it are taken
+  const uint32_t need_eq = s_need;
+  // per-thread contiguous ranges keep the output in position order
+  const int per = (ctx + 1023) / 1024;
+  const int i0 = tid * per, i1 = min(ctx, i0 + per);
+  uint32_t ngt = 0, neq = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t key = order_key(sc[i]);
+    ngt += key > thr;
+    neq += key == thr;
+  }
+  // exclusive scan of (ngt, neq) over threads, packed as 16 + 16 bits is too narrow; scan separately
+  s_cnt[tid] = neq;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const uint32_t v = tid >= off ? s_cnt[tid - off] : 0u;
+    __syncthreads();
+    s_cnt[tid] += v;
+    __syncthreads();
+  }
+  const uint32_t eq_before = s_cnt[tid] - neq;
+  const uint32_t eq_take = eq_before >= need_eq ? 0u : min(neq, need_eq - eq_before);
+  __syncthreads();
+  s_cnt[tid] = ngt + eq_take;
+  __syncthreads();
+  for (int off = 1; off < 1024; off <<= 1) {
+    const uint32_t v = tid >= off ? s_cnt[tid - off] : 0u;
+    __syncthreads();
+    s_cnt[tid] += v;
+    __syncthreads();
+  }
+  uint32_t w = s_cnt[tid] - (ngt + eq_take);
+  uint32_t eq_seen = 0;
+  for (int i = i0; i < i1; ++i) {
+    const uint32_t key = order_key(sc[i]);
+    if (key > thr) o[w++] = i;
+    else if (key == thr && eq_seen < eq_take) {
+      o[w++] = i;
+      ++eq_seen;
+    }
+  }
+  if (tid == 0) count[t] = k;
+}
+
+// ------------------------------------------------------------------------------------------------
+// sparse MLA decode: grid (T, H / 8, nsplit), 256 threads; warp h <-> head (blockIdx.y * 8 + h)
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) sparse_mla_decode_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq_t, int ldq_h, int H, const __nv_bfloat16* __restrict__ lat_cache,
+    const int32_t* __restrict__ bt, int mb, const int32_t* __restrict__ tok_seq, const int32_t* __restrict__ sel,
+    const int32_t* __restrict__ sel_count, int k, float scale, int nsplit, float* __restrict__ part_o,
+    float* __restrict__ part_ml) {
+  pdl_wait();
+  pdl_trigger();
+  constexpr int HB = 8, KC = 32;
+  __shared__ __align__(16) __nv_bfloat16 sqv[HB][ROW];
+  __shared__ __align__(16) __nv_bfloat16 rows[KC][ROW];
+  __shared__ float sp[HB][KC];
+  __shared__ int sidx[KC];
+  const int t = blockIdx.x, hb = blockIdx.y * HB, split = blockIdx.z, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int seq = tok_seq[t];
+  const int n = sel_count[t];
+  const int per = (n + nsplit - 1) / nsplit;
+  const int j0 = split * per, j1 = min(n, j0 + per);
+  for (int e = tid; e < HB * ROW; e += 256) {
+    const int h = e / ROW, d = e % ROW;
+    sqv[h][d] = (hb + h < H) ? q[(int64_t)t * ldq_t + (int64_t)(hb + h) * ldq_h + d] : __float2bfloat16(0.f);
+  }
+  float m = -INFINITY, l = 0.f, o[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) o[i] = 0.f;
+  for (int c0 = j0; c0 < j1; c0 += KC) {
+    const int cnt = min(KC, j1 - c0);
+    __syncthreads();
+    if (tid < KC) sidx[tid] = tid < cnt ? sel[(int64_t)t * k + c0 + tid] : -1;
+    __syncthreads();
+    for (int e = tid; e < KC * (ROW / 8); e += 256) {
+      const int r = e / (ROW / 8), c = e % (ROW / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (sidx[r] >= 0) v = reinterpret_cast<const uint4*>(lat_cache + slot_of(bt, mb, seq, sidx[r]) * ROW)[c];
+      reinterpret_cast<uint4*>(&rows[r][0])[c] = v;
+    }
+    __syncthreads();
+    // logits: warp = head, lane = row
+    {
+      float s = -INFINITY;
+      if (lane < cnt && sidx[lane] >= 0) {
+        float d = 0.f;
+        const __nv_bfloat162* qh = reinterpret_cast<const __nv_bfloat162*>(sqv[warp]);
+        const __nv_bfloat162* kr = reinterpret_cast<const __nv_bfloat162*>(rows[lane]);
+#pragma unroll 8
+        for (int i = 0; i < ROW / 2; ++i) {
+          const float2 a = __bfloat1622float2(qh[i]), b = __bfloat1622float2(kr[i]);
+          d = fmaf(a.x, b.x, fmaf(a.y, b.y, d));
+        }
+        s = d * scale;
+      }
+      float mx = s;
+      for (int off = 16; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+      const float m_new = fmaxf(m, mx);
+      const float p = (s == -INFINITY) ? 0.f : __expf(s - m_new);
+      float ps = p;
+      for (int off = 16; off > 0; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+      const float corr = (m == -INFINITY) ? 0.f : __expf(m - m_new);
+      l = l * corr + ps;
+      m = m_new;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] *= corr;
+      sp[warp][lane] = p;
+    }
+    __syncwarp();
+    // o[h][lane * 16 + i] += sum_r p[h][r] * c[r][lane * 16 + i]
+    for (int r = 0; r < cnt; ++r) {
+      const float p = sp[warp][r];
+      const __nv_bfloat16* cr = &rows[r][lane * 16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) o[i] = fmaf(p, __bfloat162float(cr[i]), o[i]);
+    }
+  }
+  const int h = hb + warp;
+  if (h < H) {
+    const int64_t base = ((int64_t)t * H + h) * nsplit + split;
+    float* po = part_o + base * LAT + lane * 16;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) po[i] = o[i];
+    if (lane == 0) {
+      part_ml[base * 2] = m;
+      part_ml[base * 2 + 1] = l;
+    }
+  }
+}
+
+// o_lat[t, h, :] = sum_s exp(m_s - M) o_s / sum_s exp(m_s - M) l_s ; grid (T * H), 128 threads
+__global__ void mla_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int nsplit,
+                                   __nv_bfloat16* __restrict__ out, int64_t ldo_t, int ldo_h, int H) {
+  pdl_wait();
+  pdl_trigger();
+  const int th = blockIdx.x, t = th / H, h = th % H, tid = threadIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) M = fmaxf(M, part_ml[((int64_t)th * nsplit + s) * 2]);
+  float L = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  for (int s = 0; s < nsplit; ++s) {
+    const float ms = part_ml[((int64_t)th * nsplit + s) * 2];
+    if (ms == -INFINITY) continue;
+    const float f = __expf(ms - M);
+    L += f * part_ml[((int64_t)th * nsplit + s) * 2 + 1];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] += f * part_o[((int64_t)th * nsplit + s) * LAT + tid + 128 * i];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) out[(int64_t)t * ldo_t + (int64_t)h * ldo_h + tid + 128 * i] = __float2bfloat16(acc[i] * inv);
+}
+
+// per-head projection: out[t, h, n] = sum_k x[t, h, k] W[h, n, k]; grid (H, ceil(N / 64), ceil(T / 16))
+__global__ void __launch_bounds__(256) head_gemv_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx_t, int ldx_h,
+                                                        const __nv_bfloat16* __restrict__ W, int N, int K,
+                                                        __nv_bfloat16* __restrict__ out, int64_t ldo_t, int ldo_h, int T) {
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ float sx[];  // [16][K]
+  const int h = blockIdx.x, n0 = blockIdx.y * 64, t0 = blockIdx.z * 16, tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int nt = min(16, T - t0);
+  for (int e = tid; e < 16 * K; e += 256) {
+    const int tt = e / K, kk = e % K;
+    sx[e] = tt < nt ? __bfloat162float(x[(int64_t)(t0 + tt) * ldx_t + (int64_t)h * ldx_h + kk]) : 0.f;
+  }
+  __syncthreads();
+  for (int nn = warp; nn < 64; nn += 8) {
+    const int n = n0 + nn;
+    if (n >= N) break;
+    const __nv_bfloat16* wr = W + ((int64_t)h * N + n) * K;
+    float acc[16];
+#pragma unroll
+    for (int tt = 0; tt < 16; ++tt) acc[tt] = 0.f;
+    for (int kk = lane; kk < K; kk += 32) {
+      const float wv = __bfloat162float(wr[kk]);
+#pragma unroll
+      for (int tt = 0; tt < 16; ++tt) acc[tt] = fmaf(wv, sx[tt * K + kk], acc[tt]);
+    }
+#pragma unroll
+    for (int tt = 0; tt < 16; ++tt) {
+      float v = acc[tt];
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      if (lane == 0 && tt < nt) out[(int64_t)(t0 + tt) * ldo_t + (int64_t)h * ldo_h + n] = __float2bfloat16(v);
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host wrappers
+// ------------------------------------------------------------------------------------------------
+void mla_cache_write(torch::Tensor kv, torch::Tensor kv_w, c10::optional<torch::Tensor> ik,
+                     c10::optional<torch::Tensor> ik_w, double eps, torch::Tensor positions, torch::Tensor cos_sin,
+                     torch::Tensor slots, torch::Tensor lat_cache, c10::optional<torch::Tensor> idx_cache) {
+  const int64_t T = kv.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(kv.size(1) >= ROW && lat_cache.size(-1) == ROW && lat_cache.size(-2) == MLA_BLK, "mla_cache_write: shapes");
+  TORCH_CHECK(cos_sin.size(1) == PE, "mla_cache_write: rope dim 64");
+  const bool hi = ik.has_value() && ik->defined();
+  const at::cuda::CUDAGuard guard(kv.device());
+  auto bf = [](const torch::Tensor& t) { return reinterpret_cast<const __nv_bfloat16*>(t.data_ptr()); };
+  const int64_t warps = 2 * T;
+  launch_pdl(mla_cache_write_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+             at::cuda::getCurrentCUDAStream(), bf(kv), kv.stride(0), bf(kv_w), hi ? bf(*ik) : nullptr,
+             hi ? ik->stride(0) : (int64_t)0, hi ? bf(*ik_w) : nullptr, (float)eps, positions.data_ptr<int32_t>(),
+             cos_sin.data_ptr<float>(), slots.data_ptr<int32_t>(),
+             reinterpret_cast<__nv_bfloat16*>(lat_cache.data_ptr()), hi ? idx_cache->data_ptr<uint8_t>() : nullptr,
+             (int)T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void rope_heads(torch::Tensor x, int64_t H, int64_t off, torch::Tensor positions, torch::Tensor cos_sin) {
+  const int64_t T = x.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(x.dim() == 3 && x.stride(2) == 1 && cos_sin.size(1) == PE, "rope_heads: x [T, H, D]");
+  const at::cuda::CUDAGuard guard(x.device());
+  const int64_t warps = T * H;
+  launch_pdl(rope_heads_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+             at::cuda::getCurrentCUDAStream(), reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), x.stride(0),
+             (int)x.stride(1), (int)H, (int)off, positions.data_ptr<int32_t>(), cos_sin.data_ptr<float>(), (int)T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void indexer_score(torch::Tensor q, torch::Tensor w, torch::Tensor idx_cache, torch::Tensor block_table,
+                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores) {
+  const int64_t T = q.size(0), Hi = q.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(q.size(2) == IDXD && q.stride(2) == 1 && q.stride(1) == IDXD, "indexer_score: q [T, Hi, 128]");
+  TORCH_CHECK(scores.size(1) >= max_ctx && Hi <= 64, "indexer_score: scores [T, >= max_ctx], <= 64 heads");
+  const at::cuda::CUDAGuard guard(q.device());
+  const size_t smem = (size_t)(Hi * IDXD + Hi) * sizeof(float);
+  launch_pdl(indexer_score_kernel, dim3((unsigned)T, (unsigned)((max_ctx + 127) / 128)), dim3(128), smem,
+             at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
+             w.data_ptr<float>(), (int)Hi, idx_cache.data_ptr<uint8_t>(), block_table.data_ptr<int32_t>(),
+             (int)block_table.size(1), tok_seq.data_ptr<int32_t>(), tok_ctx.data_ptr<int32_t>(),
+             scores.data_ptr<float>(), scores.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void topk_select(torch::Tensor scores, torch::Tensor tok_ctx, int64_t k, torch::Tensor out, torch::Tensor count) {
+  const int64_t T = scores.size(0);
+  if (T == 0) return;
+  TORCH_CHECK(out.size(1) == k && out.dtype() == torch::kInt32, "topk_select: out [T, k] int32");
+  const at::cuda::CUDAGuard guard(scores.device());
+  launch_pdl(topk_select_kernel, dim3((unsigned)T), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
+             scores.data_ptr<float>(), scores.stride(0), tok_ctx.data_ptr<int32_t>(), (int)k, out.data_ptr<int32_t>(),
+             count.data_ptr<int32_t>());
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
+                       torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
+                       torch::Tensor part_ml, torch::Tensor out) {
+  const int64_t T = q.size(0), H = q.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(q.size(2) >= ROW && q.stride(2) == 1, "sparse_mla_decode: q [T, H, 576] (latent | rope)");
+  const int64_t nsplit = part_o.size(1);
+  TORCH_CHECK(part_o.size(0) >= T * H && part_o.size(2) == LAT && part_o.is_contiguous() && part_ml.is_contiguous(),
+              "sparse_mla_decode: partials [T*H, nsplit, 512]");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  launch_pdl(sparse_mla_decode_kernel, dim3((unsigned)T, (unsigned)((H + 7) / 8), (unsigned)nsplit), dim3(256), 0, st,
+             reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), (int)q.stride(1), (int)H,
+             reinterpret_cast<const __nv_bfloat16*>(lat_cache.data_ptr()), block_table.data_ptr<int32_t>(),
+             (int)block_table.size(1), tok_seq.data_ptr<int32_t>(), sel.data_ptr<int32_t>(),
+             sel_count.data_ptr<int32_t>(), (int)sel.size(1), (float)scale, (int)nsplit, part_o.data_ptr<float>(),
+             part_ml.data_ptr<float>());
+  launch_pdl(mla_combine_kernel, dim3((unsigned)(T * H)), dim3(128), 0, st, part_o.data_ptr<float>(),
+             part_ml.data_ptr<float>(), (int)nsplit, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+             (int)out.stride(1), (int)H);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void head_gemv(torch::Tensor x, torch::Tensor W, torch::Tensor out) {
+  const int64_t T = x.size(0), H = W.size(0), N = W.size(1), K = W.size(2);
+  if (T == 0) return;
+  TORCH_CHECK(x.size(1) == H && x.size(2) == K && x.stride(2) == 1 && W.is_contiguous() && out.stride(2) == 1,
+              "head_gemv: x [T, H, K], W [H, N, K], out [T, H, N]");
+  const at::cuda::CUDAGuard guard(x.device());
+  const size_t smem = 16 * K * sizeof(float);
+  TORCH_CHECK(smem <= 200 * 1024, "head_gemv: K too large");
+  cudaFuncSetAttribute(head_gemv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  launch_pdl(head_gemv_kernel, dim3((unsigned)H, (unsigned)((N + 63) / 64), (unsigned)((T + 15) / 16)), dim3(256), smem,
+             at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0),
+             (int)x.stride(1), reinterpret_cast<const __nv_bfloat16*>(W.data_ptr()), (int)N, (int)K,
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0), (int)out.stride(1), (int)T);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

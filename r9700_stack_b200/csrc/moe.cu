@@ -140,56 +140,109 @@ void moe_route(torch::Tensor logits, int64_t k, int64_t mode, c10::optional<torc
 // ------------------------------------------------------------------------------------------------
 // align: counts -> 128-aligned segments -> BN-row work tiles; scatter assignment rows
 // ------------------------------------------------------------------------------------------------
+// exclusive scan of one value per thread over a 1024-thread block (warp shuffles + one smem pass)
+R9K_DEVINL int block_exclusive_scan(int v, int* wsum, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int x = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, x, o);
+    if (lane >= o) x += y;
+  }
+  if (lane == 31) wsum[warp] = x;
+  __syncthreads();
+  if (warp == 0) {
+    int w = wsum[lane];
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, w, o);
+      if (lane >= o) w += y;
+    }
+    wsum[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  total = wsum[31];
+  const int before = warp > 0 ? wsum[warp - 1] : 0;
+  __syncthreads();
+  return before + x - v;
+}
+
+// One CTA of 1024 threads = 32 warps; warp w owns the contiguous assignment segment w (32 segments),
+// so rows come out in assignment order per expert without any serial pass:
+//   1. per-segment expert counts (warp-match leaders add batch counts; no atomics across warps)
+//   2. per expert: exclusive scan over segments, total count
+//   3. block scans over experts: 128-aligned segment starts, BN-row tile offsets; work list
+//   4. each warp re-walks its segment: row = start[e] + segment base + rank within the batch
 __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restrict__ ids, int A, int e0, int E_local,
                                                          int BN, int32_t* __restrict__ perm_row,
                                                          int32_t* __restrict__ seg_start, int32_t* __restrict__ work,
                                                          int32_t* __restrict__ work_count, int max_work) {
   pdl_wait();
-  __shared__ int cnt[MOE_MAX_E], start[MOE_MAX_E], cursor[MOE_MAX_E], tiles[MOE_MAX_E];
-  __shared__ int s_tot, s_tiles;
-  for (int e = threadIdx.x; e < E_local; e += blockDim.x) cnt[e] = 0;
+  extern __shared__ int sm[];
+  int* cnt = sm;                       // [32][E_local] counts, then segment bases
+  int* start = sm + 32 * E_local;      // [E_local]
+  __shared__ int wsum[32];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int i = tid; i < 32 * E_local; i += 1024) cnt[i] = 0;
   __syncthreads();
-  for (int a = threadIdx.x; a < A; a += blockDim.x) {
-    const int e = ids[a] - e0;
-    if (e >= 0 && e < E_local) atomicAdd(&cnt[e], 1);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int s = 0, tl = 0;
-    for (int e = 0; e < E_local; ++e) {
-      start[e] = s;
-      cursor[e] = 0;
-      tiles[e] = tl;
-      s += (cnt[e] + 127) / 128 * 128;
-      tl += (cnt[e] + BN - 1) / BN;
+  const int per = (A + 31) / 32;
+  const int a0 = warp * per, a1 = min(A, a0 + per);
+  int* mycnt = cnt + warp * E_local;
+  for (int base = a0; base < a1; base += 32) {
+    const int a = base + lane;
+    int e = -1 - lane;  // unique sentinel for lanes past the segment / non-local experts
+    if (a < a1) {
+      const int ee = ids[a] - e0;
+      if (ee >= 0 && ee < E_local) e = ee;
     }
-    s_tot = s;
-    s_tiles = min(tl, max_work);
-    *work_count = s_tiles;
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (e >= 0 && lane == __ffs(peers) - 1) mycnt[e] += __popc(peers);
+    __syncwarp();
   }
   __syncthreads();
-  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
-    seg_start[e] = start[e];
-    const int nt = (cnt[e] + BN - 1) / BN;
-    for (int i = 0; i < nt; ++i) {
-      const int wi = tiles[e] + i;
+  // per expert: scan over segments; thread e (one pass: E_local <= 1024)
+  int total = 0;
+  if (tid < E_local) {
+    for (int w = 0; w < 32; ++w) {
+      const int c = cnt[w * E_local + tid];
+      cnt[w * E_local + tid] = total;
+      total += c;
+    }
+  }
+  int all_rows, all_tiles;
+  const int padded = (total + 127) / 128 * 128;
+  const int ntile = (total + BN - 1) / BN;
+  const int st = block_exclusive_scan(tid < E_local ? padded : 0, wsum, all_rows);
+  const int tl = block_exclusive_scan(tid < E_local ? ntile : 0, wsum, all_tiles);
+  if (tid < E_local) {
+    start[tid] = st;
+    seg_start[tid] = st;
+    for (int i = 0; i < ntile; ++i) {
+      const int wi = tl + i;
       if (wi < max_work) {
-        work[wi * 3 + 0] = e;
-        work[wi * 3 + 1] = start[e] + i * BN;
-        work[wi * 3 + 2] = min(BN, cnt[e] - i * BN);
+        work[wi * 3 + 0] = tid;
+        work[wi * 3 + 1] = st + i * BN;
+        work[wi * 3 + 2] = min(BN, total - i * BN);
       }
     }
   }
-  // rows in assignment order within each expert (a serial pass per expert keeps the layout deterministic)
-  for (int e = threadIdx.x; e < E_local; e += blockDim.x) {
-    if (cnt[e] == 0) continue;
-    int c = 0;
-    for (int a = 0; a < A; ++a)
-      if (ids[a] - e0 == e) perm_row[a] = start[e] + c++;
-  }
-  for (int a = threadIdx.x; a < A; a += blockDim.x) {
-    const int e = ids[a] - e0;
-    if (e < 0 || e >= E_local) perm_row[a] = -1;
+  if (tid == 0) *work_count = min(all_tiles, max_work);
+  __syncthreads();
+  for (int base = a0; base < a1; base += 32) {
+    const int a = base + lane;
+    int e = -1 - lane;
+    if (a < a1) {
+      const int ee = ids[a] - e0;
+      if (ee >= 0 && ee < E_local) e = ee;
+    }
+    const unsigned peers = __match_any_sync(0xffffffffu, e);
+    if (a < a1) {
+      if (e >= 0) perm_row[a] = start[e] + mycnt[e] + __popc(peers & ((1u << lane) - 1u));
+      else perm_row[a] = -1;
+    }
+    __syncwarp();
+    if (e >= 0 && lane == __ffs(peers) - 1) mycnt[e] += __popc(peers);
+    __syncwarp();
   }
 }
 
@@ -198,7 +251,13 @@ void moe_align(torch::Tensor ids, int64_t e0, int64_t E_local, int64_t BN, torch
   TORCH_CHECK(E_local <= MOE_MAX_E, "moe_align: too many local experts");
   TORCH_CHECK(BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256, "moe_align: BN");
   const at::cuda::CUDAGuard guard(ids.device());
-  TORCH_CHECK(launch_pdl(moe_align_kernel, dim3(1), dim3(1024), 0, at::cuda::getCurrentCUDAStream(),
+  const size_t smem = (size_t)(33 * E_local) * sizeof(int);
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 33 * MOE_MAX_E * 4);
+    attr = true;
+  }
+  TORCH_CHECK(launch_pdl(moe_align_kernel, dim3(1), dim3(1024), smem, at::cuda::getCurrentCUDAStream(),
                          ids.data_ptr<int32_t>(), (int)ids.numel(), (int)e0, (int)E_local, (int)BN,
                          perm_row.data_ptr<int32_t>(), seg_start.data_ptr<int32_t>(), work.data_ptr<int32_t>(),
                          work_count.data_ptr<int32_t>(), (int)work.size(0)) == cudaSuccess,

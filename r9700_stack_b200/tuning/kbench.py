@@ -173,6 +173,40 @@ def bench_decode(a) -> dict:
             "us": us, "weight_bytes": llm.model.weight_bytes(), "flops": 0.0}
 
 
+def bench_gdn(a) -> dict:
+    """The fused GDN decode kernel alone: S sequences, one token each; states rotate over enough
+    layers' worth of buffers that every launch reads its state from HBM."""
+    from .. import _native
+    from ..utils import status
+
+    torch.manual_seed(0)
+    S, Hk, Hv, D = a.S, a.Hk, a.Hv, 128
+    C = 2 * Hk * D + Hv * D
+    rows = C + Hv * D + 2 * Hv
+    sdt = torch.float32 if a.state == "fp32" else torch.bfloat16
+    per = S * Hv * D * D * (4 if a.state == "fp32" else 2)
+    nb = max(1, min(16, int(2 * L2_BYTES // per) + 1))
+    states = [(torch.randn(S + 1, Hv, D, D, device="cuda") * 0.01).to(sdt) for _ in range(nb)]
+    convs = [torch.randn(S + 1, C, 3, device="cuda").to(sdt) for _ in range(nb)]
+    proj = torch.randn(S, rows, device="cuda").bfloat16()
+    conv_w = (torch.randn(C, 4, device="cuda") * 0.3).bfloat16()
+    A_log = torch.rand(Hv, device="cuda") * 2
+    dt = torch.randn(Hv, device="cuda") * 0.5
+    nw = torch.ones(D, device="cuda").bfloat16()
+    slot = torch.arange(1, S + 1, dtype=torch.int32, device="cuda")
+    hs = torch.ones(S, dtype=torch.int32, device="cuda")
+    oq = torch.empty(S, Hv * D, dtype=torch.uint8, device="cuda")
+    osf = torch.zeros(((S + 127) // 128 + 1) * 512 * (Hv * D // 128) + 4096, dtype=torch.uint8, device="cuda")
+    ops = _native.ops()
+    z_off = 2 * Hk * D + Hv * D
+    f = lambda i: ops.gdn_decode_fused(proj, Hk, Hv, z_off, z_off + Hv * D, z_off + Hv * D + Hv, conv_w,
+                                       convs[i % nb], states[i % nb], slot, hs, A_log, dt, nw, 1e-6, oq, osf, None)
+    us = _time(f, a.reps, a.warmup)
+    status.check()
+    return {"kernel": "gdn_decode_fused", "S": S, "Hk": Hk, "Hv": Hv, "state": a.state, "us": us,
+            "weight_bytes": 2.0 * per, "flops": 0.0}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -195,11 +229,16 @@ def main(argv=None):
     d.add_argument("--streams", type=int, default=16)
     d.add_argument("--prompt", type=int, default=256)
     d.add_argument("--layers", type=int, default=0)
-    for p in (g, m, d):
+    gd = sub.add_parser("gdn")
+    gd.add_argument("--S", type=int, default=16)
+    gd.add_argument("--Hk", type=int, default=16)
+    gd.add_argument("--Hv", type=int, default=48)
+    gd.add_argument("--state", choices=["bf16", "fp32"], default="bf16")
+    for p in (g, m, d, gd):
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode}[a.cmd](a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:
         r["gbs"] = r["weight_bytes"] / r["us"] / 1e3

@@ -1,0 +1,137 @@
+"""MLA + lightning indexer + top-k kernels vs plain PyTorch (GLM / DeepSeek sparse attention)."""
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _ops():
+    from r9700_stack_b200 import _native
+
+    return _native.ops()
+
+
+def _check():
+    from r9700_stack_b200.utils import status
+
+    torch.cuda.synchronize()
+    status.check()
+
+
+def _rope_ref(x, pos, cs):
+    c, s = cs[pos, :32], cs[pos, 32:]
+    a, b = x[..., :32], x[..., 32:64]
+    return torch.cat([a * c - b * s, b * c + a * s, x[..., 64:]], -1)
+
+
+def _setup(ctxs, seed=0):
+    torch.manual_seed(seed)
+    BLK = 64
+    nblk = sum((c + BLK - 1) // BLK for c in ctxs) + 1
+    mb = max((c + BLK - 1) // BLK for c in ctxs)
+    perm = (torch.randperm(nblk - 1) + 1).tolist()
+    bt = torch.zeros(len(ctxs), mb, dtype=torch.int32)
+    for s, c in enumerate(ctxs):
+        for b in range((c + BLK - 1) // BLK):
+            bt[s, b] = perm.pop()
+    inv = 1.0 / (10000 ** (torch.arange(0, 64, 2, dtype=torch.float64) / 64))
+    f = torch.outer(torch.arange(max(ctxs) + 8, dtype=torch.float64), inv)
+    cs = torch.cat([f.cos(), f.sin()], -1).float().cuda()
+    return nblk, bt.cuda(), cs
+
+
+def test_cache_write_indexer_topk_and_sparse_attention():
+    ctxs = [70, 300, 5]
+    nblk, bt, cs = _setup(ctxs)
+    o = _ops()
+    # write every position of every sequence
+    seqs, poss = [], []
+    for s, c in enumerate(ctxs):
+        seqs += [s] * c
+        poss += list(range(c))
+    T = len(seqs)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")
+    slots = i32([int(bt[s, p // 64]) * 64 + p % 64 for s, p in zip(seqs, poss)])
+    kv = torch.randn(T, 576).bfloat16().cuda()
+    kvw = (1 + 0.1 * torch.randn(512)).bfloat16().cuda()
+    ik = torch.randn(T, 128).bfloat16().cuda()
+    ikw = (1 + 0.1 * torch.randn(128)).bfloat16().cuda()
+    lat = torch.zeros(nblk, 64, 576, dtype=torch.bfloat16, device="cuda")
+    icache = torch.zeros(nblk, 64, 128, dtype=torch.uint8, device="cuda")
+    o.mla_cache_write(kv, kvw, ik, ikw, 1e-6, i32(poss), cs, slots, lat, icache)
+    _check()
+    posT = torch.tensor(poss, device="cuda")
+    c = kv[:, :512].float()
+    c = c * torch.rsqrt(c.square().mean(-1, keepdim=True) + 1e-6) * kvw.float()
+    kpe = _rope_ref(kv[:, 512:].float(), posT, cs)
+    got = lat.view(-1, 576)[slots.long()].float()
+    torch.testing.assert_close(got[:, :512], c, rtol=1e-2, atol=1e-2)
+    torch.testing.assert_close(got[:, 512:], kpe, rtol=1e-2, atol=1e-2)
+    kk = ik.float() * torch.rsqrt(ik.float().square().mean(-1, keepdim=True) + 1e-6) * ikw.float()
+    kk = _rope_ref(kk, posT, cs)
+    kq = icache.view(-1, 128)[slots.long()].view(torch.float8_e4m3fn).float()
+    torch.testing.assert_close(kq, kk.clamp(-448, 448).to(torch.float8_e4m3fn).float(), rtol=0, atol=0)
+
+    # one query per sequence (its last position), 8 indexer heads, top-64
+    Hi, K, H = 8, 64, 16
+    Tq = len(ctxs)
+    tok_seq = i32(list(range(Tq)))
+    tok_ctx = i32(ctxs)
+    qi = torch.randn(Tq, Hi, 128).bfloat16().cuda()
+    wi = torch.rand(Tq, Hi).cuda()
+    maxc = max(ctxs)
+    scores = torch.empty(Tq, maxc, device="cuda")
+    o.indexer_score(qi, wi, icache, bt, tok_seq, tok_ctx, maxc, scores)
+    sel = torch.empty(Tq, K, dtype=torch.int32, device="cuda")
+    cnt = torch.empty(Tq, dtype=torch.int32, device="cuda")
+    o.topk_select(scores, tok_ctx, K, sel, cnt)
+    _check()
+    for s, cx in enumerate(ctxs):
+        rows = torch.tensor([int(bt[s, p // 64]) * 64 + p % 64 for p in range(cx)], device="cuda")
+        kf = icache.view(-1, 128)[rows].view(torch.float8_e4m3fn).float()
+        ref = (wi[s][:, None] * torch.relu(qi[s].float() @ kf.t())).sum(0)
+        torch.testing.assert_close(scores[s, :cx], ref, rtol=1e-4, atol=1e-4)
+        n = min(K, cx)
+        assert int(cnt[s]) == n
+        got_sel = sel[s, :n].cpu().tolist()
+        assert got_sel == sorted(got_sel)
+        exp = sorted(torch.topk(scores[s, :cx], n).indices.cpu().tolist())
+        assert got_sel == exp
+
+    # sparse MLA over the selected rows
+    q = torch.randn(Tq, H, 576).bfloat16().cuda()
+    scale = 1 / math.sqrt(192)
+    nsplit = 3
+    po = torch.empty(Tq * H, nsplit, 512, device="cuda")
+    pml = torch.empty(Tq * H, nsplit, 2, device="cuda")
+    out = torch.empty(Tq, H, 512, dtype=torch.bfloat16, device="cuda")
+    o.sparse_mla_decode(q, lat, bt, tok_seq, sel, cnt, scale, po, pml, out)
+    _check()
+    for s in range(Tq):
+        n = int(cnt[s])
+        pos_sel = sel[s, :n].long()
+        rows = torch.tensor([int(bt[s, int(p) // 64]) * 64 + int(p) % 64 for p in pos_sel], device="cuda")
+        R = lat.view(-1, 576)[rows].float()
+        logit = (q[s].float() @ R.t()) * scale
+        ref = torch.softmax(logit, -1) @ R[:, :512]
+        torch.testing.assert_close(out[s].float(), ref, rtol=2e-2, atol=2e-2)
+
+
+def test_head_gemv_and_rope_heads():
+    T, H, K, N = 5, 6, 512, 128
+    x = torch.randn(T, H, K).bfloat16().cuda()
+    W = (torch.randn(H, N, K) * 0.05).bfloat16().cuda()
+    out = torch.empty(T, H, N, dtype=torch.bfloat16, device="cuda")
+    _ops().head_gemv(x, W, out)
+    _check()
+    ref = torch.einsum("thk,hnk->thn", x.float(), W.float())
+    torch.testing.assert_close(out.float(), ref, rtol=2e-2, atol=2e-2)
+    _, _, cs = _setup([40])
+    y = torch.randn(T, H, 192).bfloat16().cuda()
+    pos = torch.tensor([0, 3, 7, 20, 39], dtype=torch.int32, device="cuda")
+    ref = _rope_ref(y[..., 128:].float(), pos.long()[:, None], cs)
+    _ops().rope_heads(y, H, 128, pos, cs)
+    _check()
+    torch.testing.assert_close(y[..., 128:].float(), ref, rtol=1e-2, atol=1e-2)

@@ -124,3 +124,38 @@ def test_tiny_moe_model_matches_reference():
     ref = reference_forward(llm.model, [seq.output[-2]], st)[-1]
     cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
     assert float(cos) > 0.99, float(cos)
+
+
+@pytest.mark.parametrize("T,k,E,e0,El,BN", [(16, 10, 288, 0, 288, 16), (3000, 8, 256, 64, 128, 128), (7, 2, 8, 0, 8, 16)])
+def test_align_matches_python(T, k, E, e0, El, BN):
+    torch.manual_seed(T)
+    ids = torch.randint(0, E, (T, k), dtype=torch.int32)
+    A = T * k
+    perm = torch.empty(A, dtype=torch.int32, device="cuda")
+    seg = torch.empty(El, dtype=torch.int32, device="cuda")
+    max_work = A + El
+    work = torch.zeros(max_work, 3, dtype=torch.int32, device="cuda")
+    wc = torch.zeros(1, dtype=torch.int32, device="cuda")
+    _ops().moe_align(ids.cuda(), e0, El, BN, perm, seg, work, wc)
+    _check()
+    flat = ids.flatten().tolist()
+    cnt = [0] * El
+    for e in flat:
+        if e0 <= e < e0 + El:
+            cnt[e - e0] += 1
+    start, s = [], 0
+    for c in cnt:
+        start.append(s)
+        s += (c + 127) // 128 * 128
+    ref_perm, cur = [], [0] * El
+    for e in flat:
+        if e0 <= e < e0 + El:
+            ref_perm.append(start[e - e0] + cur[e - e0])
+            cur[e - e0] += 1
+        else:
+            ref_perm.append(-1)
+    assert perm.cpu().tolist() == ref_perm
+    assert seg.cpu().tolist() == start
+    ref_work = [[e, start[e] + i * BN, min(BN, cnt[e] - i * BN)] for e in range(El) for i in range((cnt[e] + BN - 1) // BN)]
+    assert int(wc) == len(ref_work)
+    assert work[: len(ref_work)].cpu().tolist() == ref_work
