@@ -117,6 +117,7 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor b
                        torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
                        torch::Tensor part_ml, torch::Tensor out);
 void head_gemv(torch::Tensor x, torch::Tensor W, torch::Tensor out);
+void host_gather(torch::Tensor table, torch::Tensor ids, int64_t fmt, int64_t dim, torch::Tensor out);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -208,6 +209,7 @@ TORCH_LIBRARY(r9k, m) {
   m.def("sparse_mla_decode(Tensor q, Tensor lat_cache, Tensor block_table, Tensor tok_seq, Tensor sel, "
         "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out) -> ()");
   m.def("head_gemv(Tensor x, Tensor W, Tensor(a!) out) -> ()");
+  m.def("host_gather(Tensor table, Tensor ids, int fmt, int dim, Tensor(a!) out) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -219,6 +221,7 @@ TORCH_LIBRARY(r9k, m) {
 
 TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gemm_mx", &r9k::gemm_mx);
+  m.impl("host_gather", &r9k::host_gather);
   m.impl("gemm_mx_swiglu", &r9k::gemm_mx_swiglu);
   m.impl("gemm_bf16", &r9k::gemm_bf16);
   m.impl("rmsnorm_quant", &r9k::rmsnorm_quant);

@@ -462,12 +462,15 @@ __global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
   const bool hs = seq_has_state[t] != 0;
   const int c = tid >> 1, rg = tid & 1;
   ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * PER;
-  ST* myS = reinterpret_cast<ST*>(s_state) + tid * PER;
+  // 16-byte chunk v of thread tid lives at chunk index v * 256 + tid: a warp's accesses to one chunk
+  // are consecutive (conflict-free), where a per-thread contiguous layout would put all 32 lanes of
+  // a warp in the same banks
+  constexpr int NV = PER * sizeof(ST) / 16;  // chunks per thread
+  uint4* sS = reinterpret_cast<uint4*>(s_state);
   if (hs) {
-    constexpr int NV = PER * sizeof(ST) / 16;
 #pragma unroll
     for (int v = 0; v < NV; ++v)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(myS) + 16 * v),
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + v * 256 + tid)),
                    "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -529,8 +532,13 @@ __global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
 #pragma unroll 1
   for (int p = 0; p < PER / PC; ++p) {
     float S[PC];
-    if (hs) StateVec16<ST>::load(myS + p * PC, S);
-    else {
+    if (hs) {
+      constexpr int CPP = NV / (PER / PC);  // chunks per 16-entry piece
+      uint4 raw[CPP];
+#pragma unroll
+      for (int q = 0; q < CPP; ++q) raw[q] = sS[(p * CPP + q) * 256 + tid];
+      StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
+    } else {
 #pragma unroll
       for (int r = 0; r < PC; ++r) S[r] = 0.f;
     }
@@ -545,8 +553,13 @@ __global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
 #pragma unroll 1
   for (int p = 0; p < PER / PC; ++p) {
     float S[PC];
-    if (hs) StateVec16<ST>::load(myS + p * PC, S);
-    else {
+    if (hs) {
+      constexpr int CPP = NV / (PER / PC);  // chunks per 16-entry piece
+      uint4 raw[CPP];
+#pragma unroll
+      for (int q = 0; q < CPP; ++q) raw[q] = sS[(p * CPP + q) * 256 + tid];
+      StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
+    } else {
 #pragma unroll
       for (int r = 0; r < PC; ++r) S[r] = 0.f;
     }
@@ -618,8 +631,13 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   cfg.attrs = attr;
   cfg.numAttrs = 2;
 #define R9K_GDF(ST_T)                                                                                                 \
-  cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize,                     \
-                       (int)cfg.dynamicSmemBytes);                                                                    \
+  {                                                                                                                   \
+    static bool attr_done = false;                                                                                    \
+    if (!attr_done) {                                                                                                 \
+      cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4); \
+      attr_done = true;                                                                                               \
+    }                                                                                                                 \
+  }                                                                                                                   \
   TORCH_CHECK(cudaLaunchKernelEx(&cfg, gdn_decode_fused_kernel<ST_T>,                                                 \
       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)z_off, (int)b_off, \
       (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()),                                          \

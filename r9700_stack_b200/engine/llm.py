@@ -27,7 +27,7 @@ class LLM:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
         if model is None:
-            model = build_model(model_cfg, self.par, self.device, seed=seed, comm=comm)
+            model = build_model(model_cfg, self.par, self.device, seed=seed, comm=comm, max_ctx=ec.max_model_len)
         self.model = model
         blocks_per_seq = math.ceil(ec.max_model_len / ec.kv_block)
         num_blocks = ec.num_kv_blocks or (ec.max_batch * blocks_per_seq + 1)
@@ -104,7 +104,7 @@ def make_drafter(method: str, model, ec: EngineConfig, num_blocks: int, num_slot
     raise ValueError(f"unknown speculative method {method!r}")
 
 
-def build_model(cfg, par, device, seed=0, comm=None):
+def build_model(cfg, par, device, seed=0, comm=None, max_ctx: int = 32768):
     if isinstance(cfg, HybridConfig):
         if cfg.moe_experts:
             from ..models.hybrid_moe import HybridMoELM
@@ -113,4 +113,8 @@ def build_model(cfg, par, device, seed=0, comm=None):
         from ..models.hybrid import HybridLM
 
         return HybridLM(cfg, par, device, seed=seed, comm=comm)
+    from ..models.mla_moe import MLAConfig, MLAMoELM
+
+    if isinstance(cfg, MLAConfig):
+        return MLAMoELM(cfg, par, device, seed=seed, comm=comm, max_ctx=max_ctx)
     raise TypeError(f"unsupported model config {type(cfg)}")

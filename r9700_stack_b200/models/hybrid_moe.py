@@ -26,29 +26,70 @@ def _ops():
     return _native.ops()
 
 
-class MoEWorkspace(Workspace):
-    def __init__(self, model: "HybridMoELM", max_tokens: int, max_logit_rows: int):
-        super().__init__(model, max_tokens, max_logit_rows)
-        c, dev = model.cfg, model.device
-        k, El = c.moe_topk, model.e_local
+class MoEBuffers:
+    """Device buffers of one routed-expert FFN call for up to ``max_tokens`` tokens."""
+
+    def __init__(self, dev, max_tokens: int, hidden: int, n_experts: int, k: int, E_local: int, moe_ffn: int,
+                 shared_local: int):
         A = max_tokens * k
-        self.moe_act = L.alloc_act(max_tokens, c.hidden, dev)
-        self.logits_e = torch.zeros(max_tokens, c.moe_experts, dtype=torch.float32, device=dev)
+        self.moe_act = L.alloc_act(max_tokens, hidden, dev)
+        self.logits_e = torch.zeros(max_tokens, n_experts, dtype=torch.float32, device=dev)
         self.ids = torch.zeros(max_tokens, k, dtype=torch.int32, device=dev)
         self.wts = torch.zeros(max_tokens, k, dtype=torch.float32, device=dev)
         self.perm_row = torch.zeros(A, dtype=torch.int32, device=dev)
-        self.seg_start = torch.zeros(El, dtype=torch.int32, device=dev)
-        self.max_rows = A + 128 * min(El, A)
-        self.max_work = A + El
+        self.seg_start = torch.zeros(E_local, dtype=torch.int32, device=dev)
+        self.max_rows = A + 128 * min(E_local, A)
+        self.max_work = A + E_local
         self.work = torch.zeros(self.max_work, 3, dtype=torch.int32, device=dev)
         self.work_count = torch.zeros(1, dtype=torch.int32, device=dev)
-        self.sorted_act = L.alloc_act(self.max_rows, c.hidden, dev)
-        self.h_act = L.alloc_act(self.max_rows, c.moe_ffn, dev)
-        self.y_sorted = torch.zeros(self.max_rows, c.hidden, dtype=torch.bfloat16, device=dev)
-        if model.shared_local:
-            self.sh_h = torch.zeros(max_tokens, model.shared_local, dtype=torch.bfloat16, device=dev)
-            self.sh_out = torch.zeros(max_tokens, c.hidden, dtype=torch.bfloat16, device=dev)
+        self.sorted_act = L.alloc_act(self.max_rows, hidden, dev)
+        self.h_act = L.alloc_act(self.max_rows, moe_ffn, dev)
+        self.y_sorted = torch.zeros(self.max_rows, hidden, dtype=torch.bfloat16, device=dev)
+        if shared_local:
+            self.sh_h = torch.zeros(max_tokens, shared_local, dtype=torch.bfloat16, device=dev)
+            self.sh_out = torch.zeros(max_tokens, hidden, dtype=torch.bfloat16, device=dev)
             self.sh_gate = torch.zeros(max_tokens, 1, dtype=torch.float32, device=dev)
+
+
+def moe_ffn(lay, x: torch.Tensor, mb: MoEBuffers, out: torch.Tensor, *, k: int, e0: int, E_local: int, moe_ffn: int,
+            hidden: int, shared_local: int, route_mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
+            scale: float = 1.0, renorm: bool = True) -> None:
+    """Routed experts + shared expert for the T rows of x (bf16) into out (bf16), with the router
+    weights applied and summed in one rounding (moe_combine). Experts outside [e0, e0 + E_local)
+    belong to other ranks: their rows are skipped and the caller's all-reduce sums the partials."""
+    T = x.shape[0]
+    o = _ops()
+    dev = x.device
+    L.bf16_linear(x, lay["router"], out=mb.logits_e[:T], out_dtype=torch.float32)
+    o.moe_route(mb.logits_e[:T], k, route_mode, bias, n_group, topk_group, float(scale), renorm, mb.ids[:T], mb.wts[:T])
+    BN = 16 if T <= 16 else 128
+    A = T * k
+    o.moe_align(mb.ids[:T], e0, E_local, BN, mb.perm_row[:A], mb.seg_start, mb.work, mb.work_count)
+    L.quant_act(x, out=mb.moe_act.narrow(T))
+    o.moe_gather(mb.moe_act.q[:T], mb.moe_act.sf, k, mb.perm_row[:A], mb.sorted_act.q, mb.sorted_act.sf)
+    nwork = min(mb.max_work, -(-A // BN) + min(E_local, A))
+    o.gemm_mx_grouped(lay["e_gate"].q, lay["e_gate"].sf, lay["e_up"].q, lay["e_up"].sf, True, mb.sorted_act.q,
+                      mb.sorted_act.sf, mb.work[:nwork], mb.work_count, moe_ffn, E_local, BN, mb.h_act.q, mb.h_act.sf,
+                      _status(dev))
+    o.gemm_mx_grouped(lay["e_down"].q, lay["e_down"].sf, None, None, True, mb.h_act.q, mb.h_act.sf, mb.work[:nwork],
+                      mb.work_count, hidden, E_local, BN, mb.y_sorted, None, _status(dev))
+    shared = gate = None
+    if shared_local:
+        L.bf16_swiglu(x, lay["s_gate"], lay["s_up"], out=mb.sh_h[:T])
+        L.bf16_linear(mb.sh_h[:T], lay["s_down"], out=mb.sh_out[:T])
+        shared = mb.sh_out[:T]
+        if "s_gvec" in lay:
+            L.bf16_linear(x, lay["s_gvec"], out=mb.sh_gate[:T], out_dtype=torch.float32)
+            gate = mb.sh_gate[:T]
+    o.moe_combine(mb.y_sorted, mb.perm_row[:A], mb.wts[:T], k, shared, gate, out)
+
+
+class MoEWorkspace(Workspace):
+    def __init__(self, model: "HybridMoELM", max_tokens: int, max_logit_rows: int):
+        super().__init__(model, max_tokens, max_logit_rows)
+        c = model.cfg
+        self.moe = MoEBuffers(model.device, max_tokens, c.hidden, c.moe_experts, c.moe_topk, model.e_local, c.moe_ffn,
+                              model.shared_local)
 
 
 class HybridMoELM(HybridLM):
@@ -86,33 +127,10 @@ class HybridMoELM(HybridLM):
 
     def _ffn_block(self, i, lay, meta, ws: MoEWorkspace, T: int, call: int, fused: bool) -> None:
         c = self.cfg
-        k = c.moe_topk
-        o = _ops()
-        x = ws.norm_out[:T]  # bf16 output of the post-attention norm
-        L.bf16_linear(x, lay["router"], out=ws.logits_e[:T], out_dtype=torch.float32)
-        o.moe_route(ws.logits_e[:T], k, 0 if c.moe_router == "softmax" else 1, None, 1, 1, 1.0, True,
-                    ws.ids[:T], ws.wts[:T])
-        BN = 16 if T <= 16 else 128
-        A = T * k
-        o.moe_align(ws.ids[:T], self.par.tp_rank * self.e_local, self.e_local, BN, ws.perm_row[:A], ws.seg_start,
-                    ws.work, ws.work_count)
-        L.quant_act(x, out=ws.moe_act.narrow(T))
-        o.moe_gather(ws.moe_act.q[:T], ws.moe_act.sf, k, ws.perm_row[:A], ws.sorted_act.q, ws.sorted_act.sf)
-        nwork = min(ws.max_work, -(-A // BN) + self.e_local)
-        o.gemm_mx_grouped(lay["e_gate"].q, lay["e_gate"].sf, lay["e_up"].q, lay["e_up"].sf, True, ws.sorted_act.q,
-                          ws.sorted_act.sf, ws.work[:nwork], ws.work_count, c.moe_ffn, self.e_local, BN,
-                          ws.h_act.q, ws.h_act.sf, _status(self.device))
-        o.gemm_mx_grouped(lay["e_down"].q, lay["e_down"].sf, None, None, True, ws.h_act.q, ws.h_act.sf,
-                          ws.work[:nwork], ws.work_count, c.hidden, self.e_local, BN, ws.y_sorted, None,
-                          _status(self.device))
-        shared = gate = None
-        if self.shared_local:
-            L.bf16_swiglu(x, lay["s_gate"], lay["s_up"], out=ws.sh_h[:T])
-            L.bf16_linear(ws.sh_h[:T], lay["s_down"], out=ws.sh_out[:T])
-            L.bf16_linear(x, lay["s_gvec"], out=ws.sh_gate[:T], out_dtype=torch.float32)
-            shared, gate = ws.sh_out[:T], ws.sh_gate[:T]
         out = self._reduce_target(ws, T, call, fused)
-        o.moe_combine(ws.y_sorted, ws.perm_row[:A], ws.wts[:T], k, shared, gate, out)
+        moe_ffn(lay, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=self.par.tp_rank * self.e_local,
+                E_local=self.e_local, moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local,
+                route_mode=0 if c.moe_router == "softmax" else 1)
         self._after_partial(ws, T, call, fused)
 
 

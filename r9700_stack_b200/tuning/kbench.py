@@ -4,8 +4,10 @@
     python -m r9700_stack_b200.tuning.kbench gemm --N 17408 --K 5120 --M 16 --fmt fp4 --swiglu
     python -m r9700_stack_b200.tuning.kbench moe --T 16 --E 288 --topk 10 --H 2048 --I 512
     python -m r9700_stack_b200.tuning.kbench gemm ... --reps 1 --warmup 0     # one launch (for ncu -c 1)
-    python -m r9700_stack_b200.tuning.kbench decode --model dense27b --streams 16 --steps 2
+    python -m r9700_stack_b200.tuning.kbench decode --model dense27b --streams 16 --reps 2 --eager
         # eager decode steps of a whole model inside NVTX ranges "decode_step" (ncu --nvtx-include)
+
+Timed calls are captured into a CUDA graph and replayed (device time only) unless --eager.
 
 Weights rotate over enough copies that one pass over them exceeds L2 (126 MB), so every timed launch
 streams its weights from HBM; achieved bandwidth is algorithmic bytes / event time and the fraction is
@@ -35,20 +37,37 @@ def peaks() -> dict:
         return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
 
 
-def _time(fn, reps: int, warmup: int) -> float:
+def _time(fn, reps: int, warmup: int, graph: bool = True) -> float:
+    """Device time per call (us). The timed calls are captured into one CUDA graph and replayed, so
+    host launch overhead is excluded; ``graph=False`` times eager launches instead."""
+    from ..utils import status
+
     for i in range(warmup):
         fn(i)
     torch.cuda.synchronize()
     if reps <= 0:
         return 0.0
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for i in range(reps):
-        fn(i)
-    e1.record()
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                for i in range(reps):
+                    fn(i)
+        torch.cuda.current_stream().wait_stream(s)
+        g.replay()  # first replay uploads the graph
+        torch.cuda.synchronize()
+        e0.record()
+        g.replay()
+        e1.record()
+    else:
+        e0.record()
+        for i in range(reps):
+            fn(i)
+        e1.record()
     torch.cuda.synchronize()
-    from ..utils import status
-
     status.check()
     return e0.elapsed_time(e1) * 1e3 / reps  # us
 
@@ -84,7 +103,7 @@ def bench_gemm(a) -> dict:
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
             f = lambda i: L.mx_linear(x, ws[i % nw], out=out)
-    us = _time(f, a.reps, a.warmup)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
     wbytes = per + (N * K // 32) * (0 if a.fmt == "bf16" else 1) * (2 if a.swiglu else 1)
     flops = 2.0 * M * N * K * (2 if a.swiglu else 1)
     return {"kernel": "gemm", "fmt": a.fmt, "swiglu": a.swiglu, "N": N, "K": K, "M": M, "copies": nw,
@@ -127,7 +146,7 @@ def bench_moe(a) -> dict:
         ops.gemm_mx_grouped(D.q, D.sf, None, None, True, h.q, h.sf, work, wc, H, E, BN, y, None, st)
         ops.moe_combine(y, perm, wts, k, None, None, out)
 
-    us = _time(f, a.reps, a.warmup)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
     active = int((torch.bincount(ids.flatten().long(), minlength=E) > 0).sum()) if a.reps else E
     wbytes = active * 3 * I * H * (0.5 + 1 / 32)
     return {"kernel": "moe_layer", "T": T, "E": E, "topk": k, "H": H, "I": I, "active_experts": active,
@@ -168,7 +187,7 @@ def bench_decode(a) -> dict:
         llm.model.forward(meta, ws, lay.T, lay.R)
         torch.cuda.nvtx.range_pop()
 
-    us = _time(f, a.reps, a.warmup)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
     return {"kernel": "decode_step_eager", "model": cfg.name, "streams": a.streams, "layers": cfg.layers,
             "us": us, "weight_bytes": llm.model.weight_bytes(), "flops": 0.0}
 
@@ -201,7 +220,7 @@ def bench_gdn(a) -> dict:
     z_off = 2 * Hk * D + Hv * D
     f = lambda i: ops.gdn_decode_fused(proj, Hk, Hv, z_off, z_off + Hv * D, z_off + Hv * D + Hv, conv_w,
                                        convs[i % nb], states[i % nb], slot, hs, A_log, dt, nw, 1e-6, oq, osf, None)
-    us = _time(f, a.reps, a.warmup)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
     status.check()
     return {"kernel": "gdn_decode_fused", "S": S, "Hk": Hk, "Hv": Hv, "state": a.state, "us": us,
             "weight_bytes": 2.0 * per, "flops": 0.0}
@@ -235,6 +254,7 @@ def main(argv=None):
     gd.add_argument("--Hv", type=int, default=48)
     gd.add_argument("--state", choices=["bf16", "fp32"], default="bf16")
     for p in (g, m, d, gd):
+        p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
