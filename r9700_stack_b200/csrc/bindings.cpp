@@ -118,6 +118,10 @@ void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor b
                        torch::Tensor part_ml, torch::Tensor out);
 void head_gemv(torch::Tensor x, torch::Tensor W, torch::Tensor out);
 void host_gather(torch::Tensor table, torch::Tensor ids, int64_t fmt, int64_t dim, torch::Tensor out);
+void moe_gather_bf16(torch::Tensor x, int64_t k, torch::Tensor perm_row, torch::Tensor out);
+void ngram_ids(torch::Tensor ids, torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_slot,
+               torch::Tensor seq_has_state, torch::Tensor hist, int64_t n_orders, int64_t rows, bool write_state,
+               torch::Tensor out);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -210,6 +214,9 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out) -> ()");
   m.def("head_gemv(Tensor x, Tensor W, Tensor(a!) out) -> ()");
   m.def("host_gather(Tensor table, Tensor ids, int fmt, int dim, Tensor(a!) out) -> ()");
+  m.def("moe_gather_bf16(Tensor x, int k, Tensor perm_row, Tensor(a!) out) -> ()");
+  m.def("ngram_ids(Tensor ids, Tensor seq_start, Tensor seq_len, Tensor seq_slot, Tensor seq_has_state, "
+        "Tensor(a!) hist, int n_orders, int rows, bool write_state, Tensor(b!) out) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -260,6 +267,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("topk_select", &r9k::topk_select);
   m.impl("sparse_mla_decode", &r9k::sparse_mla_decode);
   m.impl("head_gemv", &r9k::head_gemv);
+  m.impl("moe_gather_bf16", &r9k::moe_gather_bf16);
+  m.impl("ngram_ids", &r9k::ngram_ids);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);

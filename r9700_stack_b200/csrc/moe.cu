@@ -340,4 +340,88 @@ void moe_combine(torch::Tensor y, torch::Tensor perm_row, torch::Tensor w, int64
               "moe_combine launch");
 }
 
+
+// ------------------------------------------------------------------------------------------------
+// bf16 gather: sorted row perm_row[a] <- token row a / k (for experts that take bf16 rows, e.g. the
+// trellis-coded experts' GEMV)
+// ------------------------------------------------------------------------------------------------
+__global__ void moe_gather_bf16_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, int H, int k,
+                                       const int32_t* __restrict__ perm_row, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int a = blockIdx.x;
+  const int p = perm_row[a];
+  if (p < 0) return;
+  const uint4* src = reinterpret_cast<const uint4*>(x + (int64_t)(a / k) * ldx);
+  uint4* dst = reinterpret_cast<uint4*>(out + (int64_t)p * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+void moe_gather_bf16(torch::Tensor x, int64_t k, torch::Tensor perm_row, torch::Tensor out) {
+  const int64_t A = perm_row.numel(), H = x.size(1);
+  TORCH_CHECK(H % 8 == 0 && x.stride(1) == 1 && x.stride(0) % 8 == 0 && out.is_contiguous(), "moe_gather_bf16: layout");
+  if (A == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(launch_pdl(moe_gather_bf16_kernel, dim3((unsigned)A), dim3(128), 0, at::cuda::getCurrentCUDAStream(),
+                         reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), (int)H, (int)k,
+                         perm_row.data_ptr<int32_t>(), reinterpret_cast<__nv_bfloat16*>(out.data_ptr())) == cudaSuccess,
+              "moe_gather_bf16 launch");
+}
+
+// ------------------------------------------------------------------------------------------------
+// n-gram hash ids of every token (Engram / n-gram embeddings): id_n(t) = hash(tokens t-n+1 .. t) mod
+// rows for n = 2 .. 1 + n_orders. Tokens before the step's chunk come from a per-state-slot history
+// of the last (max order - 1) tokens, which the kernel also advances when write_state is set
+// (one thread per sequence, after the hashes of that sequence are formed).
+// ------------------------------------------------------------------------------------------------
+constexpr int NG_HIST = 3;
+
+R9K_DEVINL int64_t ng_hash(const int32_t* win, int n, int order) {
+  int64_t h = 0x9E3779B1LL * 0 + order;
+  for (int j = 0; j < n; ++j) h = (h * 1000003LL + (int64_t)win[j] + 1) & 0x7FFFFFFFFFFFLL;
+  return h;
+}
+
+__global__ void ngram_ids_kernel(const int32_t* __restrict__ ids, const int32_t* __restrict__ seq_start,
+                                 const int32_t* __restrict__ seq_len, const int32_t* __restrict__ seq_slot,
+                                 const int32_t* __restrict__ seq_has_state, int32_t* __restrict__ hist, int S,
+                                 int n_orders, int64_t rows, int write_state, int64_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int s = blockIdx.x * blockDim.x + threadIdx.x;
+  if (s >= S) return;
+  const int t0 = seq_start[s], n = seq_len[s], slot = seq_slot[s];
+  int32_t win[NG_HIST + 1];
+  const bool hs = seq_has_state[s] != 0;
+  for (int j = 0; j < NG_HIST; ++j) win[j] = hs ? hist[slot * NG_HIST + j] : -1;  // oldest first
+  for (int i = 0; i < n; ++i) {
+    for (int j = 0; j < NG_HIST - 1; ++j) win[j] = win[j + 1];
+    win[NG_HIST - 1] = ids[t0 + i];
+    // order o uses the last o tokens of the window (missing history hashes as -1)
+    for (int o = 0; o < n_orders; ++o) {
+      const int order = o + 2;
+      int32_t w[NG_HIST];
+      for (int j = 0; j < order; ++j) w[j] = win[NG_HIST - order + j];
+      out[(int64_t)(t0 + i) * n_orders + o] = ng_hash(w, order, order) % rows;
+    }
+  }
+  if (write_state)
+    for (int j = 0; j < NG_HIST; ++j) hist[slot * NG_HIST + j] = win[j];
+}
+
+void ngram_ids(torch::Tensor ids, torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_slot,
+               torch::Tensor seq_has_state, torch::Tensor hist, int64_t n_orders, int64_t rows, bool write_state,
+               torch::Tensor out) {
+  const int64_t S = seq_start.size(0);
+  if (S == 0) return;
+  TORCH_CHECK(n_orders >= 1 && n_orders + 1 <= NG_HIST, "ngram_ids: orders 2..3");
+  TORCH_CHECK(hist.size(1) == NG_HIST && out.dtype() == torch::kInt64, "ngram_ids: hist [slots, 3], out int64");
+  const at::cuda::CUDAGuard guard(ids.device());
+  TORCH_CHECK(launch_pdl(ngram_ids_kernel, dim3((unsigned)((S + 63) / 64)), dim3(64), 0, at::cuda::getCurrentCUDAStream(),
+                         ids.data_ptr<int32_t>(), seq_start.data_ptr<int32_t>(), seq_len.data_ptr<int32_t>(),
+                         seq_slot.data_ptr<int32_t>(), seq_has_state.data_ptr<int32_t>(), hist.data_ptr<int32_t>(),
+                         (int)S, (int)n_orders, rows, write_state ? 1 : 0, out.data_ptr<int64_t>()) == cudaSuccess,
+              "ngram_ids launch");
+}
+
 }  // namespace r9k

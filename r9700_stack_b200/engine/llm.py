@@ -113,8 +113,11 @@ def build_model(cfg, par, device, seed=0, comm=None, max_ctx: int = 32768):
         from ..models.hybrid import HybridLM
 
         return HybridLM(cfg, par, device, seed=seed, comm=comm)
+    from ..models.dsv4 import DSV4Config, DSV4LM
     from ..models.mla_moe import MLAConfig, MLAMoELM
 
+    if isinstance(cfg, DSV4Config):
+        return DSV4LM(cfg, par, device, seed=seed, comm=comm, max_ctx=max_ctx)
     if isinstance(cfg, MLAConfig):
         return MLAMoELM(cfg, par, device, seed=seed, comm=comm, max_ctx=max_ctx)
     raise TypeError(f"unsupported model config {type(cfg)}")

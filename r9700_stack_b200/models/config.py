@@ -144,11 +144,39 @@ def tiny_hybrid(**kw) -> HybridConfig:
     return HybridConfig(**base)
 
 
+def _glm():
+    from .mla_moe import glm53_flash
+
+    return glm53_flash()
+
+
+def _tiny_mla():
+    from .mla_moe import tiny_mla
+
+    return tiny_mla()
+
+
+def _dsv4():
+    from .dsv4 import dsv41_flash
+
+    return dsv41_flash()
+
+
+def _tiny_dsv4():
+    from .dsv4 import tiny_dsv4
+
+    return tiny_dsv4()
+
+
 MODELS = {
     "dense27b": qwen27b_hybrid,
     "flashnext": flashnext_moe,
+    "glm53": _glm,
+    "dsv41": _dsv4,
     "tiny-hybrid": tiny_hybrid,
     "tiny-moe": tiny_moe,
+    "tiny-mla": _tiny_mla,
+    "tiny-dsv4": _tiny_dsv4,
 }
 
 

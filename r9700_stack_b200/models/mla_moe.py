@@ -118,6 +118,8 @@ class MLAMoELM:
     """Heads, FFN columns and experts are sharded over ``tp_size`` ranks; the indexer and the latent
     cache are replicated (every rank needs all positions' latent rows for its heads)."""
 
+    mx_experts = True  # routed experts as MXFP4 (subclasses with other expert formats turn this off)
+
     def __init__(self, cfg: MLAConfig, par: ParallelConfig | None = None, device="cuda", seed: int = 0, comm=None,
                  max_ctx: int = 32768):
         self.cfg = cfg
@@ -167,9 +169,10 @@ class MLAMoELM:
                 El, I = self.e_local, c.moe_ffn
                 lay["router"] = L.BF16Weight(wf.randn(c.moe_experts, H, dtype=torch.bfloat16))
                 lay["router_bias"] = (wf.randn(c.moe_experts, std=0.01)).float()
-                lay["e_gate"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
-                lay["e_up"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
-                lay["e_down"] = from_float(wr.randn(El * H, I), c.expert_format, tiled=True)
+                if self.mx_experts:
+                    lay["e_gate"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
+                    lay["e_up"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
+                    lay["e_down"] = from_float(wr.randn(El * H, I), c.expert_format, tiled=True)
                 if self.shared_local:
                     lay["s_gate"] = L.BF16Weight(bf(self.shared_local, H))
                     lay["s_up"] = L.BF16Weight(bf(self.shared_local, H))

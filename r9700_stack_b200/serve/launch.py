@@ -51,11 +51,15 @@ def plan(a) -> dict:
                       graph_batch_sizes=[int(x) for x in a.graph_sizes.split(",") if x],
                       spec_tokens=k, spec_method=a.spec if a.spec != "none" else "ngram")
     blocks = ec.num_kv_blocks or (ec.max_batch * math.ceil(ec.max_model_len / ec.kv_block) + 1)
-    hkv = max(1, cfg.n_kv_heads // world)
-    kv_bytes = len(cfg.attn_layers) * 2 * blocks * hkv * ec.kv_block * cfg.head_dim
-    hv = cfg.gdn_v_heads // world
-    state_b = 2 if cfg.gdn_state_dtype == "bf16" else 4
-    ssm_bytes = len(cfg.gdn_layers) * (ec.max_batch + 1) * hv * cfg.gdn_head_dim ** 2 * state_b
+    if hasattr(cfg, "attn_layers"):  # hybrid GDN / attention
+        hkv = max(1, cfg.n_kv_heads // world)
+        kv_bytes = len(cfg.attn_layers) * 2 * blocks * hkv * ec.kv_block * cfg.head_dim
+        hv = cfg.gdn_v_heads // world
+        state_b = 2 if cfg.gdn_state_dtype == "bf16" else 4
+        ssm_bytes = len(cfg.gdn_layers) * (ec.max_batch + 1) * hv * cfg.gdn_head_dim ** 2 * state_b
+    else:  # latent (MLA) cache: bf16 [512 | 64] rows + e4m3 indexer keys, replicated per rank
+        kv_bytes = cfg.layers * blocks * ec.kv_block * (576 * 2 + 128)
+        ssm_bytes = 0
     return {"model": cfg.name, "tp": world, "engine": ec.__dict__, "kv_blocks": blocks,
             "kv_cache_gb_per_rank": round(kv_bytes / 1e9, 2), "gdn_state_gb_per_rank": round(ssm_bytes / 1e9, 2),
             "cfg": cfg, "ec": ec}
