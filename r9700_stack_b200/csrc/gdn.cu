@@ -436,51 +436,50 @@ namespace r9k {
 // 512 threads: recurrence thread (c = tid / 4, rg = tid % 4) owns 32 contiguous dk rows of column c.
 // ------------------------------------------------------------------------------------------------
 template <typename ST>
-__global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
+__global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
     const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int z_off, int b_off, int a_off,
     const __nv_bfloat16* __restrict__ conv_w, ST* __restrict__ conv_state, ST* __restrict__ state,
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_has_state, const float* __restrict__ A_log,
     const float* __restrict__ dt_bias, const __nv_bfloat16* __restrict__ norm_w, float eps,
     uint8_t* __restrict__ out_q, uint8_t* __restrict__ out_sf, __nv_bfloat16* __restrict__ out_bf16) {
-  // grid (sequence, key head, value head within the key head's group); the rep CTAs of one key head
-  // form a cluster: all of them read the q/k conv state, and only after a cluster barrier does rank 0
-  // store its update (each CTA owns its value head's conv channels outright).
-  // The head's state (128 x 128) streams into shared memory with asynchronous copies issued before
-  // anything else, so four CTAs per SM keep 4 x 32 KB (bf16) of state reads in flight; thread
-  // (column c = tid / 2, half rg = tid % 2) then owns 64 entries and walks them in 16-entry pieces.
-  constexpr int D = 128, W = 4, PER = 64, PC = 16;
-  __shared__ float sq[D], sk[D], sv[D], so[D], sred[8];
-  __shared__ float snew[3 * D][W - 1];
-  __shared__ float sg, sb;
+  // grid (sequence, key head): the CTA owns the key head's q / k channels and its rep value heads,
+  // so it updates all of their conv state itself. Every value head's state (128 x 128) is requested
+  // with asynchronous copies before anything else (rep x 32 KB in flight per CTA for bf16 state),
+  // then the heads are updated one after another out of shared memory.
+  // Thread (column c = tid / 2, half rg = tid % 2) owns 64 entries of a column per head.
+  constexpr int D = 128, W = 4, PER = 64, PC = 16, MAXREP = 8;
+  __shared__ float sq[2][PER + 1], sk[2][PER + 1];  // [half][row]: the halves sit in different banks
+  __shared__ float sv[MAXREP][D], so[2][D], sred[2][8];
+  __shared__ float sg[MAXREP], sb[MAXREP];
   extern __shared__ __align__(16) uint8_t s_state[];
-  const int t = blockIdx.x, kh = blockIdx.y, j = blockIdx.z;
+  const int t = blockIdx.x, kh = blockIdx.y;
   const int rep = Hv / Hk;
-  const int h = kh * rep + j;
   const int tid = threadIdx.x;
   const int C = 2 * Hk * D + Hv * D;
   const int slot = seq_slot[t];  // step metadata: copied in before the forward began
   const bool hs = seq_has_state[t] != 0;
   const int c = tid >> 1, rg = tid & 1;
-  ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * PER;
-  // 16-byte chunk v of thread tid lives at chunk index v * 256 + tid: a warp's accesses to one chunk
-  // are consecutive (conflict-free), where a per-thread contiguous layout would put all 32 lanes of
-  // a warp in the same banks
-  constexpr int NV = PER * sizeof(ST) / 16;  // chunks per thread
+  constexpr int NV = PER * sizeof(ST) / 16;  // 16-byte chunks per thread and head
   uint4* sS = reinterpret_cast<uint4*>(s_state);
+  // chunk v of thread tid for head j at (j * NV + v) * 256 + tid: conflict-free
   if (hs) {
+    for (int j = 0; j < rep; ++j) {
+      const ST* Sp = state + (((int64_t)slot * Hv + kh * rep + j) * D + c) * D + rg * PER;
 #pragma unroll
-    for (int v = 0; v < NV; ++v)
-      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + v * 256 + tid)),
-                   "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
+      for (int v = 0; v < NV; ++v)
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + (j * NV + v) * 256 + tid)),
+                     "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
+    }
   }
   asm volatile("cp.async.commit_group;" ::: "memory");
   pdl_wait();
   pdl_trigger();
-  // ---- conv over q (128) | k (128) | this value head (128) channels
-  for (int ch = tid; ch < 3 * D; ch += 256) {
+  // ---- conv over q (128) | k (128) | the rep value heads (rep x 128) channels
+  const int nch = (2 + rep) * D;
+  for (int ch = tid; ch < nch; ch += 256) {
     const int part = ch / D, i = ch % D;
-    const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + h * D + i;
-    const ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
+    const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + (kh * rep + part - 2) * D + i;
+    ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
     float x[W];
 #pragma unroll
     for (int w = 0; w < W - 1; ++w) x[w] = hs ? to_f<ST>(cs[w]) : 0.f;
@@ -489,112 +488,112 @@ __global__ void __launch_bounds__(256, 4) gdn_decode_fused_kernel(
 #pragma unroll
     for (int w = 0; w < W; ++w) acc += x[w] * __bfloat162float(conv_w[(int64_t)cch * W + w]);
 #pragma unroll
-    for (int w = 0; w < W - 1; ++w) snew[ch][w] = x[w + 1];
+    for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(x[w + 1]);
     const float y = silu_f(acc);
-    if (part == 0) sq[i] = y;
-    else if (part == 1) sk[i] = y;
-    else sv[i] = y;
+    if (part == 0) sq[i / PER][i % PER] = y;
+    else if (part == 1) sk[i / PER][i % PER] = y;
+    else sv[part - 2][i] = y;
   }
-  if (tid == 0) {
+  if (tid < rep) {
+    const int h = kh * rep + tid;
     const float av = __bfloat162float(proj[(int64_t)t * ld + a_off + h]);
     const float bv = __bfloat162float(proj[(int64_t)t * ld + b_off + h]);
-    sg = __expf(-__expf(A_log[h]) * softplus_f(av + dt_bias[h]));  // decay factor exp(g)
-    sb = sigmoid_f(bv);
+    sg[tid] = __expf(-__expf(A_log[h]) * softplus_f(av + dt_bias[h]));  // decay factor exp(g)
+    sb[tid] = sigmoid_f(bv);
   }
-  // every CTA of the cluster has read the shared q/k conv state before rank 0 overwrites it
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-  for (int ch = tid; ch < 3 * D; ch += 256) {
-    const int part = ch / D, i = ch % D;
-    if (part == 2 || j == 0) {
-      const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + h * D + i;
-      ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
-#pragma unroll
-      for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(snew[ch][w]);
-    }
-  }
+  __syncthreads();
   // ---- l2 norms of q and k (warps 0 and 1)
   if (tid < 64) {
-    const float* src = tid < 32 ? sq : sk;
+    const float* src = tid < 32 ? &sq[0][0] : &sk[0][0];
     const int l = tid & 31;
     float ss = 0.f;
 #pragma unroll
-    for (int jj = 0; jj < 4; ++jj) ss += src[l + 32 * jj] * src[l + 32 * jj];
+    for (int jj = 0; jj < 4; ++jj) {
+      const int i = l + 32 * jj;
+      const float v = src[(i / PER) * (PER + 1) + i % PER];
+      ss += v * v;
+    }
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    if (l == 0) sred[tid >> 5] = rsqrtf(ss + 1e-6f);
+    if (l == 0) sred[0][tid >> 5] = rsqrtf(ss + 1e-6f);
   }
   asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
-  const float qs = sred[0] * rsqrtf((float)D), ks = sred[1];
-  const float decay = sg;
-  const float* kk = sk + rg * PER;
-  const float* qq = sq + rg * PER;
-  float kvs = 0.f;
+  const float qs = sred[0][0] * rsqrtf((float)D), ks = sred[0][1];
+  const float* kk = sk[rg];
+  const float* qq = sq[rg];
+  for (int j = 0; j < rep; ++j) {
+    const int h = kh * rep + j;
+    ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * PER;
+    const float decay = sg[j];
+    float kvs = 0.f;
 #pragma unroll 1
-  for (int p = 0; p < PER / PC; ++p) {
-    float S[PC];
-    if (hs) {
-      constexpr int CPP = NV / (PER / PC);  // chunks per 16-entry piece
-      uint4 raw[CPP];
+    for (int p = 0; p < PER / PC; ++p) {
+      float S[PC];
+      if (hs) {
+        constexpr int CPP = NV / (PER / PC);
+        uint4 raw[CPP];
 #pragma unroll
-      for (int q = 0; q < CPP; ++q) raw[q] = sS[(p * CPP + q) * 256 + tid];
-      StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
-    } else {
+        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * 256 + tid];
+        StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
+      } else {
 #pragma unroll
-      for (int r = 0; r < PC; ++r) S[r] = 0.f;
+        for (int r = 0; r < PC; ++r) S[r] = 0.f;
+      }
+#pragma unroll
+      for (int r = 0; r < PC; ++r) kvs += S[r] * kk[p * PC + r];
     }
-#pragma unroll
-    for (int r = 0; r < PC; ++r) kvs += S[r] * kk[p * PC + r];
-  }
-  kvs *= ks;
-  kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
-  const float delta = sb * (sv[c] - decay * kvs);
-  const float dk = delta * ks;
-  float ov = 0.f;
+    kvs *= ks;
+    kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
+    const float delta = sb[j] * (sv[j][c] - decay * kvs);
+    const float dk = delta * ks;
+    float ov = 0.f;
 #pragma unroll 1
-  for (int p = 0; p < PER / PC; ++p) {
-    float S[PC];
-    if (hs) {
-      constexpr int CPP = NV / (PER / PC);  // chunks per 16-entry piece
-      uint4 raw[CPP];
+    for (int p = 0; p < PER / PC; ++p) {
+      float S[PC];
+      if (hs) {
+        constexpr int CPP = NV / (PER / PC);
+        uint4 raw[CPP];
 #pragma unroll
-      for (int q = 0; q < CPP; ++q) raw[q] = sS[(p * CPP + q) * 256 + tid];
-      StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
-    } else {
+        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * 256 + tid];
+        StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
+      } else {
 #pragma unroll
-      for (int r = 0; r < PC; ++r) S[r] = 0.f;
+        for (int r = 0; r < PC; ++r) S[r] = 0.f;
+      }
+#pragma unroll
+      for (int r = 0; r < PC; ++r) {
+        S[r] = S[r] * decay + kk[p * PC + r] * dk;
+        ov += S[r] * qq[p * PC + r];
+      }
+      StateVec16<ST>::store(Sp + p * PC, S);
     }
-#pragma unroll
-    for (int r = 0; r < PC; ++r) {
-      S[r] = S[r] * decay + kk[p * PC + r] * dk;
-      ov += S[r] * qq[p * PC + r];
-    }
-    StateVec16<ST>::store(Sp + p * PC, S);
-  }
-  ov *= qs;
-  ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-  if (rg == 0) so[c] = ov;
-  __syncthreads();
-  // ---- RMSNormGated + MXFP8 of this head (warps 0..3, lane l owns column 32 * warp + l)
-  if (tid < D) {
-    const float o = so[tid];
-    float ss = o * o;
-    for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
-    if ((tid & 31) == 0) sred[2 + (tid >> 5)] = ss;
-  }
-  __syncthreads();
-  if (tid < D) {
-    const float rr = rsqrtf((sred[2] + sred[3] + sred[4] + sred[5]) / (float)D + eps);
-    const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tid]);
-    float val = so[tid] * rr * __bfloat162float(norm_w[tid]) * silu_f(z);
-    val = __bfloat162float(__float2bfloat16(val));
-    const int64_t oi = (int64_t)t * Hv * D + h * D + tid;
-    if (out_bf16 != nullptr) out_bf16[oi] = __float2bfloat16(val);
-    if (out_q != nullptr) {
-      float am = fabsf(val);
-      for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
-      const int e = mx_exponent(am, 448.f);
-      out_q[oi] = f32_to_e4m3(val * exp2i(-e));
-      if ((tid & 31) == 0) out_sf[sf_offset(t, (h * D + tid) >> 5, Hv * D / 32)] = (uint8_t)(e + 127);
+    ov *= qs;
+    ov += __shfl_xor_sync(0xffffffffu, ov, 1);
+    if (rg == 0) so[j & 1][c] = ov;
+    // ---- RMSNormGated + MXFP8 of this head: warps 4 * (j & 1) .. + 3 (column 32 * warp' + lane)
+    __syncthreads();
+    const int half = (tid >> 7), tt = tid & 127;
+    if (half == (j & 1)) {
+      const float o = so[j & 1][tt];
+      float ss = o * o;
+      for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
+      if ((tt & 31) == 0) sred[1][(j & 1) * 4 + (tt >> 5)] = ss;
+      if (j & 1) asm volatile("bar.sync 2, 128;" ::: "memory");
+      else asm volatile("bar.sync 1, 128;" ::: "memory");
+      const float* sr = &sred[1][(j & 1) * 4];
+      const float rr = rsqrtf((sr[0] + sr[1] + sr[2] + sr[3]) / (float)D + eps);
+      const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tt]);
+      float val = o * rr * __bfloat162float(norm_w[tt]) * silu_f(z);
+      val = __bfloat162float(__float2bfloat16(val));
+      const int64_t oi = (int64_t)t * Hv * D + h * D + tt;
+      if (out_bf16 != nullptr) out_bf16[oi] = __float2bfloat16(val);
+      if (out_q != nullptr) {
+        float am = fabsf(val);
+        for (int s2 = 16; s2 > 0; s2 >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, s2));
+        const int e = mx_exponent(am, 448.f);
+        out_q[oi] = f32_to_e4m3(val * exp2i(-e));
+        if ((tt & 31) == 0) out_sf[sf_offset(t, (h * D + tt) >> 5, Hv * D / 32)] = (uint8_t)(e + 127);
+      }
     }
   }
 }
@@ -617,24 +616,21 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   };
   __nv_bfloat16* ob = (out_bf16.has_value() && out_bf16->defined()) ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)S, (unsigned)Hk, (unsigned)rep);
+  cfg.gridDim = dim3((unsigned)S, (unsigned)Hk, 1);
   cfg.blockDim = dim3(256);
-  cfg.dynamicSmemBytes = (size_t)128 * 128 * state.element_size();
+  cfg.dynamicSmemBytes = (size_t)rep * 128 * 128 * state.element_size();
+  TORCH_CHECK(cfg.dynamicSmemBytes <= 200 * 1024, "gdn_decode_fused: value heads per key head x state size exceed shared memory");
   cfg.stream = st;
-  cudaLaunchAttribute attr[2];
+  cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  attr[1].id = cudaLaunchAttributeClusterDimension;
-  attr[1].val.clusterDim.x = 1;
-  attr[1].val.clusterDim.y = 1;
-  attr[1].val.clusterDim.z = (unsigned)rep;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = 1;
 #define R9K_GDF(ST_T)                                                                                                 \
   {                                                                                                                   \
     static bool attr_done = false;                                                                                    \
     if (!attr_done) {                                                                                                 \
-      cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4); \
+      cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
       attr_done = true;                                                                                               \
     }                                                                                                                 \
   }                                                                                                                   \
