@@ -436,7 +436,7 @@ namespace r9k {
 // 512 threads: recurrence thread (c = tid / 4, rg = tid % 4) owns 32 contiguous dk rows of column c.
 // ------------------------------------------------------------------------------------------------
 template <typename ST>
-__global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
+__global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
     const __nv_bfloat16* __restrict__ proj, int64_t ld, int Hk, int Hv, int z_off, int b_off, int a_off,
     const __nv_bfloat16* __restrict__ conv_w, ST* __restrict__ conv_state, ST* __restrict__ state,
     const int32_t* __restrict__ seq_slot, const int32_t* __restrict__ seq_has_state, const float* __restrict__ A_log,
@@ -446,10 +446,10 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
   // so it updates all of their conv state itself. Every value head's state (128 x 128) is requested
   // with asynchronous copies before anything else (rep x 32 KB in flight per CTA for bf16 state),
   // then the heads are updated one after another out of shared memory.
-  // Thread (column c = tid / 2, half rg = tid % 2) owns 64 entries of a column per head.
-  constexpr int D = 128, W = 4, PER = 64, PC = 16, MAXREP = 8;
-  __shared__ float sq[2][PER + 1], sk[2][PER + 1];  // [half][row]: the halves sit in different banks
-  __shared__ float sv[MAXREP][D], so[2][D], sred[2][8];
+  // Thread (column c = tid / 4, quarter rg = tid % 4) owns 32 entries of a column per head.
+  constexpr int D = 128, W = 4, PER = 32, PC = 16, MAXREP = 8, NT = 512, NG = D / PER;
+  __shared__ float sq[NG][PER + 1], sk[NG][PER + 1];  // [quarter][row]: quarters sit in different banks
+  __shared__ float sv[MAXREP][D], so[4][D], sred[2][16];
   __shared__ float sg[MAXREP], sb[MAXREP];
   extern __shared__ __align__(16) uint8_t s_state[];
   const int t = blockIdx.x, kh = blockIdx.y;
@@ -458,16 +458,16 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
   const int C = 2 * Hk * D + Hv * D;
   const int slot = seq_slot[t];  // step metadata: copied in before the forward began
   const bool hs = seq_has_state[t] != 0;
-  const int c = tid >> 1, rg = tid & 1;
+  const int c = tid >> 2, rg = tid & 3;
   constexpr int NV = PER * sizeof(ST) / 16;  // 16-byte chunks per thread and head
   uint4* sS = reinterpret_cast<uint4*>(s_state);
-  // chunk v of thread tid for head j at (j * NV + v) * 256 + tid: conflict-free
+  // chunk v of thread tid for head j at (j * NV + v) * NT + tid: conflict-free
   if (hs) {
     for (int j = 0; j < rep; ++j) {
       const ST* Sp = state + (((int64_t)slot * Hv + kh * rep + j) * D + c) * D + rg * PER;
 #pragma unroll
       for (int v = 0; v < NV; ++v)
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + (j * NV + v) * 256 + tid)),
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + (j * NV + v) * NT + tid)),
                      "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
     }
   }
@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
   pdl_trigger();
   // ---- conv over q (128) | k (128) | the rep value heads (rep x 128) channels
   const int nch = (2 + rep) * D;
-  for (int ch = tid; ch < nch; ch += 256) {
+  for (int ch = tid; ch < nch; ch += NT) {
     const int part = ch / D, i = ch % D;
     const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + (kh * rep + part - 2) * D + i;
     ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
@@ -533,7 +533,7 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
         constexpr int CPP = NV / (PER / PC);
         uint4 raw[CPP];
 #pragma unroll
-        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * 256 + tid];
+        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * NT + tid];
         StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
       } else {
 #pragma unroll
@@ -544,6 +544,7 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
     }
     kvs *= ks;
     kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
+    kvs += __shfl_xor_sync(0xffffffffu, kvs, 2);
     const float delta = sb[j] * (sv[j][c] - decay * kvs);
     const float dk = delta * ks;
     float ov = 0.f;
@@ -554,7 +555,7 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
         constexpr int CPP = NV / (PER / PC);
         uint4 raw[CPP];
 #pragma unroll
-        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * 256 + tid];
+        for (int q = 0; q < CPP; ++q) raw[q] = sS[(j * NV + p * CPP + q) * NT + tid];
         StateVec16<ST>::load(reinterpret_cast<const ST*>(raw), S);
       } else {
 #pragma unroll
@@ -569,18 +570,24 @@ __global__ void __launch_bounds__(256, 2) gdn_decode_fused_kernel(
     }
     ov *= qs;
     ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-    if (rg == 0) so[j & 1][c] = ov;
-    // ---- RMSNormGated + MXFP8 of this head: warps 4 * (j & 1) .. + 3 (column 32 * warp' + lane)
+    ov += __shfl_xor_sync(0xffffffffu, ov, 2);
+    const int gq = j & 3;  // the group of 128 threads that finishes this head
+    if (rg == 0) so[gq][c] = ov;
+    // ---- RMSNormGated + MXFP8 of this head: warps 4 gq .. 4 gq + 3 (column 32 * warp' + lane)
     __syncthreads();
-    const int half = (tid >> 7), tt = tid & 127;
-    if (half == (j & 1)) {
-      const float o = so[j & 1][tt];
+    const int grp = (tid >> 7), tt = tid & 127;
+    if (grp == gq) {
+      const float o = so[gq][tt];
       float ss = o * o;
       for (int s2 = 16; s2 > 0; s2 >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, s2);
-      if ((tt & 31) == 0) sred[1][(j & 1) * 4 + (tt >> 5)] = ss;
-      if (j & 1) asm volatile("bar.sync 2, 128;" ::: "memory");
-      else asm volatile("bar.sync 1, 128;" ::: "memory");
-      const float* sr = &sred[1][(j & 1) * 4];
+      if ((tt & 31) == 0) sred[1][gq * 4 + (tt >> 5)] = ss;
+      switch (gq) {
+        case 0: asm volatile("bar.sync 1, 128;" ::: "memory"); break;
+        case 1: asm volatile("bar.sync 2, 128;" ::: "memory"); break;
+        case 2: asm volatile("bar.sync 3, 128;" ::: "memory"); break;
+        default: asm volatile("bar.sync 4, 128;" ::: "memory"); break;
+      }
+      const float* sr = &sred[1][gq * 4];
       const float rr = rsqrtf((sr[0] + sr[1] + sr[2] + sr[3]) / (float)D + eps);
       const float z = __bfloat162float(proj[(int64_t)t * ld + z_off + h * D + tt]);
       float val = o * rr * __bfloat162float(norm_w[tt]) * silu_f(z);
@@ -617,7 +624,7 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   __nv_bfloat16* ob = (out_bf16.has_value() && out_bf16->defined()) ? reinterpret_cast<__nv_bfloat16*>(out_bf16->data_ptr()) : nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)S, (unsigned)Hk, 1);
-  cfg.blockDim = dim3(256);
+  cfg.blockDim = dim3(512);
   cfg.dynamicSmemBytes = (size_t)rep * 128 * 128 * state.element_size();
   TORCH_CHECK(cfg.dynamicSmemBytes <= 200 * 1024, "gdn_decode_fused: value heads per key head x state size exceed shared memory");
   cfg.stream = st;
