@@ -78,7 +78,7 @@ void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cach
                     torch::Tensor tok_ctx, torch::Tensor seq_start, torch::Tensor seq_len, double sm_scale,
                     double k_scale, double v_scale, torch::Tensor part_o, torch::Tensor part_ml,
                     c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
-                    c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status);
+                    c10::optional<torch::Tensor> out_q, c10::optional<torch::Tensor> out_sf, torch::Tensor status, int64_t max_rows);
 void attn_tc_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                      torch::Tensor tok_ctx, torch::Tensor tile_tab, int64_t ntiles, double sm_scale, double k_scale,
                      double v_scale, c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
@@ -184,7 +184,7 @@ TORCH_LIBRARY(r9k, m) {
   m.def("attn_tc_decode(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_ctx, "
         "Tensor seq_start, Tensor seq_len, float sm_scale, float k_scale, float v_scale, Tensor(a!) part_o, "
         "Tensor(b!) part_ml, Tensor? gate, Tensor(c!)? out, Tensor(d!)? out_q, Tensor(e!)? out_sf, "
-        "Tensor(f!) status) -> ()");
+        "Tensor(f!) status, int max_rows=0) -> ()");
   m.def("attn_tc_prefill(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_ctx, "
         "Tensor tile_tab, int ntiles, float sm_scale, float k_scale, float v_scale, Tensor? gate, "
         "Tensor(a!)? out, Tensor(b!)? out_q, Tensor(c!)? out_sf, Tensor(d!) status) -> ()");

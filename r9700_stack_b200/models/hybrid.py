@@ -294,12 +294,17 @@ class HybridLM:
                                    _status.status(self.device))
         else:
             S = meta.seq_start.shape[0]
-            nsplit = max(1, min(ws.nsplit_max, -(-296 // (S * hkv))))
+            max_rows = max(n for _, n in meta.host_seqs) if meta.host_seqs else 1
+            if max_rows * G <= 16:
+                # keys-on-M decode kernel: one CTA per SM, so one wave of splits over the 148 SMs
+                nsplit = max(1, min(ws.nsplit_max, 148 // (S * hkv)))
+            else:
+                nsplit = max(1, min(ws.nsplit_max, -(-296 // (S * hkv))))
             po = ws.part_o.view(-1)[: T * hq * nsplit * D].view(T * hq, nsplit, D)
             pml = ws.part_ml.view(-1)[: T * hq * nsplit * 2].view(T * hq, nsplit, 2)
             _ops().attn_tc_decode(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, meta.seq_start, meta.seq_len,
                                   self.sm_scale, self.k_scale, self.v_scale, po, pml, gate, out_bf, out_q, out_sf,
-                                  _status.status(self.device))
+                                  _status.status(self.device), max_rows)
         return ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"]
 
     def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):

@@ -226,6 +226,37 @@ def bench_gdn(a) -> dict:
             "weight_bytes": 2.0 * per, "flops": 0.0}
 
 
+def bench_attn(a) -> dict:
+    """tcgen05 split-KV decode attention over a paged fp8 KV cache: S sequences x ctx positions,
+    hq / hkv heads of 256, one query token per sequence (the decode shape of the dense model)."""
+    from .. import _native
+    from ..utils import status
+
+    torch.manual_seed(0)
+    S, ctx, hq, hkv, D, BLK = a.S, a.ctx, a.hq, a.hkv, 256, 64
+    nbps = (ctx + BLK - 1) // BLK
+    nblk = S * nbps + 1
+    kc = torch.randint(0, 255, (nblk, hkv, BLK, D), dtype=torch.uint8, device="cuda") & 0x7E
+    vc = torch.randint(0, 255, (nblk, hkv, BLK, D), dtype=torch.uint8, device="cuda") & 0x7E
+    bt = (torch.arange(S * nbps, dtype=torch.int32, device="cuda") + 1).view(S, nbps)
+    q = torch.randn(S, hq, D, device="cuda").bfloat16()
+    tok_ctx = torch.full((S,), ctx, dtype=torch.int32, device="cuda")
+    st0 = torch.arange(S, dtype=torch.int32, device="cuda")
+    ln = torch.ones(S, dtype=torch.int32, device="cuda")
+    nsplit = a.nsplit or max(1, min(16, 148 // (S * hkv)))
+    po = torch.empty(S * hq, nsplit, D, device="cuda")
+    pml = torch.empty(S * hq, nsplit, 2, device="cuda")
+    out = torch.empty(S, hq * D, dtype=torch.bfloat16, device="cuda")
+    ops = _native.ops()
+    stt = status.status()
+    f = lambda i: ops.attn_tc_decode(q, kc, vc, bt, tok_ctx, st0, ln, D ** -0.5, 1.0, 1.0, po, pml, None, out, None,
+                                     None, stt)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    kv_bytes = 2.0 * S * ctx * hkv * D
+    return {"kernel": "attn_tc_decode", "S": S, "ctx": ctx, "hq": hq, "hkv": hkv, "nsplit": nsplit, "us": us,
+            "weight_bytes": kv_bytes, "flops": 4.0 * S * hq * ctx * D}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -253,12 +284,18 @@ def main(argv=None):
     gd.add_argument("--Hk", type=int, default=16)
     gd.add_argument("--Hv", type=int, default=48)
     gd.add_argument("--state", choices=["bf16", "fp32"], default="bf16")
-    for p in (g, m, d, gd):
+    at = sub.add_parser("attn")
+    at.add_argument("--S", type=int, default=16)
+    at.add_argument("--ctx", type=int, default=8192)
+    at.add_argument("--hq", type=int, default=24)
+    at.add_argument("--hkv", type=int, default=4)
+    at.add_argument("--nsplit", type=int, default=0)
+    for p in (g, m, d, gd, at):
         p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn}[a.cmd](a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn, "attn": bench_attn}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:
         r["gbs"] = r["weight_bytes"] / r["us"] / 1e3

@@ -189,7 +189,7 @@ def test_decode_graph_replay_equals_eager():
 
 
 @pytest.mark.parametrize("heads", [(12, 2), (3, 1), (2, 1)])
-@pytest.mark.parametrize("case", ["decode", "verify", "prefill"])
+@pytest.mark.parametrize("case", ["decode", "verify", "verify_rowtile", "prefill"])
 def test_attn_tc_matches_simple_kernel(case, heads):
     """tcgen05 flash attention (split-KV decode / prefill tiles) vs the CUDA-core kernel above; the
     head counts cover TP1 (24/4 -> 12/2 per rank at TP2), TP8 (3 q heads on a replicated kv head) and
@@ -200,7 +200,9 @@ def test_attn_tc_matches_simple_kernel(case, heads):
     G = Hq // Hkv
     if case == "decode":
         ctxs, nq = [1, 63, 200, 1000, 2049], [1, 1, 1, 1, 1]
-    elif case == "verify":
+    elif case == "verify":  # up to 16 query rows per sequence: the keys-on-M kernel
+        ctxs, nq = [9, 300, 777], [max(1, 16 // G), 2, 1]
+    elif case == "verify_rowtile":
         ctxs, nq = [9, 300, 777], [8, 3, 5]
     else:
         ctxs, nq = [100, 700], [100, 450]
@@ -241,8 +243,9 @@ def test_attn_tc_matches_simple_kernel(case, heads):
         nsplit = 4
         po = torch.zeros(T * Hq, nsplit, D, device="cuda")
         pml = torch.zeros(T * Hq, nsplit, 2, device="cuda")
+        # verify with max_rows = 16 // G takes the keys-on-M kernel (up to 16 rows), without it the row-tile one
         _ops().attn_tc_decode(q, kc, vc, bt.cuda(), i32(tok_ctx), i32(starts), i32(nq), scale, 1.0, 1.0, po, pml,
-                              gate, out, None, None, st)
+                              gate, out, None, None, st, (16 // G) if case == "verify" else 0)
     _check()
     # fp8 Q and P inside the tensor-core kernel: compare with a tolerance relative to the output scale
     err = (out.float() - ref.float()).abs()
