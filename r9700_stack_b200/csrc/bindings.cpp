@@ -122,6 +122,9 @@ void moe_gather_bf16(torch::Tensor x, int64_t k, torch::Tensor perm_row, torch::
 void ngram_ids(torch::Tensor ids, torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_slot,
                torch::Tensor seq_has_state, torch::Tensor hist, int64_t n_orders, int64_t rows, bool write_state,
                torch::Tensor out);
+void symm_collective(int64_t mode, torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_t rank,
+                     int64_t world, int64_t slot_bytes, torch::Tensor seq, torch::Tensor status, double timeout_s);
+int64_t symm_collective_region_bytes(int64_t slot_bytes);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -217,6 +220,8 @@ TORCH_LIBRARY(r9k, m) {
   m.def("moe_gather_bf16(Tensor x, int k, Tensor perm_row, Tensor(a!) out) -> ()");
   m.def("ngram_ids(Tensor ids, Tensor seq_start, Tensor seq_len, Tensor seq_slot, Tensor seq_has_state, "
         "Tensor(a!) hist, int n_orders, int rows, bool write_state, Tensor(b!) out) -> ()");
+  m.def("symm_collective(int mode, Tensor x, Tensor(a!) out, Tensor peers, int rank, int world, int slot_bytes, "
+        "Tensor(b!) seq, Tensor(c!) status, float timeout_s) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -269,6 +274,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("head_gemv", &r9k::head_gemv);
   m.impl("moe_gather_bf16", &r9k::moe_gather_bf16);
   m.impl("ngram_ids", &r9k::ngram_ids);
+  m.impl("symm_collective", &r9k::symm_collective);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);
@@ -281,6 +287,7 @@ TORCH_LIBRARY_FRAGMENT(r9k, m) {
   m.def("symm_ipc_handle(int ptr) -> Tensor", &r9k::symm_ipc_handle);
   m.def("symm_open(Tensor handle) -> int", &r9k::symm_open);
   m.def("symm_close(int ptr) -> ()", &r9k::symm_close);
+  m.def("symm_collective_region_bytes(int slot_bytes) -> int", &r9k::symm_collective_region_bytes);
   m.def("symm_view(int ptr, int offset_bytes, int rows, int cols, int device) -> Tensor", &r9k::symm_view);
 }
 
