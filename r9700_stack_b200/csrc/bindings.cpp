@@ -125,6 +125,11 @@ void ngram_ids(torch::Tensor ids, torch::Tensor seq_start, torch::Tensor seq_len
 void symm_collective(int64_t mode, torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_t rank,
                      int64_t world, int64_t slot_bytes, torch::Tensor seq, torch::Tensor status, double timeout_s);
 int64_t symm_collective_region_bytes(int64_t slot_bytes);
+void lru_route(torch::Tensor ids, int64_t e0, int64_t E, int64_t S, torch::Tensor slot_of, torch::Tensor expert_of,
+               torch::Tensor stamp, torch::Tensor clock, torch::Tensor miss_e, torch::Tensor miss_s,
+               torch::Tensor miss_count, torch::Tensor counters, torch::Tensor slot_ids, torch::Tensor status);
+void expert_copy(std::vector<torch::Tensor> srcs, std::vector<torch::Tensor> dsts, std::vector<int64_t> bytes,
+                 torch::Tensor miss_e, torch::Tensor miss_s, torch::Tensor miss_count, int64_t max_misses);
 void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
                    torch::Tensor state, torch::Tensor seq_slot, torch::Tensor seq_start, torch::Tensor seq_len,
                    torch::Tensor seq_has_state, bool write_state, c10::optional<torch::Tensor> o);
@@ -222,6 +227,11 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(a!) hist, int n_orders, int rows, bool write_state, Tensor(b!) out) -> ()");
   m.def("symm_collective(int mode, Tensor x, Tensor(a!) out, Tensor peers, int rank, int world, int slot_bytes, "
         "Tensor(b!) seq, Tensor(c!) status, float timeout_s) -> ()");
+  m.def("lru_route(Tensor ids, int e0, int E, int S, Tensor(a!) slot_of, Tensor(b!) expert_of, Tensor(c!) stamp, "
+        "Tensor(d!) clock, Tensor(e!) miss_e, Tensor(f!) miss_s, Tensor(g!) miss_count, Tensor(h!) counters, "
+        "Tensor(i!) slot_ids, Tensor(j!) status) -> ()");
+  m.def("expert_copy(Tensor[] srcs, Tensor(a!)[] dsts, int[] bytes, Tensor miss_e, Tensor miss_s, Tensor miss_count, "
+        "int max_misses) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
@@ -275,6 +285,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("moe_gather_bf16", &r9k::moe_gather_bf16);
   m.impl("ngram_ids", &r9k::ngram_ids);
   m.impl("symm_collective", &r9k::symm_collective);
+  m.impl("lru_route", &r9k::lru_route);
+  m.impl("expert_copy", &r9k::expert_copy);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);

@@ -53,26 +53,30 @@ class MoEBuffers:
 
 def moe_ffn(lay, x: torch.Tensor, mb: MoEBuffers, out: torch.Tensor, *, k: int, e0: int, E_local: int, moe_ffn: int,
             hidden: int, shared_local: int, route_mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
-            scale: float = 1.0, renorm: bool = True) -> None:
+            scale: float = 1.0, renorm: bool = True, remap=None, route: bool = True, gemm_E: int = 0) -> None:
     """Routed experts + shared expert for the T rows of x (bf16) into out (bf16), with the router
     weights applied and summed in one rounding (moe_combine). Experts outside [e0, e0 + E_local)
     belong to other ranks: their rows are skipped and the caller's all-reduce sums the partials."""
     T = x.shape[0]
     o = _ops()
     dev = x.device
-    L.bf16_linear(x, lay["router"], out=mb.logits_e[:T], out_dtype=torch.float32)
-    o.moe_route(mb.logits_e[:T], k, route_mode, bias, n_group, topk_group, float(scale), renorm, mb.ids[:T], mb.wts[:T])
+    if route:  # (passes over groups of experts reuse the first pass's routing)
+        L.bf16_linear(x, lay["router"], out=mb.logits_e[:T], out_dtype=torch.float32)
+        o.moe_route(mb.logits_e[:T], k, route_mode, bias, n_group, topk_group, float(scale), renorm, mb.ids[:T],
+                    mb.wts[:T])
     BN = 16 if T <= 16 else 128
     A = T * k
-    o.moe_align(mb.ids[:T], e0, E_local, BN, mb.perm_row[:A], mb.seg_start, mb.work, mb.work_count)
+    ids = mb.ids[:T] if remap is None else remap(mb.ids[:T])  # expert ids, or cache slot ids
+    o.moe_align(ids, e0, E_local, BN, mb.perm_row[:A], mb.seg_start, mb.work, mb.work_count)
     L.quant_act(x, out=mb.moe_act.narrow(T))
     o.moe_gather(mb.moe_act.q[:T], mb.moe_act.sf, k, mb.perm_row[:A], mb.sorted_act.q, mb.sorted_act.sf)
     nwork = min(mb.max_work, -(-A // BN) + min(E_local, A))
+    GE = gemm_E or E_local  # experts held by the weight arrays (the work list indexes the first E_local)
     o.gemm_mx_grouped(lay["e_gate"].q, lay["e_gate"].sf, lay["e_up"].q, lay["e_up"].sf, True, mb.sorted_act.q,
-                      mb.sorted_act.sf, mb.work[:nwork], mb.work_count, moe_ffn, E_local, BN, mb.h_act.q, mb.h_act.sf,
+                      mb.sorted_act.sf, mb.work[:nwork], mb.work_count, moe_ffn, GE, BN, mb.h_act.q, mb.h_act.sf,
                       _status(dev))
     o.gemm_mx_grouped(lay["e_down"].q, lay["e_down"].sf, None, None, True, mb.h_act.q, mb.h_act.sf, mb.work[:nwork],
-                      mb.work_count, hidden, E_local, BN, mb.y_sorted, None, _status(dev))
+                      mb.work_count, hidden, GE, BN, mb.y_sorted, None, _status(dev))
     shared = gate = None
     if shared_local:
         L.bf16_swiglu(x, lay["s_gate"], lay["s_up"], out=mb.sh_h[:T])
@@ -98,6 +102,7 @@ class HybridMoELM(HybridLM):
         assert cfg.moe_experts % tp == 0
         self.e_local = cfg.moe_experts // tp
         self.shared_local = cfg.moe_shared_ffn // tp if cfg.moe_shared_ffn else 0
+        self.caches = None  # per-layer ExpertCache when experts live in host memory
         super().__init__(cfg, par, device, seed=seed, comm=comm)
 
     def _build(self, seed: int):
@@ -123,14 +128,52 @@ class HybridMoELM(HybridLM):
                 lay["s_gvec"] = L.BF16Weight(wrep.randn(1, H, dtype=torch.bfloat16))
 
     def alloc_workspace(self, max_tokens: int, max_logit_rows: int) -> Workspace:
-        return MoEWorkspace(self, max_tokens, max_logit_rows)
+        ws = MoEWorkspace(self, max_tokens, max_logit_rows)
+        if self.caches:
+            ws.slot_ids = torch.zeros(max_tokens, self.cfg.moe_topk, dtype=torch.int32, device=self.device)
+        return ws
+
+    def enable_expert_cache(self, slots: int) -> None:
+        """Move every layer's experts to pinned host memory behind a device LRU of `slots` experts."""
+        from ..ops.expert_cache import ExpertCache
+
+        self.caches = []
+        for lay in self.layers:
+            cache = ExpertCache(lay["e_gate"], lay["e_up"], lay["e_down"], self.e_local, slots, self.device)
+            del lay["e_gate"], lay["e_up"], lay["e_down"]
+            self.caches.append(cache)
+        torch.cuda.empty_cache()
 
     def _ffn_block(self, i, lay, meta, ws: MoEWorkspace, T: int, call: int, fused: bool) -> None:
         c = self.cfg
         out = self._reduce_target(ws, T, call, fused)
-        moe_ffn(lay, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=self.par.tp_rank * self.e_local,
-                E_local=self.e_local, moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local,
-                route_mode=0 if c.moe_router == "softmax" else 1)
+        mode = 0 if c.moe_router == "softmax" else 1
+        if self.caches is None:
+            moe_ffn(lay, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=self.par.tp_rank * self.e_local,
+                    E_local=self.e_local, moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local,
+                    route_mode=mode)
+        else:
+            cache = self.caches[i]
+            g, u, d = cache.weights
+            lay_c = dict(lay, e_gate=g, e_up=u, e_down=d)
+            e0 = self.par.tp_rank * self.e_local
+            if T * c.moe_topk <= cache.S:
+                # every expert this step can route to fits: device LRU + copies of the misses
+                moe_ffn(lay_c, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=0, E_local=cache.S, moe_ffn=c.moe_ffn,
+                        hidden=c.hidden, shared_local=self.shared_local, route_mode=mode,
+                        remap=lambda ids: (cache.route(ids, e0, ws.slot_ids[:T]), ws.slot_ids[:T])[1])
+            else:
+                # wider batches (prefill): stream the experts through the slots in groups of S
+                if not hasattr(ws, "moe_pass"):
+                    ws.moe_pass = torch.zeros_like(ws.norm_out)
+                for p, g0 in enumerate(range(0, self.e_local, cache.S)):
+                    n = cache.load_range(g0)
+                    dst = out if p == 0 else ws.moe_pass[:T]
+                    moe_ffn(lay_c, ws.norm_out[:T], ws.moe, dst, k=c.moe_topk, e0=e0 + g0, E_local=n,
+                            moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local if p == 0 else 0,
+                            route_mode=mode, route=p == 0, gemm_E=cache.S)
+                    if p > 0:
+                        out.add_(dst)
         self._after_partial(ws, T, call, fused)
 
 
