@@ -126,12 +126,44 @@ class HybridMoELM(HybridLM):
                 lay["s_up"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
                 lay["s_down"] = L.BF16Weight(wf.randn(H, self.shared_local, dtype=torch.bfloat16))
                 lay["s_gvec"] = L.BF16Weight(wrep.randn(1, H, dtype=torch.bfloat16))
+            if c.ple_dim:
+                lay["ple_gate"] = L.BF16Weight(wrep.randn(c.ple_dim, H, dtype=torch.bfloat16))
+                lay["ple_out"] = L.BF16Weight(wrep.randn(H, c.ple_dim, dtype=torch.bfloat16))
+        self.ple = None
+        if c.ple_dim:
+            from ..ops.hostmem import HostTable
+
+            # per-layer token embeddings, int6 rows in pinned host memory: row (token * layers + layer)
+            self.ple = HostTable.random(c.vocab * c.layers, c.ple_dim, "int6", seed=seed * 7 + 3, std=0.05)
 
     def alloc_workspace(self, max_tokens: int, max_logit_rows: int) -> Workspace:
         ws = MoEWorkspace(self, max_tokens, max_logit_rows)
         if self.caches:
             ws.slot_ids = torch.zeros(max_tokens, self.cfg.moe_topk, dtype=torch.int32, device=self.device)
+        if self.ple is not None:
+            c = self.cfg
+            ws.ple_rows = torch.zeros(max_tokens, c.layers, c.ple_dim, dtype=torch.bfloat16, device=self.device)
+            ws.ple_ids = torch.zeros(max_tokens, c.layers, dtype=torch.int64, device=self.device)
+            ws.ple_h = torch.zeros(max_tokens, c.ple_dim, dtype=torch.bfloat16, device=self.device)
+            ws.ple_lid = torch.arange(c.layers, dtype=torch.int64, device=self.device)
         return ws
+
+    def _embed(self, meta, ws, T: int) -> None:
+        super()._embed(meta, ws, T)
+        if self.ple is not None:
+            # one host gather per step brings every layer's vector of every token
+            L_ = self.cfg.layers
+            torch.add(meta.input_ids[:T].long().unsqueeze(1) * L_, ws.ple_lid, out=ws.ple_ids[:T])
+            self.ple.gather(ws.ple_ids[:T].view(-1), ws.ple_rows[:T].view(-1, self.cfg.ple_dim))
+
+    def _ple(self, i: int, lay, ws, T: int, out: torch.Tensor) -> None:
+        """out += (gelu(h W_g^T) * p_i) W_o^T / world -- the per-layer embedding term, added to this
+        rank's partial so the sublayer's all-reduce carries it (1/world on every rank)."""
+        x = ws.norm_out[:T]
+        L.bf16_linear(x, lay["ple_gate"], out=ws.ple_h[:T])
+        h = torch.nn.functional.gelu(ws.ple_h[:T], approximate="tanh").mul_(ws.ple_rows[:T, i])
+        ws.ple_h[:T].copy_(h)
+        L.bf16_linear(ws.ple_h[:T], lay["ple_out"], out=out, residual=out, alpha=1.0 / self.par.tp_size)
 
     def enable_expert_cache(self, slots: int) -> None:
         """Move every layer's experts to pinned host memory behind a device LRU of `slots` experts."""
@@ -174,6 +206,8 @@ class HybridMoELM(HybridLM):
                             route_mode=mode, route=p == 0, gemm_E=cache.S)
                     if p > 0:
                         out.add_(dst)
+        if self.ple is not None:
+            self._ple(i, lay, ws, T, out)
         self._after_partial(ws, T, call, fused)
 
 

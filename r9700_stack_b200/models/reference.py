@@ -81,7 +81,15 @@ def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Ten
         resid = bf16(resid + y)
         h = rmsnorm(resid, lay["post_norm"], c.rms_eps, c.norm_plus_one)
         if "router" in lay:
-            y = bf16(_moe(model, lay, bf16(h)))
+            y = _moe(model, lay, bf16(h))
+            if getattr(model, "ple", None) is not None:
+                y = bf16(y)
+                ids = torch.tensor(tokens, device=dev) * c.layers + i
+                p = model.ple.gather_ref(ids).to(dev)
+                g = bf16(bf16(h) @ lay["ple_gate"].w.float().T)
+                hh = bf16(torch.nn.functional.gelu(g, approximate="tanh") * bf16(p))
+                y = y + hh @ lay["ple_out"].w.float().T
+            y = bf16(y)
         else:
             g = _lin(h, lay["w_gate"], mx)
             u = _lin(h, lay["w_up"], mx)

@@ -159,3 +159,31 @@ def test_align_matches_python(T, k, E, e0, El, BN):
     ref_work = [[e, start[e] + i * BN, min(BN, cnt[e] - i * BN)] for e in range(El) for i in range((cnt[e] + BN - 1) // BN)]
     assert int(wc) == len(ref_work)
     assert work[: len(ref_work)].cpu().tolist() == ref_work
+
+
+def test_tiny_moe_with_ple_matches_reference():
+    """Per-layer embeddings from the pinned-host int6 table (Flash-Next class) vs the oracle."""
+    from r9700_stack_b200.engine.llm import LLM
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.config import EngineConfig, tiny_moe
+    from r9700_stack_b200.models.reference import ReferenceState, reference_forward
+
+    cfg = tiny_moe(gdn_state_dtype="fp32", ple_dim=64)
+    ec = EngineConfig(max_batch=2, max_model_len=256, max_prefill_tokens=128, graph_batch_sizes=[1, 2])
+    llm = LLM(cfg, ec, seed=4)
+    assert llm.model.ple is not None
+    prompt = list(range(5, 30))
+    seq = llm.add_request(prompt, SamplingParams(max_tokens=3))
+    st = ReferenceState(llm.model)
+    llm.step()
+    _check()
+    got = llm.runner.ws.logits[0].clone()
+    ref = reference_forward(llm.model, prompt, st)[-1]
+    cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
+    assert float(cos) > 0.99, float(cos)
+    llm.step()
+    _check()
+    got = llm.runner.ws.logits[0].clone()
+    ref = reference_forward(llm.model, [seq.output[-2]], st)[-1]
+    cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
+    assert float(cos) > 0.99, float(cos)
