@@ -94,11 +94,13 @@ class LLM:
 
 
 def make_drafter(method: str, model, ec: EngineConfig, num_blocks: int, num_slots: int, seed: int = 0):
-    """The drafter named by ``EngineConfig.spec_method``: ngram | mtp | block."""
-    from ..spec.drafters import ModelDrafter, NgramDrafter
+    """The drafter named by ``EngineConfig.spec_method``: ngram | mtp | block | dspark."""
+    from ..spec.drafters import DSparkDrafter, ModelDrafter, NgramDrafter
 
     if method == "ngram":
         return NgramDrafter(ec.spec_tokens)
+    if method == "dspark":
+        return DSparkDrafter(model, ec.spec_tokens, ec, num_blocks, num_slots, seed=seed)
     if method in ("mtp", "block"):
         return ModelDrafter(model, method, ec.spec_tokens, ec, num_blocks, num_slots, seed=seed)
     raise ValueError(f"unknown speculative method {method!r}")

@@ -30,7 +30,7 @@ class Drafter:
         self.pending: dict[int, list[int]] = {}
 
     def drafts(self, seqs: list[Sequence]) -> dict[int, list[int]]:
-        """Proposals for the given sequences (exactly k tokens each; sequences without one get none)."""
+        """Proposals for the given sequences (up to k tokens each; sequences without one get none)."""
         out = {}
         for s in seqs:
             d = self.pending.get(s.seq_id)
@@ -264,3 +264,70 @@ class ModelDrafter(Drafter):
             if n:
                 self.pending[g[0].seq_id] = res[i:i + n]
             i += n
+
+
+class DSparkDrafter(ModelDrafter):
+    """DSpark-style drafter: the block drafter's per-position logits refined left to right by a
+    low-rank Markov head conditioned on the previous draft token, plus a confidence head that cuts
+    each sequence's draft where the running confidence drops below ``min_conf`` (adaptive
+    verification length per sequence; at least one draft is kept).
+
+      logits_j = block_logits_j + W_head @ E_markov[d_{j-1}]       (rank-r bigram correction)
+      conf_j   = sigmoid(w_conf . [h_j, E_markov[d_j]])             (h_j: drafter output row)
+
+    Reference: r9700_vllm/dsv4_glue.py:812 (install_markov), kernels/r9k_dsv4_glue.hip:500-649
+    (r9k_dsv4_markov_kernel / _last / _conf), the pack's mtp.0.markov_head / confidence_head tensors.
+    """
+
+    def __init__(self, target_model, k: int, engine_cfg, num_blocks: int, num_slots: int, seed: int = 0,
+                 rank: int = 64, min_conf: float = 0.3):
+        super().__init__(target_model, "block", k, engine_cfg, num_blocks, num_slots, seed=seed)
+        from ..models.weights import WeightFactory
+        from ..ops import linear as L
+
+        c, dev = self.model.cfg, self.model.device
+        wf = WeightFactory(dev, seed=seed * 1000 + 4242, std=0.02)
+        V = self.model.vocab_local * self.model.par.tp_size
+        self.markov_embed = wf.randn(V, rank, dtype=torch.bfloat16)
+        self.markov_head = L.BF16Weight(wf.randn(V, rank, dtype=torch.bfloat16))
+        self.conf_w = L.BF16Weight(wf.randn(1, c.hidden + rank, std=0.05, dtype=torch.bfloat16))
+        self.min_conf = min_conf
+        mb = engine_cfg.max_batch
+        self._mk_logits = torch.zeros(mb, V, dtype=torch.float32, device=dev)
+        self._cat = torch.zeros(mb, c.hidden + rank, dtype=torch.bfloat16, device=dev)
+        self._conf = torch.zeros(mb, 1, dtype=torch.float32, device=dev)
+        self.last_lengths: list[int] = []
+
+    def _block(self, feed, h_tgt, sched) -> None:
+        from ..ops import linear as L
+
+        super()._block(feed, h_tgt, sched)  # fills self.ws.logits rows (B-1 per proposing sequence)
+        prop = [f[0] for f in feed if f[0].seq_id in self.pending]
+        if not prop:
+            return
+        S, km = len(prop), self.k
+        V = self._mk_logits.shape[1]
+        rank = self.markov_embed.shape[1]
+        base = self.ws.logits[: S * km].view(S, km, V)
+        hrows = self.ws.h_out[: S * km].view(S, km, -1)
+        prev = torch.tensor([s.tokens[-1] for s in prop], dtype=torch.int64, device=self.model.device)
+        drafts, conf_run = [], torch.ones(S, device=self.model.device)
+        keep = torch.ones(S, dtype=torch.bool, device=self.model.device)
+        lengths = torch.zeros(S, dtype=torch.int64, device=self.model.device)
+        for j in range(km):
+            e_prev = self.markov_embed.index_select(0, prev)
+            L.bf16_linear(e_prev, self.markov_head, out=self._mk_logits[:S], out_dtype=torch.float32)
+            d = torch.argmax(base[:, j] + self._mk_logits[:S], dim=-1)
+            self._cat[:S, : hrows.shape[-1]].copy_(hrows[:, j])
+            self._cat[:S, hrows.shape[-1]:].copy_(self.markov_embed.index_select(0, d))
+            L.bf16_linear(self._cat[:S], self.conf_w, out=self._conf[:S], out_dtype=torch.float32)
+            conf_run = conf_run * torch.sigmoid(self._conf[:S, 0])
+            keep = keep & ((conf_run >= self.min_conf) | (j == 0))
+            lengths += keep.long()
+            drafts.append(d)
+            prev = d
+        dl = torch.stack(drafts, 1).tolist()
+        ln = lengths.tolist()
+        self.last_lengths = ln
+        for s, row, n in zip(prop, dl, ln):
+            self.pending[s.seq_id] = row[: max(1, n)]

@@ -132,7 +132,7 @@ def test_spec_scripted_is_lossless(greedy_ref, corrupt):
         assert 0 < st["accepted"] < st["drafted"], st
 
 
-@pytest.mark.parametrize("method", ["ngram", "mtp", "block"])
+@pytest.mark.parametrize("method", ["ngram", "mtp", "block", "dspark"])
 def test_spec_drafters_lossless(greedy_ref, method):
     from r9700_stack_b200.engine.scheduler import SamplingParams
     from r9700_stack_b200.models.config import tiny_hybrid
@@ -157,3 +157,16 @@ def test_spec_moe_mtp_runs():
     _check()
     for o, r in zip(outs, ref):
         assert _agree(o, r) >= 9, (o, r)
+
+
+def test_dspark_adaptive_lengths():
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.config import tiny_hybrid
+
+    llm = _engine(tiny_hybrid(gdn_state_dtype="fp32"), k=4, method="dspark")
+    llm.drafter.min_conf = 0.5  # random heads: confidence ~ sigmoid(small) -> some drafts are cut
+    llm.generate(_prompts(), SamplingParams(max_tokens=10))
+    _check()
+    st = llm.spec_stats
+    assert st["steps"] > 0 and 0 < st["drafted"] < st["steps"] * 3 * 4 + 1
+    assert all(1 <= n <= 4 for n in llm.drafter.last_lengths)
