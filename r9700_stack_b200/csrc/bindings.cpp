@@ -125,6 +125,16 @@ void ngram_ids(torch::Tensor ids, torch::Tensor seq_start, torch::Tensor seq_len
 void symm_collective(int64_t mode, torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_t rank,
                      int64_t world, int64_t slot_bytes, torch::Tensor seq, torch::Tensor status, double timeout_s);
 int64_t symm_collective_region_bytes(int64_t slot_bytes);
+void qsa_key_write(torch::Tensor ik, torch::Tensor slots, torch::Tensor ktok);
+void qsa_compress(torch::Tensor ktok, torch::Tensor block_table, torch::Tensor tok_seq, torch::Tensor tok_ctx,
+                  torch::Tensor ckey);
+void qsa_attention(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::Tensor block_table,
+                   torch::Tensor tok_seq, torch::Tensor tok_ctx, torch::Tensor sel, torch::Tensor count,
+                   double sm_scale, double k_scale, double v_scale, int64_t nsplit, torch::Tensor part_o,
+                   torch::Tensor part_ml, c10::optional<torch::Tensor> gate, torch::Tensor out);
+void symm_ar_wht(torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_t rank, int64_t world,
+                 int64_t slot_bytes, torch::Tensor seq, torch::Tensor status, double timeout_s, int64_t bits,
+                 int64_t phase);
 void lru_route(torch::Tensor ids, int64_t e0, int64_t E, int64_t S, torch::Tensor slot_of, torch::Tensor expert_of,
                torch::Tensor stamp, torch::Tensor clock, torch::Tensor miss_e, torch::Tensor miss_s,
                torch::Tensor miss_count, torch::Tensor counters, torch::Tensor slot_ids, torch::Tensor status);
@@ -227,6 +237,13 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(a!) hist, int n_orders, int rows, bool write_state, Tensor(b!) out) -> ()");
   m.def("symm_collective(int mode, Tensor x, Tensor(a!) out, Tensor peers, int rank, int world, int slot_bytes, "
         "Tensor(b!) seq, Tensor(c!) status, float timeout_s) -> ()");
+  m.def("qsa_key_write(Tensor ik, Tensor slots, Tensor(a!) ktok) -> ()");
+  m.def("qsa_compress(Tensor ktok, Tensor block_table, Tensor tok_seq, Tensor tok_ctx, Tensor(a!) ckey) -> ()");
+  m.def("qsa_attention(Tensor q, Tensor kc, Tensor vc, Tensor block_table, Tensor tok_seq, Tensor tok_ctx, "
+        "Tensor sel, Tensor count, float sm_scale, float k_scale, float v_scale, int nsplit, Tensor(a!) part_o, "
+        "Tensor(b!) part_ml, Tensor? gate, Tensor(c!) out) -> ()");
+  m.def("symm_ar_wht(Tensor x, Tensor(a!) out, Tensor peers, int rank, int world, int slot_bytes, "
+        "Tensor(b!) seq, Tensor(c!) status, float timeout_s, int bits, int phase) -> ()");
   m.def("lru_route(Tensor ids, int e0, int E, int S, Tensor(a!) slot_of, Tensor(b!) expert_of, Tensor(c!) stamp, "
         "Tensor(d!) clock, Tensor(e!) miss_e, Tensor(f!) miss_s, Tensor(g!) miss_count, Tensor(h!) counters, "
         "Tensor(i!) slot_ids, Tensor(j!) status) -> ()");
@@ -285,6 +302,10 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("moe_gather_bf16", &r9k::moe_gather_bf16);
   m.impl("ngram_ids", &r9k::ngram_ids);
   m.impl("symm_collective", &r9k::symm_collective);
+  m.impl("symm_ar_wht", &r9k::symm_ar_wht);
+  m.impl("qsa_key_write", &r9k::qsa_key_write);
+  m.impl("qsa_compress", &r9k::qsa_compress);
+  m.impl("qsa_attention", &r9k::qsa_attention);
   m.impl("lru_route", &r9k::lru_route);
   m.impl("expert_copy", &r9k::expert_copy);
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);

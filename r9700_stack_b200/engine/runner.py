@@ -228,6 +228,7 @@ class ModelRunner:
             self._upload(arr)
             meta = self.meta.views(lay, write_state=write_state)
             meta.host_seqs = _host_seqs(out, draft)
+            meta.host_max_ctx = _host_max_ctx(out, draft)
             self.model.forward(meta, self.ws, lay.T, lay.R)
             R = lay.R
             torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
@@ -274,6 +275,7 @@ class ModelRunner:
         self._upload(arr)
         meta = self.meta.views(lay, write_state=False)
         meta.host_seqs = _host_seqs(out, draft)
+        meta.host_max_ctx = _host_max_ctx(out, draft)
         ev = None
         if self.device_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -316,6 +318,12 @@ def _host_seqs(out: SchedulerOutput, draft=None) -> list[tuple[int, int]]:
         res.append((t, n))
         t += n
     return res
+
+
+def _host_max_ctx(out: SchedulerOutput, draft=None) -> int:
+    """The longest attention context of any row of the step (position of its last token + 1)."""
+    return max(ch.start + ch.n + (len(draft[ch.seq.seq_id]) if draft is not None and ch.seq.seq_id in draft else 0)
+               for ch in out.chunks)
 
 
 def _relayout(arr: np.ndarray, src: Layout, dst: Layout) -> np.ndarray:

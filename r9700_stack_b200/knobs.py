@@ -14,13 +14,15 @@ _DEFAULTS = {
     "R9K_ATTN": "tc",  # tc | simple
     "R9K_WEIGHT_TILED": "1",  # 1: MX weights stored as contiguous 128x128 units; 0: row-major
     "R9K_GEMM_SK": "0",  # 1: skinny GEMMs use the persistent stream-K kernel
-    "R9K_FP4_UNPACK": "0",
-    "R9K_GDN_FUSED": "1",  # 1: decode steps run the one-kernel GDN layer core  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
+    "R9K_FP4_UNPACK": "0",  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
+    "R9K_GDN_FUSED": "1",  # 1: decode steps run the one-kernel GDN layer core
     "R9K_COMM": "fused",  # fused | nccl
     "R9K_AR_MODE": "pull",  # pull: consumer reads peers' partials; push: GEMM epilogue stores into peers
     "R9K_GDN_STATE": "",  # "" (model default) | bf16 | fp32
     "R9K_DISABLE": "",
     "R9K_AR_ONESHOT_MAX_KB": "512",
+    "R9K_AR_QUANT_BITS": "0",  # 4 | 6: lossy WHT-64 compressed all-reduce for large (prefill) messages; 0: exact
+    "R9K_AR_QUANT_MIN_KB": "1024",  # smallest message sent compressed
     "R9K_SPIN_TIMEOUT_MS": "1000",
 }
 _cache: dict[str, str] = {}

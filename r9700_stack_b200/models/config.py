@@ -48,6 +48,10 @@ class HybridConfig:
     gdn_state_dtype: str = "bf16"  # bf16 | fp32
     # per-layer int6 embeddings in pinned host memory (Flash-Next class)
     ple_dim: int = 0
+    # QSA sparse attention on the full-attention layers (Flash-Next class): top-k 4-token groups by an
+    # indexer of qsa_heads x 128 query heads against mean-pooled group keys (0 = dense attention)
+    qsa_topk: int = 0
+    qsa_heads: int = 4
     init_std: float = 0.02
     tie_embeddings: bool = False
     # speculative decoding
@@ -94,6 +98,7 @@ def flashnext_moe() -> HybridConfig:
         weight_format="bf16",
         lm_head_format="bf16",
         ple_dim=256,
+        qsa_topk=512,
         mtp_layers=3,
         drafter="mtp",
     )

@@ -67,6 +67,8 @@ class StepMeta:
     write_state: bool = True  # False during speculative verification
     # host copy of (first token, tokens) per sequence for eager prefill steps; None on the decode path
     host_seqs: list | None = None
+    # host upper bound of tok_ctx on eager steps (None in CUDA graphs): QSA runs dense below its top-k
+    host_max_ctx: int | None = None
 
 
 class Workspace:
@@ -109,6 +111,15 @@ class Workspace:
         self.final_bf16 = torch.zeros(max_logit_rows, H, dtype=torch.bfloat16, device=dev)
         self.logits_local = torch.zeros(max_logit_rows, model.vocab_local, dtype=torch.float32, device=dev)
         self.logits = torch.zeros(max_logit_rows, c.vocab, dtype=torch.float32, device=dev)
+        if c.qsa_topk:
+            self.qsa_proj = torch.zeros(max_tokens, (c.qsa_heads + 1) * 128, dtype=torch.bfloat16, device=dev)
+            self.qsa_w = torch.full((max_tokens, c.qsa_heads), 128 ** -0.5, dtype=torch.float32, device=dev)
+            self.qsa_vis = torch.zeros(max_tokens, dtype=torch.int32, device=dev)
+            self.qsa_sel = torch.zeros(max_tokens, c.qsa_topk, dtype=torch.int32, device=dev)
+            self.qsa_cnt = torch.zeros(max_tokens, dtype=torch.int32, device=dev)
+            # indexer scores, viewed as [rows, groups] per call (rows chunked to fit): one fixed buffer,
+            # since captured decode graphs keep the address they saw
+            self.qsa_scores = torch.empty(16 << 20, dtype=torch.float32, device=dev)
         self.spec = None  # per-GDN-layer verify buffers (alloc_spec)
         self.spec_table = None
         self.acc_len = torch.zeros(max_logit_rows, dtype=torch.int32, device=dev)
@@ -158,6 +169,11 @@ class HybridLM:
                 lay["w_o"] = wf_rank.linear(H, a["hq"] * c.head_dim, fmt)
                 lay["q_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
                 lay["k_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
+                if c.qsa_topk:
+                    # indexer (replicated on every rank so all ranks select the same groups):
+                    # qsa_heads query heads + one key head of 128, one shared norm, rope on dims [0, 64)
+                    lay["w_idx"] = wf.linear((c.qsa_heads + 1) * 128, H, fmt)
+                    lay["idx_norm"] = wf.norm(128, c.norm_plus_one)
             else:
                 d = c.gdn_head_dim
                 lay["w_in"] = wf_rank.linear(g["proj_rows"], H, fmt)
@@ -210,6 +226,14 @@ class HybridLM:
             ssm[i] = torch.zeros(num_state_slots, g["hv"], c.gdn_head_dim, c.gdn_head_dim, dtype=sdt, device=self.device)
             conv[i] = torch.zeros(num_state_slots, g["conv_ch"], c.conv_width - 1, dtype=sdt, device=self.device)
         self.kv, self.ssm, self.conv = kv, ssm, conv
+        # QSA: token indexer keys (bf16) and mean-pooled group keys (e4m3), paged like the KV cache
+        self.qsa_cache = {}
+        if c.qsa_topk:
+            for i in c.attn_layers:
+                self.qsa_cache[i] = (
+                    torch.zeros(num_kv_blocks, kv_block, 128, dtype=torch.bfloat16, device=self.device),
+                    torch.zeros(num_kv_blocks, kv_block, 128, dtype=torch.uint8, device=self.device),
+                )
 
     def alloc_spec(self, ws: Workspace, max_verify_tokens: int) -> None:
         """Per-GDN-layer buffers a verify pass fills (projections and the conv/recurrence inputs of
@@ -274,6 +298,10 @@ class HybridLM:
                                   c.norm_plus_one, meta.positions, self.cos_sin, c.rotary_dim, meta.slots,
                                   ws.q[:T], kc, vc, self.k_scale, self.v_scale)
         gate = qkv[:, gate_off:gate_off + hq * D] if gate_off >= 0 else None
+        if c.qsa_topk and self._qsa(i, lay, meta, ws, T, gate):
+            if self.mx:
+                L.quant_act(ws.attn_bf16[:T], out=ws.attn_act.narrow(T))
+            return ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"]
         out_q = ws.attn_act.q[:T] if self.mx else None
         out_sf = ws.attn_act.sf if self.mx else None
         out_bf = None if self.mx else ws.attn_bf16[:T]
@@ -306,6 +334,44 @@ class HybridLM:
                                   self.sm_scale, self.k_scale, self.v_scale, po, pml, gate, out_bf, out_q, out_sf,
                                   _status.status(self.device), max_rows)
         return ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"]
+
+    def _qsa(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int, gate) -> bool:
+        """QSA indexer for attention layer i (projection, norm + rope, token key store, group
+        compression) and, unless every row's context fits inside the top-k (then the selection is the
+        whole causal context and the dense kernels run), scoring, top-k and the sparse attention into
+        ws.attn_bf16. Returns True when the sparse attention ran."""
+        c, a = self.cfg, self.attn_dims
+        Hi, k = c.qsa_heads, c.qsa_topk
+        o = _ops()
+        proj = ws.qsa_proj[:T]
+        self._linear(ws.act.narrow(T), ws.norm_out[:T], lay["w_idx"], proj)
+        heads = proj.view(T * (Hi + 1), 128)
+        L.rmsnorm(heads, lay["idx_norm"], c.rms_eps, plus_one=c.norm_plus_one, out=heads)
+        o.rope_heads(proj.view(T, Hi + 1, 128), Hi + 1, 0, meta.positions, self.cos_sin)
+        ktok, ckey = self.qsa_cache[i]
+        o.qsa_key_write(proj[:, Hi * 128:], meta.slots, ktok)
+        o.qsa_compress(ktok, meta.block_table, meta.tok_seq, meta.tok_ctx, ckey)
+        if meta.host_max_ctx is not None and meta.host_max_ctx <= 4 * k + 3:
+            return False
+        vis = ws.qsa_vis[:T]
+        torch.floor_divide(meta.tok_ctx[:T], 4, out=vis)
+        groups = meta.block_table.shape[1] * 16
+        rows = min(T, ws.qsa_scores.numel() // groups)
+        assert rows >= 1, "context too long for the QSA score buffer"
+        iq = proj[:, : Hi * 128].view(T, Hi, 128)
+        for r0 in range(0, T, rows):
+            r1 = min(T, r0 + rows)
+            sc = ws.qsa_scores[: (r1 - r0) * groups].view(r1 - r0, groups)
+            o.indexer_score(iq[r0:r1], ws.qsa_w[r0:r1], ckey, meta.block_table, meta.tok_seq[r0:r1], vis[r0:r1],
+                            groups, sc)
+            o.topk_select(sc, vis[r0:r1], k, ws.qsa_sel[r0:r1], ws.qsa_cnt[r0:r1])
+        kc, vc = self.kv[i]
+        hq, hkv = a["hq"], a["hkv"]
+        nsplit = 1 if T * hkv >= 148 or T > ws.logit_rows else max(1, min(ws.nsplit_max, -(-296 // (T * hkv))))
+        o.qsa_attention(ws.q[:T], kc, vc, meta.block_table, meta.tok_seq, meta.tok_ctx, ws.qsa_sel[:T],
+                        ws.qsa_cnt[:T], self.sm_scale, self.k_scale, self.v_scale, nsplit, ws.part_o, ws.part_ml,
+                        gate, ws.attn_bf16[:T])
+        return True
 
     def _gdn(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int):
         c, g = self.cfg, self.gdn_dims

@@ -55,6 +55,7 @@ class ReferenceState:
         c = model.cfg
         self.k = {i: [] for i in c.attn_layers}
         self.v = {i: [] for i in c.attn_layers}
+        self.ik = {i: [] for i in c.attn_layers}  # QSA indexer token keys (bf16 values)
         g = model.gdn_dims
         self.S = {i: torch.zeros(g["hv"], c.gdn_head_dim, c.gdn_head_dim, device=model.device) for i in c.gdn_layers}
         self.conv = {i: torch.zeros(g["conv_ch"], c.conv_width - 1, device=model.device) for i in c.gdn_layers}
@@ -144,11 +145,45 @@ def _attn(model, i, lay, h, pos, st, mx):
     s = torch.einsum("thd,chd->thc", q, Kx) * model.sm_scale
     qpos = pos[:, None]
     kpos = torch.arange(ctx, device=h.device)[None, :]
-    s = s.masked_fill((kpos > qpos)[:, None, :], float("-inf"))
+    allowed = kpos <= qpos
+    if c.qsa_topk:
+        allowed = allowed & _qsa_mask(model, i, lay, h, pos, st, mx, ctx)
+    s = s.masked_fill((~allowed)[:, None, :], float("-inf"))
     p = torch.softmax(s, dim=-1)
     o = torch.einsum("thc,chd->thd", p, Vx).reshape(T, hq * D)
     o = bf16(o * torch.sigmoid(gate))
     return _lin(o, lay["w_o"], mx)
+
+
+def _qsa_mask(model, i, lay, h, pos, st, mx, ctx):
+    """QSA key mask [T, ctx]: the top-k complete 4-token groups by the indexer score plus the open
+    group's causal tail, for every query row."""
+    c = model.cfg
+    Hi, k = c.qsa_heads, c.qsa_topk
+    T = h.shape[0]
+    pj = bf16(_lin(h, lay["w_idx"], mx)).reshape(T, Hi + 1, 128)
+    pj = bf16(rmsnorm(pj, lay["idx_norm"], c.rms_eps, c.norm_plus_one))
+    pj = bf16(_rope(pj, pos, 64, c.rope_theta))
+    iq, ik = pj[:, :Hi], pj[:, Hi]
+    st.ik[i].append(ik)
+    IK = torch.cat(st.ik[i], 0)  # [ctx, 128]
+    ng = ctx // 4
+    ck = e4m3_roundtrip(IK[: 4 * ng].reshape(ng, 4, 128).sum(1) * 0.25) if ng else IK[:0]
+    mask = torch.zeros(T, ctx, dtype=torch.bool, device=h.device)
+    for t in range(T):
+        p = int(pos[t])
+        vis = (p + 1) // 4
+        if vis > k:
+            sc = (torch.relu(iq[t] @ ck[:vis].T) * 128 ** -0.5).sum(0)
+            sel = torch.topk(sc, k).indices
+        else:
+            sel = torch.arange(vis, device=h.device)
+        g = torch.zeros(ctx, dtype=torch.bool, device=h.device)
+        idx = (sel[:, None] * 4 + torch.arange(4, device=h.device)[None, :]).reshape(-1)
+        g[idx] = True
+        g[4 * vis : p + 1] = True
+        mask[t] = g
+    return mask
 
 
 def _gdn(model, i, lay, h, st, mx):

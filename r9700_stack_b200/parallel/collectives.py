@@ -57,7 +57,7 @@ class SymmCollectives:
         return out
 
     def fits(self, x: torch.Tensor) -> bool:
-        return x.dtype == torch.bfloat16 and x.numel() * 2 <= self.slot_bytes and x.numel() <= 4096 * CHUNK
+        return x.dtype == torch.bfloat16 and x.numel() * 2 <= self.slot_bytes and x.numel() <= 16384 * CHUNK
 
     def all_reduce_oneshot(self, x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
         x = x.contiguous()
@@ -81,6 +81,22 @@ class SymmCollectives:
         self.all_gather(seg, res.view(-1))
         return res
 
+    def wht_ok(self, x: torch.Tensor, bits: int) -> bool:
+        n = x.numel()
+        return (x.dtype == torch.bfloat16 and n % 64 == 0 and x.data_ptr() % 16 == 0
+                and -(-n // CHUNK) * (64 * 8 * bits + 128) <= (self.slot_bytes // self.world) & ~15)
+
+    def all_reduce_wht(self, x: torch.Tensor, bits: int = 6, out: torch.Tensor | None = None,
+                       phase: int = 3) -> torch.Tensor:
+        """Lossy compressed all-reduce: WHT-64 rotation, 4- or 6-bit codes with a bf16 scale per 64
+        elements, reduced in the rotated domain; bit-identical on every rank (``parallel.compress``
+        restates it in torch)."""
+        x = x.contiguous()
+        out = out if out is not None else torch.empty_like(x)
+        _native.ops().symm_ar_wht(x.view(-1), out.view(-1), self.peers, self.rank, self.world, self.slot_bytes,
+                                  self.seq, _status.status(self.device), float(self.timeout_s), int(bits), int(phase))
+        return out
+
     def twoshot_ok(self, x: torch.Tensor) -> bool:
         return x.numel() % (self.world * CHUNK) == 0
 
@@ -97,7 +113,15 @@ class SymmCollectives:
         return "oneshot"
 
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
-        """In-place all-reduce of x (bf16) by the calibrated algorithm."""
+        """In-place all-reduce of x (bf16) by the calibrated algorithm; with ``R9K_AR_QUANT_BITS`` set
+        (4 or 6), messages of at least ``R9K_AR_QUANT_MIN_KB`` go through the lossy compressed path."""
+        from .. import knobs
+
+        bits = knobs.get_int("R9K_AR_QUANT_BITS")
+        if (self.world > 1 and bits in (4, 6) and x.numel() * 2 >= knobs.get_int("R9K_AR_QUANT_MIN_KB") * 1024
+                and self.wht_ok(x, bits)):
+            x.copy_(self.all_reduce_wht(x, bits))
+            return x
         algo = self.should("all_reduce", x.numel() * x.element_size()) if self.fits(x) else "nccl"
         if algo == "twoshot" and not self.twoshot_ok(x):
             algo = "oneshot"

@@ -31,7 +31,7 @@ class SymmComm(NcclComm):
     fused = True
 
     def __init__(self, hidden: int, max_tokens: int, calls_per_step: int, device, group=None,
-                 timeout_s: float = 2.0):
+                 timeout_s: float = 2.0, max_prefill_tokens: int = 8192):
         super().__init__(group)
         assert calls_per_step % 2 == 0
         self.device = torch.device(device)
@@ -61,8 +61,28 @@ class SymmComm(NcclComm):
         self.peers = torch.tensor(ptrs, dtype=torch.int64)
         self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.barrier()
+        # lossy compressed all-reduce for prefill-sized messages (opt-in: R9K_AR_QUANT_BITS=4|6)
+        from .. import knobs
+
+        self.wht_bits = knobs.get_int("R9K_AR_QUANT_BITS") if self.world_size > 1 else 0
+        self.wht_min_bytes = knobs.get_int("R9K_AR_QUANT_MIN_KB") * 1024
+        self.wht = None
+        if self.wht_bits in (4, 6):
+            from .collectives import SymmCollectives
+
+            chunks = -(-max_prefill_tokens * hidden // 4096)
+            self.wht = SymmCollectives(self.device, group=group, slot_bytes=self.world_size * chunks * (64 * 8 * self.wht_bits + 128),
+                                       timeout_s=timeout_s)
 
     # -------------------------------------------------------------------------------------------
+    def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
+        """Unfused all-reduce (prefill): the compressed kernel for large messages when enabled, else NCCL."""
+        if (self.wht is not None and t.numel() * t.element_size() >= self.wht_min_bytes
+                and self.wht.wht_ok(t, self.wht_bits)):
+            t.copy_(self.wht.all_reduce_wht(t, self.wht_bits))
+            return t
+        return super().all_reduce_(t)
+
     def can_fuse(self, T: int) -> bool:
         return 0 < T <= self.max_tokens
 
@@ -101,6 +121,9 @@ class SymmComm(NcclComm):
 
     def close(self) -> None:
         ops = _native.ops()
+        if self.wht is not None:
+            self.wht.close()
+            self.wht = None
         torch.cuda.synchronize(self.device)
         for p in self._opened:
             ops.symm_close(p)

@@ -50,6 +50,16 @@ def _worker(rank, world, port, q):
             ag = c.all_gather(x)
             if not torch.equal(ag.cpu(), torch.cat([_inputs(r, n, it) for r in range(world)])):
                 errs.append(f"ag n={n}")
+        # lossy compressed all-reduce: the oracle over every rank's input, identical on all ranks
+        from r9700_stack_b200.parallel import compress as C
+
+        for bits in (4, 6):
+            n = 4096 * world * 4 + 64
+            x = _inputs(rank, n, 50 + bits).cuda()
+            y = c.all_reduce_wht(x, bits)
+            ref = C.all_reduce_ref([_inputs(r, n, 50 + bits) for r in range(world)], bits)
+            if not torch.equal(y.cpu(), ref):
+                errs.append(f"wht{bits}")
         # graph replay of interleaved collectives
         x = _inputs(rank, 65536, 99).cuda()
         s = torch.cuda.Stream()
