@@ -39,3 +39,19 @@ void spec_accept(torch::Tensor input_ids, torch::Tensor target, torch::Tensor se
 }
 
 }  // namespace r9k
+
+namespace r9k {
+
+// Device trace stamp: buf[slot] = %globaltimer (ns). One thread; captured into CUDA graphs like any
+// kernel, so replayed steps are traced too. The stamp lands when the preceding work on the stream
+// has finished (stream order; PDL is not used here on purpose).
+__global__ void trace_stamp_kernel(int64_t* buf, int64_t slot) { buf[slot] = (int64_t)globaltimer_ns(); }
+
+void trace_stamp(torch::Tensor buf, int64_t slot) {
+  TORCH_CHECK(buf.dtype() == torch::kInt64 && slot >= 0 && slot < buf.numel(), "trace_stamp: slot out of range");
+  const at::cuda::CUDAGuard guard(buf.device());
+  trace_stamp_kernel<<<1, 1, 0, at::cuda::getCurrentCUDAStream()>>>(buf.data_ptr<int64_t>(), slot);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

@@ -134,6 +134,12 @@ def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft
 class ModelRunner:
     def __init__(self, model, engine_cfg, block_size: int, max_tokens: int, max_seqs: int, max_blocks_per_seq: int):
         self.model = model
+        from .. import knobs
+
+        if knobs.get("R9K_TRACE") == "1" and getattr(model, "trace", None) is None:
+            from ..utils.trace import DeviceTrace
+
+            model.trace = DeviceTrace(model.device)
         self.cfg = engine_cfg
         self.device = model.device
         self.block_size = block_size

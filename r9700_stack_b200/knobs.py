@@ -24,6 +24,8 @@ _DEFAULTS = {
     "R9K_AR_QUANT_BITS": "0",  # 4 | 6: lossy WHT-64 compressed all-reduce for large (prefill) messages; 0: exact
     "R9K_AR_QUANT_MIN_KB": "1024",  # smallest message sent compressed
     "R9K_SPIN_TIMEOUT_MS": "1000",
+    "R9K_AR_HIST": "0",  # 1: histogram of all-reduce message sizes (utils.trace.AR_HIST)
+    "R9K_TRACE": "0",  # 1: the runner attaches a utils.trace.DeviceTrace to the model
 }
 _cache: dict[str, str] = {}
 

@@ -52,6 +52,8 @@ class HybridConfig:
     # indexer of qsa_heads x 128 query heads against mean-pooled group keys (0 = dense attention)
     qsa_topk: int = 0
     qsa_heads: int = 4
+    # hyper-connections: HC residual streams, sigmoid-gated mix into every block (0 = plain residual)
+    hc_streams: int = 0
     init_std: float = 0.02
     tie_embeddings: bool = False
     # speculative decoding
@@ -99,6 +101,7 @@ def flashnext_moe() -> HybridConfig:
         lm_head_format="bf16",
         ple_dim=256,
         qsa_topk=512,
+        hc_streams=4,
         mtp_layers=3,
         drafter="mtp",
     )

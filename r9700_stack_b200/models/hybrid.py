@@ -120,6 +120,11 @@ class Workspace:
             # indexer scores, viewed as [rows, groups] per call (rows chunked to fit): one fixed buffer,
             # since captured decode graphs keep the address they saw
             self.qsa_scores = torch.empty(16 << 20, dtype=torch.float32, device=dev)
+        if c.hc_streams:
+            HC = c.hc_streams
+            self.hc_x = torch.zeros(max_tokens, HC * H, dtype=torch.bfloat16, device=dev)  # residual streams
+            self.hc_n = torch.zeros(max_tokens, HC * H, dtype=torch.bfloat16, device=dev)  # normalised streams
+            self.hc_l = torch.zeros(max_tokens, HC, dtype=torch.float32, device=dev)
         self.spec = None  # per-GDN-layer verify buffers (alloc_spec)
         self.spec_table = None
         self.acc_len = torch.zeros(max_logit_rows, dtype=torch.int32, device=dev)
@@ -148,6 +153,7 @@ class HybridLM:
         self.v_scale = 1.0
         self._build(seed)
         self._rope_cache(8192 * 8)
+        self.trace = None  # utils.trace.DeviceTrace: %globaltimer marks between sublayers
 
     # --------------------------------------------------------------------------------------------
     def _build(self, seed: int):
@@ -182,12 +188,21 @@ class HybridLM:
                 lay["A_log"] = torch.log(torch.empty(g["hv"], device=self.device).uniform_(1, 16, generator=wf_rank.gen))
                 lay["dt_bias"] = wf_rank.randn(g["hv"], std=0.5)
                 lay["gdn_norm"] = (1.0 + wf.randn(d, std=0.1)).to(torch.bfloat16)
+            if c.hc_streams:
+                from ..ops import hc as HCo
+
+                lay["hc_in"] = HCo.random_point(wf, c.hc_streams, H)
+                lay["hc_post"] = HCo.random_point(wf, c.hc_streams, H)
             if self.ffn_local:
                 lay["w_gate"] = wf_rank.linear(self.ffn_local, H, fmt)
                 lay["w_up"] = wf_rank.linear(self.ffn_local, H, fmt)
                 lay["w_down"] = wf_rank.linear(H, self.ffn_local, fmt)
             self.layers.append(lay)
         self.final_norm = wf.norm(H, c.norm_plus_one)
+        if c.hc_streams:
+            from ..ops import hc as HCo
+
+            self.hc_final = HCo.random_point(wf, c.hc_streams, H)
         self.lm_head = wf_rank.linear(self.vocab_local, H, c.lm_head_format)
         self.mx = not isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.BF16Weight)
 
@@ -476,7 +491,13 @@ class HybridLM:
     def forward(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
         """Run T tokens; returns fp32 logits [R, vocab] for the rows in meta.logits_idx[:R]."""
         c = self.cfg
+        if c.hc_streams:
+            return self._forward_hc(meta, ws, T, R)
         fused = getattr(self.comm, "fused", False) and self.comm.can_fuse(T) and knobs.get("R9K_COMM") != "nccl"
+        tr = self.trace
+        if tr is not None:
+            tr.begin()
+            tr.mark("start")
         if fused:
             self.comm.step_begin()
         self._embed(meta, ws, T)
@@ -491,10 +512,55 @@ class HybridLM:
             else:
                 act, xb, w = self._gdn(i, lay, meta, ws, T)
             self._row_parallel(act, xb, w, ws, T, call=2 * i, fused=fused)
+            if tr is not None:
+                tr.mark(f"L{i}.{'attn' if lay['attn'] else 'gdn'}")
             self._post_reduce_norm(lay["post_norm"], ws, T, call=2 * i, fused=fused)
             self._ffn_block(i, lay, meta, ws, T, call=2 * i + 1, fused=fused)
+            if tr is not None:
+                tr.mark(f"L{i}.ffn")
         # final: residual add + norm, then the rows that need logits
         self._post_reduce_norm(self.final_norm, ws, T, call=2 * nl - 1, fused=fused, final=True)
+        out = self._lm_head(meta, ws, T, R)
+        if tr is not None:
+            tr.mark("lm_head")
+        return out
+
+    def _hc_point(self, p, ws: Workspace, T: int, block: bool, final: bool = False) -> None:
+        """Hyper-connection norm point: inject the block output ws.y into every residual stream, normalise
+        each stream, and mix the streams into the next block's input (ws.norm_out, + MXFP8 for MX weights)."""
+        from ..ops import hc as HCo
+
+        c = self.cfg
+        HC = c.hc_streams
+        if block:
+            L.bf16_linear(ws.y[:T], p.wl, out=ws.hc_l[:T], out_dtype=torch.float32)
+        HCo.combine_norm(ws.hc_x[:T], ws.y[:T] if block else None, ws.hc_l[:T] if block else None, p.w, HC, c.rms_eps,
+                         ws.hc_n[:T])
+        HCo.gate_mix(ws.hc_n[:T], p.g, HC, ws.norm_out[:T])
+        if self.mx and not final:
+            L.quant_act(ws.norm_out[:T], out=ws.act.narrow(T))
+
+    def _forward_hc(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
+        """Forward with hyper-connection residual streams (unfused all-reduce after each block)."""
+        c = self.cfg
+        HC, H = c.hc_streams, c.hidden
+        self._embed(meta, ws, T)
+        ws.hc_x[:T].view(T, HC, H).copy_(ws.resid[:T, None, :])
+        for i, lay in enumerate(self.layers):
+            self._hc_point(lay["hc_in"], ws, T, block=i > 0)
+            if lay["attn"]:
+                act, xb, w = self._attention(i, lay, meta, ws, T)
+            else:
+                act, xb, w = self._gdn(i, lay, meta, ws, T)
+            self._row_parallel(act, xb, w, ws, T, call=2 * i, fused=False)
+            self._hc_point(lay["hc_post"], ws, T, block=True)
+            self._ffn_block(i, lay, meta, ws, T, call=2 * i + 1, fused=False)
+        self._hc_point(self.hc_final, ws, T, block=True, final=True)
+        # the stream mean stands for the pre-norm hidden state (what MTP / block drafters read)
+        torch.mean(ws.hc_x[:T].view(T, HC, H), dim=1, out=ws.resid[:T])
+        return self._lm_head(meta, ws, T, R)
+
+    def _lm_head(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
         rows = ws.final_bf16[:R]
         torch.index_select(ws.norm_out[:T], 0, meta.logits_idx[:R], out=rows)
         if isinstance(self.lm_head, L.MXWeight):

@@ -70,33 +70,47 @@ def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Ten
     T = len(tokens)
     pos = torch.arange(st.pos, st.pos + T, device=dev)
     resid = model.embed[torch.tensor(tokens, device=dev)].float()
+    if c.hc_streams:
+        return _forward_hc(model, tokens, st, pos, resid)
     y = None
     for i, lay in enumerate(model.layers):
         if y is not None:
             resid = bf16(resid + y)
         h = rmsnorm(resid, lay["in_norm"], c.rms_eps, c.norm_plus_one)
-        if lay["attn"]:
-            y = bf16(_attn(model, i, lay, h, pos, st, mx))
-        else:
-            y = bf16(_gdn(model, i, lay, h, st, mx))
+        y = _mixer(model, i, lay, h, pos, st, mx)
         resid = bf16(resid + y)
         h = rmsnorm(resid, lay["post_norm"], c.rms_eps, c.norm_plus_one)
-        if "router" in lay:
-            y = _moe(model, lay, bf16(h))
-            if getattr(model, "ple", None) is not None:
-                y = bf16(y)
-                ids = torch.tensor(tokens, device=dev) * c.layers + i
-                p = model.ple.gather_ref(ids).to(dev)
-                g = bf16(bf16(h) @ lay["ple_gate"].w.float().T)
-                hh = bf16(torch.nn.functional.gelu(g, approximate="tanh") * bf16(p))
-                y = y + hh @ lay["ple_out"].w.float().T
-            y = bf16(y)
-        else:
-            g = _lin(h, lay["w_gate"], mx)
-            u = _lin(h, lay["w_up"], mx)
-            y = bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
+        y = _ffn(model, i, lay, h, tokens, mx)
     resid = bf16(resid + y)
     h = bf16(rmsnorm(resid, model.final_norm, c.rms_eps, c.norm_plus_one))
+    return _finish(model, h, st, T)
+
+
+def _mixer(model, i, lay, h, pos, st, mx):
+    if lay["attn"]:
+        return bf16(_attn(model, i, lay, h, pos, st, mx))
+    return bf16(_gdn(model, i, lay, h, st, mx))
+
+
+def _ffn(model, i, lay, h, tokens, mx):
+    c, dev = model.cfg, model.device
+    if "router" in lay:
+        y = _moe(model, lay, bf16(h))
+        if getattr(model, "ple", None) is not None:
+            y = bf16(y)
+            ids = torch.tensor(tokens, device=dev) * c.layers + i
+            p = model.ple.gather_ref(ids).to(dev)
+            g = bf16(bf16(h) @ lay["ple_gate"].w.float().T)
+            hh = bf16(torch.nn.functional.gelu(g, approximate="tanh") * bf16(p))
+            y = y + hh @ lay["ple_out"].w.float().T
+        return bf16(y)
+    g = _lin(h, lay["w_gate"], mx)
+    u = _lin(h, lay["w_up"], mx)
+    return bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
+
+
+def _finish(model, h, st, T):
+    c = model.cfg
     lm_mx = isinstance(model.lm_head, L.MXWeight)
     logits = (fake_mxfp8(h) if lm_mx else h) @ _w(model.lm_head).T
     st.pos += T
@@ -106,6 +120,30 @@ def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Ten
             st.S[k] = bf16(st.S[k])
             st.conv[k] = bf16(st.conv[k])
     return logits
+
+
+def _hc_point(model, p, X, y):
+    """Hyper-connection norm point: (new residual streams, next block input), both bf16 values."""
+    from ..ops import hc as HCo
+
+    c = model.cfg
+    l = bf16(y) @ p.wl.w.float().T if y is not None else None
+    X, N = HCo.combine_norm_ref(X, y, l, p.w, c.hc_streams, c.rms_eps)
+    return X, HCo.gate_mix_ref(N, p.g, c.hc_streams).float()
+
+
+def _forward_hc(model, tokens, st, pos, emb):
+    c, mx = model.cfg, model.mx
+    T, HC = len(tokens), c.hc_streams
+    X = emb.bfloat16().repeat(1, HC)
+    y = None
+    for i, lay in enumerate(model.layers):
+        X, h = _hc_point(model, lay["hc_in"], X, y)
+        y = _mixer(model, i, lay, h, pos, st, mx)
+        X, h = _hc_point(model, lay["hc_post"], X, y)
+        y = _ffn(model, i, lay, h, tokens, mx)
+    X, h = _hc_point(model, model.hc_final, X, y)
+    return _finish(model, h, st, T)
 
 
 def _rope(x, pos, rot, theta):

@@ -48,6 +48,9 @@ class NcclComm:
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         if self.world_size > 1:
+            from ..utils.trace import note_all_reduce
+
+            note_all_reduce(t.numel() * t.element_size())
             dist.all_reduce(t, group=self.group)
         return t
 

@@ -47,6 +47,8 @@ class EngineMetrics:
         self.steps = 0
         self.step_time_s = 0.0
         self.ttft: list[float] = []
+        self.errors = 0  # engine steps that raised (their requests ended with reason "error")
+        self.last_error: str | None = None
 
 
 class AsyncEngine:
@@ -141,7 +143,20 @@ class AsyncEngine:
                 time.sleep(self._idle_sleep)
                 continue
             t0 = time.time()
-            llm.step()
+            try:
+                llm.step()
+            except Exception as e:  # noqa: BLE001 -- a failed step must not strand the clients
+                # every live request ends with reason "error"; the engine keeps serving new ones
+                m.errors += 1
+                m.last_error = repr(e)
+                for rid in list(self._live):
+                    r = self._live.pop(rid)
+                    try:
+                        llm.abort(r.seq)
+                    except Exception:  # noqa: BLE001
+                        pass
+                    self._emit(r, [], True, "error")
+                continue
             m.steps += 1
             m.step_time_s += time.time() - t0
             for rid in list(self._live):
