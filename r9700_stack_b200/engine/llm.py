@@ -27,7 +27,13 @@ class LLM:
             device = torch.device("cuda", torch.cuda.current_device())
         self.device = torch.device(device)
         if model is None:
-            model = build_model(model_cfg, self.par, self.device, seed=seed, comm=comm, max_ctx=ec.max_model_len)
+            placement = None
+            if ec.ep_placement:
+                from ..parallel.ep_placement import load as load_placement
+
+                placement = load_placement(ec.ep_placement)
+            model = build_model(model_cfg, self.par, self.device, seed=seed, comm=comm, max_ctx=ec.max_model_len,
+                                placement=placement)
         self.model = model
         blocks_per_seq = math.ceil(ec.max_model_len / ec.kv_block)
         num_blocks = ec.num_kv_blocks or (ec.max_batch * blocks_per_seq + 1)
@@ -106,12 +112,12 @@ def make_drafter(method: str, model, ec: EngineConfig, num_blocks: int, num_slot
     raise ValueError(f"unknown speculative method {method!r}")
 
 
-def build_model(cfg, par, device, seed=0, comm=None, max_ctx: int = 32768):
+def build_model(cfg, par, device, seed=0, comm=None, max_ctx: int = 32768, placement=None):
     if isinstance(cfg, HybridConfig):
         if cfg.moe_experts:
             from ..models.hybrid_moe import HybridMoELM
 
-            return HybridMoELM(cfg, par, device, seed=seed, comm=comm)
+            return HybridMoELM(cfg, par, device, seed=seed, comm=comm, placement=placement)
         from ..models.hybrid import HybridLM
 
         return HybridLM(cfg, par, device, seed=seed, comm=comm)

@@ -214,4 +214,5 @@ class EngineConfig:
     cuda_graphs: bool = True
     graph_batch_sizes: list[int] = field(default_factory=lambda: [1, 2, 4, 8, 16])
     spec_tokens: int = 0  # draft tokens verified per step (0: no speculative decoding)
-    spec_method: str = "ngram"  # ngram | mtp | block
+    spec_method: str = "ngram"  # ngram | mtp | block | dspark
+    ep_placement: str = ""  # JSON expert placement (parallel.ep_placement) for MoE models; "" = contiguous

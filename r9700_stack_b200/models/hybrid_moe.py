@@ -94,12 +94,26 @@ class MoEWorkspace(Workspace):
         c = model.cfg
         self.moe = MoEBuffers(model.device, max_tokens, c.hidden, c.moe_experts, c.moe_topk, model.e_local, c.moe_ffn,
                               model.shared_local)
+        if model.placement is not None:
+            self.ep_ids = torch.zeros(max_tokens * c.moe_topk, dtype=torch.int32, device=model.device)
 
 
 class HybridMoELM(HybridLM):
-    def __init__(self, cfg, par=None, device="cuda", seed: int = 0, comm=None):
+    def __init__(self, cfg, par=None, device="cuda", seed: int = 0, comm=None, placement=None):
+        """``placement``: optional expert placement (``parallel.ep_placement``), one list of global
+        expert ids per rank; rank r holds placement[r] in that order. Without it rank r holds the
+        contiguous range [r E / R, (r + 1) E / R). With a placement every expert's weights are drawn
+        from a generator keyed by (layer, expert id), so the model is the same function under any
+        placement."""
         tp = (par.tp_size if par is not None else 1)
         assert cfg.moe_experts % tp == 0
+        self.placement = None
+        if placement is not None:
+            from ..parallel.ep_placement import validate
+
+            validate(placement, cfg.moe_experts)
+            assert len(placement) == tp, "one expert list per tensor-parallel rank"
+            self.placement = [list(map(int, b)) for b in placement]
         self.e_local = cfg.moe_experts // tp
         self.shared_local = cfg.moe_shared_ffn // tp if cfg.moe_shared_ffn else 0
         self.caches = None  # per-layer ExpertCache when experts live in host memory
@@ -112,15 +126,21 @@ class HybridMoELM(HybridLM):
         wf = WeightFactory(self.device, seed=seed * 1000 + 77 + r, std=c.init_std)
         wrep = WeightFactory(self.device, seed=seed * 1000 + 79, std=c.init_std)
         H, I = c.hidden, c.moe_ffn
-        for lay in self.layers:
+        for li, lay in enumerate(self.layers):
             lay["router"] = L.BF16Weight(wrep.randn(c.moe_experts, H, dtype=torch.bfloat16))
             # the local experts of a layer are generated and quantised as one stacked [E * rows, K] tensor
             # (one NVFP4 global scale per layer); tiling the stacked tensor gives exactly the unit order
             # of stack_experts() over per-expert weights, since every expert spans whole 128-row tiles
             El = self.e_local
-            lay["e_gate"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
-            lay["e_up"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
-            lay["e_down"] = from_float(wf.randn(El * H, I), "nvfp4", tiled=True)
+            if self.placement is None:
+                lay["e_gate"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
+                lay["e_up"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
+                lay["e_down"] = from_float(wf.randn(El * H, I), "nvfp4", tiled=True)
+            else:
+                mats = [self._expert_weights(seed, li, e, H, I) for e in self.placement[r]]
+                lay["e_gate"] = from_float(torch.cat([m[0] for m in mats]), "nvfp4", tiled=True)
+                lay["e_up"] = from_float(torch.cat([m[1] for m in mats]), "nvfp4", tiled=True)
+                lay["e_down"] = from_float(torch.cat([m[2] for m in mats]), "nvfp4", tiled=True)
             if self.shared_local:
                 lay["s_gate"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
                 lay["s_up"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
@@ -129,12 +149,44 @@ class HybridMoELM(HybridLM):
             if c.ple_dim:
                 lay["ple_gate"] = L.BF16Weight(wrep.randn(c.ple_dim, H, dtype=torch.bfloat16))
                 lay["ple_out"] = L.BF16Weight(wrep.randn(H, c.ple_dim, dtype=torch.bfloat16))
+        if self.placement is not None:
+            # global expert id -> local index on this rank (E_local for experts held elsewhere)
+            loc = torch.full((c.moe_experts,), self.e_local, dtype=torch.int32)
+            for j, e in enumerate(self.placement[r]):
+                loc[e] = j
+            self.expert_local = loc.to(self.device)
         self.ple = None
         if c.ple_dim:
             from ..ops.hostmem import HostTable
 
             # per-layer token embeddings, int6 rows in pinned host memory: row (token * layers + layer)
             self.ple = HostTable.random(c.vocab * c.layers, c.ple_dim, "int6", seed=seed * 7 + 3, std=0.05)
+
+    def _expert_weights(self, seed: int, layer: int, e: int, H: int, I: int):
+        """(gate [I, H], up [I, H], down [H, I]) fp32 of global expert e of a layer, placement-independent."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed(seed * 1_000_003 + layer * 4099 + e)
+        std = self.cfg.init_std
+        mk = lambda *shape: torch.randn(*shape, generator=g, device=self.device) * std  # noqa: E731
+        return mk(I, H), mk(I, H), mk(H, I)
+
+    def local_index(self, e: int) -> int:
+        """Local index of global expert e on this rank, or -1 when another rank holds it."""
+        if self.placement is None:
+            j = e - self.par.tp_rank * self.e_local
+            return j if 0 <= j < self.e_local else -1
+        row = self.placement[self.par.tp_rank]
+        return row.index(e) if e in row else -1
+
+    def _remap_ids(self, ws, T: int):
+        k = self.cfg.moe_topk
+
+        def remap(ids):
+            out = ws.ep_ids[: T * k]
+            torch.index_select(self.expert_local, 0, ids.reshape(-1), out=out)
+            return out.view(T, k)
+
+        return remap
 
     def alloc_workspace(self, max_tokens: int, max_logit_rows: int) -> Workspace:
         ws = MoEWorkspace(self, max_tokens, max_logit_rows)
@@ -169,6 +221,7 @@ class HybridMoELM(HybridLM):
         """Move every layer's experts to pinned host memory behind a device LRU of `slots` experts."""
         from ..ops.expert_cache import ExpertCache
 
+        assert self.placement is None, "the expert cache holds contiguous expert ranges"
         self.caches = []
         for lay in self.layers:
             cache = ExpertCache(lay["e_gate"], lay["e_up"], lay["e_down"], self.e_local, slots, self.device)
@@ -180,7 +233,10 @@ class HybridMoELM(HybridLM):
         c = self.cfg
         out = self._reduce_target(ws, T, call, fused)
         mode = 0 if c.moe_router == "softmax" else 1
-        if self.caches is None:
+        if self.caches is None and self.placement is not None:
+            moe_ffn(lay, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=0, E_local=self.e_local, moe_ffn=c.moe_ffn,
+                    hidden=c.hidden, shared_local=self.shared_local, route_mode=mode, remap=self._remap_ids(ws, T))
+        elif self.caches is None:
             moe_ffn(lay, ws.norm_out[:T], ws.moe, out, k=c.moe_topk, e0=self.par.tp_rank * self.e_local,
                     E_local=self.e_local, moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local,
                     route_mode=mode)

@@ -276,15 +276,14 @@ def _moe(model, lay, x):
     w = w / w.sum(-1, keepdim=True)
     xq = fake_mxfp8(x)
     I, El = c.moe_ffn, model.e_local
-    e0 = model.par.tp_rank * El
     G = lay["e_gate"].dequant().view(El, I, -1)
     U = lay["e_up"].dequant().view(El, I, -1)
     D = lay["e_down"].dequant().view(El, c.hidden, I)
     out = torch.zeros(T, c.hidden, device=x.device)
     for t in range(T):
         for j in range(c.moe_topk):
-            e = int(ids[t, j]) - e0
-            if not 0 <= e < El:
+            e = model.local_index(int(ids[t, j]))
+            if e < 0:
                 continue
             hh = Fn.silu(xq[t] @ G[e].T) * (xq[t] @ U[e].T)
             out[t] += w[t, j] * (fake_mxfp8(hh[None])[0] @ D[e].T).to(torch.bfloat16).float()

@@ -42,7 +42,8 @@ def test_combine_norm(hc, hd, per_stream, with_block):
     y = torch.empty_like(res)
     HC.combine_norm(res, blk, l, w, hc, 1e-6, y)
     _check()
-    assert torch.equal(res.cpu(), ref_res.cpu())
+    # within one bf16 rounding: the kernel's sigmoid and fused multiply-add round differently from torch's
+    assert torch.allclose(res.float().cpu(), ref_res.float().cpu(), atol=1e-2, rtol=1e-2)
     assert torch.allclose(y.float(), ref_y.float(), atol=2e-2, rtol=2e-2)
 
 

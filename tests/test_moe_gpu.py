@@ -187,3 +187,32 @@ def test_tiny_moe_with_ple_matches_reference():
     ref = reference_forward(llm.model, [seq.output[-2]], st)[-1]
     cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
     assert float(cos) > 0.99, float(cos)
+
+
+def test_expert_placement_is_the_same_function(tmp_path):
+    """A tiny MoE model under two expert placements (different local orders) gives identical logits,
+    and matches the fp32 oracle."""
+    from r9700_stack_b200.engine.llm import LLM
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.config import EngineConfig, tiny_moe
+    from r9700_stack_b200.models.reference import ReferenceState, reference_forward
+    from r9700_stack_b200.parallel import ep_placement as P
+
+    cfg = tiny_moe(gdn_state_dtype="fp32")
+    outs = []
+    for perm in ([0, 1, 2, 3, 4, 5, 6, 7], [5, 2, 7, 0, 3, 6, 1, 4]):
+        f = tmp_path / f"p{perm[0]}.json"
+        P.save(str(f), [perm])
+        ec = EngineConfig(max_batch=2, max_model_len=256, max_prefill_tokens=128, cuda_graphs=False,
+                          ep_placement=str(f))
+        llm = LLM(cfg, ec, seed=4)
+        prompt = torch.randint(0, cfg.vocab, (24,), generator=torch.Generator().manual_seed(2)).tolist()
+        llm.add_request(prompt, SamplingParams(max_tokens=2))
+        llm.step()
+        torch.cuda.synchronize()
+        got = llm.runner.ws.logits[0].clone()
+        outs.append(got)
+        ref = reference_forward(llm.model, prompt, ReferenceState(llm.model))[-1]
+        cos = float(torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0))
+        assert cos > 0.995, cos
+    assert torch.equal(outs[0], outs[1])
