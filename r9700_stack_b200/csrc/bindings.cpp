@@ -136,6 +136,8 @@ void hc_gate_mix(torch::Tensor x, torch::Tensor g, int64_t HC, torch::Tensor y);
 void hc_combine_norm(torch::Tensor res, c10::optional<torch::Tensor> block, c10::optional<torch::Tensor> l,
                      torch::Tensor w, int64_t HC, double eps, torch::Tensor y);
 void trace_stamp(torch::Tensor buf, int64_t slot);
+void hc_point(torch::Tensor res, c10::optional<torch::Tensor> y, torch::Tensor wl, torch::Tensor w, torch::Tensor g,
+              int64_t HC, double eps, torch::Tensor out);
 void symm_ar_wht(torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_t rank, int64_t world,
                  int64_t slot_bytes, torch::Tensor seq, torch::Tensor status, double timeout_s, int64_t bits,
                  int64_t phase);
@@ -249,6 +251,7 @@ TORCH_LIBRARY(r9k, m) {
   m.def("hc_gate_mix(Tensor x, Tensor g, int HC, Tensor(a!) y) -> ()");
   m.def("hc_combine_norm(Tensor(a!) res, Tensor? block, Tensor? l, Tensor w, int HC, float eps, Tensor(b!) y) -> ()");
   m.def("trace_stamp(Tensor(a!) buf, int slot) -> ()");
+  m.def("hc_point(Tensor(a!) res, Tensor? y, Tensor wl, Tensor w, Tensor g, int HC, float eps, Tensor(b!) out) -> ()");
   m.def("symm_ar_wht(Tensor x, Tensor(a!) out, Tensor peers, int rank, int world, int slot_bytes, "
         "Tensor(b!) seq, Tensor(c!) status, float timeout_s, int bits, int phase) -> ()");
   m.def("lru_route(Tensor ids, int e0, int E, int S, Tensor(a!) slot_of, Tensor(b!) expert_of, Tensor(c!) stamp, "
@@ -311,6 +314,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("symm_collective", &r9k::symm_collective);
   m.impl("symm_ar_wht", &r9k::symm_ar_wht);
   m.impl("trace_stamp", &r9k::trace_stamp);
+  m.impl("hc_point", &r9k::hc_point);
   m.impl("hc_gate_mix", &r9k::hc_gate_mix);
   m.impl("hc_combine_norm", &r9k::hc_combine_norm);
   m.impl("qsa_key_write", &r9k::qsa_key_write);

@@ -39,6 +39,8 @@ struct GemmArgs {
   const int32_t* g_work;
   const int32_t* g_count;
   int g_row_tiles;
+  // weight chunks prefetched into L2 ahead of the shared-memory ring (0: none)
+  int l2_prefetch;
 };
 
 // A (weight) tile load: row-major 2-D map, or pre-tiled 3-D map indexed by unit
@@ -46,6 +48,11 @@ R9K_DEVINL void load_a_tile(void* dst, const CUtensorMap* map, uint64_t* bar, co
                             int m0, uint64_t pol) {
   if (a.a_tiled) tma_load_3d_hint(dst, map, bar, 0, 0, (m0 >> 7) * a.kchunks + kc, pol);
   else tma_load_2d_hint(dst, map, bar, kc * box_x, m0, pol);
+}
+
+R9K_DEVINL void prefetch_a_tile(const CUtensorMap* map, const GemmArgs& a, int kc, int box_x, int m0) {
+  if (a.a_tiled) tma_prefetch_3d(map, 0, 0, (m0 >> 7) * a.kchunks + kc);
+  else tma_prefetch_2d(map, kc * box_x, m0);
 }
 
 template <int BN, bool DUAL, int EPI>

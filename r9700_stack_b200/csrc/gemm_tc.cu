@@ -36,7 +36,7 @@
 
 namespace r9k {
 
-template <int KIND, int BN, bool DUAL, int NP, int NC, bool UNPACK>
+template <int KIND, int BN, bool DUAL, int NP, int NC, bool UNPACK, int MT = 1>
 struct GemmCfg {
   static constexpr int NA = DUAL ? 2 : 1;
   static constexpr int A_BYTES = 128 * 128;                  // MMA-ready A tile (SW128)
@@ -58,8 +58,11 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES = OFF_TMEMPTR + 16 + 1024;  // + alignment slack
   // TMEM columns: NACC independent accumulators (skinny tiles round-robin their K steps over them so
   // consecutive MMAs do not serialise on one accumulator), then scale factors
-  static constexpr int NACC = BN == 16 ? 4 : BN == 32 ? (DUAL ? 2 : 4) : BN == 64 ? (DUAL ? 1 : 2) : 1;  // <= 256 TMEM cols (2 CTAs/SM)
-  static constexpr int ACC_COLS = BN * NA * NACC;
+  static constexpr int NACC1 = BN == 16 ? 4 : BN == 32 ? (DUAL ? 2 : 4) : BN == 64 ? (DUAL ? 1 : 2) : 1;  // <= 256 TMEM cols (2 CTAs/SM)
+  // MT row tiles per CTA (grouped skinny GEMMs): every tile keeps its own accumulators until the end
+  static constexpr int NACC = MT == 1 ? NACC1 : (NACC1 >= 2 ? 2 : 1);
+  static constexpr int ACC_TILE = BN * NA * NACC;  // TMEM columns of one row tile's accumulators
+  static constexpr int ACC_COLS = ACC_TILE * MT;
   static constexpr int SFA_COL = ACC_COLS;
   static constexpr int SFB_COL = SFA_COL + 4 * NA;
   static constexpr int USED_COLS = (KIND == KIND_MX) ? SFB_COL + 4 * NB_SF : ACC_COLS;
@@ -84,12 +87,13 @@ R9K_DEVINL void unpack_fp4_tile(const uint8_t* src, uint8_t* dst, int r) {
   }
 }
 
-template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK>
+template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK, int MT = 1>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmA2,
                    const __grid_constant__ CUtensorMap tmB, const GemmArgs args, float* __restrict__ ws_part,
                    int* __restrict__ ws_cnt) {
-  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK>;
+  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK, MT>;
+  static_assert(MT == 1 || (!UNPACK && EPI != EPI_PUSH), "multi-tile CTAs: plain loads, local epilogues");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* l_full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -101,7 +105,7 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int s_last, s_ok;
 
   const int warp = warp_id(), lane = lane_id();
-  int m0 = blockIdx.x * 128;  // row (A) coordinate in the weight matrix
+  int m0 = blockIdx.x * 128 * MT;  // row (A) coordinate in the weight matrix (first of MT row tiles)
   const int S = args.splits;
   const int split = (int)(blockIdx.y % S);
   const int n_tile = (int)(blockIdx.y / S);
@@ -114,7 +118,7 @@ __global__ void __launch_bounds__(192, 1)
     const int e = args.g_work[3 * blockIdx.y + 0];
     n0 = args.g_work[3 * blockIdx.y + 1];
     m_valid = n0 + args.g_work[3 * blockIdx.y + 2];
-    m0 = (e * args.g_row_tiles + (int)blockIdx.x) * 128;
+    m0 = (e * args.g_row_tiles + (int)blockIdx.x * MT) * 128;
   }
   const int kc0 = split * args.kc_per_split;
   const int kc1 = min(args.kchunks, kc0 + args.kc_per_split);
@@ -156,22 +160,24 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t pol_x = policy_evict_last();
       // Weights do not depend on the previous kernel: the first NP weight tiles are requested before
       // waiting on the predecessor grid (programmatic dependent launch). Activations come after.
-      auto load_a = [&](int i) {
-        const int s = i % NP;
-        const int kc = kc0 + i;
+      // chunk q of this CTA: row tile q / nk, k-chunk q % nk (MT row tiles stream through one ring)
+      auto load_a = [&](int q) {
+        const int s = q % NP;
+        const int kc = kc0 + q % nk;
+        const int mt = m0 + (q / nk) * 128;
         uint8_t* sa = smem + C::OFF_A + s * C::NA * C::AL_BYTES;
         mbar_arrive_expect_tx(&l_full[s], stage_tx);
-        load_a_tile(sa, &tmA, &l_full[s], args, kc, box_x, m0, pol_w);
-        if (DUAL) load_a_tile(sa + C::AL_BYTES, &tmA2, &l_full[s], args, kc, box_x, m0, pol_w);
+        load_a_tile(sa, &tmA, &l_full[s], args, kc, box_x, mt, pol_w);
+        if (DUAL) load_a_tile(sa + C::AL_BYTES, &tmA2, &l_full[s], args, kc, box_x, mt, pol_w);
         if constexpr (KIND == KIND_MX) {
           uint8_t* ssfa = smem + C::OFF_SFA + s * C::NA * 512;
-          bulk_load(ssfa, args.sfa + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
-          if (DUAL) bulk_load(ssfa + 512, args.sfa2 + ((int64_t)(m0 >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
+          bulk_load(ssfa, args.sfa + ((int64_t)(mt >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
+          if (DUAL) bulk_load(ssfa + 512, args.sfa2 + ((int64_t)(mt >> 7) * kchunks_sf + kc) * 512, 512, &l_full[s]);
         }
       };
-      auto load_b = [&](int i) {
-        const int s = i % NP;
-        const int kc = kc0 + i;
+      auto load_b = [&](int q) {
+        const int s = q % NP;
+        const int kc = kc0 + q % nk;
         tma_load_2d_hint(smem + C::OFF_B + s * C::B_BYTES, &tmB, &l_full[s], kc * ((KIND == KIND_BF16) ? 64 : 128), n0,
                          pol_x);
         if constexpr (KIND == KIND_MX) {
@@ -181,30 +187,47 @@ __global__ void __launch_bounds__(192, 1)
             bulk_load(ssfb + 512 * c, args.sfb + ((int64_t)((n0 >> 7) + c) * kchunks_sf + kc) * 512, 512, &l_full[s]);
         }
       };
-      const int npre = min(NP, nk);
-      for (int i = 0; i < npre; ++i) load_a(i);
+      // L2 prefetch of the weight chunk PD loads ahead of the ring: more bytes in flight than the
+      // shared-memory stages alone hold (weights only; activations are small and L2-resident)
+      const int PD = args.l2_prefetch;
+      auto prefetch_a = [&](int q) {
+        const int kc = kc0 + q % nk;
+        const int mt = m0 + (q / nk) * 128;
+        prefetch_a_tile(&tmA, args, kc, box_x, mt);
+        if (DUAL) prefetch_a_tile(&tmA2, args, kc, box_x, mt);
+        if constexpr (KIND == KIND_MX) {
+          bulk_prefetch_l2(args.sfa + ((int64_t)(mt >> 7) * kchunks_sf + kc) * 512, 512);
+          if (DUAL) bulk_prefetch_l2(args.sfa2 + ((int64_t)(mt >> 7) * kchunks_sf + kc) * 512, 512);
+        }
+      };
+      const int nq = nk * MT;
+      const int npre = min(NP, nq);
+      for (int q = 0; q < npre; ++q) load_a(q);
+      for (int q = npre; q < min(nq, npre + PD); ++q) prefetch_a(q);
       pdl_wait();
-      for (int i = 0; i < nk; ++i) {
-        if (i >= npre) {
-          if (!mbar_wait(&l_empty[i % NP], (uint32_t)(((i / NP) & 1) ^ 1), args.timeout_ns)) {
-            report_error(args.status, kErrMbarTimeout, 100, i);
+      for (int q = 0; q < nq; ++q) {
+        if (q >= npre) {
+          if (!mbar_wait(&l_empty[q % NP], (uint32_t)(((q / NP) & 1) ^ 1), args.timeout_ns)) {
+            report_error(args.status, kErrMbarTimeout, 100, q);
             break;
           }
-          load_a(i);
+          load_a(q);
+          if (PD > 0 && q + PD < nq) prefetch_a(q + PD);
         }
-        load_b(i);
+        load_b(q);
       }
     }
     __syncwarp();
   } else if (warp == 1) {
     // ------------------------------ MMA issuer ------------------------------
     if (lane == 0) {
-      for (int i = 0; i < nk; ++i) {
-        const int s = i % NP;
-        const int sc = i % NC;
-        if (!mbar_wait(&l_full[s], (uint32_t)((i / NP) & 1), args.timeout_ns) ||
-            (UNPACK && !mbar_wait(&c_full[sc], (uint32_t)((i / NC) & 1), args.timeout_ns))) {
-          report_error(args.status, kErrMbarTimeout, 101, i);
+      for (int q = 0; q < nk * MT; ++q) {
+        const int s = q % NP;
+        const int sc = q % NC;
+        const int i = q % nk;  // k-chunk within the row tile
+        if (!mbar_wait(&l_full[s], (uint32_t)((q / NP) & 1), args.timeout_ns) ||
+            (UNPACK && !mbar_wait(&c_full[sc], (uint32_t)((q / NC) & 1), args.timeout_ns))) {
+          report_error(args.status, kErrMbarTimeout, 101, q);
           break;
         }
         tc_fence_after();
@@ -223,7 +246,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < 4; ++k) {
           const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
           const int ai = k % C::NACC;
-          const uint32_t dacc = tbase + (uint32_t)(ai * BN * C::NA);
+          const uint32_t dacc = tbase + (uint32_t)((q / nk) * C::ACC_TILE + ai * BN * C::NA);
           const uint32_t acc = (i > 0 || k >= C::NACC) ? 1u : 0u;
           if constexpr (KIND == KIND_MX) {
             const uint32_t idesc = idesc_block_scaled(args.a_fmt, kFmtE4M3, 128, BN, (uint32_t)k, (uint32_t)k);
@@ -271,7 +294,7 @@ __global__ void __launch_bounds__(192, 1)
     // ------------------------------ epilogue ------------------------------
     GemmArgs ea = args;  // grouped mode: rows are the expert's own, tokens end at m_valid
     ea.M = m_valid;
-    const int row = (args.g_work != nullptr ? (int)blockIdx.x * 128 : m0) + row_local;
+    const int row = (args.g_work != nullptr ? (int)blockIdx.x * 128 * MT : m0) + row_local;
     const uint32_t trow = tbase + ((uint32_t)(q * 32) << 16);
     pdl_wait();
     ArCall arc;
@@ -285,15 +308,16 @@ __global__ void __launch_bounds__(192, 1)
     if (!ok) report_error(args.status, kErrMbarTimeout, 102, 0);
     tc_fence_after();
     // load one 16-column chunk of the accumulator(s), summing the NACC partial accumulators
-    auto load_acc = [&](int c, float* g, float* u) {
-      tmem_ld16(trow + c, g);
-      if (DUAL) tmem_ld16(trow + BN + c, u);
+    auto load_acc_t = [&](int t, int c, float* g, float* u) {
+      const uint32_t tr = trow + (uint32_t)(t * C::ACC_TILE);
+      tmem_ld16(tr + c, g);
+      if (DUAL) tmem_ld16(tr + BN + c, u);
       tmem_ld_wait();
 #pragma unroll
       for (int ai = 1; ai < C::NACC; ++ai) {
         float g2[16], u2[16];
-        tmem_ld16(trow + ai * BN * C::NA + c, g2);
-        if (DUAL) tmem_ld16(trow + ai * BN * C::NA + BN + c, u2);
+        tmem_ld16(tr + ai * BN * C::NA + c, g2);
+        if (DUAL) tmem_ld16(tr + ai * BN * C::NA + BN + c, u2);
         tmem_ld_wait();
 #pragma unroll
         for (int t = 0; t < 16; ++t) {
@@ -302,6 +326,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     };
+    auto load_acc = [&](int c, float* g, float* u) { load_acc_t(0, c, g, u); };
     // EPI_PUSH: the bf16 tile is staged in shared memory as [token][128 rows] (the operand buffers are
     // free once the accumulator is complete) and pushed to every rank's slot as 16-byte vectors, so
     // NVLink carries full 256-byte row segments; then one thread raises the tile's flags.
@@ -330,11 +355,14 @@ __global__ void __launch_bounds__(192, 1)
     if (S == 1) {
       if (ok && nk > 0) {
 #pragma unroll 1
-        for (int c = 0; c < BN; c += 16) {
-          float g[16], u[16];
-          load_acc(c, g, u);
-          if constexpr (EPI == EPI_PUSH) stage_push(c, g);
-          else epilogue_chunk<BN, DUAL, EPI>(ea, g, u, row, n0 + c, lane, &arc);
+        for (int t = 0; t < MT; ++t) {
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            float g[16], u[16];
+            load_acc_t(t, c, g, u);
+            if constexpr (EPI == EPI_PUSH) stage_push(c, g);
+            else epilogue_chunk<BN, DUAL, EPI>(ea, g, u, row + t * 128, n0 + c, lane, &arc);
+          }
         }
       }
       if constexpr (EPI == EPI_PUSH) flush_push();
@@ -455,18 +483,20 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
 // workspace layout: [65536 int counters][partials]
 static constexpr int64_t kWsCounters = 65536;
 
-template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK>
+template <int KIND, int BN, bool DUAL, int EPI, int NP, int NC, bool UNPACK, int MT = 1>
 static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUtensorMap& tb, GemmArgs args,
                         LaunchPlan p, torch::Tensor* ws, cudaStream_t stream) {
-  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK>;
-  auto kern = gemm_tc_kernel<KIND, BN, DUAL, EPI, NP, NC, UNPACK>;
+  using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK, MT>;
+  auto kern = gemm_tc_kernel<KIND, BN, DUAL, EPI, NP, NC, UNPACK, MT>;
   static bool attr_set = false;
   if (!attr_set) {
     TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) == cudaSuccess,
                 "r9k gemm: cannot set smem size");
     attr_set = true;
   }
-  const int grid_x = (args.N + 127) / 128;
+  TORCH_CHECK(((args.N + 127) / 128) % MT == 0, "r9k gemm: row tiles must divide over the CTAs");
+  const int grid_x = (args.N + 127) / 128 / MT;
+  if (MT > 1) p.S = 1;  // multi-tile CTAs keep whole K
   float* part = nullptr;
   int* cnt = nullptr;
   if (p.S > 1) {
@@ -479,6 +509,12 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
   }
   args.splits = p.S;
   args.kc_per_split = (args.kchunks + p.S - 1) / p.S;
+  static int l2pf = -1;
+  if (l2pf < 0) {
+    const char* e = getenv("R9K_GEMM_L2PF");
+    l2pf = e ? std::max(0, atoi(e)) : 0;
+  }
+  if (BN <= 64 && !UNPACK) args.l2_prefetch = l2pf;  // skinny (weight-streaming) GEMMs only
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid_x, p.n_tiles * p.S, 1);
   cfg.blockDim = dim3(192, 1, 1);
@@ -674,9 +710,23 @@ void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::T
   a.N = (int)N;
   GemmArgs ga = a;
   ga.N = (int)N;
-  // launch_gemm derives grid.x from args.N
-  if (dual) dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, ga, p, nullptr, st);
-  else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, ga, p, nullptr, st);
+  // launch_gemm derives grid.x from args.N. Skinny batches: several row tiles of an expert per CTA
+  // (gate/up 2, down 4), so each CTA streams enough weight chunks to amortise its start-up and fill
+  static int mt_knob = -1;
+  if (mt_knob < 0) {
+    const char* e = getenv("R9K_MOE_MT");
+    mt_knob = (e && e[0] == '0') ? 0 : 1;
+  }
+  const int rt = (int)(N / 128);
+  if (mt_knob && BN == 16 && dual && rt % 2 == 0) {
+    launch_gemm<KIND_MX, 16, true, EPI_SWIGLU_MXFP8, 3, 1, false, 2>(ta, ta2, tb, ga, p, nullptr, st);
+  } else if (mt_knob && BN == 16 && !dual && rt % 4 == 0) {
+    launch_gemm<KIND_MX, 16, false, EPI_BF16, 5, 1, false, 4>(ta, ta, tb, ga, p, nullptr, st);
+  } else if (dual) {
+    dispatch_bn<KIND_MX, true, EPI_SWIGLU_MXFP8>(ta, ta2, tb, ga, p, nullptr, st);
+  } else {
+    dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, ga, p, nullptr, st);
+  }
 }
 
 // Fused gate/up projection + SwiGLU + MXFP8 quantisation of the result.

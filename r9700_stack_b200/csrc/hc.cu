@@ -164,4 +164,160 @@ void hc_combine_norm(torch::Tensor res, c10::optional<torch::Tensor> block, c10:
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// Fused norm point: one 256-thread CTA per row does all of
+//   l[s]   = y . wl[s]                                (the injection logits, fp32)
+//   res_s  = bf16(res_s + y * 2 sigmoid(l[s] / HC))    (stored back)
+//   n_s    = bf16(res_s * rsqrt(mean(res_s^2) + eps) * (1 + w_s))
+//   out    = bf16((1 / HC) sum_s sigmoid(g_s) n_s)     (the next block's input)
+// in two passes over the row (the second re-reads the residual this CTA just wrote). Thread t owns
+// the 8-element chunks t, t + 256, ... of every stream, in both passes.
+constexpr int HCF_NT = 256;
+
+__global__ void __launch_bounds__(HCF_NT) hc_point_kernel(__nv_bfloat16* __restrict__ res, int64_t ldr,
+                                                          const __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                          const __nv_bfloat16* __restrict__ wl,
+                                                          const __nv_bfloat16* __restrict__ w, int w_per_stream,
+                                                          const __nv_bfloat16* __restrict__ g, int64_t ldg, int HC,
+                                                          int HD, float eps, __nv_bfloat16* __restrict__ out,
+                                                          int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[HCF_NT / 32][HC_MAX];
+  __shared__ float s_val[HC_MAX];
+  const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nc = HD / 8;
+  __nv_bfloat16* rr = res + (int64_t)n * ldr;
+  const __nv_bfloat16* yr = y != nullptr ? y + (int64_t)n * ldy : nullptr;
+  auto block_sum = [&](float (&v)[HC_MAX]) {
+#pragma unroll
+    for (int s = 0; s < HC_MAX; ++s) {
+      if (s >= HC) break;
+      float x = v[s];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) red[warp][s] = x;
+    }
+    __syncthreads();
+    if (tid < HC) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < HCF_NT / 32; ++k) t += red[k][tid];
+      s_val[tid] = t;
+    }
+    __syncthreads();
+  };
+  float inj[HC_MAX];
+#pragma unroll
+  for (int s = 0; s < HC_MAX; ++s) inj[s] = 0.f;
+  if (yr != nullptr) {
+    float dot[HC_MAX];
+#pragma unroll
+    for (int s = 0; s < HC_MAX; ++s) dot[s] = 0.f;
+    for (int c = tid; c < nc; c += HCF_NT) {
+      const uint4 yv = reinterpret_cast<const uint4*>(yr)[c];
+      const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&yv);
+#pragma unroll
+      for (int s = 0; s < HC_MAX; ++s) {
+        if (s >= HC) break;
+        const uint4 wv = reinterpret_cast<const uint4*>(wl + (int64_t)s * HD)[c];
+        const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dot[s] += __bfloat162float(ye[k]) * __bfloat162float(we[k]);
+      }
+    }
+    block_sum(dot);
+#pragma unroll
+    for (int s = 0; s < HC_MAX; ++s)
+      if (s < HC) inj[s] = 2.f * hc_sigmoid(s_val[s] / (float)HC);
+  }
+  // pass 1: residual update + per-stream sum of squares
+  float ss[HC_MAX];
+#pragma unroll
+  for (int s = 0; s < HC_MAX; ++s) ss[s] = 0.f;
+  for (int c = tid; c < nc; c += HCF_NT) {
+    uint4 yv = make_uint4(0, 0, 0, 0);
+    if (yr != nullptr) yv = reinterpret_cast<const uint4*>(yr)[c];
+    const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&yv);
+#pragma unroll
+    for (int s = 0; s < HC_MAX; ++s) {
+      if (s >= HC) break;
+      uint4 rv = reinterpret_cast<const uint4*>(rr + (int64_t)s * HD)[c];
+      __nv_bfloat16* re = reinterpret_cast<__nv_bfloat16*>(&rv);
+      if (yr != nullptr) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) re[k] = __float2bfloat16(__bfloat162float(re[k]) + __bfloat162float(ye[k]) * inj[s]);
+        reinterpret_cast<uint4*>(rr + (int64_t)s * HD)[c] = rv;
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = __bfloat162float(re[k]);
+        ss[s] += f * f;
+      }
+    }
+  }
+  block_sum(ss);
+  float rrms[HC_MAX];
+#pragma unroll
+  for (int s = 0; s < HC_MAX; ++s) rrms[s] = s < HC ? rsqrtf(s_val[s] / (float)HD + eps) : 0.f;
+  // pass 2: normalise every stream and mix
+  const float inv = 1.f / (float)HC;
+  const __nv_bfloat16* gr = g + (int64_t)n * ldg;
+  for (int c = tid; c < nc; c += HCF_NT) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < HC_MAX; ++s) {
+      if (s >= HC) break;
+      const uint4 rv = reinterpret_cast<const uint4*>(rr + (int64_t)s * HD)[c];
+      const uint4 wv = reinterpret_cast<const uint4*>(w + (w_per_stream ? (int64_t)s * HD : 0))[c];
+      const uint4 gv = reinterpret_cast<const uint4*>(gr + (int64_t)s * HD)[c];
+      const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv);
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv);
+      const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float t = __bfloat162float(re[k]) * rrms[s];
+        const float nv = __bfloat162float(__float2bfloat16(t + t * __bfloat162float(we[k])));
+        acc[k] += hc_sigmoid(__bfloat162float(ge[k])) * nv;
+      }
+    }
+    uint4 ov;
+    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ob[k] = __floats2bfloat162_rn(acc[2 * k] * inv, acc[2 * k + 1] * inv);
+    reinterpret_cast<uint4*>(out + (int64_t)n * ldo)[c] = ov;
+  }
+}
+
+void hc_point(torch::Tensor res, c10::optional<torch::Tensor> y, torch::Tensor wl, torch::Tensor w, torch::Tensor g,
+              int64_t HC, double eps, torch::Tensor out) {
+  const int64_t T = res.size(0);
+  if (T == 0) return;
+  const int64_t HD = out.size(1);
+  TORCH_CHECK(HC >= 1 && HC <= HC_MAX && res.size(1) == HC * HD && HD % 8 == 0, "hc_point: res [T, HC * HD], HD % 8 == 0");
+  TORCH_CHECK(res.dtype() == torch::kBFloat16 && out.dtype() == torch::kBFloat16 && wl.dtype() == torch::kBFloat16 &&
+                  w.dtype() == torch::kBFloat16 && g.dtype() == torch::kBFloat16,
+              "hc_point: bf16 tensors");
+  TORCH_CHECK(res.stride(1) == 1 && out.stride(1) == 1 && res.stride(0) % 8 == 0 && out.stride(0) % 8 == 0 &&
+                  wl.is_contiguous() && wl.size(0) == HC && wl.size(1) == HD && w.is_contiguous() &&
+                  (w.numel() == HD || w.numel() == HC * HD) && g.stride(1) == 1 && g.size(1) == HC * HD &&
+                  (g.size(0) == 1 || (g.size(0) == T && g.stride(0) % 8 == 0)),
+              "hc_point: shapes / 16-byte aligned rows");
+  const __nv_bfloat16* yp = nullptr;
+  int64_t ldy = 0;
+  if (y.has_value() && y->defined()) {
+    TORCH_CHECK(y->dtype() == torch::kBFloat16 && y->size(1) == HD && y->stride(1) == 1 && y->stride(0) % 8 == 0,
+                "hc_point: y [T, HD] bf16");
+    yp = reinterpret_cast<const __nv_bfloat16*>(y->data_ptr());
+    ldy = y->stride(0);
+  }
+  const at::cuda::CUDAGuard guard(res.device());
+  launch_pdl(hc_point_kernel, dim3((unsigned)T), dim3(HCF_NT), 0, at::cuda::getCurrentCUDAStream(),
+             reinterpret_cast<__nv_bfloat16*>(res.data_ptr()), res.stride(0), yp, ldy,
+             reinterpret_cast<const __nv_bfloat16*>(wl.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+             w.numel() == HC * HD ? 1 : 0, reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+             g.size(0) == 1 ? (int64_t)0 : g.stride(0), (int)HC, (int)HD, (float)eps,
+             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 }  // namespace r9k

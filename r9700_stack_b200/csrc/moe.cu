@@ -210,8 +210,12 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
     }
   }
   int all_rows, all_tiles;
-  const int padded = (total + 127) / 128 * 128;
+  // every work item starts on a 128-row boundary of the sorted buffer: the activation scale factors
+  // are stored in 128-row chunks and a tile reads the chunk its first row falls in. With BN < 128 an
+  // expert's rows are therefore spread as BN rows per 128-row slot.
   const int ntile = (total + BN - 1) / BN;
+  const int padded = BN >= 128 ? (total + 127) / 128 * 128 : ntile * 128;
+  const int stride = BN >= 128 ? BN : 128;
   const int st = block_exclusive_scan(tid < E_local ? padded : 0, wsum, all_rows);
   const int tl = block_exclusive_scan(tid < E_local ? ntile : 0, wsum, all_tiles);
   if (tid < E_local) {
@@ -221,7 +225,7 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
       const int wi = tl + i;
       if (wi < max_work) {
         work[wi * 3 + 0] = tid;
-        work[wi * 3 + 1] = st + i * BN;
+        work[wi * 3 + 1] = st + i * stride;
         work[wi * 3 + 2] = min(BN, total - i * BN);
       }
     }
@@ -237,7 +241,10 @@ __global__ void __launch_bounds__(1024) moe_align_kernel(const int32_t* __restri
     }
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     if (a < a1) {
-      if (e >= 0) perm_row[a] = start[e] + mycnt[e] + __popc(peers & ((1u << lane) - 1u));
+      if (e >= 0) {
+        const int r = mycnt[e] + __popc(peers & ((1u << lane) - 1u));  // rank within the expert
+        perm_row[a] = start[e] + (BN >= 128 ? r : (r / BN) * 128 + r % BN);
+      }
       else perm_row[a] = -1;
     }
     __syncwarp();

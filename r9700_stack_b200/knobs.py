@@ -25,7 +25,10 @@ _DEFAULTS = {
     "R9K_AR_QUANT_MIN_KB": "1024",  # smallest message sent compressed
     "R9K_SPIN_TIMEOUT_MS": "1000",
     "R9K_AR_HIST": "0",  # 1: histogram of all-reduce message sizes (utils.trace.AR_HIST)
-    "R9K_TRACE": "0",  # 1: the runner attaches a utils.trace.DeviceTrace to the model
+    "R9K_TRACE": "0",
+    "R9K_GEMM_L2PF": "0",  # skinny GEMMs: weight chunks prefetched into L2 beyond the smem ring (0: off; 4-16 measured slower)
+    "R9K_MOE_MT": "1",  # 1: grouped skinny MoE GEMMs run several row tiles per CTA (gate/up 2, down 4); 0: one
+    "R9K_HC_FUSED": "1",  # 1: one kernel per hyper-connection norm point; 0: logits GEMM + combine_norm + gate_mix  # 1: the runner attaches a utils.trace.DeviceTrace to the model
 }
 _cache: dict[str, str] = {}
 

@@ -532,6 +532,11 @@ class HybridLM:
 
         c = self.cfg
         HC = c.hc_streams
+        if knobs.get("R9K_HC_FUSED") != "0":
+            HCo.point(ws.hc_x[:T], ws.y[:T] if block else None, p, HC, c.rms_eps, ws.norm_out[:T])
+            if self.mx and not final:
+                L.quant_act(ws.norm_out[:T], out=ws.act.narrow(T))
+            return
         if block:
             L.bf16_linear(ws.y[:T], p.wl, out=ws.hc_l[:T], out_dtype=torch.float32)
         HCo.combine_norm(ws.hc_x[:T], ws.y[:T] if block else None, ws.hc_l[:T] if block else None, p.w, HC, c.rms_eps,
@@ -544,21 +549,36 @@ class HybridLM:
         """Forward with hyper-connection residual streams (unfused all-reduce after each block)."""
         c = self.cfg
         HC, H = c.hc_streams, c.hidden
+        tr = self.trace
+        if tr is not None:
+            tr.begin()
+            tr.mark("start")
         self._embed(meta, ws, T)
         ws.hc_x[:T].view(T, HC, H).copy_(ws.resid[:T, None, :])
         for i, lay in enumerate(self.layers):
             self._hc_point(lay["hc_in"], ws, T, block=i > 0)
+            if tr is not None:
+                tr.mark(f"L{i}.hc")
             if lay["attn"]:
                 act, xb, w = self._attention(i, lay, meta, ws, T)
             else:
                 act, xb, w = self._gdn(i, lay, meta, ws, T)
             self._row_parallel(act, xb, w, ws, T, call=2 * i, fused=False)
+            if tr is not None:
+                tr.mark(f"L{i}.{'attn' if lay['attn'] else 'gdn'}")
             self._hc_point(lay["hc_post"], ws, T, block=True)
+            if tr is not None:
+                tr.mark(f"L{i}.hc")
             self._ffn_block(i, lay, meta, ws, T, call=2 * i + 1, fused=False)
+            if tr is not None:
+                tr.mark(f"L{i}.ffn")
         self._hc_point(self.hc_final, ws, T, block=True, final=True)
         # the stream mean stands for the pre-norm hidden state (what MTP / block drafters read)
         torch.mean(ws.hc_x[:T].view(T, HC, H), dim=1, out=ws.resid[:T])
-        return self._lm_head(meta, ws, T, R)
+        out = self._lm_head(meta, ws, T, R)
+        if tr is not None:
+            tr.mark("lm_head")
+        return out
 
     def _lm_head(self, meta: StepMeta, ws: Workspace, T: int, R: int) -> torch.Tensor:
         rows = ws.final_bf16[:R]

@@ -38,7 +38,8 @@ class MoEBuffers:
         self.wts = torch.zeros(max_tokens, k, dtype=torch.float32, device=dev)
         self.perm_row = torch.zeros(A, dtype=torch.int32, device=dev)
         self.seg_start = torch.zeros(E_local, dtype=torch.int32, device=dev)
-        self.max_rows = A + 128 * min(E_local, A)
+        # sorted rows: 128-row aligned segments, and with token tiles under 128 one 128-row slot per tile
+        self.max_rows = A + 256 * min(E_local, A)
         self.max_work = A + E_local
         self.work = torch.zeros(self.max_work, 3, dtype=torch.int32, device=dev)
         self.work_count = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -64,8 +65,11 @@ def moe_ffn(lay, x: torch.Tensor, mb: MoEBuffers, out: torch.Tensor, *, k: int, 
         L.bf16_linear(x, lay["router"], out=mb.logits_e[:T], out_dtype=torch.float32)
         o.moe_route(mb.logits_e[:T], k, route_mode, bias, n_group, topk_group, float(scale), renorm, mb.ids[:T],
                     mb.wts[:T])
-    BN = 16 if T <= 16 else 128
     A = T * k
+    # token tile from the expected rows per active expert (not from T): at T = 64, top-10 over 288
+    # experts an expert sees ~2 rows, and 128-token tiles would be almost empty
+    per_expert = A / max(1, min(E_local, A))
+    BN = 16 if per_expert <= 16 else 32 if per_expert <= 32 else 64 if per_expert <= 64 else 128
     ids = mb.ids[:T] if remap is None else remap(mb.ids[:T])  # expert ids, or cache slot ids
     o.moe_align(ids, e0, E_local, BN, mb.perm_row[:A], mb.seg_start, mb.work, mb.work_count)
     L.quant_act(x, out=mb.moe_act.narrow(T))

@@ -48,6 +48,18 @@ def gate_mix(x, g, HC: int, out) -> None:
     _native.ops().hc_gate_mix(x, g, HC, out)
 
 
+def point(res, y, p: HCPoint, HC: int, eps: float, out) -> None:
+    """Fused norm point (injection logits, residual update, per-stream norm, gated mix) in one launch."""
+    _native.ops().hc_point(res, y, p.wl.w, p.w, p.g, HC, float(eps), out)
+
+
+def point_ref(res, y, p: HCPoint, HC: int, eps: float):
+    """(new residual, next block input) of a norm point, in torch."""
+    l = y.float() @ p.wl.w.float().T if y is not None else None
+    r, n = combine_norm_ref(res, y, l, p.w, HC, eps)
+    return r, gate_mix_ref(n, p.g, HC)
+
+
 def combine_norm_ref(res, block, l, w, HC: int, eps: float):
     """(new residual, normalised streams), both bf16, as the kernel computes them."""
     T, D = res.shape

@@ -27,7 +27,8 @@ def parse(argv=None):
     ap.add_argument("--max-model-len", type=int, default=32768)
     ap.add_argument("--max-prefill-tokens", type=int, default=8192)
     ap.add_argument("--kv-blocks", type=int, default=0, help="0: sized from max-batch x max-model-len")
-    ap.add_argument("--spec", default="none", choices=["none", "ngram", "mtp", "block"])
+    ap.add_argument("--spec", default="none", choices=["none", "ngram", "mtp", "block", "dspark"])
+    ap.add_argument("--ep-placement", default="", help="JSON expert placement (parallel.ep_placement) for MoE models")
     ap.add_argument("--spec-tokens", type=int, default=0)
     ap.add_argument("--graph-sizes", default="1,2,4,8,16")
     ap.add_argument("--no-graphs", action="store_true")
@@ -45,11 +46,11 @@ def plan(a) -> dict:
     world = int(os.environ.get("WORLD_SIZE", "1"))
     k = a.spec_tokens if a.spec != "none" else 0
     if a.spec != "none" and k == 0:
-        k = cfg.draft_block - 1 if a.spec == "block" else 3
+        k = cfg.draft_block - 1 if a.spec in ("block", "dspark") else 3
     ec = EngineConfig(max_batch=a.max_batch, max_model_len=a.max_model_len, max_prefill_tokens=a.max_prefill_tokens,
                       num_kv_blocks=a.kv_blocks, cuda_graphs=not a.no_graphs,
                       graph_batch_sizes=[int(x) for x in a.graph_sizes.split(",") if x],
-                      spec_tokens=k, spec_method=a.spec if a.spec != "none" else "ngram")
+                      spec_tokens=k, spec_method=a.spec if a.spec != "none" else "ngram", ep_placement=a.ep_placement)
     blocks = ec.num_kv_blocks or (ec.max_batch * math.ceil(ec.max_model_len / ec.kv_block) + 1)
     if hasattr(cfg, "attn_layers"):  # hybrid GDN / attention
         hkv = max(1, cfg.n_kv_heads // world)

@@ -124,8 +124,9 @@ def bench_moe(a) -> dict:
     x = L.quant_act(torch.randn(T, H, device="cuda").bfloat16())
     logits = torch.randn(T, E, device="cuda")
     A = T * k
-    BN = 16 if T <= 16 else 128
-    max_rows = A + 128 * min(E, A)
+    per_expert = A / max(1, min(E, A))  # token tile as moe_ffn picks it
+    BN = 16 if per_expert <= 16 else 32 if per_expert <= 32 else 64 if per_expert <= 64 else 128
+    max_rows = A + 256 * min(E, A)
     ids = torch.empty(T, k, dtype=torch.int32, device="cuda")
     wts = torch.empty(T, k, device="cuda")
     perm = torch.empty(A, dtype=torch.int32, device="cuda")

@@ -47,8 +47,14 @@ def test_combine_norm(hc, hd, per_stream, with_block):
     assert torch.allclose(y.float(), ref_y.float(), atol=2e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("fused", ["1", "0"])
 @pytest.mark.parametrize("moe", [False, True])
-def test_tiny_hc_model_matches_reference(moe):
+def test_tiny_hc_model_matches_reference(moe, fused, monkeypatch, request):
+    from r9700_stack_b200 import knobs
+
+    monkeypatch.setenv("R9K_HC_FUSED", fused)
+    knobs.refresh()
+    request.addfinalizer(knobs.refresh)  # runs after monkeypatch restored the environment
     from r9700_stack_b200.engine.llm import LLM
     from r9700_stack_b200.engine.scheduler import SamplingParams
     from r9700_stack_b200.models.config import EngineConfig, tiny_hybrid, tiny_moe
@@ -72,3 +78,21 @@ def test_tiny_hc_model_matches_reference(moe):
         got = llm.runner.ws.logits[0].clone()
         ref = reference_forward(llm.model, [seq.output[-2]], st)[-1]
         assert cos(got, ref) > 0.99, cos(got, ref)
+
+
+@pytest.mark.parametrize("hc,hd", [(4, 2048), (2, 5120), (8, 256)])
+@pytest.mark.parametrize("with_block", [True, False])
+def test_fused_point(hc, hd, with_block):
+    from r9700_stack_b200.models.weights import WeightFactory
+
+    torch.manual_seed(2)
+    T = 6
+    p = HC.random_point(WeightFactory(torch.device("cuda"), seed=5, std=0.02), hc, hd)
+    res = torch.randn(T, hc * hd).bfloat16().cuda()
+    y = torch.randn(T, hd).bfloat16().cuda() if with_block else None
+    ref_res, ref_out = HC.point_ref(res.clone(), y, p, hc, 1e-6)
+    out = torch.empty(T, hd, dtype=torch.bfloat16, device="cuda")
+    HC.point(res, y, p, hc, 1e-6, out)
+    _check()
+    assert torch.allclose(res.float(), ref_res.float(), atol=1e-2, rtol=1e-2)
+    assert torch.allclose(out.float(), ref_out.float(), atol=2e-2, rtol=2e-2)

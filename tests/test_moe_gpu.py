@@ -54,7 +54,7 @@ def test_route_sigmoid_grouped():
     torch.testing.assert_close(w.sort(-1).values, rw.sort(-1).values)
 
 
-@pytest.mark.parametrize("T,BN", [(5, 16), (40, 128)])
+@pytest.mark.parametrize("T,BN", [(5, 16), (40, 128), (40, 16), (60, 32), (90, 64)])
 def test_grouped_experts_match_torch(T, BN):
     from r9700_stack_b200.ops import linear as L
     from r9700_stack_b200.quant import formats as F
@@ -69,7 +69,7 @@ def test_grouped_experts_match_torch(T, BN):
     ids = torch.stack([torch.randperm(E)[:k] for _ in range(T)]).int().cuda()
     w = torch.rand(T, k).cuda()
     A = T * k
-    max_rows = A + 128 * min(E, A)
+    max_rows = A + 256 * min(E, A)
     perm = torch.empty(A, dtype=torch.int32, device="cuda")
     seg = torch.empty(E, dtype=torch.int32, device="cuda")
     work = torch.zeros(A + E, 3, dtype=torch.int32, device="cuda")
@@ -126,7 +126,8 @@ def test_tiny_moe_model_matches_reference():
     assert float(cos) > 0.99, float(cos)
 
 
-@pytest.mark.parametrize("T,k,E,e0,El,BN", [(16, 10, 288, 0, 288, 16), (3000, 8, 256, 64, 128, 128), (7, 2, 8, 0, 8, 16)])
+@pytest.mark.parametrize("T,k,E,e0,El,BN", [(16, 10, 288, 0, 288, 16), (3000, 8, 256, 64, 128, 128), (7, 2, 8, 0, 8, 16),
+                                            (64, 10, 8, 0, 8, 16), (200, 4, 16, 0, 16, 32)])
 def test_align_matches_python(T, k, E, e0, El, BN):
     torch.manual_seed(T)
     ids = torch.randint(0, E, (T, k), dtype=torch.int32)
@@ -143,20 +144,24 @@ def test_align_matches_python(T, k, E, e0, El, BN):
     for e in flat:
         if e0 <= e < e0 + El:
             cnt[e - e0] += 1
+    # every work item starts on a 128-row boundary: with BN < 128 one 128-row slot per BN rows
+    stride = BN if BN >= 128 else 128
     start, s = [], 0
     for c in cnt:
         start.append(s)
-        s += (c + 127) // 128 * 128
+        s += (c + 127) // 128 * 128 if BN >= 128 else (c + BN - 1) // BN * 128
     ref_perm, cur = [], [0] * El
     for e in flat:
         if e0 <= e < e0 + El:
-            ref_perm.append(start[e - e0] + cur[e - e0])
+            r = cur[e - e0]
+            ref_perm.append(start[e - e0] + (r if BN >= 128 else (r // BN) * 128 + r % BN))
             cur[e - e0] += 1
         else:
             ref_perm.append(-1)
     assert perm.cpu().tolist() == ref_perm
     assert seg.cpu().tolist() == start
-    ref_work = [[e, start[e] + i * BN, min(BN, cnt[e] - i * BN)] for e in range(El) for i in range((cnt[e] + BN - 1) // BN)]
+    ref_work = [[e, start[e] + i * stride, min(BN, cnt[e] - i * BN)] for e in range(El)
+                for i in range((cnt[e] + BN - 1) // BN)]
     assert int(wc) == len(ref_work)
     assert work[: len(ref_work)].cpu().tolist() == ref_work
 
