@@ -160,11 +160,12 @@ __global__ void __launch_bounds__(192, 1)
       const uint64_t pol_x = policy_evict_last();
       // Weights do not depend on the previous kernel: the first NP weight tiles are requested before
       // waiting on the predecessor grid (programmatic dependent launch). Activations come after.
-      // chunk q of this CTA: row tile q / nk, k-chunk q % nk (MT row tiles stream through one ring)
+      // chunk q of this CTA: row tile q / nk, k-chunk q % nk (MT row tiles stream through one ring;
+      // with MT == 1 both fold away at compile time)
       auto load_a = [&](int q) {
         const int s = q % NP;
-        const int kc = kc0 + q % nk;
-        const int mt = m0 + (q / nk) * 128;
+        const int kc = kc0 + (MT == 1 ? q : q % nk);
+        const int mt = m0 + (MT == 1 ? 0 : q / nk) * 128;
         uint8_t* sa = smem + C::OFF_A + s * C::NA * C::AL_BYTES;
         mbar_arrive_expect_tx(&l_full[s], stage_tx);
         load_a_tile(sa, &tmA, &l_full[s], args, kc, box_x, mt, pol_w);
@@ -177,7 +178,7 @@ __global__ void __launch_bounds__(192, 1)
       };
       auto load_b = [&](int q) {
         const int s = q % NP;
-        const int kc = kc0 + q % nk;
+        const int kc = kc0 + (MT == 1 ? q : q % nk);
         tma_load_2d_hint(smem + C::OFF_B + s * C::B_BYTES, &tmB, &l_full[s], kc * ((KIND == KIND_BF16) ? 64 : 128), n0,
                          pol_x);
         if constexpr (KIND == KIND_MX) {
@@ -191,8 +192,8 @@ __global__ void __launch_bounds__(192, 1)
       // shared-memory stages alone hold (weights only; activations are small and L2-resident)
       const int PD = args.l2_prefetch;
       auto prefetch_a = [&](int q) {
-        const int kc = kc0 + q % nk;
-        const int mt = m0 + (q / nk) * 128;
+        const int kc = kc0 + (MT == 1 ? q : q % nk);
+        const int mt = m0 + (MT == 1 ? 0 : q / nk) * 128;
         prefetch_a_tile(&tmA, args, kc, box_x, mt);
         if (DUAL) prefetch_a_tile(&tmA2, args, kc, box_x, mt);
         if constexpr (KIND == KIND_MX) {
@@ -224,7 +225,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int q = 0; q < nk * MT; ++q) {
         const int s = q % NP;
         const int sc = q % NC;
-        const int i = q % nk;  // k-chunk within the row tile
+        const int i = MT == 1 ? q : q % nk;  // k-chunk within the row tile
         if (!mbar_wait(&l_full[s], (uint32_t)((q / NP) & 1), args.timeout_ns) ||
             (UNPACK && !mbar_wait(&c_full[sc], (uint32_t)((q / NC) & 1), args.timeout_ns))) {
           report_error(args.status, kErrMbarTimeout, 101, q);
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(192, 1)
         for (int k = 0; k < 4; ++k) {
           const uint64_t bd = sdesc_k_sw128(sb + 32 * k);
           const int ai = k % C::NACC;
-          const uint32_t dacc = tbase + (uint32_t)((q / nk) * C::ACC_TILE + ai * BN * C::NA);
+          const uint32_t dacc = tbase + (uint32_t)((MT == 1 ? 0 : q / nk) * C::ACC_TILE + ai * BN * C::NA);
           const uint32_t acc = (i > 0 || k >= C::NACC) ? 1u : 0u;
           if constexpr (KIND == KIND_MX) {
             const uint32_t idesc = idesc_block_scaled(args.a_fmt, kFmtE4M3, 128, BN, (uint32_t)k, (uint32_t)k);
