@@ -4,6 +4,8 @@
     python -m r9700_stack_b200.tuning.kbench gemm --N 17408 --K 5120 --M 16 --fmt fp4 --swiglu
     python -m r9700_stack_b200.tuning.kbench moe --T 16 --E 288 --topk 10 --H 2048 --I 512
     python -m r9700_stack_b200.tuning.kbench gemm ... --reps 1 --warmup 0     # one launch (for ncu -c 1)
+    python -m r9700_stack_b200.tuning.kbench qsa --S 16 --ctx 8192 --topk 512     # QSA sparse decode attention
+    python -m r9700_stack_b200.tuning.kbench hc --T 16 --hc 4 --H 2048             # fused hyper-connection point
     python -m r9700_stack_b200.tuning.kbench decode --model dense27b --streams 16 --reps 2 --eager
         # eager decode steps of a whole model inside NVTX ranges "decode_step" (ncu --nvtx-include)
 
@@ -258,6 +260,60 @@ def bench_attn(a) -> dict:
             "weight_bytes": kv_bytes, "flops": 4.0 * S * hq * ctx * D}
 
 
+def bench_qsa(a) -> dict:
+    """QSA sparse decode attention (Flash-Next full-attention layers): S sequences at ctx positions,
+    each attending to k selected 4-token groups + its open group's tail, hq / hkv heads of 256 over
+    a paged fp8 KV cache. Bytes = the gathered K and V rows."""
+    from .. import _native
+    from ..utils import status
+
+    torch.manual_seed(0)
+    S, ctx, hq, hkv, D, BLK, K = a.S, a.ctx, a.hq, a.hkv, 256, 64, a.topk
+    nbps = (ctx + BLK - 1) // BLK
+    nblk = S * nbps + 1
+    kc = torch.randint(0, 255, (nblk, hkv, BLK, D), dtype=torch.uint8, device="cuda") & 0x7E
+    vc = torch.randint(0, 255, (nblk, hkv, BLK, D), dtype=torch.uint8, device="cuda") & 0x7E
+    bt = (torch.arange(S * nbps, dtype=torch.int32, device="cuda") + 1).view(S, nbps)
+    q = torch.randn(S, hq, D, device="cuda").bfloat16()
+    tok_ctx = torch.full((S,), ctx, dtype=torch.int32, device="cuda")
+    tok_seq = torch.arange(S, dtype=torch.int32, device="cuda")
+    vis = ctx // 4
+    sel = torch.stack([torch.randperm(vis, device="cuda")[:K].sort().values for _ in range(S)]).int()
+    cnt = torch.full((S,), min(K, vis), dtype=torch.int32, device="cuda")
+    nsplit = a.nsplit or max(1, min(16, -(-296 // (S * hkv))))
+    po = torch.empty(S * hq, nsplit, D, device="cuda")
+    pml = torch.empty(S * hq, nsplit, 2, device="cuda")
+    gate = torch.randn(S, hq * D, device="cuda").bfloat16()
+    out = torch.empty(S, hq * D, dtype=torch.bfloat16, device="cuda")
+    ops = _native.ops()
+    f = lambda i: ops.qsa_attention(q, kc, vc, bt, tok_seq, tok_ctx, sel, cnt, D ** -0.5, 1.0, 1.0, nsplit, po, pml,
+                                    gate, out)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    status.check()
+    keys = 4 * min(K, vis) + (ctx - 4 * vis)
+    return {"kernel": "qsa_attention", "S": S, "ctx": ctx, "topk_groups": K, "hq": hq, "hkv": hkv, "nsplit": nsplit,
+            "us": us, "weight_bytes": 2.0 * S * hkv * keys * D, "flops": 4.0 * S * hq * keys * D}
+
+
+def bench_hc(a) -> dict:
+    """Fused hyper-connection norm point: T rows, HC streams of H (bytes: residual read + write, the
+    re-read of the second pass, block output, weights, gates and the mixed output)."""
+    from ..models.weights import WeightFactory
+    from ..ops import hc as HCo
+    from ..utils import status
+
+    T, HC, H = a.T, a.hc, a.H
+    p = HCo.random_point(WeightFactory(torch.device("cuda"), seed=1, std=0.02), HC, H)
+    res = torch.randn(T, HC * H, device="cuda").bfloat16()
+    y = torch.randn(T, H, device="cuda").bfloat16()
+    out = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    f = lambda i: HCo.point(res, y, p, HC, 1e-6, out)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    status.check()
+    nbytes = 2.0 * (3 * T * HC * H + 2 * T * H + 3 * HC * H)
+    return {"kernel": "hc_point", "T": T, "HC": HC, "H": H, "us": us, "weight_bytes": nbytes, "flops": 0.0}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -291,12 +347,24 @@ def main(argv=None):
     at.add_argument("--hq", type=int, default=24)
     at.add_argument("--hkv", type=int, default=4)
     at.add_argument("--nsplit", type=int, default=0)
-    for p in (g, m, d, gd, at):
+    qs = sub.add_parser("qsa")
+    qs.add_argument("--S", type=int, default=16)
+    qs.add_argument("--ctx", type=int, default=8192)
+    qs.add_argument("--hq", type=int, default=16)
+    qs.add_argument("--hkv", type=int, default=2)
+    qs.add_argument("--topk", type=int, default=512)
+    qs.add_argument("--nsplit", type=int, default=0)
+    hcp = sub.add_parser("hc")
+    hcp.add_argument("--T", type=int, default=16)
+    hcp.add_argument("--hc", type=int, default=4)
+    hcp.add_argument("--H", type=int, default=2048)
+    for p in (g, m, d, gd, at, qs, hcp):
         p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn, "attn": bench_attn}[a.cmd](a)
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn, "attn": bench_attn,
+         "qsa": bench_qsa, "hc": bench_hc}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:
         r["gbs"] = r["weight_bytes"] / r["us"] / 1e3
