@@ -30,7 +30,6 @@ constexpr int QSA_D = 256;    // attention head dim
 constexpr int QSA_ID = 128;   // indexer dim
 constexpr int QSA_KT = 32;    // keys per tile
 constexpr int QSA_GMAX = 16;  // query heads per kv head
-constexpr int QSA_KROW = 260; // smem bytes per staged fp8 key row (65 words: conflict-free column reads)
 
 // one warp per row: 128 bf16 = 16 lanes x 16 bytes
 __global__ void qsa_key_write_kernel(const __nv_bfloat16* __restrict__ ik, int64_t ld, const int32_t* __restrict__ slots,
@@ -97,15 +96,25 @@ struct QsaArgs {
   float v_scale;
 };
 
-// grid (T, hkv, nsplit), 256 threads: warp w owns query heads w and w + 8 of this kv head
+// grid (T, hkv, nsplit), 256 threads, GP = query heads per kv head padded to 8 or 16. Per 32-key tile:
+//   gather   fp8 K and V rows into shared memory (16 bytes per thread per pass)
+//   scores   warp w owns keys 4w .. 4w + 3: each lane decodes 8 dims of the key once and dots them
+//            with every head's query; a butterfly reduction leaves head h's sum in lanes of that head
+//   softmax  warp w owns heads w (and w + 8): online max / sum over the tile, p -> p_t[key][head]
+//   P V      warp w owns dims 32w .. 32w + 31 for every head: each V element is decoded once
+// so every fp8 element is converted once per tile, not once per head.
+template <int GP>
 __global__ void __launch_bounds__(256) qsa_attn_kernel(const QsaArgs a) {
   pdl_wait();
   pdl_trigger();
-  __shared__ __align__(16) float q_s[QSA_GMAX][QSA_D];
-  __shared__ __align__(16) uint8_t k_s[QSA_KT * QSA_KROW];
-  __shared__ __align__(16) uint8_t v_s[QSA_KT][QSA_D];
-  __shared__ float p_s[QSA_GMAX][QSA_KT];
-  __shared__ int tok_s[QSA_KT];
+  __shared__ __align__(16) float q_s[GP][QSA_D];
+  // K and V tiles, double-buffered (tile i + 1 loads during tile i): 32 KB of dynamic shared memory
+  extern __shared__ __align__(16) uint8_t qsa_dyn[];
+  auto k_s = reinterpret_cast<uint8_t(*)[QSA_KT][QSA_D]>(qsa_dyn);
+  auto v_s = reinterpret_cast<uint8_t(*)[QSA_KT][QSA_D]>(qsa_dyn + 2 * QSA_KT * QSA_D);
+  __shared__ __align__(16) float s_s[GP][QSA_KT];  // scores of the tile, by head
+  __shared__ __align__(16) float p_t[QSA_KT][GP];  // probabilities, by key
+  __shared__ float corr_s[GP], m_s[GP], l_s[GP];
   const int t = blockIdx.x, h = blockIdx.y, sp = blockIdx.z, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int G = a.G;
   const int seq = a.tok_seq[t], ctx = a.tok_ctx[t];
@@ -116,126 +125,154 @@ __global__ void __launch_bounds__(256) qsa_attn_kernel(const QsaArgs a) {
   const int t0 = sp * tps, t1 = min(ntile, t0 + tps);
   const int32_t* row = a.bt + (int64_t)seq * a.mb;
   const int32_t* sel = a.sel + (int64_t)t * a.ld_sel;
-  for (int i = tid; i < G * QSA_D; i += 256) {
+  for (int i = tid; i < GP * QSA_D; i += 256) {
     const int hh = i / QSA_D, d = i - hh * QSA_D;
-    q_s[hh][d] = __bfloat162float(a.q[(int64_t)t * a.ldq + (int64_t)(h * G + hh) * QSA_D + d]);
+    q_s[hh][d] = hh < G ? __bfloat162float(a.q[(int64_t)t * a.ldq + (int64_t)(h * G + hh) * QSA_D + d]) : 0.f;
   }
-  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
-  float o[2][8];
+  // head-warp state (heads warp, warp + 8) and dim-warp accumulators (dim 32 warp + lane, every head)
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float o[GP];
 #pragma unroll
-  for (int j = 0; j < 2; ++j)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) o[j][i] = 0.f;
-  for (int tile = t0; tile < t1; ++tile) {
+  for (int j = 0; j < GP; ++j) o[j] = 0.f;
+  const int dim = 32 * warp + lane;
+  // gather of one tile into buffer b: 16 bytes of K and of V per thread per pass, zero-filled past the
+  // key list (every thread derives its key's token itself, so no extra barrier is needed)
+  auto issue = [&](int tile, int b) {
     const int j0 = tile * QSA_KT, nk = min(QSA_KT, L - j0);
-    __syncthreads();  // previous tile's smem reads are done
-    if (tid < QSA_KT) {
-      const int j = j0 + tid;
-      int tok = -1;
-      if (tid < nk) tok = j < 4 * cnt ? 4 * sel[j >> 2] + (j & 3) : 4 * vis + (j - 4 * cnt);
-      tok_s[tid] = tok;
-    }
-    __syncthreads();
-    // gather: 32 keys x 256 B of K and of V, 16 bytes per thread per pass
     for (int i = tid; i < QSA_KT * 16; i += 256) {
       const int kk = i >> 4, c = i & 15;
-      const int tok = tok_s[kk];
-      uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-      if (tok >= 0) {
-        const int64_t off = (((int64_t)row[tok >> 6] * a.hkv + h) * 64 + (tok & 63)) * QSA_D + 16 * c;
-        kv = *reinterpret_cast<const uint4*>(a.kc + off);
-        vv = *reinterpret_cast<const uint4*>(a.vc + off);
+      const int j = j0 + kk;
+      int64_t off = 0;
+      uint32_t bytes = 0;
+      if (kk < nk) {
+        const int tok = j < 4 * cnt ? 4 * sel[j >> 2] + (j & 3) : 4 * vis + (j - 4 * cnt);
+        off = (((int64_t)row[tok >> 6] * a.hkv + h) * 64 + (tok & 63)) * QSA_D + 16 * c;
+        bytes = 16;
       }
-      uint32_t* kd = reinterpret_cast<uint32_t*>(k_s + kk * QSA_KROW + 16 * c);
-      kd[0] = kv.x;
-      kd[1] = kv.y;
-      kd[2] = kv.z;
-      kd[3] = kv.w;
-      reinterpret_cast<uint4*>(&v_s[kk][0])[c] = vv;
+      const uint32_t dk = static_cast<uint32_t>(__cvta_generic_to_shared(&k_s[b][kk][16 * c]));
+      const uint32_t dv = static_cast<uint32_t>(__cvta_generic_to_shared(&v_s[b][kk][16 * c]));
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dk), "l"(a.kc + off), "r"(bytes) : "memory");
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dv), "l"(a.vc + off), "r"(bytes) : "memory");
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  if (t0 < t1) issue(t0, 0);
+  for (int tile = t0; tile < t1; ++tile) {
+    const int j0 = tile * QSA_KT, nk = min(QSA_KT, L - j0);
+    const int b = (tile - t0) & 1;
+    __syncthreads();  // the previous tile's shared reads are done (buffer b ^ 1 is free)
+    if (tile + 1 < t1) issue(tile + 1, b ^ 1);
+    else asm volatile("cp.async.commit_group;" ::: "memory");
+    asm volatile("cp.async.wait_group 1;" ::: "memory");
+    __syncthreads();
+    // scores: 4 keys per warp, lane = 8 dims
+#pragma unroll 1
+    for (int kq = 0; kq < 4; ++kq) {
+      const int kk = 4 * warp + kq;
+      const uint2 raw = *reinterpret_cast<const uint2*>(&k_s[b][kk][8 * lane]);
+      float kf[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kf[i] = e4m3_to_f32((uint8_t)(raw.x >> (8 * i)));
+        kf[4 + i] = e4m3_to_f32((uint8_t)(raw.y >> (8 * i)));
+      }
+      float v[GP];
+#pragma unroll
+      for (int hh = 0; hh < GP; ++hh) {
+        const float4 qa = *reinterpret_cast<const float4*>(&q_s[hh][8 * lane]);
+        const float4 qb = *reinterpret_cast<const float4*>(&q_s[hh][8 * lane + 4]);
+        v[hh] = qa.x * kf[0] + qa.y * kf[1] + qa.z * kf[2] + qa.w * kf[3] + qb.x * kf[4] + qb.y * kf[5] +
+                qb.z * kf[6] + qb.w * kf[7];
+      }
+      // butterfly: each step halves the values a lane holds (lanes with the mask bit keep the upper half)
+#pragma unroll
+      for (int n = GP, m = 16; n > 1; n >>= 1, m >>= 1) {
+        const bool up = lane & m;
+#pragma unroll
+        for (int j = 0; j < n / 2; ++j) {
+          const float keep = up ? v[j + n / 2] : v[j];
+          const float send = up ? v[j] : v[j + n / 2];
+          v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+      }
+      // lanes sharing the remaining low bits hold the same head's partials: finish the sum over them
+      constexpr int LOWB = GP == 16 ? 2 : 4;  // lanes per head after the butterfly
+#pragma unroll
+      for (int m = LOWB / 2; m >= 1; m >>= 1) v[0] += __shfl_xor_sync(0xffffffffu, v[0], m);
+      // step with mask m kept the upper half in lanes with bit m set, so the head is lane / LOWB
+      const int head = lane / LOWB;
+      if ((lane & (LOWB - 1)) == 0) s_s[head][kk] = v[0];
     }
     __syncthreads();
-    // scores: lane = key, warp = head (and head + 8)
+    // softmax: head-warps, lane = key
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
       const int hh = warp + 8 * j;
-      if (hh >= G) break;
-      float s = 0.f;
-      const uint32_t* kr = reinterpret_cast<const uint32_t*>(k_s + lane * QSA_KROW);
-#pragma unroll 8
-      for (int d4 = 0; d4 < QSA_D / 4; ++d4) {
-        const uint32_t w = kr[d4];
-        const float4 qv = *reinterpret_cast<const float4*>(&q_s[hh][4 * d4]);
-        s += qv.x * e4m3_to_f32((uint8_t)w) + qv.y * e4m3_to_f32((uint8_t)(w >> 8)) +
-             qv.z * e4m3_to_f32((uint8_t)(w >> 16)) + qv.w * e4m3_to_f32((uint8_t)(w >> 24));
-      }
-      s = lane < nk ? s * a.scale : -INFINITY;
-      float mx = s;
+      if (hh >= GP) break;
+      const float sc = (lane < nk && hh < G) ? s_s[hh][lane] * a.scale : -INFINITY;
+      float mx = sc;
 #pragma unroll
       for (int k = 16; k; k >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, k));
-      const float mn = fmaxf(m[j], mx);
-      const float p = exp2f(s - mn);
-      float ps = p;
+      const float mn = fmaxf(m_run[j], mx);
+      const float pv = (mn == -INFINITY) ? 0.f : exp2f(sc - mn);
+      float ps = pv;
 #pragma unroll
       for (int k = 16; k; k >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, k);
-      const float corr = exp2f(m[j] - mn);
-      l[j] = l[j] * corr + ps;
-      m[j] = mn;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) o[j][i] *= corr;
-      p_s[hh][lane] = p;
+      const float corr = (mn == -INFINITY) ? 1.f : exp2f(m_run[j] - mn);
+      l_run[j] = l_run[j] * corr + ps;
+      m_run[j] = mn;
+      p_t[lane][hh] = pv;
+      if (lane == 0) corr_s[hh] = corr;
     }
-    __syncwarp();
-    // P V: lane owns dims 8 lane .. 8 lane + 7
+    __syncthreads();
+    // P V: dim-warps, lane = dim
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int hh = warp + 8 * j;
-      if (hh >= G) break;
-      for (int kk = 0; kk < nk; ++kk) {
-        const float p = p_s[hh][kk];
-        const uint2 vw = *reinterpret_cast<const uint2*>(&v_s[kk][8 * lane]);
+    for (int hh = 0; hh < GP; ++hh) o[hh] *= corr_s[hh];
+    for (int kk = 0; kk < nk; ++kk) {
+      const float vf = e4m3_to_f32(v_s[b][kk][dim]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          o[j][i] += p * e4m3_to_f32((uint8_t)(vw.x >> (8 * i)));
-          o[j][4 + i] += p * e4m3_to_f32((uint8_t)(vw.y >> (8 * i)));
-        }
+      for (int hq4 = 0; hq4 < GP / 4; ++hq4) {
+        const float4 pp = *reinterpret_cast<const float4*>(&p_t[kk][4 * hq4]);
+        o[4 * hq4 + 0] += pp.x * vf;
+        o[4 * hq4 + 1] += pp.y * vf;
+        o[4 * hq4 + 2] += pp.z * vf;
+        o[4 * hq4 + 3] += pp.w * vf;
       }
     }
   }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+  // hand the head-warps' (max, sum) to the dim-warps
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const int hh = warp + 8 * j;
+    if (hh < GP && lane == 0) {
+      m_s[hh] = m_run[j];
+      l_s[hh] = l_run[j];
+    }
+  }
+  __syncthreads();
   if (a.nsplit == 1) {
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-      const int hh = warp + 8 * j;
+    for (int hh = 0; hh < GP; ++hh) {
       if (hh >= G) break;
       const int qh = h * G + hh;
-      const float inv = l[j] > 0.f ? a.v_scale / l[j] : 0.f;
-      float y[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) y[i] = o[j][i] * inv;
+      float y = l_s[hh] > 0.f ? o[hh] * (a.v_scale / l_s[hh]) : 0.f;
       if (a.gate != nullptr) {
-        const uint4 gv = *reinterpret_cast<const uint4*>(a.gate + (int64_t)t * a.ldg + (int64_t)qh * QSA_D + 8 * lane);
-        const __nv_bfloat16* gh = reinterpret_cast<const __nv_bfloat16*>(&gv);
-#pragma unroll
-        for (int i = 0; i < 8; ++i) y[i] *= 1.f / (1.f + __expf(-__bfloat162float(gh[i])));
+        const float g = __bfloat162float(a.gate[(int64_t)t * a.ldg + (int64_t)qh * QSA_D + dim]);
+        y *= 1.f / (1.f + __expf(-g));
       }
-      uint4 ov;
-      __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&ov);
-#pragma unroll
-      for (int i = 0; i < 4; ++i) ob[i] = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
-      *reinterpret_cast<uint4*>(a.out + (int64_t)t * a.ldo + (int64_t)qh * QSA_D + 8 * lane) = ov;
+      a.out[(int64_t)t * a.ldo + (int64_t)qh * QSA_D + dim] = __float2bfloat16(y);
     }
     return;
   }
 #pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int hh = warp + 8 * j;
+  for (int hh = 0; hh < GP; ++hh) {
     if (hh >= G) break;
     const int64_t r = (int64_t)t * a.hq + h * G + hh;
-    float* po = a.part_o + (r * a.nsplit + sp) * QSA_D + 8 * lane;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) po[i] = o[j][i];
-    if (lane == 0) {
-      a.part_ml[(r * a.nsplit + sp) * 2 + 0] = m[j];
-      a.part_ml[(r * a.nsplit + sp) * 2 + 1] = l[j];
+    a.part_o[(r * a.nsplit + sp) * QSA_D + dim] = o[hh];
+    if (tid == 0) {
+      a.part_ml[(r * a.nsplit + sp) * 2 + 0] = m_s[hh];
+      a.part_ml[(r * a.nsplit + sp) * 2 + 1] = l_s[hh];
     }
   }
 }
@@ -347,7 +384,17 @@ void qsa_attention(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::T
   a.v_scale = (float)v_scale;
   const at::cuda::CUDAGuard guard(q.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  launch_pdl(qsa_attn_kernel, dim3((unsigned)T, (unsigned)hkv, (unsigned)nsplit), dim3(256), 0, st, a);
+  constexpr int dyn = 4 * QSA_KT * QSA_D;
+  static bool attr = false;
+  if (!attr) {
+    TORCH_CHECK(cudaFuncSetAttribute(qsa_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) == cudaSuccess &&
+                    cudaFuncSetAttribute(qsa_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) ==
+                        cudaSuccess,
+                "qsa_attention: shared memory attribute");
+    attr = true;
+  }
+  if (a.G <= 8) launch_pdl(qsa_attn_kernel<8>, dim3((unsigned)T, (unsigned)hkv, (unsigned)nsplit), dim3(256), dyn, st, a);
+  else launch_pdl(qsa_attn_kernel<16>, dim3((unsigned)T, (unsigned)hkv, (unsigned)nsplit), dim3(256), dyn, st, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (nsplit == 1) return;
   launch_pdl(qsa_combine_kernel, dim3((unsigned)(T * hq)), dim3(256), 0, st, a.part_o, a.part_ml, (int)nsplit, (int)hq,
