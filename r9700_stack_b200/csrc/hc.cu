@@ -288,6 +288,138 @@ __global__ void __launch_bounds__(HCF_NT) hc_point_kernel(__nv_bfloat16* __restr
   }
 }
 
+// Register-resident variant for rows of at most R x 256 chunks (used with R = 1, HD <= 2048): every load of the
+// point (block output, residual streams, logit weights, norm weights, gates) is issued up front, so the
+// point costs one memory round trip plus two block reductions instead of a dependent chain of passes.
+constexpr int HCR = 4;  // streams held in registers by the variant below
+
+template <int R>
+__global__ void __launch_bounds__(HCF_NT) hc_point_reg_kernel(__nv_bfloat16* __restrict__ res, int64_t ldr,
+                                                              const __nv_bfloat16* __restrict__ y, int64_t ldy,
+                                                              const __nv_bfloat16* __restrict__ wl,
+                                                              const __nv_bfloat16* __restrict__ w, int w_per_stream,
+                                                              const __nv_bfloat16* __restrict__ g, int64_t ldg, int HC,
+                                                              int HD, float eps, __nv_bfloat16* __restrict__ out,
+                                                              int64_t ldo) {
+  pdl_wait();
+  pdl_trigger();
+  __shared__ float red[HCF_NT / 32][HC_MAX];
+  __shared__ float s_val[HC_MAX];
+  const int n = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nc = HD / 8;
+  __nv_bfloat16* rr = res + (int64_t)n * ldr;
+  const __nv_bfloat16* yr = y != nullptr ? y + (int64_t)n * ldy : nullptr;
+  const __nv_bfloat16* gr = g + (int64_t)n * ldg;
+  uint4 yv[R], rv[R][HCR], lv[R][HCR], wv[R][HCR], gv[R][HCR];
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = tid + j * HCF_NT;
+    const bool in = c < nc;
+    yv[j] = (in && yr != nullptr) ? reinterpret_cast<const uint4*>(yr)[c] : make_uint4(0, 0, 0, 0);
+#pragma unroll
+    for (int s = 0; s < HCR; ++s) {
+      if (s >= HC) break;
+      rv[j][s] = in ? reinterpret_cast<const uint4*>(rr + (int64_t)s * HD)[c] : make_uint4(0, 0, 0, 0);
+      lv[j][s] = (in && yr != nullptr) ? reinterpret_cast<const uint4*>(wl + (int64_t)s * HD)[c] : make_uint4(0, 0, 0, 0);
+      wv[j][s] = in ? reinterpret_cast<const uint4*>(w + (w_per_stream ? (int64_t)s * HD : 0))[c] : make_uint4(0, 0, 0, 0);
+      gv[j][s] = in ? reinterpret_cast<const uint4*>(gr + (int64_t)s * HD)[c] : make_uint4(0, 0, 0, 0);
+    }
+  }
+  auto block_sum = [&](float (&v)[HCR]) {
+#pragma unroll
+    for (int s = 0; s < HCR; ++s) {
+      if (s >= HC) break;
+      float x = v[s];
+#pragma unroll
+      for (int o = 16; o; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) red[warp][s] = x;
+    }
+    __syncthreads();
+    if (tid < HC) {
+      float t = 0.f;
+#pragma unroll
+      for (int k = 0; k < HCF_NT / 32; ++k) t += red[k][tid];
+      s_val[tid] = t;
+    }
+    __syncthreads();
+  };
+  float inj[HCR];
+#pragma unroll
+  for (int s = 0; s < HCR; ++s) inj[s] = 0.f;
+  if (yr != nullptr) {
+    float dot[HCR];
+#pragma unroll
+    for (int s = 0; s < HCR; ++s) dot[s] = 0.f;
+#pragma unroll
+    for (int j = 0; j < R; ++j) {
+      const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&yv[j]);
+#pragma unroll
+      for (int s = 0; s < HCR; ++s) {
+        if (s >= HC) break;
+        const __nv_bfloat16* le = reinterpret_cast<const __nv_bfloat16*>(&lv[j][s]);
+#pragma unroll
+        for (int k = 0; k < 8; ++k) dot[s] += __bfloat162float(ye[k]) * __bfloat162float(le[k]);
+      }
+    }
+    block_sum(dot);
+#pragma unroll
+    for (int s = 0; s < HCR; ++s)
+      if (s < HC) inj[s] = 2.f * hc_sigmoid(s_val[s] / (float)HC);
+  }
+  float ss[HCR];
+#pragma unroll
+  for (int s = 0; s < HCR; ++s) ss[s] = 0.f;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = tid + j * HCF_NT;
+    const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&yv[j]);
+#pragma unroll
+    for (int s = 0; s < HCR; ++s) {
+      if (s >= HC) break;
+      __nv_bfloat16* re = reinterpret_cast<__nv_bfloat16*>(&rv[j][s]);
+      if (yr != nullptr) {
+#pragma unroll
+        for (int k = 0; k < 8; ++k) re[k] = __float2bfloat16(__bfloat162float(re[k]) + __bfloat162float(ye[k]) * inj[s]);
+        if (c < nc) reinterpret_cast<uint4*>(rr + (int64_t)s * HD)[c] = rv[j][s];
+      }
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float f = __bfloat162float(re[k]);
+        ss[s] += f * f;
+      }
+    }
+  }
+  block_sum(ss);
+  float rrms[HCR];
+#pragma unroll
+  for (int s = 0; s < HCR; ++s) rrms[s] = s < HC ? rsqrtf(s_val[s] / (float)HD + eps) : 0.f;
+  const float inv = 1.f / (float)HC;
+#pragma unroll
+  for (int j = 0; j < R; ++j) {
+    const int c = tid + j * HCF_NT;
+    if (c >= nc) continue;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < HCR; ++s) {
+      if (s >= HC) break;
+      const __nv_bfloat16* re = reinterpret_cast<const __nv_bfloat16*>(&rv[j][s]);
+      const __nv_bfloat16* we = reinterpret_cast<const __nv_bfloat16*>(&wv[j][s]);
+      const __nv_bfloat16* ge = reinterpret_cast<const __nv_bfloat16*>(&gv[j][s]);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float t = __bfloat162float(re[k]) * rrms[s];
+        const float nv = __bfloat162float(__float2bfloat16(t + t * __bfloat162float(we[k])));
+        acc[k] += hc_sigmoid(__bfloat162float(ge[k])) * nv;
+      }
+    }
+    uint4 ov;
+    __nv_bfloat162* ob = reinterpret_cast<__nv_bfloat162*>(&ov);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) ob[k] = __floats2bfloat162_rn(acc[2 * k] * inv, acc[2 * k + 1] * inv);
+    reinterpret_cast<uint4*>(out + (int64_t)n * ldo)[c] = ov;
+  }
+}
+
 void hc_point(torch::Tensor res, c10::optional<torch::Tensor> y, torch::Tensor wl, torch::Tensor w, torch::Tensor g,
               int64_t HC, double eps, torch::Tensor out) {
   const int64_t T = res.size(0);
@@ -311,6 +443,17 @@ void hc_point(torch::Tensor res, c10::optional<torch::Tensor> y, torch::Tensor w
     ldy = y->stride(0);
   }
   const at::cuda::CUDAGuard guard(res.device());
+  const int64_t nc = HD / 8;
+  if (HC <= HCR && nc <= HCF_NT) {  // one chunk per thread (HD <= 2048); wider rows spill, so they loop
+    launch_pdl(hc_point_reg_kernel<1>, dim3((unsigned)T), dim3(HCF_NT), 0, at::cuda::getCurrentCUDAStream(),
+               reinterpret_cast<__nv_bfloat16*>(res.data_ptr()), res.stride(0), yp, ldy,
+               reinterpret_cast<const __nv_bfloat16*>(wl.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
+               w.numel() == HC * HD ? 1 : 0, reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+               g.size(0) == 1 ? (int64_t)0 : g.stride(0), (int)HC, (int)HD, (float)eps,
+               reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   launch_pdl(hc_point_kernel, dim3((unsigned)T), dim3(HCF_NT), 0, at::cuda::getCurrentCUDAStream(),
              reinterpret_cast<__nv_bfloat16*>(res.data_ptr()), res.stride(0), yp, ldy,
              reinterpret_cast<const __nv_bfloat16*>(wl.data_ptr()), reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()),
