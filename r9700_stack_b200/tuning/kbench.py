@@ -108,8 +108,13 @@ def bench_gemm(a) -> dict:
     us = _time(f, a.reps, a.warmup, graph=not a.eager)
     wbytes = per + (N * K // 32) * (0 if a.fmt == "bf16" else 1) * (2 if a.swiglu else 1)
     flops = 2.0 * M * N * K * (2 if a.swiglu else 1)
-    return {"kernel": "gemm", "fmt": a.fmt, "swiglu": a.swiglu, "N": N, "K": K, "M": M, "copies": nw,
-            "us": us, "weight_bytes": wbytes, "flops": flops}
+    r = {"kernel": "gemm", "fmt": a.fmt, "swiglu": a.swiglu, "N": N, "K": K, "M": M, "copies": nw,
+         "us": us, "weight_bytes": wbytes, "flops": flops}
+    if a.vs_torch and a.fmt == "bf16" and not a.swiglu:
+        # the library baseline: torch.matmul (cuBLAS) on the same rotated bf16 weights, same timing
+        tw = [w.w for w in ws]
+        r["torch_matmul_us"] = _time(lambda i: torch.matmul(xb, tw[i % nw].T), a.reps, a.warmup, graph=not a.eager)
+    return r
 
 
 def bench_moe(a) -> dict:
@@ -325,6 +330,7 @@ def main(argv=None):
     g.add_argument("--swiglu", action="store_true")
     g.add_argument("--tiled", type=int, default=1)
     g.add_argument("--max-copies", type=int, default=16)
+    g.add_argument("--vs-torch", action="store_true", help="bf16: also time torch.matmul (cuBLAS) on the same weights")
     m = sub.add_parser("moe")
     m.add_argument("--T", type=int, default=16)
     m.add_argument("--E", type=int, default=288)
