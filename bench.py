@@ -30,10 +30,35 @@ sys.path.insert(0, HERE)
 METRIC = "decode tok/s (1 and 16 streams), prefill tok/s @8k prompt, device-timed max/rank"
 BASELINE_DECODE16 = 640.0  # reference: 27B NVFP4 TP2, 16 streams (README.md:69)
 BASELINE_FLASHNEXT16 = 913.0  # reference: Flash-Next MTP-3 TP4, 16 streams (README.md:70)
-REF_UNAVAILABLE = (
-    "reference is a ROCm/gfx1201 vLLM plugin: its platform detect() returns None on a CUDA host and its "
-    "libr9k.so kernels need hipcc for gfx1201 (absent); it has no CUDA path to run on B200"
-)
+REF_DIR = os.path.join(HERE, "baseline", "_ref")
+
+
+def reference_probe() -> str:
+    """Try the reference's own stock entry path (installed unmodified under baseline/_ref): its vLLM
+    platform plugin ``detect()`` and its kernel library. Returns the observed reason it cannot run."""
+    if not os.path.isdir(os.path.join(REF_DIR, "r9700_vllm")):
+        return "reference not installed under baseline/_ref"
+    sys.path.insert(0, REF_DIR)
+    seen = []
+    try:
+        import r9700_vllm.platform as rp
+
+        got = rp.detect()
+        seen.append(f"r9700_vllm.platform.detect() returned {got!r} (it activates only where vLLM's ROCm probe "
+                    "finds a ROCm GPU)")
+    except Exception as e:  # noqa: BLE001 - the failure is the finding
+        seen.append(f"r9700_vllm.platform.detect() raised {type(e).__name__}: {str(e).splitlines()[0][:160]}")
+    try:
+        import glob
+
+        import r9700_vllm
+
+        libs = glob.glob(os.path.join(os.path.dirname(r9700_vllm.__file__), "**", "libr9k*.so"), recursive=True)
+        seen.append("libr9k.so present" if libs else
+                    "libr9k.so absent: its 23 .hip kernel sources build only with hipcc for gfx1201 (not in this image)")
+    except Exception as e:  # noqa: BLE001
+        seen.append(f"import r9700_vllm raised {type(e).__name__}")
+    return "reference is a ROCm/gfx1201 vLLM plugin with no CUDA path; observed: " + "; ".join(seen)
 
 
 def parse():
@@ -63,12 +88,14 @@ class ClockSampler:
     def __init__(self, gpu_index="0"):
         self.proc = None
         self.gpu = gpu_index
-        self.path = os.path.join(HERE, "gpurun_out", "clocks.csv")
+        import tempfile
+
+        fd, self.path = tempfile.mkstemp(prefix="r9k_clocks_", suffix=".csv")
+        os.close(fd)
         self.t0 = self.t1 = None
 
     def start(self):
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
             self.fh = open(self.path, "w")
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
                                           "-i", str(self.gpu), "-lms", "100"], stdout=self.fh, stderr=subprocess.DEVNULL)
@@ -106,6 +133,10 @@ class ClockSampler:
             except ValueError:
                 continue
             samples.append((ts, clk, cmax, [n for n, v in zip(self.NAMES, p[6:10]) if v.lower() == "active"]))
+        try:
+            os.unlink(self.path)
+        except OSError:
+            pass
         if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         t0, t1 = self.t0 or samples[0][0], self.t1 or samples[-1][0]
@@ -136,7 +167,8 @@ def _smi_id(dev) -> str:
 def main():
     args = parse()
     if args.impl == "reference":
-        print(json.dumps({"impl": "reference", "unavailable": REF_UNAVAILABLE, "metric": METRIC}))
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": reference_probe(), "metric": METRIC}))
         return 0
 
     import numpy as np

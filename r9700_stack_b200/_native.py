@@ -99,6 +99,9 @@ def load_library(rebuild_if_stale: bool = True) -> None:
     with _lock:
         if _loaded:
             return
+        from . import knobs
+
+        knobs.export_native()
         if not is_current():
             if not rebuild_if_stale and os.path.exists(lib_path()):
                 pass

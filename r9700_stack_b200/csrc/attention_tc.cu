@@ -873,12 +873,7 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
 }
 
 static void attn_tc_launch(const AttnArgs& a, const CUtensorMap& tk, const CUtensorMap& tv, dim3 grid, cudaStream_t st) {
-  static bool set = false;
-  if (!set) {
-    TORCH_CHECK(cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM) == cudaSuccess,
-                "attn_tc: smem attribute");
-    set = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)attn_tc_kernel, fa::SMEM) == cudaSuccess, "attn_tc: smem attribute");
   TORCH_CHECK(launch_pdl(attn_tc_kernel, grid, dim3(192), (size_t)fa::SMEM, st, tk, tv, a) == cudaSuccess, "attn_tc launch");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -944,13 +939,7 @@ void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cach
   // wider verify tiles: the row-tile kernel
   if (rows_bound <= 16 && dec_kernel_enabled()) {
     auto kern = rows_bound <= 8 ? attn_dec_kernel<8> : attn_dec_kernel<16>;
-    static bool set[2] = {false, false};
-    const int ki = rows_bound <= 8 ? 0 : 1;
-    if (!set[ki]) {
-      TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fd::SMEM) == cudaSuccess,
-                  "attn_dec: smem attribute");
-      set[ki] = true;
-    }
+    TORCH_CHECK(ensure_smem_attr((const void*)kern, fd::SMEM) == cudaSuccess, "attn_dec: smem attribute");
     TORCH_CHECK(launch_pdl(kern, dim3((unsigned)S, (unsigned)a.Hkv, (unsigned)a.nsplit), dim3(192), (size_t)fd::SMEM,
                            st, kv_tmap(k_cache), kv_tmap(v_cache), a) == cudaSuccess, "attn_dec launch");
   } else {

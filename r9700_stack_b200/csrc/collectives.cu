@@ -450,12 +450,8 @@ void symm_ar_wht(torch::Tensor x, torch::Tensor out, torch::Tensor peers, int64_
   // persistent grid: four CTAs per SM, a function of n only (identical on every rank)
   const int grid = (int)std::min<int64_t>(nchunks, 4 * 148);
   static_assert(4 * 148 <= WHT_MAX_CTAS && AR_MAX_WORLD * WHT_MAX_CTAS <= COLL_MAXCH, "flag table");
-  static bool attr = false;
-  if (!attr) {
-    TORCH_CHECK(cudaFuncSetAttribute(symm_ar_wht_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     2 * AR_MAX_WORLD * wht_chunk_bytes(6)) == cudaSuccess, "symm_ar_wht smem attribute");
-    attr = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)symm_ar_wht_kernel, 2 * AR_MAX_WORLD * wht_chunk_bytes(6)) == cudaSuccess,
+              "symm_ar_wht smem attribute");
   TORCH_CHECK(launch_pdl(symm_ar_wht_kernel, dim3((unsigned)grid), dim3(256), smem, at::cuda::getCurrentCUDAStream(), a,
                          reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), n, (int)bits, (int)phase) == cudaSuccess,

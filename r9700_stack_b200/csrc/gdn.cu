@@ -635,11 +635,7 @@ void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off,
   cfg.numAttrs = 1;
 #define R9K_GDF(ST_T)                                                                                                 \
   {                                                                                                                   \
-    static bool attr_done = false;                                                                                    \
-    if (!attr_done) {                                                                                                 \
-      cudaFuncSetAttribute(gdn_decode_fused_kernel<ST_T>, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024); \
-      attr_done = true;                                                                                               \
-    }                                                                                                                 \
+    ensure_smem_attr((const void*)gdn_decode_fused_kernel<ST_T>, 200 * 1024);                                       \
   }                                                                                                                   \
   TORCH_CHECK(cudaLaunchKernelEx(&cfg, gdn_decode_fused_kernel<ST_T>,                                                 \
       reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr()), proj.stride(0), (int)Hk, (int)Hv, (int)z_off, (int)b_off, \

@@ -273,15 +273,7 @@ __global__ void __launch_bounds__(192, 1)
 // ---------------------------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------------------------
-static int sk_num_sms() {
-  static int n = 0;
-  if (n == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+static int sk_num_sms() { return device_sm_count(); }
 
 static int sk_ctas_per_sm() {
   static int v = -1;
@@ -307,12 +299,7 @@ static bool sk_launch(const CUtensorMap& ta, const CUtensorMap& ta2, const CUten
   if (STAGES < 2) return false;
   SkArgs sk{U, P, nseg, part, counters};
   auto kern = gemm_sk_kernel<KIND, BN, DUAL, EPI, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) == cudaSuccess,
-                "gemm_sk: smem attribute");
-    attr_set = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)kern, C::SMEM_BYTES) == cudaSuccess, "gemm_sk: smem attribute");
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3((unsigned)P, 1, 1);
   cfg.blockDim = dim3(192, 1, 1);

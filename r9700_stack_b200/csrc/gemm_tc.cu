@@ -440,15 +440,7 @@ struct LaunchPlan {
   bool unpack;  // fp4 weights loaded packed and expanded on chip
 };
 
-static int g_num_sms = 0;
-static int num_sms() {
-  if (g_num_sms == 0) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&g_num_sms, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return g_num_sms;
-}
+static int num_sms() { return device_sm_count(); }
 
 static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
   LaunchPlan p;
@@ -489,12 +481,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
                         LaunchPlan p, torch::Tensor* ws, cudaStream_t stream) {
   using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK, MT>;
   auto kern = gemm_tc_kernel<KIND, BN, DUAL, EPI, NP, NC, UNPACK, MT>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM_BYTES) == cudaSuccess,
-                "r9k gemm: cannot set smem size");
-    attr_set = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)kern, C::SMEM_BYTES) == cudaSuccess, "r9k gemm: cannot set smem size");
   TORCH_CHECK(((args.N + 127) / 128) % MT == 0, "r9k gemm: row tiles must divide over the CTAs");
   const int grid_x = (args.N + 127) / 128 / MT;
   if (MT > 1) p.S = 1;  // multi-tile CTAs keep whole K
@@ -835,6 +822,7 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
 // allocation of any kind; declared and documented in r9k_noalloc.h).
 // ---------------------------------------------------------------------------------------------
 #include <cstdio>
+#include <atomic>
 #include "r9k_noalloc.h"
 
 namespace {
@@ -846,8 +834,8 @@ constexpr int kNaMaxDev = 64;
 __device__ __align__(256) float r9k_noalloc_scratch[R9K_NOALLOC_SCRATCH_BYTES / 4];
 
 struct NaDevice {
-  bool ready = false;
-  float* scratch = nullptr;  // device address of r9k_noalloc_scratch on this device
+  std::atomic<bool> ready{false};  // release-stored after scratch is set; acquire-loaded on the fast path
+  float* scratch = nullptr;        // device address of r9k_noalloc_scratch on this device
 };
 NaDevice g_na[kNaMaxDev];
 std::mutex g_na_mu;
@@ -862,7 +850,7 @@ cudaError_t na_set_attr() {
 
 int na_setup(int dev) {
   std::lock_guard<std::mutex> lk(g_na_mu);
-  if (g_na[dev].ready) return R9K_NOALLOC_OK;
+  if (g_na[dev].ready.load(std::memory_order_acquire)) return R9K_NOALLOC_OK;
   void* p = nullptr;
   cudaError_t e = cudaGetSymbolAddress(&p, r9k_noalloc_scratch);
   if (e != cudaSuccess || p == nullptr) {
@@ -888,7 +876,7 @@ int na_setup(int dev) {
     g_na_encode = reinterpret_cast<r9k::EncodeTiledFn>(fn);
   }
   g_na[dev].scratch = static_cast<float*>(p);
-  g_na[dev].ready = true;
+  g_na[dev].ready.store(true, std::memory_order_release);
   return R9K_NOALLOC_OK;
 }
 
@@ -928,11 +916,11 @@ int na_launch(const CUtensorMap& ta, const CUtensorMap& tb, r9k::GemmArgs a, int
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  // Plain stream order (no programmatic dependent launch): the kernel issues its first weight-tile
+  // loads before it waits on the preceding grid, which is only safe when nothing earlier on the
+  // stream is still writing w; a C caller gives no such guarantee.
+  cfg.attrs = nullptr;
+  cfg.numAttrs = 0;
   const cudaError_t e = cudaLaunchKernelEx(&cfg, r9k::gemm_tc_kernel<r9k::KIND_BF16, BN, false, r9k::EPI_BF16, NP, 1, false>,
                                            ta, ta, tb, a, part, cnt);
   if (e != cudaSuccess) {
@@ -949,7 +937,8 @@ extern "C" __attribute__((visibility("default"))) int r9k_gemm_bf16_noalloc(
     int* status, cudaStream_t stream) {
   auto aligned16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
   if (w == nullptr || x == nullptr || out == nullptr || N < 1 || M < 1 || K < 64 || K % 64 != 0 || ldw < K ||
-      ldx < K || ldo < N || ldw % 8 != 0 || ldx % 8 != 0 || !aligned16(w) || !aligned16(x)) {
+      ldx < K || ldo < N || ldw % 8 != 0 || ldx % 8 != 0 || ldo % 8 != 0 || !aligned16(w) || !aligned16(x) ||
+      !aligned16(out)) {
     fprintf(stderr, "r9k_gemm_bf16_noalloc: invalid arguments (N=%d M=%d K=%d ldw=%lld ldx=%lld ldo=%lld)\n", N, M,
             K, (long long)ldw, (long long)ldx, (long long)ldo);
     return R9K_NOALLOC_EINVAL;
@@ -960,7 +949,7 @@ extern "C" __attribute__((visibility("default"))) int r9k_gemm_bf16_noalloc(
   }
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kNaMaxDev) return R9K_NOALLOC_ESETUP;
-  if (!g_na[dev].ready) {
+  if (!g_na[dev].ready.load(std::memory_order_acquire)) {
     const int rc = na_setup(dev);
     if (rc != R9K_NOALLOC_OK) return rc;
   }

@@ -259,11 +259,8 @@ void moe_align(torch::Tensor ids, int64_t e0, int64_t E_local, int64_t BN, torch
   TORCH_CHECK(BN == 16 || BN == 32 || BN == 64 || BN == 128 || BN == 256, "moe_align: BN");
   const at::cuda::CUDAGuard guard(ids.device());
   const size_t smem = (size_t)(33 * E_local) * sizeof(int);
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(moe_align_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 33 * MOE_MAX_E * 4);
-    attr = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)moe_align_kernel, 33 * MOE_MAX_E * 4) == cudaSuccess,
+              "moe_align: smem attribute");
   TORCH_CHECK(launch_pdl(moe_align_kernel, dim3(1), dim3(1024), smem, at::cuda::getCurrentCUDAStream(),
                          ids.data_ptr<int32_t>(), (int)ids.numel(), (int)e0, (int)E_local, (int)BN,
                          perm_row.data_ptr<int32_t>(), seg_start.data_ptr<int32_t>(), work.data_ptr<int32_t>(),

@@ -385,14 +385,9 @@ void qsa_attention(torch::Tensor q, torch::Tensor kc, torch::Tensor vc, torch::T
   const at::cuda::CUDAGuard guard(q.device());
   auto st = at::cuda::getCurrentCUDAStream();
   constexpr int dyn = 4 * QSA_KT * QSA_D;
-  static bool attr = false;
-  if (!attr) {
-    TORCH_CHECK(cudaFuncSetAttribute(qsa_attn_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) == cudaSuccess &&
-                    cudaFuncSetAttribute(qsa_attn_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn) ==
-                        cudaSuccess,
-                "qsa_attention: shared memory attribute");
-    attr = true;
-  }
+  TORCH_CHECK(ensure_smem_attr((const void*)qsa_attn_kernel<8>, dyn) == cudaSuccess &&
+                  ensure_smem_attr((const void*)qsa_attn_kernel<16>, dyn) == cudaSuccess,
+              "qsa_attention: shared memory attribute");
   if (a.G <= 8) launch_pdl(qsa_attn_kernel<8>, dim3((unsigned)T, (unsigned)hkv, (unsigned)nsplit), dim3(256), dyn, st, a);
   else launch_pdl(qsa_attn_kernel<16>, dim3((unsigned)T, (unsigned)hkv, (unsigned)nsplit), dim3(256), dyn, st, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -29,8 +29,10 @@ enum {
 
 // out[M, N] (bf16, row stride ldo elements) = alpha * x[M, K] @ w[N, K]^T, x and w bf16 row-major
 // with row strides ldx, ldw (elements). A skinny (decode-sized) GEMM: 1 <= M <= 64, K a multiple of
-// 64, every base pointer 16-byte aligned and every row stride a multiple of 8 elements. The launch
-// goes on `stream` and returns without synchronising.
+// 64, every base pointer (w, x, out) 16-byte aligned and every row stride (ldw, ldx, ldo) a multiple
+// of 8 elements; anything else returns R9K_NOALLOC_EINVAL. The launch goes on `stream` in ordinary
+// stream order (the kernel starts after all earlier work on `stream` has finished, so w and x may be
+// written by the kernel just before it) and the call returns without synchronising.
 //
 // status: optional device pointer to 4 ints; a kernel whose bounded wait runs out writes
 // {code, kernel id, block, detail} there (first error wins) and returns. NULL records nothing.

@@ -1,41 +1,58 @@
 """``R9K_*`` environment knobs.
 
 Every kernel path has a switch that selects an alternative implementation without a rebuild, in the
-spirit of the reference's ``R9K_*=stock`` contract (README.md:144-145): e.g. ``R9K_ATTN=simple``
-selects the CUDA-core paged attention instead of the tcgen05 flash-attention kernel, and
-``R9K_COMM=nccl`` routes every collective through NCCL. ``R9K_DISABLE=a,b`` lists coarse opt-outs.
-Values are read once per process (``refresh()`` re-reads them, for tests).
+spirit of the reference's ``R9K_*=stock`` contract (README.md:144-145): every knob accepts the value
+``stock``, which selects the simplest path this library has for that step (a CUDA-core kernel instead
+of the tcgen05 one, the unfused kernel sequence instead of the fused one, NCCL instead of the NVLink
+kernels). There is no vLLM stock path under this engine, so "stock" means the baseline path here.
+``R9K_DISABLE=a,b`` lists coarse opt-outs. Values are read once per process (``refresh()`` re-reads
+them, for tests).
 """
 from __future__ import annotations
 
 import os
 
-_DEFAULTS = {
-    "R9K_ATTN": "tc",  # tc | simple
-    "R9K_WEIGHT_TILED": "1",  # 1: MX weights stored as contiguous 128x128 units; 0: row-major
-    "R9K_GEMM_SK": "0",  # 1: skinny GEMMs use the persistent stream-K kernel
-    "R9K_FP4_UNPACK": "0",  # 1: skinny fp4 GEMMs load packed bytes and expand them on chip
-    "R9K_GDN_FUSED": "1",  # 1: decode steps run the one-kernel GDN layer core
-    "R9K_COMM": "fused",  # fused | nccl
-    "R9K_AR_MODE": "pull",  # pull: consumer reads peers' partials; push: GEMM epilogue stores into peers
-    "R9K_GDN_STATE": "",  # "" (model default) | bf16 | fp32
-    "R9K_DISABLE": "",
-    "R9K_AR_ONESHOT_MAX_KB": "512",
-    "R9K_AR_QUANT_BITS": "0",  # 4 | 6: lossy WHT-64 compressed all-reduce for large (prefill) messages; 0: exact
-    "R9K_AR_QUANT_MIN_KB": "1024",  # smallest message sent compressed
-    "R9K_SPIN_TIMEOUT_MS": "1000",
-    "R9K_AR_HIST": "0",  # 1: histogram of all-reduce message sizes (utils.trace.AR_HIST)
-    "R9K_TRACE": "0",
-    "R9K_GEMM_L2PF": "0",  # skinny GEMMs: weight chunks prefetched into L2 beyond the smem ring (0: off; 4-16 measured slower)
-    "R9K_MOE_MT": "1",  # 1: grouped skinny MoE GEMMs run several row tiles per CTA (gate/up 2, down 4); 0: one
-    "R9K_HC_FUSED": "1",  # 1: one kernel per hyper-connection norm point; 0: logits GEMM + combine_norm + gate_mix  # 1: the runner attaches a utils.trace.DeviceTrace to the model
+# name -> (default, value that "stock" selects, meaning)
+_KNOBS = {
+    "R9K_ATTN": ("tc", "simple", "tc: tcgen05 flash attention; simple: CUDA-core paged attention"),
+    "R9K_ATTN_DEC": ("1", "0", "1: keys-on-M split-KV decode attention; 0: the row-tile kernel"),
+    "R9K_WEIGHT_TILED": ("1", "0", "1: MX weights stored as contiguous 128x128 units; 0: row-major"),
+    "R9K_GEMM_SK": ("0", "0", "1: skinny GEMMs use the persistent stream-K kernel"),
+    "R9K_FP4_UNPACK": ("0", "0", "1: skinny fp4 GEMMs load packed bytes and expand them on chip"),
+    "R9K_GDN_FUSED": ("1", "0", "1: decode steps run the one-kernel GDN layer core"),
+    "R9K_GDN_PREFILL": ("chunked", "serial",
+                        "chunked: tensor-core chunked delta rule for long prefill; serial: token-serial recurrence"),
+    "R9K_GDN_CHUNK_MIN": ("256", "256", "shortest sequence that takes the chunked GDN prefill"),
+    "R9K_COMM": ("fused", "nccl", "fused: NVLink kernels fused into GEMMs / norms; nccl: every collective on NCCL"),
+    "R9K_AR_MODE": ("pull", "pull", "pull: consumer reads peers' partials; push: GEMM epilogue stores into peers"),
+    "R9K_GDN_STATE": ("", "", "'' (model default) | bf16 | fp32"),
+    "R9K_DISABLE": ("", "", "comma list of coarse opt-outs (e.g. plugin)"),
+    "R9K_AR_ONESHOT_MAX_KB": ("512", "512", "largest standalone all-reduce sent one-shot"),
+    "R9K_AR_QUANT_BITS": ("0", "0", "4 | 6: lossy WHT-64 compressed all-reduce for large (prefill) messages; 0: exact"),
+    "R9K_AR_QUANT_MIN_KB": ("1024", "1024", "smallest message sent compressed"),
+    "R9K_PREFILL_AR": ("symm", "nccl", "symm: prefill all-reduces on the NVLink two-shot kernel; nccl: NCCL"),
+    "R9K_LOGITS_AG": ("symm", "nccl", "symm: logits all-gather on the NVLink kernel; nccl: NCCL"),
+    "R9K_SPIN_TIMEOUT_MS": ("1000", "1000", "bound of every device-side wait"),
+    "R9K_AR_HIST": ("0", "0", "1: histogram of all-reduce message sizes (utils.trace.AR_HIST)"),
+    "R9K_TRACE": ("0", "0", "1: the runner attaches a utils.trace.DeviceTrace to the model"),
+    "R9K_GEMM_L2PF": ("0", "0", "skinny GEMMs: weight chunks prefetched into L2 beyond the smem ring (0: off)"),
+    "R9K_MOE_MT": ("1", "0", "1: grouped skinny MoE GEMMs run several row tiles per CTA; 0: one"),
+    "R9K_HC_FUSED": ("1", "0", "1: one kernel per hyper-connection norm point; 0: logits GEMM + combine_norm + gate_mix"),
+    "R9K_NVFP4": ("mxfp4", "mxfp4", "mxfp4: NVFP4 checkpoints convert to MXFP4 at load; native: served as NVFP4"),
+    "R9K_EP": ("ar", "ar", "ar: experts' partials summed by the all-reduce; a2a: all-to-all dispatch/combine"),
 }
+# knobs the C++ library reads with getenv (kept in sync by export_native)
+_NATIVE = ("R9K_ATTN_DEC", "R9K_FP4_UNPACK", "R9K_GEMM_L2PF", "R9K_GEMM_SK", "R9K_MOE_MT")
+_DEFAULTS = {k: v[0] for k, v in _KNOBS.items()}
 _cache: dict[str, str] = {}
 
 
 def get(name: str) -> str:
     if name not in _cache:
-        _cache[name] = os.environ.get(name, _DEFAULTS.get(name, ""))
+        v = os.environ.get(name, _DEFAULTS.get(name, ""))
+        if v.strip().lower() == "stock" and name in _KNOBS:
+            v = _KNOBS[name][1]
+        _cache[name] = v
     return _cache[name]
 
 
@@ -49,6 +66,17 @@ def disabled(feature: str) -> bool:
 
 def refresh() -> None:
     _cache.clear()
+
+
+def export_native() -> None:
+    """Resolve ``stock`` for the knobs the kernel library reads itself (before it loads)."""
+    for k in _NATIVE:
+        if os.environ.get(k, "").strip().lower() == "stock":
+            os.environ[k] = _KNOBS[k][1]
+
+
+def describe() -> dict[str, str]:
+    return {k: v[2] for k, v in _KNOBS.items()}
 
 
 def all_knobs() -> dict[str, str]:

@@ -69,6 +69,8 @@ class StepMeta:
     host_seqs: list | None = None
     # host upper bound of tok_ctx on eager steps (None in CUDA graphs): QSA runs dense below its top-k
     host_max_ctx: int | None = None
+    # prefill attention tile table (built once per step on first use, shared by every attention layer)
+    attn_tiles: dict | None = None
 
 
 class Workspace:
@@ -326,13 +328,8 @@ class HybridLM:
                                    self.k_scale, self.v_scale, gate, out_bf, out_q, out_sf, 0)
         elif meta.host_seqs is not None and (T > ws.logit_rows or any(n * G > 128 for _, n in meta.host_seqs)):
             # prefill: query tiles of floor(128 / G) tokens, whole causal key range per CTA
-            qt = 128 // G
-            tab = []
-            for si, (t0, n) in enumerate(meta.host_seqs):
-                for j in range(0, n, qt):
-                    tab += [si, t0 + j, min(qt, n - j)]
-            tt = torch.tensor(tab, dtype=torch.int32).to(self.device, non_blocking=True)
-            _ops().attn_tc_prefill(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, tt, len(tab) // 3,
+            tt = self._attn_tile_table(meta, 128 // G)
+            _ops().attn_tc_prefill(ws.q[:T], kc, vc, meta.block_table, meta.tok_ctx, tt, tt.shape[0] // 3,
                                    self.sm_scale, self.k_scale, self.v_scale, gate, out_bf, out_q, out_sf,
                                    _status.status(self.device))
         else:
@@ -349,6 +346,24 @@ class HybridLM:
                                   self.sm_scale, self.k_scale, self.v_scale, po, pml, gate, out_bf, out_q, out_sf,
                                   _status.status(self.device), max_rows)
         return ws.attn_act.narrow(T), ws.attn_bf16[:T], lay["w_o"]
+
+    def _attn_tile_table(self, meta: StepMeta, qt: int) -> torch.Tensor:
+        """(sequence, first token, rows) per prefill query tile of qt tokens: built once per step from
+        the host sequence list and uploaded from pinned memory, then reused by every attention layer."""
+        if meta.attn_tiles is None:
+            meta.attn_tiles = {}
+        tt = meta.attn_tiles.get(qt)
+        if tt is None:
+            import numpy as np
+
+            rows = []
+            for si, (t0, n) in enumerate(meta.host_seqs):
+                j = np.arange(0, n, qt, dtype=np.int32)
+                rows.append(np.stack([np.full_like(j, si), t0 + j, np.minimum(qt, n - j)], axis=1))
+            host = torch.from_numpy(np.concatenate(rows).reshape(-1)).pin_memory()
+            tt = host.to(self.device, non_blocking=True)
+            meta.attn_tiles[qt] = tt
+        return tt
 
     def _qsa(self, i: int, lay, meta: StepMeta, ws: Workspace, T: int, gate) -> bool:
         """QSA indexer for attention layer i (projection, norm + rope, token key store, group
