@@ -73,6 +73,9 @@ def parse():
     ap.add_argument("--model", default="dense27b", choices=["dense27b", "flashnext"],
                     help="dense27b: BASELINE config 2 (headline); flashnext: config 3 (hybrid MoE)")
     ap.add_argument("--no-prefill-metric", action="store_true")
+    ap.add_argument("--diag", action="store_true",
+                    help="after the timed steps, print a second JSON line with a per-family step ledger (torch "
+                         "profiler) from every rank; diagnostics only, not part of the metric")
     return ap.parse_args()
 
 
@@ -226,7 +229,7 @@ def main():
     prefill_ms_max = max(comm.max_scalar(m, dev) if comm else m for m in prefill_ms) if prefill_ms else None
 
     # ---------------- decode @16 streams ----------------
-    total_new = args.warmup + 2 * args.steps + 8
+    total_new = args.warmup + 2 * args.steps + 16
     seqs = [llm.add_request(prompt(), SamplingParams(max_tokens=total_new)) for _ in range(S)]
     while any(not s.prefill_done or not s.output for s in seqs):
         llm.step()
@@ -275,6 +278,20 @@ def main():
     lc.counting = False
     launches_per_step = lc.count
     torch.cuda.synchronize(dev)
+
+    diag = None
+    if args.diag:
+        from r9700_stack_b200.utils.trace import step_ledger
+
+        led = step_ledger(llm, steps=5)
+        if comm is not None and world > 1:
+            import torch.distributed as dist
+
+            allv = [None] * world
+            dist.all_gather_object(allv, led)
+            diag = allv
+        else:
+            diag = [led]
 
     # ---------------- decode @1 stream: keep one sequence ----------------
     keep = seqs[0]
@@ -334,6 +351,8 @@ def main():
             "weights_gb_per_rank": round(llm.model.weight_bytes() / 1e9, 2),
         }
         print(json.dumps(res), flush=True)
+        if diag is not None:
+            print(json.dumps({"diag": {"decode16_ledger_per_rank": diag}}), flush=True)
     if comm is not None:
         import torch.distributed as dist
 

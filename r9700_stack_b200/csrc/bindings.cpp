@@ -17,7 +17,7 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
                torch::Tensor status, c10::optional<torch::Tensor> workspace);
 void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, int64_t N,
                   torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
-                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace);
+                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace, int64_t ll);
 void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::Tensor> w2,
                      c10::optional<torch::Tensor> w2_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf,
                      torch::Tensor work, torch::Tensor work_count, int64_t N, int64_t E, int64_t BN, torch::Tensor out,
@@ -41,6 +41,8 @@ int64_t symm_open(torch::Tensor handle);
 void symm_close(int64_t ptr);
 torch::Tensor symm_view(int64_t ptr, int64_t offset_bytes, int64_t rows, int64_t cols, int64_t device);
 void symm_step_begin(torch::Tensor step);
+torch::Tensor p2p_probe(torch::Tensor peers, int64_t rank, int64_t peer_rank, int64_t off, int64_t kind, int64_t mode,
+                        int64_t iters, torch::Tensor status, double timeout_s);
 void push_partial(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems,
                   int64_t call, torch::Tensor step, int64_t calls_per_step);
 void ar_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
@@ -53,6 +55,13 @@ void ar_pull_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t s
                      c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
                      c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
                      torch::Tensor status, double timeout_s);
+void ar_ll_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+                   torch::Tensor step, int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in,
+                   c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
+                   c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
+                   torch::Tensor status, double timeout_s);
+void ll_push(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+             torch::Tensor step, int64_t calls_per_step);
 // quant.cu
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
                    torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
@@ -168,7 +177,7 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(c!)? workspace=None) -> ()");
   m.def("gemm_mx_push(Tensor w, Tensor w_sf, bool w_fp4, Tensor x, Tensor x_sf, int N, Tensor peers, int rank, "
         "int world, int slot_elems, int call, Tensor step, int calls_per_step, Tensor(a!) status, "
-        "Tensor(b!)? workspace=None) -> ()");
+        "Tensor(b!)? workspace=None, int ll=0) -> ()");
   m.def("gemm_mx_grouped(Tensor w, Tensor w_sf, Tensor? w2, Tensor? w2_sf, bool w_fp4, Tensor x, Tensor x_sf, "
         "Tensor work, Tensor work_count, int N, int E, int BN, Tensor(a!) out, Tensor(b!)? out_sf, "
         "Tensor(c!) status) -> ()");
@@ -190,6 +199,11 @@ TORCH_LIBRARY(r9k, m) {
   m.def("ar_pull_rmsnorm(Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
         "int calls_per_step, int T, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf, Tensor(e!) status, float timeout_s) -> ()");
+  m.def("ar_ll_rmsnorm(Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
+        "int calls_per_step, int T, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
+        "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf, Tensor(e!) status, float timeout_s) -> ()");
+  m.def("ll_push(Tensor x, Tensor peers, int rank, int world, int slot_elems, int call, Tensor step, "
+        "int calls_per_step) -> ()");
   m.def("rmsnorm_quant(Tensor x, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf) -> ()");
   m.def("quant_act_mxfp8(Tensor x, Tensor(a!) q, Tensor(b!) sf) -> ()");
@@ -285,6 +299,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("push_partial", &r9k::push_partial);
   m.impl("ar_rmsnorm", &r9k::ar_rmsnorm);
   m.impl("ar_pull_rmsnorm", &r9k::ar_pull_rmsnorm);
+  m.impl("ar_ll_rmsnorm", &r9k::ar_ll_rmsnorm);
+  m.impl("ll_push", &r9k::ll_push);
   m.impl("quant_act_mxfp8", &r9k::quant_act_mxfp8);
   m.impl("quant_weight_mxfp4", &r9k::quant_weight_mxfp4);
   m.impl("quant_weight_mxfp8", &r9k::quant_weight_mxfp8);
@@ -336,6 +352,8 @@ TORCH_LIBRARY_FRAGMENT(r9k, m) {
   m.def("symm_close(int ptr) -> ()", &r9k::symm_close);
   m.def("symm_collective_region_bytes(int slot_bytes) -> int", &r9k::symm_collective_region_bytes);
   m.def("symm_view(int ptr, int offset_bytes, int rows, int cols, int device) -> Tensor", &r9k::symm_view);
+  m.def("p2p_probe(Tensor peers, int rank, int peer_rank, int off, int kind, int mode, int iters, Tensor status, "
+        "float timeout_s) -> Tensor", &r9k::p2p_probe);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "r9700_stack_b200 sm_100a kernel library"; }

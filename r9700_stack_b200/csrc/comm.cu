@@ -455,3 +455,224 @@ void ar_pull_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t s
 }
 
 }  // namespace r9k
+
+namespace r9k {
+
+// ------------------------------------------------------------------------------------------------
+// LL variant (default): producers store their bf16 partial straight into every rank's LL slot with
+// the call's epoch in each 8-byte word (GEMM epilogue, or ll_push for other producers); the consumer
+// polls its own region until every word of every source carries the epoch, then reduces in rank
+// order. Data and "ready" travel in the same NVLink write, so the consumer sees a source's data one
+// one-way NVLink latency after the producer stored it: no fence, no flag round trip, no remote load.
+//
+// The consumer does not wait on the preceding grid (its inputs announce themselves by epoch) and
+// lets the next kernel launch at once. Safe because (a) every producer triggers its dependents only
+// after its own griddepcontrol.wait returned, so when the consumer starts every kernel before the
+// producer has completed (the residual it reads, the step counter); (b) buffer k % 2 is rewritten
+// at call k + 2 only after every rank passed call k + 1, whose data each rank produced after its call
+// k consumer finished (the argument of the pull variant).
+// ------------------------------------------------------------------------------------------------
+__global__ void ll_push_kernel(const __nv_bfloat16* __restrict__ x, int64_t ldx, ArPeers pe, int H, int call) {
+  pdl_wait();
+  pdl_trigger();
+  const uint32_t epoch = ar_global_call(pe, call) + 1u;
+  const uint32_t buf = (uint32_t)call & 1u;
+  const int t = blockIdx.y;
+  const int e0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8;
+  if (e0 >= H) return;
+  const uint4 v = *reinterpret_cast<const uint4*>(x + (int64_t)t * ldx + e0);
+#pragma unroll
+  for (int p = 0; p < AR_MAX_WORLD; ++p) {
+    if (p >= pe.world) break;
+    uint32_t* d = ar_ll_slot(pe, p, buf, pe.rank) + (int64_t)t * H + e0;
+    st_ll16(d, v.x, v.y, epoch);
+    st_ll16(d + 4, v.z, v.w, epoch);
+  }
+}
+
+void ll_push(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+             torch::Tensor step, int64_t calls_per_step) {
+  const int64_t T = x.size(0), H = x.size(1);
+  TORCH_CHECK(x.dtype() == torch::kBFloat16 && x.stride(1) == 1 && x.stride(0) % 8 == 0, "ll_push: bf16 rows");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0, "ll_push: 16-byte aligned rows");
+  TORCH_CHECK(H % 256 == 0 && T * H <= slot_elems, "ll_push: H % 256 and T*H within the slot");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(x.device());
+  ArPeers pe = make_peers(peers, rank, world, slot_elems, H, step, calls_per_step);
+  const int threads = 128;
+  TORCH_CHECK(launch_pdl(ll_push_kernel, dim3((unsigned)((H / 8 + threads - 1) / threads), (unsigned)T), dim3(threads),
+                         0, at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()),
+                         x.stride(0), pe, (int)H, (int)call) == cudaSuccess,
+              "ll_push launch");
+}
+
+// Consumer: one CTA per token row, K / 8 threads, thread i owns elements [8 i, 8 i + 8) -- two 16-byte
+// LL words per source, all W x 2 loads in flight together (W is a template parameter).
+template <int W>
+__global__ void __launch_bounds__(1024) ar_ll_rmsnorm_kernel(
+    ArPeers pe, int call, const __nv_bfloat16* __restrict__ res_in, __nv_bfloat16* __restrict__ res_out,
+    const __nv_bfloat16* __restrict__ w, int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y,
+    uint8_t* __restrict__ q, uint8_t* __restrict__ sf, int* status, uint64_t timeout_ns) {
+  pdl_trigger();  // the next GEMM may launch and stream its weights (it waits for this grid's results)
+  __shared__ float sred[32];
+  __shared__ int s_fail;
+  const int r = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int e0 = tid * 8;
+  const uint32_t epoch = ar_global_call(pe, call) + 1u;
+  const uint32_t buf = (uint32_t)call & 1u;
+  if (tid == 0) s_fail = 0;
+  __syncthreads();
+  float v[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = 0.f;
+  uint4 raw[W][2];
+  const uint32_t* src[W];
+#pragma unroll
+  for (int s = 0; s < W; ++s) src[s] = ar_ll_slot(pe, pe.rank, buf, s) + (int64_t)r * K + e0;
+  uint32_t pending = (1u << (2 * W)) - 1u;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+#pragma unroll
+    for (int s = 0; s < W; ++s)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t bit = 1u << (2 * s + h);
+        if (pending & bit) {
+          raw[s][h] = ld_ll16(src[s] + 4 * h);
+          if (raw[s][h].y == epoch && raw[s][h].w == epoch) pending &= ~bit;
+        }
+      }
+    if (pending == 0u) break;
+    if (globaltimer_ns() - t0 > timeout_ns) {
+      report_error(status, kErrPeerTimeout, 320, r * 65536 + __ffs(pending) - 1);
+      s_fail = 1;
+      break;
+    }
+  }
+  __syncthreads();
+  if (s_fail) return;  // uniform: no barrier follows for a failed block, and nothing is written
+#pragma unroll
+  for (int s = 0; s < W; ++s)  // fixed rank order: identical sums on every rank
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw[s][h].x);
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw[s][h].z);
+      v[4 * h + 0] += __low2float(a);
+      v[4 * h + 1] += __high2float(a);
+      v[4 * h + 2] += __low2float(b);
+      v[4 * h + 3] += __high2float(b);
+    }
+  // the reduced partial is rounded to bf16 (as a stored GEMM output would be) before the residual add
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __bfloat162float(__float2bfloat16(v[i]));
+  if (res_in != nullptr) {
+    const uint4 rr = *reinterpret_cast<const uint4*>(res_in + (int64_t)r * K + e0);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&rr);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] += __bfloat162float(e[i]);
+  }
+  {
+    uint4 ro;
+    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&ro);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      e[i] = __float2bfloat16(v[i]);
+      v[i] = __bfloat162float(e[i]);
+    }
+    if (res_out != nullptr) *reinterpret_cast<uint4*>(res_out + (int64_t)r * K + e0) = ro;
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) sred[tid >> 5] = ss;
+  __syncthreads();
+  if (tid < 32) {
+    float t = tid < (int)(blockDim.x >> 5) ? sred[tid] : 0.f;
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (tid == 0) sred[0] = t;
+  }
+  __syncthreads();
+  const float rrs = rsqrtf(sred[0] / (float)K + eps);
+  {
+    const uint4 wr = *reinterpret_cast<const uint4*>(w + e0);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&wr);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      float wv = __bfloat162float(e[i]);
+      if (plus_one) wv += 1.f;
+      v[i] = v[i] * rrs * wv;
+    }
+  }
+  if (y != nullptr) {
+    uint4 yo;
+    __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&yo);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      e[i] = __float2bfloat16(v[i]);
+      v[i] = __bfloat162float(e[i]);
+    }
+    *reinterpret_cast<uint4*>(y + (int64_t)r * K + e0) = yo;
+  }
+  if (q != nullptr) {
+    // MX block of 32 elements = 4 consecutive threads
+    float am = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(v[i]));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    const int ex = mx_exponent(am, 448.f);
+    const float si = exp2i(-ex);
+    uint2 qo;
+    uint8_t* b8 = reinterpret_cast<uint8_t*>(&qo);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) b8[i] = f32_to_e4m3(v[i] * si);
+    *reinterpret_cast<uint2*>(q + (int64_t)r * K + e0) = qo;
+    if ((tid & 3) == 0) sf[sf_offset(r, e0 >> 5, K / 32)] = (uint8_t)(ex + 127);
+  }
+}
+
+void ar_ll_rmsnorm(torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call,
+                   torch::Tensor step, int64_t calls_per_step, int64_t T, c10::optional<torch::Tensor> res_in,
+                   c10::optional<torch::Tensor> res_out, torch::Tensor w, double eps, bool plus_one,
+                   c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf,
+                   torch::Tensor status, double timeout_s) {
+  const int64_t K = w.size(0);
+  TORCH_CHECK(K % 256 == 0 && K / 8 <= 1024, "ar_ll_rmsnorm: hidden must be a multiple of 256 and <= 8192");
+  TORCH_CHECK(T * K <= slot_elems, "ar_ll_rmsnorm: rows exceed the slot");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(w.device());
+  ArPeers pe = make_peers(peers, rank, world, slot_elems, K, step, calls_per_step);
+  auto bf = [](const c10::optional<torch::Tensor>& t) -> __nv_bfloat16* {
+    return (t.has_value() && t->defined()) ? reinterpret_cast<__nv_bfloat16*>(t->data_ptr()) : nullptr;
+  };
+  auto u8 = [](const c10::optional<torch::Tensor>& t) -> uint8_t* {
+    return (t.has_value() && t->defined()) ? t->data_ptr<uint8_t>() : nullptr;
+  };
+  const dim3 grid((unsigned)T), block((unsigned)(K / 8));
+  const auto st = at::cuda::getCurrentCUDAStream();
+  const uint64_t tmo = (uint64_t)(timeout_s * 1e9);
+  const __nv_bfloat16* wp = reinterpret_cast<const __nv_bfloat16*>(w.data_ptr());
+  cudaError_t e = cudaErrorInvalidValue;
+#define R9K_LL(WS)                                                                                                    \
+  case WS:                                                                                                            \
+    e = launch_pdl(ar_ll_rmsnorm_kernel<WS>, grid, block, 0, st, pe, (int)call, bf(res_in), bf(res_out), wp, (int)K,  \
+                   (float)eps, plus_one ? 1 : 0, bf(y), u8(q), u8(sf), status.data_ptr<int>(), tmo);                  \
+    break;
+  switch (world) {
+    R9K_LL(1)
+    R9K_LL(2)
+    R9K_LL(3)
+    R9K_LL(4)
+    R9K_LL(5)
+    R9K_LL(6)
+    R9K_LL(7)
+    R9K_LL(8)
+    default: break;
+  }
+#undef R9K_LL
+  TORCH_CHECK(e == cudaSuccess, "ar_ll_rmsnorm launch: ", cudaGetErrorString(e));
+}
+
+}  // namespace r9k

@@ -2,7 +2,13 @@
 //
 // Region of every rank: [flags: 2 buffers x 8 sources x 256 tiles x u32 (16 KiB, padded to 64 KiB)]
 //                       [data : 2 buffers x world sources x slot_elems bf16]
+//                       [LL   : 2 buffers x world sources x slot_elems/2 {bf16x2, u32 epoch} pairs]
 // Call g (global index = step * calls_per_step + k) uses buffer g & 1 and epoch g + 1.
+//
+// LL ("low-latency") slots carry the call's epoch inside every 8-byte word next to two bf16 values,
+// so a reader knows a word has arrived by its epoch alone: no fence, no separate flag, no round trip
+// before the data moves. A 16-byte store writes two such words; readers check both epochs (each
+// aligned 8-byte half is written as one unit).
 #pragma once
 #include <torch/extension.h>
 #include "common.cuh"
@@ -48,6 +54,23 @@ R9K_DEVINL uint4 ld_volatile_u4(const uint4* p) {
   uint4 v;
   asm volatile("ld.global.cg.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p)
                : "memory");
+  return v;
+}
+
+// LL slot of source `src` in rank p's region, buffer `buf`: u32 words, element e of row t at word
+// (t * H + e) rounded down to even, its pair's epoch at the next word (slot = slot_elems words).
+R9K_DEVINL uint32_t* ar_ll_slot(const ArPeers& pe, int p, uint32_t buf, int src) {
+  uint8_t* ll = pe.base[p] + AR_FLAG_BYTES + 2 * (int64_t)pe.world * pe.slot_elems * 2;
+  return reinterpret_cast<uint32_t*>(ll) + ((int64_t)buf * pe.world + src) * pe.slot_elems;
+}
+R9K_DEVINL void st_ll16(uint32_t* p, uint32_t d0, uint32_t d1, uint32_t e) {
+  asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(d0), "r"(e), "r"(d1), "r"(e)
+               : "memory");
+}
+R9K_DEVINL uint4 ld_ll16(const uint32_t* p) {
+  uint4 v;
+  asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p) : "memory");
   return v;
 }
 

@@ -34,6 +34,7 @@ struct GemmArgs {
   // EPI_PUSH: the bf16 result goes to slot [rank] of every rank's all-reduce region (NVLink stores)
   ArPeers peers;
   int ar_call;
+  int ar_ll;  // EPI_PUSH into the LL slots (epoch in every word, no tile flags)
   // grouped (MoE) mode: grid.y walks a device work list of (expert, first row, rows) token tiles;
   // expert e's weight is row tiles [e * g_row_tiles, (e + 1) * g_row_tiles) of the stacked matrix
   const int32_t* g_work;
@@ -41,7 +42,16 @@ struct GemmArgs {
   int g_row_tiles;
   // weight chunks prefetched into L2 ahead of the shared-memory ring (0: none)
   int l2_prefetch;
+  // split-K with the S splits of a tile launched as one thread-block cluster (1, S, 1): the fp32
+  // partials meet in distributed shared memory instead of a global workspace (no fix-up kernel tail)
+  int cluster_k;
 };
+
+R9K_DEVINL float ld_dsmem_f32(uint32_t addr) {
+  float v;
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  return v;
+}
 
 // A (weight) tile load: row-major 2-D map, or pre-tiled 3-D map indexed by unit
 R9K_DEVINL void load_a_tile(void* dst, const CUtensorMap* map, uint64_t* bar, const GemmArgs& a, int kc, int box_x,
@@ -55,14 +65,17 @@ R9K_DEVINL void prefetch_a_tile(const CUtensorMap* map, const GemmArgs& a, int k
   else tma_prefetch_2d(map, kc * box_x, m0);
 }
 
+// tmask: bit t set = token tok0 + t is stored by this thread's CTA (cluster split-K spreads a tile's
+// tokens over the CTAs of the cluster)
 template <int BN, bool DUAL, int EPI>
 R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u, int row, int tok0, int lane,
-                               const ArCall* arc = nullptr) {
+                               const ArCall* arc = nullptr, uint32_t tmask = 0xffffu) {
   if constexpr (EPI == EPI_SWIGLU_MXFP8) {
     uint8_t* outq = reinterpret_cast<uint8_t*>(a.out);
 #pragma unroll
     for (int t = 0; t < 16; ++t) {
       const int tok = tok0 + t;
+      if (!((tmask >> t) & 1u)) continue;  // uniform across the warp: the shuffles below stay converged
       float h = (row < a.N) ? silu_f(g[t]) * u[t] : 0.f;
       float am = fabsf(h);
 #pragma unroll
@@ -95,7 +108,7 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const int tok = tok0 + t;
-        if (tok < a.M) out[(int64_t)tok * a.ldo + row] = __float2bfloat16(silu_f(g[t]) * u[t]);
+        if (tok < a.M && ((tmask >> t) & 1u)) out[(int64_t)tok * a.ldo + row] = __float2bfloat16(silu_f(g[t]) * u[t]);
       }
     }
   } else if constexpr (EPI == EPI_F32) {
@@ -104,7 +117,7 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const int tok = tok0 + t;
-        if (tok < a.M) out[(int64_t)tok * a.ldo + row] = g[t] * a.alpha;
+        if (tok < a.M && ((tmask >> t) & 1u)) out[(int64_t)tok * a.ldo + row] = g[t] * a.alpha;
       }
     }
   } else {
@@ -113,7 +126,7 @@ R9K_DEVINL void epilogue_chunk(const GemmArgs& a, const float* g, const float* u
 #pragma unroll
       for (int t = 0; t < 16; ++t) {
         const int tok = tok0 + t;
-        if (tok < a.M) {
+        if (tok < a.M && ((tmask >> t) & 1u)) {
           float y = g[t] * a.alpha;
           if (a.residual != nullptr) y += __bfloat162float(a.residual[(int64_t)tok * a.ldr + row]);
           out[(int64_t)tok * a.ldo + row] = __float2bfloat16(y);

@@ -30,7 +30,9 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
+#include <map>
 #include <mutex>
+#include <tuple>
 #include <unordered_map>
 #include "gemm_common.cuh"
 
@@ -340,6 +342,25 @@ __global__ void __launch_bounds__(192, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
       const uint4* src = reinterpret_cast<const uint4*>(stg);
       const int W = args.peers.world;
+      if (args.ar_ll) {
+        // LL slots: two bf16 + the epoch per 8-byte word, buffer call % 2 (see comm.cuh); the data is
+        // its own ready signal, so no fence and no tile flag follow
+        const uint32_t ep = ar_global_call(args.peers, args.ar_call) + 1u;
+        const uint32_t lb = (uint32_t)args.ar_call & 1u;
+        for (int idx = ct; idx < args.M * 16; idx += 128) {
+          const int tok = idx >> 4, ch = idx & 15;
+          const uint4 v = src[tok * 16 + ch];
+          const int64_t off = (int64_t)tok * args.N + m0 + ch * 8;
+#pragma unroll
+          for (int p = 0; p < AR_MAX_WORLD; ++p) {
+            if (p >= W) break;
+            uint32_t* d = ar_ll_slot(args.peers, p, lb, args.peers.rank) + off;
+            st_ll16(d, v.x, v.y, ep);
+            st_ll16(d + 4, v.z, v.w, ep);
+          }
+        }
+        return;
+      }
       for (int idx = ct; idx < args.M * 16; idx += 128) {
         const int tok = idx >> 4, ch = idx & 15;
         const uint4 v = src[tok * 16 + ch];
@@ -367,6 +388,25 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
       if constexpr (EPI == EPI_PUSH) flush_push();
+    } else if (args.cluster_k) {
+      // cluster split-K: park this split's fp32 partial [NA][BN][128] in this CTA's shared memory (the
+      // operand ring is idle once the accumulator is complete); the splits meet below
+      float* mypart = reinterpret_cast<float*>(smem);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        float g[16], u[16];
+        if (nk > 0 && ok) {
+          load_acc(c, g, u);
+        } else {
+#pragma unroll
+          for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
+        }
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          mypart[(c + t) * 128 + row_local] = g[t];
+          if (DUAL) mypart[BN * 128 + (c + t) * 128 + row_local] = u[t];
+        }
+      }
     } else if (ok) {
       // split-K: park the fp32 partial, the last split to arrive sums all splits in split order
       const int tile_id = n_tile * gridDim.x + blockIdx.x;
@@ -418,6 +458,43 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  if (S > 1 && args.cluster_k) {
+    // every split of the tile parked its partial; each CTA of the cluster now owns the tokens
+    // t == its cluster rank (mod S) of the tile, sums the S partials over distributed shared memory in
+    // rank order (the same order for every token: deterministic) and runs the epilogue for them
+    cluster_sync();
+    if (warp >= 2) {
+      const int row_local = (warp & 3) * 32 + lane;
+      const uint32_t me = cluster_ctarank();
+      const uint32_t my_base = smem_u32(smem);
+      GemmArgs ea = args;
+      ea.M = m_valid;
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t tmask = 0;
+#pragma unroll
+        for (int t = 0; t < 16; ++t)
+          if ((uint32_t)((c + t) % S) == me && n0 + c + t < m_valid) tmask |= 1u << t;
+        if (tmask == 0) continue;
+        float g[16], u[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
+#pragma unroll 1
+        for (int k = 0; k < S; ++k) {
+          const uint32_t rb = mapa_shared(my_base, (uint32_t)k);
+#pragma unroll
+          for (int t = 0; t < 16; ++t) {
+            if (!((tmask >> t) & 1u)) continue;
+            g[t] += ld_dsmem_f32(rb + (uint32_t)(((c + t) * 128 + row_local) * 4));
+            if (DUAL) u[t] += ld_dsmem_f32(rb + (uint32_t)((BN * 128 + (c + t) * 128 + row_local) * 4));
+          }
+        }
+        epilogue_chunk<BN, DUAL, EPI>(ea, g, u, m0 + row_local, n0 + c, lane, nullptr, tmask);
+      }
+    }
+    cluster_sync();  // no CTA leaves while a peer may still read its partial
+  }
+
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -441,6 +518,15 @@ struct LaunchPlan {
 };
 
 static int num_sms() { return device_sm_count(); }
+
+static bool gemm_cluster_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("R9K_GEMM_CLUSTER");
+    v = (e && (e[0] == '0' || e[0] == 's')) ? 0 : 1;  // "0" / "stock": global-workspace split-K fix-up
+  }
+  return v == 1;
+}
 
 static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
   LaunchPlan p;
@@ -467,10 +553,42 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
     // fill the resident CTA slots: split K (global-memory fix-up, no clusters) with >= 4 chunks/split
     const int per_sm = (dual && p.unpack) ? 1 : 2;
     const int target = per_sm * num_sms();
-    p.S = std::max(1, std::min(16, target / std::max(1, tiles)));
+    // (at most 8 splits when they form a cluster: the portable cluster size)
+    p.S = std::max(1, std::min(gemm_cluster_enabled() ? 8 : 16, target / std::max(1, tiles)));
     while (p.S > 1 && kchunks / p.S < 4) --p.S;
   }
   return p;
+}
+
+// Clusters of S CTAs (1 x S x 1, 192 threads) of a kernel that can be resident at once on this
+// device (cudaOccupancyMaxActiveClusters), cached per (kernel, S, device).
+static int max_active_clusters(const void* kern, int S, int smem) {
+  static std::mutex mu;
+  static std::map<std::tuple<const void*, int, int>, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  const auto key = std::make_tuple(kern, S, dev);
+  auto it = cache.find(key);
+  if (it != cache.end()) return it->second;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1, (unsigned)S, 1);
+  cfg.blockDim = dim3(192, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 1;
+  attr[0].val.clusterDim.y = (unsigned)S;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  cache[key] = n;
+  return n;
 }
 
 // workspace layout: [65536 int counters][partials]
@@ -495,6 +613,15 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
       part = ws->data_ptr<float>() + kWsCounters;
     }
   }
+  // split-K partials meet in distributed shared memory when the splits of a tile form a cluster, and
+  // every cluster of the grid can be resident at once (else the global fix-up keeps one wave)
+  bool cluster = p.S > 1 && p.S <= 8 && EPI != EPI_PUSH && MT == 1 && gemm_cluster_enabled();
+  if (cluster) cluster = grid_x * p.n_tiles <= max_active_clusters((const void*)kern, p.S, C::SMEM_BYTES);
+  if (cluster) {
+    part = nullptr;
+    cnt = nullptr;
+  }
+  args.cluster_k = cluster ? 1 : 0;
   args.splits = p.S;
   args.kc_per_split = (args.kchunks + p.S - 1) / p.S;
   static int l2pf = -1;
@@ -508,11 +635,15 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
   cfg.blockDim = dim3(192, 1, 1);
   cfg.dynamicSmemBytes = C::SMEM_BYTES;
   cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = cluster ? (unsigned)p.S : 1u;
+  attr[1].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = cluster ? 2 : 1;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, ta2, tb, args, part, cnt);
   TORCH_CHECK(e == cudaSuccess, "r9k gemm launch failed: ", cudaGetErrorString(e));
 }
@@ -633,7 +764,7 @@ void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, t
 // on each rank then reduces. Decode-sized batches only (one token tile).
 void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, torch::Tensor x_sf, int64_t N,
                   torch::Tensor peers, int64_t rank, int64_t world, int64_t slot_elems, int64_t call, torch::Tensor step,
-                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace) {
+                  int64_t calls_per_step, torch::Tensor status, c10::optional<torch::Tensor> workspace, int64_t ll) {
   const int64_t M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 128 == 0 && N % 128 == 0, "gemm_mx_push: K and N multiples of 128");
   TORCH_CHECK(M * N <= slot_elems, "gemm_mx_push: output exceeds the slot");
@@ -655,6 +786,7 @@ void gemm_mx_push(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor
   a.timeout_ns = 1000000000ull;
   a.peers = make_peers(peers, rank, world, slot_elems, N, step, calls_per_step);
   a.ar_call = (int)call;
+  a.ar_ll = ll ? 1 : 0;
   torch::Tensor* ws = (workspace.has_value() && workspace->defined()) ? &(*workspace) : nullptr;
   dispatch_bn<KIND_MX, false, EPI_PUSH>(ta, ta, tb, a, p, ws, at::cuda::getCurrentCUDAStream());
 }

@@ -157,6 +157,7 @@ class ModelRunner:
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self.device_events: list | None = None  # (start, end) CUDA events around each replayed step
+        self.logit_log: list | None = None  # (seq_id, fp32 logits row on the host) per sampled row (tests)
 
     # ------------------------------------------------------------------------------------------
     def _upload(self, arr: np.ndarray) -> None:
@@ -238,6 +239,12 @@ class ModelRunner:
             self.model.forward(meta, self.ws, lay.T, lay.R)
             R = lay.R
             torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
+        if self.logit_log is not None:
+            r = 0
+            for ch in out.chunks:
+                if ch.sample:
+                    self.logit_log.append((ch.seq.seq_id, self.ws.logits[r].float().cpu()))
+                    r += 1
         if not sample:
             return {}
         self.sample_host[:R].copy_(self.sample_out[:R], non_blocking=True)

@@ -18,13 +18,15 @@ _KNOBS = {
     "R9K_ATTN_DEC": ("1", "0", "1: keys-on-M split-KV decode attention; 0: the row-tile kernel"),
     "R9K_WEIGHT_TILED": ("1", "0", "1: MX weights stored as contiguous 128x128 units; 0: row-major"),
     "R9K_GEMM_SK": ("0", "0", "1: skinny GEMMs use the persistent stream-K kernel"),
+    "R9K_GEMM_CLUSTER": ("1", "0", "1: split-K GEMM tiles reduce over distributed shared memory (cluster); 0: global fix-up"),
     "R9K_FP4_UNPACK": ("0", "0", "1: skinny fp4 GEMMs load packed bytes and expand them on chip"),
     "R9K_GDN_FUSED": ("1", "0", "1: decode steps run the one-kernel GDN layer core"),
     "R9K_GDN_PREFILL": ("chunked", "serial",
                         "chunked: tensor-core chunked delta rule for long prefill; serial: token-serial recurrence"),
     "R9K_GDN_CHUNK_MIN": ("256", "256", "shortest sequence that takes the chunked GDN prefill"),
     "R9K_COMM": ("fused", "nccl", "fused: NVLink kernels fused into GEMMs / norms; nccl: every collective on NCCL"),
-    "R9K_AR_MODE": ("pull", "pull", "pull: consumer reads peers' partials; push: GEMM epilogue stores into peers"),
+    "R9K_AR_MODE": ("ll", "pull", "ll: GEMM epilogue stores epoch-tagged partials into peers, consumer polls its own "
+                    "memory; pull: consumer reads peers' partials; push: plain stores + per-tile flags"),
     "R9K_GDN_STATE": ("", "", "'' (model default) | bf16 | fp32"),
     "R9K_DISABLE": ("", "", "comma list of coarse opt-outs (e.g. plugin)"),
     "R9K_AR_ONESHOT_MAX_KB": ("512", "512", "largest standalone all-reduce sent one-shot"),
@@ -42,7 +44,7 @@ _KNOBS = {
     "R9K_EP": ("ar", "ar", "ar: experts' partials summed by the all-reduce; a2a: all-to-all dispatch/combine"),
 }
 # knobs the C++ library reads with getenv (kept in sync by export_native)
-_NATIVE = ("R9K_ATTN_DEC", "R9K_FP4_UNPACK", "R9K_GEMM_L2PF", "R9K_GEMM_SK", "R9K_MOE_MT")
+_NATIVE = ("R9K_ATTN_DEC", "R9K_FP4_UNPACK", "R9K_GEMM_L2PF", "R9K_GEMM_SK", "R9K_MOE_MT", "R9K_GEMM_CLUSTER")
 _DEFAULTS = {k: v[0] for k, v in _KNOBS.items()}
 _cache: dict[str, str] = {}
 

@@ -96,10 +96,11 @@ class DSV4LM(MLAMoELM):
         for i, lay in enumerate(self.layers):
             lay["hc_attn"], lay["hc_ffn"] = mhc_params(2 * i), mhc_params(2 * i + 1)
             if "router" in lay:
-                seed_e = seed * 100000 + i * 1000 + r * 10
-                lay["x_gate"] = X.random_linear(H, I, c.expert_bits, self.device, seed=seed_e + 1, experts=El)
-                lay["x_up"] = X.random_linear(H, I, c.expert_bits, self.device, seed=seed_e + 2, experts=El)
-                lay["x_down"] = X.random_linear(I, H, c.expert_bits, self.device, seed=seed_e + 3, experts=El)
+                # expert e of layer i is keyed by (layer, e): rank r's slice is the TP=1 model's experts
+                seed_e = seed * 100000 + i * 10
+                lay["x_gate"] = X.random_linear(H, I, c.expert_bits, self.device, seed=seed_e + 1, experts=El, first=r * El)
+                lay["x_up"] = X.random_linear(H, I, c.expert_bits, self.device, seed=seed_e + 2, experts=El, first=r * El)
+                lay["x_down"] = X.random_linear(I, H, c.expert_bits, self.device, seed=seed_e + 3, experts=El, first=r * El)
             if i in c.engram_layers:
                 lay["engram"] = HostTable.random(c.engram_rows, c.engram_dim, "fp8", seed=seed * 31 + i, std=0.02)
                 lay["eng_proj"] = L.BF16Weight(wf.randn(H, c.engram_dim, dtype=torch.bfloat16))

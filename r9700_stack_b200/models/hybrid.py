@@ -23,7 +23,7 @@ from .. import _native, knobs
 from ..ops import linear as L
 from .config import HybridConfig, ParallelConfig
 from ..utils import status as _status
-from .weights import WeightFactory, from_float
+from .weights import TPFactory, WeightFactory, from_float
 
 
 def _ops():
@@ -167,14 +167,25 @@ class HybridLM:
         self.embed = wf.randn(c.vocab, H, std=c.init_std, dtype=torch.bfloat16)
         self.layers = []
         a, g = self.attn_dims, self.gdn_dims
-        wf_rank = WeightFactory(self.device, seed=seed * 1000 + 31 + r, std=c.init_std)
+        # sharded tensors: the whole model's tensor from its own seed, cut to this rank's shard
+        tpf = TPFactory(self.device, seed=seed * 1000 + 31, std=c.init_std)
+        D, d = c.head_dim, c.gdn_head_dim
+        hq, hkv = a["hq"], a["hkv"]
+        kv0 = (r * hq) // (c.n_q_heads // c.n_kv_heads)  # first kv head of this rank (replicated past tp = n_kv)
+        qseg = (c.n_q_heads * D, r * hq * D, hq * D)
+        kvseg = (c.n_kv_heads * D, kv0 * D, hkv * D)
+        qkv_segs = [qseg, qseg, kvseg, kvseg] if c.attn_output_gate else [qseg, kvseg, kvseg]
+        hk, hv = g["hk"], g["hv"]
+        kseg = (c.gdn_k_heads * d, r * hk * d, hk * d)
+        vseg = (c.gdn_v_heads * d, r * hv * d, hv * d)
+        hseg = (c.gdn_v_heads, r * hv, hv)
         for i in range(c.layers):
             lay = {"attn": c.is_attention(i)}
             lay["in_norm"] = wf.norm(H, c.norm_plus_one)
             lay["post_norm"] = wf.norm(H, c.norm_plus_one)
             if lay["attn"]:
-                lay["w_qkv"] = wf_rank.linear(a["qkv_rows"], H, fmt)
-                lay["w_o"] = wf_rank.linear(H, a["hq"] * c.head_dim, fmt)
+                lay["w_qkv"] = tpf.rows(qkv_segs, H, fmt)
+                lay["w_o"] = tpf.cols(H, c.n_q_heads * D, r * hq * D, hq * D, fmt)
                 lay["q_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
                 lay["k_norm"] = wf.norm(c.head_dim, c.norm_plus_one)
                 if c.qsa_topk:
@@ -183,12 +194,13 @@ class HybridLM:
                     lay["w_idx"] = wf.linear((c.qsa_heads + 1) * 128, H, fmt)
                     lay["idx_norm"] = wf.norm(128, c.norm_plus_one)
             else:
-                d = c.gdn_head_dim
-                lay["w_in"] = wf_rank.linear(g["proj_rows"], H, fmt)
-                lay["w_out"] = wf_rank.linear(H, g["hv"] * d, fmt)
-                lay["conv_w"] = wf_rank.randn(g["conv_ch"], c.conv_width, std=0.3, dtype=torch.bfloat16)
-                lay["A_log"] = torch.log(torch.empty(g["hv"], device=self.device).uniform_(1, 16, generator=wf_rank.gen))
-                lay["dt_bias"] = wf_rank.randn(g["hv"], std=0.5)
+                # in_proj rows: [q | k | v | z | b | a], each split by heads
+                lay["w_in"] = tpf.rows([kseg, kseg, vseg, vseg, hseg, hseg], H, fmt)
+                lay["w_out"] = tpf.cols(H, c.gdn_v_heads * d, r * hv * d, hv * d, fmt)
+                lay["conv_w"] = tpf.raw_rows([kseg, kseg, vseg], c.conv_width, std=0.3, dtype=torch.bfloat16)
+                u = torch.rand(c.gdn_v_heads, generator=tpf._gen(), device=self.device)
+                lay["A_log"] = torch.log(1.0 + 15.0 * u[r * hv:(r + 1) * hv])
+                lay["dt_bias"] = tpf.raw_rows([hseg], std=0.5)
                 lay["gdn_norm"] = (1.0 + wf.randn(d, std=0.1)).to(torch.bfloat16)
             if c.hc_streams:
                 from ..ops import hc as HCo
@@ -196,16 +208,18 @@ class HybridLM:
                 lay["hc_in"] = HCo.random_point(wf, c.hc_streams, H)
                 lay["hc_post"] = HCo.random_point(wf, c.hc_streams, H)
             if self.ffn_local:
-                lay["w_gate"] = wf_rank.linear(self.ffn_local, H, fmt)
-                lay["w_up"] = wf_rank.linear(self.ffn_local, H, fmt)
-                lay["w_down"] = wf_rank.linear(H, self.ffn_local, fmt)
+                fl = self.ffn_local
+                lay["w_gate"] = tpf.rows([(c.ffn, r * fl, fl)], H, fmt)
+                lay["w_up"] = tpf.rows([(c.ffn, r * fl, fl)], H, fmt)
+                lay["w_down"] = tpf.cols(H, c.ffn, r * fl, fl, fmt)
             self.layers.append(lay)
         self.final_norm = wf.norm(H, c.norm_plus_one)
         if c.hc_streams:
             from ..ops import hc as HCo
 
             self.hc_final = HCo.random_point(wf, c.hc_streams, H)
-        self.lm_head = wf_rank.linear(self.vocab_local, H, c.lm_head_format)
+        vl = self.vocab_local
+        self.lm_head = tpf.rows([(c.vocab, r * vl, vl)], H, c.lm_head_format)
         self.mx = not isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.BF16Weight)
 
     def _rope_cache(self, max_pos: int):
@@ -350,8 +364,10 @@ class HybridLM:
     def _attn_tile_table(self, meta: StepMeta, qt: int) -> torch.Tensor:
         """(sequence, first token, rows) per prefill query tile of qt tokens: built once per step from
         the host sequence list and uploaded from pinned memory, then reused by every attention layer."""
-        if meta.attn_tiles is None:
-            meta.attn_tiles = {}
+        # step metadata views are reused across steps of the same shape: the table belongs to this
+        # step's host sequence list (held by the cache, so an identity check cannot be fooled)
+        if meta.attn_tiles is None or meta.attn_tiles.get("seqs") is not meta.host_seqs:
+            meta.attn_tiles = {"seqs": meta.host_seqs}
         tt = meta.attn_tiles.get(qt)
         if tt is None:
             import numpy as np

@@ -19,7 +19,7 @@ import torch
 from .. import _native
 from ..ops import linear as L
 from .hybrid import HybridLM, Workspace
-from .weights import WeightFactory, from_float
+from .weights import TPFactory, WeightFactory, from_float
 
 
 def _ops():
@@ -126,29 +126,32 @@ class HybridMoELM(HybridLM):
     def _build(self, seed: int):
         c = self.cfg
         super()._build(seed)
-        r = self.par.tp_rank
-        wf = WeightFactory(self.device, seed=seed * 1000 + 77 + r, std=c.init_std)
+        r, tp = self.par.tp_rank, self.par.tp_size
+        tpf = TPFactory(self.device, seed=seed * 1000 + 77, std=c.init_std)
         wrep = WeightFactory(self.device, seed=seed * 1000 + 79, std=c.init_std)
         H, I = c.hidden, c.moe_ffn
+        E, El = c.moe_experts, self.e_local
+        mine = self.placement[r] if self.placement is not None else list(range(r * El, (r + 1) * El))
+        sl = self.shared_local
+
+        def experts(rows_per, K):
+            # every expert of the layer drawn as one stacked [E * rows, K] tensor (one NVFP4 global scale
+            # per tensor, as a checkpoint stores it), then this rank's experts in placement order; every
+            # expert spans whole 128-row tiles, so tiling the selection gives stack_experts()' unit order
+            full = tpf.full(E * rows_per, K)
+            sel = full.view(E, rows_per, K)[torch.tensor(mine, device=self.device)].reshape(El * rows_per, K)
+            return from_float(sel, "nvfp4", tiled=True, global_from=full)
+
         for li, lay in enumerate(self.layers):
             lay["router"] = L.BF16Weight(wrep.randn(c.moe_experts, H, dtype=torch.bfloat16))
-            # the local experts of a layer are generated and quantised as one stacked [E * rows, K] tensor
-            # (one NVFP4 global scale per layer); tiling the stacked tensor gives exactly the unit order
-            # of stack_experts() over per-expert weights, since every expert spans whole 128-row tiles
-            El = self.e_local
-            if self.placement is None:
-                lay["e_gate"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
-                lay["e_up"] = from_float(wf.randn(El * I, H), "nvfp4", tiled=True)
-                lay["e_down"] = from_float(wf.randn(El * H, I), "nvfp4", tiled=True)
-            else:
-                mats = [self._expert_weights(seed, li, e, H, I) for e in self.placement[r]]
-                lay["e_gate"] = from_float(torch.cat([m[0] for m in mats]), "nvfp4", tiled=True)
-                lay["e_up"] = from_float(torch.cat([m[1] for m in mats]), "nvfp4", tiled=True)
-                lay["e_down"] = from_float(torch.cat([m[2] for m in mats]), "nvfp4", tiled=True)
-            if self.shared_local:
-                lay["s_gate"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
-                lay["s_up"] = L.BF16Weight(wf.randn(self.shared_local, H, dtype=torch.bfloat16))
-                lay["s_down"] = L.BF16Weight(wf.randn(H, self.shared_local, dtype=torch.bfloat16))
+            lay["e_gate"] = experts(I, H)
+            lay["e_up"] = experts(I, H)
+            lay["e_down"] = experts(H, I)
+            if sl:
+                S = c.moe_shared_ffn
+                lay["s_gate"] = L.BF16Weight(tpf.raw_rows([(S, r * sl, sl)], H, dtype=torch.bfloat16))
+                lay["s_up"] = L.BF16Weight(tpf.raw_rows([(S, r * sl, sl)], H, dtype=torch.bfloat16))
+                lay["s_down"] = L.BF16Weight(tpf.full(H, S)[:, r * sl:(r + 1) * sl].to(torch.bfloat16).contiguous())
                 lay["s_gvec"] = L.BF16Weight(wrep.randn(1, H, dtype=torch.bfloat16))
             if c.ple_dim:
                 lay["ple_gate"] = L.BF16Weight(wrep.randn(c.ple_dim, H, dtype=torch.bfloat16))
@@ -165,14 +168,6 @@ class HybridMoELM(HybridLM):
 
             # per-layer token embeddings, int6 rows in pinned host memory: row (token * layers + layer)
             self.ple = HostTable.random(c.vocab * c.layers, c.ple_dim, "int6", seed=seed * 7 + 3, std=0.05)
-
-    def _expert_weights(self, seed: int, layer: int, e: int, H: int, I: int):
-        """(gate [I, H], up [I, H], down [H, I]) fp32 of global expert e of a layer, placement-independent."""
-        g = torch.Generator(device=self.device)
-        g.manual_seed(seed * 1_000_003 + layer * 4099 + e)
-        std = self.cfg.init_std
-        mk = lambda *shape: torch.randn(*shape, generator=g, device=self.device) * std  # noqa: E731
-        return mk(I, H), mk(I, H), mk(H, I)
 
     def local_index(self, e: int) -> int:
         """Local index of global expert e on this rank, or -1 when another rank holds it."""

@@ -24,7 +24,7 @@ from ..ops import linear as L
 from .config import ParallelConfig
 from .hybrid import NoComm, StepMeta
 from .hybrid_moe import MoEBuffers, moe_ffn
-from .weights import WeightFactory, from_float
+from .weights import TPFactory, WeightFactory, from_float
 
 LAT, PE, IDX = 512, 64, 128
 
@@ -144,42 +144,50 @@ class MLAMoELM:
     def _build(self, seed: int):
         c, r = self.cfg, self.par.tp_rank
         wf = WeightFactory(self.device, seed=seed * 1000 + 17, std=c.init_std)
-        wr = WeightFactory(self.device, seed=seed * 1000 + 31 + r, std=c.init_std)
+        tpf = TPFactory(self.device, seed=seed * 1000 + 31, std=c.init_std)
+        tp = self.par.tp_size
         H, nh = c.hidden, self.nh
-        bf = lambda *s, std=None: wr.randn(*s, std=std, dtype=torch.bfloat16)
+        QH = c.qk_nope + PE
+        h0 = r * nh  # first head of this rank
+        bfw = lambda t: L.BF16Weight(t.to(torch.bfloat16).contiguous())  # noqa: E731
         self.embed = wf.randn(c.vocab, H, dtype=torch.bfloat16)
         self.layers = []
         for i in range(c.layers):
             lay = {
                 "in_norm": wf.norm(H, False), "post_norm": wf.norm(H, False),
                 "w_dq": L.BF16Weight(wf.randn(c.q_lora, H, dtype=torch.bfloat16)), "q_norm": wf.norm(c.q_lora, False),
-                "w_uq": L.BF16Weight(bf(nh * (c.qk_nope + PE), c.q_lora)),
+                "w_uq": bfw(tpf.raw_rows([(c.n_heads * QH, h0 * QH, nh * QH)], c.q_lora)),
                 "w_dkv": L.BF16Weight(wf.randn(LAT + PE, H, dtype=torch.bfloat16)), "kv_norm": wf.norm(LAT, False),
-                "w_uk": bf(nh, LAT, c.qk_nope, std=0.05), "w_uv": bf(nh, c.v_head, LAT, std=0.05),
-                "w_o": L.BF16Weight(bf(H, nh * c.v_head)),
+                "w_uk": tpf.full(c.n_heads, LAT, c.qk_nope, std=0.05)[h0:h0 + nh].to(torch.bfloat16).contiguous(),
+                "w_uv": tpf.full(c.n_heads, c.v_head, LAT, std=0.05)[h0:h0 + nh].to(torch.bfloat16).contiguous(),
+                "w_o": bfw(tpf.full(H, c.n_heads * c.v_head)[:, h0 * c.v_head:(h0 + nh) * c.v_head]),
                 "w_iq": L.BF16Weight(wf.randn(c.index_heads * IDX, c.q_lora, dtype=torch.bfloat16)),
                 "w_ik": L.BF16Weight(wf.randn(IDX, H, dtype=torch.bfloat16)), "ik_norm": wf.norm(IDX, False),
                 "w_iw": L.BF16Weight(wf.randn(c.index_heads, H, dtype=torch.bfloat16)),
             }
             if i < c.first_dense:
-                lay["w_gate"] = L.BF16Weight(bf(self.dense_local, H))
-                lay["w_up"] = L.BF16Weight(bf(self.dense_local, H))
-                lay["w_down"] = L.BF16Weight(bf(H, self.dense_local))
+                dl = self.dense_local
+                lay["w_gate"] = bfw(tpf.raw_rows([(c.dense_ffn, r * dl, dl)], H))
+                lay["w_up"] = bfw(tpf.raw_rows([(c.dense_ffn, r * dl, dl)], H))
+                lay["w_down"] = bfw(tpf.full(H, c.dense_ffn)[:, r * dl:(r + 1) * dl])
             else:
-                El, I = self.e_local, c.moe_ffn
+                El, I, E = self.e_local, c.moe_ffn, c.moe_experts
                 lay["router"] = L.BF16Weight(wf.randn(c.moe_experts, H, dtype=torch.bfloat16))
                 lay["router_bias"] = (wf.randn(c.moe_experts, std=0.01)).float()
                 if self.mx_experts:
-                    lay["e_gate"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
-                    lay["e_up"] = from_float(wr.randn(El * I, H), c.expert_format, tiled=True)
-                    lay["e_down"] = from_float(wr.randn(El * H, I), c.expert_format, tiled=True)
+                    for name, rows_per, K in (("e_gate", I, H), ("e_up", I, H), ("e_down", H, I)):
+                        full = tpf.full(E * rows_per, K)
+                        lay[name] = from_float(full[r * El * rows_per:(r + 1) * El * rows_per], c.expert_format,
+                                               tiled=True, global_from=full)
                 if self.shared_local:
-                    lay["s_gate"] = L.BF16Weight(bf(self.shared_local, H))
-                    lay["s_up"] = L.BF16Weight(bf(self.shared_local, H))
-                    lay["s_down"] = L.BF16Weight(bf(H, self.shared_local))
+                    sl, S = self.shared_local, c.moe_shared_ffn
+                    lay["s_gate"] = bfw(tpf.raw_rows([(S, r * sl, sl)], H))
+                    lay["s_up"] = bfw(tpf.raw_rows([(S, r * sl, sl)], H))
+                    lay["s_down"] = bfw(tpf.full(H, S)[:, r * sl:(r + 1) * sl])
             self.layers.append(lay)
         self.final_norm = wf.norm(H, False)
-        self.lm_head = L.BF16Weight(wr.randn(self.vocab_local, H, dtype=torch.bfloat16))
+        vl = self.vocab_local
+        self.lm_head = bfw(tpf.raw_rows([(c.vocab, r * vl, vl)], H))
         self.mx = False
 
     def weight_bytes(self) -> int:

@@ -38,13 +38,74 @@ class WeightFactory:
         return (1.0 + self.randn(n, std=0.1)).to(torch.bfloat16)
 
 
-def from_float(w: torch.Tensor, fmt: str, tiled: bool | None = None):
+class TPFactory:
+    """Weights of the whole (unsharded) model, each tensor drawn from its own seed and then sliced to
+    this rank's tensor-parallel shard, so the model built at TP size N is exactly the TP=1 model split
+    N ways (the property the multi-GPU token-equality tests check). Every rank makes the same sequence
+    of calls; the call index keys the seed."""
+
+    def __init__(self, device, seed: int, std: float):
+        self.device = torch.device(device)
+        self.seed = seed
+        self.std = std
+        self.n = 0
+
+    def _gen(self) -> torch.Generator:
+        g = torch.Generator(device=self.device)
+        g.manual_seed(self.seed * 1_000_003 + 7919 * self.n)
+        self.n += 1
+        return g
+
+    def full(self, *shape, std: float | None = None) -> torch.Tensor:
+        """The next whole tensor, N(0, std) fp32."""
+        return torch.randn(*shape, generator=self._gen(), device=self.device) * (self.std if std is None else std)
+
+    @staticmethod
+    def take_rows(full: torch.Tensor, segs) -> torch.Tensor:
+        """segs = [(rows, start, count), ...]: `full` is the segments stacked along dim 0; keep rows
+        [start, start + count) of each segment."""
+        out, off = [], 0
+        for rows, start, count in segs:
+            out.append(full[off + start: off + start + count])
+            off += rows
+        assert off == full.shape[0], "segments must cover the whole tensor"
+        return torch.cat(out) if len(out) > 1 else out[0].contiguous()
+
+    @staticmethod
+    def _checkpoint(full: torch.Tensor, fmt: str):
+        """Block-fp8 checkpoints are quantised in 128x128 blocks of the whole tensor, whose borders
+        need not fall on shard borders: quantise the whole tensor, then cut the shard from its exact
+        dequantisation (what a loader of such a checkpoint does before requantising to MXFP8)."""
+        if fmt == "block_fp8":
+            q, s = block_fp8_quantize_device(full)
+            return block_fp8_dequant_device(q, s), "mxfp8"
+        return full, fmt
+
+    def rows(self, segs, K: int, fmt: str, std: float | None = None):
+        """A row-parallel shard (column-parallel linear: output features split) in format `fmt`."""
+        full, f2 = self._checkpoint(self.full(sum(s[0] for s in segs), K, std=std), fmt)
+        return from_float(self.take_rows(full, segs), f2, global_from=full)
+
+    def cols(self, N: int, K: int, start: int, count: int, fmt: str, std: float | None = None):
+        """A column shard (row-parallel linear: input features split) in format `fmt`."""
+        full, f2 = self._checkpoint(self.full(N, K, std=std), fmt)
+        return from_float(full[:, start:start + count].contiguous(), f2, global_from=full)
+
+    def raw_rows(self, segs, *rest, std: float | None = None, dtype=torch.float32) -> torch.Tensor:
+        full = self.full(sum(s[0] for s in segs), *rest, std=std)
+        return self.take_rows(full, segs).to(dtype)
+
+
+def from_float(w: torch.Tensor, fmt: str, tiled: bool | None = None, global_from: torch.Tensor | None = None):
     """Quantise into `fmt`, then apply the load-time transforms (format conversion, and the
-    contiguous-unit tiling of MX weights that makes every TMA box one contiguous HBM read)."""
+    contiguous-unit tiling of MX weights that makes every TMA box one contiguous HBM read).
+    ``global_from``: the whole tensor a shard was cut from; NVFP4's per-tensor global scale is taken
+    from it, as a checkpoint stores one global scale per (unsharded) tensor."""
     if tiled is None:
         tiled = knobs.get("R9K_WEIGHT_TILED") != "0"
     if fmt == "nvfp4":
-        packed, s16, g = L.nvfp4_quantize(w)
+        gs = F.nvfp4_global_scale(global_from.float()) if global_from is not None else None
+        packed, s16, g = L.nvfp4_quantize(w, global_scale=gs)
         mw = L.mx_from_nvfp4(packed, s16, g, search=True)
         return mw.to_tiled() if tiled else mw
     if fmt == "mxfp4":

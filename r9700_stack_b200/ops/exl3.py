@@ -92,9 +92,12 @@ class Exl3Linear:
 
 
 def random_linear(n_in: int, n_out: int, K: int, device, seed: int = 0, cb: int = E.MCG, experts: int = 0,
-                  scale: float = 0.02) -> Exl3Linear:
+                  scale: float = 0.02, first: int = 0) -> Exl3Linear:
+    """Random trellis weights; with ``experts`` > 0, experts first .. first + experts - 1 of a stack
+    whose expert e is keyed by (seed, e), so any rank's slice of the stack is the same tensors."""
     if experts:
-        parts = [E.random_pack(n_in, n_out, K, seed=seed * 1000 + e, scale=scale) for e in range(experts)]
+        parts = [E.random_pack(n_in, n_out, K, seed=seed * 1000 + e, scale=scale)
+                 for e in range(first, first + experts)]
         tr = torch.stack([p[0] for p in parts]).to(device)
         suh = torch.stack([p[1] for p in parts]).to(device)
         svh = torch.stack([p[2] for p in parts]).to(device)

@@ -1,13 +1,20 @@
 """Symmetric-memory tensor-parallel communicator with the all-reduce fused into its neighbours.
 
-Each rank allocates one device region (CUDA IPC shared with its peers). For decode-sized batches:
+Each rank allocates one device region (CUDA IPC shared with its peers). For decode-sized batches
+(``R9K_AR_MODE``):
 
-* the row-parallel GEMM that ends a sublayer (o_proj, GDN out_proj, FFN down_proj) runs with the
-  push epilogue (``gemm_mx_push``): its bf16 partial tiles are stored straight into every rank's
-  region over NVLink and a per-tile flag is raised;
-* the RMSNorm that follows runs as ``ar_rmsnorm``: it waits for every rank's flags, sums the
-  partials in rank order (bit-identical on every rank), adds the residual and emits the next GEMM's
-  MXFP8 input.
+* ``ll`` (default): the row-parallel GEMM that ends a sublayer (o_proj, GDN out_proj, FFN
+  down_proj) runs with the push epilogue (``gemm_mx_push``, LL form): its bf16 partial tiles go
+  straight into every rank's LL slot over NVLink with the call's epoch inside every 8-byte word;
+  other producers use ``ll_push``. The RMSNorm that follows runs as ``ar_ll_rmsnorm``: it polls its
+  own region until every source's words carry the epoch, sums the partials in rank order
+  (bit-identical on every rank), adds the residual and emits the next GEMM's MXFP8 input. The data
+  is its own ready signal: no fence and no flag round trip (the release/acquire flag handshake costs
+  two system-scope releases, ~5.6 us a round trip on B200 against ~2.5 us relaxed;
+  ``tuning/arbench.py --latency``).
+* ``pull``: the GEMM writes its partial locally; the consumer raises a ready flag and reads the
+  peers' partials over NVLink.
+* ``push``: as ``ll`` but plain bf16 slots with per-tile flags (fence + release store).
 
 No separate all-reduce kernel runs. Batches larger than the slot (prefill) fall back to NCCL.
 Reference counterpart: the one-kernel P2P all-reduce family of r9700_vllm/comm/r9k_ar.py:87-601
@@ -41,7 +48,8 @@ class SymmComm(NcclComm):
         self.timeout_s = timeout_s
         self.slot_elems = max_tokens * hidden
         ops = _native.ops()
-        nbytes = AR_FLAG_BYTES + 2 * self.world_size * self.slot_elems * 2
+        # flag page, plain slots (pull / push), LL slots (two bf16 + an epoch per 8 bytes)
+        nbytes = AR_FLAG_BYTES + 2 * self.world_size * self.slot_elems * 2 + 2 * self.world_size * self.slot_elems * 4
         self.local_ptr = int(ops.symm_alloc(nbytes))
         handle = ops.symm_ipc_handle(self.local_ptr).numpy().tobytes()
         handles = [None] * self.world_size
@@ -92,13 +100,13 @@ class SymmComm(NcclComm):
     def gemm_push(self, act, w, call: int) -> None:
         _native.ops().gemm_mx_push(w.q, w.sf, w.fp4, act.q, act.sf, w.N, self.peers, self.rank, self.world_size,
                                    self.slot_elems, call, self.step, self.calls_per_step,
-                                   _status.status(self.device), _gemm_ws(self.device))
+                                   _status.status(self.device), _gemm_ws(self.device), 1 if self.mode == "ll" else 0)
 
     @property
     def mode(self) -> str:
         from .. import knobs
 
-        return knobs.get("R9K_AR_MODE") or "pull"
+        return knobs.get("R9K_AR_MODE") or "ll"
 
     def out_buffer(self, call: int, T: int) -> torch.Tensor:
         """Pull mode: where this rank's row-parallel GEMM writes its partial for call `call` (a static
@@ -107,12 +115,13 @@ class SymmComm(NcclComm):
         return _native.ops().symm_view(self.local_ptr, off, T, self.hidden, self.device.index or 0)
 
     def push(self, x: torch.Tensor, call: int) -> None:
-        _native.ops().push_partial(x, self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
-                                   self.calls_per_step)
+        fn = _native.ops().ll_push if self.mode == "ll" else _native.ops().push_partial
+        fn(x, self.peers, self.rank, self.world_size, self.slot_elems, call, self.step, self.calls_per_step)
 
     def ar_rmsnorm(self, call: int, T: int, w: torch.Tensor, eps: float, plus_one: bool, *, residual=None,
                    residual_out=None, y=None, quant_out=None) -> None:
-        fn = _native.ops().ar_pull_rmsnorm if self.mode == "pull" else _native.ops().ar_rmsnorm
+        o = _native.ops()
+        fn = {"pull": o.ar_pull_rmsnorm, "ll": o.ar_ll_rmsnorm}.get(self.mode, o.ar_rmsnorm)
         fn(self.peers, self.rank, self.world_size, self.slot_elems, call, self.step,
                                  self.calls_per_step, T, residual, residual_out, w, float(eps), bool(plus_one), y,
                                  quant_out.q if quant_out is not None else None,

@@ -14,7 +14,7 @@ def _check():
     status.check()
 
 
-@pytest.mark.parametrize("mode", ["push", "pull"])
+@pytest.mark.parametrize("mode", ["push", "pull", "ll"])
 def test_fused_allreduce_norm_matches_unfused(mode, monkeypatch):
     from r9700_stack_b200 import knobs
     from r9700_stack_b200.ops import linear as L
@@ -40,12 +40,12 @@ def test_fused_allreduce_norm_matches_unfused(mode, monkeypatch):
         r2 = resid.clone()
         a2 = L.alloc_act(T, H, "cuda")
         comm.step_begin()
-        if mode == "push":
+        if mode in ("push", "ll"):
             comm.gemm_push(x, w, call=0)
         else:
             L.mx_linear(x, w, out=comm.out_buffer(0, T))
         comm.ar_rmsnorm(0, T, nw, 1e-6, True, residual=r2, residual_out=r2, quant_out=a2)
-        if mode == "push":
+        if mode in ("push", "ll"):
             comm.push(y, call=1)
         else:
             comm.out_buffer(1, T).copy_(y)
@@ -78,3 +78,36 @@ def test_tiny_model_fused_comm_equals_plain():
         if comm is not None:
             comm.close()
     assert outs[0] == outs[1]
+
+
+def test_ll_wait_runs_out_and_reports(monkeypatch):
+    """A consumer whose data never arrives gives up after its limit, records kErrPeerTimeout in the
+    status word and returns; the context stays usable (the next call on the same stream works)."""
+    from r9700_stack_b200 import knobs
+    from r9700_stack_b200.ops import linear as L
+    from r9700_stack_b200.parallel.symm import SymmComm
+    from r9700_stack_b200.utils import status
+
+    monkeypatch.setenv("R9K_AR_MODE", "ll")
+    knobs.refresh()
+    H, T = 1024, 4
+    comm = SymmComm(H, max_tokens=T, calls_per_step=2, device="cuda", timeout_s=0.001)
+    nw = torch.ones(H, dtype=torch.bfloat16, device="cuda")
+    a = L.alloc_act(T, H, "cuda")
+    st = status.status(torch.device("cuda"))
+    comm.step_begin()
+    comm.ar_rmsnorm(0, T, nw, 1e-6, False, quant_out=a)  # nothing was pushed for call 0 of this step
+    torch.cuda.synchronize()
+    word = st.tolist()
+    assert word[0] == 2 and word[1] == 320, word  # kErrPeerTimeout from the LL consumer
+    st.zero_()
+    # the same communicator keeps working: push, then reduce
+    x = torch.randn(T, H, device="cuda").bfloat16()
+    comm.push(x, call=1)
+    y = torch.empty(T, H, dtype=torch.bfloat16, device="cuda")
+    comm.ar_rmsnorm(1, T, nw, 1e-6, False, y=y)
+    _check()
+    ref = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6)
+    torch.testing.assert_close(y.float(), ref, rtol=2e-2, atol=2e-2)
+    comm.close()
+    knobs.refresh()
