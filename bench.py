@@ -227,6 +227,14 @@ def main():
                 prefill_ms.append(e0.elapsed_time(e1))
             assert not llm.has_unfinished()
     prefill_ms_max = max(comm.max_scalar(m, dev) if comm else m for m in prefill_ms) if prefill_ms else None
+    prefill_ledger = None
+    if args.diag and not args.no_prefill_metric:
+        from r9700_stack_b200.utils.trace import step_ledger
+
+        llm.add_request(prompt(), SamplingParams(max_tokens=1))
+        barrier_sync()
+        prefill_ledger = step_ledger(llm, steps=1)
+        barrier_sync()
 
     # ---------------- decode @16 streams ----------------
     total_new = args.warmup + 2 * args.steps + 16
@@ -352,7 +360,8 @@ def main():
         }
         print(json.dumps(res), flush=True)
         if diag is not None:
-            print(json.dumps({"diag": {"decode16_ledger_per_rank": diag}}), flush=True)
+            print(json.dumps({"diag": {"decode16_ledger_per_rank": diag, "prefill8k_ledger_rank0": prefill_ledger}}),
+                  flush=True)
     if comm is not None:
         import torch.distributed as dist
 

@@ -43,7 +43,17 @@ def _cfg(case: str, world: int):
 CASES = ["hybrid", "hybrid_push", "hybrid_pull", "hybrid_bf16", "moe", "moe_hc", "mla"]
 
 
-def _generate(case, world, rank, dev, comm):
+MX_CASES = ("hybrid", "hybrid_push", "hybrid_pull")
+
+
+def _oracle(model, prompt):
+    """fp32 PyTorch restatement of the same model (same weights, same quantisation points)."""
+    from r9700_stack_b200.models.reference import ReferenceState, reference_forward
+
+    return reference_forward(model, prompt, ReferenceState(model))[-1].float().cpu().numpy()
+
+
+def _generate(case, world, rank, dev, comm, oracle=False):
     from r9700_stack_b200.engine.llm import LLM
     from r9700_stack_b200.engine.scheduler import SamplingParams
     from r9700_stack_b200.models.config import EngineConfig, ParallelConfig
@@ -62,6 +72,8 @@ def _generate(case, world, rank, dev, comm):
     # numpy arrays travel through the result queue by value (torch tensors would go as shared-memory
     # handles that die with the worker process)
     res = [(list(s.output), torch.stack(logits[s.seq_id]).numpy()) for s in seqs]
+    if oracle:
+        res = [r + (_oracle(llm.model, p),) for r, p in zip(res, PROMPTS)]
     llm.runner.graphs.clear()
     del llm
     torch.cuda.empty_cache()
@@ -105,7 +117,7 @@ def _worker(rank, world, port, q, cases):
         ref = {}
         for case in cases:
             knobs.refresh()
-            ref[case] = _generate(case, 1, 0, dev, NoComm())
+            ref[case] = _generate(case, 1, 0, dev, NoComm(), oracle=case in MX_CASES)
         q.put((rank, out, ref))
     else:
         q.put((rank, out, None))
@@ -127,8 +139,15 @@ def _compare(case, got, ref):
     direction (cosine, the same bar as the fp32-oracle model tests), not bit for bit; a token may
     differ only where TP=1's top-2 margin is inside the observed logit difference (a near tie)."""
     errs = []
-    bar = 0.995 if "bf16" in case or case == "mla" else 0.99
-    for i, ((toks, lg), (rtoks, rlg)) in enumerate(zip(got, ref)):
+    bar = 0.995 if "bf16" in case or case == "mla" else 0.98
+    for i, ((toks, lg), (rtoks, rlg, *orc)) in enumerate(zip(got, ref)):
+        if orc:
+            # MXFP8 activations re-round differently once a sum is split over ranks, and random-init
+            # weights amplify that layer by layer: TP=N must be as close to the fp32 oracle as TP=1
+            o = orc[0]
+            c1, cn = _cos(rlg[0], o), _cos(lg[0], o)
+            if cn < c1 - 0.01:
+                errs.append(f"{case} seq{i}: cosine to the fp32 oracle {cn:.4f} vs TP1 {c1:.4f}")
         for t in range(min(len(toks), len(rtoks))):
             c = _cos(lg[t], rlg[t])
             if c < bar:
@@ -166,7 +185,7 @@ def test_tp_matches_tp1():
     for p in ps:
         p.join(timeout=120)
     assert len(res) == world, f"only ranks {sorted(res)} reported"
-    tt = lambda d: {k: [(t, torch.from_numpy(l)) for t, l in v] for k, v in d.items()}  # noqa: E731
+    tt = lambda d: {k: [(t, *(torch.from_numpy(x) for x in xs)) for t, *xs in v] for k, v in d.items()}  # noqa: E731
     res = {r: (tt(o), tt(f) if f is not None else None) for r, (o, f) in res.items()}
     out0, ref = res[0]
     errs = []
