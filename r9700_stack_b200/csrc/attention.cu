@@ -199,6 +199,49 @@ __global__ void __launch_bounds__(128) paged_attention_kernel(
   }
 }
 
+// Store new keys and values into the paged e4m3 cache by slot (slot = block * 64 + offset; negative
+// slots are padding and skipped): one warp per (token, kv head), lane l handles elements l, l + 32, ...
+__global__ void kv_cache_write_kernel(const __nv_bfloat16* __restrict__ k, int64_t ldk, const __nv_bfloat16* __restrict__ v,
+                                      int64_t ldv, const int64_t* __restrict__ slots, int T, int Hkv, int D,
+                                      uint8_t* __restrict__ kc, uint8_t* __restrict__ vc, float k_inv, float v_inv) {
+  pdl_wait();
+  pdl_trigger();
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (gw >= (int64_t)T * Hkv) return;
+  const int t = (int)(gw / Hkv), h = (int)(gw % Hkv);
+  const int64_t slot = slots[t];
+  if (slot < 0) return;
+  const int64_t blk = slot / KV_BLOCK, off = slot % KV_BLOCK;
+  const int64_t dst = ((blk * Hkv + h) * KV_BLOCK + off) * D;
+  const __nv_bfloat16* kr = k + (int64_t)t * ldk + (int64_t)h * D;
+  const __nv_bfloat16* vr = v + (int64_t)t * ldv + (int64_t)h * D;
+  for (int i = lane; i < D; i += 32) {
+    kc[dst + i] = (uint8_t)__nv_cvt_float_to_fp8(__bfloat162float(kr[i]) * k_inv, __NV_SATFINITE, __NV_E4M3);
+    vc[dst + i] = (uint8_t)__nv_cvt_float_to_fp8(__bfloat162float(vr[i]) * v_inv, __NV_SATFINITE, __NV_E4M3);
+  }
+}
+
+void kv_cache_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::Tensor k_cache,
+                    torch::Tensor v_cache, double k_scale, double v_scale) {
+  const int64_t T = k.size(0), Hkv = k.size(1), D = k.size(2);
+  TORCH_CHECK(k.dtype() == torch::kBFloat16 && v.dtype() == torch::kBFloat16 && k.stride(2) == 1 && v.stride(2) == 1 &&
+                  k.stride(1) == D && v.stride(1) == D, "kv_cache_write: bf16 [T, Hkv, D] with contiguous heads");
+  TORCH_CHECK(slots.dtype() == torch::kInt64 && slots.numel() >= T, "kv_cache_write: int64 slot per token");
+  TORCH_CHECK(k_cache.dim() == 4 && k_cache.size(1) == Hkv && k_cache.size(2) == KV_BLOCK && k_cache.size(3) == D &&
+                  k_cache.is_contiguous() && v_cache.is_contiguous() && k_cache.dtype() == torch::kUInt8,
+              "kv_cache_write: caches uint8 [blocks, Hkv, 64, D]");
+  if (T == 0) return;
+  const at::cuda::CUDAGuard guard(k.device());
+  const int64_t warps = T * Hkv;
+  launch_pdl(kv_cache_write_kernel, dim3((unsigned)((warps * 32 + 255) / 256)), dim3(256), 0,
+             at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(k.data_ptr()), k.stride(0),
+             reinterpret_cast<const __nv_bfloat16*>(v.data_ptr()), v.stride(0), slots.data_ptr<int64_t>(), (int)T,
+             (int)Hkv, (int)D, k_cache.data_ptr<uint8_t>(), v_cache.data_ptr<uint8_t>(), (float)(1.0 / k_scale),
+             (float)(1.0 / v_scale));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                      torch::Tensor tok_seq, torch::Tensor tok_ctx, double sm_scale, double k_scale, double v_scale,
                      c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,

@@ -78,6 +78,8 @@ void qk_norm_rope_cache(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t q_of
                         torch::Tensor qw, torch::Tensor kw, double eps, bool plus_one, torch::Tensor positions,
                         torch::Tensor cos_sin, int64_t rot, torch::Tensor slots, torch::Tensor q_out,
                         torch::Tensor k_cache, torch::Tensor v_cache, double k_scale, double v_scale);
+void kv_cache_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::Tensor k_cache,
+                    torch::Tensor v_cache, double k_scale, double v_scale);
 void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
                      torch::Tensor tok_seq, torch::Tensor tok_ctx, double sm_scale, double k_scale, double v_scale,
                      c10::optional<torch::Tensor> gate, c10::optional<torch::Tensor> out,
@@ -216,6 +218,8 @@ TORCH_LIBRARY(r9k, m) {
   m.def("qk_norm_rope_cache(Tensor qkv, int Hq, int Hkv, int q_off, int k_off, int v_off, Tensor qw, Tensor kw, "
         "float eps, bool plus_one, Tensor positions, Tensor cos_sin, int rot, Tensor slots, Tensor(a!) q_out, "
         "Tensor(b!) k_cache, Tensor(c!) v_cache, float k_scale, float v_scale) -> ()");
+  m.def("kv_cache_write(Tensor k, Tensor v, Tensor slots, Tensor(a!) k_cache, Tensor(b!) v_cache, float k_scale, "
+        "float v_scale) -> ()");
   m.def("paged_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_seq, "
         "Tensor tok_ctx, float sm_scale, float k_scale, float v_scale, Tensor? gate, Tensor(a!)? out, "
         "Tensor(b!)? out_q, Tensor(c!)? out_sf, int window) -> ()");
@@ -309,6 +313,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("dequant_mx", &r9k::dequant_mx);
   m.impl("qk_norm_rope_cache", &r9k::qk_norm_rope_cache);
   m.impl("paged_attention", &r9k::paged_attention);
+  m.impl("kv_cache_write", &r9k::kv_cache_write);
   m.impl("attn_tc_decode", &r9k::attn_tc_decode);
   m.impl("attn_tc_prefill", &r9k::attn_tc_prefill);
   m.impl("gdn_conv_prep", &r9k::gdn_conv_prep);

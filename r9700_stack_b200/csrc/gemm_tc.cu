@@ -560,37 +560,6 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
   return p;
 }
 
-// Clusters of S CTAs (1 x S x 1, 192 threads) of a kernel that can be resident at once on this
-// device (cudaOccupancyMaxActiveClusters), cached per (kernel, S, device).
-static int max_active_clusters(const void* kern, int S, int smem) {
-  static std::mutex mu;
-  static std::map<std::tuple<const void*, int, int>, int> cache;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  std::lock_guard<std::mutex> lk(mu);
-  const auto key = std::make_tuple(kern, S, dev);
-  auto it = cache.find(key);
-  if (it != cache.end()) return it->second;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(1, (unsigned)S, 1);
-  cfg.blockDim = dim3(192, 1, 1);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 1;
-  attr[0].val.clusterDim.y = (unsigned)S;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  int n = 0;
-  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
-    cudaGetLastError();
-    n = 0;
-  }
-  cache[key] = n;
-  return n;
-}
-
 // workspace layout: [65536 int counters][partials]
 static constexpr int64_t kWsCounters = 65536;
 
@@ -613,10 +582,11 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
       part = ws->data_ptr<float>() + kWsCounters;
     }
   }
-  // split-K partials meet in distributed shared memory when the splits of a tile form a cluster, and
-  // every cluster of the grid can be resident at once (else the global fix-up keeps one wave)
-  bool cluster = p.S > 1 && p.S <= 8 && EPI != EPI_PUSH && MT == 1 && gemm_cluster_enabled();
-  if (cluster) cluster = grid_x * p.n_tiles <= max_active_clusters((const void*)kern, p.S, C::SMEM_BYTES);
+  // split-K partials meet in distributed shared memory when the splits of a tile form a cluster of 2,
+  // 4 or 8 CTAs (measured: 7-CTA clusters of the 5120 x 17408 decode GEMM pack into fewer resident
+  // clusters per GPC and take two waves, 27.6 vs 14.8 us; power-of-two clusters run faster than the
+  // global fix-up, e.g. 2176 x 5120 gate/up 16.6 -> 12.3 us)
+  const bool cluster = (p.S == 2 || p.S == 4 || p.S == 8) && EPI != EPI_PUSH && MT == 1 && gemm_cluster_enabled();
   if (cluster) {
     part = nullptr;
     cnt = nullptr;
