@@ -216,17 +216,33 @@ class HybridMoELM(HybridLM):
         ws.ple_h[:T].copy_(h)
         L.bf16_linear(ws.ple_h[:T], lay["ple_out"], out=out, residual=out, alpha=1.0 / self.par.tp_size)
 
-    def enable_expert_cache(self, slots: int) -> None:
-        """Move every layer's experts to pinned host memory behind a device LRU of `slots` experts."""
-        from ..ops.expert_cache import ExpertCache
+    def enable_expert_cache(self, slots: int, profile: str | None = None) -> None:
+        """Move every layer's experts to pinned host memory behind a device LRU of `slots` experts.
+        ``profile``: a routing profile (safetensors, ``RoutingProfile.save``) whose most routed experts
+        of each layer are preloaded (warm start)."""
+        from ..ops.expert_cache import ExpertCache, RoutingProfile
 
         assert self.placement is None, "the expert cache holds contiguous expert ranges"
+        prof = RoutingProfile.load(profile) if profile else None
+        e0 = self.par.tp_rank * self.e_local
         self.caches = []
-        for lay in self.layers:
+        for i, lay in enumerate(self.layers):
             cache = ExpertCache(lay["e_gate"], lay["e_up"], lay["e_down"], self.e_local, slots, self.device)
             del lay["e_gate"], lay["e_up"], lay["e_down"]
+            if prof is not None:
+                cache.warm_ids = prof.top(i, slots, e0, self.e_local)
+                cache.warm(cache.warm_ids)
             self.caches.append(cache)
         torch.cuda.empty_cache()
+
+    def record_routing(self, enable: bool = True) -> None:
+        """Start (or stop) recording every layer's routed experts into ``self.routing_profile``."""
+        from ..ops.expert_cache import RoutingProfile
+
+        if enable:
+            self.routing_profile = RoutingProfile(len(self.layers), self.cfg.moe_experts, self.device)
+        else:
+            self.routing_profile = None
 
     def _ffn_block(self, i, lay, meta, ws: MoEWorkspace, T: int, call: int, fused: bool) -> None:
         c = self.cfg
@@ -253,14 +269,17 @@ class HybridMoELM(HybridLM):
                 # wider batches (prefill): stream the experts through the slots in groups of S
                 if not hasattr(ws, "moe_pass"):
                     ws.moe_pass = torch.zeros_like(ws.norm_out)
-                for p, g0 in enumerate(range(0, self.e_local, cache.S)):
-                    n = cache.load_range(g0)
+                for p, grp in enumerate(cache.stream_groups()):
+                    n = cache.warm(grp)
                     dst = out if p == 0 else ws.moe_pass[:T]
-                    moe_ffn(lay_c, ws.norm_out[:T], ws.moe, dst, k=c.moe_topk, e0=e0 + g0, E_local=n,
+                    moe_ffn(lay_c, ws.norm_out[:T], ws.moe, dst, k=c.moe_topk, e0=0, E_local=n,
                             moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local if p == 0 else 0,
-                            route_mode=mode, route=p == 0, gemm_E=cache.S)
+                            route_mode=mode, route=p == 0, gemm_E=cache.S,
+                            remap=lambda ids: cache.slots_for(ids, e0, ws.slot_ids[:T]))
                     if p > 0:
                         out.add_(dst)
+        if getattr(self, "routing_profile", None) is not None:
+            self.routing_profile.record(i, ws.moe.ids[:T])
         if self.ple is not None:
             self._ple(i, lay, ws, T, out)
         self._after_partial(ws, T, call, fused)

@@ -69,3 +69,34 @@ def test_moe_model_with_cache_matches_resident():
             st = m.caches[0].stats()
             assert st["misses"] > 0 and st["hits"] > 0
     assert outs[0] == outs[1]
+
+
+def test_routing_profile_warm_start(tmp_path):
+    """A routing profile recorded while serving preloads each layer's most routed experts: the warm
+    cache misses less on the same traffic and the tokens stay those of resident experts."""
+    from r9700_stack_b200.engine.llm import LLM, build_model
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.config import EngineConfig, ParallelConfig, tiny_moe
+    from r9700_stack_b200.ops.expert_cache import RoutingProfile
+
+    cfg = tiny_moe()
+    prompts = [[5, 6, 7, 8, 9, 10], [40, 41, 42]]
+    ec = EngineConfig(max_batch=2, max_model_len=128, max_prefill_tokens=64, cuda_graphs=False)
+    m = build_model(cfg, ParallelConfig(), torch.device("cuda"), seed=9)
+    m.record_routing(True)
+    want = LLM(cfg, ec, seed=9, model=m).generate(prompts, SamplingParams(max_tokens=8))
+    path = str(tmp_path / "expertprofile.safetensors")
+    m.routing_profile.save(path)
+    prof = RoutingProfile.load(path)
+    assert int(prof.counts.sum()) == int(m.routing_profile.counts.sum().cpu()) > 0
+    misses = {}
+    for warm in (False, True):
+        mm = build_model(cfg, ParallelConfig(), torch.device("cuda"), seed=9)
+        mm.enable_expert_cache(slots=6, profile=path if warm else None)
+        if warm:
+            top = prof.top(0, 6)
+            assert sorted(int(e) for e in mm.caches[0].expert_of.tolist()) == sorted(top)
+        got = LLM(cfg, ec, seed=9, model=mm).generate(prompts, SamplingParams(max_tokens=8))
+        assert got == want
+        misses[warm] = sum(c.stats()["misses"] for c in mm.caches)
+    assert misses[True] < misses[False], misses
