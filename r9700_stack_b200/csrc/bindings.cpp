@@ -78,6 +78,14 @@ void qk_norm_rope_cache(torch::Tensor qkv, int64_t Hq, int64_t Hkv, int64_t q_of
                         torch::Tensor qw, torch::Tensor kw, double eps, bool plus_one, torch::Tensor positions,
                         torch::Tensor cos_sin, int64_t rot, torch::Tensor slots, torch::Tensor q_out,
                         torch::Tensor k_cache, torch::Tensor v_cache, double k_scale, double v_scale);
+void nvls_all_reduce(c10::optional<torch::Tensor> x, torch::Tensor out, int64_t mc, int64_t local, int64_t cap_bytes,
+                     torch::Tensor sig_ptrs, int64_t sig_slots, int64_t rank, int64_t world, torch::Tensor seq,
+                     torch::Tensor status, double timeout_s);
+void nvls_all_gather(torch::Tensor x, torch::Tensor out, int64_t mc, int64_t local, int64_t cap_bytes,
+                     torch::Tensor sig_ptrs, int64_t sig_slots, int64_t rank, int64_t world, torch::Tensor seq,
+                     torch::Tensor status, double timeout_s);
+void gemm_nvf4(torch::Tensor wq, torch::Tensor ws, double alpha, c10::optional<torch::Tensor> wq2,
+               c10::optional<torch::Tensor> ws2, double alpha2, torch::Tensor x, torch::Tensor out, torch::Tensor status);
 void kv_cache_write(torch::Tensor k, torch::Tensor v, torch::Tensor slots, torch::Tensor k_cache,
                     torch::Tensor v_cache, double k_scale, double v_scale);
 void paged_attention(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cache, torch::Tensor block_table,
@@ -218,6 +226,12 @@ TORCH_LIBRARY(r9k, m) {
   m.def("qk_norm_rope_cache(Tensor qkv, int Hq, int Hkv, int q_off, int k_off, int v_off, Tensor qw, Tensor kw, "
         "float eps, bool plus_one, Tensor positions, Tensor cos_sin, int rot, Tensor slots, Tensor(a!) q_out, "
         "Tensor(b!) k_cache, Tensor(c!) v_cache, float k_scale, float v_scale) -> ()");
+  m.def("nvls_all_reduce(Tensor? x, Tensor(a!) out, int mc, int local, int cap_bytes, Tensor sig_ptrs, "
+        "int sig_slots, int rank, int world, Tensor(b!) seq, Tensor(c!) status, float timeout_s) -> ()");
+  m.def("nvls_all_gather(Tensor x, Tensor(a!) out, int mc, int local, int cap_bytes, Tensor sig_ptrs, "
+        "int sig_slots, int rank, int world, Tensor(b!) seq, Tensor(c!) status, float timeout_s) -> ()");
+  m.def("gemm_nvf4(Tensor wq, Tensor ws, float alpha, Tensor? wq2, Tensor? ws2, float alpha2, Tensor x, "
+        "Tensor(a!) out, Tensor(b!) status) -> ()");
   m.def("kv_cache_write(Tensor k, Tensor v, Tensor slots, Tensor(a!) k_cache, Tensor(b!) v_cache, float k_scale, "
         "float v_scale) -> ()");
   m.def("paged_attention(Tensor q, Tensor k_cache, Tensor v_cache, Tensor block_table, Tensor tok_seq, "
@@ -314,6 +328,9 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("qk_norm_rope_cache", &r9k::qk_norm_rope_cache);
   m.impl("paged_attention", &r9k::paged_attention);
   m.impl("kv_cache_write", &r9k::kv_cache_write);
+  m.impl("nvls_all_reduce", &r9k::nvls_all_reduce);
+  m.impl("nvls_all_gather", &r9k::nvls_all_gather);
+  m.impl("gemm_nvf4", &r9k::gemm_nvf4);
   m.impl("attn_tc_decode", &r9k::attn_tc_decode);
   m.impl("attn_tc_prefill", &r9k::attn_tc_prefill);
   m.impl("gdn_conv_prep", &r9k::gdn_conv_prep);

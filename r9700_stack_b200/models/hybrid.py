@@ -220,7 +220,8 @@ class HybridLM:
             self.hc_final = HCo.random_point(wf, c.hc_streams, H)
         vl = self.vocab_local
         self.lm_head = tpf.rows([(c.vocab, r * vl, vl)], H, c.lm_head_format)
-        self.mx = not isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.BF16Weight)
+        # MX weights take MXFP8 activations; bf16 and native NVFP4 weights take bf16 activations
+        self.mx = isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.MXWeight)
 
     def _rope_cache(self, max_pos: int):
         c = self.cfg
@@ -302,6 +303,8 @@ class HybridLM:
     def _linear(self, act: L.MXAct, xb: torch.Tensor, w, out: torch.Tensor):
         if isinstance(w, L.MXWeight):
             L.mx_linear(act, w, out=out)
+        elif isinstance(w, L.NVF4Weight):
+            L.nvf4_linear(xb, w, out=out)
         else:
             L.bf16_linear(xb, w, out=out)
 
@@ -461,7 +464,10 @@ class HybridLM:
         if self.mx:
             L.mx_swiglu(ws.act.narrow(T), lay["w_gate"], lay["w_up"], out=ws.ffn_act.narrow(T))
             return ws.ffn_act.narrow(T), None, lay["w_down"]
-        L.bf16_swiglu(ws.norm_out[:T], lay["w_gate"], lay["w_up"], out=ws.ffn_bf16[:T])
+        if isinstance(lay["w_gate"], L.NVF4Weight):
+            L.nvf4_swiglu(ws.norm_out[:T], lay["w_gate"], lay["w_up"], out=ws.ffn_bf16[:T])
+        else:
+            L.bf16_swiglu(ws.norm_out[:T], lay["w_gate"], lay["w_up"], out=ws.ffn_bf16[:T])
         return None, ws.ffn_bf16[:T], lay["w_down"]
 
     def _ffn_block(self, i: int, lay, meta, ws: Workspace, T: int, call: int, fused: bool) -> None:

@@ -33,7 +33,7 @@ def bf16(x: torch.Tensor) -> torch.Tensor:
 
 
 def _w(w) -> torch.Tensor:
-    if isinstance(w, L.MXWeight):
+    if isinstance(w, (L.MXWeight, L.NVF4Weight)):
         return w.dequant()
     if isinstance(w, L.BF16Weight):
         return w.w.float()

@@ -101,11 +101,14 @@ def from_float(w: torch.Tensor, fmt: str, tiled: bool | None = None, global_from
     contiguous-unit tiling of MX weights that makes every TMA box one contiguous HBM read).
     ``global_from``: the whole tensor a shard was cut from; NVFP4's per-tensor global scale is taken
     from it, as a checkpoint stores one global scale per (unsharded) tensor."""
+    tiled_forced = tiled is True  # grouped expert stacks need the MX tiled layout
     if tiled is None:
         tiled = knobs.get("R9K_WEIGHT_TILED") != "0"
     if fmt == "nvfp4":
         gs = F.nvfp4_global_scale(global_from.float()) if global_from is not None else None
         packed, s16, g = L.nvfp4_quantize(w, global_scale=gs)
+        if knobs.get("R9K_NVFP4") == "native" and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and not tiled_forced:
+            return L.NVF4Weight.from_checkpoint(packed, s16, g)
         mw = L.mx_from_nvfp4(packed, s16, g, search=True)
         return mw.to_tiled() if tiled else mw
     if fmt == "mxfp4":
@@ -140,7 +143,7 @@ def block_fp8_dequant_device(q: torch.Tensor, s: torch.Tensor, block: int = 128)
 
 
 def weight_nbytes(w) -> int:
-    if isinstance(w, L.MXWeight):
+    if isinstance(w, (L.MXWeight, L.NVF4Weight)):
         return w.nbytes
     if isinstance(w, L.BF16Weight):
         return w.w.numel() * 2

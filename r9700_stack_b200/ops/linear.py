@@ -121,6 +121,42 @@ class BF16Weight:
 
 
 @dataclass
+class NVF4Weight:
+    """NVFP4 weight served without conversion (``R9K_NVFP4=native``): the checkpoint's e2m1 codes and
+    e4m3 block-16 scales, re-laid out into [N/128][K/64] units of 128 rows x 64 elements (4 KiB of
+    codes ``q``, 512 B of scales ``s``), and alpha = 1 / global scale. ``gemm_nvf4`` expands units to
+    bf16 on chip (exact) and multiplies bf16 activations."""
+
+    q: torch.Tensor  # uint8 [N/128 * K/64, 128, 32]
+    s: torch.Tensor  # uint8 [N/128 * K/64, 128, 4]
+    alpha: float
+    N: int
+    K: int
+
+    @property
+    def nbytes(self) -> int:
+        return self.q.numel() + self.s.numel()
+
+    @staticmethod
+    def from_checkpoint(packed: torch.Tensor, s16: torch.Tensor, g: float) -> "NVF4Weight":
+        """packed [N, K/2] (low nibble = even element), s16 [N, K/16] e4m3 bytes, global scale g."""
+        N, K = packed.shape[0], packed.shape[1] * 2
+        assert N % 128 == 0 and K % 64 == 0, "native NVFP4 needs N % 128 == 0 and K % 64 == 0"
+        q = packed.contiguous().view(N // 128, 128, K // 64, 32).permute(0, 2, 1, 3).reshape(-1, 128, 32).contiguous()
+        s = s16.contiguous().view(torch.uint8).view(N // 128, 128, K // 64, 4).permute(0, 2, 1, 3)
+        return NVF4Weight(q, s.reshape(-1, 128, 4).contiguous(), 1.0 / float(g), N, K)
+
+    def dequant(self) -> torch.Tensor:
+        """fp32 [N, K] (the exact checkpoint values)."""
+        from ..quant import formats as F
+
+        N, K = self.N, self.K
+        packed = self.q.view(N // 128, K // 64, 128, 32).permute(0, 2, 1, 3).reshape(N, K // 2)
+        s16 = self.s.view(N // 128, K // 64, 128, 4).permute(0, 2, 1, 3).reshape(N, K // 16)
+        return F.dequant_nvfp4(packed.cpu(), s16.cpu(), 1.0 / self.alpha).to(self.q.device)
+
+
+@dataclass
 class MXAct:
     q: torch.Tensor  # uint8 [M, K] e4m3
     sf: torch.Tensor  # uint8 chunk layout (rows padded to 128)
@@ -263,6 +299,22 @@ def bf16_swiglu(x: torch.Tensor, w_gate: BF16Weight, w_up: BF16Weight, out: torc
     if out is None:
         out = torch.empty(x.shape[0], w_gate.N, dtype=torch.bfloat16, device=x.device)
     _ops().gemm_bf16_swiglu(w_gate.w, w_up.w, x, out, _status.status(x.device), gemm_workspace(x.device))
+    return out
+
+
+def nvf4_linear(x: torch.Tensor, w: NVF4Weight, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out = x @ W^T for bf16 x and a native NVFP4 weight."""
+    if out is None:
+        out = torch.empty(x.shape[0], w.N, dtype=torch.bfloat16, device=x.device)
+    _ops().gemm_nvf4(w.q, w.s, w.alpha, None, None, 1.0, x, out, _status.status(x.device))
+    return out
+
+
+def nvf4_swiglu(x: torch.Tensor, w_gate: NVF4Weight, w_up: NVF4Weight, out: torch.Tensor | None = None):
+    """silu(x W_gate^T) * (x W_up^T) in one kernel (native NVFP4 weights, bf16 in and out)."""
+    if out is None:
+        out = torch.empty(x.shape[0], w_gate.N, dtype=torch.bfloat16, device=x.device)
+    _ops().gemm_nvf4(w_gate.q, w_gate.s, w_gate.alpha, w_up.q, w_up.s, w_up.alpha, x, out, _status.status(x.device))
     return out
 
 

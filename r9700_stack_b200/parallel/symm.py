@@ -16,7 +16,10 @@ Each rank allocates one device region (CUDA IPC shared with its peers). For deco
   peers' partials over NVLink.
 * ``push``: as ``ll`` but plain bf16 slots with per-tile flags (fence + release store).
 
-No separate all-reduce kernel runs. Batches larger than the slot (prefill) fall back to NCCL.
+No separate all-reduce kernel runs for decode. Batches larger than the slot (prefill) go through the
+NVLS two-shot all-reduce (``parallel.nvls``: the switch reduces, every element once, same bits on
+every rank; ``R9K_PREFILL_AR``), and the logits all-gather through the NVLS all-gather
+(``R9K_LOGITS_AG``); NCCL takes them where the platform has no multicast object.
 Reference counterpart: the one-kernel P2P all-reduce family of r9700_vllm/comm/r9k_ar.py:87-601
 (PCIe pair/quartet/host stages); on NVSwitch every peer is one hop, so there is no hierarchy.
 """
@@ -72,6 +75,21 @@ class SymmComm(NcclComm):
         # lossy compressed all-reduce for prefill-sized messages (opt-in: R9K_AR_QUANT_BITS=4|6)
         from .. import knobs
 
+        # NVLS (multicast) collectives for prefill all-reduces and the logits all-gather
+        self.nvls = None
+        if self.world_size > 1 and (knobs.get("R9K_PREFILL_AR") == "symm" or knobs.get("R9K_LOGITS_AG") == "symm"):
+            from .nvls import NvlsComm
+
+            try:
+                cap = max(max_prefill_tokens * hidden * 2, 64 << 20)
+                nv = NvlsComm(self.device, group=group, capacity_bytes=(cap + (1 << 20) - 1) // (1 << 20) * (1 << 20),
+                              timeout_s=timeout_s)
+                self.nvls = nv if nv.available else None
+            except Exception as e:  # noqa: BLE001 - no multicast support: NCCL keeps these collectives
+                import logging
+
+                logging.getLogger("vllm.r9700_stack_b200").info("NVLS unavailable (%s); NCCL for prefill", e)
+        self._ag_out: dict = {}
         self.wht_bits = knobs.get_int("R9K_AR_QUANT_BITS") if self.world_size > 1 else 0
         self.wht_min_bytes = knobs.get_int("R9K_AR_QUANT_MIN_KB") * 1024
         self.wht = None
@@ -84,12 +102,40 @@ class SymmComm(NcclComm):
 
     # -------------------------------------------------------------------------------------------
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
-        """Unfused all-reduce (prefill): the compressed kernel for large messages when enabled, else NCCL."""
+        """Unfused all-reduce (prefill): the lossy compressed kernel when enabled, the NVLS two-shot
+        kernel when the platform has multicast, else NCCL."""
+        from .. import knobs
+
         if (self.wht is not None and t.numel() * t.element_size() >= self.wht_min_bytes
                 and self.wht.wht_ok(t, self.wht_bits)):
             t.copy_(self.wht.all_reduce_wht(t, self.wht_bits))
             return t
+        if self.nvls is not None and knobs.get("R9K_PREFILL_AR") == "symm" and self.nvls.fits_all_reduce(t):
+            from ..utils.trace import note_all_reduce
+
+            note_all_reduce(t.numel() * t.element_size())
+            return self.nvls.all_reduce_(t)
         return super().all_reduce_(t)
+
+    def all_gather_lastdim(self, t: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        """[R, n] per rank -> [R, world * n]: the NVLS all-gather for fp32 logits, else NCCL."""
+        from .. import knobs
+
+        if (self.nvls is not None and knobs.get("R9K_LOGITS_AG") == "symm" and t.dim() == 2
+                and t.is_contiguous() and self.nvls.fits_all_gather(t)):
+            R, n = t.shape
+            key = (R, n, t.dtype)
+            buf = self._ag_out.get(key)
+            if buf is None:
+                buf = torch.empty(self.world_size, R, n, dtype=t.dtype, device=t.device)
+                self._ag_out[key] = buf
+            self.nvls.all_gather(t, buf)
+            res = buf.permute(1, 0, 2).reshape(R, self.world_size * n)
+            if out is not None:
+                out.copy_(res)
+                return out
+            return res
+        return super().all_gather_lastdim(t, out)
 
     def can_fuse(self, T: int) -> bool:
         return 0 < T <= self.max_tokens
@@ -130,6 +176,7 @@ class SymmComm(NcclComm):
 
     def close(self) -> None:
         ops = _native.ops()
+        self.nvls = None
         if self.wht is not None:
             self.wht.close()
             self.wht = None
