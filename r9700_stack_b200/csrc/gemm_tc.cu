@@ -65,9 +65,13 @@ struct GemmCfg {
   static constexpr int NACC = MT == 1 ? NACC1 : (NACC1 >= 2 ? 2 : 1);
   static constexpr int ACC_TILE = BN * NA * NACC;  // TMEM columns of one row tile's accumulators
   static constexpr int ACC_COLS = ACC_TILE * MT;
+  // scale factors: one TMEM set per load stage, so the tcgen05.cp of chunk q + 1 writes other columns
+  // than the ones chunk q's MMAs still read and the two overlap in the tensor pipe
+  static constexpr int SF_SETS = (KIND == KIND_MX) ? NP : 1;
+  static constexpr int SF_STRIDE = 4 * NA + 4 * NB_SF;
   static constexpr int SFA_COL = ACC_COLS;
   static constexpr int SFB_COL = SFA_COL + 4 * NA;
-  static constexpr int USED_COLS = (KIND == KIND_MX) ? SFB_COL + 4 * NB_SF : ACC_COLS;
+  static constexpr int USED_COLS = (KIND == KIND_MX) ? ACC_COLS + SF_SETS * SF_STRIDE : ACC_COLS;
   static constexpr int TMEM_COLS = USED_COLS <= 32 ? 32 : USED_COLS <= 64 ? 64 : USED_COLS <= 128 ? 128
                                    : USED_COLS <= 256 ? 256 : 512;
   static constexpr int TILE_F = NA * BN * 128;  // floats of one split-K partial tile
@@ -237,13 +241,15 @@ __global__ void __launch_bounds__(192, 1)
         const uint32_t sa = UNPACK ? smem_u32(smem + C::OFF_C + sc * C::NA * C::A_BYTES)
                                    : smem_u32(smem + C::OFF_A + s * C::NA * C::AL_BYTES);
         const uint32_t sb = smem_u32(smem + C::OFF_B + s * C::B_BYTES);
+        const uint32_t sfo = (uint32_t)((q % C::SF_SETS) * C::SF_STRIDE);  // this stage's scale-factor set
         if constexpr (KIND == KIND_MX) {
           const uint32_t ssfa = smem_u32(smem + C::OFF_SFA + s * C::NA * 512);
           const uint32_t ssfb = smem_u32(smem + C::OFF_SFB + s * C::SFB_BYTES);
-          tc_cp_32x128b_warpx4(tbase + C::SFA_COL, sdesc_sf(ssfa));
-          if (DUAL) tc_cp_32x128b_warpx4(tbase + C::SFA_COL + 4, sdesc_sf(ssfa + 512));
+          tc_cp_32x128b_warpx4(tbase + C::SFA_COL + sfo, sdesc_sf(ssfa));
+          if (DUAL) tc_cp_32x128b_warpx4(tbase + C::SFA_COL + sfo + 4, sdesc_sf(ssfa + 512));
 #pragma unroll
-          for (int c = 0; c < C::NB_SF; ++c) tc_cp_32x128b_warpx4(tbase + C::SFB_COL + 4 * c, sdesc_sf(ssfb + 512 * c));
+          for (int c = 0; c < C::NB_SF; ++c)
+            tc_cp_32x128b_warpx4(tbase + C::SFB_COL + sfo + 4 * c, sdesc_sf(ssfb + 512 * c));
         }
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -253,12 +259,12 @@ __global__ void __launch_bounds__(192, 1)
           const uint32_t acc = (i > 0 || k >= C::NACC) ? 1u : 0u;
           if constexpr (KIND == KIND_MX) {
             const uint32_t idesc = idesc_block_scaled(args.a_fmt, kFmtE4M3, 128, BN, (uint32_t)k, (uint32_t)k);
-            const uint32_t sfb_addr = (tbase + C::SFB_COL) | ((uint32_t)k << 30);
+            const uint32_t sfb_addr = (tbase + C::SFB_COL + sfo) | ((uint32_t)k << 30);
             mma_mxf8f6f4_ss(dacc, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc,
-                            (tbase + C::SFA_COL) | ((uint32_t)k << 30), sfb_addr);
+                            (tbase + C::SFA_COL + sfo) | ((uint32_t)k << 30), sfb_addr);
             if (DUAL)
               mma_mxf8f6f4_ss(dacc + BN, sdesc_k_sw128(sa + C::A_BYTES + 32 * k), bd, idesc, acc,
-                              (tbase + C::SFA_COL + 4) | ((uint32_t)k << 30), sfb_addr);
+                              (tbase + C::SFA_COL + sfo + 4) | ((uint32_t)k << 30), sfb_addr);
           } else {
             constexpr uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, BN);
             mma_f16_ss(dacc, sdesc_k_sw128(sa + 32 * k), bd, idesc, acc);

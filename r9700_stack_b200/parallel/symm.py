@@ -53,22 +53,51 @@ class SymmComm(NcclComm):
         ops = _native.ops()
         # flag page, plain slots (pull / push), LL slots (two bf16 + an epoch per 8 bytes)
         nbytes = AR_FLAG_BYTES + 2 * self.world_size * self.slot_elems * 2 + 2 * self.world_size * self.slot_elems * 4
-        self.local_ptr = int(ops.symm_alloc(nbytes))
-        handle = ops.symm_ipc_handle(self.local_ptr).numpy().tobytes()
+        # set-up is all-or-nothing: a rank that cannot allocate, export or open a region makes every
+        # rank keep NCCL (reference: comm/r9k_ar.py:422-439, the "ok" exchange of every rank)
+        self.local_ptr, self._opened, ok, handle = 0, [], True, b""
+        try:
+            self.local_ptr = int(ops.symm_alloc(nbytes))
+            handle = ops.symm_ipc_handle(self.local_ptr).numpy().tobytes()
+        except Exception as e:  # noqa: BLE001 - reported and agreed on below
+            ok, self.setup_error = False, repr(e)
         handles = [None] * self.world_size
         if self.world_size > 1:
             dist.all_gather_object(handles, handle, group=group)
         else:
             handles = [handle]
         ptrs = []
-        self._opened = []
-        for i, h in enumerate(handles):
-            if i == self.rank:
-                ptrs.append(self.local_ptr)
-            else:
-                p = int(ops.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
-                self._opened.append(p)
-                ptrs.append(p)
+        if ok and all(handles):
+            try:
+                for i, h in enumerate(handles):
+                    if i == self.rank:
+                        ptrs.append(self.local_ptr)
+                    else:
+                        p = int(ops.symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+                        self._opened.append(p)
+                        ptrs.append(p)
+            except Exception as e:  # noqa: BLE001
+                ok, self.setup_error = False, repr(e)
+        else:
+            ok = False
+        if self.world_size > 1:
+            flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+            ok = bool(int(flag))
+        if not ok:
+            import logging
+
+            logging.getLogger("vllm.r9700_stack_b200").warning(
+                "symmetric-memory set-up failed on some rank (%s): every rank keeps NCCL",
+                getattr(self, "setup_error", "a peer"))
+            self.fused = False  # the models then route every all-reduce through NCCL
+            for p_ in self._opened:
+                ops.symm_close(p_)
+            self._opened = []
+            if self.local_ptr:
+                ops.symm_free(self.local_ptr)
+                self.local_ptr = 0
+            ptrs = [0] * self.world_size
         self.peers = torch.tensor(ptrs, dtype=torch.int64)
         self.step = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.barrier()
