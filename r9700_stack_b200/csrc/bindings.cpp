@@ -24,6 +24,7 @@ void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::T
                      c10::optional<torch::Tensor> out_sf, torch::Tensor status);
 void gemm_bf16_swiglu(torch::Tensor wg, torch::Tensor wu, torch::Tensor x, torch::Tensor out, torch::Tensor status,
                       c10::optional<torch::Tensor> workspace);
+void gemm_trace(c10::optional<torch::Tensor> buf);
 // moe.cu
 void moe_route(torch::Tensor logits, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias, int64_t n_group,
                int64_t topk_group, double scale, bool renorm, torch::Tensor ids, torch::Tensor w);
@@ -376,6 +377,8 @@ TORCH_LIBRARY_FRAGMENT(r9k, m) {
   m.def("symm_view(int ptr, int offset_bytes, int rows, int cols, int device) -> Tensor", &r9k::symm_view);
   m.def("p2p_probe(Tensor peers, int rank, int peer_rank, int off, int kind, int mode, int iters, Tensor status, "
         "float timeout_s) -> Tensor", &r9k::p2p_probe);
+  // tuning: per-CTA timestamps of the tiled GEMM into an int64 buffer (None switches them off)
+  m.def("gemm_trace(Tensor? buf) -> ()", &r9k::gemm_trace);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "r9700_stack_b200 sm_100a kernel library"; }

@@ -45,7 +45,12 @@ struct GemmArgs {
   // split-K with the S splits of a tile launched as one thread-block cluster (1, S, 1): the fp32
   // partials meet in distributed shared memory instead of a global workspace (no fix-up kernel tail)
   int cluster_k;
+  // tuning trace (null unless set with gemm_trace): per CTA, %globaltimer at kernel entry, set-up
+  // done, producer past the programmatic wait, first stage landed, last MMA issued, accumulator
+  // complete (epilogue), CTA done
+  unsigned long long* trace;
 };
+enum { kTrEntry = 0, kTrSetup, kTrPdl, kTrFirst, kTrIssued, kTrAcc, kTrDone, kTrN = 8 };
 
 R9K_DEVINL float ld_dsmem_f32(uint32_t addr) {
   float v;

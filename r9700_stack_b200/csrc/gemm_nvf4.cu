@@ -346,8 +346,8 @@ void gemm_nvf4(torch::Tensor wq, torch::Tensor ws, double alpha, c10::optional<t
   const int64_t M = x.size(0), K = x.size(1), N = out.size(1);
   TORCH_CHECK(x.dtype() == torch::kBFloat16 && x.stride(1) == 1 && out.dtype() == torch::kBFloat16 && out.stride(1) == 1,
               "gemm_nvf4: bf16 activations and output");
-  TORCH_CHECK(K % 64 == 0 && N % 128 == 0 && out.size(0) == M, "gemm_nvf4: K % 64, N % 128");
-  const int64_t units = (N / 128) * (K / 64);
+  TORCH_CHECK(K % 64 == 0 && out.size(0) == M, "gemm_nvf4: K % 64");
+  const int64_t units = ((N + 127) / 128) * (K / 64);  // weight rows padded to 128 (zero codes)
   TORCH_CHECK(wq.numel() == units * 4096 && ws.numel() == units * 512 && wq.is_contiguous() && ws.is_contiguous(),
               "gemm_nvf4: weight units [N/128][K/64][128][32] and scales [N/128][K/64][128][4]");
   const bool dual = wq2.has_value() && wq2->defined();
@@ -356,7 +356,7 @@ void gemm_nvf4(torch::Tensor wq, torch::Tensor ws, double alpha, c10::optional<t
   const at::cuda::CUDAGuard guard(x.device());
   const int BN = M <= 16 ? 16 : M <= 32 ? 32 : M <= 64 ? 64 : 128;
   const int n_tiles = (int)((M + BN - 1) / BN);
-  const int grid_x = (int)(N / 128);
+  const int grid_x = (int)((N + 127) / 128);
   const int kchunks = (int)(K / 64);
   int S = 1;
   const int target = 2 * device_sm_count();

@@ -111,6 +111,9 @@ __global__ void __launch_bounds__(192, 1)
   __shared__ int s_last, s_ok;
 
   const int warp = warp_id(), lane = lane_id();
+  unsigned long long* tr =
+      args.trace ? args.trace + ((int64_t)blockIdx.y * gridDim.x + blockIdx.x) * kTrN : nullptr;
+  if (tr && threadIdx.x == 0) tr[kTrEntry] = globaltimer_ns();
   int m0 = blockIdx.x * 128 * MT;  // row (A) coordinate in the weight matrix (first of MT row tiles)
   const int S = args.splits;
   const int split = (int)(blockIdx.y % S);
@@ -153,6 +156,7 @@ __global__ void __launch_bounds__(192, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tbase = *tmem_holder;
+  if (tr && threadIdx.x == 0) tr[kTrSetup] = globaltimer_ns();
 
   const uint32_t a_tx = (KIND == KIND_BF16) ? 128 * 128 : (args.a_fmt == kFmtE2M1 ? 128 * 64 : 128 * 128);
   const uint32_t stage_tx = a_tx * C::NA + BN * 128 + (KIND == KIND_MX ? 512 * C::NA + 512 * C::NB_SF : 0);
@@ -212,6 +216,7 @@ __global__ void __launch_bounds__(192, 1)
       for (int q = 0; q < npre; ++q) load_a(q);
       for (int q = npre; q < min(nq, npre + PD); ++q) prefetch_a(q);
       pdl_wait();
+      if (tr) tr[kTrPdl] = globaltimer_ns();
       for (int q = 0; q < nq; ++q) {
         if (q >= npre) {
           if (!mbar_wait(&l_empty[q % NP], (uint32_t)(((q / NP) & 1) ^ 1), args.timeout_ns)) {
@@ -237,6 +242,7 @@ __global__ void __launch_bounds__(192, 1)
           report_error(args.status, kErrMbarTimeout, 101, q);
           break;
         }
+        if (tr && q == 0) tr[kTrFirst] = globaltimer_ns();
         tc_fence_after();
         const uint32_t sa = UNPACK ? smem_u32(smem + C::OFF_C + sc * C::NA * C::A_BYTES)
                                    : smem_u32(smem + C::OFF_A + s * C::NA * C::AL_BYTES);
@@ -275,6 +281,7 @@ __global__ void __launch_bounds__(192, 1)
         if (UNPACK) tc_commit(&c_empty[sc]);
       }
       tc_commit(tmem_full);  // arrives once every MMA issued above has completed
+      if (tr) tr[kTrIssued] = globaltimer_ns();
       pdl_trigger();
     }
     __syncwarp();
@@ -315,6 +322,7 @@ __global__ void __launch_bounds__(192, 1)
     asm volatile("bar.sync 1, 128;" ::: "memory");
     const bool ok = s_ok != 0;
     if (!ok) report_error(args.status, kErrMbarTimeout, 102, 0);
+    if (tr && threadIdx.x == 64) tr[kTrAcc] = globaltimer_ns();
     tc_fence_after();
     // load one 16-column chunk of the accumulator(s), summing the NACC partial accumulators
     auto load_acc_t = [&](int t, int c, float* g, float* u) {
@@ -503,6 +511,7 @@ __global__ void __launch_bounds__(192, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (tr && threadIdx.x == 0) tr[kTrDone] = globaltimer_ns();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);
@@ -562,8 +571,29 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
     // (at most 8 splits when they form a cluster: the portable cluster size)
     p.S = std::max(1, std::min(gemm_cluster_enabled() ? 8 : 16, target / std::max(1, tiles)));
     while (p.S > 1 && kchunks / p.S < 4) --p.S;
+    static int force_s = -1;
+    if (force_s < 0) {
+      const char* e = getenv("R9K_GEMM_SPLITS");  // tuning: force the K split count of skinny GEMMs
+      force_s = e ? std::max(0, atoi(e)) : 0;
+    }
+    if (force_s > 0) p.S = std::min(force_s, std::max(1, kchunks));
   }
   return p;
+}
+
+// tuning trace buffer (gemm_trace): the tiled kernel stamps kTrN timestamps per CTA when it fits
+static unsigned long long* g_trace = nullptr;
+static int64_t g_trace_cap = 0;
+
+void gemm_trace(c10::optional<torch::Tensor> buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->is_contiguous(), "gemm_trace: int64 cuda buffer");
+    g_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    g_trace_cap = buf->numel();
+  } else {
+    g_trace = nullptr;
+    g_trace_cap = 0;
+  }
 }
 
 // workspace layout: [65536 int counters][partials]
@@ -606,6 +636,7 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& ta2, const CUt
     l2pf = e ? std::max(0, atoi(e)) : 0;
   }
   if (BN <= 64 && !UNPACK) args.l2_prefetch = l2pf;  // skinny (weight-streaming) GEMMs only
+  args.trace = ((int64_t)grid_x * p.n_tiles * p.S * kTrN <= g_trace_cap) ? g_trace : nullptr;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid_x, p.n_tiles * p.S, 1);
   cfg.blockDim = dim3(192, 1, 1);

@@ -51,7 +51,11 @@ R9K_DEVINL void mm_st_v4(void* p, const uint4& v) {
 }
 
 // CTA-wide barrier with CTA `slot` of every rank; false if a peer did not arrive in time
+// (epochs only grow: every collective on one signal pad draws them from the same sequence counter)
 R9K_DEVINL bool nvls_barrier(const NvlsArgs& a, int slot, uint32_t epoch) {
+  // multicast stores and the unicast reads after the barrier reach the same memory through two
+  // virtual aliases
+  asm volatile("fence.proxy.alias;" ::: "memory");
   __syncthreads();  // every thread's stores of this CTA happen before the release below
   bool ok = true;
   if (threadIdx.x < a.world) {

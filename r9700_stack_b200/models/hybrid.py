@@ -221,7 +221,10 @@ class HybridLM:
         vl = self.vocab_local
         self.lm_head = tpf.rows([(c.vocab, r * vl, vl)], H, c.lm_head_format)
         # MX weights take MXFP8 activations; bf16 and native NVFP4 weights take bf16 activations
-        self.mx = isinstance(self.layers[0].get("w_in", self.layers[-1].get("w_qkv")), L.MXWeight)
+        kinds = {isinstance(w, L.MXWeight) for lay in self.layers for n, w in lay.items()
+                 if n in ("w_in", "w_out", "w_qkv", "w_o", "w_idx", "w_gate", "w_up", "w_down")}
+        assert len(kinds) == 1, "every layer's linear weights must be MX, or all bf16 / native NVFP4"
+        self.mx = kinds.pop()
 
     def _rope_cache(self, max_pos: int):
         c = self.cfg

@@ -54,10 +54,13 @@ class MoEBuffers:
 
 def moe_ffn(lay, x: torch.Tensor, mb: MoEBuffers, out: torch.Tensor, *, k: int, e0: int, E_local: int, moe_ffn: int,
             hidden: int, shared_local: int, route_mode: int = 0, bias=None, n_group: int = 1, topk_group: int = 1,
-            scale: float = 1.0, renorm: bool = True, remap=None, route: bool = True, gemm_E: int = 0) -> None:
+            scale: float = 1.0, renorm: bool = True, remap=None, route: bool = True, gemm_E: int = 0,
+            combine: bool = True):
     """Routed experts + shared expert for the T rows of x (bf16) into out (bf16), with the router
     weights applied and summed in one rounding (moe_combine). Experts outside [e0, e0 + E_local)
-    belong to other ranks: their rows are skipped and the caller's all-reduce sums the partials."""
+    belong to other ranks: their rows are skipped and the caller's all-reduce sums the partials.
+    ``combine=False`` stops before the combine (the expert rows stay in mb.y_sorted at mb.perm_row)
+    and returns the shared expert's output and gate for the caller's own combine."""
     T = x.shape[0]
     o = _ops()
     dev = x.device
@@ -89,6 +92,8 @@ def moe_ffn(lay, x: torch.Tensor, mb: MoEBuffers, out: torch.Tensor, *, k: int, 
         if "s_gvec" in lay:
             L.bf16_linear(x, lay["s_gvec"], out=mb.sh_gate[:T], out_dtype=torch.float32)
             gate = mb.sh_gate[:T]
+    if not combine:
+        return shared, gate
     o.moe_combine(mb.y_sorted, mb.perm_row[:A], mb.wts[:T], k, shared, gate, out)
 
 
@@ -266,18 +271,29 @@ class HybridMoELM(HybridLM):
                         hidden=c.hidden, shared_local=self.shared_local, route_mode=mode,
                         remap=lambda ids: (cache.route(ids, e0, ws.slot_ids[:T]), ws.slot_ids[:T])[1])
             else:
-                # wider batches (prefill): stream the experts through the slots in groups of S
-                if not hasattr(ws, "moe_pass"):
-                    ws.moe_pass = torch.zeros_like(ws.norm_out)
+                # wider batches (prefill): stream the experts through the slots in groups of S; each
+                # pass parks its expert rows in token-pair order, one combine sums them all (the same
+                # order and single rounding as resident experts)
+                A = T * c.moe_topk
+                pair = getattr(ws, "moe_pair", None)
+                if pair is None or pair.shape[0] < A + 1:
+                    ws.moe_pair = pair = torch.zeros(A + 1, c.hidden, dtype=torch.bfloat16, device=self.device)
+                    ws.moe_ident = torch.arange(A, dtype=torch.int32, device=self.device)
+                ident = ws.moe_ident[:A]
+                mb = ws.moe
+                shared = gate = None
                 for p, grp in enumerate(cache.stream_groups()):
                     n = cache.warm(grp)
-                    dst = out if p == 0 else ws.moe_pass[:T]
-                    moe_ffn(lay_c, ws.norm_out[:T], ws.moe, dst, k=c.moe_topk, e0=0, E_local=n,
-                            moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local if p == 0 else 0,
-                            route_mode=mode, route=p == 0, gemm_E=cache.S,
-                            remap=lambda ids: cache.slots_for(ids, e0, ws.slot_ids[:T]))
-                    if p > 0:
-                        out.add_(dst)
+                    sg = moe_ffn(lay_c, ws.norm_out[:T], mb, out, k=c.moe_topk, e0=0, E_local=n,
+                                 moe_ffn=c.moe_ffn, hidden=c.hidden, shared_local=self.shared_local if p == 0 else 0,
+                                 route_mode=mode, route=p == 0, gemm_E=cache.S, combine=False,
+                                 remap=lambda ids: cache.slots_for(ids, e0, ws.slot_ids[:T]))
+                    if p == 0:
+                        shared, gate = sg
+                    src = mb.perm_row[:A].long()
+                    dest = torch.where(src >= 0, ident.long(), torch.full_like(src, A))  # row A: discard
+                    pair.index_copy_(0, dest, mb.y_sorted[src.clamp(min=0)])
+                _ops().moe_combine(pair, ident, mb.wts[:T], c.moe_topk, shared, gate, out)
         if getattr(self, "routing_profile", None) is not None:
             self.routing_profile.record(i, ws.moe.ids[:T])
         if self.ple is not None:

@@ -107,7 +107,7 @@ def from_float(w: torch.Tensor, fmt: str, tiled: bool | None = None, global_from
     if fmt == "nvfp4":
         gs = F.nvfp4_global_scale(global_from.float()) if global_from is not None else None
         packed, s16, g = L.nvfp4_quantize(w, global_scale=gs)
-        if knobs.get("R9K_NVFP4") == "native" and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0 and not tiled_forced:
+        if knobs.get("R9K_NVFP4") == "native" and w.shape[1] % 64 == 0 and not tiled_forced:
             return L.NVF4Weight.from_checkpoint(packed, s16, g)
         mw = L.mx_from_nvfp4(packed, s16, g, search=True)
         return mw.to_tiled() if tiled else mw

@@ -139,11 +139,17 @@ class NVF4Weight:
 
     @staticmethod
     def from_checkpoint(packed: torch.Tensor, s16: torch.Tensor, g: float) -> "NVF4Weight":
-        """packed [N, K/2] (low nibble = even element), s16 [N, K/16] e4m3 bytes, global scale g."""
+        """packed [N, K/2] (low nibble = even element), s16 [N, K/16] e4m3 bytes, global scale g.
+        Rows are padded to a multiple of 128 with zero codes and scales (the kernel masks them)."""
         N, K = packed.shape[0], packed.shape[1] * 2
-        assert N % 128 == 0 and K % 64 == 0, "native NVFP4 needs N % 128 == 0 and K % 64 == 0"
-        q = packed.contiguous().view(N // 128, 128, K // 64, 32).permute(0, 2, 1, 3).reshape(-1, 128, 32).contiguous()
-        s = s16.contiguous().view(torch.uint8).view(N // 128, 128, K // 64, 4).permute(0, 2, 1, 3)
+        assert K % 64 == 0, "native NVFP4 needs K % 64 == 0"
+        Np = -(-N // 128) * 128
+        packed, s16 = packed.contiguous(), s16.contiguous().view(torch.uint8)
+        if Np != N:
+            packed = torch.cat([packed, packed.new_zeros(Np - N, packed.shape[1])])
+            s16 = torch.cat([s16, s16.new_zeros(Np - N, s16.shape[1])])
+        q = packed.view(Np // 128, 128, K // 64, 32).permute(0, 2, 1, 3).reshape(-1, 128, 32).contiguous()
+        s = s16.view(Np // 128, 128, K // 64, 4).permute(0, 2, 1, 3)
         return NVF4Weight(q, s.reshape(-1, 128, 4).contiguous(), 1.0 / float(g), N, K)
 
     def dequant(self) -> torch.Tensor:
@@ -151,8 +157,9 @@ class NVF4Weight:
         from ..quant import formats as F
 
         N, K = self.N, self.K
-        packed = self.q.view(N // 128, K // 64, 128, 32).permute(0, 2, 1, 3).reshape(N, K // 2)
-        s16 = self.s.view(N // 128, K // 64, 128, 4).permute(0, 2, 1, 3).reshape(N, K // 16)
+        Np = -(-N // 128) * 128
+        packed = self.q.view(Np // 128, K // 64, 128, 32).permute(0, 2, 1, 3).reshape(Np, K // 2)[:N]
+        s16 = self.s.view(Np // 128, K // 64, 128, 4).permute(0, 2, 1, 3).reshape(Np, K // 16)[:N]
         return F.dequant_nvfp4(packed.cpu(), s16.cpu(), 1.0 / self.alpha).to(self.q.device)
 
 

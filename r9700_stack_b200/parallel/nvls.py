@@ -31,8 +31,9 @@ class NvlsComm:
         self.local = int(self.buf.data_ptr())
         self.sig = torch.tensor([int(p) for p in self.handle.signal_pad_ptrs], dtype=torch.int64)
         self.sig_slots = int(symm_mem.get_signal_pad_size()) // 4
-        self.seq_ar = torch.zeros(2, dtype=torch.int32, device=self.device)
-        self.seq_ag = torch.zeros(2, dtype=torch.int32, device=self.device)
+        # one [sequence, ticket] pair for every collective of this object: they share the signal pads,
+        # so their barrier epochs must come from one increasing sequence
+        self.seq = torch.zeros(2, dtype=torch.int32, device=self.device)
         # every rank must agree (a rank without multicast makes the whole group fall back)
         ok = torch.tensor([1 if self.mc else 0], dtype=torch.int32, device=self.device)
         dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=self.group)
@@ -45,7 +46,7 @@ class NvlsComm:
 
     def all_reduce_(self, t: torch.Tensor) -> torch.Tensor:
         _native.ops().nvls_all_reduce(t, t, self.mc, self.local, self.capacity, self.sig, self.sig_slots, self.rank,
-                                      self.world, self.seq_ar, _status.status(self.device), self.timeout_s)
+                                      self.world, self.seq, _status.status(self.device), self.timeout_s)
         return t
 
     def fits_all_gather(self, t: torch.Tensor) -> bool:
@@ -56,5 +57,5 @@ class NvlsComm:
     def all_gather(self, t: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
         """out [W, *t.shape] (rank-major)."""
         _native.ops().nvls_all_gather(t, out, self.mc, self.local, self.capacity, self.sig, self.sig_slots,
-                                      self.rank, self.world, self.seq_ag, _status.status(self.device), self.timeout_s)
+                                      self.rank, self.world, self.seq, _status.status(self.device), self.timeout_s)
         return out

@@ -105,16 +105,50 @@ def bench_gemm(a) -> dict:
         else:
             out = torch.empty(M, N, dtype=torch.bfloat16, device="cuda")
             f = lambda i: L.mx_linear(x, ws[i % nw], out=out)
+    tr = None
+    if getattr(a, "trace", False):
+        tr = torch.zeros(1 << 20, dtype=torch.int64, device="cuda")
+        torch.ops.r9k.gemm_trace(tr)
     us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    if tr is not None:
+        torch.ops.r9k.gemm_trace(None)
     wbytes = per + (N * K // 32) * (0 if a.fmt == "bf16" else 1) * (2 if a.swiglu else 1)
     flops = 2.0 * M * N * K * (2 if a.swiglu else 1)
     r = {"kernel": "gemm", "fmt": a.fmt, "swiglu": a.swiglu, "N": N, "K": K, "M": M, "copies": nw,
          "us": us, "weight_bytes": wbytes, "flops": flops}
+    if tr is not None:
+        r["trace"] = trace_summary(tr)
     if a.vs_torch and a.fmt == "bf16" and not a.swiglu:
         # the library baseline: torch.matmul (cuBLAS) on the same rotated bf16 weights, same timing
         tw = [w.w for w in ws]
         r["torch_matmul_us"] = _time(lambda i: torch.matmul(xb, tw[i % nw].T), a.reps, a.warmup, graph=not a.eager)
     return r
+
+
+TRACE_POINTS = ("entry", "setup", "pdl", "first", "issued", "acc", "done")
+
+
+def trace_summary(buf: torch.Tensor) -> dict:
+    """Per-phase timing of the last traced GEMM launch (gemm_trace stamps, 8 per CTA): each point's
+    min / median / max over CTAs in us from the first CTA's entry, and the median of each phase."""
+    t = buf.view(-1, 8)[:, : len(TRACE_POINTS)].cpu()
+    t = t[t[:, 0] > 0]
+    if t.numel() == 0:
+        return {}
+    rel = (t - t[:, 0].min()).double() / 1e3
+    out = {"ctas": int(t.shape[0])}
+    for i, name in enumerate(TRACE_POINTS):
+        col = rel[:, i][t[:, i] > 0]
+        if col.numel():
+            out[name] = [round(float(col.min()), 2), round(float(col.median()), 2), round(float(col.max()), 2)]
+    ph = {}
+    for i in range(1, len(TRACE_POINTS)):
+        ok = (t[:, i] > 0) & (t[:, i - 1] > 0)
+        if ok.any():
+            d = (t[ok, i] - t[ok, i - 1]).double() / 1e3
+            ph[f"{TRACE_POINTS[i - 1]}->{TRACE_POINTS[i]}"] = round(float(d.median()), 2)
+    out["phase_median_us"] = ph
+    return out
 
 
 def bench_moe(a) -> dict:
@@ -331,6 +365,7 @@ def main(argv=None):
     g.add_argument("--tiled", type=int, default=1)
     g.add_argument("--max-copies", type=int, default=16)
     g.add_argument("--vs-torch", action="store_true", help="bf16: also time torch.matmul (cuBLAS) on the same weights")
+    g.add_argument("--trace", action="store_true", help="per-CTA phase timestamps of the last launch (gemm_trace)")
     m = sub.add_parser("moe")
     m.add_argument("--T", type=int, default=16)
     m.add_argument("--E", type=int, default=288)
