@@ -3,6 +3,7 @@ GDN/attention 27B-class model, tensor-parallel over the job'
 
     python bench.py [--gpus N] [--steps K] [--warmup W]            # this framework
     python bench.py --impl reference ...                           # the reference (prints unavailable)
+    python bench.py --impl vllm ...                                # stock vLLM bf16 on the same shapes
 
 For N > 1 launch with torchrun (one rank per GPU, NCCL). Weights are random N(0, 0.02) quantised to
 NVFP4 (converted to MXFP4 at load), lm_head block fp8 (-> MXFP8), fp8 KV cache; prompts are uniform
@@ -66,7 +67,9 @@ def parse():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference", "vllm"],
+                    help="ours | reference (the installed reference's stock path) | vllm (stock vLLM, bf16, "
+                         "NCCL + cuBLAS: a second comparator, see bench_vllm.py)")
     ap.add_argument("--streams", type=int, default=16)
     ap.add_argument("--prompt-len", type=int, default=8192)
     ap.add_argument("--layers", type=int, default=0, help="override layer count (debug only; invalid for the metric)")
@@ -173,6 +176,10 @@ def main():
         if int(os.environ.get("RANK", "0")) == 0:
             print(json.dumps({"impl": "reference", "unavailable": reference_probe(), "metric": METRIC}))
         return 0
+    if args.impl == "vllm":
+        import bench_vllm
+
+        return bench_vllm.run(args, METRIC)
 
     import numpy as np
     import torch

@@ -172,6 +172,12 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
 void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torch::Tensor w, double eps,
                         c10::optional<torch::Tensor> y, c10::optional<torch::Tensor> out_q,
                         c10::optional<torch::Tensor> out_sf);
+void gdn_state_prefetch(torch::Tensor state, c10::optional<torch::Tensor> conv_state, torch::Tensor seq_slot);
+// gdn_chunk.cu
+void gdn_chunked(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                 torch::Tensor state, torch::Tensor ctab, torch::Tensor seq_chunk0, torch::Tensor seq_slot,
+                 torch::Tensor seq_has_state, bool write_state, torch::Tensor w, torch::Tensor qg, torch::Tensor khT,
+                 torch::Tensor p, torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status);
 void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,
                       torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor state, torch::Tensor seq_slot,
                       torch::Tensor seq_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
@@ -294,6 +300,10 @@ TORCH_LIBRARY(r9k, m) {
         "int max_misses) -> ()");
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
+  m.def("gdn_state_prefetch(Tensor state, Tensor? conv_state, Tensor seq_slot) -> ()");
+  m.def("gdn_chunked(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor ctab, "
+        "Tensor seq_chunk0, Tensor seq_slot, Tensor seq_has_state, bool write_state, Tensor(b!) w, Tensor(c!) qg, "
+        "Tensor(d!) khT, Tensor(e!) p, Tensor(f!) uT, Tensor(g!) gC, Tensor(h!) o, Tensor(i!) status) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
         "Tensor(a!) conv_state, Tensor(b!) state, Tensor seq_slot, Tensor seq_has_state, Tensor A_log, "
         "Tensor dt_bias, Tensor norm_w, float eps, Tensor(c!)? out_q, Tensor(d!)? out_sf, Tensor(e!)? out_bf16) -> ()");
@@ -364,6 +374,8 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gdn_recurrent", &r9k::gdn_recurrent);
   m.impl("gdn_out_norm_quant", &r9k::gdn_out_norm_quant);
   m.impl("gdn_decode_fused", &r9k::gdn_decode_fused);
+  m.impl("gdn_state_prefetch", &r9k::gdn_state_prefetch);
+  m.impl("gdn_chunked", &r9k::gdn_chunked);
 }
 
 // host-only helpers of the symmetric-memory runtime (no tensors on the device side of the call)

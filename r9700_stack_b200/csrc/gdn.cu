@@ -16,10 +16,11 @@
 //                         verify, run on commit).
 //  * gdn_recurrent      - the delta-rule recurrence (state stored transposed, [dv][dk] per head).
 //                         Columns of S evolve independently, so the grid
-//                         splits each head's dv columns over CTAs (32 per CTA); four lanes share a
-//                         column (32 rows each) and reduce with shuffles, so no block barrier runs
-//                         per token. Serves decode (1 token), spec verify (T tokens, state not
-//                         written), commit (accepted tokens, state written) and prefill.
+//                         splits each head's dv columns over CTAs (16 per CTA); eight lanes share a
+//                         column (16 rows each) and reduce with shuffles, one reduction per token
+//                         (the output dot and the next key dot share it), no block barrier per
+//                         token. Serves decode (1 token), spec verify (T tokens, state not written),
+//                         commit (accepted tokens, state written) and prefill.
 //  * gdn_out_norm_quant - RMSNormGated + MXFP8 quantisation of the result for out_proj.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -217,6 +218,33 @@ template <> struct StateVec16<__nv_bfloat16> {
   }
 };
 
+R9K_DEVINL void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+R9K_DEVINL void cp_async_4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+
+// waits until at most n of this thread's cp.async groups are still in flight (n < 8)
+R9K_DEVINL void cp_async_wait_pending(int n) {
+  switch (n) {
+    case 0: asm volatile("cp.async.wait_group 0;" ::: "memory"); break;
+    case 1: asm volatile("cp.async.wait_group 1;" ::: "memory"); break;
+    case 2: asm volatile("cp.async.wait_group 2;" ::: "memory"); break;
+    case 3: asm volatile("cp.async.wait_group 3;" ::: "memory"); break;
+    case 4: asm volatile("cp.async.wait_group 4;" ::: "memory"); break;
+    case 5: asm volatile("cp.async.wait_group 5;" ::: "memory"); break;
+    case 6: asm volatile("cp.async.wait_group 6;" ::: "memory"); break;
+    default: asm volatile("cp.async.wait_group 7;" ::: "memory"); break;
+  }
+}
+
+// Token-serial delta rule. CTA = (sequence, value head, 16 state columns), 128 threads: lane
+// (column cl, row group rg) of a warp owns 16 dk rows of one column, so 8 lanes share a column and
+// reduce with three xor shuffles. The critical path per token is one shuffle reduction: the output
+// dot S_t . q_t and the next token's key dot S_t . k_{t+1} read the same updated state and reduce
+// together. q / k / v / g / beta are staged CH tokens at a time with cp.async into two buffers, the
+// next chunk landing while this one runs.
 template <typename ST, int DK>
 __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const float* __restrict__ q, const float* __restrict__ k, const float* __restrict__ v,
@@ -225,65 +253,119 @@ __global__ void __launch_bounds__(128) gdn_recurrent_kernel(
     const int32_t* __restrict__ seq_has_state, int write_state, float* __restrict__ o) {
   pdl_wait();
   pdl_trigger();  // dependents may launch and prefetch while this grid runs
-  static_assert(DK == 128, "row groups of 32");
-  constexpr int CH = 16;  // tokens staged per chunk
-  __shared__ float sq[CH][DK], sk[CH][DK], sv[CH][32], sg[CH], sb[CH];
+  static_assert(DK == 128, "8 row groups of 16");
+  constexpr int CH = 16, RPL = 16, RS = RPL + 4;  // RS: row-group stride (conflict-free 16-byte reads)
+  __shared__ __align__(16) float sq[2][CH][8][RS];
+  __shared__ __align__(16) float sk[2][CH][8][RS];
+  __shared__ __align__(16) float sv[2][CH][16];
+  __shared__ float sg[2][CH], sb[2][CH];
   const int s = blockIdx.x, h = blockIdx.y, cs = blockIdx.z;
-  const int tid = threadIdx.x, c = tid >> 2, rg = tid & 3;
-  const int col = cs * 32 + c;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int rg = lane & 7, cl = ((tid >> 5) << 2) | (lane >> 3);
+  const int col = cs * 16 + cl;
   const int kh = h / (Hv / Hk);
   const int slot = seq_slot[s], t0 = seq_start[s], n = seq_len[s];
   if (n <= 0 && !write_state) return;
-  ST* Sp = state + (((int64_t)slot * Hv + h) * dv + col) * DK + rg * 32;
-  float S[32];
-  if (seq_has_state[s] != 0) StateVec<ST>::load(Sp, S);
+  ST* Sp = state + (((int64_t)slot * Hv + h) * dv + col) * DK + rg * RPL;
+  float S[RPL];
+  if (seq_has_state[s] != 0) StateVec16<ST>::load(Sp, S);
   else {
 #pragma unroll
-    for (int r = 0; r < 32; ++r) S[r] = 0.f;
+    for (int r = 0; r < RPL; ++r) S[r] = 0.f;
   }
-  for (int base = 0; base < n; base += CH) {
+  auto stage = [&](int buf, int base) {
     const int cnt = min(CH, n - base);
-    __syncthreads();
-    for (int e = tid; e < cnt * DK; e += 128) {
-      const int tt = e / DK, i = e % DK;
-      const int64_t tok = t0 + base + tt;
-      const int si = (i & 31) * 4 + (i >> 5);  // interleave: row i = rg*32 + r -> r*4 + rg
-      sq[tt][si] = q[(tok * Hk + kh) * DK + i];
-      sk[tt][si] = k[(tok * Hk + kh) * DK + i];
-    }
     for (int e = tid; e < cnt * 32; e += 128) {
-      const int tt = e / 32, cc = e % 32;
-      const int64_t tok = t0 + base + tt;
-      sv[tt][cc] = v[(tok * Hv + h) * dv + cs * 32 + cc];
+      const int tt = e >> 5, pc = e & 31;
+      const int64_t off = ((int64_t)(t0 + base + tt) * Hk + kh) * DK + pc * 4;
+      cp_async_16(&sq[buf][tt][pc >> 2][(pc & 3) * 4], q + off);
+      cp_async_16(&sk[buf][tt][pc >> 2][(pc & 3) * 4], k + off);
     }
-    if (tid < cnt) {
-      const int64_t tok = t0 + base + tid;
-      sg[tid] = __expf(g[tok * Hv + h]);
-      sb[tid] = beta[tok * Hv + h];
+    if (tid < cnt * 4) {
+      const int tt = tid >> 2, pc = tid & 3;
+      cp_async_16(&sv[buf][tt][pc * 4], v + ((int64_t)(t0 + base + tt) * Hv + h) * dv + cs * 16 + pc * 4);
     }
-    __syncthreads();
-    for (int tt = 0; tt < cnt; ++tt) {
-      const float decay = sg[tt];
-      const float* kk = &sk[tt][rg];
-      const float* qq = &sq[tt][rg];
-      float kv = 0.f;
+    if (tid >= 64 && tid < 64 + cnt) {
+      const int64_t tok = t0 + base + (tid - 64);
+      cp_async_4(&sg[buf][tid - 64], g + tok * Hv + h);
+      cp_async_4(&sb[buf][tid - 64], beta + tok * Hv + h);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  auto ld16 = [&](const float* p, float* x) {
 #pragma unroll
-      for (int r = 0; r < 32; ++r) kv += S[r] * kk[4 * r];
+    for (int i = 0; i < 4; ++i) {
+      const float4 f = reinterpret_cast<const float4*>(p)[i];
+      x[4 * i] = f.x; x[4 * i + 1] = f.y; x[4 * i + 2] = f.z; x[4 * i + 3] = f.w;
+    }
+  };
+  if (n > 0) {
+    stage(0, 0);
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    __syncthreads();
+    float kc[RPL];
+    ld16(&sk[0][0][rg][0], kc);
+    float kv;
+    {
+      float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll
+      for (int r = 0; r < RPL; r += 4) {
+        a0 += S[r] * kc[r]; a1 += S[r + 1] * kc[r + 1]; a2 += S[r + 2] * kc[r + 2]; a3 += S[r + 3] * kc[r + 3];
+      }
+      kv = (a0 + a1) + (a2 + a3);
       kv += __shfl_xor_sync(0xffffffffu, kv, 1);
       kv += __shfl_xor_sync(0xffffffffu, kv, 2);
-      const float delta = sb[tt] * (sv[tt][c] - decay * kv);
-      float ov = 0.f;
+      kv += __shfl_xor_sync(0xffffffffu, kv, 4);
+    }
+    for (int base = 0; base < n; base += CH) {
+      const int buf = (base / CH) & 1;
+      const int cnt = min(CH, n - base);
+      const bool has_next_chunk = base + CH < n;
+      if (has_next_chunk) stage(buf ^ 1, base + CH);
+#pragma unroll 1
+      for (int tt = 0; tt < cnt; ++tt) {
+        const float decay = __expf(sg[buf][tt]), bt = sb[buf][tt], vt = sv[buf][tt][cl];
+        float qv[RPL], kn[RPL];
+        ld16(&sq[buf][tt][rg][0], qv);
+        const bool last = tt == cnt - 1;
+        const bool more = !last || has_next_chunk;
+        if (!last) {
+          ld16(&sk[buf][tt + 1][rg][0], kn);
+        } else {
+          // the next chunk has landed and every thread is done with this buffer past this point
+          asm volatile("cp.async.wait_all;" ::: "memory");
+          __syncthreads();
+          if (more) ld16(&sk[buf ^ 1][0][rg][0], kn);
+        }
+        const float delta = bt * (vt - decay * kv);
+        float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f, k0 = 0.f, k1 = 0.f, k2 = 0.f, k3 = 0.f;
 #pragma unroll
-      for (int r = 0; r < 32; ++r) {
-        S[r] = S[r] * decay + kk[4 * r] * delta;
-        ov += S[r] * qq[4 * r];
+        for (int r = 0; r < RPL; r += 4) {
+          S[r] = S[r] * decay + kc[r] * delta;
+          S[r + 1] = S[r + 1] * decay + kc[r + 1] * delta;
+          S[r + 2] = S[r + 2] * decay + kc[r + 2] * delta;
+          S[r + 3] = S[r + 3] * decay + kc[r + 3] * delta;
+          o0 += S[r] * qv[r]; o1 += S[r + 1] * qv[r + 1]; o2 += S[r + 2] * qv[r + 2]; o3 += S[r + 3] * qv[r + 3];
+          if (more) {
+            k0 += S[r] * kn[r]; k1 += S[r + 1] * kn[r + 1]; k2 += S[r + 2] * kn[r + 2]; k3 += S[r + 3] * kn[r + 3];
+          }
+        }
+        float ov = (o0 + o1) + (o2 + o3), kvn = (k0 + k1) + (k2 + k3);
+#pragma unroll
+        for (int m = 1; m <= 4; m <<= 1) {
+          ov += __shfl_xor_sync(0xffffffffu, ov, m);
+          kvn += __shfl_xor_sync(0xffffffffu, kvn, m);
+        }
+        if (o != nullptr && rg == 0) o[((int64_t)(t0 + base + tt) * Hv + h) * dv + col] = ov;
+        kv = kvn;
+        if (more) {
+#pragma unroll
+          for (int r = 0; r < RPL; ++r) kc[r] = kn[r];
+        }
       }
-      ov += __shfl_xor_sync(0xffffffffu, ov, 1);
-      ov += __shfl_xor_sync(0xffffffffu, ov, 2);
-      if (o != nullptr && rg == 0) o[((int64_t)(t0 + base + tt) * Hv + h) * dv + col] = ov;
     }
   }
-  if (write_state) StateVec<ST>::store(Sp, S);
+  if (write_state) StateVec16<ST>::store(Sp, S);
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -385,11 +467,11 @@ void gdn_recurrent(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Ten
   if (S == 0) return;
   const int Hk = (int)q.size(1), DK = (int)q.size(2);
   const int Hv = (int)v.size(1), dv = (int)v.size(2);
-  TORCH_CHECK(dv % 32 == 0 && DK == 128, "gdn_recurrent: dk 128, dv % 32");
+  TORCH_CHECK(dv % 16 == 0 && DK == 128, "gdn_recurrent: dk 128, dv % 16");
   TORCH_CHECK(state.size(1) == Hv && state.size(2) == dv && state.size(3) == DK, "gdn_recurrent: state [slots, Hv, dv, dk]");
   const at::cuda::CUDAGuard guard(q.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  dim3 grid((unsigned)S, (unsigned)Hv, (unsigned)(dv / 32));
+  dim3 grid((unsigned)S, (unsigned)Hv, (unsigned)(dv / 16));
   float* op = (o.has_value() && o->defined()) ? o->data_ptr<float>() : nullptr;
   if (state.dtype() == torch::kFloat32)
     launch_pdl(gdn_recurrent_kernel<float, 128>, grid, dim3(128), 0, st,
@@ -462,6 +544,8 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
   constexpr int NV = PER * sizeof(ST) / 16;  // 16-byte chunks per thread and head
   uint4* sS = reinterpret_cast<uint4*>(s_state);
   // chunk v of thread tid for head j at (j * NV + v) * NT + tid: conflict-free
+  // one cp.async group per value head: head j waits only for its own state (each thread reads back
+  // exactly the chunks it requested, so no block barrier is needed for them)
   if (hs) {
     for (int j = 0; j < rep; ++j) {
       const ST* Sp = state + (((int64_t)slot * Hv + kh * rep + j) * D + c) * D + rg * PER;
@@ -469,9 +553,9 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
       for (int v = 0; v < NV; ++v)
         asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(sS + (j * NV + v) * NT + tid)),
                      "l"(reinterpret_cast<const uint8_t*>(Sp) + 16 * v) : "memory");
+      asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
-  asm volatile("cp.async.commit_group;" ::: "memory");
   pdl_wait();
   pdl_trigger();
   // ---- conv over q (128) | k (128) | the rep value heads (rep x 128) channels
@@ -516,7 +600,6 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
     for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
     if (l == 0) sred[0][tid >> 5] = rsqrtf(ss + 1e-6f);
   }
-  asm volatile("cp.async.wait_all;" ::: "memory");
   __syncthreads();
   const float qs = sred[0][0] * rsqrtf((float)D), ks = sred[0][1];
   const float* kk = sk[rg];
@@ -525,6 +608,7 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
     const int h = kh * rep + j;
     ST* Sp = state + (((int64_t)slot * Hv + h) * D + c) * D + rg * PER;
     const float decay = sg[j];
+    if (hs) cp_async_wait_pending(rep - 1 - j);
     float kvs = 0.f;
 #pragma unroll 1
     for (int p = 0; p < PER / PC; ++p) {
@@ -603,6 +687,52 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
       }
     }
   }
+}
+
+// ------------------------------------------------------------------------------------------------
+// L2 prefetch of the recurrent and conv state of the sequences in a decode step: launched in front of
+// the layer's in_proj GEMM, it brings the state rows the fused GDN kernel will read into L2 while the
+// GEMM streams its weights (evict-first), so the GDN kernel does not start with a 25 MB HBM read. A
+// hint only: nothing reads its result. grid (sequences, pieces), 4 KiB per bulk prefetch.
+// ------------------------------------------------------------------------------------------------
+__global__ void gdn_state_prefetch_kernel(const uint8_t* __restrict__ state, int64_t state_row,
+                                          const uint8_t* __restrict__ conv, int64_t conv_row,
+                                          const int32_t* __restrict__ seq_slot) {
+  pdl_trigger();  // the GEMM behind may launch at once; nothing here depends on the kernel before
+  const int slot = seq_slot[blockIdx.x];
+  constexpr int64_t PIECE = 4096;
+  const uint8_t* sr = state + (int64_t)slot * state_row;
+  for (int64_t o = ((int64_t)blockIdx.y * blockDim.x + threadIdx.x) * PIECE; o < state_row;
+       o += (int64_t)gridDim.y * blockDim.x * PIECE) {
+    const uint32_t n = (uint32_t)(state_row - o < PIECE ? state_row - o : PIECE);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(sr + o), "r"(n) : "memory");
+  }
+  if (blockIdx.y == 0 && conv != nullptr) {
+    const uint8_t* cr = conv + (int64_t)slot * conv_row;
+    for (int64_t o = (int64_t)threadIdx.x * PIECE; o < conv_row; o += (int64_t)blockDim.x * PIECE) {
+      const uint32_t n = (uint32_t)(conv_row - o < PIECE ? conv_row - o : PIECE);
+      asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(cr + o), "r"(n) : "memory");
+    }
+  }
+}
+
+void gdn_state_prefetch(torch::Tensor state, c10::optional<torch::Tensor> conv_state, torch::Tensor seq_slot) {
+  const int64_t S = seq_slot.size(0);
+  if (S == 0) return;
+  TORCH_CHECK(state.is_contiguous() && seq_slot.dtype() == torch::kInt32, "gdn_state_prefetch: state, int32 slots");
+  const int64_t srow = state.numel() / state.size(0) * state.element_size();
+  const bool has_conv = conv_state.has_value() && conv_state->defined();
+  const int64_t crow = has_conv ? conv_state->numel() / conv_state->size(0) * conv_state->element_size() : 0;
+  TORCH_CHECK(srow % 16 == 0 && crow % 16 == 0 && (reinterpret_cast<uintptr_t>(state.data_ptr()) & 15) == 0 &&
+              (!has_conv || (reinterpret_cast<uintptr_t>(conv_state->data_ptr()) & 15) == 0),
+              "gdn_state_prefetch: 16-byte rows");
+  const at::cuda::CUDAGuard guard(state.device());
+  const int pieces = (int)std::min<int64_t>(8, (srow / 4096 + 127) / 128);
+  TORCH_CHECK(launch_pdl(gdn_state_prefetch_kernel, dim3((unsigned)S, (unsigned)std::max(1, pieces)), dim3(128), 0,
+                         at::cuda::getCurrentCUDAStream(), reinterpret_cast<const uint8_t*>(state.data_ptr()), srow,
+                         has_conv ? reinterpret_cast<const uint8_t*>(conv_state->data_ptr()) : nullptr, crow,
+                         seq_slot.data_ptr<int32_t>()) == cudaSuccess,
+              "gdn_state_prefetch launch");
 }
 
 void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,

@@ -1,0 +1,610 @@
+// Chunked gated delta rule for prefill on tcgen05 (sm_100a).
+//
+// The token-serial recurrence (gdn.cu) does ~6 FLOP per state element per token on CUDA cores with a
+// shuffle reduction on the critical path of every token. For long prompts the same result is computed
+// chunk-wise (the WY / UT form of the delta rule; the reference keeps this form for long prefill in
+// its stock chunked core, r9700_vllm/models/gdn.py:28-33). Per sequence, value head h and chunk of
+// C = 128 tokens with cumulative log-decay gc_t (gamma_t = exp(gc_t)), state S (dk x dv) entering the
+// chunk:
+//   L[t][j] = beta_t exp(gc_t - gc_j) k_t . k_j   (j < t)        T = (I + L)^-1   (unit lower)
+//   P[t][j] = exp(gc_t - gc_j) q_t . k_j          (j <= t)
+//   U = T (beta v),   W = T (beta gamma k)                          (chunk-local, no S)
+//   Delta = U - W S,  O = (gamma q) S + P Delta,  S' = gamma_C S + (gamma_C / gamma k)^T Delta
+// Phase 1 (gdn_chunk_prep, one CTA per chunk and value head, all in parallel): KK^T and QK^T on the
+// tensor cores, the masks and decays, T by blocked forward substitution in fp32, then U and W on the
+// tensor cores. It writes the operands of phase 2 (bf16 W, gamma q, K-hat^T and P; fp32 U^T).
+// Phase 2 (gdn_chunk_scan, one CTA per sequence and value head, chunks in order): everything is kept
+// transposed so TMEM lane n is state column n (dv): the state S^T lives in TMEM in fp32 for the whole
+// sequence; per chunk
+//   MMA1  Delta^T_acc = S^T W^T        MMA2  O^T = S^T (gamma q)^T
+//   E1    Delta^T = U^T - Delta^T_acc (bf16 operand), S^T *= gamma_C (in TMEM)
+//   MMA3  S^T += Delta^T K-hat         MMA4  O^T += Delta^T P^T
+//   E2    O^T -> o (fp32, the same layout gdn_recurrent writes), S^T -> bf16 operand of the next MMA1
+// The operand tiles of the next chunk stream in by TMA while the current chunk's epilogues run.
+// All MMAs are kind::f16 with bf16 operands and fp32 accumulation, M = N = 128, K = 128 (8 steps).
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include "common.cuh"
+#include "tmap.h"
+
+namespace r9k {
+namespace gch {
+constexpr int C = 128;              // tokens per chunk
+constexpr int D = 128;              // head dim (dk == dv)
+constexpr int REG = 128 * 128;      // one 128-row x 64-element bf16 swizzle region (16 KB)
+constexpr int TILE = 2 * REG;       // a 128 x 128 bf16 operand (two regions along K)
+constexpr int LS = 129;             // fp32 row stride of L / T in shared memory (bank spread)
+// phase 1 shared memory
+constexpr int P1_KT = 0;            // k rows (A and B of KK^T), later beta v^T (B of U)
+constexpr int P1_QT = P1_KT + TILE; // q rows (A of QK^T), later beta gamma k^T (B of W)
+constexpr int P1_L = P1_QT + TILE;  // L fp32 [128][LS]; after the solve, T as a bf16 operand
+constexpr int P1_T = P1_L + C * LS * 4;  // T fp32 [128][LS]
+constexpr int P1_X = P1_T + C * LS * 4;  // off-diagonal products of the blocked solve [16][LS]
+constexpr int P1_BAR = P1_X + 16 * LS * 4;
+constexpr int P1_SMEM = P1_BAR + 64 + 1024;
+// phase 2 shared memory
+constexpr int P2_S = 0, P2_D = TILE, P2_W = 2 * TILE, P2_Q = 3 * TILE, P2_K = 4 * TILE, P2_P = 5 * TILE;
+constexpr int P2_BAR = 6 * TILE;
+constexpr int P2_SMEM = P2_BAR + 128 + 1024;
+}  // namespace gch
+
+R9K_DEVINL float to_float(float x) { return x; }
+R9K_DEVINL float to_float(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <typename T> R9K_DEVINL T from_float(float x);
+template <> R9K_DEVINL float from_float<float>(float x) { return x; }
+template <> R9K_DEVINL __nv_bfloat16 from_float<__nv_bfloat16>(float x) { return __float2bfloat16(x); }
+
+// 8 floats -> 8 bf16 in one 16-byte word
+R9K_DEVINL uint4 pack8_bf16(const float* x) {
+  uint4 r;
+  __nv_bfloat162 h[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(x[2 * i], x[2 * i + 1]);
+  r.x = *reinterpret_cast<uint32_t*>(&h[0]);
+  r.y = *reinterpret_cast<uint32_t*>(&h[1]);
+  r.z = *reinterpret_cast<uint32_t*>(&h[2]);
+  r.w = *reinterpret_cast<uint32_t*>(&h[3]);
+  return r;
+}
+// 16 consecutive elements [e0, e0 + 16) of row r of a 128x128 bf16 K-major operand (128-byte swizzle)
+R9K_DEVINL void st_tile16(uint8_t* tile, int r, int e0, const float* x) {
+  uint8_t* reg = tile + (e0 >> 6) * gch::REG;
+  const int c0 = (e0 & 63) >> 3;
+#pragma unroll
+  for (int i = 0; i < 2; ++i)
+    *reinterpret_cast<uint4*>(reg + r * 128 + (((c0 + i) ^ (r & 7)) << 4)) = pack8_bf16(x + 8 * i);
+}
+// 128x128x128 bf16 MMA, both operands K-major 128-byte-swizzled tiles: d (+)= a b^T
+R9K_DEVINL void mma_tile(uint32_t d, uint32_t a, uint32_t b, uint32_t accumulate) {
+  constexpr uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, 128);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t off = (uint32_t)((k >> 2) * gch::REG + (k & 3) * 32);
+    mma_f16_ss(d, sdesc_k_sw128(a + off), sdesc_k_sw128(b + off), idesc, (accumulate || k > 0) ? 1u : 0u);
+  }
+}
+
+struct ChunkArgs {
+  const float* q;      // [T, Hk, 128] (l2-normalised, scaled)
+  const float* k;      // [T, Hk, 128] (l2-normalised)
+  const float* v;      // [T, Hv, 128]
+  const float* g;      // [T, Hv] log decay
+  const float* beta;   // [T, Hv]
+  int Hk, Hv;
+  const int32_t* ctab;  // [chunks][3]: first token, tokens (1..128), sequence row
+  int nchunks;
+  // phase 1 outputs / phase 2 operands, per (chunk, head) at index (chunk * Hv + head)
+  __nv_bfloat16* w;    // [.., 128 tokens, 128 dk]
+  __nv_bfloat16* qg;   // gamma q [.., 128 tokens, 128 dk]
+  __nv_bfloat16* khT;  // (gamma_C / gamma k)^T [.., 128 dk, 128 tokens]
+  __nv_bfloat16* p;    // [.., 128 t, 128 j]
+  float* uT;           // U^T [.., 128 dv, 128 tokens]
+  float* gC;           // gamma_C [..]
+  // phase 2
+  const int32_t* seq_chunk0;  // [S + 1]: chunk range of each sequence
+  const int32_t* seq_slot;
+  const int32_t* seq_has_state;
+  int write_state;
+  float* o;            // [T, Hv, 128]
+  int* status;
+  uint64_t timeout_ns;
+};
+
+// ------------------------------------------------------------------------------------------------
+// Phase 1: grid (chunks, Hv), 128 threads (thread t = token t, or dim t for the transposed tiles)
+// ------------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const ChunkArgs a) {
+  using namespace gch;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* Kt = smem + P1_KT;
+  uint8_t* Qt = smem + P1_QT;
+  float* Ls = reinterpret_cast<float*>(smem + P1_L);
+  float* Ts = reinterpret_cast<float*>(smem + P1_T);
+  float* Xs = reinterpret_cast<float*>(smem + P1_X);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + P1_BAR);
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P1_BAR + 16);
+  __shared__ float sgc[C], sb[C], sgam[C];
+  __shared__ float swsum[4];
+  const int cid = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int t0 = a.ctab[3 * cid], n = a.ctab[3 * cid + 1];
+  const int kh = h / (a.Hv / a.Hk);
+  const int64_t oidx = (int64_t)cid * a.Hv + h;
+  pdl_wait();
+  if (tid == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_holder, 256);
+    tmem_relinquish();
+  }
+  // ---- k, q rows (token t) as bf16 operands; g, beta
+  {
+    const int t = tid;
+    float x[16];
+    for (int part = 0; part < 2; ++part) {
+      const float* src = (part == 0 ? a.k : a.q) + ((int64_t)(t0 + t) * a.Hk + kh) * D;
+      uint8_t* dst = part == 0 ? Kt : Qt;
+#pragma unroll 1
+      for (int e = 0; e < D; e += 16) {
+        if (t < n) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4) {
+            const float4 f = *reinterpret_cast<const float4*>(src + e + i);
+            x[i] = f.x; x[i + 1] = f.y; x[i + 2] = f.z; x[i + 3] = f.w;
+          }
+        } else {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) x[i] = 0.f;
+        }
+        st_tile16(dst, t, e, x);
+      }
+    }
+    const float gv = t < n ? a.g[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+    sb[t] = t < n ? a.beta[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+    // inclusive prefix sum of g over the chunk (warp scans + warp offsets)
+    float s = gv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, s, o);
+      if (lane >= o) s += y;
+    }
+    if (lane == 31) swsum[warp] = s;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) s += swsum[w];
+    sgc[t] = s;
+    sgam[t] = __expf(s);
+  }
+  fence_proxy_async();  // the operand tiles were written by threads; the tensor cores read them
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_holder;
+  if (tid == 0) {
+    mma_tile(tb, smem_u32(Kt), smem_u32(Kt), 0);        // KK^T  -> cols [0, 128)
+    mma_tile(tb + 128, smem_u32(Qt), smem_u32(Kt), 0);  // QK^T  -> cols [128, 256)
+    tc_commit(bar);
+  }
+  const bool ok0 = mbar_wait(bar, 0, a.timeout_ns);
+  if (!ok0) report_error(a.status, kErrMbarTimeout, 600, 0);
+  tc_fence_after();
+  const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+  // ---- L and P rows (thread = token t)
+  {
+    const int t = tid;
+    const float gct = sgc[t], bt = sb[t];
+    float* prow_f = Ts + t * LS;  // P row staged in the (still unused) T buffer
+#pragma unroll 1
+    for (int j0 = 0; j0 < C; j0 += 16) {
+      float kk[16], qk[16];
+      if (ok0) {
+        tmem_ld16(trow + j0, kk);
+        tmem_ld16(trow + 128 + j0, qk);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) kk[i] = qk[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = j0 + i;
+        const float dec = __expf(fminf(gct - sgc[j], 0.f));
+        Ls[t * LS + j] = (j < t && t < n) ? bt * dec * kk[i] : 0.f;
+        prow_f[j] = (j <= t && t < n) ? dec * qk[i] : 0.f;
+      }
+    }
+    // P row t and gamma q row t to global (bf16, row-major tiles)
+    __nv_bfloat16* pd = a.p + (oidx * C + t) * C;
+    __nv_bfloat16* qd = a.qg + (oidx * C + t) * D;
+    const float* qs = a.q + ((int64_t)(t0 + t) * a.Hk + kh) * D;
+    const float gam = t < n ? sgam[t] : 0.f;
+#pragma unroll 1
+    for (int e = 0; e < C; e += 8) {
+      float x[8], y[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        x[i] = prow_f[e + i];
+        y[i] = t < n ? gam * qs[e + i] : 0.f;
+      }
+      *reinterpret_cast<uint4*>(pd + e) = pack8_bf16(x);
+      *reinterpret_cast<uint4*>(qd + e) = pack8_bf16(y);
+    }
+  }
+  __syncthreads();
+  // ---- T = (I + L)^-1, blocks of 16 rows: diagonal blocks by forward substitution (thread = column
+  // of its block), then block row i from X = L[i, <i] T[<i, <i] and T[i, <i] = -T_ii X
+  {
+    const int bi = tid >> 4, cc = tid & 15, base = bi * 16;
+    float tcol[16];
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < r; ++j) acc += Ls[(base + r) * LS + base + j] * tcol[j];
+      tcol[r] = r < cc ? 0.f : (r == cc ? 1.f : -acc);
+    }
+#pragma unroll
+    for (int r = 0; r < 16; ++r) Ts[(base + r) * LS + base + cc] = tcol[r];
+    // zero the strictly upper blocks (rows of block bi, columns of later blocks)
+    for (int c2 = base + 16; c2 < C; ++c2) Ts[(base + cc) * LS + c2] = 0.f;
+  }
+  __syncthreads();
+#pragma unroll 1
+  for (int i = 1; i < 8; ++i) {
+    const int r = tid & 15, cg = tid >> 4;  // row of block i, column group (columns cg, cg + 8, ...)
+    const int rowL = (16 * i + r) * LS;
+    for (int c = cg; c < 16 * i; c += 8) {
+      float acc = 0.f;
+      for (int kk = c; kk < 16 * i; ++kk) acc += Ls[rowL + kk] * Ts[kk * LS + c];
+      Xs[r * LS + c] = acc;
+    }
+    __syncthreads();
+    for (int c = cg; c < 16 * i; c += 8) {
+      float acc = 0.f;
+#pragma unroll
+      for (int m = 0; m < 16; ++m) acc += Ts[(16 * i + r) * LS + 16 * i + m] * Xs[m * LS + c];
+      Ts[(16 * i + r) * LS + c] = -acc;  // T_ii[r][m] is zero for m > r
+    }
+    __syncthreads();
+  }
+  // ---- T (bf16 operand, rows t) into the L buffer; beta v^T and beta gamma k^T (rows = dim) into Kt/Qt
+  uint8_t* Tt = smem + P1_L;
+  {
+    float x[16];
+    const int t = tid;
+    // T rows: read the whole row first (the bf16 tile overlaps the fp32 L rows of other threads only
+    // after the barrier below, so stage through registers row by row)
+    __syncthreads();
+#pragma unroll 1
+    for (int e = 0; e < C; e += 16) {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = Ts[t * LS + e + i];
+      st_tile16(Tt, t, e, x);
+    }
+    const int d = tid;
+#pragma unroll 1
+    for (int e = 0; e < C; e += 16) {
+      float y[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int j = e + i;
+        const bool in = j < n;
+        x[i] = in ? sb[j] * a.v[((int64_t)(t0 + j) * a.Hv + h) * D + d] : 0.f;
+        y[i] = in ? sb[j] * sgam[j] * a.k[((int64_t)(t0 + j) * a.Hk + kh) * D + d] : 0.f;
+      }
+      st_tile16(Kt, d, e, x);
+      st_tile16(Qt, d, e, y);
+    }
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (tid == 0) {
+    mma_tile(tb, smem_u32(Tt), smem_u32(Kt), 0);        // U = T (beta v)        -> cols [0, 128)
+    mma_tile(tb + 128, smem_u32(Tt), smem_u32(Qt), 0);  // W = T (beta gamma k)  -> cols [128, 256)
+    tc_commit(bar);
+  }
+  const bool ok1 = mbar_wait(bar, 1, a.timeout_ns);
+  if (!ok1) report_error(a.status, kErrMbarTimeout, 601, 0);
+  tc_fence_after();
+  {
+    const int t = tid;
+    float* ut = a.uT + oidx * D * C;
+    __nv_bfloat16* wd = a.w + (oidx * C + t) * D;
+#pragma unroll 1
+    for (int e = 0; e < D; e += 16) {
+      float u[16], w[16];
+      if (ok1) {
+        tmem_ld16(trow + e, u);
+        tmem_ld16(trow + 128 + e, w);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) u[i] = w[i] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) ut[(int64_t)(e + i) * C + t] = u[i];  // U^T[d][t]: coalesced over t
+      *reinterpret_cast<uint4*>(wd + e) = pack8_bf16(w);
+      *reinterpret_cast<uint4*>(wd + e + 8) = pack8_bf16(w + 8);
+    }
+    // K-hat^T[d][t] = gamma_C / gamma_t k[t][d] (row d, thread = d)
+    const int d = tid;
+    const float gcl = sgc[n - 1];
+    __nv_bfloat16* kd = a.khT + (oidx * D + d) * C;
+#pragma unroll 1
+    for (int e = 0; e < C; e += 8) {
+      float x[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int j = e + i;
+        x[i] = j < n ? __expf(fminf(gcl - sgc[j], 0.f)) * a.k[((int64_t)(t0 + j) * a.Hk + kh) * D + d] : 0.f;
+      }
+      *reinterpret_cast<uint4*>(kd + e) = pack8_bf16(x);
+    }
+    if (tid == 0) a.gC[oidx] = __expf(gcl);
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tb, 256);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// Phase 2: grid (sequences, Hv), 160 threads: warps 0-3 epilogue (thread n = state column n, TMEM lane
+// n), warp 4 lane 0 issues the MMAs. Epilogue thread 0 issues the TMA loads of the operand tiles.
+// ------------------------------------------------------------------------------------------------
+template <typename ST>
+__global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_constant__ CUtensorMap tmW,
+                                                                const __grid_constant__ CUtensorMap tmQ,
+                                                                const __grid_constant__ CUtensorMap tmK,
+                                                                const __grid_constant__ CUtensorMap tmP,
+                                                                ST* __restrict__ state, const ChunkArgs a) {
+  using namespace gch;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* St = smem + P2_S;
+  uint8_t* Dt = smem + P2_D;
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + P2_BAR);  // W, gamma q landed
+  uint64_t* full_b = full_a + 1;                                   // K-hat^T, P landed
+  uint64_t* mma1 = full_a + 2;                                     // MMA1 + MMA2 done
+  uint64_t* mma2 = full_a + 3;                                     // MMA3 + MMA4 done
+  uint64_t* s_ready = full_a + 4;                                  // S^T operand written (128 arrivals)
+  uint64_t* d_ready = full_a + 5;                                  // Delta^T operand written, S scaled
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P2_BAR + 64);
+  __shared__ volatile int s_abort;
+  const int s = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int c0 = a.seq_chunk0[s], c1 = a.seq_chunk0[s + 1];
+  const int slot = a.seq_slot[s];
+  if (tid == 0) {
+    mbar_init(full_a, 1);
+    mbar_init(full_b, 1);
+    mbar_init(mma1, 1);
+    mbar_init(mma2, 1);
+    mbar_init(s_ready, 128);
+    mbar_init(d_ready, 128);
+    fence_mbar_init();
+    s_abort = 0;
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmK);
+    prefetch_tmap(&tmP);
+  }
+  if (warp == 4) {
+    tmem_alloc(tmem_holder, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tb = *tmem_holder;
+  constexpr uint32_t DACC = 0, OACC = 128, SM = 256;
+  pdl_wait();  // phase 1 wrote the operands
+  auto load_a = [&](int c) {
+    const int row = (c * a.Hv + h) * C;
+    mbar_arrive_expect_tx(full_a, 2 * TILE);
+    tma_load_2d(smem + P2_W, &tmW, full_a, 0, row);
+    tma_load_2d(smem + P2_W + REG, &tmW, full_a, 64, row);
+    tma_load_2d(smem + P2_Q, &tmQ, full_a, 0, row);
+    tma_load_2d(smem + P2_Q + REG, &tmQ, full_a, 64, row);
+  };
+  auto load_b = [&](int c) {
+    const int row = (c * a.Hv + h) * C;
+    mbar_arrive_expect_tx(full_b, 2 * TILE);
+    tma_load_2d(smem + P2_K, &tmK, full_b, 0, row);
+    tma_load_2d(smem + P2_K + REG, &tmK, full_b, 64, row);
+    tma_load_2d(smem + P2_P, &tmP, full_b, 0, row);
+    tma_load_2d(smem + P2_P + REG, &tmP, full_b, 64, row);
+  };
+  if (warp == 4) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      for (int c = c0; c < c1; ++c) {
+        const uint32_t ph = (uint32_t)((c - c0) & 1);
+        if (!mbar_wait(full_a, ph, a.timeout_ns) || !mbar_wait(s_ready, ph, a.timeout_ns)) {
+          report_error(a.status, kErrMbarTimeout, 610, c);
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        mma_tile(tb + DACC, smem_u32(St), smem_u32(smem + P2_W), 0);
+        mma_tile(tb + OACC, smem_u32(St), smem_u32(smem + P2_Q), 0);
+        tc_commit(mma1);
+        if (!mbar_wait(d_ready, ph, a.timeout_ns) || !mbar_wait(full_b, ph, a.timeout_ns)) {
+          report_error(a.status, kErrMbarTimeout, 611, c);
+          s_abort = 1;
+          break;
+        }
+        tc_fence_after();
+        mma_tile(tb + SM, smem_u32(Dt), smem_u32(smem + P2_K), 1);
+        mma_tile(tb + OACC, smem_u32(Dt), smem_u32(smem + P2_P), 1);
+        tc_commit(mma2);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ epilogue warps ------------------------------
+    const int nrow = tid;  // state column n = TMEM lane n
+    const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+    ST* Sp = state + (((int64_t)slot * a.Hv + h) * D + nrow) * D;  // S^T row n (= state column n)
+    const bool hs = a.seq_has_state[s] != 0;
+    if (tid == 0 && c1 > c0) {
+      load_a(c0);
+      load_b(c0);
+    }
+    // initial state: TMEM master (fp32) and the bf16 operand
+#pragma unroll 1
+    for (int e = 0; e < D; e += 16) {
+      float x[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) x[i] = hs ? to_float(Sp[e + i]) : 0.f;
+      tmem_st16(trow + SM + e, x);
+      st_tile16(St, nrow, e, x);
+    }
+    tmem_st_wait();
+    fence_proxy_async();
+    tc_fence_before();
+    mbar_arrive(s_ready);
+    bool ok = true;
+    for (int c = c0; c < c1 && ok; ++c) {
+      const uint32_t ph = (uint32_t)((c - c0) & 1);
+      const int t0 = a.ctab[3 * c], n = a.ctab[3 * c + 1];
+      const int64_t oidx = (int64_t)c * a.Hv + h;
+      const float* ur = a.uT + (oidx * D + nrow) * C;  // U^T row n
+      const float gC = a.gC[oidx];
+      // ---- E1: Delta^T = U^T - S^T W^T; S^T *= gamma_C
+      ok = __all_sync(0xffffffffu, mbar_wait(mma1, ph, a.timeout_ns)) && !s_abort;
+      if (!ok) break;
+      tc_fence_after();
+      if (tid == 0 && c + 1 < c1) load_a(c + 1);  // W / gamma q buffers are free again
+#pragma unroll 1
+      for (int e = 0; e < C; e += 16) {
+        float x[16], sm[16];
+        tmem_ld16(trow + DACC + e, x);
+        tmem_ld16(trow + SM + e, sm);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; i += 4) {
+          const float4 u4 = *reinterpret_cast<const float4*>(ur + e + i);
+          x[i] = u4.x - x[i]; x[i + 1] = u4.y - x[i + 1]; x[i + 2] = u4.z - x[i + 2]; x[i + 3] = u4.w - x[i + 3];
+        }
+#pragma unroll
+        for (int i = 0; i < 16; ++i) sm[i] *= gC;
+        st_tile16(Dt, nrow, e, x);
+        tmem_st16(trow + SM + e, sm);
+      }
+      tmem_st_wait();
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(d_ready);
+      // ---- E2: O^T -> o; S^T -> next operand
+      ok = __all_sync(0xffffffffu, mbar_wait(mma2, ph, a.timeout_ns)) && !s_abort;
+      if (!ok) break;
+      tc_fence_after();
+      if (tid == 0 && c + 1 < c1) load_b(c + 1);
+#pragma unroll 1
+      for (int e = 0; e < C; e += 16) {
+        float x[16];
+        tmem_ld16(trow + OACC + e, x);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (e + i < n) a.o[((int64_t)(t0 + e + i) * a.Hv + h) * D + nrow] = x[i];
+      }
+      if (c + 1 < c1) {
+#pragma unroll 1
+        for (int e = 0; e < D; e += 16) {
+          float x[16];
+          tmem_ld16(trow + SM + e, x);
+          tmem_ld_wait();
+          st_tile16(St, nrow, e, x);
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        mbar_arrive(s_ready);
+      }
+    }
+    if (!ok) report_error(a.status, kErrMbarTimeout, 612, 0);
+    if (ok && a.write_state) {
+#pragma unroll 1
+      for (int e = 0; e < D; e += 16) {
+        float x[16];
+        tmem_ld16(trow + SM + e, x);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) Sp[e + i] = from_float<ST>(x[i]);
+      }
+    }
+  }
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tb, 512);
+  }
+}
+
+// ------------------------------------------------------------------------------------------------
+// host
+// ------------------------------------------------------------------------------------------------
+// q, k [T, Hk, 128], v [T, Hv, 128], g / beta [T, Hv] fp32 (gdn_conv_prep outputs); ctab [chunks, 3]
+// int32 (first token, tokens, sequence); seq_chunk0 [S + 1] int32; scratch: w, qg, khT, p bf16
+// [chunks * Hv * 128, 128], uT fp32 [chunks * Hv * 128, 128], gC fp32 [chunks * Hv]; o [T, Hv, 128].
+void gdn_chunked(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
+                 torch::Tensor state, torch::Tensor ctab, torch::Tensor seq_chunk0, torch::Tensor seq_slot,
+                 torch::Tensor seq_has_state, bool write_state, torch::Tensor w, torch::Tensor qg, torch::Tensor khT,
+                 torch::Tensor p, torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status) {
+  using namespace gch;
+  const int64_t nchunks = ctab.size(0), S = seq_slot.size(0);
+  if (nchunks == 0 || S == 0) return;
+  const int Hk = (int)q.size(1), Hv = (int)v.size(1);
+  TORCH_CHECK(q.size(2) == D && v.size(2) == D && Hv % Hk == 0, "gdn_chunked: head dim 128, Hv % Hk");
+  TORCH_CHECK(state.size(1) == Hv && state.size(2) == D && state.size(3) == D, "gdn_chunked: state [slots, Hv, 128, 128]");
+  TORCH_CHECK(ctab.dtype() == torch::kInt32 && ctab.size(1) == 3 && seq_chunk0.numel() == S + 1, "gdn_chunked: tables");
+  const int64_t rows = nchunks * Hv * C;
+  TORCH_CHECK(w.numel() >= rows * D && qg.numel() >= rows * D && khT.numel() >= rows * C && p.numel() >= rows * C &&
+                  uT.numel() >= rows * C && gC.numel() >= nchunks * Hv,
+              "gdn_chunked: scratch too small");
+  for (auto* t : {&q, &k, &v, &g, &beta, &o}) TORCH_CHECK(t->is_contiguous() && t->dtype() == torch::kFloat32, "gdn_chunked: fp32 inputs");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  ChunkArgs a = {};
+  a.q = q.data_ptr<float>(); a.k = k.data_ptr<float>(); a.v = v.data_ptr<float>();
+  a.g = g.data_ptr<float>(); a.beta = beta.data_ptr<float>();
+  a.Hk = Hk; a.Hv = Hv;
+  a.ctab = ctab.data_ptr<int32_t>(); a.nchunks = (int)nchunks;
+  a.w = reinterpret_cast<__nv_bfloat16*>(w.data_ptr()); a.qg = reinterpret_cast<__nv_bfloat16*>(qg.data_ptr());
+  a.khT = reinterpret_cast<__nv_bfloat16*>(khT.data_ptr()); a.p = reinterpret_cast<__nv_bfloat16*>(p.data_ptr());
+  a.uT = uT.data_ptr<float>(); a.gC = gC.data_ptr<float>();
+  a.seq_chunk0 = seq_chunk0.data_ptr<int32_t>(); a.seq_slot = seq_slot.data_ptr<int32_t>();
+  a.seq_has_state = seq_has_state.data_ptr<int32_t>(); a.write_state = write_state ? 1 : 0;
+  a.o = o.data_ptr<float>();
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 2000000000ull;
+  TORCH_CHECK(ensure_smem_attr((const void*)gdn_chunk_prep_kernel, P1_SMEM) == cudaSuccess, "gdn_chunked: smem");
+  TORCH_CHECK(launch_pdl(gdn_chunk_prep_kernel, dim3((unsigned)nchunks, (unsigned)Hv), dim3(128), (size_t)P1_SMEM, st, a) ==
+                  cudaSuccess,
+              "gdn_chunk_prep launch");
+  const CUtensorMap tW = tmap_bf16_kmajor(w.data_ptr(), rows, D, D, 128);
+  const CUtensorMap tQ = tmap_bf16_kmajor(qg.data_ptr(), rows, D, D, 128);
+  const CUtensorMap tK = tmap_bf16_kmajor(khT.data_ptr(), rows, C, C, 128);
+  const CUtensorMap tP = tmap_bf16_kmajor(p.data_ptr(), rows, C, C, 128);
+#define R9K_GCS(ST_T)                                                                                             \
+  {                                                                                                               \
+    TORCH_CHECK(ensure_smem_attr((const void*)gdn_chunk_scan_kernel<ST_T>, P2_SMEM) == cudaSuccess, "gdn_chunked"); \
+    TORCH_CHECK(launch_pdl(gdn_chunk_scan_kernel<ST_T>, dim3((unsigned)S, (unsigned)Hv), dim3(160), (size_t)P2_SMEM,  \
+                           st, tW, tQ, tK, tP, reinterpret_cast<ST_T*>(state.data_ptr()), a) == cudaSuccess,         \
+                "gdn_chunk_scan launch");                                                                         \
+  }
+  if (state.dtype() == torch::kFloat32) R9K_GCS(float) else R9K_GCS(__nv_bfloat16)
+#undef R9K_GCS
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+}  // namespace r9k

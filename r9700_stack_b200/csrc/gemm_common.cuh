@@ -47,10 +47,19 @@ struct GemmArgs {
   int cluster_k;
   // tuning trace (null unless set with gemm_trace): per CTA, %globaltimer at kernel entry, set-up
   // done, producer past the programmatic wait, first stage landed, last MMA issued, accumulator
-  // complete (epilogue), CTA done
+  // complete (epilogue), CTA done (epilogue thread; slot 7: the same seen by thread 0); cluster split-K:
+  // partial parked, first cluster barrier passed, reduced + stored, second barrier passed
   unsigned long long* trace;
 };
-enum { kTrEntry = 0, kTrSetup, kTrPdl, kTrFirst, kTrIssued, kTrAcc, kTrDone, kTrN = 8 };
+enum { kTrEntry = 0, kTrSetup, kTrPdl, kTrFirst, kTrIssued, kTrAcc, kTrDone, kTrDone0, kTrParked, kTrSync1,
+       kTrReduced, kTrSync2, kTrN = 12 };
+
+R9K_DEVINL float4 ld_dsmem_v4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr) : "memory");
+  return v;
+}
 
 R9K_DEVINL float ld_dsmem_f32(uint32_t addr) {
   float v;

@@ -281,10 +281,22 @@ __global__ void __launch_bounds__(192, 1)
         const int tok = n0 + t;
         if (tok >= args.M) break;
         float g = 0.f, u = 0.f;
-        for (int k = 0; k < S; ++k) {  // fixed split order: deterministic
-          const uint32_t rb = mapa_shared(base, (uint32_t)k);
-          g += ld_dsmem_f32_nvf4(rb + (uint32_t)((t * 128 + row_local) * 4));
-          if (DUAL) u += ld_dsmem_f32_nvf4(rb + (uint32_t)((BN * 128 + t * 128 + row_local) * 4));
+        // every split's value requested first (all in flight together), then summed in split order
+        float vg[8], vu[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k < S) {
+            const uint32_t rb = mapa_shared(base, (uint32_t)k);
+            vg[k] = ld_dsmem_f32_nvf4(rb + (uint32_t)((t * 128 + row_local) * 4));
+            if (DUAL) vu[k] = ld_dsmem_f32_nvf4(rb + (uint32_t)((BN * 128 + t * 128 + row_local) * 4));
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+          if (k < S) {
+            g += vg[k];
+            if (DUAL) u += vu[k];
+          }
         }
         if (row < args.N) {
           const float y = EPI == NVF4_EPI_SWIGLU ? silu_f(g * args.alpha) * (u * args.alpha2) : g * args.alpha;

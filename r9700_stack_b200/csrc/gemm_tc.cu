@@ -100,6 +100,8 @@ __global__ void __launch_bounds__(192, 1)
                    int* __restrict__ ws_cnt) {
   using C = GemmCfg<KIND, BN, DUAL, NP, NC, UNPACK, MT>;
   static_assert(MT == 1 || (!UNPACK && EPI != EPI_PUSH), "multi-tile CTAs: plain loads, local epilogues");
+  constexpr int kPartStride = BN + 4;  // floats per parked row (cluster split-K): 16-byte rows, no bank conflicts
+  static_assert(C::NA * 128 * kPartStride * 4 <= C::OFF_BAR, "parked partials fit in the idle operand ring");
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* l_full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -403,8 +405,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       if constexpr (EPI == EPI_PUSH) flush_push();
     } else if (args.cluster_k) {
-      // cluster split-K: park this split's fp32 partial [NA][BN][128] in this CTA's shared memory (the
-      // operand ring is idle once the accumulator is complete); the splits meet below
+      // cluster split-K: park this split's fp32 partial [NA][128 rows][BN + 4] in this CTA's shared
+      // memory (the operand ring is idle once the accumulator is complete; a row's tokens are
+      // contiguous, so the peers read them as 16-byte vectors); the splits meet below
       float* mypart = reinterpret_cast<float*>(smem);
 #pragma unroll 1
       for (int c = 0; c < BN; c += 16) {
@@ -415,10 +418,12 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll
           for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
         }
+        float4* pg = reinterpret_cast<float4*>(mypart + row_local * kPartStride + c);
+        float4* pu = reinterpret_cast<float4*>(mypart + 128 * kPartStride + row_local * kPartStride + c);
 #pragma unroll
-        for (int t = 0; t < 16; ++t) {
-          mypart[(c + t) * 128 + row_local] = g[t];
-          if (DUAL) mypart[BN * 128 + (c + t) * 128 + row_local] = u[t];
+        for (int j = 0; j < 4; ++j) {
+          pg[j] = make_float4(g[4 * j], g[4 * j + 1], g[4 * j + 2], g[4 * j + 3]);
+          if (DUAL) pu[j] = make_float4(u[4 * j], u[4 * j + 1], u[4 * j + 2], u[4 * j + 3]);
         }
       }
     } else if (ok) {
@@ -455,6 +460,8 @@ __global__ void __launch_bounds__(192, 1)
           float g[16], u[16];
 #pragma unroll
           for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
+          // (unrolled so several splits' loads are in flight together; the sum stays in split order)
+#pragma unroll 2
           for (int r = 0; r < S; ++r) {
             const float* src = base + (int64_t)r * C::TILE_F;
 #pragma unroll
@@ -473,45 +480,70 @@ __global__ void __launch_bounds__(192, 1)
   }
 
   if (S > 1 && args.cluster_k) {
-    // every split of the tile parked its partial; each CTA of the cluster now owns the tokens
-    // t == its cluster rank (mod S) of the tile, sums the S partials over distributed shared memory in
-    // rank order (the same order for every token: deterministic) and runs the epilogue for them
+    // every split of the tile parked its partial; CTA r of the cluster owns the contiguous token slice
+    // [r BN / S, (r + 1) BN / S) of the tile: for each 4-token group it needs, it requests the group
+    // from all S splits at once (16-byte distributed-shared-memory loads, all in flight together),
+    // then sums them in split order (deterministic) and runs the epilogue for its tokens
+    if (tr && threadIdx.x == 64) tr[kTrParked] = globaltimer_ns();
     cluster_sync();
+    if (tr && threadIdx.x == 64) tr[kTrSync1] = globaltimer_ns();
     if (warp >= 2) {
       const int row_local = (warp & 3) * 32 + lane;
       const uint32_t me = cluster_ctarank();
       const uint32_t my_base = smem_u32(smem);
       GemmArgs ea = args;
       ea.M = m_valid;
+      const int tpc = BN / S;
+      const int ta = (int)me * tpc, tb = ta + tpc;
 #pragma unroll 1
-      for (int c = 0; c < BN; c += 16) {
+      for (int c = ta & ~15; c < tb; c += 16) {
         uint32_t tmask = 0;
 #pragma unroll
         for (int t = 0; t < 16; ++t)
-          if ((uint32_t)((c + t) % S) == me && n0 + c + t < m_valid) tmask |= 1u << t;
+          if (c + t >= ta && c + t < tb && n0 + c + t < m_valid) tmask |= 1u << t;
         if (tmask == 0) continue;
         float g[16], u[16];
 #pragma unroll
         for (int t = 0; t < 16; ++t) g[t] = u[t] = 0.f;
-#pragma unroll 1
-        for (int k = 0; k < S; ++k) {
-          const uint32_t rb = mapa_shared(my_base, (uint32_t)k);
 #pragma unroll
-          for (int t = 0; t < 16; ++t) {
-            if (!((tmask >> t) & 1u)) continue;
-            g[t] += ld_dsmem_f32(rb + (uint32_t)(((c + t) * 128 + row_local) * 4));
-            if (DUAL) u[t] += ld_dsmem_f32(rb + (uint32_t)((BN * 128 + (c + t) * 128 + row_local) * 4));
+        for (int j = 0; j < 4; ++j) {
+          if (((tmask >> (4 * j)) & 0xFu) == 0) continue;
+          const uint32_t off = (uint32_t)((row_local * kPartStride + c + 4 * j) * 4);
+          constexpr int KB = DUAL ? 2 : 4;  // splits requested per batch (bounded registers)
+#pragma unroll 1
+          for (int k0 = 0; k0 < S; k0 += KB) {
+            float4 vg[KB], vu[KB];
+#pragma unroll
+            for (int k = 0; k < KB; ++k) {
+              if (k0 + k < S) {
+                const uint32_t rb = mapa_shared(my_base, (uint32_t)(k0 + k)) + off;
+                vg[k] = ld_dsmem_v4(rb);
+                if (DUAL) vu[k] = ld_dsmem_v4(rb + 128u * kPartStride * 4u);
+              }
+            }
+#pragma unroll
+            for (int k = 0; k < KB; ++k) {
+              if (k0 + k < S) {
+                g[4 * j] += vg[k].x; g[4 * j + 1] += vg[k].y; g[4 * j + 2] += vg[k].z; g[4 * j + 3] += vg[k].w;
+                if (DUAL) {
+                  u[4 * j] += vu[k].x; u[4 * j + 1] += vu[k].y; u[4 * j + 2] += vu[k].z; u[4 * j + 3] += vu[k].w;
+                }
+              }
+            }
           }
         }
         epilogue_chunk<BN, DUAL, EPI>(ea, g, u, m0 + row_local, n0 + c, lane, nullptr, tmask);
       }
     }
+    if (tr && threadIdx.x == 64) tr[kTrReduced] = globaltimer_ns();
     cluster_sync();  // no CTA leaves while a peer may still read its partial
+    if (tr && threadIdx.x == 64) tr[kTrSync2] = globaltimer_ns();
   }
 
   tc_fence_before();
   __syncthreads();
-  if (tr && threadIdx.x == 0) tr[kTrDone] = globaltimer_ns();
+  if (tr && threadIdx.x == 64) tr[kTrDone] = globaltimer_ns();
+  if (tr && threadIdx.x == 0) tr[kTrDone0] = globaltimer_ns();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tbase, C::TMEM_COLS);

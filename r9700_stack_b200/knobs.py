@@ -22,8 +22,11 @@ _KNOBS = {
     "R9K_FP4_UNPACK": ("0", "0", "1: skinny fp4 GEMMs load packed bytes and expand them on chip"),
     "R9K_GDN_FUSED": ("1", "0", "1: decode steps run the one-kernel GDN layer core"),
     "R9K_GDN_PREFILL": ("chunked", "serial",
-                        "chunked: tensor-core chunked delta rule for long prefill; serial: token-serial recurrence"),
-    "R9K_GDN_CHUNK_MIN": ("256", "256", "shortest sequence that takes the chunked GDN prefill"),
+                        "chunked: prefill runs the tcgen05 chunked delta rule (WY form, 128-token chunks); serial: "
+                        "the token-serial recurrence"),
+    "R9K_GDN_CHUNK_MIN": ("256", "256", "fewest tokens in a step's longest sequence that take the chunked GDN prefill"),
+    "R9K_GDN_PREFETCH": ("0", "0", "1: decode steps prefetch each GDN layer's recurrent state into L2 during its in_proj GEMM "
+                         "(measured slower: 16-stream decode 2207 vs 2250 tok/s)"),
     "R9K_COMM": ("fused", "nccl", "fused: NVLink kernels fused into GEMMs / norms; nccl: every collective on NCCL"),
     "R9K_AR_MODE": ("ll", "pull", "ll: GEMM epilogue stores epoch-tagged partials into peers, consumer polls its own "
                     "memory; pull: consumer reads peers' partials; push: plain stores + per-tile flags"),

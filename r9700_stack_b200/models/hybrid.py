@@ -71,6 +71,8 @@ class StepMeta:
     host_max_ctx: int | None = None
     # prefill attention tile table (built once per step on first use, shared by every attention layer)
     attn_tiles: dict | None = None
+    # chunked-GDN tables of an eager prefill step (built on first use, shared by every GDN layer)
+    gdn_chunks: tuple | None = None
 
 
 class Workspace:
@@ -434,13 +436,17 @@ class HybridLM:
             assert T <= ws.spec_tokens, "verify batch exceeds the speculative buffers"
             sb = ws.spec[i]
         proj = (sb["proj"] if sb is not None else ws.proj)[:T]
+        ssm, conv = self.ssm[i], self.conv[i]
+        o = _ops()
+        decode = meta.write_state and T == meta.seq_start.shape[0] and knobs.get("R9K_GDN_FUSED") != "0"
+        if decode and knobs.get("R9K_GDN_PREFETCH") != "0":
+            # the state rows this step updates land in L2 while in_proj streams its weights
+            o.gdn_state_prefetch(ssm, conv, meta.seq_state_slot)
         self._linear(ws.act.narrow(T), ws.norm_out[:T], lay["w_in"], proj)
         z_off = 2 * hk * d + hv * d
         b_off = z_off + hv * d
         a_off = b_off + hv
-        ssm, conv = self.ssm[i], self.conv[i]
-        o = _ops()
-        if meta.write_state and T == meta.seq_start.shape[0] and knobs.get("R9K_GDN_FUSED") != "0":
+        if decode:
             # decode: every sequence has one token -> one fused kernel per layer
             o.gdn_decode_fused(proj, hk, hv, z_off, b_off, a_off, lay["conv_w"], conv, ssm, meta.seq_state_slot,
                                meta.seq_has_state, lay["A_log"], lay["dt_bias"], lay["gdn_norm"], c.rms_eps,
@@ -453,14 +459,51 @@ class HybridLM:
                         ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T])
         if meta.write_state:
             o.gdn_conv_state_update(proj, conv, meta.seq_state_slot, meta.seq_start, meta.seq_len, meta.seq_has_state)
-        o.gdn_recurrent(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, meta.seq_state_slot,
-                        meta.seq_start, meta.seq_len, meta.seq_has_state, meta.write_state, ws.go[:T])
+        if (sb is None and meta.write_state and meta.host_seqs and knobs.get("R9K_GDN_PREFILL") == "chunked"
+                and max(n for _, n in meta.host_seqs) >= knobs.get_int("R9K_GDN_CHUNK_MIN")):
+            # long prefill: the chunked delta rule on the tensor cores (same inputs and outputs)
+            ctab, c0, nch = self._gdn_chunk_tables(meta)
+            buf = self._gdn_chunk_scratch(ws, nch * hv * 128)
+            o.gdn_chunked(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, ctab, c0, meta.seq_state_slot,
+                          meta.seq_has_state, True, *buf, ws.go[:T], _status.status(self.device))
+        else:
+            o.gdn_recurrent(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, meta.seq_state_slot,
+                            meta.seq_start, meta.seq_len, meta.seq_has_state, meta.write_state, ws.go[:T])
         if self.mx:
             o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, None, ws.gdn_act.q[:T],
                                  ws.gdn_act.sf)
         else:
             o.gdn_out_norm_quant(ws.go[:T], proj, z_off, lay["gdn_norm"], c.rms_eps, ws.gdn_bf16[:T], None, None)
         return ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"]
+
+    def _gdn_chunk_tables(self, meta: StepMeta):
+        """(chunk table [chunks, 3] = first token, tokens, sequence; first chunk of each sequence [S + 1];
+        chunk count) for the chunked GDN prefill, 128 tokens per chunk, built once per step."""
+        if meta.gdn_chunks is not None and meta.gdn_chunks[0] is meta.host_seqs:
+            return meta.gdn_chunks[1:]
+        rows, first = [], [0]
+        for si, (t0, n) in enumerate(meta.host_seqs):
+            rows += [(t0 + j, min(128, n - j), si) for j in range(0, n, 128)]
+            first.append(len(rows))
+        host = torch.tensor(rows or [(0, 0, 0)], dtype=torch.int32).reshape(-1).pin_memory()
+        hf = torch.tensor(first, dtype=torch.int32).pin_memory()
+        ctab = host.to(self.device, non_blocking=True).view(-1, 3)[: len(rows)]
+        c0 = hf.to(self.device, non_blocking=True)
+        meta.gdn_chunks = (meta.host_seqs, ctab, c0, len(rows))
+        return ctab, c0, len(rows)
+
+    def _gdn_chunk_scratch(self, ws: Workspace, rows: int):
+        """Phase-1 outputs of the chunked GDN (W, gamma q, K-hat^T, P in bf16; U^T fp32; gamma_C), grown to
+        `rows` (chunks x value heads x 128) on demand; eager prefill steps only."""
+        buf = getattr(ws, "gdn_chunk_buf", None)
+        if buf is None or buf[0].shape[0] < rows:
+            cap = max(rows, 128 * 16)
+            dev = self.device
+            bf = lambda: torch.empty(cap, 128, dtype=torch.bfloat16, device=dev)
+            buf = (bf(), bf(), bf(), bf(), torch.empty(cap, 128, dtype=torch.float32, device=dev),
+                   torch.empty(cap // 128, dtype=torch.float32, device=dev))
+            ws.gdn_chunk_buf = buf
+        return buf
 
     def _ffn(self, lay, ws: Workspace, T: int):
         """Gate/up + SwiGLU (fused); returns the down projection's input and weight."""

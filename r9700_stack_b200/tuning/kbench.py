@@ -107,7 +107,7 @@ def bench_gemm(a) -> dict:
             f = lambda i: L.mx_linear(x, ws[i % nw], out=out)
     tr = None
     if getattr(a, "trace", False):
-        tr = torch.zeros(1 << 20, dtype=torch.int64, device="cuda")
+        tr = torch.zeros(12 << 16, dtype=torch.int64, device="cuda")
         torch.ops.r9k.gemm_trace(tr)
     us = _time(f, a.reps, a.warmup, graph=not a.eager)
     if tr is not None:
@@ -125,13 +125,14 @@ def bench_gemm(a) -> dict:
     return r
 
 
-TRACE_POINTS = ("entry", "setup", "pdl", "first", "issued", "acc", "done")
+TRACE_POINTS = ("entry", "setup", "pdl", "first", "issued", "acc", "done", "done_t0", "parked", "sync1", "reduced",
+                "sync2")
 
 
 def trace_summary(buf: torch.Tensor) -> dict:
-    """Per-phase timing of the last traced GEMM launch (gemm_trace stamps, 8 per CTA): each point's
+    """Per-phase timing of the last traced GEMM launch (gemm_trace stamps, 12 per CTA): each point's
     min / median / max over CTAs in us from the first CTA's entry, and the median of each phase."""
-    t = buf.view(-1, 8)[:, : len(TRACE_POINTS)].cpu()
+    t = buf.view(-1, 12)[:, : len(TRACE_POINTS)].cpu()
     t = t[t[:, 0] > 0]
     if t.numel() == 0:
         return {}
@@ -147,6 +148,11 @@ def trace_summary(buf: torch.Tensor) -> dict:
         if ok.any():
             d = (t[ok, i] - t[ok, i - 1]).double() / 1e3
             ph[f"{TRACE_POINTS[i - 1]}->{TRACE_POINTS[i]}"] = round(float(d.median()), 2)
+    for a, b in (("acc", "parked"), ("parked", "sync1"), ("sync1", "reduced"), ("reduced", "sync2"), ("sync2", "done")):
+        ia, ib = TRACE_POINTS.index(a), TRACE_POINTS.index(b)
+        ok = (t[:, ia] > 0) & (t[:, ib] > 0)
+        if ok.any():
+            ph[f"{a}->{b}"] = round(float(((t[ok, ib] - t[ok, ia]).double() / 1e3).median()), 2)
     out["phase_median_us"] = ph
     return out
 
@@ -242,6 +248,8 @@ def bench_gdn(a) -> dict:
 
     torch.manual_seed(0)
     S, Hk, Hv, D = a.S, a.Hk, a.Hv, 128
+    if a.prefill:
+        return _bench_gdn_prefill(a)
     C = 2 * Hk * D + Hv * D
     rows = C + Hv * D + 2 * Hv
     sdt = torch.float32 if a.state == "fp32" else torch.bfloat16
@@ -266,6 +274,43 @@ def bench_gdn(a) -> dict:
     status.check()
     return {"kernel": "gdn_decode_fused", "S": S, "Hk": Hk, "Hv": Hv, "state": a.state, "us": us,
             "weight_bytes": 2.0 * per, "flops": 0.0}
+
+
+def _bench_gdn_prefill(a) -> dict:
+    """The token-serial delta-rule recurrence over a prefill: one sequence of ``--prefill`` tokens,
+    Hv value heads (the conv / norm kernels around it are not included)."""
+    from .. import _native
+
+    T, Hk, Hv, D = a.prefill, a.Hk, a.Hv, 128
+    nrm = lambda x: x / x.norm(dim=-1, keepdim=True)
+    q = nrm(torch.randn(T, Hk, D, device="cuda")) * D ** -0.5
+    k = nrm(torch.randn(T, Hk, D, device="cuda"))
+    v = torch.randn(T, Hv, D, device="cuda")
+    g = -torch.rand(T, Hv, device="cuda") * 0.5
+    b = torch.rand(T, Hv, device="cuda")
+    sdt = torch.float32 if a.state == "fp32" else torch.bfloat16
+    st = torch.zeros(2, Hv, D, D, device="cuda", dtype=sdt)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32, device="cuda")
+    slot, s0, ln, hs = i32([1]), i32([0]), i32([T]), i32([0])
+    o = torch.empty(T, Hv, D, device="cuda")
+    ops = _native.ops()
+    if a.chunked:
+        from ..utils import status
+
+        rows = [(j, min(128, T - j), 0) for j in range(0, T, 128)]
+        ctab = torch.tensor(rows, dtype=torch.int32, device="cuda")
+        c0 = i32([0, len(rows)])
+        nr = len(rows) * Hv * 128
+        buf = [torch.empty(nr, 128, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
+        buf += [torch.empty(nr, 128, device="cuda"), torch.empty(len(rows) * Hv, device="cuda")]
+        stat = status.status(torch.device("cuda"))
+        f = lambda i: ops.gdn_chunked(q, k, v, g, b, st, ctab, c0, slot, hs, True, *buf, o, stat)
+    else:
+        f = lambda i: ops.gdn_recurrent(q, k, v, g, b, st, slot, s0, ln, hs, True, o)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    return {"kernel": "gdn_chunked_prefill" if a.chunked else "gdn_recurrent_prefill", "T": T, "Hk": Hk, "Hv": Hv,
+            "state": a.state, "us": us,
+            "us_per_token": us / T, "weight_bytes": 0.0, "flops": 6.0 * T * Hv * D * D}
 
 
 def bench_attn(a) -> dict:
@@ -382,6 +427,8 @@ def main(argv=None):
     gd.add_argument("--Hk", type=int, default=16)
     gd.add_argument("--Hv", type=int, default=48)
     gd.add_argument("--state", choices=["bf16", "fp32"], default="bf16")
+    gd.add_argument("--prefill", type=int, default=0, help="time the prefill recurrence over this many tokens")
+    gd.add_argument("--chunked", action="store_true", help="with --prefill: the tcgen05 chunked kernels")
     at = sub.add_parser("attn")
     at.add_argument("--S", type=int, default=16)
     at.add_argument("--ctx", type=int, default=8192)

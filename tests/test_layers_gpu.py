@@ -66,10 +66,10 @@ def test_paged_attention_matches_torch():
 def test_gdn_kernels_match_torch():
     torch.manual_seed(1)
     Hk, Hv, d, W = 2, 4, 128, 4
-    lens = [1, 5, 33]
-    has = [1, 0, 1]
-    nslots = 4
-    slots = [1, 2, 3]
+    lens = [1, 5, 33, 16]  # one token, a partial chunk, three chunks ending on one token, one whole chunk
+    has = [1, 0, 1, 1]
+    nslots = 5
+    slots = [1, 2, 3, 4]
     T = sum(lens)
     C = 2 * Hk * d + Hv * d
     proj_rows = C + Hv * d + 2 * Hv
