@@ -67,6 +67,7 @@ void ll_push(torch::Tensor x, torch::Tensor peers, int64_t rank, int64_t world, 
 void rmsnorm_quant(torch::Tensor x, c10::optional<torch::Tensor> res_in, c10::optional<torch::Tensor> res_out,
                    torch::Tensor w, double eps, bool plus_one, c10::optional<torch::Tensor> y,
                    c10::optional<torch::Tensor> q, c10::optional<torch::Tensor> sf);
+void swiglu_quant_mxfp8(torch::Tensor g, torch::Tensor u, torch::Tensor q, torch::Tensor sf);
 void quant_act_mxfp8(torch::Tensor x, torch::Tensor q, torch::Tensor sf);
 void quant_weight_mxfp4(torch::Tensor w, torch::Tensor packed, torch::Tensor sf, bool search);
 void quant_weight_mxfp8(torch::Tensor w, torch::Tensor q, torch::Tensor sf);
@@ -107,7 +108,8 @@ void attn_tc_prefill(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cac
 void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv, int64_t b_off, int64_t a_off,
                    torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor tok_slot, torch::Tensor tok_pos,
                    torch::Tensor tok_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor q_out,
-                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out);
+                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out,
+                   c10::optional<torch::Tensor> qkv_bf16);
 void gdn_conv_state_update(torch::Tensor proj, torch::Tensor conv_state, torch::Tensor seq_slot,
                            torch::Tensor seq_start, torch::Tensor seq_len, torch::Tensor seq_has_state);
 void gdn_spec_commit(torch::Tensor table, int64_t Hk, int64_t Hv, int64_t dv, int64_t C, int64_t W, int64_t ld,
@@ -174,10 +176,10 @@ void gdn_out_norm_quant(torch::Tensor o, torch::Tensor proj, int64_t z_off, torc
                         c10::optional<torch::Tensor> out_sf);
 void gdn_state_prefetch(torch::Tensor state, c10::optional<torch::Tensor> conv_state, torch::Tensor seq_slot);
 // gdn_chunk.cu
-void gdn_chunked(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
-                 torch::Tensor state, torch::Tensor ctab, torch::Tensor seq_chunk0, torch::Tensor seq_slot,
-                 torch::Tensor seq_has_state, bool write_state, torch::Tensor w, torch::Tensor qg, torch::Tensor khT,
-                 torch::Tensor p, torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status);
+void gdn_chunked(torch::Tensor qkv, torch::Tensor g, torch::Tensor beta, torch::Tensor state, torch::Tensor ctab,
+                 torch::Tensor seq_chunk0, torch::Tensor seq_slot, torch::Tensor seq_has_state, bool write_state,
+                 int64_t Hk, int64_t Hv, torch::Tensor w, torch::Tensor qg, torch::Tensor kh, torch::Tensor p,
+                 torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status);
 void gdn_decode_fused(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t z_off, int64_t b_off, int64_t a_off,
                       torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor state, torch::Tensor seq_slot,
                       torch::Tensor seq_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
@@ -223,6 +225,7 @@ TORCH_LIBRARY(r9k, m) {
         "int calls_per_step) -> ()");
   m.def("rmsnorm_quant(Tensor x, Tensor? res_in, Tensor(a!)? res_out, Tensor w, float eps, bool plus_one, "
         "Tensor(b!)? y, Tensor(c!)? q, Tensor(d!)? sf) -> ()");
+  m.def("swiglu_quant_mxfp8(Tensor g, Tensor u, Tensor(a!) q, Tensor(b!) sf) -> ()");
   m.def("quant_act_mxfp8(Tensor x, Tensor(a!) q, Tensor(b!) sf) -> ()");
   m.def("quant_weight_mxfp4(Tensor w, Tensor(a!) packed, Tensor(b!) sf, bool search) -> ()");
   m.def("quant_weight_mxfp8(Tensor w, Tensor(a!) q, Tensor(b!) sf) -> ()");
@@ -253,7 +256,8 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor(a!)? out, Tensor(b!)? out_q, Tensor(c!)? out_sf, Tensor(d!) status) -> ()");
   m.def("gdn_conv_prep(Tensor proj, int Hk, int Hv, int dk, int dv, int b_off, int a_off, Tensor conv_w, "
         "Tensor conv_state, Tensor tok_slot, Tensor tok_pos, Tensor tok_has_state, Tensor A_log, Tensor dt_bias, "
-        "Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!) g_out, Tensor(e!) beta_out) -> ()");
+        "Tensor(a!) q_out, Tensor(b!) k_out, Tensor(c!) v_out, Tensor(d!) g_out, Tensor(e!) beta_out, "
+        "Tensor(f!)? qkv_bf16=None) -> ()");
   m.def("gdn_conv_state_update(Tensor proj, Tensor(a!) conv_state, Tensor seq_slot, Tensor seq_start, "
         "Tensor seq_len, Tensor seq_has_state) -> ()");
   m.def("gdn_spec_commit(Tensor table, int Hk, int Hv, int dv, int C, int W, int ld, bool state_f32, "
@@ -301,9 +305,9 @@ TORCH_LIBRARY(r9k, m) {
   m.def("gdn_recurrent(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor seq_slot, "
         "Tensor seq_start, Tensor seq_len, Tensor seq_has_state, bool write_state, Tensor(b!)? o) -> ()");
   m.def("gdn_state_prefetch(Tensor state, Tensor? conv_state, Tensor seq_slot) -> ()");
-  m.def("gdn_chunked(Tensor q, Tensor k, Tensor v, Tensor g, Tensor beta, Tensor(a!) state, Tensor ctab, "
-        "Tensor seq_chunk0, Tensor seq_slot, Tensor seq_has_state, bool write_state, Tensor(b!) w, Tensor(c!) qg, "
-        "Tensor(d!) khT, Tensor(e!) p, Tensor(f!) uT, Tensor(g!) gC, Tensor(h!) o, Tensor(i!) status) -> ()");
+  m.def("gdn_chunked(Tensor qkv, Tensor g, Tensor beta, Tensor(a!) state, Tensor ctab, Tensor seq_chunk0, "
+        "Tensor seq_slot, Tensor seq_has_state, bool write_state, int Hk, int Hv, Tensor(b!) w, Tensor(c!) qg, "
+        "Tensor(d!) kh, Tensor(e!) p, Tensor(f!) uT, Tensor(g!) gC, Tensor(h!) o, Tensor(i!) status) -> ()");
   m.def("gdn_decode_fused(Tensor proj, int Hk, int Hv, int z_off, int b_off, int a_off, Tensor conv_w, "
         "Tensor(a!) conv_state, Tensor(b!) state, Tensor seq_slot, Tensor seq_has_state, Tensor A_log, "
         "Tensor dt_bias, Tensor norm_w, float eps, Tensor(c!)? out_q, Tensor(d!)? out_sf, Tensor(e!)? out_bf16) -> ()");
@@ -330,6 +334,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("ar_pull_rmsnorm", &r9k::ar_pull_rmsnorm);
   m.impl("ar_ll_rmsnorm", &r9k::ar_ll_rmsnorm);
   m.impl("ll_push", &r9k::ll_push);
+  m.impl("swiglu_quant_mxfp8", &r9k::swiglu_quant_mxfp8);
   m.impl("quant_act_mxfp8", &r9k::quant_act_mxfp8);
   m.impl("quant_weight_mxfp4", &r9k::quant_weight_mxfp4);
   m.impl("quant_weight_mxfp8", &r9k::quant_weight_mxfp8);

@@ -49,7 +49,7 @@ __global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int
                                      const int32_t* __restrict__ has_state_tok, const float* __restrict__ A_log,
                                      const float* __restrict__ dt_bias, float* __restrict__ q_out,
                                      float* __restrict__ k_out, float* __restrict__ v_out, float* __restrict__ g_out,
-                                     float* __restrict__ beta_out) {
+                                     float* __restrict__ beta_out, __nv_bfloat16* __restrict__ qkv_bf16) {
   pdl_wait();
   pdl_trigger();  // dependents may launch and prefetch while this grid runs
   const int t = blockIdx.x;
@@ -104,9 +104,19 @@ __global__ void gdn_conv_prep_kernel(const __nv_bfloat16* __restrict__ proj, int
     if (hh < Hk) { inv *= rsqrtf((float)dk); dst = q_out + ((int64_t)t * Hk + hh) * dk; }
     else dst = k_out + ((int64_t)t * Hk + (hh - Hk)) * dk;
     *reinterpret_cast<float4*>(dst + lane * 4) = make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) acc[k] *= inv;
   } else {
     float* dst = v_out + ((int64_t)t * Hv + (hh - 2 * Hk)) * dv;
     *reinterpret_cast<float4*>(dst + lane * 4) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+  }
+  if (qkv_bf16 != nullptr) {
+    // [T, 2 Hk + Hv, 128] bf16 copy (q | k | v heads) for the chunked prefill's tensor-core tiles
+    const __nv_bfloat162 lo = __floats2bfloat162_rn(acc[0], acc[1]), hi = __floats2bfloat162_rn(acc[2], acc[3]);
+    uint2 pk;
+    pk.x = *reinterpret_cast<const uint32_t*>(&lo);
+    pk.y = *reinterpret_cast<const uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(qkv_bf16 + ((int64_t)t * NH + hh) * 128 + lane * 4) = pk;
   }
 }
 
@@ -414,9 +424,17 @@ __global__ void gdn_out_norm_quant_kernel(const float* __restrict__ o, const __n
 void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64_t dv, int64_t b_off, int64_t a_off,
                    torch::Tensor conv_w, torch::Tensor conv_state, torch::Tensor tok_slot, torch::Tensor tok_pos,
                    torch::Tensor tok_has_state, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor q_out,
-                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out) {
+                   torch::Tensor k_out, torch::Tensor v_out, torch::Tensor g_out, torch::Tensor beta_out,
+                   c10::optional<torch::Tensor> qkv_bf16) {
   const int64_t T = proj.size(0);
   if (T == 0) return;
+  __nv_bfloat16* qb = nullptr;
+  if (qkv_bf16.has_value() && qkv_bf16->defined()) {
+    TORCH_CHECK(qkv_bf16->dtype() == torch::kBFloat16 && qkv_bf16->is_contiguous() &&
+                    qkv_bf16->numel() >= T * (2 * Hk + Hv) * 128,
+                "gdn_conv_prep: qkv_bf16 [T, 2 Hk + Hv, 128] bf16");
+    qb = reinterpret_cast<__nv_bfloat16*>(qkv_bf16->data_ptr());
+  }
   const int64_t C = 2 * Hk * dk + Hv * dv;
   const int W = (int)conv_w.size(1);
   TORCH_CHECK(conv_state.size(-1) == W - 1 && conv_state.size(1) == C, "gdn_conv_prep: conv state shape");
@@ -431,7 +449,7 @@ void gdn_conv_prep(torch::Tensor proj, int64_t Hk, int64_t Hv, int64_t dk, int64
       (int)b_off, (int)a_off, reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr()), W,                           \
       reinterpret_cast<const ST_T*>(conv_state.data_ptr()), tok_slot.data_ptr<int32_t>(), tok_pos.data_ptr<int32_t>(),  \
       tok_has_state.data_ptr<int32_t>(), A_log.data_ptr<float>(), dt_bias.data_ptr<float>(), q_out.data_ptr<float>(),  \
-      k_out.data_ptr<float>(), v_out.data_ptr<float>(), g_out.data_ptr<float>(), beta_out.data_ptr<float>());
+      k_out.data_ptr<float>(), v_out.data_ptr<float>(), g_out.data_ptr<float>(), beta_out.data_ptr<float>(), qb);
   if (conv_state.dtype() == torch::kFloat32) { R9K_CONV(float) } else { R9K_CONV(__nv_bfloat16) }
 #undef R9K_CONV
   C10_CUDA_KERNEL_LAUNCH_CHECK();

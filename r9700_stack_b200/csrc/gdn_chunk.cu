@@ -12,13 +12,14 @@
 //   Delta = U - W S,  O = (gamma q) S + P Delta,  S' = gamma_C S + (gamma_C / gamma k)^T Delta
 // Phase 1 (gdn_chunk_prep, one CTA per chunk and value head, all in parallel): KK^T and QK^T on the
 // tensor cores, the masks and decays, T by blocked forward substitution in fp32, then U and W on the
-// tensor cores. It writes the operands of phase 2 (bf16 W, gamma q, K-hat^T and P; fp32 U^T).
+// tensor cores (V and K enter as MN-major operands in their natural row layout). It writes the
+// operands of phase 2 (bf16 W, gamma q, K-hat and P rows; fp32 U^T).
 // Phase 2 (gdn_chunk_scan, one CTA per sequence and value head, chunks in order): everything is kept
 // transposed so TMEM lane n is state column n (dv): the state S^T lives in TMEM in fp32 for the whole
 // sequence; per chunk
 //   MMA1  Delta^T_acc = S^T W^T        MMA2  O^T = S^T (gamma q)^T
 //   E1    Delta^T = U^T - Delta^T_acc (bf16 operand), S^T *= gamma_C (in TMEM)
-//   MMA3  S^T += Delta^T K-hat         MMA4  O^T += Delta^T P^T
+//   MMA3  S^T += Delta^T K-hat (MN-major) MMA4  O^T += Delta^T P^T
 //   E2    O^T -> o (fp32, the same layout gdn_recurrent writes), S^T -> bf16 operand of the next MMA1
 // The operand tiles of the next chunk stream in by TMA while the current chunk's epilogues run.
 // All MMAs are kind::f16 with bf16 operands and fp32 accumulation, M = N = 128, K = 128 (8 steps).
@@ -35,12 +36,13 @@ constexpr int D = 128;              // head dim (dk == dv)
 constexpr int REG = 128 * 128;      // one 128-row x 64-element bf16 swizzle region (16 KB)
 constexpr int TILE = 2 * REG;       // a 128 x 128 bf16 operand (two regions along K)
 constexpr int LS = 129;             // fp32 row stride of L / T in shared memory (bank spread)
-// phase 1 shared memory
-constexpr int P1_KT = 0;            // k rows (A and B of KK^T), later beta v^T (B of U)
-constexpr int P1_QT = P1_KT + TILE; // q rows (A of QK^T), later beta gamma k^T (B of W)
-constexpr int P1_L = P1_QT + TILE;  // L fp32 [128][LS]; after the solve, T as a bf16 operand
-constexpr int P1_T = P1_L + C * LS * 4;  // T fp32 [128][LS]
-constexpr int P1_X = P1_T + C * LS * 4;  // off-diagonal products of the blocked solve [16][LS]
+// phase 1 shared memory (operand tiles 1 KB aligned for the 128-byte swizzle)
+constexpr int P1_Q = 0;             // q rows (TMA; A of QK^T), then T diag(beta) (A of U)
+constexpr int P1_K = TILE;          // k rows (TMA; A and B of KK^T, MN-major B of W)
+constexpr int P1_V = 2 * TILE;      // v rows (TMA; MN-major B of U)
+constexpr int P1_T2 = 3 * TILE;     // T diag(beta gamma) (A of W)
+constexpr int P1_L = 4 * TILE;      // L fp32 [128][LS], turned into T in place
+constexpr int P1_X = P1_L + C * LS * 4;  // off-diagonal products of the blocked solve [16][LS]
 constexpr int P1_BAR = P1_X + 16 * LS * 4;
 constexpr int P1_SMEM = P1_BAR + 64 + 1024;
 // phase 2 shared memory
@@ -85,10 +87,44 @@ R9K_DEVINL void mma_tile(uint32_t d, uint32_t a, uint32_t b, uint32_t accumulate
   }
 }
 
+// 128-byte-swizzled MN-major operand: rows along K (128 bytes = 64 bf16 of N per row), the two N-halves
+// `lbo` bytes apart, 8-row groups `sbo` bytes apart
+R9K_DEVINL uint64_t sdesc_mn(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+// d (+)= a b with a K-major [M rows][K] and b MN-major [K rows][N] (rows of 128 bf16 in two regions)
+R9K_DEVINL void mma_tile_mn(uint32_t d, uint32_t a, uint32_t b, uint32_t accumulate) {
+  constexpr uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, 128) | (1u << 16);  // B MN-major
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const uint32_t aoff = (uint32_t)((k >> 2) * gch::REG + (k & 3) * 32);
+    mma_f16_ss(d, sdesc_k_sw128(a + aoff), sdesc_mn(b + (uint32_t)(k * 16 * 128), gch::REG, 1024), idesc,
+               (accumulate || k > 0) ? 1u : 0u);
+  }
+}
+// 16 consecutive elements [e0, e0 + 16) of row r of a swizzled bf16 tile, as floats
+R9K_DEVINL void ld_tile16(const uint8_t* tile, int r, int e0, float* x) {
+  const uint8_t* reg = tile + (e0 >> 6) * gch::REG;
+  const int c0 = (e0 & 63) >> 3;
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const uint4 v = *reinterpret_cast<const uint4*>(reg + r * 128 + (((c0 + i) ^ (r & 7)) << 4));
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 f = __bfloat1622float2(h[j]);
+      x[8 * i + 2 * j] = f.x;
+      x[8 * i + 2 * j + 1] = f.y;
+    }
+  }
+}
+
 struct ChunkArgs {
-  const float* q;      // [T, Hk, 128] (l2-normalised, scaled)
-  const float* k;      // [T, Hk, 128] (l2-normalised)
-  const float* v;      // [T, Hv, 128]
   const float* g;      // [T, Hv] log decay
   const float* beta;   // [T, Hv]
   int Hk, Hv;
@@ -97,7 +133,7 @@ struct ChunkArgs {
   // phase 1 outputs / phase 2 operands, per (chunk, head) at index (chunk * Hv + head)
   __nv_bfloat16* w;    // [.., 128 tokens, 128 dk]
   __nv_bfloat16* qg;   // gamma q [.., 128 tokens, 128 dk]
-  __nv_bfloat16* khT;  // (gamma_C / gamma k)^T [.., 128 dk, 128 tokens]
+  __nv_bfloat16* kh;   // gamma_C / gamma k [.., 128 tokens, 128 dk]
   __nv_bfloat16* p;    // [.., 128 t, 128 j]
   float* uT;           // U^T [.., 128 dv, 128 tokens]
   float* gC;           // gamma_C [..]
@@ -112,94 +148,119 @@ struct ChunkArgs {
 };
 
 // ------------------------------------------------------------------------------------------------
-// Phase 1: grid (chunks, Hv), 128 threads (thread t = token t, or dim t for the transposed tiles)
+// Phase 1: grid (chunks, Hv), 128 threads (thread t = token row t). q, k, v arrive as bf16 tiles by TMA
+// from the conv step's [T, 2 Hk + Hv, 128] copy (one round trip); every later operand is formed in
+// shared memory or TMEM, so nothing is gathered column-wise from global memory.
 // ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const ChunkArgs a) {
+__global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tmQKV,
+                                                                const ChunkArgs a) {
   using namespace gch;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* Kt = smem + P1_KT;
-  uint8_t* Qt = smem + P1_QT;
-  float* Ls = reinterpret_cast<float*>(smem + P1_L);
-  float* Ts = reinterpret_cast<float*>(smem + P1_T);
+  uint8_t* Qt = smem + P1_Q;
+  uint8_t* Kt = smem + P1_K;
+  uint8_t* Vt = smem + P1_V;
+  uint8_t* T2 = smem + P1_T2;
+  float* Ls = reinterpret_cast<float*>(smem + P1_L);  // L, then T (in place)
   float* Xs = reinterpret_cast<float*>(smem + P1_X);
-  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + P1_BAR);
-  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P1_BAR + 16);
+  uint64_t* bar = reinterpret_cast<uint64_t*>(smem + P1_BAR);  // [0] tiles landed, [1] MMA done
+  uint32_t* tmem_holder = reinterpret_cast<uint32_t*>(smem + P1_BAR + 32);
   __shared__ float sgc[C], sb[C], sgam[C];
   __shared__ float swsum[4];
   const int cid = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int t0 = a.ctab[3 * cid], n = a.ctab[3 * cid + 1];
   const int kh = h / (a.Hv / a.Hk);
   const int64_t oidx = (int64_t)cid * a.Hv + h;
-  pdl_wait();
   if (tid == 0) {
-    mbar_init(bar, 1);
+    mbar_init(&bar[0], 1);
+    mbar_init(&bar[1], 1);
     fence_mbar_init();
+    prefetch_tmap(&tmQKV);
   }
   if (warp == 0) {
     tmem_alloc(tmem_holder, 256);
     tmem_relinquish();
   }
-  // ---- k, q rows (token t) as bf16 operands; g, beta
-  {
-    const int t = tid;
-    float x[16];
-    for (int part = 0; part < 2; ++part) {
-      const float* src = (part == 0 ? a.k : a.q) + ((int64_t)(t0 + t) * a.Hk + kh) * D;
-      uint8_t* dst = part == 0 ? Kt : Qt;
-#pragma unroll 1
-      for (int e = 0; e < D; e += 16) {
-        if (t < n) {
-#pragma unroll
-          for (int i = 0; i < 16; i += 4) {
-            const float4 f = *reinterpret_cast<const float4*>(src + e + i);
-            x[i] = f.x; x[i + 1] = f.y; x[i + 2] = f.z; x[i + 3] = f.w;
-          }
-        } else {
-#pragma unroll
-          for (int i = 0; i < 16; ++i) x[i] = 0.f;
-        }
-        st_tile16(dst, t, e, x);
-      }
-    }
-    const float gv = t < n ? a.g[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
-    sb[t] = t < n ? a.beta[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
-    // inclusive prefix sum of g over the chunk (warp scans + warp offsets)
-    float s = gv;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += y;
-    }
-    if (lane == 31) swsum[warp] = s;
-    __syncthreads();
-    for (int w = 0; w < warp; ++w) s += swsum[w];
-    sgc[t] = s;
-    sgam[t] = __expf(s);
-  }
-  fence_proxy_async();  // the operand tiles were written by threads; the tensor cores read them
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tb = *tmem_holder;
+  pdl_wait();
   if (tid == 0) {
-    mma_tile(tb, smem_u32(Kt), smem_u32(Kt), 0);        // KK^T  -> cols [0, 128)
-    mma_tile(tb + 128, smem_u32(Qt), smem_u32(Kt), 0);  // QK^T  -> cols [128, 256)
-    tc_commit(bar);
+    // rows t0 .. t0 + 127 of head columns (q: kh, k: Hk + kh, v: 2 Hk + h); rows past the step's tokens
+    // read zeros, rows of the next sequence are masked below
+    mbar_arrive_expect_tx(&bar[0], 3 * TILE);
+    const int heads[3] = {kh, a.Hk + kh, 2 * a.Hk + h};
+    uint8_t* dst[3] = {Qt, Kt, Vt};
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+      tma_load_3d_hint(dst[i], &tmQKV, &bar[0], 0, heads[i], t0, policy_evict_first());
+      tma_load_3d_hint(dst[i] + REG, &tmQKV, &bar[0], 64, heads[i], t0, policy_evict_first());
+    }
   }
-  const bool ok0 = mbar_wait(bar, 0, a.timeout_ns);
+  // gates: inclusive prefix sum of the log decay over the chunk (warp scans + warp offsets)
+  {
+    const int t = tid;
+    const float gv = t < n ? a.g[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+    sb[t] = t < n ? a.beta[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+    float sacc = gv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, sacc, o);
+      if (lane >= o) sacc += y;
+    }
+    if (lane == 31) swsum[warp] = sacc;
+    __syncthreads();
+    for (int w = 0; w < warp; ++w) sacc += swsum[w];
+    sgc[t] = sacc;
+    sgam[t] = __expf(sacc);
+  }
+  __syncthreads();
+  const bool ok0 = mbar_wait(&bar[0], 0, a.timeout_ns);
   if (!ok0) report_error(a.status, kErrMbarTimeout, 600, 0);
+  if (tid == 0 && ok0) {
+    tc_fence_after();
+    mma_tile(tb, smem_u32(Kt), smem_u32(Kt), 0);        // KK^T -> cols [0, 128)
+    mma_tile(tb + 128, smem_u32(Qt), smem_u32(Kt), 0);  // QK^T -> cols [128, 256)
+    tc_commit(&bar[1]);
+  }
+  // while the tensor cores run: gamma q rows and K-hat rows (gamma_C / gamma_t k_t) to global
+  const float gcl = sgc[n - 1];
+  {
+    const int t = tid;
+    const bool in = t < n;
+    const float gq = in ? sgam[t] : 0.f, gk = in ? __expf(fminf(gcl - sgc[t], 0.f)) : 0.f;
+    __nv_bfloat16* qd = a.qg + (oidx * C + t) * D;
+    __nv_bfloat16* kd = a.kh + (oidx * C + t) * D;
+#pragma unroll 1
+    for (int e = 0; e < D; e += 16) {
+      float x[16], y[16];
+      ld_tile16(Qt, t, e, x);
+      ld_tile16(Kt, t, e, y);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        x[i] *= gq;
+        y[i] *= gk;
+      }
+      *reinterpret_cast<uint4*>(qd + e) = pack8_bf16(x);
+      *reinterpret_cast<uint4*>(qd + e + 8) = pack8_bf16(x + 8);
+      *reinterpret_cast<uint4*>(kd + e) = pack8_bf16(y);
+      *reinterpret_cast<uint4*>(kd + e + 8) = pack8_bf16(y + 8);
+    }
+  }
+  const bool ok1 = ok0 && __syncthreads_and(mbar_wait(&bar[1], 0, a.timeout_ns));
+  if (!ok1 && tid == 0) report_error(a.status, kErrMbarTimeout, 601, 0);
   tc_fence_after();
   const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
-  // ---- L and P rows (thread = token t)
+  // ---- L row t (shared, fp32) and P row t (global, bf16)
   {
     const int t = tid;
     const float gct = sgc[t], bt = sb[t];
-    float* prow_f = Ts + t * LS;  // P row staged in the (still unused) T buffer
+    __nv_bfloat16* pd = a.p + (oidx * C + t) * C;
 #pragma unroll 1
     for (int j0 = 0; j0 < C; j0 += 16) {
       float kk[16], qk[16];
-      if (ok0) {
+      if (ok1) {
         tmem_ld16(trow + j0, kk);
         tmem_ld16(trow + 128 + j0, qk);
         tmem_ld_wait();
@@ -212,29 +273,15 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const ChunkArgs 
         const int j = j0 + i;
         const float dec = __expf(fminf(gct - sgc[j], 0.f));
         Ls[t * LS + j] = (j < t && t < n) ? bt * dec * kk[i] : 0.f;
-        prow_f[j] = (j <= t && t < n) ? dec * qk[i] : 0.f;
+        qk[i] = (j <= t && t < n) ? dec * qk[i] : 0.f;
       }
-    }
-    // P row t and gamma q row t to global (bf16, row-major tiles)
-    __nv_bfloat16* pd = a.p + (oidx * C + t) * C;
-    __nv_bfloat16* qd = a.qg + (oidx * C + t) * D;
-    const float* qs = a.q + ((int64_t)(t0 + t) * a.Hk + kh) * D;
-    const float gam = t < n ? sgam[t] : 0.f;
-#pragma unroll 1
-    for (int e = 0; e < C; e += 8) {
-      float x[8], y[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        x[i] = prow_f[e + i];
-        y[i] = t < n ? gam * qs[e + i] : 0.f;
-      }
-      *reinterpret_cast<uint4*>(pd + e) = pack8_bf16(x);
-      *reinterpret_cast<uint4*>(qd + e) = pack8_bf16(y);
+      *reinterpret_cast<uint4*>(pd + j0) = pack8_bf16(qk);
+      *reinterpret_cast<uint4*>(pd + j0 + 8) = pack8_bf16(qk + 8);
     }
   }
   __syncthreads();
-  // ---- T = (I + L)^-1, blocks of 16 rows: diagonal blocks by forward substitution (thread = column
-  // of its block), then block row i from X = L[i, <i] T[<i, <i] and T[i, <i] = -T_ii X
+  // ---- T = (I + L)^-1 in place, blocks of 16 rows: diagonal blocks by forward substitution (thread =
+  // column of its block), then block row i: X = L[i, <i] T[<i, <i], T[i, <i] = -T_ii X
   {
     const int bi = tid >> 4, cc = tid & 15, base = bi * 16;
     float tcol[16];
@@ -245,104 +292,91 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const ChunkArgs 
       for (int j = 0; j < r; ++j) acc += Ls[(base + r) * LS + base + j] * tcol[j];
       tcol[r] = r < cc ? 0.f : (r == cc ? 1.f : -acc);
     }
+    __syncthreads();  // every thread has read its diagonal block of L
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Ts[(base + r) * LS + base + cc] = tcol[r];
-    // zero the strictly upper blocks (rows of block bi, columns of later blocks)
-    for (int c2 = base + 16; c2 < C; ++c2) Ts[(base + cc) * LS + c2] = 0.f;
+    for (int r = 0; r < 16; ++r) Ls[(base + r) * LS + base + cc] = tcol[r];
+    for (int c2 = base + 16; c2 < C; ++c2) Ls[(base + cc) * LS + c2] = 0.f;  // strictly upper blocks
   }
   __syncthreads();
 #pragma unroll 1
   for (int i = 1; i < 8; ++i) {
-    const int r = tid & 15, cg = tid >> 4;  // row of block i, column group (columns cg, cg + 8, ...)
-    const int rowL = (16 * i + r) * LS;
-    for (int c = cg; c < 16 * i; c += 8) {
-      float acc = 0.f;
-      for (int kk = c; kk < 16 * i; ++kk) acc += Ls[rowL + kk] * Ts[kk * LS + c];
-      Xs[r * LS + c] = acc;
+    const int r = tid & 15, cg = tid >> 4;
+    const int row = (16 * i + r) * LS;
+    // thread (r, cg) owns X[r][cg + 8 m], m < 2 i: one L load per k2 feeds all of its columns
+    // (independent accumulators, loads of T broadcast across the 16 threads of a column group)
+    float acc[14];
+#pragma unroll
+    for (int m = 0; m < 14; ++m) acc[m] = 0.f;
+#pragma unroll 2
+    for (int k2 = 0; k2 < 16 * i; ++k2) {
+      const float lv = Ls[row + k2];
+#pragma unroll
+      for (int m = 0; m < 14; ++m) {
+        const int c = cg + 8 * m;
+        if (m < 2 * i && k2 >= c) acc[m] += lv * Ls[k2 * LS + c];
+      }
     }
+#pragma unroll
+    for (int m = 0; m < 14; ++m)
+      if (m < 2 * i) Xs[r * LS + cg + 8 * m] = acc[m];
     __syncthreads();
     for (int c = cg; c < 16 * i; c += 8) {
       float acc = 0.f;
 #pragma unroll
-      for (int m = 0; m < 16; ++m) acc += Ts[(16 * i + r) * LS + 16 * i + m] * Xs[m * LS + c];
-      Ts[(16 * i + r) * LS + c] = -acc;  // T_ii[r][m] is zero for m > r
+      for (int m = 0; m < 16; ++m) acc += Ls[row + 16 * i + m] * Xs[m * LS + c];
+      Ls[row + c] = -acc;  // L[i, <i] is consumed (in X); T_ii[r][m] is zero for m > r
     }
     __syncthreads();
   }
-  // ---- T (bf16 operand, rows t) into the L buffer; beta v^T and beta gamma k^T (rows = dim) into Kt/Qt
-  uint8_t* Tt = smem + P1_L;
+  // ---- T diag(beta) (A of U, over the q tile) and T diag(beta gamma) (A of W)
   {
-    float x[16];
     const int t = tid;
-    // T rows: read the whole row first (the bf16 tile overlaps the fp32 L rows of other threads only
-    // after the barrier below, so stage through registers row by row)
-    __syncthreads();
 #pragma unroll 1
     for (int e = 0; e < C; e += 16) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) x[i] = Ts[t * LS + e + i];
-      st_tile16(Tt, t, e, x);
-    }
-    const int d = tid;
-#pragma unroll 1
-    for (int e = 0; e < C; e += 16) {
-      float y[16];
+      float x[16], y[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int j = e + i;
-        const bool in = j < n;
-        x[i] = in ? sb[j] * a.v[((int64_t)(t0 + j) * a.Hv + h) * D + d] : 0.f;
-        y[i] = in ? sb[j] * sgam[j] * a.k[((int64_t)(t0 + j) * a.Hk + kh) * D + d] : 0.f;
+        const float tv = Ls[t * LS + e + i];
+        x[i] = tv * sb[e + i];
+        y[i] = tv * sb[e + i] * sgam[e + i];
       }
-      st_tile16(Kt, d, e, x);
-      st_tile16(Qt, d, e, y);
+      st_tile16(Qt, t, e, x);
+      st_tile16(T2, t, e, y);
     }
   }
   fence_proxy_async();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (tid == 0) {
-    mma_tile(tb, smem_u32(Tt), smem_u32(Kt), 0);        // U = T (beta v)        -> cols [0, 128)
-    mma_tile(tb + 128, smem_u32(Tt), smem_u32(Qt), 0);  // W = T (beta gamma k)  -> cols [128, 256)
-    tc_commit(bar);
+  if (tid == 0 && ok1) {
+    mma_tile_mn(tb, smem_u32(Qt), smem_u32(Vt), 0);        // U = T diag(beta) V          -> cols [0, 128)
+    mma_tile_mn(tb + 128, smem_u32(T2), smem_u32(Kt), 0);  // W = T diag(beta gamma) K    -> cols [128, 256)
+    tc_commit(&bar[1]);
   }
-  const bool ok1 = mbar_wait(bar, 1, a.timeout_ns);
-  if (!ok1) report_error(a.status, kErrMbarTimeout, 601, 0);
+  const bool ok2 = ok1 && __syncthreads_and(mbar_wait(&bar[1], 1, a.timeout_ns));
+  if (!ok2 && tid == 0) report_error(a.status, kErrMbarTimeout, 602, 0);
   tc_fence_after();
   {
     const int t = tid;
+    const bool in = t < n && ok2;
     float* ut = a.uT + oidx * D * C;
     __nv_bfloat16* wd = a.w + (oidx * C + t) * D;
 #pragma unroll 1
     for (int e = 0; e < D; e += 16) {
       float u[16], w[16];
-      if (ok1) {
+      if (ok2) {
         tmem_ld16(trow + e, u);
         tmem_ld16(trow + 128 + e, w);
         tmem_ld_wait();
-      } else {
-#pragma unroll
-        for (int i = 0; i < 16; ++i) u[i] = w[i] = 0.f;
       }
 #pragma unroll
-      for (int i = 0; i < 16; ++i) ut[(int64_t)(e + i) * C + t] = u[i];  // U^T[d][t]: coalesced over t
+      for (int i = 0; i < 16; ++i) {
+        u[i] = in ? u[i] : 0.f;
+        w[i] = in ? w[i] : 0.f;
+        ut[(int64_t)(e + i) * C + t] = u[i];  // U^T[d][t]: coalesced over t
+      }
       *reinterpret_cast<uint4*>(wd + e) = pack8_bf16(w);
       *reinterpret_cast<uint4*>(wd + e + 8) = pack8_bf16(w + 8);
-    }
-    // K-hat^T[d][t] = gamma_C / gamma_t k[t][d] (row d, thread = d)
-    const int d = tid;
-    const float gcl = sgc[n - 1];
-    __nv_bfloat16* kd = a.khT + (oidx * D + d) * C;
-#pragma unroll 1
-    for (int e = 0; e < C; e += 8) {
-      float x[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int j = e + i;
-        x[i] = j < n ? __expf(fminf(gcl - sgc[j], 0.f)) * a.k[((int64_t)(t0 + j) * a.Hk + kh) * D + d] : 0.f;
-      }
-      *reinterpret_cast<uint4*>(kd + e) = pack8_bf16(x);
     }
     if (tid == 0) a.gC[oidx] = __expf(gcl);
   }
@@ -441,7 +475,7 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
           break;
         }
         tc_fence_after();
-        mma_tile(tb + SM, smem_u32(Dt), smem_u32(smem + P2_K), 1);
+        mma_tile_mn(tb + SM, smem_u32(Dt), smem_u32(smem + P2_K), 1);  // K-hat rows: MN-major B
         mma_tile(tb + OACC, smem_u32(Dt), smem_u32(smem + P2_P), 1);
         tc_commit(mma2);
       }
@@ -477,12 +511,16 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
       const int64_t oidx = (int64_t)c * a.Hv + h;
       const float* ur = a.uT + (oidx * D + nrow) * C;  // U^T row n
       const float gC = a.gC[oidx];
+      // the U^T row is requested before waiting on the tensor cores, so its latency hides behind MMA1/2
+      float4 uv[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) uv[i] = *reinterpret_cast<const float4*>(ur + 4 * i);
       // ---- E1: Delta^T = U^T - S^T W^T; S^T *= gamma_C
       ok = __all_sync(0xffffffffu, mbar_wait(mma1, ph, a.timeout_ns)) && !s_abort;
       if (!ok) break;
       tc_fence_after();
       if (tid == 0 && c + 1 < c1) load_a(c + 1);  // W / gamma q buffers are free again
-#pragma unroll 1
+#pragma unroll
       for (int e = 0; e < C; e += 16) {
         float x[16], sm[16];
         tmem_ld16(trow + DACC + e, x);
@@ -490,7 +528,7 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
         tmem_ld_wait();
 #pragma unroll
         for (int i = 0; i < 16; i += 4) {
-          const float4 u4 = *reinterpret_cast<const float4*>(ur + e + i);
+          const float4 u4 = uv[(e + i) >> 2];
           x[i] = u4.x - x[i]; x[i + 1] = u4.y - x[i + 1]; x[i + 2] = u4.z - x[i + 2]; x[i + 3] = u4.w - x[i + 3];
         }
 #pragma unroll
@@ -553,47 +591,61 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
 // ------------------------------------------------------------------------------------------------
 // host
 // ------------------------------------------------------------------------------------------------
-// q, k [T, Hk, 128], v [T, Hv, 128], g / beta [T, Hv] fp32 (gdn_conv_prep outputs); ctab [chunks, 3]
-// int32 (first token, tokens, sequence); seq_chunk0 [S + 1] int32; scratch: w, qg, khT, p bf16
-// [chunks * Hv * 128, 128], uT fp32 [chunks * Hv * 128, 128], gC fp32 [chunks * Hv]; o [T, Hv, 128].
-void gdn_chunked(torch::Tensor q, torch::Tensor k, torch::Tensor v, torch::Tensor g, torch::Tensor beta,
-                 torch::Tensor state, torch::Tensor ctab, torch::Tensor seq_chunk0, torch::Tensor seq_slot,
-                 torch::Tensor seq_has_state, bool write_state, torch::Tensor w, torch::Tensor qg, torch::Tensor khT,
-                 torch::Tensor p, torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status) {
+// qkv: bf16 [T, 2 Hk + Hv, 128] (q | k | v heads from gdn_conv_prep); g / beta fp32 [T, Hv]; ctab [chunks, 3]
+// int32 (first token, tokens, sequence); seq_chunk0 [S + 1] int32; scratch: w, qg, kh, p bf16
+// [chunks * Hv * 128, 128], uT fp32 [chunks * Hv * 128, 128], gC fp32 [chunks * Hv]; o fp32 [T, Hv, 128].
+void gdn_chunked(torch::Tensor qkv, torch::Tensor g, torch::Tensor beta, torch::Tensor state, torch::Tensor ctab,
+                 torch::Tensor seq_chunk0, torch::Tensor seq_slot, torch::Tensor seq_has_state, bool write_state,
+                 int64_t Hk, int64_t Hv, torch::Tensor w, torch::Tensor qg, torch::Tensor kh, torch::Tensor p,
+                 torch::Tensor uT, torch::Tensor gC, torch::Tensor o, torch::Tensor status) {
   using namespace gch;
   const int64_t nchunks = ctab.size(0), S = seq_slot.size(0);
   if (nchunks == 0 || S == 0) return;
-  const int Hk = (int)q.size(1), Hv = (int)v.size(1);
-  TORCH_CHECK(q.size(2) == D && v.size(2) == D && Hv % Hk == 0, "gdn_chunked: head dim 128, Hv % Hk");
+  const int64_t T = g.size(0), NH = 2 * Hk + Hv;
+  TORCH_CHECK(qkv.dtype() == torch::kBFloat16 && qkv.is_contiguous() && qkv.numel() >= T * NH * D &&
+                  (reinterpret_cast<uintptr_t>(qkv.data_ptr()) & 15) == 0,
+              "gdn_chunked: qkv bf16 [T, 2 Hk + Hv, 128]");
+  TORCH_CHECK(Hv % Hk == 0 && g.size(1) == Hv && o.size(1) == Hv && o.size(2) == D, "gdn_chunked: heads");
   TORCH_CHECK(state.size(1) == Hv && state.size(2) == D && state.size(3) == D, "gdn_chunked: state [slots, Hv, 128, 128]");
   TORCH_CHECK(ctab.dtype() == torch::kInt32 && ctab.size(1) == 3 && seq_chunk0.numel() == S + 1, "gdn_chunked: tables");
   const int64_t rows = nchunks * Hv * C;
-  TORCH_CHECK(w.numel() >= rows * D && qg.numel() >= rows * D && khT.numel() >= rows * C && p.numel() >= rows * C &&
+  TORCH_CHECK(w.numel() >= rows * D && qg.numel() >= rows * D && kh.numel() >= rows * D && p.numel() >= rows * C &&
                   uT.numel() >= rows * C && gC.numel() >= nchunks * Hv,
               "gdn_chunked: scratch too small");
-  for (auto* t : {&q, &k, &v, &g, &beta, &o}) TORCH_CHECK(t->is_contiguous() && t->dtype() == torch::kFloat32, "gdn_chunked: fp32 inputs");
-  const at::cuda::CUDAGuard guard(q.device());
+  for (auto* t : {&g, &beta, &o}) TORCH_CHECK(t->is_contiguous() && t->dtype() == torch::kFloat32, "gdn_chunked: fp32");
+  const at::cuda::CUDAGuard guard(g.device());
   auto st = at::cuda::getCurrentCUDAStream();
   ChunkArgs a = {};
-  a.q = q.data_ptr<float>(); a.k = k.data_ptr<float>(); a.v = v.data_ptr<float>();
   a.g = g.data_ptr<float>(); a.beta = beta.data_ptr<float>();
-  a.Hk = Hk; a.Hv = Hv;
+  a.Hk = (int)Hk; a.Hv = (int)Hv;
   a.ctab = ctab.data_ptr<int32_t>(); a.nchunks = (int)nchunks;
   a.w = reinterpret_cast<__nv_bfloat16*>(w.data_ptr()); a.qg = reinterpret_cast<__nv_bfloat16*>(qg.data_ptr());
-  a.khT = reinterpret_cast<__nv_bfloat16*>(khT.data_ptr()); a.p = reinterpret_cast<__nv_bfloat16*>(p.data_ptr());
+  a.kh = reinterpret_cast<__nv_bfloat16*>(kh.data_ptr()); a.p = reinterpret_cast<__nv_bfloat16*>(p.data_ptr());
   a.uT = uT.data_ptr<float>(); a.gC = gC.data_ptr<float>();
   a.seq_chunk0 = seq_chunk0.data_ptr<int32_t>(); a.seq_slot = seq_slot.data_ptr<int32_t>();
   a.seq_has_state = seq_has_state.data_ptr<int32_t>(); a.write_state = write_state ? 1 : 0;
   a.o = o.data_ptr<float>();
   a.status = status.data_ptr<int>();
   a.timeout_ns = 2000000000ull;
+  // q|k|v copy as a 3-D map (128 elements, heads, tokens): a box is 64 elements x 1 head x 128 tokens
+  CUtensorMap tqkv;
+  {
+    cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)NH, (cuuint64_t)T};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)NH * D * 2};
+    cuuint32_t box[3] = {64, 1, 128};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = get_encode_fn()(&tqkv, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, qkv.data_ptr(), dims, strides, box, estr,
+                                 CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                                 CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    TORCH_CHECK(r == CUDA_SUCCESS, "gdn_chunked: q|k|v tensor map (", (int)r, ")");
+  }
   TORCH_CHECK(ensure_smem_attr((const void*)gdn_chunk_prep_kernel, P1_SMEM) == cudaSuccess, "gdn_chunked: smem");
-  TORCH_CHECK(launch_pdl(gdn_chunk_prep_kernel, dim3((unsigned)nchunks, (unsigned)Hv), dim3(128), (size_t)P1_SMEM, st, a) ==
-                  cudaSuccess,
+  TORCH_CHECK(launch_pdl(gdn_chunk_prep_kernel, dim3((unsigned)nchunks, (unsigned)Hv), dim3(128), (size_t)P1_SMEM, st,
+                         tqkv, a) == cudaSuccess,
               "gdn_chunk_prep launch");
   const CUtensorMap tW = tmap_bf16_kmajor(w.data_ptr(), rows, D, D, 128);
   const CUtensorMap tQ = tmap_bf16_kmajor(qg.data_ptr(), rows, D, D, 128);
-  const CUtensorMap tK = tmap_bf16_kmajor(khT.data_ptr(), rows, C, C, 128);
+  const CUtensorMap tK = tmap_bf16_kmajor(kh.data_ptr(), rows, D, D, 128);
   const CUtensorMap tP = tmap_bf16_kmajor(p.data_ptr(), rows, C, C, 128);
 #define R9K_GCS(ST_T)                                                                                             \
   {                                                                                                               \

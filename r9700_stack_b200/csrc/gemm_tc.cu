@@ -586,6 +586,12 @@ static LaunchPlan plan_gemm(int N, int M, int kchunks, bool dual, bool fp4) {
     const int rt = (N + 127) / 128;
     if ((long)rt * ((M + 255) / 256) < num_sms()) p.BN = 128;
   }
+  static int force_bn = -1;
+  if (force_bn < 0) {
+    const char* e = getenv("R9K_GEMM_BN");  // tuning: force the token tile of prefill-sized GEMMs
+    force_bn = e ? std::max(0, atoi(e)) : 0;
+  }
+  if (force_bn > 0 && M > 128 && (force_bn == 128 || (force_bn == 256 && !dual))) p.BN = force_bn;
   p.n_tiles = (M + p.BN - 1) / p.BN;
   static int unpack_knob = -1;
   if (unpack_knob < 0) {

@@ -213,6 +213,65 @@ __global__ void quant_act_mxfp8_kernel(const __nv_bfloat16* __restrict__ x, int6
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// SwiGLU + MXFP8: h = silu(g) * u from the bf16 outputs of the gate and up GEMMs (prefill-sized M,
+// where two wide GEMMs beat the dual-accumulator kernel whose per-token quantising epilogue leaves the
+// tensor cores idle). Thread = 8 consecutive elements; 4 threads = one 32-element MX block.
+// ------------------------------------------------------------------------------------------------
+__global__ void swiglu_quant_mxfp8_kernel(const __nv_bfloat16* __restrict__ g, const __nv_bfloat16* __restrict__ u,
+                                          int64_t ld, int M, int N, uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
+  pdl_wait();
+  pdl_trigger();
+  const int groups = N / 8;
+  const int64_t total = (int64_t)M * groups;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t r = i / groups;
+    const int c = (int)(i % groups) * 8;
+    const uint4 gv = *reinterpret_cast<const uint4*>(g + r * ld + c);
+    const uint4 uv = *reinterpret_cast<const uint4*>(u + r * ld + c);
+    const __nv_bfloat162* gh = reinterpret_cast<const __nv_bfloat162*>(&gv);
+    const __nv_bfloat162* uh = reinterpret_cast<const __nv_bfloat162*>(&uv);
+    float h[8];
+    float am = 0.f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 a = __bfloat1622float2(gh[j]), b = __bfloat1622float2(uh[j]);
+      h[2 * j] = silu_f(a.x) * b.x;
+      h[2 * j + 1] = silu_f(a.y) * b.y;
+      am = fmaxf(am, fmaxf(fabsf(h[2 * j]), fabsf(h[2 * j + 1])));
+    }
+    // the 4 threads of a block are consecutive lanes (N % 32 == 0, groups of 8 elements)
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 1));
+    am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, 2));
+    const int e = mx_exponent(am, 448.f);
+    const float sc = exp2i(-e);
+    uint2 out;
+    uint8_t* ob = reinterpret_cast<uint8_t*>(&out);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) ob[j] = f32_to_e4m3(h[j] * sc);
+    *reinterpret_cast<uint2*>(q + r * N + c) = out;
+    if ((c & 31) == 0) sf[sf_offset(r, c >> 5, N / 32)] = (uint8_t)(e + 127);
+  }
+}
+
+void swiglu_quant_mxfp8(torch::Tensor g, torch::Tensor u, torch::Tensor q, torch::Tensor sf) {
+  const int64_t M = g.size(0), N = g.size(1);
+  TORCH_CHECK(g.dtype() == torch::kBFloat16 && u.dtype() == torch::kBFloat16 && g.sizes() == u.sizes() &&
+                  g.stride(0) == u.stride(0) && g.stride(1) == 1 && u.stride(1) == 1 && g.stride(0) % 8 == 0,
+              "swiglu_quant_mxfp8: bf16 [M, N] gate / up with one 16-byte-aligned row stride");
+  TORCH_CHECK(N % 32 == 0 && q.size(0) >= M && q.size(1) == N, "swiglu_quant_mxfp8: N % 32, q [M, N]");
+  TORCH_CHECK(sf.numel() >= ((M + 127) / 128) * ((N / 32 + 3) / 4) * 512, "swiglu_quant_mxfp8: sf too small");
+  if (M == 0) return;
+  const at::cuda::CUDAGuard guard(g.device());
+  const int64_t threads = M * (N / 8);
+  const int64_t blocks = std::min<int64_t>((threads + 255) / 256, (int64_t)device_sm_count() * 16);
+  TORCH_CHECK(launch_pdl(swiglu_quant_mxfp8_kernel, dim3((unsigned)blocks), dim3(256), 0,
+                         at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(g.data_ptr()),
+                         reinterpret_cast<const __nv_bfloat16*>(u.data_ptr()), g.stride(0), (int)M, (int)N,
+                         q.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>()) == cudaSuccess,
+              "swiglu_quant_mxfp8 launch");
+}
+
 void quant_act_mxfp8(torch::Tensor x, torch::Tensor q, torch::Tensor sf) {
   const int64_t M = x.size(0), K = x.size(1);
   TORCH_CHECK(K % 32 == 0 && x.stride(1) == 1 && x.dtype() == torch::kBFloat16, "quant_act_mxfp8: bf16 [M, K%32]");

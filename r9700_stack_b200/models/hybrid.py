@@ -454,18 +454,22 @@ class HybridLM:
                                None if self.mx else ws.gdn_bf16[:T])
             return ws.gdn_act.narrow(T), ws.gdn_bf16[:T], lay["w_out"]
         gk, gv, gg, gb = (ws.gk, ws.gv, ws.gg, ws.gb) if sb is None else (sb["k"], sb["v"], sb["g"], sb["b"])
+        # long prefill: the chunked delta rule on the tensor cores (same state and output)
+        chunked = (sb is None and meta.write_state and bool(meta.host_seqs)
+                   and knobs.get("R9K_GDN_PREFILL") == "chunked"
+                   and max(n for _, n in meta.host_seqs) >= knobs.get_int("R9K_GDN_CHUNK_MIN"))
+        ctab = c0 = buf = None
+        if chunked:
+            ctab, c0, nch = self._gdn_chunk_tables(meta)
+            buf = self._gdn_chunk_scratch(ws, nch * hv * 128, T * (2 * hk + hv) * 128)
         o.gdn_conv_prep(proj, hk, hv, d, d, b_off, a_off, lay["conv_w"], conv, meta.tok_state_slot,
                         meta.tok_pos_in_chunk, meta.tok_has_state, lay["A_log"], lay["dt_bias"],
-                        ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T])
+                        ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], buf[0] if chunked else None)
         if meta.write_state:
             o.gdn_conv_state_update(proj, conv, meta.seq_state_slot, meta.seq_start, meta.seq_len, meta.seq_has_state)
-        if (sb is None and meta.write_state and meta.host_seqs and knobs.get("R9K_GDN_PREFILL") == "chunked"
-                and max(n for _, n in meta.host_seqs) >= knobs.get_int("R9K_GDN_CHUNK_MIN")):
-            # long prefill: the chunked delta rule on the tensor cores (same inputs and outputs)
-            ctab, c0, nch = self._gdn_chunk_tables(meta)
-            buf = self._gdn_chunk_scratch(ws, nch * hv * 128)
-            o.gdn_chunked(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, ctab, c0, meta.seq_state_slot,
-                          meta.seq_has_state, True, *buf, ws.go[:T], _status.status(self.device))
+        if chunked:
+            o.gdn_chunked(buf[0], gg[:T], gb[:T], ssm, ctab, c0, meta.seq_state_slot, meta.seq_has_state, True, hk, hv,
+                          *buf[1:], ws.go[:T], _status.status(self.device))
         else:
             o.gdn_recurrent(ws.gq[:T], gk[:T], gv[:T], gg[:T], gb[:T], ssm, meta.seq_state_slot,
                             meta.seq_start, meta.seq_len, meta.seq_has_state, meta.write_state, ws.go[:T])
@@ -492,15 +496,17 @@ class HybridLM:
         meta.gdn_chunks = (meta.host_seqs, ctab, c0, len(rows))
         return ctab, c0, len(rows)
 
-    def _gdn_chunk_scratch(self, ws: Workspace, rows: int):
-        """Phase-1 outputs of the chunked GDN (W, gamma q, K-hat^T, P in bf16; U^T fp32; gamma_C), grown to
-        `rows` (chunks x value heads x 128) on demand; eager prefill steps only."""
+    def _gdn_chunk_scratch(self, ws: Workspace, rows: int, qkv_elems: int):
+        """Buffers of the chunked GDN: the bf16 q|k|v copy of the conv step, then phase 1's outputs (W,
+        gamma q, K-hat, P in bf16; U^T fp32; gamma_C), grown on demand (eager prefill steps only)."""
         buf = getattr(ws, "gdn_chunk_buf", None)
-        if buf is None or buf[0].shape[0] < rows:
-            cap = max(rows, 128 * 16)
+        if buf is None or buf[1].shape[0] < rows or buf[0].numel() < qkv_elems:
+            cap = max(rows, 128 * 16, buf[1].shape[0] if buf is not None else 0)
+            qcap = max(qkv_elems, buf[0].numel() if buf is not None else 0)
             dev = self.device
             bf = lambda: torch.empty(cap, 128, dtype=torch.bfloat16, device=dev)
-            buf = (bf(), bf(), bf(), bf(), torch.empty(cap, 128, dtype=torch.float32, device=dev),
+            buf = (torch.empty(qcap, dtype=torch.bfloat16, device=dev), bf(), bf(), bf(), bf(),
+                   torch.empty(cap, 128, dtype=torch.float32, device=dev),
                    torch.empty(cap // 128, dtype=torch.float32, device=dev))
             ws.gdn_chunk_buf = buf
         return buf

@@ -279,15 +279,42 @@ def mx_linear(
     return out
 
 
+SWIGLU_SPLIT_M = 256  # from this many tokens on, gate / up run as two GEMMs + one SwiGLU-quant pass
+
+
 def mx_swiglu(x: MXAct, w_gate: MXWeight, w_up: MXWeight, out: MXAct | None = None) -> MXAct:
+    """silu(x W_gate^T) * (x W_up^T) as MXFP8. Decode-sized M: one dual-accumulator kernel with the
+    SwiGLU and the quantisation in its epilogue. Prefill-sized M: the gate and up GEMMs at full tile
+    width into one bf16 buffer, then swiglu_quant_mxfp8 (measured at 17408 x 5120, M = 8192: the dual
+    kernel 3.87 ms, 0.76 PFLOP/s; one wide GEMM 1.06 ms)."""
     M = x.M
     if out is None:
         out = alloc_act(M, w_gate.N, x.q.device)
+    if M >= SWIGLU_SPLIT_M and w_gate.N % 32 == 0 and not torch.cuda.is_current_stream_capturing():
+        N = w_gate.N
+        gu = _swiglu_scratch(M, N, x.q.device)
+        mx_linear(x, w_gate, out=gu[0])
+        mx_linear(x, w_up, out=gu[1])
+        _ops().swiglu_quant_mxfp8(gu[0], gu[1], out.q, out.sf)
+        return out
     _ops().gemm_mx_swiglu(
         w_gate.q, w_gate.sf, w_up.q, w_up.sf, w_gate.fp4, x.q, x.sf, out.q, out.sf, _status.status(x.q.device),
         gemm_workspace(x.q.device),
     )
     return out
+
+
+_SWIGLU_BUF: dict = {}
+
+
+def _swiglu_scratch(M: int, N: int, device) -> torch.Tensor:
+    """[2, M, N] bf16 gate / up outputs of the split SwiGLU path, reused across calls (eager prefill)."""
+    key = torch.device(device)
+    buf = _SWIGLU_BUF.get(key)
+    if buf is None or buf.numel() < 2 * M * N:
+        buf = torch.empty(2 * M * N, dtype=torch.bfloat16, device=key)
+        _SWIGLU_BUF[key] = buf
+    return buf[: 2 * M * N].view(2, M, N)
 
 
 def bf16_linear(

@@ -304,7 +304,8 @@ def _bench_gdn_prefill(a) -> dict:
         buf = [torch.empty(nr, 128, dtype=torch.bfloat16, device="cuda") for _ in range(4)]
         buf += [torch.empty(nr, 128, device="cuda"), torch.empty(len(rows) * Hv, device="cuda")]
         stat = status.status(torch.device("cuda"))
-        f = lambda i: ops.gdn_chunked(q, k, v, g, b, st, ctab, c0, slot, hs, True, *buf, o, stat)
+        qkv = torch.cat([q, k, v], 1).bfloat16().contiguous()
+        f = lambda i: ops.gdn_chunked(qkv, g, b, st, ctab, c0, slot, hs, True, Hk, Hv, *buf, o, stat)
     else:
         f = lambda i: ops.gdn_recurrent(q, k, v, g, b, st, slot, s0, ln, hs, True, o)
     us = _time(f, a.reps, a.warmup, graph=not a.eager)

@@ -62,22 +62,25 @@ def test_chunked_matches_serial(sdt):
     buf += [torch.empty(rows, 128, device="cuda"), torch.empty(nch * Hv, device="cuda")]
     st = st0.clone()
     o = torch.full((T, Hv, 128), float("nan"), device="cuda")
-    ops.gdn_chunked(q, k, v, gg, b, st, ctab, c0, slots, i32(has), True, *buf, o, status.status(torch.device("cuda")))
+    qkv = torch.cat([q, k, v], 1).bfloat16().contiguous()  # the conv step's bf16 copy
+    ops.gdn_chunked(qkv, gg, b, st, ctab, c0, slots, i32(has), True, Hk, Hv, *buf, o, status.status(torch.device("cuda")))
     torch.cuda.synchronize()
     status.check()
     assert torch.isfinite(o).all()
     for si, (t0, n) in enumerate(zip(starts, lens)):
         e_o = _rel(o[t0:t0 + n], o_ref[t0:t0 + n])
         e_s = _rel(st[si + 1], st_ref[si + 1])
-        assert e_o < 3e-2, (si, n, e_o)
-        assert e_s < 3e-2, (si, n, e_s)
+        assert e_o < 1e-2, (si, n, e_o)  # bf16 operands: measured ~4e-3 against a float64 recurrence
+        assert e_s < 1e-2, (si, n, e_s)
     # untouched slot
     assert torch.equal(st[0], st0[0])
 
 
 def test_hybrid_prefill_chunked_vs_serial(monkeypatch):
-    """One tiny hybrid model, a 300-token prompt: the chunked prefill's first logits and the decode
-    tokens that follow agree with the serial prefill's."""
+    """One tiny hybrid model, a 300-token prompt: the chunked prefill's first logits agree with the
+    serial prefill's. bf16 weights: with MX weights every layer re-quantises its activations to e4m3,
+    which turns the chunked path's ~0.4% bf16-operand differences into flipped roundings (cosine
+    ~0.99 between two equally valid runs), so that check would measure the quantiser, not the GDN."""
     from r9700_stack_b200 import knobs
     from r9700_stack_b200.engine.llm import LLM
     from r9700_stack_b200.engine.scheduler import SamplingParams
@@ -89,7 +92,7 @@ def test_hybrid_prefill_chunked_vs_serial(monkeypatch):
         monkeypatch.setenv("R9K_GDN_PREFILL", mode)
         monkeypatch.setenv("R9K_GDN_CHUNK_MIN", "64")
         knobs.refresh()
-        cfg = tiny_hybrid(gdn_state_dtype="fp32")
+        cfg = tiny_hybrid(gdn_state_dtype="fp32", weight_format="bf16", lm_head_format="bf16")
         ec = EngineConfig(max_batch=2, max_model_len=512, max_prefill_tokens=512, cuda_graphs=False)
         llm = LLM(cfg, ec, seed=5)
         llm.runner.logit_log = []

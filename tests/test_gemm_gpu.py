@@ -119,6 +119,32 @@ def test_gemm_swiglu_mxfp8(L, N, K, M):
     assert bool((err <= tol).all()), float((err / tol).max())
 
 
+def test_swiglu_split_matches_dual(L):
+    """Prefill-sized M takes two GEMMs + swiglu_quant_mxfp8; it agrees with the dual-accumulator kernel
+    (the only difference is the bf16 rounding of the gate / up outputs before the activation)."""
+    torch.manual_seed(9)
+    N, K, M = 512, 1024, 300
+    g = L.mx_from_float((torch.randn(N, K) * 0.05).cuda())
+    u = L.mx_from_float((torch.randn(N, K) * 0.05).cuda())
+    xa = L.quant_act(torch.randn(M, K).bfloat16().cuda())
+    assert M >= L.SWIGLU_SPLIT_M
+    split = L.mx_swiglu(xa, g, u)
+    old = L.SWIGLU_SPLIT_M
+    L.SWIGLU_SPLIT_M = 1 << 30
+    try:
+        dual = L.mx_swiglu(xa, g, u)
+    finally:
+        L.SWIGLU_SPLIT_M = old
+    _check_status()
+    a = F.dequant_mx(split.q.cpu(), split.sf.cpu(), M, N, fp4=False)
+    b = F.dequant_mx(dual.q.cpu(), dual.sf.cpu(), M, N, fp4=False)
+    # one e4m3 step at the top of a block is 32/448 of the block's amax; the bf16 rounding of the gate /
+    # up outputs may flip a rounding (or the block exponent), never more than about two such steps
+    tol = 0.15 * b.abs().reshape(M, N // 32, 32).amax(-1).repeat_interleave(32, 1) + 1e-6
+    assert bool(((a - b).abs() <= tol).all())
+    assert float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)) > 0.999
+
+
 @pytest.mark.parametrize("N,K,M", [(128, 64, 1), (256, 512, 16), (384, 1024, 100), (256, 256, 513), (2048, 4096, 8)])
 def test_gemm_bf16(L, N, K, M):
     torch.manual_seed(11)
