@@ -25,6 +25,7 @@ void gemm_mx_grouped(torch::Tensor w, torch::Tensor w_sf, c10::optional<torch::T
 void gemm_bf16_swiglu(torch::Tensor wg, torch::Tensor wu, torch::Tensor x, torch::Tensor out, torch::Tensor status,
                       c10::optional<torch::Tensor> workspace);
 void gemm_trace(c10::optional<torch::Tensor> buf);
+void gdn_chunk_trace(c10::optional<torch::Tensor> buf);
 // moe.cu
 void moe_route(torch::Tensor logits, int64_t k, int64_t mode, c10::optional<torch::Tensor> bias, int64_t n_group,
                int64_t topk_group, double scale, bool renorm, torch::Tensor ids, torch::Tensor w);
@@ -396,6 +397,7 @@ TORCH_LIBRARY_FRAGMENT(r9k, m) {
         "float timeout_s) -> Tensor", &r9k::p2p_probe);
   // tuning: per-CTA timestamps of the tiled GEMM into an int64 buffer (None switches them off)
   m.def("gemm_trace(Tensor? buf) -> ()", &r9k::gemm_trace);
+  m.def("gdn_chunk_trace(Tensor? buf) -> ()", &r9k::gdn_chunk_trace);
 }
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) { m.doc() = "r9700_stack_b200 sm_100a kernel library"; }

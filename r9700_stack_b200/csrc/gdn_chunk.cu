@@ -145,6 +145,7 @@ struct ChunkArgs {
   float* o;            // [T, Hv, 128]
   int* status;
   uint64_t timeout_ns;
+  unsigned long long* trace;  // tuning: 8 %globaltimer stamps per phase-1 CTA, or null
 };
 
 // ------------------------------------------------------------------------------------------------
@@ -171,6 +172,8 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   const int t0 = a.ctab[3 * cid], n = a.ctab[3 * cid + 1];
   const int kh = h / (a.Hv / a.Hk);
   const int64_t oidx = (int64_t)cid * a.Hv + h;
+  unsigned long long* tr = (a.trace != nullptr && tid == 0) ? a.trace + oidx * 8 : nullptr;
+  if (tr) tr[0] = globaltimer_ns();
   if (tid == 0) {
     mbar_init(&bar[0], 1);
     mbar_init(&bar[1], 1);
@@ -218,6 +221,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   __syncthreads();
   const bool ok0 = mbar_wait(&bar[0], 0, a.timeout_ns);
   if (!ok0) report_error(a.status, kErrMbarTimeout, 600, 0);
+  if (tr) tr[1] = globaltimer_ns();
   if (tid == 0 && ok0) {
     tc_fence_after();
     mma_tile(tb, smem_u32(Kt), smem_u32(Kt), 0);        // KK^T -> cols [0, 128)
@@ -250,6 +254,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   }
   const bool ok1 = ok0 && __syncthreads_and(mbar_wait(&bar[1], 0, a.timeout_ns));
   if (!ok1 && tid == 0) report_error(a.status, kErrMbarTimeout, 601, 0);
+  if (tr) tr[2] = globaltimer_ns();
   tc_fence_after();
   const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
   // ---- L row t (shared, fp32) and P row t (global, bf16)
@@ -280,6 +285,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
     }
   }
   __syncthreads();
+  if (tr) tr[3] = globaltimer_ns();
   // ---- T = (I + L)^-1 in place, blocks of 16 rows: diagonal blocks by forward substitution (thread =
   // column of its block), then block row i: X = L[i, <i] T[<i, <i], T[i, <i] = -T_ii X
   {
@@ -328,6 +334,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
     }
     __syncthreads();
   }
+  if (tr) tr[4] = globaltimer_ns();
   // ---- T diag(beta) (A of U, over the q tile) and T diag(beta gamma) (A of W)
   {
     const int t = tid;
@@ -353,8 +360,10 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
     mma_tile_mn(tb + 128, smem_u32(T2), smem_u32(Kt), 0);  // W = T diag(beta gamma) K    -> cols [128, 256)
     tc_commit(&bar[1]);
   }
+  if (tr) tr[5] = globaltimer_ns();
   const bool ok2 = ok1 && __syncthreads_and(mbar_wait(&bar[1], 1, a.timeout_ns));
   if (!ok2 && tid == 0) report_error(a.status, kErrMbarTimeout, 602, 0);
+  if (tr) tr[6] = globaltimer_ns();
   tc_fence_after();
   {
     const int t = tid;
@@ -380,6 +389,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
     }
     if (tid == 0) a.gC[oidx] = __expf(gcl);
   }
+  if (tr) tr[7] = globaltimer_ns();
   pdl_trigger();
   tc_fence_before();
   __syncthreads();
@@ -594,6 +604,20 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
 // qkv: bf16 [T, 2 Hk + Hv, 128] (q | k | v heads from gdn_conv_prep); g / beta fp32 [T, Hv]; ctab [chunks, 3]
 // int32 (first token, tokens, sequence); seq_chunk0 [S + 1] int32; scratch: w, qg, kh, p bf16
 // [chunks * Hv * 128, 128], uT fp32 [chunks * Hv * 128, 128], gC fp32 [chunks * Hv]; o fp32 [T, Hv, 128].
+static unsigned long long* g_chunk_trace = nullptr;
+static int64_t g_chunk_trace_cap = 0;
+// tuning: 8 timestamps per phase-1 CTA of the next gdn_chunked calls into `buf` (None: off)
+void gdn_chunk_trace(c10::optional<torch::Tensor> buf) {
+  if (buf.has_value() && buf->defined()) {
+    TORCH_CHECK(buf->is_cuda() && buf->dtype() == torch::kInt64 && buf->is_contiguous(), "gdn_chunk_trace: int64 cuda");
+    g_chunk_trace = reinterpret_cast<unsigned long long*>(buf->data_ptr<int64_t>());
+    g_chunk_trace_cap = buf->numel();
+  } else {
+    g_chunk_trace = nullptr;
+    g_chunk_trace_cap = 0;
+  }
+}
+
 void gdn_chunked(torch::Tensor qkv, torch::Tensor g, torch::Tensor beta, torch::Tensor state, torch::Tensor ctab,
                  torch::Tensor seq_chunk0, torch::Tensor seq_slot, torch::Tensor seq_has_state, bool write_state,
                  int64_t Hk, int64_t Hv, torch::Tensor w, torch::Tensor qg, torch::Tensor kh, torch::Tensor p,
@@ -627,6 +651,7 @@ void gdn_chunked(torch::Tensor qkv, torch::Tensor g, torch::Tensor beta, torch::
   a.o = o.data_ptr<float>();
   a.status = status.data_ptr<int>();
   a.timeout_ns = 2000000000ull;
+  a.trace = (nchunks * Hv * 8 <= g_chunk_trace_cap) ? g_chunk_trace : nullptr;
   // q|k|v copy as a 3-D map (128 elements, heads, tokens): a box is 64 elements x 1 head x 128 tokens
   CUtensorMap tqkv;
   {

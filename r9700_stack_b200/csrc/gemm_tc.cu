@@ -751,6 +751,19 @@ static CUtensorMap weight_tmap(const torch::Tensor& w, bool fp4, int64_t N, int6
   return fp4 ? tmap_fp4_kmajor(w.data_ptr(), N, K, 128) : tmap_u8_kmajor(w.data_ptr(), N, K, 128);
 }
 
+bool gemm_mx_swap(const CUtensorMap& tw, const torch::Tensor& x, const torch::Tensor& x_sf, const torch::Tensor& w_sf,
+                  bool w_fp4, bool w_tiled, torch::Tensor& out, const c10::optional<torch::Tensor>& residual, double alpha,
+                  torch::Tensor& status);
+
+static bool gemm_swap_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("R9K_GEMM_SWAP");
+    v = (e && (e[0] == '0' || e[0] == 's')) ? 0 : 1;  // "0" / "stock": weight rows on the MMA's M side
+  }
+  return v == 1;
+}
+
 static bool use_stream_k() {
   static int v = -1;
   if (v < 0) {
@@ -800,6 +813,9 @@ void gemm_mx(torch::Tensor w, torch::Tensor w_sf, bool w_fp4, torch::Tensor x, t
     p = plan_gemm((int)N, (int)M, (int)(K / 128), false, w_fp4);
     ta = weight_tmap(w, w_fp4, N, K, p.unpack);
   }
+  if (p.BN >= 128 && M >= 256 && !p.unpack && gemm_swap_enabled() &&
+      gemm_mx_swap(ta, x, x_sf, w_sf, w_fp4, w.dim() == 3, out, residual, alpha, status))
+    return;  // prefill-sized M: tokens on the MMA's M side, vector epilogue (gemm_swap.cu)
   if (f32) dispatch_bn<KIND_MX, false, EPI_F32>(ta, ta, tb, a, p, ws, st);
   else dispatch_bn<KIND_MX, false, EPI_BF16>(ta, ta, tb, a, p, ws, st);
 }

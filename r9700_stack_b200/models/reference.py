@@ -63,10 +63,13 @@ class ReferenceState:
 
 
 @torch.no_grad()
-def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Tensor:
-    """Process `tokens` (continuing from `st`); returns fp32 logits [len(tokens), vocab_local]."""
+def reference_forward(model, tokens: list[int], st: ReferenceState, quantize_acts: bool = True) -> torch.Tensor:
+    """Process `tokens` (continuing from `st`); returns fp32 logits [len(tokens), vocab_local].
+    ``quantize_acts=False`` keeps the activations in full precision before MX GEMMs and the MX lm_head
+    (the same weights, without the activation quantiser): the "truth" two differently-rounded runs of an
+    MX model are both measured against."""
     c, dev = model.cfg, model.device
-    mx = model.mx
+    mx = model.mx and quantize_acts
     T = len(tokens)
     pos = torch.arange(st.pos, st.pos + T, device=dev)
     resid = model.embed[torch.tensor(tokens, device=dev)].float()
@@ -83,7 +86,7 @@ def reference_forward(model, tokens: list[int], st: ReferenceState) -> torch.Ten
         y = _ffn(model, i, lay, h, tokens, mx)
     resid = bf16(resid + y)
     h = bf16(rmsnorm(resid, model.final_norm, c.rms_eps, c.norm_plus_one))
-    return _finish(model, h, st, T)
+    return _finish(model, h, st, T, quantize_acts)
 
 
 def _mixer(model, i, lay, h, pos, st, mx):
@@ -109,9 +112,9 @@ def _ffn(model, i, lay, h, tokens, mx):
     return bf16(_lin(Fn.silu(g) * u, lay["w_down"], mx))
 
 
-def _finish(model, h, st, T):
+def _finish(model, h, st, T, quantize_acts: bool = True):
     c = model.cfg
-    lm_mx = isinstance(model.lm_head, L.MXWeight)
+    lm_mx = isinstance(model.lm_head, L.MXWeight) and quantize_acts
     logits = (fake_mxfp8(h) if lm_mx else h) @ _w(model.lm_head).T
     st.pos += T
     # recurrent state is stored in the state dtype between steps

@@ -9,7 +9,7 @@ from __future__ import annotations
 import torch
 
 HOST_OPS = {"symm_alloc", "symm_free", "symm_ipc_handle", "symm_open", "symm_close", "symm_view",
-            "symm_collective_region_bytes", "p2p_probe", "gemm_trace"}
+            "symm_collective_region_bytes", "p2p_probe", "gemm_trace", "gdn_chunk_trace"}
 _done: set[str] = set()
 
 

@@ -306,6 +306,19 @@ def _bench_gdn_prefill(a) -> dict:
         stat = status.status(torch.device("cuda"))
         qkv = torch.cat([q, k, v], 1).bfloat16().contiguous()
         f = lambda i: ops.gdn_chunked(qkv, g, b, st, ctab, c0, slot, hs, True, Hk, Hv, *buf, o, stat)
+        if a.trace:
+            tr = torch.zeros(len(rows) * Hv * 8, dtype=torch.int64, device="cuda")
+            ops.gdn_chunk_trace(tr)
+            f(0)
+            torch.cuda.synchronize()
+            ops.gdn_chunk_trace(None)
+            t = tr.view(-1, 8).cpu().double()
+            t = t[t[:, 0] > 0]
+            names = ("entry", "tiles", "mma1", "LP", "solve", "Ttiles", "mma2", "out")
+            ph = {f"{names[i - 1]}->{names[i]}": round(float((t[:, i] - t[:, i - 1]).median()) / 1e3, 2)
+                  for i in range(1, 8)}
+            print(json.dumps({"gdn_phase1_median_us": ph, "ctas": int(t.shape[0]),
+                              "span_us": round(float(t[:, 7].max() - t[:, 0].min()) / 1e3, 1)}))
     else:
         f = lambda i: ops.gdn_recurrent(q, k, v, g, b, st, slot, s0, ln, hs, True, o)
     us = _time(f, a.reps, a.warmup, graph=not a.eager)
@@ -430,6 +443,7 @@ def main(argv=None):
     gd.add_argument("--state", choices=["bf16", "fp32"], default="bf16")
     gd.add_argument("--prefill", type=int, default=0, help="time the prefill recurrence over this many tokens")
     gd.add_argument("--chunked", action="store_true", help="with --prefill: the tcgen05 chunked kernels")
+    gd.add_argument("--trace", action="store_true", help="with --chunked: phase-1 timestamps")
     at = sub.add_parser("attn")
     at.add_argument("--S", type=int, default=16)
     at.add_argument("--ctx", type=int, default=8192)

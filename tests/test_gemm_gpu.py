@@ -78,7 +78,7 @@ def _ref_gemm(x_act, w_dq):
 @pytest.mark.parametrize("fp4", [True, False])
 @pytest.mark.parametrize("N,K,M", [(128, 128, 1), (256, 512, 16), (384, 1024, 40), (200, 512, 7), (256, 512, 130),
                                    (128, 4096, 1), (640, 2048, 300), (5120, 4096, 16), (640, 256, 5), (128, 8192, 3),
-                                   (2048, 512, 64), (1152, 17408, 2)])
+                                   (2048, 512, 64), (1152, 17408, 2), (2060, 1024, 513), (384, 512, 256)])
 def test_gemm_mx(L, fp4, N, K, M):
     torch.manual_seed(N + K + M)
     w = torch.randn(N, K) * 0.02

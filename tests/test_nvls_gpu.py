@@ -49,7 +49,7 @@ def _worker(rank, world, port, q):
                 out = torch.empty(world, a.numel(), dtype=torch.float32, device=dev)
                 c.all_gather(a, out)
                 torch.cuda.synchronize(dev)
-                want = torch.stack([_inp(r, 1004, 100 + it, torch.float32)[: a.numel()] for r in range(world)])
+                want = torch.stack([_inp(r, 4 * 1000 + 4, 100 + it, torch.float32)[: a.numel()] for r in range(world)])
                 if not torch.equal(out.cpu(), want):
                     res["errs"].append(f"ag it={it}")
             # graph replays of interleaved collectives

@@ -47,10 +47,12 @@ MX_CASES = ("hybrid", "hybrid_push", "hybrid_pull")
 
 
 def _oracle(model, prompt):
-    """fp32 PyTorch restatement of the same model (same weights, same quantisation points)."""
+    """fp32 PyTorch restatement of the same model (same weights) with unquantised activations: TP=1
+    and TP=N round their MXFP8 activations at different points (a TP all-reduce sums bf16 partials),
+    so both are measured against the model without the activation quantiser."""
     from r9700_stack_b200.models.reference import ReferenceState, reference_forward
 
-    return reference_forward(model, prompt, ReferenceState(model))[-1].float().cpu().numpy()
+    return reference_forward(model, prompt, ReferenceState(model), quantize_acts=False)[-1].float().cpu().numpy()
 
 
 def _generate(case, world, rank, dev, comm, oracle=False):
@@ -143,7 +145,8 @@ def _compare(case, got, ref):
     for i, ((toks, lg), (rtoks, rlg, *orc)) in enumerate(zip(got, ref)):
         if orc:
             # MXFP8 activations re-round differently once a sum is split over ranks, and random-init
-            # weights amplify that layer by layer: TP=N must be as close to the fp32 oracle as TP=1
+            # weights amplify that layer by layer: TP=N must be as close to the unquantised oracle as
+            # TP=1 (both carry the quantiser's error, at different points)
             o = orc[0]
             c1, cn = _cos(rlg[0], o), _cos(lg[0], o)
             if cn < c1 - 0.01:
