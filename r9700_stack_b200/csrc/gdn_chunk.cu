@@ -149,11 +149,12 @@ struct ChunkArgs {
 };
 
 // ------------------------------------------------------------------------------------------------
-// Phase 1: grid (chunks, Hv), 128 threads (thread t = token row t). q, k, v arrive as bf16 tiles by TMA
+// Phase 1: grid (chunks, Hv), 256 threads (token row t = tid % 128, each half of the threads taking half of
+// a row's columns; the blocked solve spreads over all 256). q, k, v arrive as bf16 tiles by TMA
 // from the conv step's [T, 2 Hk + Hv, 128] copy (one round trip); every later operand is formed in
 // shared memory or TMEM, so nothing is gathered column-wise from global memory.
 // ------------------------------------------------------------------------------------------------
-__global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tmQKV,
+__global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(const __grid_constant__ CUtensorMap tmQKV,
                                                                 const ChunkArgs a) {
   using namespace gch;
   extern __shared__ uint8_t smem_raw[];
@@ -203,20 +204,25 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   }
   // gates: inclusive prefix sum of the log decay over the chunk (warp scans + warp offsets)
   {
-    const int t = tid;
-    const float gv = t < n ? a.g[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
-    sb[t] = t < n ? a.beta[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
-    float sacc = gv;
+    const int t = tid & 127;
+    float sacc = 0.f;
+    if (tid < 128) {
+      const float gv = t < n ? a.g[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+      sb[t] = t < n ? a.beta[(int64_t)(t0 + t) * a.Hv + h] : 0.f;
+      sacc = gv;
 #pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float y = __shfl_up_sync(0xffffffffu, sacc, o);
-      if (lane >= o) sacc += y;
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, sacc, o);
+        if (lane >= o) sacc += y;
+      }
+      if (lane == 31) swsum[warp] = sacc;
     }
-    if (lane == 31) swsum[warp] = sacc;
     __syncthreads();
-    for (int w = 0; w < warp; ++w) sacc += swsum[w];
-    sgc[t] = sacc;
-    sgam[t] = __expf(sacc);
+    if (tid < 128) {
+      for (int w = 0; w < warp; ++w) sacc += swsum[w];
+      sgc[t] = sacc;
+      sgam[t] = __expf(sacc);
+    }
   }
   __syncthreads();
   const bool ok0 = mbar_wait(&bar[0], 0, a.timeout_ns);
@@ -230,14 +236,15 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   }
   // while the tensor cores run: gamma q rows and K-hat rows (gamma_C / gamma_t k_t) to global
   const float gcl = sgc[n - 1];
+  const int half = tid >> 7;  // 256 threads: token row t = tid % 128, column half `half`
   {
-    const int t = tid;
+    const int t = tid & 127;
     const bool in = t < n;
     const float gq = in ? sgam[t] : 0.f, gk = in ? __expf(fminf(gcl - sgc[t], 0.f)) : 0.f;
     __nv_bfloat16* qd = a.qg + (oidx * C + t) * D;
     __nv_bfloat16* kd = a.kh + (oidx * C + t) * D;
 #pragma unroll 1
-    for (int e = 0; e < D; e += 16) {
+    for (int e = half * 64; e < half * 64 + 64; e += 16) {
       float x[16], y[16];
       ld_tile16(Qt, t, e, x);
       ld_tile16(Kt, t, e, y);
@@ -256,14 +263,14 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   if (!ok1 && tid == 0) report_error(a.status, kErrMbarTimeout, 601, 0);
   if (tr) tr[2] = globaltimer_ns();
   tc_fence_after();
-  const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+  const uint32_t trow = tb + ((uint32_t)((warp & 3) * 32) << 16);  // warps w and w + 4 share a lane quadrant
   // ---- L row t (shared, fp32) and P row t (global, bf16)
   {
-    const int t = tid;
+    const int t = tid & 127;
     const float gct = sgc[t], bt = sb[t];
     __nv_bfloat16* pd = a.p + (oidx * C + t) * C;
 #pragma unroll 1
-    for (int j0 = 0; j0 < C; j0 += 16) {
+    for (int j0 = half * 64; j0 < half * 64 + 64; j0 += 16) {
       float kk[16], qk[16];
       if (ok1) {
         tmem_ld16(trow + j0, kk);
@@ -289,44 +296,48 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   // ---- T = (I + L)^-1 in place, blocks of 16 rows: diagonal blocks by forward substitution (thread =
   // column of its block), then block row i: X = L[i, <i] T[<i, <i], T[i, <i] = -T_ii X
   {
-    const int bi = tid >> 4, cc = tid & 15, base = bi * 16;
+    const int bi = (tid >> 4) & 7, cc = tid & 15, base = bi * 16;
     float tcol[16];
+    if (tid < 128) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) {
-      float acc = 0.f;
+      for (int r = 0; r < 16; ++r) {
+        float acc = 0.f;
 #pragma unroll
-      for (int j = 0; j < r; ++j) acc += Ls[(base + r) * LS + base + j] * tcol[j];
-      tcol[r] = r < cc ? 0.f : (r == cc ? 1.f : -acc);
+        for (int j = 0; j < r; ++j) acc += Ls[(base + r) * LS + base + j] * tcol[j];
+        tcol[r] = r < cc ? 0.f : (r == cc ? 1.f : -acc);
+      }
     }
     __syncthreads();  // every thread has read its diagonal block of L
+    if (tid < 128) {
 #pragma unroll
-    for (int r = 0; r < 16; ++r) Ls[(base + r) * LS + base + cc] = tcol[r];
-    for (int c2 = base + 16; c2 < C; ++c2) Ls[(base + cc) * LS + c2] = 0.f;  // strictly upper blocks
+      for (int r = 0; r < 16; ++r) Ls[(base + r) * LS + base + cc] = tcol[r];
+      for (int c2 = base + 16; c2 < C; ++c2) Ls[(base + cc) * LS + c2] = 0.f;  // strictly upper blocks
+    }
   }
   __syncthreads();
 #pragma unroll 1
   for (int i = 1; i < 8; ++i) {
     const int r = tid & 15, cg = tid >> 4;
     const int row = (16 * i + r) * LS;
-    // thread (r, cg) owns X[r][cg + 8 m], m < 2 i: one L load per k2 feeds all of its columns
+    // thread (r, cg) owns X[r][cg + 16 m], m < i: one L load per k2 feeds all of its columns
     // (independent accumulators, loads of T broadcast across the 16 threads of a column group)
-    float acc[14];
+    float acc[7];
 #pragma unroll
-    for (int m = 0; m < 14; ++m) acc[m] = 0.f;
+    for (int m = 0; m < 7; ++m) acc[m] = 0.f;
 #pragma unroll 2
     for (int k2 = 0; k2 < 16 * i; ++k2) {
       const float lv = Ls[row + k2];
 #pragma unroll
-      for (int m = 0; m < 14; ++m) {
-        const int c = cg + 8 * m;
-        if (m < 2 * i && k2 >= c) acc[m] += lv * Ls[k2 * LS + c];
+      for (int m = 0; m < 7; ++m) {
+        const int c = cg + 16 * m;
+        if (m < i && k2 >= c) acc[m] += lv * Ls[k2 * LS + c];
       }
     }
 #pragma unroll
-    for (int m = 0; m < 14; ++m)
-      if (m < 2 * i) Xs[r * LS + cg + 8 * m] = acc[m];
+    for (int m = 0; m < 7; ++m)
+      if (m < i) Xs[r * LS + cg + 16 * m] = acc[m];
     __syncthreads();
-    for (int c = cg; c < 16 * i; c += 8) {
+    for (int c = cg; c < 16 * i; c += 16) {
       float acc = 0.f;
 #pragma unroll
       for (int m = 0; m < 16; ++m) acc += Ls[row + 16 * i + m] * Xs[m * LS + c];
@@ -337,9 +348,9 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   if (tr) tr[4] = globaltimer_ns();
   // ---- T diag(beta) (A of U, over the q tile) and T diag(beta gamma) (A of W)
   {
-    const int t = tid;
+    const int t = tid & 127;
 #pragma unroll 1
-    for (int e = 0; e < C; e += 16) {
+    for (int e = half * 64; e < half * 64 + 64; e += 16) {
       float x[16], y[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
@@ -366,12 +377,12 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_prep_kernel(const __grid_con
   if (tr) tr[6] = globaltimer_ns();
   tc_fence_after();
   {
-    const int t = tid;
+    const int t = tid & 127;
     const bool in = t < n && ok2;
     float* ut = a.uT + oidx * D * C;
     __nv_bfloat16* wd = a.w + (oidx * C + t) * D;
 #pragma unroll 1
-    for (int e = 0; e < D; e += 16) {
+    for (int e = half * 64; e < half * 64 + 64; e += 16) {
       float u[16], w[16];
       if (ok2) {
         tmem_ld16(trow + e, u);
@@ -494,7 +505,7 @@ __global__ void __launch_bounds__(160, 1) gdn_chunk_scan_kernel(const __grid_con
   } else {
     // ------------------------------ epilogue warps ------------------------------
     const int nrow = tid;  // state column n = TMEM lane n
-    const uint32_t trow = tb + ((uint32_t)(warp * 32) << 16);
+    const uint32_t trow = tb + ((uint32_t)((warp & 3) * 32) << 16);  // warps w and w + 4 share a lane quadrant
     ST* Sp = state + (((int64_t)slot * a.Hv + h) * D + nrow) * D;  // S^T row n (= state column n)
     const bool hs = a.seq_has_state[s] != 0;
     if (tid == 0 && c1 > c0) {
@@ -665,7 +676,7 @@ void gdn_chunked(torch::Tensor qkv, torch::Tensor g, torch::Tensor beta, torch::
     TORCH_CHECK(r == CUDA_SUCCESS, "gdn_chunked: q|k|v tensor map (", (int)r, ")");
   }
   TORCH_CHECK(ensure_smem_attr((const void*)gdn_chunk_prep_kernel, P1_SMEM) == cudaSuccess, "gdn_chunked: smem");
-  TORCH_CHECK(launch_pdl(gdn_chunk_prep_kernel, dim3((unsigned)nchunks, (unsigned)Hv), dim3(128), (size_t)P1_SMEM, st,
+  TORCH_CHECK(launch_pdl(gdn_chunk_prep_kernel, dim3((unsigned)nchunks, (unsigned)Hv), dim3(256), (size_t)P1_SMEM, st,
                          tqkv, a) == cudaSuccess,
               "gdn_chunk_prep launch");
   const CUtensorMap tW = tmap_bf16_kmajor(w.data_ptr(), rows, D, D, 128);

@@ -1,4 +1,4 @@
-// Prefill-sized MX GEMM with the token dimension on the MMA's M side ("swap AB").
+// Prefill-sized MX and bf16 GEMMs with the token dimension on the MMA's M side ("swap AB").
 //
 // out[M, N] = X[M, K] W[N, K]^T. The skinny-GEMM kernel (gemm_tc.cu) puts 128 weight rows on TMEM
 // lanes, so its epilogue thread owns one output feature and writes it for every token: 2-byte stores
@@ -18,7 +18,7 @@
 
 namespace r9k {
 
-template <int BNW, int NP>
+template <int KIND, int BNW, int NP>
 struct SwapCfg {
   static constexpr int A_BYTES = 128 * 128;        // 128 tokens x 128 fp8
   static constexpr int B_BYTES = BNW * 128;        // BNW weight rows x 128 elements (1 byte each in smem)
@@ -26,22 +26,25 @@ struct SwapCfg {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + NP * A_BYTES;
   static constexpr int OFF_SFA = OFF_B + NP * B_BYTES;
-  static constexpr int OFF_SFB = OFF_SFA + NP * 512;
-  static constexpr int OFF_BAR = OFF_SFB + NP * 512 * NB;
+  static constexpr int SF_A = KIND == KIND_MX ? 512 : 0;   // scale-factor bytes per stage (MX only)
+  static constexpr int OFF_SFB = OFF_SFA + NP * SF_A;
+  static constexpr int OFF_BAR = OFF_SFB + NP * SF_A * NB;
   static constexpr int NUM_BARS = 2 * NP + 1;
   static constexpr int OFF_TMEMPTR = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = OFF_TMEMPTR + 16 + 1024;
   static constexpr int SF_STRIDE = 4 + 4 * NB;    // TMEM columns of one stage's scale factors
   static constexpr int SFA_COL = BNW;
   static constexpr int SFB_COL = BNW + 4;
-  static constexpr int USED = BNW + NP * SF_STRIDE;
+  static constexpr int USED = BNW + (KIND == KIND_MX ? NP * SF_STRIDE : 0);
   static constexpr int TMEM_COLS = USED <= 256 ? 256 : 512;
 };
 
-template <int BNW, int EPI, int NP>
+template <int KIND, int BNW, int EPI, int NP>
 __global__ void __launch_bounds__(192, 1)
     gemm_swap_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW, GemmArgs args) {
-  using C = SwapCfg<BNW, NP>;
+  using C = SwapCfg<KIND, BNW, NP>;
+  constexpr bool MX = KIND == KIND_MX;
+  constexpr int KBOX = MX ? 128 : 64;  // elements of K per stage (128-byte smem rows)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* l_full = reinterpret_cast<uint64_t*>(smem + C::OFF_BAR);
@@ -75,8 +78,9 @@ __global__ void __launch_bounds__(192, 1)
   // weight row tiles of this CTA inside N (a tile past N is neither loaded nor used: its columns are
   // masked in the epilogue, and its scale-factor chunk would lie outside the scale tensor)
   const int nb = min(C::NB, (args.N - f0 + 127) / 128);
-  const uint32_t w_tx = (uint32_t)((args.a_fmt == kFmtE2M1 ? 128 * 64 : 128 * 128) + 512) * (uint32_t)nb;
-  const uint32_t stage_tx = w_tx + 128 * 128 + 512;
+  const uint32_t w_tx =
+      (uint32_t)((MX && args.a_fmt == kFmtE2M1 ? 128 * 64 : 128 * 128) + C::SF_A) * (uint32_t)nb;
+  const uint32_t stage_tx = w_tx + 128 * 128 + C::SF_A;
 
   if (warp == 0) {
     // ------------------------------ TMA producer ------------------------------
@@ -90,15 +94,18 @@ __global__ void __launch_bounds__(192, 1)
         for (int b = 0; b < C::NB; ++b) {
           if (b >= nb) break;
           const int rows0 = f0 + b * 128;
-          load_a_tile(smem + C::OFF_B + s * C::B_BYTES + b * 128 * 128, &tmW, &l_full[s], args, q, 128, rows0, pol_w);
-          bulk_load(smem + C::OFF_SFB + (s * C::NB + b) * 512,
-                    args.sfa + ((int64_t)(rows0 >> 7) * kchunks_sf + q) * 512, 512, &l_full[s]);
+          load_a_tile(smem + C::OFF_B + s * C::B_BYTES + b * 128 * 128, &tmW, &l_full[s], args, q, KBOX, rows0, pol_w);
+          if constexpr (MX)
+            bulk_load(smem + C::OFF_SFB + (s * C::NB + b) * 512,
+                      args.sfa + ((int64_t)(rows0 >> 7) * kchunks_sf + q) * 512, 512, &l_full[s]);
         }
       };
       auto load_x = [&](int q) {
         const int s = q % NP;
-        tma_load_2d_hint(smem + C::OFF_A + s * C::A_BYTES, &tmX, &l_full[s], q * 128, t0, pol_x);
-        bulk_load(smem + C::OFF_SFA + s * 512, args.sfb + ((int64_t)(t0 >> 7) * kchunks_sf + q) * 512, 512, &l_full[s]);
+        tma_load_2d_hint(smem + C::OFF_A + s * C::A_BYTES, &tmX, &l_full[s], q * KBOX, t0, pol_x);
+        if constexpr (MX)
+          bulk_load(smem + C::OFF_SFA + s * 512, args.sfb + ((int64_t)(t0 >> 7) * kchunks_sf + q) * 512, 512,
+                    &l_full[s]);
       };
       const int npre = min(NP, nk);
       for (int q = 0; q < npre; ++q) load_w(q);  // weights do not depend on the previous kernel
@@ -127,18 +134,25 @@ __global__ void __launch_bounds__(192, 1)
         tc_fence_after();
         const uint32_t sa = smem_u32(smem + C::OFF_A + s * C::A_BYTES);
         const uint32_t sb = smem_u32(smem + C::OFF_B + s * C::B_BYTES);
-        const uint32_t sfo = (uint32_t)(s * C::SF_STRIDE);
-        tc_cp_32x128b_warpx4(tbase + C::SFA_COL + sfo, sdesc_sf(smem_u32(smem + C::OFF_SFA + s * 512)));
+        if constexpr (MX) {
+          const uint32_t sfo = (uint32_t)(s * C::SF_STRIDE);
+          tc_cp_32x128b_warpx4(tbase + C::SFA_COL + sfo, sdesc_sf(smem_u32(smem + C::OFF_SFA + s * 512)));
 #pragma unroll
-        for (int b = 0; b < C::NB; ++b)
-          tc_cp_32x128b_warpx4(tbase + C::SFB_COL + sfo + 4 * b,
-                               sdesc_sf(smem_u32(smem + C::OFF_SFB + (s * C::NB + b) * 512)));
+          for (int b = 0; b < C::NB; ++b)
+            tc_cp_32x128b_warpx4(tbase + C::SFB_COL + sfo + 4 * b,
+                                 sdesc_sf(smem_u32(smem + C::OFF_SFB + (s * C::NB + b) * 512)));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t idesc = idesc_block_scaled(kFmtE4M3, args.a_fmt, 128, BNW, (uint32_t)k, (uint32_t)k);
-          mma_mxf8f6f4_ss(tbase, sdesc_k_sw128(sa + 32 * k), sdesc_k_sw128(sb + 32 * k), idesc,
-                          (q > 0 || k > 0) ? 1u : 0u, (tbase + C::SFA_COL + sfo) | ((uint32_t)k << 30),
-                          (tbase + C::SFB_COL + sfo) | ((uint32_t)k << 30));
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t idesc = idesc_block_scaled(kFmtE4M3, args.a_fmt, 128, BNW, (uint32_t)k, (uint32_t)k);
+            mma_mxf8f6f4_ss(tbase, sdesc_k_sw128(sa + 32 * k), sdesc_k_sw128(sb + 32 * k), idesc,
+                            (q > 0 || k > 0) ? 1u : 0u, (tbase + C::SFA_COL + sfo) | ((uint32_t)k << 30),
+                            (tbase + C::SFB_COL + sfo) | ((uint32_t)k << 30));
+          }
+        } else {
+          constexpr uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, BNW);
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            mma_f16_ss(tbase, sdesc_k_sw128(sa + 32 * k), sdesc_k_sw128(sb + 32 * k), idesc, (q > 0 || k > 0) ? 1u : 0u);
         }
         tc_commit(&l_empty[s]);
       }
@@ -235,43 +249,15 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// x: e4m3 [M, K] + chunk scales; w: MX weight (row-major [N, K/2 | K] or tiled units) + chunk scales.
-// Returns false (nothing launched) where the shapes or strides do not fit the vector epilogue.
-bool gemm_mx_swap(const CUtensorMap& tw, const torch::Tensor& x, const torch::Tensor& x_sf, const torch::Tensor& w_sf,
-                  bool w_fp4, bool w_tiled, torch::Tensor& out, const c10::optional<torch::Tensor>& residual, double alpha,
-                  torch::Tensor& status) {
-  const int64_t N = out.size(1), M = x.size(0), K = x.size(1);
-  const bool f32 = out.dtype() == torch::kFloat32;
-  const int esz = f32 ? 4 : 2;
-  if ((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) || (out.stride(0) * esz) % 16) return false;
-  const bool has_res = residual.has_value() && residual->defined();
-  if (has_res && ((reinterpret_cast<uintptr_t>(residual->data_ptr()) & 15) || (residual->stride(0) * 2) % 16)) return false;
-  if (x_sf.numel() < ((M + 127) / 128) * ((K / 32 + 3) / 4) * 512) return false;
+template <int KIND>
+static bool swap_launch(const CUtensorMap& tx, const CUtensorMap& tw, GemmArgs& a, bool f32, int64_t M, int64_t N) {
   constexpr int BNW = 256, NP = 4;
-  using Cfg = SwapCfg<BNW, NP>;
-  GemmArgs a = {};
-  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
-  a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
-  a.a_tiled = w_tiled ? 1 : 0;
-  a.sfa = w_sf.data_ptr<uint8_t>();  // weight scales (B operand here)
-  a.sfb = x_sf.data_ptr<uint8_t>();  // activation scales (A operand here)
-  a.sf_kblocks = (int)(K / 32);
-  a.out = out.data_ptr(); a.ldo = (int)out.stride(0);
-  if (has_res) {
-    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
-    a.ldr = (int)residual->stride(0);
-  }
-  a.alpha = (float)alpha;
-  a.status = status.data_ptr<int>();
-  a.timeout_ns = 1000000000ull;
-  const CUtensorMap tx = tmap_u8_kmajor(x.data_ptr(), M, K, 128);
-  auto st = at::cuda::getCurrentCUDAStream();
-  const dim3 grid((unsigned)((N + BNW - 1) / BNW), (unsigned)((M + 127) / 128));
+  using Cfg = SwapCfg<KIND, BNW, NP>;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
+  cfg.gridDim = dim3((unsigned)((N + BNW - 1) / BNW), (unsigned)((M + 127) / 128));
   cfg.blockDim = dim3(192);
   cfg.dynamicSmemBytes = Cfg::SMEM_BYTES;
-  cfg.stream = st;
+  cfg.stream = at::cuda::getCurrentCUDAStream();
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -279,16 +265,72 @@ bool gemm_mx_swap(const CUtensorMap& tw, const torch::Tensor& x, const torch::Te
   cfg.numAttrs = 1;
   cudaError_t e;
   if (f32) {
-    auto kern = gemm_swap_kernel<BNW, EPI_F32, NP>;
-    TORCH_CHECK(ensure_smem_attr((const void*)kern, Cfg::SMEM_BYTES) == cudaSuccess, "gemm_mx_swap: smem");
+    auto kern = gemm_swap_kernel<KIND, BNW, EPI_F32, NP>;
+    TORCH_CHECK(ensure_smem_attr((const void*)kern, Cfg::SMEM_BYTES) == cudaSuccess, "gemm swap: smem");
     e = cudaLaunchKernelEx(&cfg, kern, tx, tw, a);
   } else {
-    auto kern = gemm_swap_kernel<BNW, EPI_BF16, NP>;
-    TORCH_CHECK(ensure_smem_attr((const void*)kern, Cfg::SMEM_BYTES) == cudaSuccess, "gemm_mx_swap: smem");
+    auto kern = gemm_swap_kernel<KIND, BNW, EPI_BF16, NP>;
+    TORCH_CHECK(ensure_smem_attr((const void*)kern, Cfg::SMEM_BYTES) == cudaSuccess, "gemm swap: smem");
     e = cudaLaunchKernelEx(&cfg, kern, tx, tw, a);
   }
-  TORCH_CHECK(e == cudaSuccess, "gemm_mx_swap launch: ", cudaGetErrorString(e));
+  TORCH_CHECK(e == cudaSuccess, "gemm swap launch: ", cudaGetErrorString(e));
   return true;
+}
+
+// the vector epilogue wants 16-byte aligned output / residual rows
+static bool swap_fits(const torch::Tensor& out, const c10::optional<torch::Tensor>& residual) {
+  const int esz = out.dtype() == torch::kFloat32 ? 4 : 2;
+  if ((reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) || (out.stride(0) * esz) % 16) return false;
+  if (residual.has_value() && residual->defined() &&
+      ((reinterpret_cast<uintptr_t>(residual->data_ptr()) & 15) || (residual->stride(0) * 2) % 16))
+    return false;
+  return true;
+}
+
+static void swap_common(GemmArgs& a, torch::Tensor& out, const c10::optional<torch::Tensor>& residual, double alpha,
+                        torch::Tensor& status) {
+  a.out = out.data_ptr(); a.ldo = (int)out.stride(0);
+  if (residual.has_value() && residual->defined()) {
+    a.residual = reinterpret_cast<const __nv_bfloat16*>(residual->data_ptr());
+    a.ldr = (int)residual->stride(0);
+  }
+  a.alpha = (float)alpha;
+  a.status = status.data_ptr<int>();
+  a.timeout_ns = 1000000000ull;
+}
+
+// x: e4m3 [M, K] + chunk scales; w: MX weight (row-major [N, K/2 | K] or tiled units) + chunk scales.
+// Returns false (nothing launched) where the shapes or strides do not fit the vector epilogue.
+bool gemm_mx_swap(const CUtensorMap& tw, const torch::Tensor& x, const torch::Tensor& x_sf, const torch::Tensor& w_sf,
+                  bool w_fp4, bool w_tiled, torch::Tensor& out, const c10::optional<torch::Tensor>& residual, double alpha,
+                  torch::Tensor& status) {
+  const int64_t N = out.size(1), M = x.size(0), K = x.size(1);
+  if (!swap_fits(out, residual)) return false;
+  if (x_sf.numel() < ((M + 127) / 128) * ((K / 32 + 3) / 4) * 512) return false;
+  GemmArgs a = {};
+  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 128);
+  a.a_fmt = w_fp4 ? kFmtE2M1 : kFmtE4M3;
+  a.a_tiled = w_tiled ? 1 : 0;
+  a.sfa = w_sf.data_ptr<uint8_t>();  // weight scales (B operand here)
+  a.sfb = x_sf.data_ptr<uint8_t>();  // activation scales (A operand here)
+  a.sf_kblocks = (int)(K / 32);
+  swap_common(a, out, residual, alpha, status);
+  const CUtensorMap tx = tmap_u8_kmajor(x.data_ptr(), M, K, 128);
+  return swap_launch<KIND_MX>(tx, tw, a, out.dtype() == torch::kFloat32, M, N);
+}
+
+// bf16 x [M, K] (row stride ldx) times bf16 w [N, K] (row stride ldw)
+bool gemm_bf16_swap(const torch::Tensor& w, const torch::Tensor& x, torch::Tensor& out,
+                    const c10::optional<torch::Tensor>& residual, double alpha, torch::Tensor& status) {
+  const int64_t N = w.size(0), M = x.size(0), K = x.size(1);
+  if (!swap_fits(out, residual)) return false;
+  GemmArgs a = {};
+  a.N = (int)N; a.M = (int)M; a.K = (int)K; a.kchunks = (int)(K / 64);
+  a.a_tiled = 0;
+  swap_common(a, out, residual, alpha, status);
+  const CUtensorMap tx = tmap_bf16_kmajor(x.data_ptr(), M, K, x.stride(0), 128);
+  const CUtensorMap tw = tmap_bf16_kmajor(w.data_ptr(), N, K, w.stride(0), 128);
+  return swap_launch<KIND_BF16>(tx, tw, a, out.dtype() == torch::kFloat32, M, N);
 }
 
 }  // namespace r9k

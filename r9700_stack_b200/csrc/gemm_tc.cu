@@ -755,6 +755,9 @@ bool gemm_mx_swap(const CUtensorMap& tw, const torch::Tensor& x, const torch::Te
                   bool w_fp4, bool w_tiled, torch::Tensor& out, const c10::optional<torch::Tensor>& residual, double alpha,
                   torch::Tensor& status);
 
+bool gemm_bf16_swap(const torch::Tensor& w, const torch::Tensor& x, torch::Tensor& out,
+                    const c10::optional<torch::Tensor>& residual, double alpha, torch::Tensor& status);
+
 static bool gemm_swap_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -1004,6 +1007,8 @@ void gemm_bf16(torch::Tensor w, torch::Tensor x, torch::Tensor out, c10::optiona
                           : gemm_sk_dispatch<KIND_BF16, false, EPI_BF16>(ta, ta, tb, a, *ws, st);
     if (done) return;
   }
+  if (p.BN >= 128 && M >= 256 && gemm_swap_enabled() && gemm_bf16_swap(w, x, out, residual, alpha, status))
+    return;  // prefill-sized M: tokens on the MMA's M side (gemm_swap.cu)
   if (f32) dispatch_bn<KIND_BF16, false, EPI_F32>(ta, ta, tb, a, p, ws, st);
   else dispatch_bn<KIND_BF16, false, EPI_BF16>(ta, ta, tb, a, p, ws, st);
 }

@@ -145,7 +145,8 @@ def test_swiglu_split_matches_dual(L):
     assert float(torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), dim=0)) > 0.999
 
 
-@pytest.mark.parametrize("N,K,M", [(128, 64, 1), (256, 512, 16), (384, 1024, 100), (256, 256, 513), (2048, 4096, 8)])
+@pytest.mark.parametrize("N,K,M", [(128, 64, 1), (256, 512, 16), (384, 1024, 100), (256, 256, 513), (2048, 4096, 8),
+                                   (2060, 512, 300)])
 def test_gemm_bf16(L, N, K, M):
     torch.manual_seed(11)
     w = (torch.randn(N, K) * 0.05).bfloat16()
