@@ -10,9 +10,10 @@ import torch.multiprocessing as mp
 from r9700_stack_b200.parallel.protocol_sim import ProtocolTimeout, SimRank, SimRegions
 
 
-def _worker(rank, world, regions, iters, n, stop_at, results):
+def _worker(rank, world, regions, iters, n, stop_at, results, start):
     rng = random.Random(rank)
     sr = SimRank(regions, rank, world, timeout_s=1.0)
+    start.wait(timeout=120)  # spawned ranks finish importing at different times; the skew under test starts here
     try:
         for it in range(iters):
             if stop_at is not None and rank == world - 1 and it == stop_at:
@@ -35,7 +36,9 @@ def _run(world, iters, stop_at=None):
     regions = SimRegions(world, 64)
     mgr = ctx.Manager()
     results = mgr.dict()
-    ps = [ctx.Process(target=_worker, args=(r, world, regions, iters, 64, stop_at, results)) for r in range(world)]
+    start = ctx.Barrier(world)
+    ps = [ctx.Process(target=_worker, args=(r, world, regions, iters, 64, stop_at, results, start))
+          for r in range(world)]
     for p in ps:
         p.start()
     for p in ps:
