@@ -825,13 +825,16 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// merge split-KV partials, apply the output gate, write bf16 and/or MXFP8. One warp per (token, head).
+// merge split-KV partials, apply the output gate, write bf16 and/or MXFP8. One warp per (token, head):
+// lane s holds split s's (max, sum), so the global max and the weighted sum are two shuffle
+// reductions, and the partial rows are requested four splits at a time (independent loads in flight
+// instead of one dependent read per split). Empty splits (sum 0) get weight 0 and are selected away,
+// so whatever their partial rows hold never reaches the output.
 __global__ void attn_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int T, int Hq,
                                     int nsplit, float v_scale, const __nv_bfloat16* __restrict__ gate, int64_t ld_gate,
                                     __nv_bfloat16* __restrict__ out_bf16, uint8_t* __restrict__ out_q,
                                     uint8_t* __restrict__ out_sf, int out_kblocks) {
   pdl_wait();
-  pdl_trigger();  // dependents may launch and prefetch while this grid runs
   pdl_trigger();  // the next GEMM may start streaming its weights
   constexpr int D = fa::D;
   const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
@@ -839,20 +842,33 @@ __global__ void attn_combine_kernel(const float* __restrict__ part_o, const floa
   if (gw >= (int64_t)T * Hq) return;
   const int tok = (int)(gw / Hq), head = (int)(gw % Hq);
   const float* ml = part_ml + gw * nsplit * 2;
-  const int used = nsplit;  // every split writes (max, sum); empty ones carry sum 0
-  float M = -INFINITY;
-  for (int s = 0; s < used; ++s) M = fmaxf(M, ml[2 * s]);
-  float L = 0.f, acc[8];
+  float m_l = -INFINITY, l_l = 0.f;
+  if (lane < nsplit) {
+    const float2 v = *reinterpret_cast<const float2*>(ml + 2 * lane);
+    m_l = v.x;
+    l_l = v.y;
+  }
+  const bool live = l_l > 0.f && m_l != -INFINITY;
+  float M = live ? m_l : -INFINITY;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+  const float w_l = live ? exp2f(m_l - M) : 0.f;
+  float L = w_l * l_l;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+  float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  for (int s = 0; s < used; ++s) {
-    const float m = ml[2 * s], l = ml[2 * s + 1];
-    if (l <= 0.f || m == -INFINITY) continue;
-    const float w = exp2f(m - M);
-    L += w * l;
-    const float* po = part_o + (gw * nsplit + s) * D;
+  const float* po0 = part_o + gw * nsplit * D + lane;
+#pragma unroll 4
+  for (int s = 0; s < nsplit; ++s) {
+    const float w = __shfl_sync(0xffffffffu, w_l, s);
+    const float* po = po0 + (int64_t)s * D;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) acc[i] += w * po[lane + 32 * i];
+    for (int i = 0; i < 8; ++i) {
+      const float p = po[32 * i];
+      acc[i] += w > 0.f ? w * p : 0.f;
+    }
   }
   const float inv = L > 0.f ? v_scale / L : 0.f;
 #pragma unroll
@@ -927,6 +943,7 @@ void attn_tc_decode(torch::Tensor q, torch::Tensor k_cache, torch::Tensor v_cach
   a.seq_start = seq_start.data_ptr<int32_t>();
   a.seq_len = seq_len.data_ptr<int32_t>();
   a.nsplit = (int)part_ml.size(1);
+  TORCH_CHECK(a.nsplit >= 1 && a.nsplit <= 32, "attn_tc: 1..32 KV splits (the combine keeps one split per lane)");
   TORCH_CHECK(part_o.size(0) >= T * a.Hq && part_o.size(1) == a.nsplit && part_o.size(2) == fa::D && part_o.is_contiguous() &&
                   part_ml.is_contiguous(), "attn_tc: part_o / part_ml must be contiguous [T*Hq, nsplit, ...]");
   TORCH_CHECK(seq_start.size(0) == S && S <= 65535, "attn_tc: seq count");

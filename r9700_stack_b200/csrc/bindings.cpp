@@ -118,6 +118,9 @@ void gdn_spec_commit(torch::Tensor table, int64_t Hk, int64_t Hv, int64_t dv, in
                      torch::Tensor seq_has_state);
 void spec_accept(torch::Tensor input_ids, torch::Tensor target, torch::Tensor seq_start, torch::Tensor seq_len,
                  torch::Tensor acc_len);
+void dspark_markov_step(torch::Tensor base, int64_t j, torch::Tensor embed, torch::Tensor head, torch::Tensor hrows,
+                        torch::Tensor conf_w, double min_conf, torch::Tensor prev, torch::Tensor run,
+                        torch::Tensor lengths, torch::Tensor drafts, torch::Tensor part, torch::Tensor counter);
 void mhc_seam(torch::Tensor R, c10::optional<torch::Tensor> so, c10::optional<torch::Tensor> post_in,
               c10::optional<torch::Tensor> comb_in, torch::Tensor fn, torch::Tensor scale, torch::Tensor base,
               double rms_eps, double pre_eps, double sk_eps, double post_mult, int64_t sk_repeat, torch::Tensor R_out,
@@ -264,6 +267,8 @@ TORCH_LIBRARY(r9k, m) {
   m.def("gdn_spec_commit(Tensor table, int Hk, int Hv, int dv, int C, int W, int ld, bool state_f32, "
         "Tensor seq_slot, Tensor seq_start, Tensor acc_len, Tensor seq_has_state) -> ()");
   m.def("spec_accept(Tensor input_ids, Tensor target, Tensor seq_start, Tensor seq_len, Tensor(a!) acc_len) -> ()");
+  m.def("dspark_markov_step(Tensor base, int j, Tensor embed, Tensor head, Tensor hrows, Tensor conf_w, float min_conf, "
+        "Tensor(a!) prev, Tensor(b!) run, Tensor(c!) lengths, Tensor(d!) drafts, Tensor(e!) part, Tensor(f!) counter) -> ()");
   m.def("mhc_seam(Tensor R, Tensor? so, Tensor? post_in, Tensor? comb_in, Tensor fn, Tensor scale, Tensor base, "
         "float rms_eps, float pre_eps, float sk_eps, float post_mult, int sk_repeat, Tensor(a!) R_out, "
         "Tensor(b!) post_out, Tensor(c!) comb_out, Tensor(d!) li, Tensor(e!) part) -> ()");
@@ -354,6 +359,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("gdn_conv_state_update", &r9k::gdn_conv_state_update);
   m.impl("gdn_spec_commit", &r9k::gdn_spec_commit);
   m.impl("spec_accept", &r9k::spec_accept);
+  m.impl("dspark_markov_step", &r9k::dspark_markov_step);
   m.impl("mhc_seam", &r9k::mhc_seam);
   m.impl("exl3_dequant", &r9k::exl3_dequant);
   m.impl("exl3_gemv", &r9k::exl3_gemv);

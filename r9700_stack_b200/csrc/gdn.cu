@@ -574,21 +574,44 @@ __global__ void __launch_bounds__(512, 2) gdn_decode_fused_kernel(
       asm volatile("cp.async.commit_group;" ::: "memory");
     }
   }
+  // ---- conv over q (128) | k (128) | the rep value heads (rep x 128) channels. The conv state (last
+  // written by this layer's previous step) and the conv weights do not depend on the preceding grid:
+  // they are read into registers before waiting on it; only the new projection row comes after.
+  constexpr int MAXCH = ((2 + MAXREP) * D + NT - 1) / NT;
+  const int nch = (2 + rep) * D;
+  auto chan = [&](int ch) {
+    const int part = ch / D, i = ch % D;
+    return part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + (kh * rep + part - 2) * D + i;
+  };
+  float cst[MAXCH][W - 1], cwt[MAXCH][W];
+#pragma unroll
+  for (int u = 0; u < MAXCH; ++u) {
+    const int ch = tid + u * NT;
+    if (ch < nch) {
+      const int cch = chan(ch);
+      const ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
+#pragma unroll
+      for (int w = 0; w < W - 1; ++w) cst[u][w] = hs ? to_f<ST>(cs[w]) : 0.f;
+#pragma unroll
+      for (int w = 0; w < W; ++w) cwt[u][w] = __bfloat162float(conv_w[(int64_t)cch * W + w]);
+    }
+  }
   pdl_wait();
   pdl_trigger();
-  // ---- conv over q (128) | k (128) | the rep value heads (rep x 128) channels
-  const int nch = (2 + rep) * D;
-  for (int ch = tid; ch < nch; ch += NT) {
+#pragma unroll
+  for (int u = 0; u < MAXCH; ++u) {
+    const int ch = tid + u * NT;
+    if (ch >= nch) break;
     const int part = ch / D, i = ch % D;
-    const int cch = part == 0 ? kh * D + i : part == 1 ? Hk * D + kh * D + i : 2 * Hk * D + (kh * rep + part - 2) * D + i;
+    const int cch = chan(ch);
     ST* cs = conv_state + ((int64_t)slot * C + cch) * (W - 1);
     float x[W];
 #pragma unroll
-    for (int w = 0; w < W - 1; ++w) x[w] = hs ? to_f<ST>(cs[w]) : 0.f;
+    for (int w = 0; w < W - 1; ++w) x[w] = cst[u][w];
     x[W - 1] = __bfloat162float(proj[(int64_t)t * ld + cch]);
     float acc = 0.f;
 #pragma unroll
-    for (int w = 0; w < W; ++w) acc += x[w] * __bfloat162float(conv_w[(int64_t)cch * W + w]);
+    for (int w = 0; w < W; ++w) acc += x[w] * cwt[u][w];
 #pragma unroll
     for (int w = 0; w < W - 1; ++w) cs[w] = from_f<ST>(x[w + 1]);
     const float y = silu_f(acc);

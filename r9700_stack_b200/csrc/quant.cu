@@ -41,14 +41,19 @@ __global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, con
                                      __nv_bfloat16* __restrict__ res_out, const __nv_bfloat16* __restrict__ w,
                                      int K, float eps, int plus_one, __nv_bfloat16* __restrict__ y, int64_t ldy,
                                      uint8_t* __restrict__ q, uint8_t* __restrict__ sf) {
-  pdl_wait();
-  pdl_trigger();  // dependents may launch and prefetch while this grid runs
-  pdl_trigger();  // the next GEMM may start streaming its weights
   __shared__ float sred[32];
   const int64_t r = blockIdx.x;
   const int kblocks = K / 32;
   const int blk = threadIdx.x;
   const bool act = blk < kblocks;
+  // the norm weights are parameters, not the preceding grid's output: read them before waiting on it
+  uint4 wraw[4];
+  if (act) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wraw[i] = reinterpret_cast<const uint4*>(w + blk * 32)[i];
+  }
+  pdl_wait();
+  pdl_trigger();  // the next GEMM may start streaming its weights
   float v[32];
   float ss = 0.f;
   if (act) {
@@ -106,12 +111,10 @@ __global__ void rmsnorm_quant_kernel(const TIn* __restrict__ x, int64_t ldx, con
   __syncthreads();
   if (!act) return;
   const float rr = rsqrtf(sred[0] / (float)K + eps);
-  const __nv_bfloat16* wb = w + blk * 32;
   float am = 0.f;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const uint4 raw = reinterpret_cast<const uint4*>(wb)[i];
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&wraw[i]);
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
       float wv = __bfloat162float(e[k]);

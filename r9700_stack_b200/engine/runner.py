@@ -4,7 +4,8 @@ Per step the host packs every int32 metadata field into one pinned buffer with a
 only on (tokens, sequences, block-table width), issues one ``cudaMemcpyAsync`` into a device buffer of
 the same layout and runs the model on views of it. Decode steps replay a CUDA graph captured per
 padded batch size (padding rows are real one-token sequences on the reserved block 0 / state slot 0,
-so they never touch live memory). Prefill steps run eagerly.
+so they never touch live memory), and speculative verify steps replay one captured per (padded batch
+size, rows per sequence). Prefill steps run eagerly.
 """
 from __future__ import annotations
 
@@ -67,8 +68,10 @@ class MetaBuffers:
         return m
 
 
-def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft: dict | None = None):
-    """Host-side metadata for a scheduled step. Returns (Layout, np.int32 array, sample_rows, chunks)."""
+def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft: dict | None = None,
+              pad_len: int = 1):
+    """Host-side metadata for a scheduled step: (Layout, np.int32 array). Sequences past the real ones
+    (up to ``pad_to_seqs``) are padding of ``pad_len`` tokens each; every padding token is sampled."""
     chunks = out.chunks
     S_real = len(chunks)
     S = max(S_real, pad_to_seqs)
@@ -110,13 +113,14 @@ def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft
             else:
                 logits_idx.append(t + n - 1)
         t += n
-    # padding sequences: one token each on block 0 / state slot 0, no KV write
+    # padding sequences: pad_len tokens each on block 0 / state slot 0, no KV write
     for i in range(S_real, S):
-        toks.append(0); pos.append(0); slots.append(-1); tseq.append(i); tctx.append(1)
-        tslot.append(0); tpic.append(0); ths.append(0)
-        sslot.append(0); sstart.append(t); slen.append(1); shs.append(0)
-        logits_idx.append(t)
-        t += 1
+        for j in range(pad_len):
+            toks.append(0); pos.append(j); slots.append(-1); tseq.append(i); tctx.append(j + 1)
+            tslot.append(0); tpic.append(j); ths.append(0)
+            logits_idx.append(t + j)
+        sslot.append(0); sstart.append(t); slen.append(pad_len); shs.append(0)
+        t += pad_len
     T = t
     R = len(logits_idx)
     lay = Layout(T, S, MB, R)
@@ -150,6 +154,7 @@ class ModelRunner:
         cap = 8 * max_tokens + 5 * max_seqs + 2 * max_tokens + max_seqs * max_blocks_per_seq + 64
         self.meta = MetaBuffers(self.device, cap)
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.spec_graphs: dict[tuple[int, int], torch.cuda.CUDAGraph] = {}  # (batch, rows per sequence)
         self.graph_pool = None
         self.sample_out = torch.zeros(self.ws.logit_rows, dtype=torch.int64, device=self.device)
         self.sample_host = torch.zeros(self.ws.logit_rows, dtype=torch.int64, pin_memory=True)
@@ -276,32 +281,79 @@ class ModelRunner:
             res[s.seq_id] = [t]
 
 
+    def _verify(self, meta: StepMeta, T: int, S: int) -> None:
+        """Target forward over every verified row with the recurrent state read-only, the argmax of
+        every row, greedy acceptance on the device and the commit of the accepted tokens."""
+        from .. import _native
+
+        self.model.forward(meta, self.ws, T, T)
+        torch.argmax(self.ws.logits[:T], dim=-1, out=self.sample_out[:T])
+        acc = self.ws.acc_len[:S]
+        _native.ops().spec_accept(meta.input_ids, self.sample_out, meta.seq_start, meta.seq_len, acc)
+        self.model.commit(meta, self.ws, acc)
+
+    def _spec_graph(self, b: int, n: int) -> tuple[torch.cuda.CUDAGraph, Layout]:
+        """The verify step of b sequences of n rows each (last token + n - 1 drafts) as a CUDA graph,
+        captured on first use on a padding-only batch (block 0, state slot 0, no KV writes)."""
+        from .scheduler import SchedulerOutput
+
+        lay, arr = pack_step(SchedulerOutput("decode", []), self.block_size, pad_to_seqs=b, pad_len=n)
+        lay_g = Layout(lay.T, lay.S, self.max_blocks_per_seq, lay.R)
+        g = self.spec_graphs.get((b, n))
+        if g is not None:
+            return g, lay_g
+        self._upload(_relayout(arr, lay, lay_g))
+        meta = self.meta.views(lay_g, write_state=False)
+        meta.host_seqs = [(i * n, n) for i in range(b)]  # every captured sequence has n rows
+        meta.host_max_ctx = None
+        s = torch.cuda.Stream(self.device)
+        s.wait_stream(torch.cuda.current_stream(self.device))
+        with torch.cuda.stream(s):
+            for _ in range(2):
+                self._verify(meta, lay_g.T, b)
+        torch.cuda.current_stream(self.device).wait_stream(s)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.graph_pool):
+            self._verify(meta, lay_g.T, b)
+        self.graph_pool = g.pool()
+        self.spec_graphs[(b, n)] = g
+        torch.cuda.synchronize(self.device)
+        return g, lay_g
+
     def execute_spec(self, out: SchedulerOutput, draft: dict[int, list[int]]):
         """Speculative verify + commit: run [last token, drafts] of every sequence with the recurrent
         state read-only, take the target's argmax at every position, accept drafts greedily on the device,
         fold the accepted tokens into the GDN state (one launch) and return per sequence the accepted
-        drafts plus the bonus token, and the number of verified positions committed."""
-        from .. import _native
-
-        lay, arr = pack_step(out, self.block_size, draft=draft)
-        assert lay.R == lay.T
-        self._upload(arr)
-        meta = self.meta.views(lay, write_state=False)
-        meta.host_seqs = _host_seqs(out, draft)
-        meta.host_max_ctx = _host_max_ctx(out, draft)
+        drafts plus the bonus token, and the number of verified positions committed. A step whose
+        sequences all carry the same number of drafts replays a graph captured per (padded batch size,
+        rows per sequence); other steps run eagerly."""
+        n = _uniform_rows(out, draft)
+        gb = self._graph_bs(len(out.chunks)) if n > 1 else None
         ev = None
         if self.device_events is not None:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-            ev[0].record()
-        self.model.forward(meta, self.ws, lay.T, lay.R)
-        R = lay.R
-        torch.argmax(self.ws.logits[:R], dim=-1, out=self.sample_out[:R])
-        acc = self.ws.acc_len[: lay.S]
-        _native.ops().spec_accept(meta.input_ids, self.sample_out, meta.seq_start, meta.seq_len, acc)
-        self.model.commit(meta, self.ws, acc)
+        if gb is not None:
+            g, lay_g = self._spec_graph(gb, n)
+            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb, draft=draft, pad_len=n)
+            self._upload(_relayout(arr, lay, lay_g))
+            if ev is not None:
+                ev[0].record()
+            g.replay()
+        else:
+            lay, arr = pack_step(out, self.block_size, draft=draft)
+            assert lay.R == lay.T
+            self._upload(arr)
+            meta = self.meta.views(lay, write_state=False)
+            meta.host_seqs = _host_seqs(out, draft)
+            meta.host_max_ctx = _host_max_ctx(out, draft)
+            if ev is not None:
+                ev[0].record()
+            self._verify(meta, lay.T, lay.S)
         if ev is not None:
             ev[1].record()
             self.device_events.append(ev)
+        R = sum(1 + len(draft.get(ch.seq.seq_id, [])) for ch in out.chunks)  # real rows lead the padding
         self.sample_host[:R].copy_(self.sample_out[:R], non_blocking=True)
         torch.cuda.current_stream(self.device).synchronize()
         self.d2h_bytes = R * 8
@@ -322,6 +374,13 @@ class ModelRunner:
         if hot:
             self._resample(hot, res)
         return res, accepted
+
+
+def _uniform_rows(out: SchedulerOutput, draft: dict[int, list[int]]) -> int:
+    """Rows per sequence when every sequence verifies one sampled token plus the same number of
+    drafts (the shape a verify graph is captured for), else 0."""
+    ns = {1 + len(draft.get(ch.seq.seq_id, [])) if ch.n == 1 and ch.sample else 0 for ch in out.chunks}
+    return ns.pop() if len(ns) == 1 else 0
 
 
 def _host_seqs(out: SchedulerOutput, draft=None) -> list[tuple[int, int]]:

@@ -292,42 +292,75 @@ class DSparkDrafter(ModelDrafter):
         self.markov_head = L.BF16Weight(wf.randn(V, rank, dtype=torch.bfloat16))
         self.conf_w = L.BF16Weight(wf.randn(1, c.hidden + rank, std=0.05, dtype=torch.bfloat16))
         self.min_conf = min_conf
-        mb = engine_cfg.max_batch
-        self._mk_logits = torch.zeros(mb, V, dtype=torch.float32, device=dev)
-        self._cat = torch.zeros(mb, c.hidden + rank, dtype=torch.bfloat16, device=dev)
-        self._conf = torch.zeros(mb, 1, dtype=torch.float32, device=dev)
+        self.vocab = V
+        mb, km, grid = engine_cfg.max_batch, k, -(-V // 512)
+        # refinement state on the device: drafts, running confidence, kept lengths, the per-CTA
+        # maxima of one launch and its arrival counter (re-armed by the launch itself)
+        self._mk_state = (torch.zeros(mb * km, dtype=torch.int64, device=dev),
+                          torch.zeros(mb, dtype=torch.float32, device=dev),
+                          torch.zeros(mb, dtype=torch.int32, device=dev),
+                          torch.zeros(64 * grid * 2, dtype=torch.float32, device=dev),
+                          torch.zeros(1, dtype=torch.int32, device=dev))
         self.last_lengths: list[int] = []
 
     def _block(self, feed, h_tgt, sched) -> None:
-        from ..ops import linear as L
-
         super()._block(feed, h_tgt, sched)  # fills self.ws.logits rows (B-1 per proposing sequence)
         prop = [f[0] for f in feed if f[0].seq_id in self.pending]
         if not prop:
             return
-        S, km = len(prop), self.k
-        V = self._mk_logits.shape[1]
-        rank = self.markov_embed.shape[1]
+        S, km, V = len(prop), self.k, self.vocab
         base = self.ws.logits[: S * km].view(S, km, V)
         hrows = self.ws.h_out[: S * km].view(S, km, -1)
         prev = torch.tensor([s.tokens[-1] for s in prop], dtype=torch.int64, device=self.model.device)
-        drafts, conf_run = [], torch.ones(S, device=self.model.device)
-        keep = torch.ones(S, dtype=torch.bool, device=self.model.device)
-        lengths = torch.zeros(S, dtype=torch.int64, device=self.model.device)
+        dl, ln = self.refine(base, hrows, prev)
+        self.last_lengths = ln
+        for s, row, n in zip(prop, dl, ln):
+            self.pending[s.seq_id] = row[: max(1, n)]
+
+    def refine(self, base: torch.Tensor, hrows: torch.Tensor, prev: torch.Tensor):
+        """Markov-refined drafts [S][k] and kept lengths [S] from the block drafter's logits
+        base [S, k, V] (fp32), its output rows hrows [S, k, H] and the last target token of every
+        sequence: one ``dspark_markov_step`` launch per draft position, one copy to the host."""
+        from .. import _native
+
+        S, km, V = base.shape
+        drafts, run, lengths, part, counter = self._mk_state
+        assert S * km <= drafts.numel(), "more proposing sequences than the engine's batch"
+        base, hrows, prev = base.contiguous(), hrows.contiguous(), prev.clone()
+        w_conf = self.conf_w.w.reshape(-1)
+        ops = _native.ops()
+        for c0 in range(0, S, 64):  # the kernel holds up to 64 sequences' embeddings in shared memory
+            c1 = min(S, c0 + 64)
+            for j in range(km):
+                ops.dspark_markov_step(base[c0:c1], j, self.markov_embed, self.markov_head.w, hrows[c0:c1], w_conf,
+                                       float(self.min_conf), prev[c0:c1], run[c0:c1], lengths[c0:c1],
+                                       drafts[c0 * km:c1 * km], part, counter)
+        host = torch.cat([drafts[: S * km], lengths[:S].long()]).cpu()
+        return host[: S * km].view(S, km).tolist(), host[S * km:].tolist()
+
+    def refine_reference(self, base: torch.Tensor, hrows: torch.Tensor, prev: torch.Tensor):
+        """The same refinement as :meth:`refine` in plain torch ops (fp32 logits), for tests."""
+        from ..ops import linear as L
+
+        S, km, V = base.shape
+        dev = base.device
+        drafts, conf_run = [], torch.ones(S, device=dev)
+        keep = torch.ones(S, dtype=torch.bool, device=dev)
+        lengths = torch.zeros(S, dtype=torch.int64, device=dev)
+        H = hrows.shape[-1]
+        mk = torch.zeros(S, V, dtype=torch.float32, device=dev)
+        cat = torch.zeros(S, H + self.markov_embed.shape[1], dtype=torch.bfloat16, device=dev)
+        conf = torch.zeros(S, 1, dtype=torch.float32, device=dev)
         for j in range(km):
             e_prev = self.markov_embed.index_select(0, prev)
-            L.bf16_linear(e_prev, self.markov_head, out=self._mk_logits[:S], out_dtype=torch.float32)
-            d = torch.argmax(base[:, j] + self._mk_logits[:S], dim=-1)
-            self._cat[:S, : hrows.shape[-1]].copy_(hrows[:, j])
-            self._cat[:S, hrows.shape[-1]:].copy_(self.markov_embed.index_select(0, d))
-            L.bf16_linear(self._cat[:S], self.conf_w, out=self._conf[:S], out_dtype=torch.float32)
-            conf_run = conf_run * torch.sigmoid(self._conf[:S, 0])
+            L.bf16_linear(e_prev, self.markov_head, out=mk, out_dtype=torch.float32)
+            d = torch.argmax(base[:, j] + mk, dim=-1)
+            cat[:, :H].copy_(hrows[:, j])
+            cat[:, H:].copy_(self.markov_embed.index_select(0, d))
+            L.bf16_linear(cat, self.conf_w, out=conf, out_dtype=torch.float32)
+            conf_run = conf_run * torch.sigmoid(conf[:, 0])
             keep = keep & ((conf_run >= self.min_conf) | (j == 0))
             lengths += keep.long()
             drafts.append(d)
             prev = d
-        dl = torch.stack(drafts, 1).tolist()
-        ln = lengths.tolist()
-        self.last_lengths = ln
-        for s, row, n in zip(prop, dl, ln):
-            self.pending[s.seq_id] = row[: max(1, n)]
+        return torch.stack(drafts, 1).tolist(), lengths.tolist()

@@ -170,3 +170,25 @@ def test_dspark_adaptive_lengths():
     st = llm.spec_stats
     assert st["steps"] > 0 and 0 < st["drafted"] < st["steps"] * 3 * 4 + 1
     assert all(1 <= n <= 4 for n in llm.drafter.last_lengths)
+
+
+def test_dspark_markov_kernel_matches_torch():
+    """The one-launch-per-position Markov refinement (argmax over the vocabulary, confidence head,
+    kept lengths) against the same refinement in torch ops with fp32 logits, two rounds in a row
+    (the launch re-arms its own arrival counter)."""
+    from r9700_stack_b200.models.config import tiny_hybrid
+
+    llm = _engine(tiny_hybrid(gdn_state_dtype="fp32"), k=4, method="dspark")
+    dr = llm.drafter
+    dr.min_conf = 0.5
+    g = torch.Generator(device="cuda").manual_seed(9)
+    S, km, V = 3, 4, dr.vocab
+    H = dr.conf_w.w.shape[1] - dr.markov_embed.shape[1]
+    for _ in range(2):
+        base = torch.randn(S, km, V, device="cuda", generator=g)
+        hrows = torch.randn(S, km, H, device="cuda", generator=g).bfloat16()
+        prev = torch.randint(0, V, (S,), device="cuda", generator=g)
+        got = dr.refine(base, hrows, prev)
+        want = dr.refine_reference(base, hrows, prev)
+        _check()
+        assert got == want, (got, want)
