@@ -90,8 +90,9 @@ template <int CB>
 __global__ void __launch_bounds__(256) exl3_dequant_kernel(const uint16_t* __restrict__ trellis, int K,
                                                           const __half* __restrict__ suh, const __half* __restrict__ svh,
                                                           int n_in, int n_out, __nv_bfloat16* __restrict__ out) {
+  // no early trigger: the output is a GEMM weight, and the GEMM requests its first weight tiles
+  // before its own grid-dependency wait, so it must not start until this grid has finished
   pdl_wait();
-  pdl_trigger();
   extern __shared__ float sw[];  // [128][129]
   const int ob = blockIdx.x, ib = blockIdx.y, tid = threadIdx.x;
   const int nw = 16 * K, to_n = n_out / 16;

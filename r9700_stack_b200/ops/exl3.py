@@ -65,9 +65,13 @@ class Exl3Linear:
         return self.trellis.numel() * 2 + self.suh.numel() * 2 + self.svh.numel() * 2
 
     def dequant_bf16(self) -> L.BF16Weight:
+        """The effective weight as bf16 [out, in], for wide batches (a load-time conversion). The
+        tcgen05 GEMM requests its first weight tiles before waiting on the preceding kernel, so the
+        stream is drained here: no GEMM may start while the dequantisation is still writing."""
         assert not self.stacked
         out = torch.empty(self.n_out, self.n_in, dtype=torch.bfloat16, device=self.trellis.device)
         _ops().exl3_dequant(self.trellis, self.suh, self.svh, self.K, self.cb, out)
+        torch.cuda.current_stream(out.device).synchronize()
         return L.BF16Weight(out)
 
     def gemv(self, x: torch.Tensor, out: torch.Tensor, work=None, work_count=None, n_items: int = 1,

@@ -103,7 +103,9 @@ class Exl3LinearMethod(LinearMethodBase):
         cb = E.MCG if self.cfg.codebook == "mcg" else E.MUL1
         layer.r9k_exl3 = X.Exl3Linear(layer.trellis.data.contiguous(), layer.suh.data.contiguous(),
                                       layer.svh.data.contiguous(), self.K, cb)
-        layer.r9k_dense = None  # bf16 weight, made on the first wide batch
+        # bf16 weight for wide batches (M > 16), made now: at load time, outside any graph capture,
+        # and finished before a GEMM reads it
+        layer.r9k_dense = layer.r9k_exl3.dequant_bf16()
 
     def apply(self, layer: torch.nn.Module, x: torch.Tensor, bias: torch.Tensor | None = None) -> torch.Tensor:
         w: X.Exl3Linear = layer.r9k_exl3
@@ -114,8 +116,6 @@ class Exl3LinearMethod(LinearMethodBase):
             out = torch.empty(M, w.n_out, dtype=torch.bfloat16, device=x.device)
             w.gemv(x2, out)
         else:
-            if layer.r9k_dense is None:
-                layer.r9k_dense = w.dequant_bf16()
             out = L.bf16_linear(x2, layer.r9k_dense)
         if bias is not None:
             out = out + bias
