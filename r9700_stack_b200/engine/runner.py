@@ -68,47 +68,73 @@ class MetaBuffers:
         return m
 
 
+def _token_ids(seq, start: int, n: int) -> list[int]:
+    """Tokens [start, start + n) of a sequence without joining its prompt and output."""
+    P = len(seq.prompt)
+    if start >= P:
+        return seq.output[start - P : start - P + n]
+    if start + n <= P:
+        return seq.prompt[start : start + n]
+    return seq.prompt[start:] + seq.output[: start + n - P]
+
+
+def _block_row(seq) -> np.ndarray:
+    """The sequence's block list as int32, rebuilt only when a block was added or the list replaced."""
+    row = getattr(seq, "_bt_row", None)
+    if row is None or row[0] is not seq.blocks or row[1].shape[0] != len(seq.blocks):
+        row = (seq.blocks, np.asarray(seq.blocks, dtype=np.int32))
+        seq._bt_row = row
+    return row[1]
+
+
 def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft: dict | None = None,
-              pad_len: int = 1):
+              pad_len: int = 1, mb: int | None = None):
     """Host-side metadata for a scheduled step: (Layout, np.int32 array). Sequences past the real ones
-    (up to ``pad_to_seqs``) are padding of ``pad_len`` tokens each; every padding token is sampled."""
+    (up to ``pad_to_seqs``) are padding of ``pad_len`` tokens each; every padding token is sampled.
+    ``mb`` fixes the block-table width (a captured graph's); by default it is the widest sequence's."""
     chunks = out.chunks
     S_real = len(chunks)
     S = max(S_real, pad_to_seqs)
     toks, pos, slots, tseq, tctx, tslot, tpic, ths = [], [], [], [], [], [], [], []
     sslot, sstart, slen, shs = [], [], [], []
     logits_idx = []
-    MB = 1
-    for ch in chunks:
-        MB = max(MB, len(ch.seq.blocks))
-    MB = max(MB, 1)
-    bt = np.zeros((S, MB), dtype=np.int32)
+    rows = [_block_row(ch.seq) for ch in chunks]
+    MB = max([1] + [r.shape[0] for r in rows])
+    if mb is not None:
+        assert mb >= MB, "block table wider than the captured layout"
+        MB = mb
     t = 0
     for i, ch in enumerate(chunks):
         seq = ch.seq
-        all_toks = seq.tokens
-        ids = all_toks[ch.start : ch.start + ch.n]
-        if draft is not None and seq.seq_id in draft:
-            ids = ids + draft[seq.seq_id]
+        ids = _token_ids(seq, ch.start, ch.n)
+        d = draft.get(seq.seq_id) if draft is not None else None
+        if d:
+            ids = ids + d
         n = len(ids)
-        p = np.arange(ch.start, ch.start + n, dtype=np.int64)
-        blocks = np.asarray(seq.blocks, dtype=np.int64)
-        toks.extend(ids)
-        pos.extend(p.tolist())
-        slots.extend((blocks[p // block_size] * block_size + p % block_size).tolist())
-        tseq.extend([i] * n)
-        tctx.extend((p + 1).tolist())
-        tslot.extend([seq.state_slot] * n)
-        tpic.extend(range(n))
+        blocks = seq.blocks
         hs = 1 if ch.start > 0 else 0
+        toks.extend(ids)
+        if n == 1:
+            p0 = ch.start
+            pos.append(p0)
+            slots.append(blocks[p0 // block_size] * block_size + p0 % block_size)
+            tctx.append(p0 + 1)
+            tpic.append(0)
+        else:
+            p = np.arange(ch.start, ch.start + n, dtype=np.int64)
+            pos.extend(p.tolist())
+            slots.extend((rows[i][p // block_size].astype(np.int64) * block_size + p % block_size).tolist())
+            tctx.extend((p + 1).tolist())
+            tpic.extend(range(n))
+        tseq.extend([i] * n)
+        tslot.extend([seq.state_slot] * n)
         ths.extend([hs] * n)
         sslot.append(seq.state_slot)
         sstart.append(t)
         slen.append(n)
         shs.append(hs)
-        bt[i, : len(seq.blocks)] = seq.blocks
         if ch.sample:
-            if draft is not None and seq.seq_id in draft:
+            if d:
                 logits_idx.extend(range(t + ch.n - 1, t + n))
             else:
                 logits_idx.append(t + n - 1)
@@ -131,7 +157,9 @@ def pack_step(out: SchedulerOutput, block_size: int, pad_to_seqs: int = 0, draft
                        ("tok_has_state", ths), ("seq_state_slot", sslot), ("seq_start", sstart),
                        ("seq_len", slen), ("seq_has_state", shs), ("logits_idx", logits_idx)):
         arr[off[name] : off[name] + len(vals)] = vals
-    arr[off["block_table"] : off["block_table"] + S * MB] = bt.reshape(-1)
+    bt = arr[off["block_table"] : off["block_table"] + S * MB].reshape(S, MB)
+    for i, r in enumerate(rows):
+        bt[i, : r.shape[0]] = r
     return lay, arr
 
 
@@ -222,9 +250,7 @@ class ModelRunner:
             return {}
         gb = self._graph_bs(len(out.chunks)) if (out.kind == "decode" and draft is None) else None
         if gb is not None:
-            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb)
-            lay_g = Layout(lay.T, lay.S, self.max_blocks_per_seq, lay.R)
-            arr = _relayout(arr, lay, lay_g)
+            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb, mb=self.max_blocks_per_seq)
             self._upload(arr)
             if self.device_events is not None:
                 ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -335,8 +361,9 @@ class ModelRunner:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
         if gb is not None:
             g, lay_g = self._spec_graph(gb, n)
-            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb, draft=draft, pad_len=n)
-            self._upload(_relayout(arr, lay, lay_g))
+            lay, arr = pack_step(out, self.block_size, pad_to_seqs=gb, draft=draft, pad_len=n,
+                                 mb=self.max_blocks_per_seq)
+            self._upload(arr)
             if ev is not None:
                 ev[0].record()
             g.replay()

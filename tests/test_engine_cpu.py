@@ -68,6 +68,34 @@ def test_pack_step_metadata():
     assert (bt2[:, :lay.MB] == bt).all() and (bt2[:, lay.MB:] == 0).all()
 
 
+def test_pack_step_decode_fast_path_matches_relayout():
+    """Decode packing (one token per sequence, read without joining prompt and output, block rows
+    cached per sequence) written straight at a graph's table width equals the default packing
+    re-laid to that width; drafts extend a row; a chunk straddling prompt and output reads both."""
+    s = _sched()
+    a = Sequence(list(range(6)), SamplingParams(max_tokens=8))
+    b = Sequence(list(range(3)), SamplingParams(max_tokens=8))
+    s.add(a); s.add(b)
+    s.finish_step(s.schedule(), {a.seq_id: [40], b.seq_id: [50]})
+    for step in range(3):
+        out = s.schedule()
+        lay, arr = pack_step(out, 4, pad_to_seqs=4)
+        lay_w, arr_w = pack_step(out, 4, pad_to_seqs=4, mb=9)
+        assert (lay_w.T, lay_w.S, lay_w.MB, lay_w.R) == (lay.T, lay.S, 9, lay.R)
+        assert (arr_w == _relayout(arr, lay, Layout(lay.T, lay.S, 9, lay.R))).all()
+        off, _ = lay.offsets()
+        assert arr[off["input_ids"]:off["input_ids"] + 2].tolist() == [a.tokens[-1], b.tokens[-1]]
+        s.finish_step(out, {a.seq_id: [41 + step], b.seq_id: [51 + step]})
+    out = s.schedule(lookahead=3)
+    lay, arr = pack_step(out, 4, draft={a.seq_id: [7, 8]})
+    off, _ = lay.offsets()
+    assert arr[off["input_ids"]:off["input_ids"] + lay.T].tolist() == [a.tokens[-1], 7, 8, b.tokens[-1]]
+    assert arr[off["positions"]:off["positions"] + 3].tolist() == [a.length - 1, a.length, a.length + 1]
+    from r9700_stack_b200.engine.runner import _token_ids
+
+    assert _token_ids(a, 4, 4) == a.tokens[4:8]
+
+
 def test_preemption_when_out_of_blocks():
     s = _sched(num_blocks=6, block_size=4, max_prefill_tokens=64)
     seqs = [Sequence(list(range(7)), SamplingParams(max_tokens=8)) for _ in range(2)]
