@@ -142,6 +142,9 @@ void topk_select(torch::Tensor scores, torch::Tensor tok_ctx, int64_t k, torch::
 void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
                        torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
                        torch::Tensor part_ml, torch::Tensor out);
+void sparse_mla_decode_tc(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
+                          torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
+                          torch::Tensor part_ml, torch::Tensor out, torch::Tensor status);
 void head_gemv(torch::Tensor x, torch::Tensor W, torch::Tensor out);
 void host_gather(torch::Tensor table, torch::Tensor ids, int64_t fmt, int64_t dim, torch::Tensor out);
 void moe_gather_bf16(torch::Tensor x, int64_t k, torch::Tensor perm_row, torch::Tensor out);
@@ -285,6 +288,8 @@ TORCH_LIBRARY(r9k, m) {
   m.def("topk_select(Tensor scores, Tensor tok_ctx, int k, Tensor(a!) out, Tensor(b!) count) -> ()");
   m.def("sparse_mla_decode(Tensor q, Tensor lat_cache, Tensor block_table, Tensor tok_seq, Tensor sel, "
         "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out) -> ()");
+  m.def("sparse_mla_decode_tc(Tensor q, Tensor lat_cache, Tensor block_table, Tensor tok_seq, Tensor sel, "
+        "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out, Tensor(d!) status) -> ()");
   m.def("head_gemv(Tensor x, Tensor W, Tensor(a!) out) -> ()");
   m.def("host_gather(Tensor table, Tensor ids, int fmt, int dim, Tensor(a!) out) -> ()");
   m.def("moe_gather_bf16(Tensor x, int k, Tensor perm_row, Tensor(a!) out) -> ()");
@@ -369,6 +374,7 @@ TORCH_LIBRARY_IMPL(r9k, CUDA, m) {
   m.impl("indexer_score", &r9k::indexer_score);
   m.impl("topk_select", &r9k::topk_select);
   m.impl("sparse_mla_decode", &r9k::sparse_mla_decode);
+  m.impl("sparse_mla_decode_tc", &r9k::sparse_mla_decode_tc);
   m.impl("head_gemv", &r9k::head_gemv);
   m.impl("moe_gather_bf16", &r9k::moe_gather_bf16);
   m.impl("ngram_ids", &r9k::ngram_ids);

@@ -472,6 +472,303 @@ void topk_select(torch::Tensor scores, torch::Tensor tok_ctx, int64_t k, torch::
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------------------------
+// sparse MLA on tcgen05: grid (T, ceil(H / 32), nsplit), 128 threads. The selected latent rows sit on
+// the MMA's M side (128 keys per tile) and up to 32 heads on N:
+//   S^T [keys x heads]  = K [keys x 576] . Q^T              (9 K-major planes of 64 dims each)
+//   O^T [dims x heads] += V^T [dims x keys] . P^T [keys x heads]   (V^T: the same planes, MN-major)
+// Thread r owns key row r (TMEM lane r) for the softmax; column (head) maxima and sums are butterfly
+// reductions inside a warp (31 shuffles for 32 columns) and four partials across warps. O^T lives in
+// TMEM (4 tiles of 128 dims x 32 heads) and is rescaled in place when a head's maximum grows. The
+// gathered rows are written by cp.async into the 128-byte-swizzled layout the MMA descriptors read,
+// so no tensor map (and no gather TMA) is involved. Partials (o, max, sum) go to mla_combine.
+// (reference: kernels/r9k_sparse_mla.hip:99-205, the split-K sparse MLA decode it replaces with tensor
+// cores; the math is the CUDA-core sparse_mla_decode_kernel above.)
+// ------------------------------------------------------------------------------------------------
+namespace smla {
+constexpr int HN = 32, KT = 128, PLANES = ROW / 64;        // heads per CTA, keys per tile, 64-dim planes
+constexpr uint32_t KPLANE = KT * 128, QPLANE = HN * 128;  // bytes
+constexpr uint32_t OFF_K = 0, OFF_Q = OFF_K + PLANES * KPLANE, OFF_P = OFF_Q + PLANES * QPLANE;
+constexpr uint32_t OFF_END = OFF_P + 2 * QPLANE;
+constexpr int SMEM = (int)OFF_END + 1024;  // + 1 KiB alignment slack
+constexpr uint32_t TMEM_COLS = 256, COL_S = 0, COL_O = 32;
+}  // namespace smla
+
+R9K_DEVINL void cp_async16_sw(uint8_t* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile (8-row groups of 1 KiB)
+R9K_DEVINL uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// MN-major 128-byte-swizzled operand: rows along K (128 bytes = 64 elements of M or N per row), the two
+// 64-element halves `lbo` bytes apart, 8-row groups `sbo` bytes apart
+R9K_DEVINL uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// v[c] of every lane -> lane l returns the reduction of column l over the warp (transpose-reduce:
+// each step trades the half of the columns this lane does not keep)
+template <bool MAX>
+R9K_DEVINL float col_reduce32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) {
+    const bool up = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = up ? v[i] : v[i + k];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, k);
+      const float keep = up ? v[i + k] : v[i];
+      v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
+    }
+  }
+  return v[0];
+}
+
+__global__ void __launch_bounds__(128, 1) sparse_mla_tc_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq_t, int ldq_h, int H, const __nv_bfloat16* __restrict__ lat_cache,
+    const int32_t* __restrict__ bt, int mb, const int32_t* __restrict__ tok_seq, const int32_t* __restrict__ sel,
+    const int32_t* __restrict__ sel_count, int k, float scale, int nsplit, float* __restrict__ part_o,
+    float* __restrict__ part_ml, int* __restrict__ status) {
+  using namespace smla;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float red[4][32];
+  __shared__ float s_mnew[32], s_corr[32];
+  __shared__ int s_rescale;
+  const int t = blockIdx.x, hb = blockIdx.y * HN, split = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const uint64_t timeout_ns = 1000000000ull;
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_holder;
+  const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+  const uint32_t kbase = smem_u32(smem + OFF_K), qbase = smem_u32(smem + OFF_Q), pbase = smem_u32(smem + OFF_P);
+
+  pdl_wait();  // queries, selections and the cache rows come from the preceding kernels
+  pdl_trigger();
+  const int seq = tok_seq[t];
+  const int n = sel_count[t];
+  const int per = (n + nsplit - 1) / nsplit;  // the CUDA-core kernel's partition of the selected rows
+  const int j0 = min(n, split * per), j1 = min(n, j0 + per);
+
+  // the CTA's heads as 9 K-major planes of [32 rows][64 dims]
+  for (int e = tid; e < PLANES * HN * 8; e += 128) {
+    const int pl = e / (HN * 8), r = (e / 8) % HN, c = e % 8;
+    uint8_t* dst = smem + OFF_Q + pl * QPLANE + sw128_off(r, c);
+    if (hb + r < H) cp_async16_sw(dst, q + (int64_t)t * ldq_t + (int64_t)(hb + r) * ldq_h + pl * 64 + c * 8);
+    else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+  }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+
+  float m_run = -INFINITY, l_run = 0.f;  // running max / sum of head (hb + lane), kept by warp 0
+  uint32_t phase = 0;
+  int ntile = 0;
+  bool failed = false;  // a bounded MMA wait ran out (uniform over the CTA)
+  for (int c0 = j0; c0 < j1; c0 += KT) {
+    const int cnt = min(KT, j1 - c0);
+    const int pos = tid < cnt ? sel[(int64_t)t * k + c0 + tid] : -1;
+    const bool live = pos >= 0;
+    // key row tid -> row tid of every plane (zeros past the selection: V rows must stay finite)
+    if (live) {
+      const __nv_bfloat16* src = lat_cache + slot_of(bt, mb, seq, pos) * ROW;
+#pragma unroll
+      for (int pl = 0; pl < PLANES; ++pl)
+#pragma unroll
+        for (int c = 0; c < 8; ++c) cp_async16_sw(smem + OFF_K + pl * KPLANE + sw128_off(tid, c), src + pl * 64 + c * 8);
+    } else {
+#pragma unroll
+      for (int pl = 0; pl < PLANES; ++pl)
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+          *reinterpret_cast<uint4*>(smem + OFF_K + pl * KPLANE + sw128_off(tid, c)) = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;\n\tcp.async.wait_all;" ::: "memory");
+    fence_proxy_async();  // generic-proxy shared writes -> the MMA's async-proxy reads
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      constexpr uint32_t idS = idesc_dense(kFmtBF16, kFmtBF16, 128, HN);
+#pragma unroll 1
+      for (int pl = 0; pl < PLANES; ++pl)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tbase + COL_S, sdesc_k_sw128(kbase + pl * KPLANE + kk * 32),
+                     sdesc_k_sw128(qbase + pl * QPLANE + kk * 32), idS, (pl | kk) ? 1u : 0u);
+      tc_commit(&bar);
+    }
+    bool ok = mbar_wait(&bar, phase, timeout_ns);
+    phase ^= 1;
+    if (!__syncthreads_and(ok)) {
+      failed = true;
+      break;
+    }
+    tc_fence_after();
+    float sv[32];
+    tmem_ld16(trow + COL_S, sv);
+    tmem_ld16(trow + COL_S + 16, sv + 16);
+    tmem_ld_wait();
+#pragma unroll
+    for (int h = 0; h < 32; ++h) sv[h] = live ? sv[h] * scale : -INFINITY;
+    {
+      float v[32];
+#pragma unroll
+      for (int h = 0; h < 32; ++h) v[h] = sv[h];
+      red[warp][lane] = col_reduce32<true>(v, lane);
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const float mt = fmaxf(fmaxf(red[0][lane], red[1][lane]), fmaxf(red[2][lane], red[3][lane]));
+      const float mn = fmaxf(m_run, mt);
+      const float corr = (m_run == -INFINITY) ? 0.f : __expf(m_run - mn);
+      s_mnew[lane] = mn;
+      s_corr[lane] = corr;
+      m_run = mn;
+      const bool any = __any_sync(0xffffffffu, corr != 1.f);
+      if (lane == 0) s_rescale = any ? 1 : 0;
+    }
+    __syncthreads();
+    float pv[32];
+#pragma unroll
+    for (int h = 0; h < 32; ++h) {
+      const float mn = s_mnew[h];
+      const float e = (sv[h] == -INFINITY || mn == -INFINITY) ? 0.f : __expf(sv[h] - mn);
+      pv[h] = __bfloat162float(__float2bfloat16(e));  // the sum counts what the MMA multiplies
+    }
+    {
+      // P^T as the K-major B operand: [32 heads][128 keys] in two planes of 64 keys
+      uint8_t* pl = smem + OFF_P + (tid >> 6) * QPLANE;
+      const int kc = tid & 63, ch = kc >> 3, el = kc & 7;
+#pragma unroll
+      for (int h = 0; h < 32; ++h)
+        *reinterpret_cast<__nv_bfloat16*>(pl + sw128_off(h, ch) + el * 2) = __float2bfloat16(pv[h]);
+    }
+    __syncthreads();
+    red[warp][lane] = col_reduce32<false>(pv, lane);
+    __syncthreads();
+    if (warp == 0) l_run = l_run * s_corr[lane] + (red[0][lane] + red[1][lane] + red[2][lane] + red[3][lane]);
+    if (ntile > 0 && s_rescale) {
+      // O^T tile mt, lane = dim: scale head column h by corr[h]
+#pragma unroll 1
+      for (int mt = 0; mt < 4; ++mt) {
+        float o[32];
+        tmem_ld16(trow + COL_O + mt * HN, o);
+        tmem_ld16(trow + COL_O + mt * HN + 16, o + 16);
+        tmem_ld_wait();
+#pragma unroll
+        for (int h = 0; h < 32; ++h) o[h] *= s_corr[h];
+        tmem_st16(trow + COL_O + mt * HN, o);
+        tmem_st16(trow + COL_O + mt * HN + 16, o + 16);
+      }
+      tmem_st_wait();
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      constexpr uint32_t idO = idesc_dense(kFmtBF16, kFmtBF16, 128, HN) | (1u << 15);  // A (V^T) MN-major
+#pragma unroll 1
+      for (int mt = 0; mt < 4; ++mt)
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_f16_ss(tbase + COL_O + mt * HN, sdesc_mn_sw128(kbase + 2 * mt * KPLANE + ks * 2048, KPLANE, 1024),
+                     sdesc_k_sw128(pbase + (ks >> 2) * QPLANE + (ks & 3) * 32), idO, (ntile > 0 || ks > 0) ? 1u : 0u);
+      tc_commit(&bar);
+    }
+    ok = mbar_wait(&bar, phase, timeout_ns);
+    phase ^= 1;
+    if (!__syncthreads_and(ok)) {
+      failed = true;
+      break;
+    }
+    tc_fence_after();
+    ++ntile;
+  }
+  if (failed) {
+    if (tid == 0) report_error(status, kErrMbarTimeout, 700, t);
+    (void)mbar_wait(&bar, phase, timeout_ns);  // the last MMA batch, if it is still running
+    ntile = 0;                                  // report an empty split
+  }
+  if (warp == 0 && hb + lane < H) {
+    const int64_t base = ((int64_t)t * H + hb + lane) * nsplit + split;
+    part_ml[base * 2] = ntile ? m_run : -INFINITY;
+    part_ml[base * 2 + 1] = ntile ? l_run : 0.f;
+  }
+  const int hn = min(HN, H - hb);
+#pragma unroll 1
+  for (int mt = 0; mt < 4; ++mt) {
+    float o[32];
+    if (ntile) {
+      tmem_ld16(trow + COL_O + mt * HN, o);
+      tmem_ld16(trow + COL_O + mt * HN + 16, o + 16);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int h = 0; h < 32; ++h) o[h] = 0.f;
+    }
+    const int d = mt * 128 + tid;
+#pragma unroll
+    for (int h = 0; h < 32; ++h)
+      if (h < hn) part_o[(((int64_t)t * H + hb + h) * nsplit + split) * LAT + d] = o[h];
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+void sparse_mla_decode_tc(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
+                          torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
+                          torch::Tensor part_ml, torch::Tensor out, torch::Tensor status) {
+  const int64_t T = q.size(0), H = q.size(1);
+  if (T == 0) return;
+  TORCH_CHECK(q.dtype() == torch::kBFloat16 && q.size(2) >= ROW && q.stride(2) == 1 && q.stride(1) % 8 == 0 &&
+                  q.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0,
+              "sparse_mla_decode_tc: q [T, H, 576] bf16 with 16-byte aligned rows");
+  TORCH_CHECK(lat_cache.dtype() == torch::kBFloat16 && lat_cache.is_contiguous() && lat_cache.size(-1) == ROW,
+              "sparse_mla_decode_tc: latent cache [blocks, 64, 576] bf16");
+  const int64_t nsplit = part_o.size(1);
+  TORCH_CHECK(part_o.size(0) >= T * H && part_o.size(2) == LAT && part_o.is_contiguous() && part_ml.is_contiguous(),
+              "sparse_mla_decode_tc: partials [T*H, nsplit, 512]");
+  TORCH_CHECK(T <= 2147483647 && nsplit <= 65535, "sparse_mla_decode_tc: grid");
+  const at::cuda::CUDAGuard guard(q.device());
+  auto st = at::cuda::getCurrentCUDAStream();
+  TORCH_CHECK(ensure_smem_attr((const void*)sparse_mla_tc_kernel, smla::SMEM) == cudaSuccess,
+              "sparse_mla_decode_tc: smem attribute");
+  TORCH_CHECK(launch_pdl(sparse_mla_tc_kernel, dim3((unsigned)T, (unsigned)((H + smla::HN - 1) / smla::HN), (unsigned)nsplit),
+                         dim3(128), (size_t)smla::SMEM, st, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+                         q.stride(0), (int)q.stride(1), (int)H,
+                         reinterpret_cast<const __nv_bfloat16*>(lat_cache.data_ptr()), block_table.data_ptr<int32_t>(),
+                         (int)block_table.size(1), tok_seq.data_ptr<int32_t>(), sel.data_ptr<int32_t>(),
+                         sel_count.data_ptr<int32_t>(), (int)sel.size(1), (float)scale, (int)nsplit,
+                         part_o.data_ptr<float>(), part_ml.data_ptr<float>(), status.data_ptr<int>()) == cudaSuccess,
+              "sparse_mla_decode_tc launch");
+  launch_pdl(mla_combine_kernel, dim3((unsigned)(T * H)), dim3(128), 0, st, part_o.data_ptr<float>(),
+             part_ml.data_ptr<float>(), (int)nsplit, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0),
+             (int)out.stride(1), (int)H);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
 void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
                        torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
                        torch::Tensor part_ml, torch::Tensor out) {

@@ -16,6 +16,8 @@ import os
 _KNOBS = {
     "R9K_ATTN": ("tc", "simple", "tc: tcgen05 flash attention; simple: CUDA-core paged attention"),
     "R9K_ATTN_DEC": ("1", "0", "1: keys-on-M split-KV decode attention; 0: the row-tile kernel"),
+    "R9K_MLA_ATTN": ("tc", "simple", "tc: sparse MLA attention on tcgen05 (selected keys on the MMA's M side, heads on N); "
+                     "simple: the CUDA-core kernel"),
     "R9K_WEIGHT_TILED": ("1", "0", "1: MX weights stored as contiguous 128x128 units; 0: row-major"),
     "R9K_GEMM_SK": ("0", "0", "1: skinny GEMMs use the persistent stream-K kernel"),
     "R9K_GEMM_SWAP": ("1", "0", "1: prefill-sized MX GEMMs put tokens on the MMA's M side (vector epilogue); 0: weight rows"),

@@ -19,8 +19,9 @@ from dataclasses import dataclass, replace
 
 import torch
 
-from .. import _native
+from .. import _native, knobs
 from ..ops import linear as L
+from ..utils import status as _status
 from .config import ParallelConfig
 from .hybrid import NoComm, StepMeta
 from .hybrid_moe import MoEBuffers, moe_ffn
@@ -244,8 +245,12 @@ class MLAMoELM:
             o.topk_select(ws.scores[:n], meta.tok_ctx[sl], c.index_topk, ws.sel[:n], ws.sel_cnt[:n])
             po = ws.part_o[: n * nh]
             pml = ws.part_ml[: n * nh]
-            o.sparse_mla_decode(qf[sl], self.lat[i], meta.block_table, meta.tok_seq[sl], ws.sel[:n], ws.sel_cnt[:n],
-                                self.scale, po, pml, ws.o_lat[sl])
+            if knobs.get("R9K_MLA_ATTN") == "simple":
+                o.sparse_mla_decode(qf[sl], self.lat[i], meta.block_table, meta.tok_seq[sl], ws.sel[:n],
+                                    ws.sel_cnt[:n], self.scale, po, pml, ws.o_lat[sl])
+            else:
+                o.sparse_mla_decode_tc(qf[sl], self.lat[i], meta.block_table, meta.tok_seq[sl], ws.sel[:n],
+                                       ws.sel_cnt[:n], self.scale, po, pml, ws.o_lat[sl], _status.status(self.device))
         o.head_gemv(ws.o_lat[:T], lay["w_uv"], ws.o[:T])
         L.bf16_linear(ws.o[:T].view(T, -1), lay["w_o"], out=ws.y[:T])
         self.comm.all_reduce_(ws.y[:T])

@@ -412,6 +412,40 @@ def bench_hc(a) -> dict:
     return {"kernel": "hc_point", "T": T, "HC": HC, "H": H, "us": us, "weight_bytes": nbytes, "flops": 0.0}
 
 
+def bench_mla(a) -> dict:
+    """Sparse MLA attention (GLM / DeepSeek-class): T query tokens of H heads, each attending to k
+    selected latent rows (576 bf16 = 512 latent + 64 rope) of a paged cache at ctx positions, split
+    over nsplit partials + the combine. ``--simple`` times the CUDA-core kernel instead of tcgen05.
+    Bytes = the gathered rows; FLOPs = 2 T H k (576 + 512)."""
+    from .. import _native
+    from ..utils import status
+
+    torch.manual_seed(0)
+    T, H, ctx, K, BLK = a.T, a.H, a.ctx, a.topk, 64
+    nbps = (ctx + BLK - 1) // BLK
+    nblk = T * nbps + 1
+    lat = (torch.randn(nblk, BLK, 576, device="cuda") * 0.5).bfloat16()
+    bt = (torch.arange(T * nbps, dtype=torch.int32, device="cuda") + 1).view(T, nbps)
+    tok_seq = torch.arange(T, dtype=torch.int32, device="cuda")
+    n = min(K, ctx)
+    sel = torch.stack([torch.randperm(ctx, device="cuda")[:n].sort().values for _ in range(T)]).int()
+    cnt = torch.full((T,), n, dtype=torch.int32, device="cuda")
+    q = torch.randn(T, H, 576, device="cuda").bfloat16()
+    nsplit = a.nsplit or 4
+    po = torch.empty(T * H, nsplit, 512, device="cuda")
+    pml = torch.empty(T * H, nsplit, 2, device="cuda")
+    out = torch.empty(T, H, 512, dtype=torch.bfloat16, device="cuda")
+    ops, st = _native.ops(), status.status(torch.device("cuda"))
+    if a.simple:
+        f = lambda i: ops.sparse_mla_decode(q, lat, bt, tok_seq, sel, cnt, 192 ** -0.5, po, pml, out)
+    else:
+        f = lambda i: ops.sparse_mla_decode_tc(q, lat, bt, tok_seq, sel, cnt, 192 ** -0.5, po, pml, out, st)
+    us = _time(f, a.reps, a.warmup, graph=not a.eager)
+    status.check()
+    return {"kernel": "sparse_mla_decode" + ("" if a.simple else "_tc"), "T": T, "H": H, "ctx": ctx, "topk": n,
+            "nsplit": nsplit, "us": us, "weight_bytes": 1152.0 * T * n, "flops": 2.0 * T * H * n * (576 + 512)}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -457,17 +491,24 @@ def main(argv=None):
     qs.add_argument("--hkv", type=int, default=2)
     qs.add_argument("--topk", type=int, default=512)
     qs.add_argument("--nsplit", type=int, default=0)
+    ml = sub.add_parser("mla")
+    ml.add_argument("--T", type=int, default=16)
+    ml.add_argument("--H", type=int, default=64)
+    ml.add_argument("--ctx", type=int, default=8192)
+    ml.add_argument("--topk", type=int, default=2048)
+    ml.add_argument("--nsplit", type=int, default=0)
+    ml.add_argument("--simple", action="store_true", help="the CUDA-core kernel")
     hcp = sub.add_parser("hc")
     hcp.add_argument("--T", type=int, default=16)
     hcp.add_argument("--hc", type=int, default=4)
     hcp.add_argument("--H", type=int, default=2048)
-    for p in (g, m, d, gd, at, qs, hcp):
+    for p in (g, m, d, gd, at, qs, ml, hcp):
         p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
     r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn, "attn": bench_attn,
-         "qsa": bench_qsa, "hc": bench_hc}[a.cmd](a)
+         "qsa": bench_qsa, "mla": bench_mla, "hc": bench_hc}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:
         r["gbs"] = r["weight_bytes"] / r["us"] / 1e3

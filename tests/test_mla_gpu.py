@@ -135,3 +135,52 @@ def test_head_gemv_and_rope_heads():
     _ops().rope_heads(y, H, 128, pos, cs)
     _check()
     torch.testing.assert_close(y[..., 128:].float(), ref, rtol=1e-2, atol=1e-2)
+
+
+@pytest.mark.parametrize("H", [16, 40, 64])
+def test_sparse_mla_tc_matches_reference(H):
+    """The tcgen05 sparse MLA (keys on the MMA's M side, heads on N, O^T in TMEM) against fp32 softmax
+    attention over the selected latent rows and against the CUDA-core kernel: selections of 0 to 700
+    rows (several 128-key tiles, empty splits), head counts that fill one, one and a part, and two
+    32-head groups, two calls in a row."""
+    o = _ops()
+    from r9700_stack_b200.utils import status
+
+    ctxs = [900, 130, 5, 1, 700]
+    counts = [700, 130, 5, 0, 257]
+    nblk, bt, _ = _setup(ctxs, seed=4)
+    g = torch.Generator().manual_seed(7)
+    lat = (torch.randn(nblk, 64, 576, generator=g) * 0.5).bfloat16().cuda()
+    Tq, K = len(ctxs), 768
+    sel = torch.full((Tq, K), -1, dtype=torch.int32)
+    for s, (cx, n) in enumerate(zip(ctxs, counts)):
+        sel[s, :n] = torch.randperm(cx, generator=g)[:n].sort().values.int()
+    sel, cnt = sel.cuda(), torch.tensor(counts, dtype=torch.int32, device="cuda")
+    tok_seq = torch.arange(Tq, dtype=torch.int32, device="cuda")
+    q = torch.randn(Tq, H, 576, generator=g).bfloat16().cuda()
+    scale = 1 / math.sqrt(192)
+    nsplit = 4
+    po = torch.empty(Tq * H, nsplit, 512, device="cuda")
+    pml = torch.empty(Tq * H, nsplit, 2, device="cuda")
+    outs = []
+    for _ in range(2):
+        out = torch.full((Tq, H, 512), float("nan"), dtype=torch.bfloat16, device="cuda")
+        o.sparse_mla_decode_tc(q, lat, bt, tok_seq, sel, cnt, scale, po, pml, out, status.status(torch.device("cuda")))
+        _check()
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1])
+    simple = torch.empty(Tq, H, 512, dtype=torch.bfloat16, device="cuda")
+    o.sparse_mla_decode(q, lat, bt, tok_seq, sel, cnt, scale, po, pml, simple)
+    _check()
+    for s in range(Tq):
+        n = counts[s]
+        if n == 0:
+            assert torch.all(outs[0][s] == 0)
+            continue
+        pos = sel[s, :n].long().cpu()
+        rows = torch.tensor([int(bt[s, int(p) // 64]) * 64 + int(p) % 64 for p in pos], device="cuda")
+        R = lat.view(-1, 576)[rows].float()
+        ref = torch.softmax((q[s].float() @ R.t()) * scale, -1) @ R[:, :512]
+        err = float((outs[0][s].float() - ref).norm() / ref.norm())
+        assert err < 1e-2, (s, err)  # bf16 probabilities in the P V product
+        torch.testing.assert_close(outs[0][s].float(), simple[s].float(), rtol=3e-2, atol=3e-2)
