@@ -137,7 +137,8 @@ void mla_cache_write(torch::Tensor kv, torch::Tensor kv_w, c10::optional<torch::
                      torch::Tensor slots, torch::Tensor lat_cache, c10::optional<torch::Tensor> idx_cache);
 void rope_heads(torch::Tensor x, int64_t H, int64_t off, torch::Tensor positions, torch::Tensor cos_sin);
 void indexer_score(torch::Tensor q, torch::Tensor w, torch::Tensor idx_cache, torch::Tensor block_table,
-                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores);
+                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores,
+                   c10::optional<torch::Tensor> status);
 void topk_select(torch::Tensor scores, torch::Tensor tok_ctx, int64_t k, torch::Tensor out, torch::Tensor count);
 void sparse_mla_decode(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
                        torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
@@ -284,7 +285,7 @@ TORCH_LIBRARY(r9k, m) {
         "Tensor cos_sin, Tensor slots, Tensor(a!) lat_cache, Tensor(b!)? idx_cache) -> ()");
   m.def("rope_heads(Tensor(a!) x, int H, int off, Tensor positions, Tensor cos_sin) -> ()");
   m.def("indexer_score(Tensor q, Tensor w, Tensor idx_cache, Tensor block_table, Tensor tok_seq, Tensor tok_ctx, "
-        "int max_ctx, Tensor(a!) scores) -> ()");
+        "int max_ctx, Tensor(a!) scores, Tensor(b!)? status=None) -> ()");
   m.def("topk_select(Tensor scores, Tensor tok_ctx, int k, Tensor(a!) out, Tensor(b!) count) -> ()");
   m.def("sparse_mla_decode(Tensor q, Tensor lat_cache, Tensor block_table, Tensor tok_seq, Tensor sel, "
         "Tensor sel_count, float scale, Tensor(a!) part_o, Tensor(b!) part_ml, Tensor(c!) out) -> ()");

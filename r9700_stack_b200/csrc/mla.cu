@@ -41,6 +41,42 @@ R9K_DEVINL int64_t slot_of(const int32_t* bt, int mb, int seq, int pos) {
 }
 }  // namespace
 
+R9K_DEVINL void cp_async16_sw(uint8_t* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile (8-row groups of 1 KiB)
+R9K_DEVINL uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+// MN-major 128-byte-swizzled operand: rows along K (128 bytes = 64 elements of M or N per row), the two
+// 64-element halves `lbo` bytes apart, 8-row groups `sbo` bytes apart
+R9K_DEVINL uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+// v[c] of every lane -> lane l returns the reduction of column l over the warp (transpose-reduce:
+// each step trades the half of the columns this lane does not keep)
+template <bool MAX>
+R9K_DEVINL float col_reduce32(float (&v)[32], int lane) {
+#pragma unroll
+  for (int k = 16; k >= 1; k >>= 1) {
+    const bool up = (lane & k) != 0;
+#pragma unroll
+    for (int i = 0; i < k; ++i) {
+      const float send = up ? v[i] : v[i + k];
+      const float recv = __shfl_xor_sync(0xffffffffu, send, k);
+      const float keep = up ? v[i + k] : v[i];
+      v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
+    }
+  }
+  return v[0];
+}
+
+
 // ------------------------------------------------------------------------------------------------
 // cache write: one warp per token for the latent row, one for the indexer key
 // ------------------------------------------------------------------------------------------------
@@ -445,13 +481,160 @@ void rope_heads(torch::Tensor x, int64_t H, int64_t off, torch::Tensor positions
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+// ------------------------------------------------------------------------------------------------
+// indexer scores on tcgen05: grid (T, ceil(max_ctx / 128)), 128 threads. Keys on the MMA's M side
+// (128 positions per CTA, e4m3 rows widened to bf16 in shared memory: exact), the token's index heads
+// on N, K = 128 dims: S^T [keys x heads] in TMEM; thread r (TMEM lane r) then sums w[h] relu(S[r][h])
+// over its row, so the head reduction needs no cross-thread traffic.
+// ------------------------------------------------------------------------------------------------
+namespace sidx {
+constexpr int KT = 128;
+constexpr uint32_t KPLANE = KT * 128;                 // 64 dims of 128 keys, bf16
+constexpr uint32_t OFF_K = 0, OFF_Q = 2 * KPLANE;     // then 2 planes of [HN rows][64 dims]
+constexpr uint32_t QPLANE_MAX = 64 * 128;
+constexpr int SMEM = (int)(OFF_Q + 2 * QPLANE_MAX) + 1024;
+constexpr uint32_t TMEM_COLS = 64;
+}  // namespace sidx
+
+__global__ void __launch_bounds__(128) indexer_score_tc_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq, const float* __restrict__ w, int Hi, int HN,
+    const uint8_t* __restrict__ idx_cache, const int32_t* __restrict__ bt, int mb, const int32_t* __restrict__ tok_seq,
+    const int32_t* __restrict__ tok_ctx, float* __restrict__ scores, int64_t lds, int* __restrict__ status) {
+  using namespace sidx;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float sw[64];
+  const int t = blockIdx.x, tid = threadIdx.x, warp = tid >> 5;
+  const uint32_t QPLANE = (uint32_t)HN * 128;
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(&tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_holder;
+  pdl_wait();
+  pdl_trigger();
+  const int ctx = tok_ctx[t], seq = tok_seq[t];
+  const int s0 = blockIdx.y * KT, s = s0 + tid;
+  if (s0 < ctx) {
+    // the token's heads: 2 K-major planes of [HN rows][64 dims] (rows past Hi are zero)
+    for (int e = tid; e < 2 * HN * 8; e += 128) {
+      const int pl = e / (HN * 8), r = (e / 8) % HN, c = e % 8;
+      uint8_t* dst = smem + OFF_Q + pl * QPLANE + sw128_off(r, c);
+      if (r < Hi) cp_async16_sw(dst, q + (int64_t)t * ldq + r * IDXD + pl * 64 + c * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    if (tid < Hi) sw[tid] = w[(int64_t)t * Hi + tid];
+    // key row tid: 128 e4m3 values widened to bf16 (exact) into the two K planes
+    uint4 raw[8];
+    if (s < ctx) {
+      const uint4* kr = reinterpret_cast<const uint4*>(idx_cache + slot_of(bt, mb, seq, s) * IDXD);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) raw[i] = kr[i];
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) raw[i] = make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {  // 16 fp8 -> two 16-byte chunks of 8 bf16
+      const uint8_t* b = reinterpret_cast<const uint8_t*>(&raw[i]);
+#pragma unroll
+      for (int hlf = 0; hlf < 2; ++hlf) {
+        uint4 o;
+        __nv_bfloat16* e = reinterpret_cast<__nv_bfloat16*>(&o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) e[j] = __float2bfloat16(e4m3_to_f(b[hlf * 8 + j]));
+        const int c16 = 2 * i + hlf;  // 16-byte chunk 0..15 of the 256-byte bf16 row
+        *reinterpret_cast<uint4*>(smem + OFF_K + (c16 >> 3) * KPLANE + sw128_off(tid, c16 & 7)) = o;
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const uint32_t idesc = idesc_dense(kFmtBF16, kFmtBF16, 128, HN);
+      const uint32_t kb = smem_u32(smem + OFF_K), qb = smem_u32(smem + OFF_Q);
+#pragma unroll
+      for (int pl = 0; pl < 2; ++pl)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tbase, sdesc_k_sw128(kb + pl * KPLANE + kk * 32), sdesc_k_sw128(qb + pl * QPLANE + kk * 32), idesc,
+                     (pl | kk) ? 1u : 0u);
+      tc_commit(&bar);
+    }
+    const bool ok = mbar_wait(&bar, 0, 1000000000ull);
+    if (__syncthreads_and(ok)) {
+      tc_fence_after();
+      float acc = 0.f;
+      const uint32_t trow = tbase + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+      for (int c0 = 0; c0 < HN; c0 += 16) {
+        float d[16];
+        tmem_ld16(trow + c0, d);
+        tmem_ld_wait();
+#pragma unroll
+        for (int j = 0; j < 16; ++j)
+          if (c0 + j < Hi) acc = fmaf(sw[c0 + j], fmaxf(d[j], 0.f), acc);
+      }
+      if (s < lds) scores[(int64_t)t * lds + s] = s < ctx ? acc : -INFINITY;
+    } else {
+      if (tid == 0) report_error(status, kErrMbarTimeout, 701, t);
+      (void)mbar_wait(&bar, 0, 1000000000ull);
+    }
+  } else if (s < lds) {
+    scores[(int64_t)t * lds + s] = -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+static bool indexer_tc_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("R9K_INDEXER");
+    v = (e && (e[0] == 's')) ? 0 : 1;  // "simple" / "stock": the CUDA-core kernel
+  }
+  return v == 1;
+}
+
 void indexer_score(torch::Tensor q, torch::Tensor w, torch::Tensor idx_cache, torch::Tensor block_table,
-                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores) {
+                   torch::Tensor tok_seq, torch::Tensor tok_ctx, int64_t max_ctx, torch::Tensor scores,
+                   c10::optional<torch::Tensor> status) {
   const int64_t T = q.size(0), Hi = q.size(1);
   if (T == 0) return;
   TORCH_CHECK(q.size(2) == IDXD && q.stride(2) == 1 && q.stride(1) == IDXD, "indexer_score: q [T, Hi, 128]");
   TORCH_CHECK(scores.size(1) >= max_ctx && Hi <= 64, "indexer_score: scores [T, >= max_ctx], <= 64 heads");
   const at::cuda::CUDAGuard guard(q.device());
+  if (indexer_tc_enabled() && reinterpret_cast<uintptr_t>(q.data_ptr()) % 16 == 0 && q.stride(0) % 8 == 0) {
+    int* stt = (status.has_value() && status->defined()) ? status->data_ptr<int>() : nullptr;
+    const int HN = (int)((Hi + 15) / 16 * 16);
+    TORCH_CHECK(ensure_smem_attr((const void*)indexer_score_tc_kernel, sidx::SMEM) == cudaSuccess,
+                "indexer_score: smem attribute");
+    TORCH_CHECK(launch_pdl(indexer_score_tc_kernel, dim3((unsigned)T, (unsigned)((max_ctx + 127) / 128)), dim3(128),
+                           (size_t)sidx::SMEM, at::cuda::getCurrentCUDAStream(),
+                           reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0), w.data_ptr<float>(), (int)Hi,
+                           HN, idx_cache.data_ptr<uint8_t>(), block_table.data_ptr<int32_t>(), (int)block_table.size(1),
+                           tok_seq.data_ptr<int32_t>(), tok_ctx.data_ptr<int32_t>(), scores.data_ptr<float>(),
+                           scores.stride(0), stt) == cudaSuccess,
+                "indexer_score_tc launch");
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   const size_t smem = (size_t)(Hi * IDXD + Hi) * sizeof(float);
   launch_pdl(indexer_score_kernel, dim3((unsigned)T, (unsigned)((max_ctx + 127) / 128)), dim3(128), smem,
              at::cuda::getCurrentCUDAStream(), reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()), q.stride(0),
@@ -493,41 +676,6 @@ constexpr uint32_t OFF_END = OFF_P + 2 * QPLANE;
 constexpr int SMEM = (int)OFF_END + 1024;  // + 1 KiB alignment slack
 constexpr uint32_t TMEM_COLS = 256, COL_S = 0, COL_O = 32;
 }  // namespace smla
-
-R9K_DEVINL void cp_async16_sw(uint8_t* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-// byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile (8-row groups of 1 KiB)
-R9K_DEVINL uint32_t sw128_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
-
-// MN-major 128-byte-swizzled operand: rows along K (128 bytes = 64 elements of M or N per row), the two
-// 64-element halves `lbo` bytes apart, 8-row groups `sbo` bytes apart
-R9K_DEVINL uint64_t sdesc_mn_sw128(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
-  uint64_t d = (uint64_t)((saddr & 0x3FFFFu) >> 4);
-  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
-  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
-  d |= (uint64_t)1u << 46;
-  d |= (uint64_t)2u << 61;
-  return d;
-}
-
-// v[c] of every lane -> lane l returns the reduction of column l over the warp (transpose-reduce:
-// each step trades the half of the columns this lane does not keep)
-template <bool MAX>
-R9K_DEVINL float col_reduce32(float (&v)[32], int lane) {
-#pragma unroll
-  for (int k = 16; k >= 1; k >>= 1) {
-    const bool up = (lane & k) != 0;
-#pragma unroll
-    for (int i = 0; i < k; ++i) {
-      const float send = up ? v[i] : v[i + k];
-      const float recv = __shfl_xor_sync(0xffffffffu, send, k);
-      const float keep = up ? v[i + k] : v[i];
-      v[i] = MAX ? fmaxf(keep, recv) : keep + recv;
-    }
-  }
-  return v[0];
-}
 
 __global__ void __launch_bounds__(128, 1) sparse_mla_tc_kernel(
     const __nv_bfloat16* __restrict__ q, int64_t ldq_t, int ldq_h, int H, const __nv_bfloat16* __restrict__ lat_cache,

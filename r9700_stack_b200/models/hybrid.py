@@ -417,7 +417,7 @@ class HybridLM:
             r1 = min(T, r0 + rows)
             sc = ws.qsa_scores[: (r1 - r0) * groups].view(r1 - r0, groups)
             o.indexer_score(iq[r0:r1], ws.qsa_w[r0:r1], ckey, meta.block_table, meta.tok_seq[r0:r1], vis[r0:r1],
-                            groups, sc)
+                            groups, sc, _status.status(self.device))
             o.topk_select(sc, vis[r0:r1], k, ws.qsa_sel[r0:r1], ws.qsa_cnt[r0:r1])
         kc, vc = self.kv[i]
         hq, hkv = a["hq"], a["hkv"]

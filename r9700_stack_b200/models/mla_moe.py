@@ -241,7 +241,7 @@ class MLAMoELM:
             n = min(C, T - t0)
             sl = slice(t0, t0 + n)
             o.indexer_score(ws.qi[sl], ws.wi[sl], self.icache[i], meta.block_table, meta.tok_seq[sl],
-                            meta.tok_ctx[sl], ws.max_ctx, ws.scores[:n])
+                            meta.tok_ctx[sl], ws.max_ctx, ws.scores[:n], _status.status(self.device))
             o.topk_select(ws.scores[:n], meta.tok_ctx[sl], c.index_topk, ws.sel[:n], ws.sel_cnt[:n])
             po = ws.part_o[: n * nh]
             pml = ws.part_ml[: n * nh]

@@ -436,6 +436,21 @@ def bench_mla(a) -> dict:
     pml = torch.empty(T * H, nsplit, 2, device="cuda")
     out = torch.empty(T, H, 512, dtype=torch.bfloat16, device="cuda")
     ops, st = _native.ops(), status.status(torch.device("cuda"))
+    if a.indexer:
+        # lightning-indexer scores over the whole context (R9K_INDEXER=simple: the CUDA-core kernel)
+        Hi = 32
+        ic = torch.randint(0, 255, (nblk, BLK, 128), dtype=torch.uint8, device="cuda") & 0x7E
+        qi = torch.randn(T, Hi, 128, device="cuda").bfloat16()
+        wi = torch.rand(T, Hi, device="cuda")
+        ctxs = torch.full((T,), ctx, dtype=torch.int32, device="cuda")
+        sc = torch.empty(T, ctx, device="cuda")
+        f = lambda i: ops.indexer_score(qi, wi, ic, bt, tok_seq, ctxs, ctx, sc, st)
+        us = _time(f, a.reps, a.warmup, graph=not a.eager)
+        status.check()
+        import os
+
+        return {"kernel": "indexer_score_" + os.environ.get("R9K_INDEXER", "tc"), "T": T, "Hi": Hi, "ctx": ctx,
+                "us": us, "weight_bytes": 128.0 * T * ctx, "flops": 2.0 * T * Hi * ctx * 128}
     if a.simple:
         f = lambda i: ops.sparse_mla_decode(q, lat, bt, tok_seq, sel, cnt, 192 ** -0.5, po, pml, out)
     else:
@@ -498,6 +513,7 @@ def main(argv=None):
     ml.add_argument("--topk", type=int, default=2048)
     ml.add_argument("--nsplit", type=int, default=0)
     ml.add_argument("--simple", action="store_true", help="the CUDA-core kernel")
+    ml.add_argument("--indexer", action="store_true", help="time the indexer scores instead (32 heads, whole context)")
     hcp = sub.add_parser("hc")
     hcp.add_argument("--T", type=int, default=16)
     hcp.add_argument("--hc", type=int, default=4)

@@ -184,3 +184,32 @@ def test_sparse_mla_tc_matches_reference(H):
         err = float((outs[0][s].float() - ref).norm() / ref.norm())
         assert err < 1e-2, (s, err)  # bf16 probabilities in the P V product
         torch.testing.assert_close(outs[0][s].float(), simple[s].float(), rtol=3e-2, atol=3e-2)
+
+
+@pytest.mark.parametrize("Hi", [8, 20, 64])
+def test_indexer_score_long_context(Hi):
+    """Indexer scores (tcgen05 by default: e4m3 keys widened to bf16, heads on the MMA's N side)
+    against w . relu(q k^T) in fp32 over several 128-key tiles, a context that ends mid-tile,
+    positions past it (-inf) and a score row longer than every context."""
+    o = _ops()
+    from r9700_stack_b200.utils import status
+
+    ctxs = [900, 129, 1]
+    nblk, bt, _ = _setup(ctxs, seed=2)
+    g = torch.Generator().manual_seed(3)
+    icache = (torch.randn(nblk, 64, 128, generator=g) * 2).to(torch.float8_e4m3fn).view(torch.uint8).cuda()
+    Tq = len(ctxs)
+    qi = torch.randn(Tq, Hi, 128, generator=g).bfloat16().cuda()
+    wi = torch.rand(Tq, Hi, generator=g).cuda()
+    tok_seq = torch.arange(Tq, dtype=torch.int32, device="cuda")
+    tok_ctx = torch.tensor(ctxs, dtype=torch.int32, device="cuda")
+    maxc = 1024
+    scores = torch.full((Tq, maxc + 8), float("nan"), device="cuda")
+    o.indexer_score(qi, wi, icache, bt, tok_seq, tok_ctx, maxc, scores, status.status(torch.device("cuda")))
+    _check()
+    for s, cx in enumerate(ctxs):
+        rows = torch.tensor([int(bt[s, p // 64]) * 64 + p % 64 for p in range(cx)], device="cuda")
+        kf = icache.view(-1, 128)[rows].view(torch.float8_e4m3fn).float()
+        ref = (wi[s][:, None] * torch.relu(qi[s].float() @ kf.t())).sum(0)
+        torch.testing.assert_close(scores[s, :cx], ref, rtol=1e-4, atol=1e-3)
+        assert torch.all(scores[s, cx:maxc] == float("-inf"))
