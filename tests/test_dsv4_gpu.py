@@ -1,6 +1,7 @@
 """DeepSeek-V4-class model (mHC streams, sparse MLA, trellis-coded experts, host Engram tables):
-CUDA-graph decode equals eager decode, decode agrees with a fresh prefill of the same tokens
-(the reference's decode-vs-prefill divergence gate), and speculative decoding runs through it."""
+its logits against the fp32 oracle (prefill and graph decode), CUDA-graph decode equals eager
+decode, decode agrees with a fresh prefill of the same tokens (the reference's decode-vs-prefill
+divergence gate), and speculative decoding runs through it."""
 import pytest
 import torch
 
@@ -19,6 +20,35 @@ def _llm(graphs=True, k=0, seed=3):
 
 def _prompts():
     return [[5, 6, 7, 8], list(range(30, 70)), [11] * 9]
+
+
+def test_tiny_dsv4_matches_reference():
+    """Prefill of a prompt longer than the indexer's top-k, then two graph-replayed decode steps:
+    every step's last-row logits against ``reference_forward_dsv4`` (mHC seams, sparse MLA, Engram
+    n-grams, trellis experts dequantised densely)."""
+    from r9700_stack_b200.engine.scheduler import SamplingParams
+    from r9700_stack_b200.models.reference_mla import DSV4RefState, reference_forward_dsv4
+    from r9700_stack_b200.utils import status
+
+    llm = _llm(graphs=True, seed=5)
+    prompt = list(range(7, 37))  # 30 tokens > index_topk 24
+    seq = llm.add_request(prompt, SamplingParams(max_tokens=4))
+    st = DSV4RefState(llm.model)
+    llm.step()
+    torch.cuda.synchronize()
+    status.check()
+    got = llm.runner.ws.logits[0].clone()
+    ref = reference_forward_dsv4(llm.model, prompt, st)[-1]
+    cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
+    assert float(cos) > 0.99, float(cos)
+    for _ in range(2):
+        llm.step()
+        torch.cuda.synchronize()
+        status.check()
+        got = llm.runner.ws.logits[0].clone()
+        ref = reference_forward_dsv4(llm.model, [seq.output[-2]], st)[-1]
+        cos = torch.nn.functional.cosine_similarity(got.double(), ref.double(), dim=0)
+        assert float(cos) > 0.99, float(cos)
 
 
 def test_graph_equals_eager_and_finite():
