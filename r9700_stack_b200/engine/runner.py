@@ -81,8 +81,9 @@ def _token_ids(seq, start: int, n: int) -> list[int]:
 def _block_row(seq) -> np.ndarray:
     """The sequence's block list as int32, rebuilt only when a block was added or the list replaced."""
     row = getattr(seq, "_bt_row", None)
-    if row is None or row[0] is not seq.blocks or row[1].shape[0] != len(seq.blocks):
-        row = (seq.blocks, np.asarray(seq.blocks, dtype=np.int32))
+    b = seq.blocks
+    if row is None or row[0] is not b or row[1].shape[0] != len(b) or (b and row[1][-1] != b[-1]):
+        row = (b, np.asarray(b, dtype=np.int32))
         seq._bt_row = row
     return row[1]
 
