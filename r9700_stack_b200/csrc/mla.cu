@@ -885,6 +885,320 @@ __global__ void __launch_bounds__(128, 1) sparse_mla_tc_kernel(
   }
 }
 
+// ------------------------------------------------------------------------------------------------
+// sparse MLA on tcgen05, pipelined: the same math as sparse_mla_tc_kernel, with the phases of a tile
+// overlapped across warps and with two CTAs per SM. Warp 0 gathers the selected rows into a ring of
+// two slots, each holding two 64-dim planes of 128 keys (32 KiB); warp 1 issues the MMAs; warps 2-5
+// run the softmax. Per 128-key tile the ring carries planes (0,1) (2,3) (4,5) (6,7) (8) for
+// S^T = K Q^T, then (0,1) (2,3) (4,5) (6,7) again for O^T += V^T P^T (a re-read that the L2 serves),
+// so the gather of the next planes runs under the MMAs and the softmax of the current ones. The
+// softmax keeps the running max / sum of its 32 heads and rescales O^T in TMEM after the previous
+// tile's P V has completed.
+// ------------------------------------------------------------------------------------------------
+namespace smla2 {
+constexpr int HN = 32, KT = 128, PLANES = ROW / 64, NSLOT = 2, LOADS = 9;  // 5 S loads + 4 P V loads
+constexpr uint32_t PLANE = KT * 128, SLOT = 2 * PLANE, QPLANE = HN * 128;
+constexpr uint32_t OFF_Q = 0, OFF_RING = OFF_Q + PLANES * QPLANE, OFF_P = OFF_RING + NSLOT * SLOT;
+constexpr uint32_t OFF_END = OFF_P + 2 * QPLANE;
+constexpr int SMEM = (int)OFF_END + 1024;
+constexpr uint32_t TMEM_COLS = 256, COL_S = 0, COL_O = 32;
+constexpr uint64_t TIMEOUT = 1000000000ull;
+}  // namespace smla2
+
+R9K_DEVINL void cp_async_mbar_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+R9K_DEVINL void named_bar_sync(int id, int n) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory"); }
+// named barrier that also ORs a predicate over the participating threads (the same answer for all)
+R9K_DEVINL bool named_bar_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred pi, po;\n\t"
+      "setp.ne.u32 pi, %1, 0;\n\t"
+      "bar.red.or.pred po, %2, %3, pi;\n\t"
+      "selp.u32 %0, 1, 0, po;\n\t}\n"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+
+__global__ void __launch_bounds__(192, 2) sparse_mla_tc2_kernel(
+    const __nv_bfloat16* __restrict__ q, int64_t ldq_t, int ldq_h, int H, const __nv_bfloat16* __restrict__ lat_cache,
+    const int32_t* __restrict__ bt, int mb, const int32_t* __restrict__ tok_seq, const int32_t* __restrict__ sel,
+    const int32_t* __restrict__ sel_count, int k, float scale, int nsplit, float* __restrict__ part_o,
+    float* __restrict__ part_ml, int* __restrict__ status) {
+  using namespace smla2;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ uint64_t full[NSLOT], empty[NSLOT], s_full, p_ready, pv_done, q_full;
+  __shared__ uint32_t tmem_holder;
+  __shared__ float red[4][32];
+  __shared__ float s_mnew[32], s_corr[32];
+  __shared__ int s_rescale;
+  const int t = blockIdx.x, hb = blockIdx.y * HN, split = blockIdx.z;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      mbar_init(&full[i], 32);  // one arrive per producer lane (cp.async completion, no increment)
+      mbar_init(&empty[i], 1);
+    }
+    mbar_init(&s_full, 1);
+    mbar_init(&p_ready, 128);
+    mbar_init(&pv_done, 1);
+    mbar_init(&q_full, 32);
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&tmem_holder, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = tmem_holder;
+  pdl_wait();
+  pdl_trigger();
+  const int seq = tok_seq[t];
+  const int n = sel_count[t];
+  const int per = (n + nsplit - 1) / nsplit;
+  const int j0 = min(n, split * per), j1 = min(n, j0 + per);
+  const int ntiles = (j1 - j0 + KT - 1) / KT;
+
+  if (warp == 0) {
+    // ------------------------------ gather producer ------------------------------
+    // the CTA's heads as 9 K-major planes of [32 rows][64 dims]
+    for (int e = lane; e < PLANES * HN * 8; e += 32) {
+      const int pl = e / (HN * 8), r = (e / 8) % HN, c = e % 8;
+      uint8_t* dst = smem + OFF_Q + pl * QPLANE + sw128_off(r, c);
+      if (hb + r < H) cp_async16_sw(dst, q + (int64_t)t * ldq_t + (int64_t)(hb + r) * ldq_h + pl * 64 + c * 8);
+      else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+    }
+    fence_proxy_async();
+    cp_async_mbar_arrive_noinc(&q_full);
+    int load = 0;
+    bool stop = false;
+    for (int it = 0; it < ntiles && !stop; ++it) {
+      const int c0 = j0 + it * KT, cnt = min(KT, j1 - c0);
+      const __nv_bfloat16* src[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int r = lane + 32 * u;
+        const int pos = r < cnt ? sel[(int64_t)t * k + c0 + r] : -1;
+        src[u] = pos >= 0 ? lat_cache + slot_of(bt, mb, seq, pos) * ROW : nullptr;
+      }
+#pragma unroll 1
+      for (int j = 0; j < LOADS; ++j, ++load) {
+        const int sl = load % NSLOT;
+        const bool got = mbar_wait(&empty[sl], (uint32_t)(((load / NSLOT) & 1) ^ 1), TIMEOUT);
+        if (!__all_sync(0xffffffffu, got)) {
+          if (lane == 0) report_error(status, kErrMbarTimeout, 702, load);
+          stop = true;
+          break;
+        }
+        const int p0 = j < 5 ? 2 * j : 2 * (j - 5);  // first plane of this load
+        const int np = (j == 4) ? 1 : 2;             // load 4 carries plane 8 alone
+        uint8_t* base = smem + OFF_RING + sl * SLOT;
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const int r = lane + 32 * u;
+          for (int h = 0; h < np; ++h) {
+#pragma unroll
+            for (int c = 0; c < 8; ++c) {
+              uint8_t* dst = base + h * PLANE + sw128_off(r, c);
+              if (src[u] != nullptr) cp_async16_sw(dst, src[u] + (p0 + h) * 64 + c * 8);
+              else *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+            }
+          }
+        }
+        fence_proxy_async();
+        cp_async_mbar_arrive_noinc(&full[sl]);
+      }
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else if (warp == 1) {
+    // ------------------------------ MMA issuer ------------------------------
+    if (lane == 0) {
+      constexpr uint32_t idS = idesc_dense(kFmtBF16, kFmtBF16, 128, HN);
+      constexpr uint32_t idO = idesc_dense(kFmtBF16, kFmtBF16, 128, HN) | (1u << 15);  // A (V^T) MN-major
+      const uint32_t qbase = smem_u32(smem + OFF_Q), pbase = smem_u32(smem + OFF_P);
+      bool ok = mbar_wait(&q_full, 0, TIMEOUT);
+      int load = 0;
+      for (int it = 0; it < ntiles && ok; ++it) {
+        for (int j = 0; j < LOADS && ok; ++j, ++load) {
+          const int sl = load % NSLOT;
+          if (j == 5) {  // P of this tile written, O rescaled
+            ok = mbar_wait(&p_ready, (uint32_t)(it & 1), TIMEOUT);
+            if (!ok) break;
+            tc_fence_after();
+          }
+          ok = mbar_wait(&full[sl], (uint32_t)((load / NSLOT) & 1), TIMEOUT);
+          if (!ok) break;
+          fence_proxy_async();
+          tc_fence_after();
+          const uint32_t sb = smem_u32(smem + OFF_RING + sl * SLOT);
+          if (j < 5) {
+            const int np = (j == 4) ? 1 : 2;
+            for (int h = 0; h < np; ++h) {
+              const int pl = 2 * j + h;
+#pragma unroll
+              for (int kk = 0; kk < 4; ++kk)
+                mma_f16_ss(tbase + COL_S, sdesc_k_sw128(sb + h * PLANE + kk * 32),
+                           sdesc_k_sw128(qbase + pl * QPLANE + kk * 32), idS, (pl | kk) ? 1u : 0u);
+            }
+            tc_commit(&empty[sl]);
+            if (j == 4) tc_commit(&s_full);
+          } else {
+            const int mt = j - 5;
+#pragma unroll
+            for (int ks = 0; ks < 8; ++ks)
+              mma_f16_ss(tbase + COL_O + mt * HN, sdesc_mn_sw128(sb + ks * 2048, PLANE, 1024),
+                         sdesc_k_sw128(pbase + (ks >> 2) * QPLANE + (ks & 3) * 32), idO,
+                         (it > 0 || ks > 0) ? 1u : 0u);
+            tc_commit(&empty[sl]);
+            if (mt == 3) tc_commit(&pv_done);
+          }
+        }
+      }
+      if (!ok) report_error(status, kErrMbarTimeout, 703, load);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------ softmax (warps 2-5) ------------------------------
+    // every control decision that could split the four warps goes through bar.red.or, so they all
+    // take the same branch and meet at the same named barriers
+    const int sw = warp - 2;                                    // 0..3 among the softmax warps
+    const int row = (warp & 3) * 32 + lane;                     // TMEM lane this thread may access
+    const uint32_t trow = tbase + ((uint32_t)((warp & 3) * 32) << 16);
+    float m_run = -INFINITY, l_run = 0.f;  // head (hb + lane), kept by softmax warp 0
+    bool fail = false;
+    for (int it = 0; it < ntiles; ++it) {
+      const int c0 = j0 + it * KT, cnt = min(KT, j1 - c0);
+      const bool live = row < cnt && sel[(int64_t)t * k + c0 + row] >= 0;
+      const bool bad = !mbar_wait(&s_full, (uint32_t)(it & 1), TIMEOUT);
+      if (named_bar_or(1, 128, bad)) {
+        fail = true;
+        break;
+      }
+      tc_fence_after();
+      float sv[32];
+      tmem_ld16(trow + COL_S, sv);
+      tmem_ld16(trow + COL_S + 16, sv + 16);
+      tmem_ld_wait();
+#pragma unroll
+      for (int h = 0; h < 32; ++h) sv[h] = live ? sv[h] * scale : -INFINITY;
+      {
+        float v[32];
+#pragma unroll
+        for (int h = 0; h < 32; ++h) v[h] = sv[h];
+        red[sw][lane] = col_reduce32<true>(v, lane);
+      }
+      named_bar_sync(1, 128);
+      if (sw == 0) {
+        const float mt = fmaxf(fmaxf(red[0][lane], red[1][lane]), fmaxf(red[2][lane], red[3][lane]));
+        const float mn = fmaxf(m_run, mt);
+        const float corr = (m_run == -INFINITY) ? 0.f : __expf(m_run - mn);
+        s_mnew[lane] = mn;
+        s_corr[lane] = corr;
+        m_run = mn;
+        const bool any = __any_sync(0xffffffffu, corr != 1.f);
+        if (lane == 0) s_rescale = any ? 1 : 0;
+      }
+      named_bar_sync(1, 128);
+      float pv[32];
+#pragma unroll
+      for (int h = 0; h < 32; ++h) {
+        const float mn = s_mnew[h];
+        const float e = (sv[h] == -INFINITY || mn == -INFINITY) ? 0.f : __expf(sv[h] - mn);
+        pv[h] = __bfloat162float(__float2bfloat16(e));
+      }
+      // the previous tile's P V must be complete before P and O change
+      const bool bad2 = it > 0 && !mbar_wait(&pv_done, (uint32_t)((it - 1) & 1), TIMEOUT);
+      if (named_bar_or(1, 128, bad2)) {
+        fail = true;
+        break;
+      }
+      {
+        uint8_t* pl = smem + OFF_P + (row >> 6) * QPLANE;
+        const int kc = row & 63, ch = kc >> 3, el = kc & 7;
+#pragma unroll
+        for (int h = 0; h < 32; ++h)
+          *reinterpret_cast<__nv_bfloat16*>(pl + sw128_off(h, ch) + el * 2) = __float2bfloat16(pv[h]);
+      }
+      red[sw][lane] = col_reduce32<false>(pv, lane);
+      named_bar_sync(1, 128);
+      if (sw == 0) l_run = l_run * s_corr[lane] + (red[0][lane] + red[1][lane] + red[2][lane] + red[3][lane]);
+      if (it > 0 && s_rescale) {
+        tc_fence_after();
+#pragma unroll 1
+        for (int mt = 0; mt < 4; ++mt) {
+          float o[32];
+          tmem_ld16(trow + COL_O + mt * HN, o);
+          tmem_ld16(trow + COL_O + mt * HN + 16, o + 16);
+          tmem_ld_wait();
+#pragma unroll
+          for (int h = 0; h < 32; ++h) o[h] *= s_corr[h];
+          tmem_st16(trow + COL_O + mt * HN, o);
+          tmem_st16(trow + COL_O + mt * HN + 16, o + 16);
+        }
+        tmem_st_wait();
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&p_ready);
+      named_bar_sync(1, 128);  // red[] and s_* are rewritten by the next tile
+    }
+    // epilogue: after the last tile's P V
+    if (ntiles > 0 && !fail) {
+      const bool bad = !mbar_wait(&pv_done, (uint32_t)((ntiles - 1) & 1), TIMEOUT);
+      fail = named_bar_or(1, 128, bad);
+    }
+    const bool done = ntiles > 0 && !fail;
+    if (fail && sw == 0 && lane == 0) report_error(status, kErrMbarTimeout, 704, t);
+    tc_fence_after();
+    if (sw == 0 && hb + lane < H) {
+      const int64_t base = ((int64_t)t * H + hb + lane) * nsplit + split;
+      part_ml[base * 2] = done ? m_run : -INFINITY;
+      part_ml[base * 2 + 1] = done ? l_run : 0.f;
+    }
+    const int hn = min(HN, H - hb);
+#pragma unroll 1
+    for (int mt = 0; mt < 4; ++mt) {
+      float o[32];
+      if (done) {
+        tmem_ld16(trow + COL_O + mt * HN, o);
+        tmem_ld16(trow + COL_O + mt * HN + 16, o + 16);
+        tmem_ld_wait();
+      } else {
+#pragma unroll
+        for (int h = 0; h < 32; ++h) o[h] = 0.f;
+      }
+      const int d = mt * 128 + row;
+#pragma unroll
+      for (int h = 0; h < 32; ++h)
+        if (h < hn) part_o[(((int64_t)t * H + hb + h) * nsplit + split) * LAT + d] = o[h];
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+}
+
+// 1: single-stage kernel always (R9K_MLA_ATTN=tc1); 0: by grid size (the pipelined kernel needs two
+// CTAs on every SM to pay for its re-read of the V planes: measured 2.51 vs 2.75 ms at 1024 tokens x 64
+// heads x top-2048, 58 vs 48 us at 16 tokens)
+static int mla_tc_mode() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("R9K_MLA_ATTN");
+    v = (e && strcmp(e, "tc1") == 0) ? 1 : 0;
+  }
+  return v;
+}
+
 void sparse_mla_decode_tc(torch::Tensor q, torch::Tensor lat_cache, torch::Tensor block_table, torch::Tensor tok_seq,
                           torch::Tensor sel, torch::Tensor sel_count, double scale, torch::Tensor part_o,
                           torch::Tensor part_ml, torch::Tensor out, torch::Tensor status) {
@@ -901,10 +1215,13 @@ void sparse_mla_decode_tc(torch::Tensor q, torch::Tensor lat_cache, torch::Tenso
   TORCH_CHECK(T <= 2147483647 && nsplit <= 65535, "sparse_mla_decode_tc: grid");
   const at::cuda::CUDAGuard guard(q.device());
   auto st = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(ensure_smem_attr((const void*)sparse_mla_tc_kernel, smla::SMEM) == cudaSuccess,
-              "sparse_mla_decode_tc: smem attribute");
-  TORCH_CHECK(launch_pdl(sparse_mla_tc_kernel, dim3((unsigned)T, (unsigned)((H + smla::HN - 1) / smla::HN), (unsigned)nsplit),
-                         dim3(128), (size_t)smla::SMEM, st, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
+  const int64_t ctas = T * ((H + smla::HN - 1) / smla::HN) * nsplit;
+  const bool v2 = mla_tc_mode() == 0 && ctas >= 2 * device_sm_count();
+  auto kern = v2 ? sparse_mla_tc2_kernel : sparse_mla_tc_kernel;
+  const int smem = v2 ? smla2::SMEM : smla::SMEM;
+  TORCH_CHECK(ensure_smem_attr((const void*)kern, smem) == cudaSuccess, "sparse_mla_decode_tc: smem attribute");
+  TORCH_CHECK(launch_pdl(kern, dim3((unsigned)T, (unsigned)((H + smla::HN - 1) / smla::HN), (unsigned)nsplit),
+                         dim3(v2 ? 192 : 128), (size_t)smem, st, reinterpret_cast<const __nv_bfloat16*>(q.data_ptr()),
                          q.stride(0), (int)q.stride(1), (int)H,
                          reinterpret_cast<const __nv_bfloat16*>(lat_cache.data_ptr()), block_table.data_ptr<int32_t>(),
                          (int)block_table.size(1), tok_seq.data_ptr<int32_t>(), sel.data_ptr<int32_t>(),

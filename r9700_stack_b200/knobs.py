@@ -18,8 +18,9 @@ _KNOBS = {
     "R9K_ATTN_DEC": ("1", "0", "1: keys-on-M split-KV decode attention; 0: the row-tile kernel"),
     "R9K_INDEXER": ("tc", "simple", "tc: lightning-indexer / QSA group scores on tcgen05 (keys on M, heads on N); "
                     "simple: the CUDA-core kernel"),
-    "R9K_MLA_ATTN": ("tc", "simple", "tc: sparse MLA attention on tcgen05 (selected keys on the MMA's M side, heads on N); "
-                     "simple: the CUDA-core kernel"),
+    "R9K_MLA_ATTN": ("tc", "simple", "tc: sparse MLA attention on tcgen05 (selected keys on the MMA's M side, heads on "
+                     "N; the pipelined gather/MMA/softmax kernel when the grid fills two CTAs per SM, else the "
+                     "single-stage one); tc1: always the single-stage kernel; simple: the CUDA-core kernel"),
     "R9K_WEIGHT_TILED": ("1", "0", "1: MX weights stored as contiguous 128x128 units; 0: row-major"),
     "R9K_GEMM_SK": ("0", "0", "1: skinny GEMMs use the persistent stream-K kernel"),
     "R9K_GEMM_SWAP": ("1", "0", "1: prefill-sized MX GEMMs put tokens on the MMA's M side (vector epilogue); 0: weight rows"),
@@ -52,7 +53,7 @@ _KNOBS = {
     "R9K_EP": ("ar", "ar", "ar: experts' partials summed by the all-reduce; a2a: all-to-all dispatch/combine"),
 }
 # knobs the C++ library reads with getenv (kept in sync by export_native)
-_NATIVE = ("R9K_ATTN_DEC", "R9K_INDEXER", "R9K_FP4_UNPACK", "R9K_GEMM_L2PF", "R9K_GEMM_SK", "R9K_MOE_MT", "R9K_GEMM_CLUSTER",
+_NATIVE = ("R9K_ATTN_DEC", "R9K_INDEXER", "R9K_MLA_ATTN", "R9K_FP4_UNPACK", "R9K_GEMM_L2PF", "R9K_GEMM_SK", "R9K_MOE_MT", "R9K_GEMM_CLUSTER",
            "R9K_GEMM_SWAP")
 _DEFAULTS = {k: v[0] for k, v in _KNOBS.items()}
 _cache: dict[str, str] = {}

@@ -240,6 +240,41 @@ def bench_decode(a) -> dict:
             "us": us, "weight_bytes": llm.model.weight_bytes(), "flops": 0.0}
 
 
+def bench_prefill(a) -> dict:
+    """One prompt of ``--prompt`` tokens prefilled through ``LLM.step()`` (all chunks of one step),
+    device-timed with CUDA events after a warm-up prompt; ``--layers`` builds a shallower copy of the
+    model (the per-layer time is reported so a full-depth figure can be scaled from it)."""
+    import numpy as np
+
+    from ..engine.llm import LLM
+    from ..engine.scheduler import SamplingParams
+    from ..models.config import EngineConfig, flashnext_moe, qwen27b_hybrid
+    from ..models.mla_moe import glm53_flash
+
+    full = {"dense27b": qwen27b_hybrid, "flashnext": flashnext_moe, "glm53": glm53_flash}[a.model]()
+    cfg = full.scaled(layers=a.layers) if a.layers else full
+    P = a.prompt
+    ec = EngineConfig(max_batch=1, max_model_len=P + 64, max_prefill_tokens=P, cuda_graphs=False)
+    llm = LLM(cfg, ec, seed=0)
+    rng = np.random.default_rng(0)
+    times = []
+    for it in range(1 + a.reps):
+        llm.add_request(rng.integers(0, cfg.vocab, P).tolist(), SamplingParams(max_tokens=1))
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        while llm.has_unfinished():
+            llm.step()
+        e1.record()
+        torch.cuda.synchronize()
+        if it:
+            times.append(e0.elapsed_time(e1))
+    ms = min(times)
+    return {"kernel": "prefill_step", "model": cfg.name, "prompt": P, "layers": cfg.layers, "full_layers": full.layers,
+            "ms": ms, "tok_s": P / (ms / 1e3), "ms_per_layer": ms / cfg.layers,
+            "full_depth_ms_est": ms / cfg.layers * full.layers, "us": ms * 1e3, "weight_bytes": 0.0, "flops": 0.0}
+
+
 def bench_gdn(a) -> dict:
     """The fused GDN decode kernel alone: S sequences, one token each; states rotate over enough
     layers' worth of buffers that every launch reads its state from HBM."""
@@ -485,6 +520,10 @@ def main(argv=None):
     d.add_argument("--streams", type=int, default=16)
     d.add_argument("--prompt", type=int, default=256)
     d.add_argument("--layers", type=int, default=0)
+    pf = sub.add_parser("prefill")
+    pf.add_argument("--model", choices=["dense27b", "flashnext", "glm53"], default="glm53")
+    pf.add_argument("--prompt", type=int, default=8192)
+    pf.add_argument("--layers", type=int, default=0)
     gd = sub.add_parser("gdn")
     gd.add_argument("--S", type=int, default=16)
     gd.add_argument("--Hk", type=int, default=16)
@@ -518,12 +557,13 @@ def main(argv=None):
     hcp.add_argument("--T", type=int, default=16)
     hcp.add_argument("--hc", type=int, default=4)
     hcp.add_argument("--H", type=int, default=2048)
-    for p in (g, m, d, gd, at, qs, ml, hcp):
+    for p in (g, m, d, pf, gd, at, qs, ml, hcp):
         p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "gdn": bench_gdn, "attn": bench_attn,
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "prefill": bench_prefill, "gdn": bench_gdn,
+         "attn": bench_attn,
          "qsa": bench_qsa, "mla": bench_mla, "hc": bench_hc}[a.cmd](a)
     pk = peaks()
     if r["us"] > 0:

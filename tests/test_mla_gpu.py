@@ -213,3 +213,37 @@ def test_indexer_score_long_context(Hi):
         ref = (wi[s][:, None] * torch.relu(qi[s].float() @ kf.t())).sum(0)
         torch.testing.assert_close(scores[s, :cx], ref, rtol=1e-4, atol=1e-3)
         assert torch.all(scores[s, cx:maxc] == float("-inf"))
+
+
+def test_sparse_mla_tc_pipelined_grid():
+    """A grid large enough for the pipelined tcgen05 kernel (40 tokens x 2 head groups x 4 splits >= two
+    CTAs per SM): every token against fp32 softmax attention over its selected rows."""
+    o = _ops()
+    from r9700_stack_b200.utils import status
+
+    Tq, H, K = 40, 64, 640
+    ctxs = [700 + 7 * i for i in range(Tq)]
+    nblk, bt, _ = _setup(ctxs, seed=6)
+    g = torch.Generator().manual_seed(8)
+    lat = (torch.randn(nblk, 64, 576, generator=g) * 0.5).bfloat16().cuda()
+    counts = [K if i % 5 else 300 + i for i in range(Tq)]
+    sel = torch.full((Tq, K), -1, dtype=torch.int32)
+    for s in range(Tq):
+        sel[s, :counts[s]] = torch.randperm(ctxs[s], generator=g)[:counts[s]].sort().values.int()
+    sel, cnt = sel.cuda(), torch.tensor(counts, dtype=torch.int32, device="cuda")
+    tok_seq = torch.arange(Tq, dtype=torch.int32, device="cuda")
+    q = torch.randn(Tq, H, 576, generator=g).bfloat16().cuda()
+    scale = 1 / math.sqrt(192)
+    po = torch.empty(Tq * H, 4, 512, device="cuda")
+    pml = torch.empty(Tq * H, 4, 2, device="cuda")
+    out = torch.full((Tq, H, 512), float("nan"), dtype=torch.bfloat16, device="cuda")
+    o.sparse_mla_decode_tc(q, lat, bt, tok_seq, sel, cnt, scale, po, pml, out, status.status(torch.device("cuda")))
+    _check()
+    for s in range(Tq):
+        n = counts[s]
+        pos = sel[s, :n].long().cpu()
+        rows = torch.tensor([int(bt[s, int(p) // 64]) * 64 + int(p) % 64 for p in pos], device="cuda")
+        R = lat.view(-1, 576)[rows].float()
+        ref = torch.softmax((q[s].float() @ R.t()) * scale, -1) @ R[:, :512]
+        err = float((out[s].float() - ref).norm() / ref.norm())
+        assert err < 1e-2, (s, err)
