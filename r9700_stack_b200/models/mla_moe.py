@@ -34,6 +34,23 @@ def _ops():
     return _native.ops()
 
 
+HEAD_GEMM_MIN_TOKENS = 256
+
+
+def head_project(x: torch.Tensor, W: torch.Tensor, out: torch.Tensor) -> torch.Tensor:
+    """Per-head projection out[t, h, :N] = x[t, h, :K] @ W[h]^T (W [H, N, K] bf16). Wide batches
+    (prefill) run one tcgen05 GEMM per head on strided views of x and out (tokens on the MMA's M
+    side); decode-sized batches run the one-launch CUDA-core ``head_gemv``."""
+    T, H = x.shape[0], W.shape[0]
+    N, K = W.shape[1], W.shape[2]
+    if T < HEAD_GEMM_MIN_TOKENS or K % 64 or x.stride(2) != 1 or out.stride(2) != 1:
+        _ops().head_gemv(x, W, out)
+        return out
+    for h in range(H):
+        L.bf16_linear(x[:, h, :K], L.BF16Weight(W[h]), out=out[:, h, :N])
+    return out
+
+
 @dataclass
 class MLAConfig:
     name: str = "mla-moe"
@@ -226,7 +243,7 @@ class MLAMoELM:
         L.bf16_linear(ws.cq[:T], lay["w_uq"], out=q.view(T, -1))
         o.rope_heads(q, nh, c.qk_nope, meta.positions, self.cos_sin)
         qf = ws.qfull[:T]
-        o.head_gemv(q[:, :, : c.qk_nope], lay["w_uk"], qf[:, :, :LAT])
+        head_project(q[:, :, : c.qk_nope], lay["w_uk"], qf[:, :, :LAT])
         qf[:, :, LAT:].copy_(q[:, :, c.qk_nope:])
         L.bf16_linear(h, lay["w_dkv"], out=ws.kv_a[:T])
         L.bf16_linear(h, lay["w_ik"], out=ws.ik[:T])
@@ -251,7 +268,7 @@ class MLAMoELM:
             else:
                 o.sparse_mla_decode_tc(qf[sl], self.lat[i], meta.block_table, meta.tok_seq[sl], ws.sel[:n],
                                        ws.sel_cnt[:n], self.scale, po, pml, ws.o_lat[sl], _status.status(self.device))
-        o.head_gemv(ws.o_lat[:T], lay["w_uv"], ws.o[:T])
+        head_project(ws.o_lat[:T], lay["w_uv"], ws.o[:T])
         L.bf16_linear(ws.o[:T].view(T, -1), lay["w_o"], out=ws.y[:T])
         self.comm.all_reduce_(ws.y[:T])
 

@@ -247,3 +247,22 @@ def test_sparse_mla_tc_pipelined_grid():
         ref = torch.softmax((q[s].float() @ R.t()) * scale, -1) @ R[:, :512]
         err = float((out[s].float() - ref).norm() / ref.norm())
         assert err < 1e-2, (s, err)
+
+
+@pytest.mark.parametrize("N,K", [(512, 128), (128, 512)])
+def test_head_project_wide_batch_matches_head_gemv(N, K):
+    """Prefill-sized per-head projections (one tcgen05 GEMM per head on strided views) against the
+    CUDA-core head_gemv on the same strided operands."""
+    from r9700_stack_b200.models.mla_moe import head_project
+
+    T, H = 300, 6
+    g = torch.Generator().manual_seed(4)
+    xs = torch.randn(T, H, K + 64, generator=g).bfloat16().cuda()  # strided: extra columns per head
+    W = (torch.randn(H, N, K, generator=g) * 0.05).bfloat16().cuda()
+    a = torch.zeros(T, H, N + 64, dtype=torch.bfloat16, device="cuda")
+    b = torch.zeros_like(a)
+    head_project(xs[:, :, :K], W, a[:, :, :N])
+    _ops().head_gemv(xs[:, :, :K], W, b[:, :, :N])
+    _check()
+    torch.testing.assert_close(a[:, :, :N].float(), b[:, :, :N].float(), rtol=2e-2, atol=2e-2)
+    assert torch.all(a[:, :, N:] == 0)
