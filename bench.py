@@ -83,8 +83,10 @@ def parse():
 
 
 class ClockSampler:
-    """nvidia-smi clocks / throttle reasons sampled every 100 ms; only samples whose timestamp falls
-    inside the marked timed region are kept (the nearest one if the region is shorter than a period)."""
+    """SM clocks and clock-event (throttle) reasons during the timed region: nvidia-smi every 100 ms,
+    plus NVML read every 10 ms from a thread (read-only queries), so a region of a few hundred ms still
+    holds many samples. Only samples whose timestamp falls inside the marked region are kept (the
+    nearest one if the region is shorter than a period)."""
 
     FIELDS = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -99,6 +101,26 @@ class ClockSampler:
         fd, self.path = tempfile.mkstemp(prefix="r9k_clocks_", suffix=".csv")
         os.close(fd)
         self.t0 = self.t1 = None
+        self.nvml: list = []
+        self._halt = None
+        self._thread = None
+
+    def _nvml_loop(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = (pynvml.nvmlDeviceGetHandleByUUID(self.gpu) if str(self.gpu).startswith("GPU-")
+                 else pynvml.nvmlDeviceGetHandleByIndex(int(self.gpu)))
+            cmax = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20, "sw_power_cap": 0x4}
+            while not self._halt.is_set():
+                clk = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                r = pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h)
+                self.nvml.append((time.time(), clk, cmax, [n for n, b in bits.items() if r & b]))
+                self._halt.wait(0.01)
+        except Exception:
+            return
 
     def start(self):
         try:
@@ -110,6 +132,11 @@ class ClockSampler:
                 time.sleep(0.05)
         except Exception:
             self.proc = None
+        import threading
+
+        self._halt = threading.Event()
+        self._thread = threading.Thread(target=self._nvml_loop, daemon=True)
+        self._thread.start()
 
     def mark_start(self):
         self.t0 = time.time()
@@ -118,18 +145,22 @@ class ClockSampler:
         self.t1 = time.time()
 
     def stop(self) -> dict:
-        if self.proc is None:
+        if self._halt is not None:
+            self._halt.set()
+            self._thread.join(timeout=5)
+        samples = list(self.nvml)
+        if self.proc is None and not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except Exception:
-            self.proc.kill()
-        self.fh.close()
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
         from datetime import datetime
 
-        samples = []
-        for line in open(self.path):
+        for line in (open(self.path) if self.proc is not None else []):
             p = [x.strip() for x in line.split(",")]
             if len(p) < 10:
                 continue
@@ -145,6 +176,7 @@ class ClockSampler:
             pass
         if not samples:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        samples.sort(key=lambda x: x[0])
         t0, t1 = self.t0 or samples[0][0], self.t1 or samples[-1][0]
         inside = [x for x in samples if t0 <= x[0] <= t1]
         if not inside:
