@@ -275,6 +275,50 @@ def bench_prefill(a) -> dict:
             "full_depth_ms_est": ms / cfg.layers * full.layers, "us": ms * 1e3, "weight_bytes": 0.0, "flops": 0.0}
 
 
+def bench_spec(a) -> dict:
+    """Speculative verify steps (1 + k rows per sequence: forward, argmax, acceptance, GDN commit)
+    through ``ModelRunner.execute_spec``, end to end on the host clock (metadata packing, upload,
+    launch or graph replay, the token read-back), replayed from the verify CUDA graph and eagerly."""
+    import time
+
+    import numpy as np
+
+    from ..engine.llm import LLM
+    from ..engine.scheduler import SamplingParams, ScheduledChunk, SchedulerOutput
+    from ..models.config import EngineConfig, flashnext_moe, qwen27b_hybrid
+
+    full = qwen27b_hybrid() if a.model == "dense27b" else flashnext_moe()
+    cfg = full.scaled(layers=a.layers) if a.layers else full
+    ec = EngineConfig(max_batch=a.streams, max_model_len=a.prompt + 256, max_prefill_tokens=max(a.prompt, 256),
+                      cuda_graphs=True, graph_batch_sizes=[1, 2, 4, 8, 16], spec_tokens=a.k, spec_method="ngram")
+    llm = LLM(cfg, ec, seed=0)
+    rng = np.random.default_rng(0)
+    seqs = [llm.add_request(rng.integers(0, cfg.vocab, a.prompt).tolist(), SamplingParams(max_tokens=64))
+            for _ in range(a.streams)]
+    while any(not s.prefill_done or not s.output for s in seqs):
+        out = llm.scheduler.schedule()
+        llm.scheduler.finish_step(out, llm.runner.execute(out))
+    for s in seqs:
+        assert llm.scheduler.ensure(s, s.length + a.k + 1)
+    out = SchedulerOutput("decode", [ScheduledChunk(s, s.length - 1, 1, True) for s in seqs])
+    drafts = {s.seq_id: [1] * a.k for s in seqs}
+    res = {}
+    for mode in ("graph", "eager"):
+        llm.runner.cfg.cuda_graphs = mode == "graph"
+        for _ in range(a.warmup):
+            llm.runner.execute_spec(out, drafts)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(a.reps):
+            llm.runner.execute_spec(out, drafts)
+        torch.cuda.synchronize()
+        res[mode + "_us"] = (time.perf_counter() - t0) / a.reps * 1e6
+    llm.runner.cfg.cuda_graphs = True
+    return {"kernel": "spec_verify_step", "model": cfg.name, "layers": cfg.layers, "streams": a.streams, "k": a.k,
+            **res, "graph_speedup": res["eager_us"] / res["graph_us"], "us": res["graph_us"],
+            "weight_bytes": 0.0, "flops": 0.0}
+
+
 def bench_gdn(a) -> dict:
     """The fused GDN decode kernel alone: S sequences, one token each; states rotate over enough
     layers' worth of buffers that every launch reads its state from HBM."""
@@ -524,6 +568,12 @@ def main(argv=None):
     pf.add_argument("--model", choices=["dense27b", "flashnext", "glm53"], default="glm53")
     pf.add_argument("--prompt", type=int, default=8192)
     pf.add_argument("--layers", type=int, default=0)
+    sp = sub.add_parser("spec")
+    sp.add_argument("--model", choices=["dense27b", "flashnext"], default="dense27b")
+    sp.add_argument("--layers", type=int, default=0)
+    sp.add_argument("--streams", type=int, default=16)
+    sp.add_argument("--prompt", type=int, default=256)
+    sp.add_argument("--k", type=int, default=3)
     gd = sub.add_parser("gdn")
     gd.add_argument("--S", type=int, default=16)
     gd.add_argument("--Hk", type=int, default=16)
@@ -557,12 +607,13 @@ def main(argv=None):
     hcp.add_argument("--T", type=int, default=16)
     hcp.add_argument("--hc", type=int, default=4)
     hcp.add_argument("--H", type=int, default=2048)
-    for p in (g, m, d, pf, gd, at, qs, ml, hcp):
+    for p in (g, m, d, pf, sp, gd, at, qs, ml, hcp):
         p.add_argument("--eager", action="store_true", help="time eager launches (host overhead included)")
         p.add_argument("--reps", type=int, default=50)
         p.add_argument("--warmup", type=int, default=5)
     a = ap.parse_args(argv)
-    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "prefill": bench_prefill, "gdn": bench_gdn,
+    r = {"gemm": bench_gemm, "moe": bench_moe, "decode": bench_decode, "prefill": bench_prefill, "spec": bench_spec,
+         "gdn": bench_gdn,
          "attn": bench_attn,
          "qsa": bench_qsa, "mla": bench_mla, "hc": bench_hc}[a.cmd](a)
     pk = peaks()
